@@ -1,0 +1,204 @@
+/*
+ * itts_gpt.h -- C ABI of the B200 (sm_100a) IndexTTS-2.5 Stage-1 GPT decoder.
+ *
+ * Drop-in for the decoder / KV-cache / sampler interface of tyrchen/index-tts-rs
+ * (crates/core/src/models/mod.rs:41-59 re-exports; the implementations are in
+ * crates/core/src/models/gpt.rs and crates/core/src/models/sampler.rs).  Each entry
+ * point below names the Rust item it replaces.  A Rust `-sys` crate binds this
+ * header one to one; see INTEGRATION.md.
+ *
+ * Conventions
+ *  - Every call returns an int status: ITTS_OK or one of the ITTS_E_* codes, which
+ *    mirror IndexTtsError::{Validation, Mlx (device), WeightLoad, Io}
+ *    (crates/core/src/error.rs).  Nothing aborts the process.  The message of the
+ *    calling thread's last failure is returned by itts_last_error().
+ *  - Handles are opaque.  One host thread owns a handle at a time (the reference keeps
+ *    every GPU object on one worker thread, crates/core/src/engine/actor.rs:1-5).
+ *    Each itts_gpt owns one CUDA stream on its device; handles on different devices
+ *    are independent (no global device state), so one worker per GPU runs in parallel.
+ *  - All pointers are host pointers to caller-owned memory unless the name says
+ *    otherwise.  Device memory is allocated at load / cache-creation time only.
+ */
+#ifndef ITTS_GPT_H
+#define ITTS_GPT_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes (crates/core/src/error.rs IndexTtsError variants). */
+#define ITTS_OK 0
+#define ITTS_E_VALIDATION 1 /* IndexTtsError::Validation{field, reason} */
+#define ITTS_E_CUDA 2       /* IndexTtsError::Mlx: device execution failure */
+#define ITTS_E_WEIGHTLOAD 3 /* IndexTtsError::WeightLoad: missing / mis-shaped tensor */
+#define ITTS_E_IO 4         /* IndexTtsError::Io */
+#define ITTS_E_TIMEOUT 5    /* a bounded device wait gave up */
+
+/* Tensor dtypes accepted by itts_gpt_from_tensors (safetensors names in parens). */
+#define ITTS_DTYPE_F32 0 /* "F32" */
+#define ITTS_DTYPE_F16 1 /* "F16" (scales / biases only) */
+#define ITTS_DTYPE_U32 2 /* "U32" (packed weights) */
+#define ITTS_DTYPE_I32 3 /* "I32" (accepted as packed weights, like loader.rs:919) */
+
+/* Model constants (crates/core/src/models/gpt.rs:31-72, sampler.rs:19). */
+#define ITTS_HEAD_DIM 64
+#define ITTS_GROUP_SIZE 64
+#define ITTS_MEL_VOCAB 8194
+#define ITTS_START_TEXT_TOKEN 0
+#define ITTS_STOP_TEXT_TOKEN 1
+#define ITTS_START_MEL_TOKEN 8192
+#define ITTS_STOP_MEL_TOKEN 8193
+#define ITTS_BITSET_WORDS 129
+#define ITTS_DEFAULT_KV_MAX_SEQ 2048
+#define ITTS_MAX_SAMPLE_LOGITS 16384 /* largest logits slice itts_sample_next_token takes */
+
+typedef struct itts_gpt itts_gpt; /* replaces `Gpt` (gpt.rs:436-450) */
+typedef struct itts_kv itts_kv;   /* replaces `KvCache` (gpt.rs:74-81), with batch slots */
+
+/* One named host tensor; replaces a `FilteredWeights` entry (loader.rs). */
+typedef struct itts_tensor {
+    const char *name;   /* reference tensor name, e.g. "gpt.h.0.attn.c_attn.scales" */
+    int32_t dtype;      /* ITTS_DTYPE_* */
+    int32_t ndim;       /* 1 or 2 */
+    int64_t shape[4];
+    const void *data;   /* host pointer, row-major */
+} itts_tensor;
+
+/* SamplingParams (crates/core/src/config.rs:1283-1320). */
+typedef struct itts_sampling_params {
+    int32_t greedy;           /* argmax after the repetition penalty */
+    uint32_t top_k;           /* 0..=8194, 0 = no top-k filtering (config.rs:614-620) */
+    float top_p;              /* 0.01..=1.0 */
+    float temperature;        /* 0.05..=2.0 */
+    float repetition_penalty; /* 1.0..=50.0 */
+    uint32_t max_mel_tokens;  /* 1..=1815 */
+} itts_sampling_params;
+
+/* CodePrompt (crates/core/src/models/sampler.rs:287-301); conds is [n_conds, d]. */
+typedef struct itts_code_prompt {
+    const int32_t *text_tokens;
+    int32_t n_text;
+    const float *conds;
+    int32_t n_conds; /* the reference fixes 3 (gpt.rs:549-553); the benchmark uses 32 */
+    int32_t lang_id;
+    const int32_t *prior_codes;
+    int32_t n_prior;
+    int32_t min_codes;
+} itts_code_prompt;
+
+/* ---- errors, parameters, host-side sampler state ------------------------------ */
+
+/* Copies the calling thread's last error message (NUL-terminated, truncated to len)
+ * and returns its full length. */
+size_t itts_last_error(char *buf, size_t len);
+
+/* Range checks of the SamplingParams newtypes (config.rs:454-682, 1309-1310). */
+int itts_sampling_params_validate(const itts_sampling_params *params);
+
+/* SamplerRng::new (sampler.rs:41-45): returns the initial state for `seed`. */
+uint64_t itts_rng_new(uint64_t seed);
+/* SamplerRng::next_f32 (sampler.rs:58-61), advancing *state. */
+float itts_rng_next_f32(uint64_t *state);
+/* SeenTokenBitSet::new_with_initial_tokens (sampler.rs:110-115): {1, 8192}. */
+void itts_seen_initial(uint64_t words[ITTS_BITSET_WORDS]);
+/* SeenTokenBitSet::insert (sampler.rs:118-124). */
+void itts_seen_insert(uint64_t words[ITTS_BITSET_WORDS], int64_t token_id);
+
+/* ---- model ---------------------------------------------------------------------- */
+
+/* Gpt::load_from_path (gpt.rs:522-525, loader.rs:768-856): reads a gpt_int8
+ * safetensors file (F32 or F16 scales/biases) onto `device`. */
+int itts_gpt_load(const char *path, int device, itts_gpt **out);
+/* Gpt::from_weights (gpt.rs:477-515): the same from caller-owned host tensors. */
+int itts_gpt_from_tensors(const itts_tensor *tensors, int32_t n_tensors, int device,
+                          itts_gpt **out);
+void itts_gpt_free(itts_gpt *gpt);
+/* Gpt::num_layers (gpt.rs:529-531). */
+int32_t itts_gpt_num_layers(const itts_gpt *gpt);
+/* Geometry: {n_layers, d, n_heads, ff, mel_vocab, text_vocab, mel_pos_len,
+ * text_pos_len, lang_vocab, scales_are_f16}. */
+int itts_gpt_dims(const itts_gpt *gpt, int32_t dims[10]);
+
+/* ---- KV cache --------------------------------------------------------------------- */
+
+/* KvCache::new (gpt.rs:102-128) with `max_batch` independent request slots, each of
+ * capacity max_seq positions (fp16 K/V in HBM).  max_seq == 0 is a Validation error
+ * like gpt.rs:103-108. */
+int itts_kv_create(itts_gpt *gpt, int32_t max_seq, int32_t max_batch, itts_kv **out);
+void itts_kv_free(itts_kv *kv);
+/* KvCache::reset (gpt.rs:131-133) of one slot, or of every slot when slot < 0. */
+int itts_kv_reset(itts_kv *kv, int32_t slot);
+/* KvCache::valid_len (gpt.rs:137-139). */
+int itts_kv_valid_len(const itts_kv *kv, int32_t slot, int32_t *out);
+/* KvCache::max_seq (gpt.rs:143-145). */
+int32_t itts_kv_max_seq(const itts_kv *kv);
+int32_t itts_kv_max_batch(const itts_kv *kv);
+
+/* ---- forward ---------------------------------------------------------------------- */
+
+/* Gpt::prefill_after (gpt.rs:655-696); Gpt::prefill when n_prior == 0 (gpt.rs:636-644).
+ * Resets `slot`, runs the causal forward over
+ * [conds, <BOS> text <EOS>, <START_MEL>, prior codes] and writes the [mel_vocab] logits
+ * of the last position to logits_out (may be NULL). */
+int itts_gpt_prefill(itts_gpt *gpt, itts_kv *kv, int32_t slot, const int32_t *text_tokens,
+                     int32_t n_text, const float *conds, int32_t n_conds, int32_t lang_id,
+                     const int32_t *prior_codes, int32_t n_prior, float *logits_out);
+
+/* Gpt::step (gpt.rs:706-754), batched: for i in 0..n, feeds mel token toks[i] at mel
+ * position pos[i] into slot slots[i] (slots distinct), appending one KV position each.
+ * logits_out is [n, mel_vocab] (may be NULL). */
+int itts_gpt_step(itts_gpt *gpt, itts_kv *kv, int32_t n, const int32_t *slots,
+                  const int32_t *toks, const int32_t *pos, float *logits_out);
+
+/* ---- sampling and the decode loop --------------------------------------------------- */
+
+/* sample_next_token (sampler.rs:191-284), run by the on-device sampler: applies the
+ * repetition penalty to `logits` in place (written back), then greedy argmax or
+ * temperature / top-k / top-p / multinomial draw.  *rng_state advances exactly when the
+ * reference draws.  1 <= n_logits <= ITTS_MAX_SAMPLE_LOGITS. */
+int itts_sample_next_token(itts_gpt *gpt, float *logits, int32_t n_logits,
+                           const uint64_t seen_words[ITTS_BITSET_WORDS],
+                           const itts_sampling_params *params, uint64_t *rng_state,
+                           int32_t *token_out);
+
+/* generate_codes_after (sampler.rs:340-392); generate_codes (sampler.rs:309-326) is the
+ * case n_prior == 0, min_codes == 0.  Prefill, then a CUDA-graph decode step per token
+ * with sampling on the device; only the codes return to the host.  codes_out must hold
+ * min(max_mel_tokens, 1815 - n_prior) entries (max_codes says how many it holds). */
+int itts_generate_codes_after(itts_gpt *gpt, itts_kv *kv, int32_t slot,
+                              const itts_code_prompt *prompt,
+                              const itts_sampling_params *params, uint64_t *rng_state,
+                              int32_t *codes_out, int32_t max_codes, int32_t *n_codes_out);
+
+/* Ragged batched generate: request r runs generate_codes_after in slot r with its own
+ * prompt, params[r] and rng_states[r]; all live requests share each decode step and
+ * each leaves the batch at its own STOP.  codes_out is [n_req, codes_stride];
+ * n_codes_out[r] receives request r's count.  Results equal n_req independent calls. */
+int itts_generate_batch(itts_gpt *gpt, itts_kv *kv, int32_t n_req,
+                        const itts_code_prompt *prompts, const itts_sampling_params *params,
+                        uint64_t *rng_states, int32_t *codes_out, int32_t codes_stride,
+                        int32_t *n_codes_out);
+
+/* Device time (CUDA events on the handle's stream) of the last generate call:
+ * prefill_ms (all prefills) and decode_ms (first sample through the last step), and the
+ * number of decode-step graph launches it made. */
+int itts_gpt_last_timing(const itts_gpt *gpt, float *prefill_ms, float *decode_ms,
+                         int32_t *decode_launches);
+
+/* ---- measurement (no reference counterpart) ----------------------------------------- */
+
+/* Replays `iters` times a CUDA graph holding only the weight-streaming kernels of one
+ * decode step for `nb` batch columns (the int8 linears and the head, with their fused
+ * LayerNorm / epilogues; the KV scatter is skipped for inactive slots) and returns the
+ * mean device time per replay (CUDA events on the handle's stream) and the number of
+ * kernel launches per replay.  Roofline of the dominant kernel. */
+int itts_bench_weight_stream(itts_gpt *gpt, itts_kv *kv, int32_t nb, int32_t iters,
+                             float *ms_per_iter, int32_t *launches_per_iter);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ITTS_GPT_H */

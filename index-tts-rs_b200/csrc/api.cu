@@ -1,0 +1,1053 @@
+// api.cu -- the C ABI declared in include/itts_gpt.h.
+//
+// Host orchestration of the decoder: weight upload (Gpt::from_weights,
+// crates/core/src/models/gpt.rs:477-515), safetensors reading (loader.rs:768-856),
+// the batch-slot KV cache (gpt.rs:74-217), prefill / step (gpt.rs:655-754), the
+// sampler (sampler.rs:191-284) and the decode loop (sampler.rs:340-392), which
+// replays one captured CUDA graph per decode step.  No CPU fallback: every numeric
+// step runs in the kernels of decode.cu / prefill.cu / sample.cu.
+#include <cuda_runtime.h>
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <cerrno>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/itts_gpt.h"
+#include "kernels.h"
+
+namespace itts {
+void kernels_init_decode();
+void kernels_init_sample();
+}  // namespace itts
+
+using namespace itts;
+
+static thread_local std::string t_err;
+
+static int set_err(int code, const std::string &msg) {
+    t_err = msg;
+    return code;
+}
+static int validation(const char *field, const std::string &reason) {
+    return set_err(ITTS_E_VALIDATION, std::string("validation error on `") + field + "`: " + reason);
+}
+static int weight_load(const std::string &artifact, const std::string &msg) {
+    return set_err(ITTS_E_WEIGHTLOAD, "weight load error in `" + artifact + "`: " + msg);
+}
+
+#define CUDA_TRY(x)                                                                       \
+    do {                                                                                  \
+        cudaError_t e_ = (x);                                                             \
+        if (e_ != cudaSuccess)                                                            \
+            return set_err(ITTS_E_CUDA, std::string("device error: ") + #x + ": " +       \
+                                            cudaGetErrorString(e_));                      \
+    } while (0)
+
+#define TRY(x)                 \
+    do {                       \
+        int rc_ = (x);         \
+        if (rc_ != ITTS_OK)    \
+            return rc_;        \
+    } while (0)
+
+struct itts_gpt {
+    int device = 0;
+    ModelView m{};
+    std::vector<LayerW> layers;
+    void *arena = nullptr;
+    cudaStream_t stream = nullptr;
+    cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
+    float last_prefill_ms = 0.f, last_decode_ms = 0.f;
+    int last_launches = 0;
+    // standalone sampler scratch
+    SlotState *d_sstate = nullptr;
+    float *d_slogits = nullptr;
+    int *d_sidx = nullptr;  // [0] = batch slot 0, [1] = token out
+    SlotState *h_sstate = nullptr;
+};
+
+struct itts_kv {
+    itts_gpt *gpt = nullptr;
+    int max_seq = 0, max_batch = 0;
+    __half *k = nullptr, *v = nullptr;
+    SlotState *d_slots = nullptr;
+    int *d_batch_slot = nullptr;
+    DecodeBufs db{};
+    PrefillBufs pb{};
+    int32_t *d_codes = nullptr;
+    int codes_stride = 0;
+    int *d_text = nullptr, *d_prior = nullptr;
+    float *d_conds = nullptr;
+    int max_conds = 0;
+    std::vector<SlotState> h_state;  // host mirror (authoritative between calls)
+    SlotState *h_pinned = nullptr;   // staging [max_batch]
+    int32_t *h_i32 = nullptr;        // staging ints
+    float *h_f32 = nullptr;          // staging conds
+    size_t h_f32_cap = 0;
+    std::vector<cudaGraphExec_t> graphs;  // by batch size
+    std::vector<cudaGraph_t> graph_defs;
+};
+
+// ------------------------------------------------------------------------------
+// errors, params, host-side sampler helpers
+// ------------------------------------------------------------------------------
+extern "C" size_t itts_last_error(char *buf, size_t len) {
+    if (buf && len) {
+        size_t n = std::min(len - 1, t_err.size());
+        std::memcpy(buf, t_err.data(), n);
+        buf[n] = 0;
+    }
+    return t_err.size();
+}
+
+extern "C" int itts_sampling_params_validate(const itts_sampling_params *p) {
+    if (!p) return validation("params", "null pointer");
+    auto fin = [](float v) { return std::isfinite(v); };
+    if (!fin(p->temperature) || !(p->temperature >= 0.05f && p->temperature <= 2.0f))
+        return validation("temperature", "must be finite and in 0.05..=2.0, got " + std::to_string(p->temperature));
+    if (!fin(p->top_p) || !(p->top_p >= 0.01f && p->top_p <= 1.0f))
+        return validation("top_p", "must be finite and in 0.01..=1.0, got " + std::to_string(p->top_p));
+    if (p->top_k > (uint32_t)ITTS_MEL_VOCAB)
+        return validation("top_k", "must be <= 8194, got " + std::to_string(p->top_k));
+    if (!fin(p->repetition_penalty) || !(p->repetition_penalty >= 1.0f && p->repetition_penalty <= 50.0f))
+        return validation("repetition_penalty", "must be finite and in 1.0..=50.0, got " + std::to_string(p->repetition_penalty));
+    if (p->max_mel_tokens < 1 || p->max_mel_tokens > 1815)
+        return validation("max_mel_tokens", "must be in 1..=1815, got " + std::to_string(p->max_mel_tokens));
+    return ITTS_OK;
+}
+
+extern "C" uint64_t itts_rng_new(uint64_t seed) { return seed ^ 0x9E3779B97F4A7C15ULL; }
+
+extern "C" float itts_rng_next_f32(uint64_t *s) {
+    *s += 0x9E3779B97F4A7C15ULL;
+    uint64_t z = *s;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ULL;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBULL;
+    z ^= z >> 31;
+    return (float)(uint32_t)(z >> 40) * (1.0f / 16777216.0f);
+}
+
+extern "C" void itts_seen_insert(uint64_t *w, int64_t tok) {
+    if (tok < 0) return;
+    const uint64_t wi = (uint64_t)tok / 64, bi = (uint64_t)tok % 64;
+    if (wi < ITTS_BITSET_WORDS) w[wi] |= 1ULL << bi;
+}
+
+extern "C" void itts_seen_initial(uint64_t *w) {
+    std::memset(w, 0, ITTS_BITSET_WORDS * sizeof(uint64_t));
+    itts_seen_insert(w, ITTS_STOP_TEXT_TOKEN);
+    itts_seen_insert(w, ITTS_START_MEL_TOKEN);
+}
+
+// ------------------------------------------------------------------------------
+// model upload
+// ------------------------------------------------------------------------------
+namespace {
+
+struct TensorTable {
+    std::unordered_map<std::string, const itts_tensor *> by_name;
+    const itts_tensor *get(const std::string &n) const {
+        auto it = by_name.find(n);
+        return it == by_name.end() ? nullptr : it->second;
+    }
+};
+
+std::string shape_str(const itts_tensor *t) {
+    std::string s = "[";
+    for (int i = 0; i < t->ndim; ++i) s += (i ? ", " : "") + std::to_string(t->shape[i]);
+    return s + "]";
+}
+
+// tensor_array_shaped (loader.rs:316-331): presence, rank, extents.
+int expect(const TensorTable &tt, const std::string &name, std::vector<int64_t> shape,
+           const itts_tensor **out) {
+    const itts_tensor *t = tt.get(name);
+    if (!t) return weight_load("gpt_int8.safetensors", "missing tensor `" + name + "`");
+    bool ok = t->ndim == (int)shape.size();
+    for (size_t i = 0; ok && i < shape.size(); ++i) ok = t->shape[i] == shape[i];
+    if (!ok) {
+        std::string e = "[";
+        for (size_t i = 0; i < shape.size(); ++i) e += (i ? ", " : "") + std::to_string(shape[i]);
+        return weight_load(name, "shape " + shape_str(t) + " != expected " + e + "]");
+    }
+    if (!t->data) return weight_load(name, "null data pointer");
+    *out = t;
+    return ITTS_OK;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+}  // namespace
+
+static void gpt_destroy(itts_gpt *g) {
+    if (!g) return;
+    cudaSetDevice(g->device);
+    if (g->stream) cudaStreamSynchronize(g->stream);
+    for (auto &e : g->ev)
+        if (e) cudaEventDestroy(e);
+    cudaFree(g->arena);
+    cudaFree(g->d_sstate);
+    cudaFree(g->d_slogits);
+    cudaFree(g->d_sidx);
+    cudaFreeHost(g->h_sstate);
+    if (g->stream) cudaStreamDestroy(g->stream);
+    delete g;
+}
+
+extern "C" int itts_gpt_from_tensors(const itts_tensor *tensors, int32_t n_tensors, int device,
+                                     itts_gpt **out) {
+    if (!out) return validation("out", "null pointer");
+    *out = nullptr;
+    if (!tensors || n_tensors <= 0) return weight_load("gpt_int8.safetensors", "no tensors");
+    TensorTable tt;
+    for (int i = 0; i < n_tensors; ++i)
+        if (tensors[i].name) tt.by_name[tensors[i].name] = &tensors[i];
+
+    const itts_tensor *mel = tt.get("mel_embedding.weight");
+    if (!mel || mel->ndim != 2)
+        return weight_load("gpt_int8.safetensors", "missing tensor `mel_embedding.weight`");
+    const int64_t d = mel->shape[1], mel_vocab = mel->shape[0];
+    if (d <= 0 || d % 64 != 0 || d > 5120)
+        return weight_load("mel_embedding.weight", "model dim must be a positive multiple of 64, <= 5120");
+    if (mel_vocab <= ITTS_STOP_MEL_TOKEN || mel_vocab > ITTS_MAX_SAMPLE_LOGITS)
+        return weight_load("mel_embedding.weight", "mel vocabulary must hold the STOP token (8193) and be <= 16384");
+    int n_layers = 0;
+    while (tt.get("gpt.h." + std::to_string(n_layers) + ".ln_1.weight")) ++n_layers;
+    if (n_layers == 0) return weight_load("gpt_int8.safetensors", "missing tensor `gpt.h.0.ln_1.weight`");
+    const itts_tensor *fcb = tt.get("gpt.h.0.mlp.c_fc.bias");
+    if (!fcb || fcb->ndim != 1) return weight_load("gpt_int8.safetensors", "missing tensor `gpt.h.0.mlp.c_fc.bias`");
+    const int64_t ff = fcb->shape[0];
+    if (ff <= 0 || ff % 64 != 0 || ff > 5120)
+        return weight_load("gpt.h.0.mlp.c_fc.bias", "MLP dim must be a positive multiple of 64, <= 5120");
+    const itts_tensor *hs = tt.get("mel_head.scales");
+    if (!hs) return weight_load("gpt_int8.safetensors", "missing tensor `mel_head.scales`");
+    if (hs->dtype != ITTS_DTYPE_F16 && hs->dtype != ITTS_DTYPE_F32)
+        return weight_load("mel_head.scales", "scales must be F32 or F16");
+    const bool sb_half = hs->dtype == ITTS_DTYPE_F16;
+    const int sb_bytes = sb_half ? 2 : 4;
+
+    const itts_tensor *te = tt.get("text_embedding.weight");
+    const itts_tensor *le = tt.get("lang_embedding.weight");
+    const itts_tensor *mp = tt.get("mel_pos_embedding.emb.weight");
+    const itts_tensor *tp = tt.get("text_pos_embedding.emb.weight");
+    for (auto pr : {std::make_pair(te, "text_embedding.weight"), std::make_pair(le, "lang_embedding.weight"),
+                    std::make_pair(mp, "mel_pos_embedding.emb.weight"), std::make_pair(tp, "text_pos_embedding.emb.weight")})
+        if (!pr.first || pr.first->ndim != 2 || pr.first->shape[1] != d)
+            return weight_load(pr.second, pr.first ? "shape " + shape_str(pr.first) + " has the wrong model dim"
+                                                   : std::string("missing tensor"));
+
+    struct Up { const itts_tensor *t; size_t bytes; size_t off; };
+    std::vector<Up> ups;
+    auto add = [&](const itts_tensor *t, size_t bytes) { ups.push_back({t, bytes, 0}); return (int)ups.size() - 1; };
+    auto f32 = [&](const std::string &name, std::vector<int64_t> shape, int *idx) -> int {
+        const itts_tensor *t;
+        TRY(expect(tt, name, shape, &t));
+        if (t->dtype != ITTS_DTYPE_F32) return weight_load(name, "expected F32");
+        size_t n = 1;
+        for (auto s : shape) n *= (size_t)s;
+        *idx = add(t, n * 4);
+        return ITTS_OK;
+    };
+    struct LinIdx { int w, s, b, bias, out, in; };
+    auto lin = [&](const std::string &p, int64_t o, int64_t in, LinIdx *li) -> int {
+        const itts_tensor *w, *s, *b;
+        TRY(expect(tt, p + ".weight", {o, in / 4}, &w));
+        if (w->dtype != ITTS_DTYPE_U32 && w->dtype != ITTS_DTYPE_I32) return weight_load(p + ".weight", "expected U32");
+        TRY(expect(tt, p + ".scales", {o, in / 64}, &s));
+        TRY(expect(tt, p + ".biases", {o, in / 64}, &b));
+        const int want = sb_half ? ITTS_DTYPE_F16 : ITTS_DTYPE_F32;
+        if (s->dtype != want || b->dtype != want)
+            return weight_load(p + ".scales", "scales/biases must all share one dtype (F16 or F32)");
+        li->w = add(w, (size_t)o * in);
+        li->s = add(s, (size_t)o * (in / 64) * sb_bytes);
+        li->b = add(b, (size_t)o * (in / 64) * sb_bytes);
+        TRY(f32(p + ".bias", {o}, &li->bias));
+        li->out = (int)o;
+        li->in = (int)in;
+        return ITTS_OK;
+    };
+    int i_te, i_le, i_me, i_mp, i_tp, i_lfw, i_lfb, i_fnw, i_fnb;
+    TRY(f32("text_embedding.weight", {te->shape[0], d}, &i_te));
+    TRY(f32("lang_embedding.weight", {le->shape[0], d}, &i_le));
+    TRY(f32("mel_embedding.weight", {mel_vocab, d}, &i_me));
+    TRY(f32("mel_pos_embedding.emb.weight", {mp->shape[0], d}, &i_mp));
+    TRY(f32("text_pos_embedding.emb.weight", {tp->shape[0], d}, &i_tp));
+    TRY(f32("gpt.ln_f.weight", {d}, &i_lfw));
+    TRY(f32("gpt.ln_f.bias", {d}, &i_lfb));
+    TRY(f32("final_norm.weight", {d}, &i_fnw));
+    TRY(f32("final_norm.bias", {d}, &i_fnb));
+    LinIdx head;
+    TRY(lin("mel_head", mel_vocab, d, &head));
+    struct LayIdx { int l1w, l1b, l2w, l2b; LinIdx a, p, fc, mp; };
+    std::vector<LayIdx> li(n_layers);
+    for (int i = 0; i < n_layers; ++i) {
+        const std::string p = "gpt.h." + std::to_string(i);
+        TRY(f32(p + ".ln_1.weight", {d}, &li[i].l1w));
+        TRY(f32(p + ".ln_1.bias", {d}, &li[i].l1b));
+        TRY(f32(p + ".ln_2.weight", {d}, &li[i].l2w));
+        TRY(f32(p + ".ln_2.bias", {d}, &li[i].l2b));
+        TRY(lin(p + ".attn.c_attn", 3 * d, d, &li[i].a));
+        TRY(lin(p + ".attn.c_proj", d, d, &li[i].p));
+        TRY(lin(p + ".mlp.c_fc", ff, d, &li[i].fc));
+        TRY(lin(p + ".mlp.c_proj", d, ff, &li[i].mp));
+    }
+
+    itts_gpt *g = new itts_gpt();
+    g->device = device;
+    {
+        cudaError_t e = cudaSetDevice(device);
+        if (e != cudaSuccess) { delete g; return set_err(ITTS_E_CUDA, std::string("cudaSetDevice: ") + cudaGetErrorString(e)); }
+    }
+    static bool inited[64] = {false};
+    if (device >= 0 && device < 64 && !inited[device]) {
+        kernels_init_decode();
+        kernels_init_sample();
+        inited[device] = true;
+    }
+    size_t total = 0;
+    for (auto &u : ups) { u.off = total; total = align256(total + u.bytes); }
+    auto fail = [&](cudaError_t e, const char *what) {
+        std::string msg = std::string("device error: ") + what + ": " + cudaGetErrorString(e);
+        gpt_destroy(g);
+        return set_err(ITTS_E_CUDA, msg);
+    };
+    cudaError_t e;
+    if ((e = cudaStreamCreateWithFlags(&g->stream, cudaStreamNonBlocking)) != cudaSuccess) return fail(e, "stream");
+    for (auto &ev : g->ev)
+        if ((e = cudaEventCreate(&ev)) != cudaSuccess) return fail(e, "event");
+    if ((e = cudaMalloc(&g->arena, total)) != cudaSuccess) return fail(e, "weights");
+    char *base = (char *)g->arena;
+    for (auto &u : ups)
+        if ((e = cudaMemcpyAsync(base + u.off, u.t->data, u.bytes, cudaMemcpyHostToDevice, g->stream)) != cudaSuccess)
+            return fail(e, "weight upload");
+    if ((e = cudaStreamSynchronize(g->stream)) != cudaSuccess) return fail(e, "weight upload");
+    auto P = [&](int idx) { return (const void *)(base + ups[idx].off); };
+    auto F = [&](int idx) { return (const float *)(base + ups[idx].off); };
+    auto mk = [&](const LinIdx &x) {
+        QLinear q;
+        q.q = (const uint8_t *)P(x.w);
+        q.scales = P(x.s);
+        q.biases = P(x.b);
+        q.bias = F(x.bias);
+        q.out = x.out;
+        q.in = x.in;
+        return q;
+    };
+    g->layers.resize(n_layers);
+    for (int i = 0; i < n_layers; ++i) {
+        LayerW &L = g->layers[i];
+        L.ln1_w = F(li[i].l1w); L.ln1_b = F(li[i].l1b); L.ln2_w = F(li[i].l2w); L.ln2_b = F(li[i].l2b);
+        L.c_attn = mk(li[i].a); L.c_proj = mk(li[i].p); L.c_fc = mk(li[i].fc); L.mlp_proj = mk(li[i].mp);
+    }
+    ModelView &m = g->m;
+    m.n_layers = n_layers; m.d = (int)d; m.n_heads = (int)(d / 64); m.ff = (int)ff;
+    m.mel_vocab = (int)mel_vocab; m.text_vocab = (int)te->shape[0]; m.lang_vocab = (int)le->shape[0];
+    m.mel_pos_len = (int)mp->shape[0]; m.text_pos_len = (int)tp->shape[0];
+    m.sb_half = sb_half;
+    m.text_emb = F(i_te); m.lang_emb = F(i_le); m.mel_emb = F(i_me); m.mel_pos = F(i_mp); m.text_pos = F(i_tp);
+    m.ln_f_w = F(i_lfw); m.ln_f_b = F(i_lfb); m.final_w = F(i_fnw); m.final_b = F(i_fnb);
+    m.mel_head = mk(head);
+    m.layers = g->layers.data();
+    if ((e = cudaMalloc(&g->d_sstate, sizeof(SlotState))) != cudaSuccess) return fail(e, "scratch");
+    if ((e = cudaMalloc(&g->d_slogits, ITTS_MAX_SAMPLE_LOGITS * sizeof(float))) != cudaSuccess) return fail(e, "scratch");
+    if ((e = cudaMalloc(&g->d_sidx, 2 * sizeof(int))) != cudaSuccess) return fail(e, "scratch");
+    if ((e = cudaMallocHost(&g->h_sstate, sizeof(SlotState) + 64)) != cudaSuccess) return fail(e, "pinned");
+    *out = g;
+    return ITTS_OK;
+}
+
+// ------------------------------------------------------------------------------
+// safetensors (the format gpt_int8.safetensors uses): u64 header length, JSON
+// header {name: {dtype, shape, data_offsets}}, raw little-endian data.
+// ------------------------------------------------------------------------------
+namespace {
+struct JsonCursor {
+    const char *p, *e;
+    void ws() { while (p < e && (*p == ' ' || *p == '\n' || *p == '\r' || *p == '\t')) ++p; }
+    bool lit(char c) { ws(); if (p < e && *p == c) { ++p; return true; } return false; }
+    bool str(std::string &s) {
+        ws();
+        if (p >= e || *p != '"') return false;
+        ++p;
+        s.clear();
+        while (p < e && *p != '"') {
+            if (*p == '\\' && p + 1 < e) { s.push_back(p[1]); p += 2; } else s.push_back(*p++);
+        }
+        if (p >= e) return false;
+        ++p;
+        return true;
+    }
+    bool num(int64_t &v) {
+        ws();
+        char *end = nullptr;
+        v = strtoll(p, &end, 10);
+        if (end == p) return false;
+        p = end;
+        return true;
+    }
+    bool skip() {  // skip any JSON value
+        ws();
+        if (p >= e) return false;
+        if (*p == '"') { std::string s; return str(s); }
+        if (*p == '{' || *p == '[') {
+            const char open = *p, close = open == '{' ? '}' : ']';
+            ++p;
+            if (lit(close)) return true;
+            for (;;) {
+                if (open == '{') { std::string k; if (!str(k) || !lit(':')) return false; }
+                if (!skip()) return false;
+                if (lit(',')) continue;
+                return lit(close);
+            }
+        }
+        while (p < e && *p != ',' && *p != '}' && *p != ']') ++p;
+        return true;
+    }
+};
+}  // namespace
+
+extern "C" int itts_gpt_load(const char *path, int device, itts_gpt **out) {
+    if (!out) return validation("out", "null pointer");
+    *out = nullptr;
+    if (!path) return validation("path", "null pointer");
+    const int fd = open(path, O_RDONLY);
+    if (fd < 0) return set_err(ITTS_E_IO, std::string("I/O error at `") + path + "`: " + strerror(errno));
+    struct stat sb;
+    if (fstat(fd, &sb) != 0 || sb.st_size < 8) { close(fd); return weight_load(path, "file too small"); }
+    const size_t size = (size_t)sb.st_size;
+    void *map = mmap(nullptr, size, PROT_READ, MAP_PRIVATE, fd, 0);
+    close(fd);
+    if (map == MAP_FAILED) return set_err(ITTS_E_IO, std::string("I/O error at `") + path + "`: mmap failed");
+    const unsigned char *bytes = (const unsigned char *)map;
+    uint64_t hlen = 0;
+    std::memcpy(&hlen, bytes, 8);
+    int rc = ITTS_OK;
+    std::vector<itts_tensor> ts;
+    std::vector<std::string> names;
+    if (hlen > size - 8) {
+        rc = weight_load(path, "invalid header length");
+    } else {
+        JsonCursor c{(const char *)bytes + 8, (const char *)bytes + 8 + hlen};
+        const unsigned char *data = bytes + 8 + hlen;
+        const size_t data_len = size - 8 - hlen;
+        if (!c.lit('{')) rc = weight_load(path, "invalid header");
+        while (rc == ITTS_OK && !c.lit('}')) {
+            std::string key;
+            if (!c.str(key) || !c.lit(':')) { rc = weight_load(path, "invalid header"); break; }
+            if (key == "__metadata__") {
+                if (!c.skip()) rc = weight_load(path, "invalid header");
+            } else {
+                itts_tensor t{};
+                std::string dtype;
+                int64_t off0 = -1, off1 = -1;
+                if (!c.lit('{')) { rc = weight_load(path, "invalid header"); break; }
+                while (rc == ITTS_OK && !c.lit('}')) {
+                    std::string f;
+                    if (!c.str(f) || !c.lit(':')) { rc = weight_load(path, "invalid header"); break; }
+                    if (f == "dtype") {
+                        if (!c.str(dtype)) rc = weight_load(path, "invalid dtype");
+                    } else if (f == "shape") {
+                        if (!c.lit('[')) { rc = weight_load(path, "invalid shape"); break; }
+                        while (!c.lit(']')) {
+                            int64_t v;
+                            if (!c.num(v) || t.ndim >= 4) { rc = weight_load(path, "invalid shape"); break; }
+                            t.shape[t.ndim++] = v;
+                            c.lit(',');
+                        }
+                    } else if (f == "data_offsets") {
+                        if (!c.lit('[') || !c.num(off0) || !c.lit(',') || !c.num(off1) || !c.lit(']'))
+                            rc = weight_load(path, "invalid data_offsets");
+                    } else if (!c.skip()) {
+                        rc = weight_load(path, "invalid header");
+                    }
+                    c.lit(',');
+                }
+                if (rc != ITTS_OK) break;
+                if (dtype == "F32") t.dtype = ITTS_DTYPE_F32;
+                else if (dtype == "F16") t.dtype = ITTS_DTYPE_F16;
+                else if (dtype == "U32") t.dtype = ITTS_DTYPE_U32;
+                else if (dtype == "I32") t.dtype = ITTS_DTYPE_I32;
+                else t.dtype = -1;  // other tensors are ignored unless the decoder needs them
+                if (off0 < 0 || off1 < off0 || (size_t)off1 > data_len) { rc = weight_load(key, "data offsets out of range"); break; }
+                int64_t n = 1;
+                for (int i = 0; i < t.ndim; ++i) n *= t.shape[i];
+                const int es = t.dtype == ITTS_DTYPE_F16 ? 2 : 4;
+                if (t.dtype >= 0 && n * es != off1 - off0) { rc = weight_load(key, "byte size does not match shape"); break; }
+                t.data = data + off0;
+                names.push_back(key);
+                ts.push_back(t);
+            }
+            c.lit(',');
+        }
+    }
+    if (rc == ITTS_OK) {
+        for (size_t i = 0; i < ts.size(); ++i) ts[i].name = names[i].c_str();
+        rc = itts_gpt_from_tensors(ts.data(), (int32_t)ts.size(), device, out);
+    }
+    munmap(map, size);
+    return rc;
+}
+
+extern "C" void itts_gpt_free(itts_gpt *g) { gpt_destroy(g); }
+
+extern "C" int32_t itts_gpt_num_layers(const itts_gpt *g) { return g ? g->m.n_layers : 0; }
+
+extern "C" int itts_gpt_dims(const itts_gpt *g, int32_t dims[10]) {
+    if (!g || !dims) return validation("gpt", "null pointer");
+    const ModelView &m = g->m;
+    int32_t v[10] = {m.n_layers, m.d, m.n_heads, m.ff, m.mel_vocab, m.text_vocab, m.mel_pos_len,
+                     m.text_pos_len, m.lang_vocab, m.sb_half ? 1 : 0};
+    std::memcpy(dims, v, sizeof v);
+    return ITTS_OK;
+}
+
+// ------------------------------------------------------------------------------
+// KV cache
+// ------------------------------------------------------------------------------
+static void kv_destroy(itts_kv *kv) {
+    if (!kv) return;
+    cudaSetDevice(kv->gpt->device);
+    cudaStreamSynchronize(kv->gpt->stream);
+    for (auto g : kv->graphs)
+        if (g) cudaGraphExecDestroy(g);
+    for (auto g : kv->graph_defs)
+        if (g) cudaGraphDestroy(g);
+    void *dev[] = {kv->k, kv->v, kv->d_slots, kv->d_batch_slot, kv->db.x, kv->db.q, kv->db.attn,
+                   kv->db.u, kv->db.logits, kv->db.partials, kv->db.counters, kv->pb.x, kv->pb.n,
+                   kv->pb.qkv, kv->pb.attn, kv->pb.u, kv->d_codes, kv->d_text, kv->d_prior, kv->d_conds};
+    for (void *p : dev) cudaFree(p);
+    cudaFreeHost(kv->h_pinned);
+    cudaFreeHost(kv->h_i32);
+    cudaFreeHost(kv->h_f32);
+    delete kv;
+}
+
+static SlotState blank_slot(int max_seq) {
+    SlotState s;
+    std::memset(&s, 0, sizeof s);
+    s.max_seq = max_seq;
+    s.temperature = 0.8f;
+    s.top_p = 0.8f;
+    s.rep_penalty = 1.0f;
+    return s;
+}
+
+extern "C" int itts_kv_create(itts_gpt *g, int32_t max_seq, int32_t max_batch, itts_kv **out) {
+    if (!out) return validation("out", "null pointer");
+    *out = nullptr;
+    if (!g) return validation("gpt", "null pointer");
+    if (max_seq <= 0) return validation("max_seq", "KV cache max_seq must be >= 1");
+    if (max_batch <= 0) return validation("max_batch", "must be >= 1");
+    CUDA_TRY(cudaSetDevice(g->device));
+    const ModelView &m = g->m;
+    itts_kv *kv = new itts_kv();
+    kv->gpt = g;
+    kv->max_seq = max_seq;
+    kv->max_batch = max_batch;
+    kv->db.split_len = 128;
+    kv->db.max_splits = (max_seq + kv->db.split_len - 1) / kv->db.split_len;
+    kv->pb.max_tokens = max_seq;
+    kv->codes_stride = m.mel_pos_len;
+    kv->max_conds = max_seq;
+    const size_t kv_elems = (size_t)m.n_layers * max_batch * m.n_heads * max_seq * kHeadDim;
+    cudaError_t e = cudaSuccess;
+    auto A = [&](void **p, size_t bytes) { if (e == cudaSuccess) e = cudaMalloc(p, bytes); };
+    A((void **)&kv->k, kv_elems * 2);
+    A((void **)&kv->v, kv_elems * 2);
+    A((void **)&kv->d_slots, sizeof(SlotState) * max_batch);
+    A((void **)&kv->d_batch_slot, sizeof(int) * max_batch);
+    A((void **)&kv->db.x, sizeof(float) * max_batch * m.d);
+    A((void **)&kv->db.q, sizeof(float) * max_batch * m.d);
+    A((void **)&kv->db.attn, sizeof(float) * max_batch * m.d);
+    A((void **)&kv->db.u, sizeof(float) * max_batch * m.ff);
+    A((void **)&kv->db.logits, sizeof(float) * max_batch * m.mel_vocab);
+    A((void **)&kv->db.partials, sizeof(float) * max_batch * m.n_heads * kv->db.max_splits * 66);
+    A((void **)&kv->db.counters, sizeof(int) * max_batch * m.n_heads);
+    A((void **)&kv->pb.x, sizeof(float) * (size_t)max_seq * m.d);
+    A((void **)&kv->pb.n, sizeof(float) * (size_t)max_seq * m.d);
+    A((void **)&kv->pb.qkv, sizeof(float) * (size_t)max_seq * 3 * m.d);
+    A((void **)&kv->pb.attn, sizeof(float) * (size_t)max_seq * m.d);
+    A((void **)&kv->pb.u, sizeof(float) * (size_t)max_seq * m.ff);
+    A((void **)&kv->d_codes, sizeof(int32_t) * max_batch * kv->codes_stride);
+    A((void **)&kv->d_text, sizeof(int) * (m.text_pos_len + 2));
+    A((void **)&kv->d_prior, sizeof(int) * (m.mel_pos_len + 2));
+    A((void **)&kv->d_conds, sizeof(float) * (size_t)max_seq * m.d);
+    if (e == cudaSuccess) e = cudaMallocHost((void **)&kv->h_pinned, sizeof(SlotState) * max_batch);
+    if (e == cudaSuccess) e = cudaMallocHost((void **)&kv->h_i32, sizeof(int32_t) * (m.text_pos_len + m.mel_pos_len + 4 * max_batch + 8));
+    kv->h_f32_cap = (size_t)max_seq * m.d;
+    if (e == cudaSuccess) e = cudaMallocHost((void **)&kv->h_f32, sizeof(float) * kv->h_f32_cap);
+    if (e == cudaSuccess) e = cudaMemsetAsync(kv->db.counters, 0, sizeof(int) * max_batch * m.n_heads, g->stream);
+    kv->h_state.assign(max_batch, blank_slot(max_seq));
+    if (e == cudaSuccess) {
+        std::memcpy(kv->h_pinned, kv->h_state.data(), sizeof(SlotState) * max_batch);
+        e = cudaMemcpyAsync(kv->d_slots, kv->h_pinned, sizeof(SlotState) * max_batch, cudaMemcpyHostToDevice, g->stream);
+    }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(g->stream);
+    if (e != cudaSuccess) {
+        std::string msg = std::string("device error: KV cache allocation: ") + cudaGetErrorString(e);
+        kv_destroy(kv);
+        return set_err(ITTS_E_CUDA, msg);
+    }
+    kv->graphs.assign(max_batch + 1, nullptr);
+    kv->graph_defs.assign(max_batch + 1, nullptr);
+    *out = kv;
+    return ITTS_OK;
+}
+
+extern "C" void itts_kv_free(itts_kv *kv) { kv_destroy(kv); }
+
+extern "C" int itts_kv_reset(itts_kv *kv, int32_t slot) {
+    if (!kv) return validation("kv", "null pointer");
+    if (slot >= kv->max_batch) return validation("slot", "out of range");
+    for (int s = 0; s < kv->max_batch; ++s)
+        if (slot < 0 || s == slot) kv->h_state[s].valid_len = 0;
+    return ITTS_OK;
+}
+
+extern "C" int itts_kv_valid_len(const itts_kv *kv, int32_t slot, int32_t *out) {
+    if (!kv || !out) return validation("kv", "null pointer");
+    if (slot < 0 || slot >= kv->max_batch) return validation("slot", "out of range");
+    *out = kv->h_state[slot].valid_len;
+    return ITTS_OK;
+}
+
+extern "C" int32_t itts_kv_max_seq(const itts_kv *kv) { return kv ? kv->max_seq : 0; }
+extern "C" int32_t itts_kv_max_batch(const itts_kv *kv) { return kv ? kv->max_batch : 0; }
+
+static DecodeView decode_view(itts_kv *kv, int nb) {
+    const ModelView &m = kv->gpt->m;
+    DecodeView dv;
+    dv.slots = kv->d_slots;
+    dv.batch_slot = kv->d_batch_slot;
+    dv.nb = nb;
+    dv.n_slots = kv->max_batch;
+    dv.n_heads = m.n_heads;
+    dv.max_seq = kv->max_seq;
+    dv.d = m.d;
+    dv.k_cache = kv->k;
+    dv.v_cache = kv->v;
+    return dv;
+}
+
+// Pushes the host mirror of `slots` to the device.
+static int push_slots(itts_kv *kv, const int *slots, int n) {
+    cudaStream_t st = kv->gpt->stream;
+    CUDA_TRY(cudaStreamSynchronize(st));  // staging buffer reuse
+    for (int i = 0; i < n; ++i) {
+        kv->h_pinned[i] = kv->h_state[slots[i]];
+    }
+    for (int i = 0; i < n; ++i)
+        CUDA_TRY(cudaMemcpyAsync(kv->d_slots + slots[i], kv->h_pinned + i, sizeof(SlotState),
+                                 cudaMemcpyHostToDevice, st));
+    return ITTS_OK;
+}
+
+static int pull_slots(itts_kv *kv, const int *slots, int n) {
+    cudaStream_t st = kv->gpt->stream;
+    for (int i = 0; i < n; ++i)
+        CUDA_TRY(cudaMemcpyAsync(kv->h_pinned + i, kv->d_slots + slots[i], sizeof(SlotState),
+                                 cudaMemcpyDeviceToHost, st));
+    CUDA_TRY(cudaStreamSynchronize(st));
+    for (int i = 0; i < n; ++i) kv->h_state[slots[i]] = kv->h_pinned[i];
+    return ITTS_OK;
+}
+
+static int set_batch_slots(itts_kv *kv, const int *slots, int n) {
+    cudaStream_t st = kv->gpt->stream;
+    CUDA_TRY(cudaStreamSynchronize(st));
+    int32_t *h = kv->h_i32;
+    for (int i = 0; i < n; ++i) h[i] = slots[i];
+    CUDA_TRY(cudaMemcpyAsync(kv->d_batch_slot, h, sizeof(int) * n, cudaMemcpyHostToDevice, st));
+    CUDA_TRY(cudaStreamSynchronize(st));
+    return ITTS_OK;
+}
+
+// ------------------------------------------------------------------------------
+// prefill (gpt.rs:535-627, 655-696)
+// ------------------------------------------------------------------------------
+static int validate_prompt(const ModelView &m, const int32_t *text, int n_text, const float *conds,
+                           int n_conds, int lang, const int32_t *prior, int n_prior, int max_seq,
+                           int *T_out) {
+    if (!text || n_text <= 0) return validation("text_tokens", "text_tokens must not be empty");
+    if (n_prior < 0 || (n_prior > 0 && !prior)) return validation("codes", "invalid prior codes");
+    if (n_prior + 3 > m.mel_pos_len)
+        return validation("codes", std::to_string(n_prior) + " codes exceed the Mel positional capacity");
+    const int full = n_text + 2;
+    if (full > m.text_pos_len)
+        return validation("text_tokens", "text sequence length " + std::to_string(full) + " exceeds " + std::to_string(m.text_pos_len));
+    if (!conds || n_conds <= 0) return validation("conds", "expected at least one conditioning row of width " + std::to_string(m.d));
+    if (lang < 0 || lang >= m.lang_vocab)
+        return validation("lang_id", "lang_id " + std::to_string(lang) + " out of range 0.." + std::to_string(m.lang_vocab));
+    for (int i = 0; i < n_text; ++i)
+        if (text[i] < 0 || text[i] >= m.text_vocab)
+            return validation("text_tokens", "token id " + std::to_string(text[i]) + " out of range");
+    for (int i = 0; i < n_prior; ++i)
+        if (prior[i] < 0 || prior[i] >= m.mel_vocab)
+            return validation("codes", "code " + std::to_string(prior[i]) + " out of range");
+    const int T = n_conds + full + 1 + n_prior;
+    if (T > max_seq)
+        return validation("kv_cache", "sequence length " + std::to_string(T) + " exceeds KV cache capacity " + std::to_string(max_seq));
+    *T_out = T;
+    return ITTS_OK;
+}
+
+static int prefill_impl(itts_gpt *g, itts_kv *kv, int slot, const int32_t *text, int n_text,
+                        const float *conds, int n_conds, int lang, const int32_t *prior,
+                        int n_prior, float *d_logits_row) {
+    const ModelView &m = g->m;
+    int T = 0;
+    TRY(validate_prompt(m, text, n_text, conds, n_conds, lang, prior, n_prior, kv->max_seq, &T));
+    cudaStream_t st = g->stream;
+    CUDA_TRY(cudaStreamSynchronize(st));  // staging reuse
+    int32_t *h = kv->h_i32;
+    h[0] = kStartText;
+    for (int i = 0; i < n_text; ++i) h[1 + i] = text[i];
+    h[n_text + 1] = kStopText;
+    int32_t *hp = h + n_text + 2;
+    for (int i = 0; i < n_prior; ++i) hp[i] = prior[i];
+    const size_t nc = (size_t)n_conds * m.d;
+    if (nc > kv->h_f32_cap) return validation("conds", "too many conditioning rows for this KV cache");
+    std::memcpy(kv->h_f32, conds, nc * sizeof(float));
+    CUDA_TRY(cudaMemcpyAsync(kv->d_text, h, sizeof(int) * (n_text + 2), cudaMemcpyHostToDevice, st));
+    if (n_prior)
+        CUDA_TRY(cudaMemcpyAsync(kv->d_prior, hp, sizeof(int) * n_prior, cudaMemcpyHostToDevice, st));
+    CUDA_TRY(cudaMemcpyAsync(kv->d_conds, kv->h_f32, nc * sizeof(float), cudaMemcpyHostToDevice, st));
+    launch_embed_prefix(m, kv->d_text, n_text + 2, kv->d_conds, n_conds, lang, kv->d_prior, n_prior,
+                        kv->pb.x, st);
+    DecodeView dv = decode_view(kv, 1);
+    prefill_forward(m, dv, slot, T, kv->pb, d_logits_row, st);
+    CUDA_TRY(cudaGetLastError());
+    kv->h_state[slot].valid_len = T;
+    return ITTS_OK;
+}
+
+extern "C" int itts_gpt_prefill(itts_gpt *g, itts_kv *kv, int32_t slot, const int32_t *text,
+                                int32_t n_text, const float *conds, int32_t n_conds, int32_t lang,
+                                const int32_t *prior, int32_t n_prior, float *logits_out) {
+    if (!g || !kv || kv->gpt != g) return validation("gpt", "null pointer or cache of another model");
+    if (slot < 0 || slot >= kv->max_batch) return validation("slot", "out of range");
+    CUDA_TRY(cudaSetDevice(g->device));
+    kv->h_state[slot].valid_len = 0;  // cache.reset() (gpt.rs:664)
+    TRY(prefill_impl(g, kv, slot, text, n_text, conds, n_conds, lang, prior, n_prior,
+                     kv->db.logits + (size_t)slot * g->m.mel_vocab));
+    TRY(push_slots(kv, &slot, 1));
+    if (logits_out)
+        CUDA_TRY(cudaMemcpyAsync(logits_out, kv->db.logits + (size_t)slot * g->m.mel_vocab,
+                                 sizeof(float) * g->m.mel_vocab, cudaMemcpyDeviceToHost, g->stream));
+    CUDA_TRY(cudaStreamSynchronize(g->stream));
+    return ITTS_OK;
+}
+
+// ------------------------------------------------------------------------------
+// step (gpt.rs:706-754), batched over distinct slots
+// ------------------------------------------------------------------------------
+extern "C" int itts_gpt_step(itts_gpt *g, itts_kv *kv, int32_t n, const int32_t *slots,
+                             const int32_t *toks, const int32_t *pos, float *logits_out) {
+    if (!g || !kv || kv->gpt != g) return validation("gpt", "null pointer or cache of another model");
+    if (n <= 0 || n > kv->max_batch || !slots || !toks || !pos) return validation("n", "batch size out of range");
+    const ModelView &m = g->m;
+    std::vector<char> seen_slot(kv->max_batch, 0);
+    for (int i = 0; i < n; ++i) {
+        if (slots[i] < 0 || slots[i] >= kv->max_batch || seen_slot[slots[i]]) return validation("slots", "slots must be distinct and in range");
+        seen_slot[slots[i]] = 1;
+        if (toks[i] < 0 || toks[i] >= m.mel_vocab)
+            return validation("mel_token_id", "mel_token_id " + std::to_string(toks[i]) + " out of range 0.." + std::to_string(m.mel_vocab));
+        if (pos[i] < 0 || pos[i] >= m.mel_pos_len)
+            return validation("pos_idx", "pos_idx " + std::to_string(pos[i]) + " out of range 0.." + std::to_string(m.mel_pos_len));
+        if (kv->h_state[slots[i]].valid_len + 1 > kv->max_seq)
+            return validation("kv_cache", "sequence length " + std::to_string(kv->h_state[slots[i]].valid_len + 1) +
+                                              " exceeds KV cache capacity " + std::to_string(kv->max_seq));
+    }
+    CUDA_TRY(cudaSetDevice(g->device));
+    for (int i = 0; i < n; ++i) {
+        SlotState &s = kv->h_state[slots[i]];
+        s.tok = toks[i];
+        s.pos = pos[i];
+        s.active = 1;
+        s.max_seq = kv->max_seq;
+    }
+    TRY(push_slots(kv, slots, n));
+    TRY(set_batch_slots(kv, slots, n));
+    DecodeView dv = decode_view(kv, n);
+    decode_forward(m, dv, kv->db, g->stream);
+    CUDA_TRY(cudaGetLastError());
+    for (int i = 0; i < n; ++i) kv->h_state[slots[i]].valid_len += 1;
+    TRY(push_slots(kv, slots, n));
+    if (logits_out)
+        CUDA_TRY(cudaMemcpyAsync(logits_out, kv->db.logits, sizeof(float) * n * m.mel_vocab,
+                                 cudaMemcpyDeviceToHost, g->stream));
+    CUDA_TRY(cudaStreamSynchronize(g->stream));
+    return ITTS_OK;
+}
+
+// ------------------------------------------------------------------------------
+// sampler (sampler.rs:191-284)
+// ------------------------------------------------------------------------------
+static void fill_params(SlotState &s, const itts_sampling_params *p) {
+    s.greedy = p->greedy ? 1 : 0;
+    s.top_k = p->top_k;
+    s.top_p = p->top_p;
+    s.temperature = p->temperature;
+    s.rep_penalty = p->repetition_penalty;
+}
+
+extern "C" int itts_sample_next_token(itts_gpt *g, float *logits, int32_t n,
+                                      const uint64_t *seen, const itts_sampling_params *params,
+                                      uint64_t *rng_state, int32_t *token_out) {
+    if (!g || !logits || !seen || !rng_state || !token_out) return validation("logits", "null pointer");
+    if (n <= 0) return validation("logits", "logits slice must not be empty");
+    if (n > ITTS_MAX_SAMPLE_LOGITS) return validation("logits", "at most 16384 logits");
+    TRY(itts_sampling_params_validate(params));
+    CUDA_TRY(cudaSetDevice(g->device));
+    cudaStream_t st = g->stream;
+    SlotState &s = *g->h_sstate;
+    s = blank_slot(0x7FFFFFFF);
+    fill_params(s, params);
+    s.active = 1;
+    s.max_steps = 0x7FFFFFFF;
+    s.rng = *rng_state;
+    std::memcpy(s.seen, seen, sizeof(s.seen));
+    int *hidx = reinterpret_cast<int *>(reinterpret_cast<char *>(g->h_sstate) + sizeof(SlotState));
+    hidx[0] = 0;
+    CUDA_TRY(cudaMemcpyAsync(g->d_sstate, &s, sizeof(SlotState), cudaMemcpyHostToDevice, st));
+    CUDA_TRY(cudaMemcpyAsync(g->d_sidx, hidx, sizeof(int), cudaMemcpyHostToDevice, st));
+    CUDA_TRY(cudaMemcpyAsync(g->d_slogits, logits, sizeof(float) * n, cudaMemcpyHostToDevice, st));
+    SampleArgs a{};
+    a.slots = g->d_sstate;
+    a.batch_slot = g->d_sidx;
+    a.nb = 1;
+    a.logits = g->d_slogits;
+    a.ld_logits = n;
+    a.n_logits = n;
+    a.after_forward = 0;
+    a.write_back = 1;
+    a.codes = nullptr;
+    a.token_out = g->d_sidx + 1;
+    launch_sample(a, st);
+    CUDA_TRY(cudaGetLastError());
+    CUDA_TRY(cudaMemcpyAsync(logits, g->d_slogits, sizeof(float) * n, cudaMemcpyDeviceToHost, st));
+    CUDA_TRY(cudaMemcpyAsync(&s, g->d_sstate, sizeof(SlotState), cudaMemcpyDeviceToHost, st));
+    CUDA_TRY(cudaMemcpyAsync(hidx + 1, g->d_sidx + 1, sizeof(int), cudaMemcpyDeviceToHost, st));
+    CUDA_TRY(cudaStreamSynchronize(st));
+    *rng_state = s.rng;
+    *token_out = hidx[1];
+    return ITTS_OK;
+}
+
+// ------------------------------------------------------------------------------
+// decode loop (sampler.rs:340-392): prefill every request, sample, then replay the
+// captured decode step until every request stopped.
+// ------------------------------------------------------------------------------
+static int get_graph(itts_kv *kv, int nb, cudaGraphExec_t *out) {
+    if (kv->graphs[nb]) { *out = kv->graphs[nb]; return ITTS_OK; }
+    itts_gpt *g = kv->gpt;
+    cudaStream_t st = g->stream;
+    cudaGraph_t graph = nullptr;
+    CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+    DecodeView dv = decode_view(kv, nb);
+    decode_forward(g->m, dv, kv->db, st);
+    SampleArgs a{};
+    a.slots = kv->d_slots;
+    a.batch_slot = kv->d_batch_slot;
+    a.nb = nb;
+    a.logits = kv->db.logits;
+    a.ld_logits = g->m.mel_vocab;
+    a.n_logits = g->m.mel_vocab;
+    a.after_forward = 1;
+    a.write_back = 0;
+    a.codes = kv->d_codes;
+    a.codes_stride = kv->codes_stride;
+    launch_sample(a, st);
+    CUDA_TRY(cudaStreamEndCapture(st, &graph));
+    cudaGraphExec_t exec = nullptr;
+    CUDA_TRY(cudaGraphInstantiate(&exec, graph, 0));
+    kv->graph_defs[nb] = graph;
+    kv->graphs[nb] = exec;
+    *out = exec;
+    return ITTS_OK;
+}
+
+static int generate_impl(itts_gpt *g, itts_kv *kv, int n, const int *slots,
+                         const itts_code_prompt *prompts, const itts_sampling_params *params,
+                         int params_stride, uint64_t *rngs, int32_t *codes_out, int stride,
+                         int32_t *n_out) {
+    const ModelView &m = g->m;
+    if (n <= 0 || n > kv->max_batch) return validation("n_req", "batch size out of range");
+    std::vector<int> max_steps(n), Ts(n);
+    int max_replays = 0;
+    for (int r = 0; r < n; ++r) {
+        const itts_sampling_params *p = params + (size_t)r * params_stride;
+        TRY(itts_sampling_params_validate(p));
+        const itts_code_prompt &pr = prompts[r];
+        const int cap = std::max(0, m.mel_pos_len - 3 - pr.n_prior);
+        max_steps[r] = std::min((int)p->max_mel_tokens, cap);  // sampler.rs:348-349
+        if (max_steps[r] == 0)
+            return validation("max_mel_tokens", "no Mel positions left to generate (max_mel_tokens is 0 or the prior codes fill the capacity)");
+        if (stride < max_steps[r]) return validation("codes_out", "buffer smaller than the step limit");
+        TRY(validate_prompt(m, pr.text_tokens, pr.n_text, pr.conds, pr.n_conds, pr.lang_id,
+                            pr.prior_codes, pr.n_prior, kv->max_seq, &Ts[r]));
+        max_replays = std::max(max_replays, max_steps[r] - 1);
+    }
+    CUDA_TRY(cudaSetDevice(g->device));
+    cudaStream_t st = g->stream;
+    CUDA_TRY(cudaEventRecord(g->ev[0], st));
+    for (int r = 0; r < n; ++r) {
+        const itts_code_prompt &pr = prompts[r];
+        kv->h_state[slots[r]].valid_len = 0;
+        TRY(prefill_impl(g, kv, slots[r], pr.text_tokens, pr.n_text, pr.conds, pr.n_conds,
+                         pr.lang_id, pr.prior_codes, pr.n_prior, kv->db.logits + (size_t)r * m.mel_vocab));
+    }
+    CUDA_TRY(cudaEventRecord(g->ev[1], st));
+    for (int r = 0; r < n; ++r) {
+        SlotState s = blank_slot(kv->max_seq);
+        fill_params(s, params + (size_t)r * params_stride);
+        s.valid_len = Ts[r];
+        s.active = 1;
+        s.max_steps = max_steps[r];
+        s.min_codes = prompts[r].min_codes;
+        s.n_prior = prompts[r].n_prior;
+        s.rng = rngs[r];
+        itts_seen_initial(s.seen);  // sampler.rs:368: prior codes are not penalised
+        kv->h_state[slots[r]] = s;
+    }
+    TRY(push_slots(kv, slots, n));
+    TRY(set_batch_slots(kv, slots, n));
+    cudaGraphExec_t graph;
+    TRY(get_graph(kv, n, &graph));
+    SampleArgs a{};
+    a.slots = kv->d_slots;
+    a.batch_slot = kv->d_batch_slot;
+    a.nb = n;
+    a.logits = kv->db.logits;
+    a.ld_logits = m.mel_vocab;
+    a.n_logits = m.mel_vocab;
+    a.after_forward = 0;
+    a.write_back = 0;
+    a.codes = kv->d_codes;
+    a.codes_stride = kv->codes_stride;
+    launch_sample(a, st);
+    CUDA_TRY(cudaGetLastError());
+    int launched = 0, chunk = 8;
+    for (;;) {
+        TRY(pull_slots(kv, slots, n));
+        bool any = false;
+        for (int r = 0; r < n; ++r) any |= kv->h_state[slots[r]].active != 0;
+        if (!any || launched >= max_replays) break;
+        const int todo = std::min(chunk, max_replays - launched);
+        for (int i = 0; i < todo; ++i) CUDA_TRY(cudaGraphLaunch(graph, st));
+        launched += todo;
+        chunk = std::min(chunk * 2, 64);
+    }
+    CUDA_TRY(cudaEventRecord(g->ev[2], st));
+    int err_slot = -1;
+    for (int r = 0; r < n; ++r) {
+        SlotState &s = kv->h_state[slots[r]];
+        if (s.error && err_slot < 0) err_slot = r;
+        rngs[r] = s.rng;
+        n_out[r] = s.n_codes;
+        s.active = 0;
+        if (s.n_codes > 0)
+            CUDA_TRY(cudaMemcpyAsync(codes_out + (size_t)r * stride,
+                                     kv->d_codes + (size_t)slots[r] * kv->codes_stride,
+                                     sizeof(int32_t) * s.n_codes, cudaMemcpyDeviceToHost, st));
+    }
+    CUDA_TRY(cudaStreamSynchronize(st));
+    CUDA_TRY(cudaEventElapsedTime(&g->last_prefill_ms, g->ev[0], g->ev[1]));
+    CUDA_TRY(cudaEventElapsedTime(&g->last_decode_ms, g->ev[1], g->ev[2]));
+    g->last_launches = launched;
+    if (err_slot >= 0) {
+        const SlotState &s = kv->h_state[slots[err_slot]];
+        return validation("kv_cache", "sequence length " + std::to_string(s.valid_len + 1) +
+                                          " exceeds KV cache capacity " + std::to_string(kv->max_seq));
+    }
+    return ITTS_OK;
+}
+
+extern "C" int itts_generate_codes_after(itts_gpt *g, itts_kv *kv, int32_t slot,
+                                         const itts_code_prompt *prompt,
+                                         const itts_sampling_params *params, uint64_t *rng_state,
+                                         int32_t *codes_out, int32_t max_codes,
+                                         int32_t *n_codes_out) {
+    if (!g || !kv || kv->gpt != g || !prompt || !params || !rng_state || !codes_out || !n_codes_out)
+        return validation("gpt", "null pointer or cache of another model");
+    if (slot < 0 || slot >= kv->max_batch) return validation("slot", "out of range");
+    int s = slot;
+    return generate_impl(g, kv, 1, &s, prompt, params, 0, rng_state, codes_out, max_codes, n_codes_out);
+}
+
+extern "C" int itts_generate_batch(itts_gpt *g, itts_kv *kv, int32_t n_req,
+                                   const itts_code_prompt *prompts,
+                                   const itts_sampling_params *params, uint64_t *rng_states,
+                                   int32_t *codes_out, int32_t codes_stride, int32_t *n_codes_out) {
+    if (!g || !kv || kv->gpt != g || !prompts || !params || !rng_states || !codes_out || !n_codes_out)
+        return validation("gpt", "null pointer or cache of another model");
+    if (n_req <= 0 || n_req > kv->max_batch) return validation("n_req", "batch size out of range");
+    std::vector<int> slots(n_req);
+    for (int i = 0; i < n_req; ++i) slots[i] = i;
+    return generate_impl(g, kv, n_req, slots.data(), prompts, params, 1, rng_states, codes_out,
+                         codes_stride, n_codes_out);
+}
+
+extern "C" int itts_gpt_last_timing(const itts_gpt *g, float *prefill_ms, float *decode_ms,
+                                    int32_t *launches) {
+    if (!g) return validation("gpt", "null pointer");
+    if (prefill_ms) *prefill_ms = g->last_prefill_ms;
+    if (decode_ms) *decode_ms = g->last_decode_ms;
+    if (launches) *launches = g->last_launches;
+    return ITTS_OK;
+}
+
+// ------------------------------------------------------------------------------
+// measurement: the weight-streaming kernels of one decode step, replayed
+// ------------------------------------------------------------------------------
+extern "C" int itts_bench_weight_stream(itts_gpt *g, itts_kv *kv, int32_t nb, int32_t iters,
+                                        float *ms, int32_t *launches) {
+    if (!g || !kv || kv->gpt != g || !ms) return validation("gpt", "null pointer");
+    if (nb <= 0 || nb > kv->max_batch || iters <= 0) return validation("nb", "out of range");
+    CUDA_TRY(cudaSetDevice(g->device));
+    cudaStream_t st = g->stream;
+    const ModelView &m = g->m;
+    std::vector<int> slots(nb);
+    for (int i = 0; i < nb; ++i) slots[i] = i;
+    TRY(set_batch_slots(kv, slots.data(), nb));
+    DecodeView dv = decode_view(kv, nb);
+    DecodeBufs &b = kv->db;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+    int n_launch = 0;
+    const int per = (nb + 7) / 8;
+    for (int l = 0; l < m.n_layers; ++l) {
+        const LayerW &L = m.layers[l];
+        launch_gemv(L.c_attn, m.sb_half, EPI_QKV, 1, L.ln1_w, L.ln1_b, nullptr, nullptr, b.x, b.q, nb, &dv, l, st);
+        launch_gemv(L.c_proj, m.sb_half, EPI_RESID, 0, nullptr, nullptr, nullptr, nullptr, b.attn, b.x, nb, nullptr, l, st);
+        launch_gemv(L.c_fc, m.sb_half, EPI_GELU, 1, L.ln2_w, L.ln2_b, nullptr, nullptr, b.x, b.u, nb, nullptr, l, st);
+        launch_gemv(L.mlp_proj, m.sb_half, EPI_RESID, 0, nullptr, nullptr, nullptr, nullptr, b.u, b.x, nb, nullptr, l, st);
+        n_launch += 4 * per;
+    }
+    launch_gemv(m.mel_head, m.sb_half, EPI_PLAIN, 2, m.ln_f_w, m.ln_f_b, m.final_w, m.final_b, b.x, b.logits, nb, nullptr, 0, st);
+    n_launch += per;
+    CUDA_TRY(cudaStreamEndCapture(st, &graph));
+    CUDA_TRY(cudaGraphInstantiate(&exec, graph, 0));
+    for (int i = 0; i < 3; ++i) CUDA_TRY(cudaGraphLaunch(exec, st));
+    CUDA_TRY(cudaEventRecord(g->ev[0], st));
+    for (int i = 0; i < iters; ++i) CUDA_TRY(cudaGraphLaunch(exec, st));
+    CUDA_TRY(cudaEventRecord(g->ev[1], st));
+    CUDA_TRY(cudaStreamSynchronize(st));
+    float t = 0.f;
+    CUDA_TRY(cudaEventElapsedTime(&t, g->ev[0], g->ev[1]));
+    cudaGraphExecDestroy(exec);
+    cudaGraphDestroy(graph);
+    *ms = t / (float)iters;
+    if (launches) *launches = n_launch;
+    return ITTS_OK;
+}

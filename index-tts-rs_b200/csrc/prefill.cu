@@ -1,0 +1,272 @@
+// prefill.cu -- prompt (prefill) kernels: sequence embedding, row LayerNorm,
+// int8 group-64 dequant GEMM with bias / GELU / residual / KV-scatter epilogues,
+// and causal attention.
+//
+// Reference semantics: Gpt::prefix_embedding / sequence_embedding
+// (crates/core/src/models/gpt.rs:535-627), Gpt::prefill_after (gpt.rs:655-696),
+// Gpt2Block::forward with the causal mask (gpt.rs:325-384).
+#include "kernels.h"
+
+namespace itts {
+
+// Row r of [conds(n_conds), text_emb[0,t..,1] + lang_emb[lang] + text_pos[i],
+//           mel_emb[8192] + mel_pos[0], mel_emb[prior[c]] + mel_pos[c + 2]]
+__global__ void embed_prefix_kernel(ModelView m, const int *full_text, int n_full,
+                                    const float *conds, int n_conds, int lang, const int *prior,
+                                    int n_prior, float *x) {
+    const int r = blockIdx.x, d = m.d;
+    float *out = x + (size_t)r * d;
+    if (r < n_conds) {
+        for (int i = threadIdx.x; i < d; i += blockDim.x) out[i] = conds[(size_t)r * d + i];
+    } else if (r < n_conds + n_full) {
+        const int t = r - n_conds, tok = full_text[t];
+        for (int i = threadIdx.x; i < d; i += blockDim.x)
+            out[i] = (m.text_emb[(size_t)tok * d + i] + m.lang_emb[(size_t)lang * d + i]) +
+                     m.text_pos[(size_t)t * d + i];
+    } else if (r == n_conds + n_full) {
+        for (int i = threadIdx.x; i < d; i += blockDim.x)
+            out[i] = m.mel_emb[(size_t)kStartMel * d + i] + m.mel_pos[i];
+    } else {
+        const int c = r - (n_conds + n_full + 1), tok = prior[c];
+        for (int i = threadIdx.x; i < d; i += blockDim.x)
+            out[i] = m.mel_emb[(size_t)tok * d + i] + m.mel_pos[(size_t)(c + 2) * d + i];
+    }
+}
+
+void launch_embed_prefix(const ModelView &m, const int *full_text, int n_full, const float *conds,
+                         int n_conds, int lang, const int *prior, int n_prior, float *x,
+                         cudaStream_t st) {
+    const int T = n_conds + n_full + 1 + n_prior;
+    embed_prefix_kernel<<<T, 256, 0, st>>>(m, full_text, n_full, conds, n_conds, lang, prior,
+                                            n_prior, x);
+}
+
+// y[t] = LayerNorm(x[t]) * w + b, one CTA per row, two-pass statistics.
+__global__ void __launch_bounds__(256) layernorm_rows_kernel(const float *x, const float *w,
+                                                             const float *b, int d, float *y) {
+    const int t = blockIdx.x;
+    const float *row = x + (size_t)t * d;
+    __shared__ float red[8];
+    __shared__ float stat;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float s = 0.f;
+    for (int i = threadIdx.x; i < d; i += blockDim.x) s += row[i];
+    s = warp_sum(s);
+    if (lane == 0) red[warp] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float a = 0.f;
+        for (int i = 0; i < (int)(blockDim.x >> 5); ++i) a += red[i];
+        stat = a / (float)d;
+    }
+    __syncthreads();
+    const float mean = stat;
+    float v = 0.f;
+    for (int i = threadIdx.x; i < d; i += blockDim.x) {
+        const float c = row[i] - mean;
+        v += c * c;
+    }
+    v = warp_sum(v);
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float a = 0.f;
+        for (int i = 0; i < (int)(blockDim.x >> 5); ++i) a += red[i];
+        stat = 1.0f / sqrtf(a / (float)d + kNormEps);
+    }
+    __syncthreads();
+    const float rstd = stat;
+    for (int i = threadIdx.x; i < d; i += blockDim.x)
+        y[(size_t)t * d + i] = (row[i] - mean) * rstd * w[i] + b[i];
+}
+
+// ---------------------------------------------------------------------------
+// GEMM: y[t, o] = x[t, :] . W[o, :] + bias[o] for T prompt positions.
+// CTA tile 64 positions x 64 outputs, K step = one quantization group (64);
+// the weight tile is dequantized once into shared memory (fp32) and reused by
+// all 64 positions.  Thread tile 4 x 4.
+// ---------------------------------------------------------------------------
+struct GemmParams {
+    QLinear W;
+    bool sb_half;
+    const float *x;  // [T, K]
+    float *y;        // [T, OUT]
+    int T;
+    // EPI_QKV: K/V of position t into the cache at position t
+    __half *k_cache, *v_cache;
+    int slot, n_slots, n_heads, max_seq, layer, d;
+};
+
+template <int EPI>
+__global__ void __launch_bounds__(256) gemm_q8_kernel(GemmParams p) {
+    constexpr int BM = 64, BN = 64, BK = 64, PAD = 4;
+    __shared__ __align__(16) float Xs[BK][BM + PAD];
+    __shared__ __align__(16) float Ws[BK][BN + PAD];
+    const int K = p.W.in, OUT = p.W.out, G = K / kGroup;
+    const int t0 = blockIdx.y * BM, o0 = blockIdx.x * BN;
+    const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
+    float acc[4][4] = {};
+    for (int k0 = 0; k0 < K; k0 += BK) {
+        {  // X tile: thread loads 16 consecutive k of one position
+            const int t = tid >> 2, kq = (tid & 3) * 16;
+            const int tt = t0 + t;
+#pragma unroll
+            for (int j = 0; j < 16; j += 4) {
+                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (tt < p.T) v = *reinterpret_cast<const float4 *>(p.x + (size_t)tt * K + k0 + kq + j);
+                Xs[kq + j][t] = v.x;
+                Xs[kq + j + 1][t] = v.y;
+                Xs[kq + j + 2][t] = v.z;
+                Xs[kq + j + 3][t] = v.w;
+            }
+        }
+        {  // W tile: thread dequantizes 16 bytes of one output row
+            const int r = tid >> 2, kq = (tid & 3) * 16;
+            const int o = o0 + r;
+            float s = 0.f, z = 0.f;
+            uint4 w = make_uint4(0, 0, 0, 0);
+            if (o < OUT) {
+                w = ld_stream(p.W.q + (size_t)o * K + k0 + kq);
+                s = load_sb(p.W.scales, p.sb_half, (size_t)o * G + k0 / kGroup);
+                z = load_sb(p.W.biases, p.sb_half, (size_t)o * G + k0 / kGroup);
+            }
+            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int j = 0; j < 16; ++j) Ws[kq + j][r] = s * byte_to_float(ww[j >> 2], j & 3) + z;
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int kk = 0; kk < BK; ++kk) {
+            const float4 a = *reinterpret_cast<const float4 *>(&Xs[kk][ty * 4]);
+            const float4 b = *reinterpret_cast<const float4 *>(&Ws[kk][tx * 4]);
+            const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int t = t0 + ty * 4 + i;
+        if (t >= p.T) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int o = o0 + tx * 4 + j;
+            if (o >= OUT) continue;
+            const float v = acc[i][j] + p.W.bias[o];
+            float *yp = p.y + (size_t)t * OUT + o;
+            if (EPI == EPI_PLAIN) *yp = v;
+            else if (EPI == EPI_GELU) *yp = gelu_tanh(v);
+            else if (EPI == EPI_RESID) *yp += v;
+            else {
+                *yp = v;
+                if (o >= p.d) {
+                    const int rr = o - p.d, which = rr / p.d, oo = rr - which * p.d;
+                    __half *cache = which == 0 ? p.k_cache : p.v_cache;
+                    if (t < p.max_seq)
+                        cache[kv_index(p.layer, p.slot, oo >> 6, t, p.n_slots, p.n_heads, p.max_seq) +
+                              (oo & 63)] = __float2half_rn(v);
+                }
+            }
+        }
+    }
+}
+
+static void launch_gemm(int epi, const GemmParams &p, cudaStream_t st) {
+    dim3 grid((p.W.out + 63) / 64, (p.T + 63) / 64);
+    switch (epi) {
+    case EPI_PLAIN: gemm_q8_kernel<EPI_PLAIN><<<grid, 256, 0, st>>>(p); break;
+    case EPI_GELU: gemm_q8_kernel<EPI_GELU><<<grid, 256, 0, st>>>(p); break;
+    case EPI_RESID: gemm_q8_kernel<EPI_RESID><<<grid, 256, 0, st>>>(p); break;
+    default: gemm_q8_kernel<EPI_QKV><<<grid, 256, 0, st>>>(p); break;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Causal attention over the prompt: one thread per query, 64 queries x one head
+// per CTA; K/V tiles of 64 positions staged in shared memory (fp32, from the
+// QKV output); online softmax.  Query t sees keys 0..t.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(64) attn_prefill_kernel(const float *qkv, int T, int d,
+                                                          float *out) {
+    __shared__ float Ks[64][65];
+    __shared__ float Vs[64][65];
+    const int h = blockIdx.y, q0 = blockIdx.x * 64, t = q0 + threadIdx.x;
+    const int ld = 3 * d;
+    float q[64], acc[64];
+    float m = -INFINITY, l = 0.f;
+    if (t < T) {
+#pragma unroll
+        for (int e = 0; e < 64; ++e) q[e] = qkv[(size_t)t * ld + h * 64 + e] * kAttnScale;
+    }
+#pragma unroll
+    for (int e = 0; e < 64; ++e) acc[e] = 0.f;
+    const int last = min(T - 1, q0 + 63);
+    for (int k0 = 0; k0 <= last; k0 += 64) {
+        __syncthreads();
+        for (int i = threadIdx.x; i < 64 * 64; i += 64) {
+            const int r = i >> 6, e = i & 63, kk = k0 + r;
+            Ks[r][e] = kk < T ? qkv[(size_t)kk * ld + d + h * 64 + e] : 0.f;
+            Vs[r][e] = kk < T ? qkv[(size_t)kk * ld + 2 * d + h * 64 + e] : 0.f;
+        }
+        __syncthreads();
+        if (t < T) {
+            const int jn = min(64, t - k0 + 1);
+            for (int j = 0; j < jn; ++j) {
+                float s = 0.f;
+#pragma unroll
+                for (int e = 0; e < 64; ++e) s = fmaf(q[e], Ks[j][e], s);
+                const float mn = fmaxf(m, s);
+                const float corr = m == -INFINITY ? 0.f : expf(m - mn);
+                const float pj = expf(s - mn);
+                l = l * corr + pj;
+#pragma unroll
+                for (int e = 0; e < 64; ++e) acc[e] = acc[e] * corr + pj * Vs[j][e];
+                m = mn;
+            }
+        }
+    }
+    if (t < T) {
+        const float inv = 1.0f / l;
+#pragma unroll
+        for (int e = 0; e < 64; ++e) out[(size_t)t * d + h * 64 + e] = acc[e] * inv;
+    }
+}
+
+void prefill_forward(const ModelView &m, const DecodeView &dv, int slot, int T, PrefillBufs &pb,
+                     float *logits_row, cudaStream_t st) {
+    const int d = m.d;
+    for (int l = 0; l < m.n_layers; ++l) {
+        const LayerW &L = m.layers[l];
+        layernorm_rows_kernel<<<T, 256, 0, st>>>(pb.x, L.ln1_w, L.ln1_b, d, pb.n);
+        GemmParams g{};
+        g.sb_half = m.sb_half;
+        g.T = T;
+        g.k_cache = dv.k_cache;
+        g.v_cache = dv.v_cache;
+        g.slot = slot;
+        g.n_slots = dv.n_slots;
+        g.n_heads = dv.n_heads;
+        g.max_seq = dv.max_seq;
+        g.layer = l;
+        g.d = d;
+        g.W = L.c_attn; g.x = pb.n; g.y = pb.qkv;
+        launch_gemm(EPI_QKV, g, st);
+        attn_prefill_kernel<<<dim3((T + 63) / 64, m.n_heads), 64, 0, st>>>(pb.qkv, T, d, pb.attn);
+        g.W = L.c_proj; g.x = pb.attn; g.y = pb.x;
+        launch_gemm(EPI_RESID, g, st);
+        layernorm_rows_kernel<<<T, 256, 0, st>>>(pb.x, L.ln2_w, L.ln2_b, d, pb.n);
+        g.W = L.c_fc; g.x = pb.n; g.y = pb.u;
+        launch_gemm(EPI_GELU, g, st);
+        g.W = L.mlp_proj; g.x = pb.u; g.y = pb.x;
+        launch_gemm(EPI_RESID, g, st);
+    }
+    // ln_f then final_norm on the last row, then mel_head (gpt.rs:673-692)
+    launch_gemv(m.mel_head, m.sb_half, EPI_PLAIN, 2, m.ln_f_w, m.ln_f_b, m.final_w, m.final_b,
+                pb.x + (size_t)(T - 1) * d, logits_row, 1, nullptr, 0, st);
+}
+
+}  // namespace itts

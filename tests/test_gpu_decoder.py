@@ -1,0 +1,217 @@
+"""B200 decoder (through the C ABI) vs the CPU checker.
+
+Tolerances are the ones the task states for this path: teacher-forced logits within
+max-abs 2e-2 and relative 1e-2 (max |diff| / max |ref|) per step; greedy tokens agree
+on at least 99% of steps; sampling bit-exact given the same logits and uniform draws
+(test_gpu_sampler.py)."""
+import numpy as np
+import pytest
+
+import itts_gpt as ig
+import oracle as orc
+from itts_gpt.synth import ModelConfig, make_conds, make_text, make_weights, save_safetensors
+
+pytestmark = pytest.mark.gpu
+
+ATOL = 2e-2
+RTOL = 1e-2
+
+
+def check_logits(got, ref, what=""):
+    err = float(np.max(np.abs(got - ref)))
+    rel = err / max(float(np.max(np.abs(ref))), 1e-12)
+    assert err <= ATOL and rel <= RTOL, f"{what}: max abs {err:.3e}, rel {rel:.3e}"
+    return err
+
+
+@pytest.fixture(scope="module")
+def small(small_weights):
+    g = ig.Gpt.from_weights(small_weights, device=0)
+    yield g, orc.OracleModel(small_weights)
+    g.close()
+
+
+def test_prefill_matches_checker(small, small_cfg):
+    gpt, om = small
+    for n_text, n_conds, lang, prior in ((1, 3, 0, []), (17, 3, 1, []), (64, 32, 5, [])
+                                         , (40, 32, 1, [3, 900, 8191])):
+        text = make_text(n_text, small_cfg.text_vocab, seed=n_text)
+        conds = make_conds(small_cfg.d, n_conds, seed=n_conds)
+        kv = ig.KvCache(gpt, max_seq=512)
+        got = gpt.prefill_after(text, conds, lang, prior, kv)
+        ref = om.prefill(om.kv(512), text, conds, lang, prior)
+        check_logits(got, ref, f"prefill T={n_conds + n_text + 3 + len(prior)}")
+        assert kv.valid_len() == n_conds + n_text + 3 + len(prior)
+
+
+def _teacher_forced(gpt, om, cfg, n_text, n_conds, steps, seed, max_seq=1024):
+    text = make_text(n_text, cfg.text_vocab, seed=seed)
+    conds = make_conds(cfg.d, n_conds, seed=seed + 1)
+    codes = np.random.default_rng(seed).integers(0, 8192, steps).tolist()
+    kv = ig.KvCache(gpt, max_seq=max_seq)
+    okv = om.kv(max_seq)
+    g = [gpt.prefill(text, conds, 1, kv)]
+    r = [om.prefill(okv, text, conds, 1)]
+    for i, c in enumerate(codes):
+        g.append(gpt.step(kv, c, i + 2))
+        r.append(om.step(okv, c, i + 2))
+    assert kv.valid_len() == okv.valid_len()
+    return np.stack(g), np.stack(r)
+
+
+def test_teacher_forced_steps_small(small, small_cfg):
+    gpt, om = small
+    g, r = _teacher_forced(gpt, om, small_cfg, 20, 3, 40, seed=3)
+    for i in range(len(g)):
+        check_logits(g[i], r[i], f"step {i}")
+    agree = np.mean(np.argmax(g, 1) == np.argmax(r, 1))
+    assert agree >= 0.99
+
+
+def test_step_batch_equals_single_steps(small, small_cfg):
+    gpt, _ = small
+    kv = ig.KvCache(gpt, max_seq=256, max_batch=5)
+    texts = [make_text(n, small_cfg.text_vocab, seed=n) for n in (3, 30, 9, 50, 12)]
+    conds = make_conds(small_cfg.d, 3, seed=1)
+    for s, t in enumerate(texts):
+        gpt.prefill(t, conds, 1, kv, slot=s)
+    slots = [4, 0, 2]
+    out = gpt.step_batch(kv, slots, [7, 8, 9], [2, 2, 2])
+    for j, s in enumerate(slots):
+        kv1 = ig.KvCache(gpt, max_seq=256)
+        gpt.prefill(texts[s], conds, 1, kv1)
+        one = gpt.step(kv1, [7, 8, 9][j], 2)
+        np.testing.assert_allclose(out[j], one, atol=1e-5, rtol=1e-5)
+    assert [kv.valid_len(s) for s in range(5)] == [3 + t.size + 3 + (s in slots) for s, t in enumerate(texts)]
+
+
+def test_generate_greedy_matches_checker(small, small_cfg):
+    gpt, om = small
+    text = make_text(25, small_cfg.text_vocab, seed=9)
+    conds = make_conds(small_cfg.d, 32, seed=10)
+    kv = ig.KvCache(gpt, max_seq=512)
+    p = ig.SamplingParams(greedy=True, max_mel_tokens=64)
+    codes = ig.generate_codes(gpt, text, conds, 1, kv, p, ig.SamplerRng(0))
+    ref, _ = om.generate(om.kv(512), text, conds, 1, orc.params_c(greedy=True, max_mel_tokens=64), 0)
+    n = min(len(codes), len(ref))
+    agree = np.mean(np.array(codes[:n]) == np.array(ref[:n])) if n else 1.0
+    assert agree >= 0.99 and len(codes) == len(ref)
+
+
+def test_generate_sampled_matches_checker(small, small_cfg):
+    gpt, om = small
+    text = make_text(30, small_cfg.text_vocab, seed=12)
+    conds = make_conds(small_cfg.d, 3, seed=13)
+    kv = ig.KvCache(gpt, max_seq=512)
+    p = ig.SamplingParams(top_k=30, top_p=0.8, temperature=0.8, repetition_penalty=10.0,
+                          max_mel_tokens=48)
+    r = ig.SamplerRng(77)
+    codes = ig.generate_codes_after(gpt, ig.CodePrompt(text, conds, 1, min_codes=48), kv, p, r)
+    ref, st = om.generate(om.kv(512), text, conds, 1, orc.params_c(False, 30, 0.8, 0.8, 10.0, 48),
+                          ig.SamplerRng(77).state, min_codes=48)
+    assert codes == ref
+    assert r.state == st
+
+
+def test_generate_batch_equals_independent_calls(small, small_cfg):
+    gpt, _ = small
+    lens = [5, 40, 17, 60, 9, 33]
+    prompts = [ig.CodePrompt(make_text(n, small_cfg.text_vocab, seed=n),
+                             make_conds(small_cfg.d, 3 if i % 2 else 32, seed=i), 1 + i % 3,
+                             prior_codes=[1, 2, 3] if i == 2 else ())
+               for i, n in enumerate(lens)]
+    params = [ig.SamplingParams(greedy=i % 2 == 0, top_k=30, max_mel_tokens=20 + 5 * i) for i in range(6)]
+    kvb = ig.KvCache(gpt, max_seq=512, max_batch=6)
+    rb = [ig.SamplerRng(100 + i) for i in range(6)]
+    batch = ig.generate_batch(gpt, prompts, kvb, params, rb)
+    for i in range(6):
+        kv1 = ig.KvCache(gpt, max_seq=512)
+        r1 = ig.SamplerRng(100 + i)
+        one = ig.generate_codes_after(gpt, prompts[i], kv1, params[i], r1)
+        assert batch[i] == one, i
+        assert rb[i].state == r1.state
+
+
+def test_load_from_path_and_f32_scales(tmp_path, small_cfg, small_weights):
+    path = tmp_path / "gpt_int8.safetensors"
+    save_safetensors(str(path), small_weights)
+    g1 = ig.Gpt.load_from_path(str(path))
+    g2 = ig.Gpt.from_weights(small_weights)
+    text = make_text(10, small_cfg.text_vocab, seed=1)
+    conds = make_conds(small_cfg.d, 3, seed=2)
+    a = g1.prefill(text, conds, 1, ig.KvCache(g1, 128))
+    b = g2.prefill(text, conds, 1, ig.KvCache(g2, 128))
+    assert np.array_equal(a, b)
+    # the real checkpoint stores f32 scales/biases (loader.rs:875-931)
+    cfg32 = ModelConfig(n_layers=2, d=256, ff=1024, text_vocab=500, sb_half=False)
+    w32 = make_weights(cfg32, seed=3, ln_beta_std=0.02)
+    g3 = ig.Gpt.from_weights(w32)
+    assert not g3.scales_f16
+    om = orc.OracleModel(w32)
+    check_logits(g3.prefill(text, conds, 2, ig.KvCache(g3, 128)), om.prefill(om.kv(128), text, conds, 2))
+
+
+def test_validation_errors(small, small_cfg):
+    gpt, _ = small
+    with pytest.raises(ig.ValidationError, match="max_seq"):
+        ig.KvCache(gpt, max_seq=0)
+    kv = ig.KvCache(gpt, max_seq=40)
+    conds = make_conds(small_cfg.d, 3, seed=1)
+    with pytest.raises(ig.ValidationError, match="text_tokens"):
+        gpt.prefill([], conds, 1, kv)
+    with pytest.raises(ig.ValidationError, match="text_tokens"):
+        gpt.prefill([5] * 601, conds, 1, kv)
+    with pytest.raises(ig.ValidationError, match="lang_id"):
+        gpt.prefill([5], conds, 107, kv)
+    with pytest.raises(ig.ValidationError, match="conds"):
+        gpt.prefill([5], np.zeros((1, 3, 7), np.float32), 1, kv)
+    with pytest.raises(ig.ValidationError, match="kv_cache"):
+        gpt.prefill([5] * 40, conds, 1, kv)
+    gpt.prefill([5] * 30, conds, 1, kv)
+    with pytest.raises(ig.ValidationError, match="mel_token_id"):
+        gpt.step(kv, 8194, 2)
+    with pytest.raises(ig.ValidationError, match="pos_idx"):
+        gpt.step(kv, 5, 1818)
+    for i in range(4):
+        gpt.step(kv, 5, 2 + i)
+    with pytest.raises(ig.ValidationError, match="kv_cache"):
+        gpt.step(kv, 5, 6)
+    # generation that outgrows the cache fails like update_layer (gpt.rs:157-165)
+    with pytest.raises(ig.ValidationError, match="kv_cache"):
+        ig.generate_codes_after(gpt, ig.CodePrompt([5] * 30, conds, 1, min_codes=20), kv,
+                                ig.SamplingParams(greedy=True, max_mel_tokens=20), ig.SamplerRng(0))
+    with pytest.raises(ig.ValidationError, match="max_mel_tokens"):
+        ig.generate_codes_after(gpt, ig.CodePrompt([5], conds, 1, prior_codes=[5] * 1815),
+                                ig.KvCache(gpt, 4000), ig.SamplingParams(greedy=True), ig.SamplerRng(0))
+
+
+# ---------------------------------------------------------------------------
+# full-size decoder (24 layers, d=1280, 20 heads, ff=5120, fp16 scales)
+# ---------------------------------------------------------------------------
+@pytest.fixture(scope="module")
+def full():
+    cfg = ModelConfig()
+    w = make_weights(cfg, seed=2024)
+    g = ig.Gpt.from_weights(w, device=0)
+    yield cfg, g, orc.OracleModel(w)
+    g.close()
+
+
+def test_full_size_teacher_forced(full):
+    cfg, gpt, om = full
+    g, r = _teacher_forced(gpt, om, cfg, 64, 32, 24, seed=41, max_seq=512)
+    errs = [check_logits(g[i], r[i], f"full step {i}") for i in range(len(g))]
+    agree = np.mean(np.argmax(g, 1) == np.argmax(r, 1))
+    assert agree >= 0.99, agree
+    print(f"full-size teacher-forced: max |dlogit| {max(errs):.2e}, argmax agreement {agree:.3f}")
+
+
+def test_full_size_greedy_generate(full):
+    cfg, gpt, om = full
+    text = make_text(64, cfg.text_vocab, seed=1)
+    conds = make_conds(cfg.d, 32, seed=2)
+    p = ig.SamplingParams(greedy=True, max_mel_tokens=32)
+    codes = ig.generate_codes(gpt, text, conds, 1, ig.KvCache(gpt, 512), p, ig.SamplerRng(0))
+    ref, _ = om.generate(om.kv(512), text, conds, 1, orc.params_c(greedy=True, max_mel_tokens=32), 0)
+    n = min(len(codes), len(ref))
+    assert n > 0 and np.mean(np.array(codes[:n]) == np.array(ref[:n])) >= 0.99
