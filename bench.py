@@ -223,9 +223,11 @@ def run_ours(args, rank, world, local_rank):
         dist.barrier()
     clk = clocks.stop()
 
-    # weight-stream kernels of one decode step, timed alone (roofline of the GEMV)
-    ws_ms, ws_launches = _bench_weight_stream(gpt, kv, iters=50)
+    # the decode-step forward (the persistent kernel), timed alone at the mean KV length
+    L_avg = N_CONDS + N_TEXT + 3 + (N_MEL - 1) // 2
+    ws_ms, ws_launches = _bench_decode_forward(gpt, kv, L_avg, iters=100)
     wbytes = cfg.weight_bytes()
+    step_bytes = wbytes + kv_bytes_per_step(cfg, L_avg + 1)
 
     times = np.array([dev_ms / 1000.0, wall])
     if world > 1:
@@ -236,15 +238,14 @@ def run_ours(args, rank, world, local_rank):
     tokens = N_MEL * args.steps * world
     if rank != 0:
         return
-    # kernels of ours per generate: prefill (1 embed + 7 per layer + head) + first sample,
-    # then per decode step 1 embed + 5 per layer + head + sampler
-    prefill_k = 1 + 7 * cfg.n_layers + 1
-    step_k = 1 + 5 * cfg.n_layers + 1 + 1
+    # kernels of ours per generate: prefill (embed + 7 per layer + 2 LN + head GEMM),
+    # the first sample, then per decode step the forward (ws_launches) + the sampler
+    prefill_k = 1 + 7 * cfg.n_layers + 3
+    step_k = ws_launches + 1
     gpu_launches = args.steps * (prefill_k + 1 + step_k * (N_MEL - 1))
     h2d = 4 * (N_TEXT + 2) + 4 * N_CONDS * cfg.d
     d2h = 4 * N_MEL
-    L_avg = N_CONDS + N_TEXT + 3 + (N_MEL - 1) / 2
-    achieved = wbytes / (ws_ms * 1e-3) / 1e9
+    achieved = step_bytes / (ws_ms * 1e-3) / 1e9
     line = {
         "metric": "mel tokens/s (cfg2 batch-1 decode; ms/mel-token = 1000 / per-GPU value)",
         "value": tokens / dev_s, "unit": "mel tokens/s", "n_gpus": world, "steps": args.steps,
@@ -260,11 +261,14 @@ def run_ours(args, rank, world, local_rank):
         "e2e": {"value": tokens / wall_s, "unit": "mel tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "gpu_launches": int(gpu_launches),
-        "roofline": {"bound": "hbm", "kernel": "gemv_kernel (int8 g64 dequant GEMV, all linears "
-                     "of one decode step)", "achieved": achieved, "peak": hbm_peak,
-                     "unit": "GB/s", "frac": achieved / hbm_peak, "peak_source": peak_src,
-                     "algorithmic_bytes_per_launch_set": wbytes, "launches": ws_launches,
-                     "ms": ws_ms, "traffic": None},
+        "roofline": {"bound": "hbm", "kernel": "mk_decode_kernel (persistent decode step: int8 "
+                     "g64 dequant GEMVs + flash-decode attention, one launch per token)",
+                     "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                     "frac": achieved / hbm_peak, "peak_source": peak_src,
+                     "algorithmic_bytes_per_launch": step_bytes,
+                     "bytes_formula": "514,144,936 weight B + 122,880 B x KV positions (fp16 K+V)",
+                     "kv_positions": L_avg + 1, "launches_per_step": ws_launches,
+                     "ms_per_launch": ws_ms, "traffic": None},
         "clocks": clk,
     }
     if not args.no_cpu_baseline:
@@ -275,11 +279,12 @@ def run_ours(args, rank, world, local_rank):
     print(json.dumps(line), flush=True)
 
 
-def _bench_weight_stream(gpt, kv, iters):
+def _bench_decode_forward(gpt, kv, kv_len, iters):
     import ctypes as C
     from itts_gpt import _lib
     ms, n = C.c_float(), C.c_int32()
-    rc = _lib.load_lib().itts_bench_weight_stream(gpt._h, kv._h, 1, iters, C.byref(ms), C.byref(n))
+    rc = _lib.load_lib().itts_bench_decode_forward(gpt._h, kv._h, 1, kv_len, iters, C.byref(ms),
+                                                   C.byref(n))
     if rc != 0:
         raise RuntimeError(_lib.last_error())
     return ms.value, n.value

@@ -115,6 +115,7 @@ int itts_gpt_load(const char *path, int device, itts_gpt **out);
 /* Gpt::from_weights (gpt.rs:477-515): the same from caller-owned host tensors. */
 int itts_gpt_from_tensors(const itts_tensor *tensors, int32_t n_tensors, int device,
                           itts_gpt **out);
+/* Every itts_kv created from `gpt` must be freed before `gpt`. */
 void itts_gpt_free(itts_gpt *gpt);
 /* Gpt::num_layers (gpt.rs:529-531). */
 int32_t itts_gpt_num_layers(const itts_gpt *gpt);
@@ -190,13 +191,20 @@ int itts_gpt_last_timing(const itts_gpt *gpt, float *prefill_ms, float *decode_m
 
 /* ---- measurement (no reference counterpart) ----------------------------------------- */
 
-/* Replays `iters` times a CUDA graph holding only the weight-streaming kernels of one
- * decode step for `nb` batch columns (the int8 linears and the head, with their fused
- * LayerNorm / epilogues; the KV scatter is skipped for inactive slots) and returns the
- * mean device time per replay (CUDA events on the handle's stream) and the number of
- * kernel launches per replay.  Roofline of the dominant kernel. */
-int itts_bench_weight_stream(itts_gpt *gpt, itts_kv *kv, int32_t nb, int32_t iters,
-                             float *ms_per_iter, int32_t *launches_per_iter);
+/* Replays `iters` times the decode-step forward (everything but the sampler) for slots
+ * 0..nb-1 with kv_len cached positions each (the cache contents are whatever the slots
+ * hold; the forward appends position kv_len without advancing the slots), and returns
+ * the mean device time per step (CUDA events on the handle's stream) and the number of
+ * kernel launches per step.  The slots' host-visible state is restored afterwards. */
+int itts_bench_decode_forward(itts_gpt *gpt, itts_kv *kv, int32_t nb, int32_t kv_len,
+                              int32_t iters, float *ms_per_step, int32_t *launches_per_step);
+
+/* The same for one step of the persistent decode-step kernel (nb <= 4), with per-CTA
+ * stage timestamps (device globaltimer, ns): out[cta * events_per_cta + i], 0 where a CTA
+ * recorded nothing.  out_len must be at least grid * 256. */
+int itts_bench_trace(itts_gpt *gpt, itts_kv *kv, int32_t nb, int32_t kv_len,
+                     unsigned long long *out, int32_t out_len, int32_t *grid,
+                     int32_t *events_per_cta);
 
 #ifdef __cplusplus
 }

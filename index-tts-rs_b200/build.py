@@ -20,7 +20,7 @@ CSRC = PKG / "csrc"
 BUILD = PKG / "_build"
 INCLUDE = PKG.parent / "include"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-CU_SOURCES = ["decode.cu", "prefill.cu", "sample.cu", "api.cu"]
+CU_SOURCES = ["decode.cu", "mk_decode.cu", "prefill.cu", "sample.cu", "api.cu"]
 
 
 def _nvcc() -> str:
@@ -68,7 +68,8 @@ def build(verbose: bool = False, ptxas_verbose: bool = False) -> dict:
         objs = list(ex.map(compile_one, CU_SOURCES))
     lib = PKG / "libitts_gpt.so"
     if _stale(lib, objs):
-        _run([nvcc] + ARCH + ["-shared", "-o", str(lib)] + [str(o) for o in objs] + ["-lcudart"])
+        _run([nvcc] + ARCH + ["-shared", "-o", str(lib)] + [str(o) for o in objs] +
+             ["-lcudart", "-Xlinker", "--no-undefined"])
     synth = PKG / "libitts_synth.so"
     if _stale(synth, [CSRC / "synth.cpp"]):
         _run([_host_cxx(), "-O3", "-fopenmp", "-fPIC", "-shared", "-ffp-contract=off",

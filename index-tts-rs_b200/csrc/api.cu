@@ -18,6 +18,7 @@
 #include <cstdio>
 #include <cstring>
 #include <string>
+#include <thread>
 #include <unordered_map>
 #include <vector>
 
@@ -25,7 +26,6 @@
 #include "kernels.h"
 
 namespace itts {
-void kernels_init_decode();
 void kernels_init_sample();
 }  // namespace itts
 
@@ -62,7 +62,8 @@ static int weight_load(const std::string &artifact, const std::string &msg) {
 struct itts_gpt {
     int device = 0;
     ModelView m{};
-    std::vector<LayerW> layers;
+    std::vector<MkLayer> layers;
+    MkLayer *d_layers = nullptr;
     void *arena = nullptr;
     cudaStream_t stream = nullptr;
     cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
@@ -95,6 +96,8 @@ struct itts_kv {
     size_t h_f32_cap = 0;
     std::vector<cudaGraphExec_t> graphs;  // by batch size
     std::vector<cudaGraph_t> graph_defs;
+    std::vector<char> graph_failed;       // capture unsupported: launch directly
+    size_t ll_bytes = 0;
 };
 
 // ------------------------------------------------------------------------------
@@ -195,6 +198,7 @@ static void gpt_destroy(itts_gpt *g) {
     for (auto &e : g->ev)
         if (e) cudaEventDestroy(e);
     cudaFree(g->arena);
+    cudaFree(g->d_layers);
     cudaFree(g->d_sstate);
     cudaFree(g->d_slogits);
     cudaFree(g->d_sidx);
@@ -233,7 +237,6 @@ extern "C" int itts_gpt_from_tensors(const itts_tensor *tensors, int32_t n_tenso
     if (hs->dtype != ITTS_DTYPE_F16 && hs->dtype != ITTS_DTYPE_F32)
         return weight_load("mel_head.scales", "scales must be F32 or F16");
     const bool sb_half = hs->dtype == ITTS_DTYPE_F16;
-    const int sb_bytes = sb_half ? 2 : 4;
 
     const itts_tensor *te = tt.get("text_embedding.weight");
     const itts_tensor *le = tt.get("lang_embedding.weight");
@@ -245,34 +248,89 @@ extern "C" int itts_gpt_from_tensors(const itts_tensor *tensors, int32_t n_tenso
             return weight_load(pr.second, pr.first ? "shape " + shape_str(pr.first) + " has the wrong model dim"
                                                    : std::string("missing tensor"));
 
-    struct Up { const itts_tensor *t; size_t bytes; size_t off; };
+    if (d % 128 != 0 || ff % 128 != 0)
+        return weight_load("gpt_int8.safetensors", "model and MLP dims must be multiples of 128");
+
+    // Host-side plan: f32 tensors are copied as they are; every quantized linear is
+    // re-tiled (mk.h) into a staging buffer first.
+    struct Up { const void *src; size_t bytes; size_t off; std::vector<uint8_t> staged; };
     std::vector<Up> ups;
-    auto add = [&](const itts_tensor *t, size_t bytes) { ups.push_back({t, bytes, 0}); return (int)ups.size() - 1; };
+    ups.reserve(16 + 13 * n_layers);
+    auto add = [&](const void *src, size_t bytes) {
+        ups.push_back({src, bytes, 0, {}});
+        return (int)ups.size() - 1;
+    };
     auto f32 = [&](const std::string &name, std::vector<int64_t> shape, int *idx) -> int {
         const itts_tensor *t;
         TRY(expect(tt, name, shape, &t));
         if (t->dtype != ITTS_DTYPE_F32) return weight_load(name, "expected F32");
         size_t n = 1;
-        for (auto s : shape) n *= (size_t)s;
-        *idx = add(t, n * 4);
+        for (auto sdim : shape) n *= (size_t)sdim;
+        *idx = add(t->data, n * 4);
         return ITTS_OK;
     };
-    struct LinIdx { int w, s, b, bias, out, in; };
+    struct LinIdx { int tiles, bias; MkLin lin; };
     auto lin = [&](const std::string &p, int64_t o, int64_t in, LinIdx *li) -> int {
-        const itts_tensor *w, *s, *b;
+        const itts_tensor *w, *sc, *bi;
         TRY(expect(tt, p + ".weight", {o, in / 4}, &w));
         if (w->dtype != ITTS_DTYPE_U32 && w->dtype != ITTS_DTYPE_I32) return weight_load(p + ".weight", "expected U32");
-        TRY(expect(tt, p + ".scales", {o, in / 64}, &s));
-        TRY(expect(tt, p + ".biases", {o, in / 64}, &b));
+        TRY(expect(tt, p + ".scales", {o, in / 64}, &sc));
+        TRY(expect(tt, p + ".biases", {o, in / 64}, &bi));
         const int want = sb_half ? ITTS_DTYPE_F16 : ITTS_DTYPE_F32;
-        if (s->dtype != want || b->dtype != want)
+        if (sc->dtype != want || bi->dtype != want)
             return weight_load(p + ".scales", "scales/biases must all share one dtype (F16 or F32)");
-        li->w = add(w, (size_t)o * in);
-        li->s = add(s, (size_t)o * (in / 64) * sb_bytes);
-        li->b = add(b, (size_t)o * (in / 64) * sb_bytes);
+        MkLin L{};
+        L.out = (int)o;
+        L.in = (int)in;
+        L.kc = MK_MAX_KC;
+        while (in % L.kc != 0) L.kc -= 128;
+        L.n_kc = (int)(in / L.kc);
+        L.n_rb = (int)((o + 15) / 16);
+        L.sbb = sb_half ? 4 : 8;
+        L.tile_bytes = mk_tile_bytes(L.kc, L.sbb);
+        const itts_tensor *bt;
+        TRY(expect(tt, p + ".bias", {o}, &bt));
+        if (bt->dtype != ITTS_DTYPE_F32) return weight_load(p + ".bias", "expected F32");
+        const float *bias_src = (const float *)bt->data;
+        const size_t total = (size_t)L.n_rb * L.n_kc * L.tile_bytes;
+        li->tiles = add(nullptr, total);
+        std::vector<uint8_t> &buf = ups[li->tiles].staged;
+        buf.assign(total, 0);
+        const uint8_t *q = (const uint8_t *)w->data;
+        const int G = (int)(in / 64);
+        const size_t sb_bytes = sb_half ? 2 : 4;
+        const uint8_t *sp = (const uint8_t *)sc->data, *bp = (const uint8_t *)bi->data;
+        auto work = [&](int rb0, int rb1) {
+            for (int rb = rb0; rb < rb1; ++rb)
+                for (int m = 0; m < 16; ++m) {
+                    const int64_t row = (int64_t)rb * 16 + m;
+                    if (row >= o) break;
+                    for (int64_t k = 0; k < in; k += 64) {
+                        const size_t qo = mk_q_offset(L, (int)row, (int)k);  // group start
+                        const uint8_t *src = q + row * in + k;
+                        for (int e = 0; e < 64; ++e) buf[qo + frag_pos_host(e)] = src[e];
+                        const size_t so = mk_sb_offset(L, (int)row, (int)k);
+                        const size_t gi = (size_t)row * G + (size_t)(k / 64);
+                        std::memcpy(&buf[so], sp + gi * sb_bytes, sb_bytes);
+                        std::memcpy(&buf[so + sb_bytes], bp + gi * sb_bytes, sb_bytes);
+                    }
+                    for (int kci = 0; kci < L.n_kc; ++kci) {
+                        const size_t tile = (size_t)rb * L.n_kc + kci;
+                        std::memcpy(&buf[tile * L.tile_bytes + mk_tile_bias_offset(L.kc, L.sbb) + m * 4],
+                                    bias_src + row, 4);
+                    }
+                }
+        };
+        const int nt = std::max(1, std::min(16, (int)std::thread::hardware_concurrency()));
+        std::vector<std::thread> th;
+        const int per = (L.n_rb + nt - 1) / nt;
+        for (int i = 0; i < nt; ++i) {
+            const int a = i * per, b = std::min(L.n_rb, a + per);
+            if (a < b) th.emplace_back(work, a, b);
+        }
+        for (auto &t : th) t.join();
         TRY(f32(p + ".bias", {o}, &li->bias));
-        li->out = (int)o;
-        li->in = (int)in;
+        li->lin = L;
         return ITTS_OK;
     };
     int i_te, i_le, i_me, i_mp, i_tp, i_lfw, i_lfb, i_fnw, i_fnb;
@@ -309,7 +367,6 @@ extern "C" int itts_gpt_from_tensors(const itts_tensor *tensors, int32_t n_tenso
     }
     static bool inited[64] = {false};
     if (device >= 0 && device < 64 && !inited[device]) {
-        kernels_init_decode();
         kernels_init_sample();
         inited[device] = true;
     }
@@ -326,28 +383,27 @@ extern "C" int itts_gpt_from_tensors(const itts_tensor *tensors, int32_t n_tenso
         if ((e = cudaEventCreate(&ev)) != cudaSuccess) return fail(e, "event");
     if ((e = cudaMalloc(&g->arena, total)) != cudaSuccess) return fail(e, "weights");
     char *base = (char *)g->arena;
-    for (auto &u : ups)
-        if ((e = cudaMemcpyAsync(base + u.off, u.t->data, u.bytes, cudaMemcpyHostToDevice, g->stream)) != cudaSuccess)
+    for (auto &u : ups) {
+        const void *src = u.staged.empty() ? u.src : (const void *)u.staged.data();
+        if ((e = cudaMemcpy(base + u.off, src, u.bytes, cudaMemcpyHostToDevice)) != cudaSuccess)
             return fail(e, "weight upload");
-    if ((e = cudaStreamSynchronize(g->stream)) != cudaSuccess) return fail(e, "weight upload");
-    auto P = [&](int idx) { return (const void *)(base + ups[idx].off); };
+    }
     auto F = [&](int idx) { return (const float *)(base + ups[idx].off); };
     auto mk = [&](const LinIdx &x) {
-        QLinear q;
-        q.q = (const uint8_t *)P(x.w);
-        q.scales = P(x.s);
-        q.biases = P(x.b);
-        q.bias = F(x.bias);
-        q.out = x.out;
-        q.in = x.in;
-        return q;
+        MkLin L = x.lin;
+        L.tiles = (const uint8_t *)(base + ups[x.tiles].off);
+        L.bias = F(x.bias);
+        return L;
     };
     g->layers.resize(n_layers);
     for (int i = 0; i < n_layers; ++i) {
-        LayerW &L = g->layers[i];
+        MkLayer &L = g->layers[i];
         L.ln1_w = F(li[i].l1w); L.ln1_b = F(li[i].l1b); L.ln2_w = F(li[i].l2w); L.ln2_b = F(li[i].l2b);
-        L.c_attn = mk(li[i].a); L.c_proj = mk(li[i].p); L.c_fc = mk(li[i].fc); L.mlp_proj = mk(li[i].mp);
+        L.qkv = mk(li[i].a); L.proj = mk(li[i].p); L.fc = mk(li[i].fc); L.mlp = mk(li[i].mp);
     }
+    if ((e = cudaMalloc(&g->d_layers, sizeof(MkLayer) * n_layers)) != cudaSuccess) return fail(e, "layers");
+    if ((e = cudaMemcpy(g->d_layers, g->layers.data(), sizeof(MkLayer) * n_layers, cudaMemcpyHostToDevice)) != cudaSuccess)
+        return fail(e, "layers");
     ModelView &m = g->m;
     m.n_layers = n_layers; m.d = (int)d; m.n_heads = (int)(d / 64); m.ff = (int)ff;
     m.mel_vocab = (int)mel_vocab; m.text_vocab = (int)te->shape[0]; m.lang_vocab = (int)le->shape[0];
@@ -357,6 +413,7 @@ extern "C" int itts_gpt_from_tensors(const itts_tensor *tensors, int32_t n_tenso
     m.ln_f_w = F(i_lfw); m.ln_f_b = F(i_lfb); m.final_w = F(i_fnw); m.final_b = F(i_fnb);
     m.mel_head = mk(head);
     m.layers = g->layers.data();
+    m.d_layers = g->d_layers;
     if ((e = cudaMalloc(&g->d_sstate, sizeof(SlotState))) != cudaSuccess) return fail(e, "scratch");
     if ((e = cudaMalloc(&g->d_slogits, ITTS_MAX_SAMPLE_LOGITS * sizeof(float))) != cudaSuccess) return fail(e, "scratch");
     if ((e = cudaMalloc(&g->d_sidx, 2 * sizeof(int))) != cudaSuccess) return fail(e, "scratch");
@@ -521,9 +578,11 @@ static void kv_destroy(itts_kv *kv) {
         if (g) cudaGraphExecDestroy(g);
     for (auto g : kv->graph_defs)
         if (g) cudaGraphDestroy(g);
-    void *dev[] = {kv->k, kv->v, kv->d_slots, kv->d_batch_slot, kv->db.x, kv->db.q, kv->db.attn,
-                   kv->db.u, kv->db.logits, kv->db.partials, kv->db.counters, kv->pb.x, kv->pb.n,
-                   kv->pb.qkv, kv->pb.attn, kv->pb.u, kv->d_codes, kv->d_text, kv->d_prior, kv->d_conds};
+    void *dev[] = {kv->k, kv->v, kv->d_slots, kv->d_batch_slot, kv->db.x, kv->db.n, kv->db.n2,
+                   kv->db.q, kv->db.attn, kv->db.u, kv->db.logits, kv->db.partials,
+                   kv->db.counters, kv->db.qkv_ll, kv->db.epoch, kv->db.err, kv->db.trace,
+                   kv->pb.x, kv->pb.n, kv->pb.qkv, kv->pb.attn,
+                   kv->pb.u, kv->d_codes, kv->d_text, kv->d_prior, kv->d_conds};
     for (void *p : dev) cudaFree(p);
     cudaFreeHost(kv->h_pinned);
     cudaFreeHost(kv->h_i32);
@@ -566,12 +625,43 @@ extern "C" int itts_kv_create(itts_gpt *g, int32_t max_seq, int32_t max_batch, i
     A((void **)&kv->d_slots, sizeof(SlotState) * max_batch);
     A((void **)&kv->d_batch_slot, sizeof(int) * max_batch);
     A((void **)&kv->db.x, sizeof(float) * max_batch * m.d);
-    A((void **)&kv->db.q, sizeof(float) * max_batch * m.d);
+    A((void **)&kv->db.n, sizeof(float) * max_batch * m.d);
+    A((void **)&kv->db.n2, sizeof(float) * max_batch * m.d);
+    A((void **)&kv->db.q, sizeof(float) * max_batch * 3 * m.d);
     A((void **)&kv->db.attn, sizeof(float) * max_batch * m.d);
     A((void **)&kv->db.u, sizeof(float) * max_batch * m.ff);
     A((void **)&kv->db.logits, sizeof(float) * max_batch * m.mel_vocab);
     A((void **)&kv->db.partials, sizeof(float) * max_batch * m.n_heads * kv->db.max_splits * 66);
     A((void **)&kv->db.counters, sizeof(int) * max_batch * m.n_heads);
+    // persistent decode-step kernel
+    {
+        int nsl = 0, grid = 0;
+        kv->db.mk_grid = 0;
+        for (int nb = 0; nb <= MK_MAX_NB; ++nb) kv->db.mk_nslot[nb] = 0;
+        for (int nb = 1; nb <= MK_MAX_NB && nb <= max_batch; ++nb) {
+            grid = mk_config(nb, std::max(m.d, m.ff), m.d, m.n_layers, &nsl);
+            if (grid <= 0) break;
+            kv->db.mk_grid = grid;
+            kv->db.mk_nslot[nb] = nsl;
+        }
+        const size_t L = m.n_layers, NBM = MK_MAX_NB;
+        kv->ll_bytes = sizeof(uint64_t) * L * NBM * (3 * m.d + m.d + m.d + m.ff + m.d) +
+                       sizeof(uint64_t) * (L * NBM * m.n_heads * MK_MAX_UNITS * MK_PART_WORDS + NBM * m.d);
+        A((void **)&kv->db.qkv_ll, kv->ll_bytes);
+        if (e == cudaSuccess) {
+            uint64_t *b = kv->db.qkv_ll;
+            kv->db.attn_ll = b + L * NBM * 3 * m.d;
+            kv->db.ao_ll = kv->db.attn_ll + L * NBM * m.n_heads * MK_MAX_UNITS * MK_PART_WORDS;
+            kv->db.h_ll = kv->db.ao_ll + L * NBM * m.d;
+            kv->db.u_ll = kv->db.h_ll + L * NBM * m.d;
+            kv->db.x_ll = kv->db.u_ll + L * NBM * m.ff;  // L + 1 layers of outputs
+            e = cudaMemsetAsync(kv->db.qkv_ll, 0, kv->ll_bytes, g->stream);
+        }
+        A((void **)&kv->db.epoch, sizeof(uint32_t) * std::max(grid, 1024));
+        if (e == cudaSuccess) e = cudaMemsetAsync(kv->db.epoch, 0, sizeof(uint32_t) * std::max(grid, 1024), g->stream);
+        A((void **)&kv->db.err, sizeof(int) * 4);
+        kv->db.trace = nullptr;
+    }
     A((void **)&kv->pb.x, sizeof(float) * (size_t)max_seq * m.d);
     A((void **)&kv->pb.n, sizeof(float) * (size_t)max_seq * m.d);
     A((void **)&kv->pb.qkv, sizeof(float) * (size_t)max_seq * 3 * m.d);
@@ -599,6 +689,7 @@ extern "C" int itts_kv_create(itts_gpt *g, int32_t max_seq, int32_t max_batch, i
     }
     kv->graphs.assign(max_batch + 1, nullptr);
     kv->graph_defs.assign(max_batch + 1, nullptr);
+    kv->graph_failed.assign(max_batch + 1, 0);
     *out = kv;
     return ITTS_OK;
 }
@@ -747,6 +838,23 @@ extern "C" int itts_gpt_prefill(itts_gpt *g, itts_kv *kv, int32_t slot, const in
     return ITTS_OK;
 }
 
+// The persistent decode-step kernel's error word is cleared before a run of steps; a
+// nonzero value after it means a bounded wait in the kernel gave up.  (Its per-CTA launch
+// counters are never reset: the LL tags they generate must not repeat.)
+static int reset_step_sync(itts_kv *kv) {
+    CUDA_TRY(cudaMemsetAsync(kv->db.err, 0, sizeof(int) * 4, kv->gpt->stream));
+    return ITTS_OK;
+}
+
+static int check_step_sync(itts_kv *kv) {
+    int err = 0;
+    CUDA_TRY(cudaMemcpy(&err, kv->db.err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (err != 0)
+        return set_err(ITTS_E_TIMEOUT, "device wait timed out in the decode-step kernel (code " +
+                                           std::to_string(err) + ")");
+    return ITTS_OK;
+}
+
 // ------------------------------------------------------------------------------
 // step (gpt.rs:706-754), batched over distinct slots
 // ------------------------------------------------------------------------------
@@ -777,9 +885,11 @@ extern "C" int itts_gpt_step(itts_gpt *g, itts_kv *kv, int32_t n, const int32_t 
     }
     TRY(push_slots(kv, slots, n));
     TRY(set_batch_slots(kv, slots, n));
+    TRY(reset_step_sync(kv));
     DecodeView dv = decode_view(kv, n);
-    decode_forward(m, dv, kv->db, g->stream);
-    CUDA_TRY(cudaGetLastError());
+    CUDA_TRY(decode_forward(m, dv, kv->db, g->stream));
+    CUDA_TRY(cudaStreamSynchronize(g->stream));
+    TRY(check_step_sync(kv));
     for (int i = 0; i < n; ++i) kv->h_state[slots[i]].valid_len += 1;
     TRY(push_slots(kv, slots, n));
     if (logits_out)
@@ -847,14 +957,8 @@ extern "C" int itts_sample_next_token(itts_gpt *g, float *logits, int32_t n,
 // decode loop (sampler.rs:340-392): prefill every request, sample, then replay the
 // captured decode step until every request stopped.
 // ------------------------------------------------------------------------------
-static int get_graph(itts_kv *kv, int nb, cudaGraphExec_t *out) {
-    if (kv->graphs[nb]) { *out = kv->graphs[nb]; return ITTS_OK; }
+static void launch_step_sample(itts_kv *kv, int nb, cudaStream_t st) {
     itts_gpt *g = kv->gpt;
-    cudaStream_t st = g->stream;
-    cudaGraph_t graph = nullptr;
-    CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-    DecodeView dv = decode_view(kv, nb);
-    decode_forward(g->m, dv, kv->db, st);
     SampleArgs a{};
     a.slots = kv->d_slots;
     a.batch_slot = kv->d_batch_slot;
@@ -867,7 +971,25 @@ static int get_graph(itts_kv *kv, int nb, cudaGraphExec_t *out) {
     a.codes = kv->d_codes;
     a.codes_stride = kv->codes_stride;
     launch_sample(a, st);
-    CUDA_TRY(cudaStreamEndCapture(st, &graph));
+}
+
+// One decode step (forward + sampler) captured as a CUDA graph per batch size.
+static int get_graph(itts_kv *kv, int nb, cudaGraphExec_t *out) {
+    if (kv->graphs[nb]) { *out = kv->graphs[nb]; return ITTS_OK; }
+    itts_gpt *g = kv->gpt;
+    cudaStream_t st = g->stream;
+    cudaGraph_t graph = nullptr;
+    CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+    DecodeView dv = decode_view(kv, nb);
+    const cudaError_t fe = decode_forward(g->m, dv, kv->db, st);
+    launch_step_sample(kv, nb, st);
+    const cudaError_t ce = cudaStreamEndCapture(st, &graph);
+    if (fe != cudaSuccess || ce != cudaSuccess) {
+        if (graph) cudaGraphDestroy(graph);
+        cudaGetLastError();
+        return set_err(ITTS_E_CUDA, std::string("decode-step graph capture failed: ") +
+                                        cudaGetErrorString(fe != cudaSuccess ? fe : ce));
+    }
     cudaGraphExec_t exec = nullptr;
     CUDA_TRY(cudaGraphInstantiate(&exec, graph, 0));
     kv->graph_defs[nb] = graph;
@@ -921,8 +1043,13 @@ static int generate_impl(itts_gpt *g, itts_kv *kv, int n, const int *slots,
     }
     TRY(push_slots(kv, slots, n));
     TRY(set_batch_slots(kv, slots, n));
-    cudaGraphExec_t graph;
-    TRY(get_graph(kv, n, &graph));
+    TRY(reset_step_sync(kv));
+    cudaGraphExec_t graph = nullptr;
+    if (!kv->graph_failed[n] && get_graph(kv, n, &graph) != ITTS_OK) {
+        kv->graph_failed[n] = 1;  // e.g. a cooperative launch the driver cannot capture
+        graph = nullptr;
+    }
+    DecodeView step_dv = decode_view(kv, n);
     SampleArgs a{};
     a.slots = kv->d_slots;
     a.batch_slot = kv->d_batch_slot;
@@ -943,7 +1070,14 @@ static int generate_impl(itts_gpt *g, itts_kv *kv, int n, const int *slots,
         for (int r = 0; r < n; ++r) any |= kv->h_state[slots[r]].active != 0;
         if (!any || launched >= max_replays) break;
         const int todo = std::min(chunk, max_replays - launched);
-        for (int i = 0; i < todo; ++i) CUDA_TRY(cudaGraphLaunch(graph, st));
+        for (int i = 0; i < todo; ++i) {
+            if (graph) {
+                CUDA_TRY(cudaGraphLaunch(graph, st));
+            } else {
+                CUDA_TRY(decode_forward(m, step_dv, kv->db, st));
+                launch_step_sample(kv, n, st);
+            }
+        }
         launched += todo;
         chunk = std::min(chunk * 2, 64);
     }
@@ -961,6 +1095,7 @@ static int generate_impl(itts_gpt *g, itts_kv *kv, int n, const int *slots,
                                      sizeof(int32_t) * s.n_codes, cudaMemcpyDeviceToHost, st));
     }
     CUDA_TRY(cudaStreamSynchronize(st));
+    TRY(check_step_sync(kv));
     CUDA_TRY(cudaEventElapsedTime(&g->last_prefill_ms, g->ev[0], g->ev[1]));
     CUDA_TRY(cudaEventElapsedTime(&g->last_decode_ms, g->ev[1], g->ev[2]));
     g->last_launches = launched;
@@ -1007,47 +1142,69 @@ extern "C" int itts_gpt_last_timing(const itts_gpt *g, float *prefill_ms, float 
 }
 
 // ------------------------------------------------------------------------------
-// measurement: the weight-streaming kernels of one decode step, replayed
+// measurement: the decode-step forward alone, replayed on fixed inputs
 // ------------------------------------------------------------------------------
-extern "C" int itts_bench_weight_stream(itts_gpt *g, itts_kv *kv, int32_t nb, int32_t iters,
-                                        float *ms, int32_t *launches) {
+extern "C" int itts_bench_decode_forward(itts_gpt *g, itts_kv *kv, int32_t nb, int32_t kv_len,
+                                         int32_t iters, float *ms, int32_t *launches) {
     if (!g || !kv || kv->gpt != g || !ms) return validation("gpt", "null pointer");
     if (nb <= 0 || nb > kv->max_batch || iters <= 0) return validation("nb", "out of range");
+    if (kv_len < 1 || kv_len + 1 > kv->max_seq) return validation("kv_len", "out of range");
     CUDA_TRY(cudaSetDevice(g->device));
     cudaStream_t st = g->stream;
-    const ModelView &m = g->m;
     std::vector<int> slots(nb);
-    for (int i = 0; i < nb; ++i) slots[i] = i;
-    TRY(set_batch_slots(kv, slots.data(), nb));
-    DecodeView dv = decode_view(kv, nb);
-    DecodeBufs &b = kv->db;
-    cudaGraph_t graph = nullptr;
-    cudaGraphExec_t exec = nullptr;
-    CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-    int n_launch = 0;
-    const int per = (nb + 7) / 8;
-    for (int l = 0; l < m.n_layers; ++l) {
-        const LayerW &L = m.layers[l];
-        launch_gemv(L.c_attn, m.sb_half, EPI_QKV, 1, L.ln1_w, L.ln1_b, nullptr, nullptr, b.x, b.q, nb, &dv, l, st);
-        launch_gemv(L.c_proj, m.sb_half, EPI_RESID, 0, nullptr, nullptr, nullptr, nullptr, b.attn, b.x, nb, nullptr, l, st);
-        launch_gemv(L.c_fc, m.sb_half, EPI_GELU, 1, L.ln2_w, L.ln2_b, nullptr, nullptr, b.x, b.u, nb, nullptr, l, st);
-        launch_gemv(L.mlp_proj, m.sb_half, EPI_RESID, 0, nullptr, nullptr, nullptr, nullptr, b.u, b.x, nb, nullptr, l, st);
-        n_launch += 4 * per;
+    std::vector<SlotState> saved(nb);
+    for (int i = 0; i < nb; ++i) {
+        slots[i] = i;
+        saved[i] = kv->h_state[i];
+        SlotState &s = kv->h_state[i];
+        s.active = 1;
+        s.valid_len = kv_len;  // the forward appends position kv_len and reads 0..kv_len
+        s.tok = 5 + i;
+        s.pos = 2;
+        s.max_seq = kv->max_seq;
     }
-    launch_gemv(m.mel_head, m.sb_half, EPI_PLAIN, 2, m.ln_f_w, m.ln_f_b, m.final_w, m.final_b, b.x, b.logits, nb, nullptr, 0, st);
-    n_launch += per;
-    CUDA_TRY(cudaStreamEndCapture(st, &graph));
-    CUDA_TRY(cudaGraphInstantiate(&exec, graph, 0));
-    for (int i = 0; i < 3; ++i) CUDA_TRY(cudaGraphLaunch(exec, st));
+    TRY(push_slots(kv, slots.data(), nb));
+    TRY(set_batch_slots(kv, slots.data(), nb));
+    TRY(reset_step_sync(kv));
+    DecodeView dv = decode_view(kv, nb);
+    for (int i = 0; i < 3; ++i) CUDA_TRY(decode_forward(g->m, dv, kv->db, st));
     CUDA_TRY(cudaEventRecord(g->ev[0], st));
-    for (int i = 0; i < iters; ++i) CUDA_TRY(cudaGraphLaunch(exec, st));
+    for (int i = 0; i < iters; ++i) CUDA_TRY(decode_forward(g->m, dv, kv->db, st));
     CUDA_TRY(cudaEventRecord(g->ev[1], st));
     CUDA_TRY(cudaStreamSynchronize(st));
+    TRY(check_step_sync(kv));
     float t = 0.f;
     CUDA_TRY(cudaEventElapsedTime(&t, g->ev[0], g->ev[1]));
-    cudaGraphExecDestroy(exec);
-    cudaGraphDestroy(graph);
+    for (int i = 0; i < nb; ++i) kv->h_state[i] = saved[i];
+    TRY(push_slots(kv, slots.data(), nb));
+    CUDA_TRY(cudaStreamSynchronize(st));
     *ms = t / (float)iters;
-    if (launches) *launches = n_launch;
+    if (launches) *launches = decode_forward_launches(g->m, kv->db, nb);
     return ITTS_OK;
+}
+
+// Runs one decode-step forward like itts_bench_decode_forward with per-CTA stage
+// timestamps (globaltimer, ns) recorded by the persistent kernel; out receives
+// [grid][events_per_cta] values (0 where a CTA recorded nothing).
+extern "C" int itts_bench_trace(itts_gpt *g, itts_kv *kv, int32_t nb, int32_t kv_len,
+                                unsigned long long *out, int32_t out_len, int32_t *grid,
+                                int32_t *events_per_cta) {
+    if (!g || !kv || kv->gpt != g || !out || !grid || !events_per_cta) return validation("gpt", "null pointer");
+    if (kv->db.mk_grid <= 0 || nb > MK_MAX_NB) return validation("nb", "the persistent kernel is not used for this batch");
+    const size_t n = (size_t)kv->db.mk_grid * MK_TRACE_EVENTS;
+    if ((size_t)out_len < n) return validation("out_len", "too small");
+    CUDA_TRY(cudaSetDevice(g->device));
+    unsigned long long *d = nullptr;
+    CUDA_TRY(cudaMalloc(&d, n * sizeof(unsigned long long)));
+    cudaMemset(d, 0, n * sizeof(unsigned long long));
+    kv->db.trace = d;
+    float ms = 0.f;
+    int32_t launches = 0;
+    const int rc = itts_bench_decode_forward(g, kv, nb, kv_len, 1, &ms, &launches);
+    kv->db.trace = nullptr;
+    if (rc == ITTS_OK) cudaMemcpy(out, d, n * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
+    cudaFree(d);
+    *grid = kv->db.mk_grid;
+    *events_per_cta = MK_TRACE_EVENTS;
+    return rc;
 }

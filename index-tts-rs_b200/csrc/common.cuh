@@ -1,10 +1,7 @@
 // common.cuh -- device-side data layout shared by the decoder kernels.
 //
 // HBM layout (one itts_gpt per device):
-//   quantized linear: q    u8  [out, in]      (the reference's u32 [out, in/4] words,
-//                                               read as bytes: byte j of word i/4 is q[i])
-//                     s, b f16|f32 [out, in/64] (affine group scale / offset)
-//                     bias f32 [out]
+//   quantized linear: tiled int8 weights + (scale, offset) pairs, see mk.h; bias f32 [out]
 //   LayerNorm weight/bias, embedding tables: f32 as in the checkpoint.
 //   KV cache (itts_kv): K and V each fp16 [layer][slot][head][max_seq][64], so one
 //   head's keys are contiguous 128-byte rows for the split-K decode attention.
@@ -24,19 +21,6 @@ constexpr int kStartText = 0;
 constexpr int kStopText = 1;
 constexpr float kAttnScale = 0.125f;  // 64^-0.5 (gpt.rs:67)
 constexpr float kNormEps = 1e-5f;     // gpt.rs:42
-
-struct QLinear {
-    const uint8_t *q;
-    const void *scales;
-    const void *biases;
-    const float *bias;
-    int out, in;
-};
-
-struct LayerW {
-    const float *ln1_w, *ln1_b, *ln2_w, *ln2_b;
-    QLinear c_attn, c_proj, c_fc, mlp_proj;
-};
 
 // Per-request decode state, resident in HBM so a captured decode-step graph can
 // replay unchanged: the sampler kernel writes the next token / position here and
@@ -61,11 +45,6 @@ struct SlotState {
     uint64_t rng;                 // SamplerRng state (sampler.rs:24-26)
     uint64_t seen[kBitsetWords];  // SeenTokenBitSet (sampler.rs:67-69)
 };
-
-__device__ __forceinline__ float load_sb(const void *p, bool half_sb, size_t idx) {
-    return half_sb ? __half2float(reinterpret_cast<const __half *>(p)[idx])
-                   : reinterpret_cast<const float *>(p)[idx];
-}
 
 // Streaming 128-bit load of weights read once per step (no L1 allocation).
 __device__ __forceinline__ uint4 ld_stream(const void *p) {

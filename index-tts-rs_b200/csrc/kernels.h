@@ -1,6 +1,7 @@
 // kernels.h -- host launchers of the decoder kernels (all on one CUDA stream).
 #pragma once
 #include "common.cuh"
+#include "mk.h"
 
 namespace itts {
 
@@ -20,16 +21,23 @@ struct ModelView {
     bool sb_half;
     const float *text_emb, *lang_emb, *mel_emb, *mel_pos, *text_pos;
     const float *ln_f_w, *ln_f_b, *final_w, *final_b;
-    QLinear mel_head;
-    const LayerW *layers;  // host array [n_layers]
+    MkLin mel_head;
+    const MkLayer *layers;    // host array [n_layers]
+    const MkLayer *d_layers;  // the same, in device memory (persistent kernel)
 };
 
 // Decode-step scratch (sized for max_batch columns).
 struct DecodeBufs {
-    float *x, *q, *attn, *u, *logits;
+    float *x, *n, *n2, *q, *attn, *u, *logits;  // q holds [max_batch][3d] (QKV output)
     float *partials;  // [max_batch][H][max_splits][2 + 64]
     int *counters;    // [max_batch][H], zero between launches
     int max_splits, split_len;
+    // persistent decode-step kernel state (LL activation buffers, see mk.h)
+    uint64_t *qkv_ll, *attn_ll, *ao_ll, *h_ll, *u_ll, *x_ll;
+    uint32_t *epoch;  // [grid] launch counters, never reset
+    int *err;
+    unsigned long long *trace;  // optional per-CTA stage timestamps
+    int mk_grid, mk_nslot[MK_MAX_NB + 1];
 };
 
 // Prefill scratch for one request of up to max_tokens positions.
@@ -40,18 +48,27 @@ struct PrefillBufs {
 
 void kernels_init();  // one-time function attributes (dynamic shared memory)
 
-// y/x rows are batch columns 0..nb-1 (stride = in / out features).
-void launch_gemv(const QLinear &W, bool sb_half, int epi, int ln_mode, const float *ln_w,
-                 const float *ln_b, const float *ln2_w, const float *ln2_b, const float *x,
-                 float *y, int nb, const DecodeView *dv, int layer, cudaStream_t st);
-
 void launch_embed_step(const ModelView &m, const DecodeView &dv, float *x, cudaStream_t st);
 
-void launch_attn_decode(const DecodeView &dv, int layer, const float *q, DecodeBufs &b,
-                        cudaStream_t st);
+void launch_attn_decode(const DecodeView &dv, int layer, const float *q, int q_stride,
+                        DecodeBufs &b, cudaStream_t st);
 
-// Whole decode forward for dv.nb columns: embedding, all layers, double LN + head.
-void decode_forward(const ModelView &m, const DecodeView &dv, DecodeBufs &b, cudaStream_t st);
+void launch_layernorm_rows(const float *x, const float *w, const float *b, int rows, int d,
+                           float *y, cudaStream_t st);
+
+// y[t, :] = x[t, :] . W^T + bias with an epilogue, for t < T.  In decode mode (dv != null)
+// the QKV epilogue appends row t's K/V to slot batch_slot[t] at its valid_len; in prefill
+// mode (dv == null, kv_slot >= 0) row t's K/V go to position t of kv_slot.
+void launch_gemm(int epi, const MkLin &W, const float *x, float *y, int T, const DecodeView *dv,
+                 __half *k_cache, __half *v_cache, int kv_slot, int n_slots, int n_heads,
+                 int max_seq, int layer, int d, cudaStream_t st);
+
+// Decode forward for dv.nb columns: the persistent kernel when nb <= MK_MAX_NB (one
+// launch), else the GEMM path (embedding, 7 launches per layer, head).
+cudaError_t decode_forward(const ModelView &m, const DecodeView &dv, DecodeBufs &b,
+                           cudaStream_t st);
+// Number of kernels decode_forward launches for nb columns.
+int decode_forward_launches(const ModelView &m, const DecodeBufs &b, int nb);
 
 // Prefill of one request already embedded in pb.x[0..T): all layers; K/V of every
 // position written to `slot`; logits of position T-1 into logits_row.

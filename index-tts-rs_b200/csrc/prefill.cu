@@ -81,6 +81,11 @@ __global__ void __launch_bounds__(256) layernorm_rows_kernel(const float *x, con
         y[(size_t)t * d + i] = (row[i] - mean) * rstd * w[i] + b[i];
 }
 
+void launch_layernorm_rows(const float *x, const float *w, const float *b, int rows, int d,
+                           float *y, cudaStream_t st) {
+    layernorm_rows_kernel<<<rows, 256, 0, st>>>(x, w, b, d, y);
+}
+
 // ---------------------------------------------------------------------------
 // GEMM: y[t, o] = x[t, :] . W[o, :] + bias[o] for T prompt positions.
 // CTA tile 64 positions x 64 outputs, K step = one quantization group (64);
@@ -88,14 +93,16 @@ __global__ void __launch_bounds__(256) layernorm_rows_kernel(const float *x, con
 // all 64 positions.  Thread tile 4 x 4.
 // ---------------------------------------------------------------------------
 struct GemmParams {
-    QLinear W;
-    bool sb_half;
+    MkLin W;
     const float *x;  // [T, K]
     float *y;        // [T, OUT]
     int T;
-    // EPI_QKV: K/V of position t into the cache at position t
+    // EPI_QKV: prefill writes row t's K/V at position t of kv_slot; decode (slots != null)
+    // writes them at the valid_len of slot batch_slot[t]
     __half *k_cache, *v_cache;
-    int slot, n_slots, n_heads, max_seq, layer, d;
+    const SlotState *slots;
+    const int *batch_slot;
+    int kv_slot, n_slots, n_heads, max_seq, layer, d;
 };
 
 template <int EPI>
@@ -103,7 +110,7 @@ __global__ void __launch_bounds__(256) gemm_q8_kernel(GemmParams p) {
     constexpr int BM = 64, BN = 64, BK = 64, PAD = 4;
     __shared__ __align__(16) float Xs[BK][BM + PAD];
     __shared__ __align__(16) float Ws[BK][BN + PAD];
-    const int K = p.W.in, OUT = p.W.out, G = K / kGroup;
+    const int K = p.W.in, OUT = p.W.out;
     const int t0 = blockIdx.y * BM, o0 = blockIdx.x * BN;
     const int tid = threadIdx.x, ty = tid >> 4, tx = tid & 15;
     float acc[4][4] = {};
@@ -121,19 +128,29 @@ __global__ void __launch_bounds__(256) gemm_q8_kernel(GemmParams p) {
                 Xs[kq + j + 3][t] = v.w;
             }
         }
-        {  // W tile: thread dequantizes 16 bytes of one output row
-            const int r = tid >> 2, kq = (tid & 3) * 16;
+        {  // W tile: thread dequantizes the 16 bytes (fragment order) at [16c, 16c+16)
+            // of one row's quantization group
+            const int r = tid >> 2, c = tid & 3;
             const int o = o0 + r;
             float s = 0.f, z = 0.f;
             uint4 w = make_uint4(0, 0, 0, 0);
             if (o < OUT) {
-                w = ld_stream(p.W.q + (size_t)o * K + k0 + kq);
-                s = load_sb(p.W.scales, p.sb_half, (size_t)o * G + k0 / kGroup);
-                z = load_sb(p.W.biases, p.sb_half, (size_t)o * G + k0 / kGroup);
+                w = ld_stream(p.W.tiles + mk_q_offset(p.W, o, k0) + c * 16);
+                const uint8_t *sb = p.W.tiles + mk_sb_offset(p.W, o, k0);
+                if (p.W.sbb == 4) {
+                    const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(sb));
+                    s = f.x; z = f.y;
+                } else {
+                    const float2 f = *reinterpret_cast<const float2 *>(sb);
+                    s = f.x; z = f.y;
+                }
             }
             const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-            for (int j = 0; j < 16; ++j) Ws[kq + j][r] = s * byte_to_float(ww[j >> 2], j & 3) + z;
+            for (int pb = 0; pb < 16; ++pb) {
+                const int k = (pb >> 2) * 16 + ((pb >> 1) & 1) * 8 + 2 * c + (pb & 1);
+                Ws[k][r] = s * byte_to_float(ww[pb >> 2], pb & 3) + z;
+            }
         }
         __syncthreads();
 #pragma unroll 8
@@ -166,8 +183,16 @@ __global__ void __launch_bounds__(256) gemm_q8_kernel(GemmParams p) {
                 if (o >= p.d) {
                     const int rr = o - p.d, which = rr / p.d, oo = rr - which * p.d;
                     __half *cache = which == 0 ? p.k_cache : p.v_cache;
-                    if (t < p.max_seq)
-                        cache[kv_index(p.layer, p.slot, oo >> 6, t, p.n_slots, p.n_heads, p.max_seq) +
+                    int slot = p.kv_slot, pos = t;
+                    bool write = t < p.max_seq;
+                    if (p.slots) {
+                        slot = p.batch_slot[t];
+                        const SlotState &st = p.slots[slot];
+                        pos = st.valid_len;
+                        write = st.active && pos < p.max_seq;
+                    }
+                    if (write)
+                        cache[kv_index(p.layer, slot, oo >> 6, pos, p.n_slots, p.n_heads, p.max_seq) +
                               (oo & 63)] = __float2half_rn(v);
                 }
             }
@@ -175,8 +200,27 @@ __global__ void __launch_bounds__(256) gemm_q8_kernel(GemmParams p) {
     }
 }
 
-static void launch_gemm(int epi, const GemmParams &p, cudaStream_t st) {
-    dim3 grid((p.W.out + 63) / 64, (p.T + 63) / 64);
+void launch_gemm(int epi, const MkLin &W, const float *x, float *y, int T, const DecodeView *dv,
+                 __half *k_cache, __half *v_cache, int kv_slot, int n_slots, int n_heads,
+                 int max_seq, int layer, int d, cudaStream_t st) {
+    GemmParams p{};
+    p.W = W;
+    p.x = x;
+    p.y = y;
+    p.T = T;
+    p.k_cache = k_cache;
+    p.v_cache = v_cache;
+    p.kv_slot = kv_slot;
+    p.n_slots = n_slots;
+    p.n_heads = n_heads;
+    p.max_seq = max_seq;
+    p.layer = layer;
+    p.d = d;
+    if (dv) {
+        p.slots = dv->slots;
+        p.batch_slot = dv->batch_slot;
+    }
+    dim3 grid((W.out + 63) / 64, (T + 63) / 64);
     switch (epi) {
     case EPI_PLAIN: gemm_q8_kernel<EPI_PLAIN><<<grid, 256, 0, st>>>(p); break;
     case EPI_GELU: gemm_q8_kernel<EPI_GELU><<<grid, 256, 0, st>>>(p); break;
@@ -240,33 +284,24 @@ void prefill_forward(const ModelView &m, const DecodeView &dv, int slot, int T, 
                      float *logits_row, cudaStream_t st) {
     const int d = m.d;
     for (int l = 0; l < m.n_layers; ++l) {
-        const LayerW &L = m.layers[l];
-        layernorm_rows_kernel<<<T, 256, 0, st>>>(pb.x, L.ln1_w, L.ln1_b, d, pb.n);
-        GemmParams g{};
-        g.sb_half = m.sb_half;
-        g.T = T;
-        g.k_cache = dv.k_cache;
-        g.v_cache = dv.v_cache;
-        g.slot = slot;
-        g.n_slots = dv.n_slots;
-        g.n_heads = dv.n_heads;
-        g.max_seq = dv.max_seq;
-        g.layer = l;
-        g.d = d;
-        g.W = L.c_attn; g.x = pb.n; g.y = pb.qkv;
-        launch_gemm(EPI_QKV, g, st);
+        const MkLayer &L = m.layers[l];
+        launch_layernorm_rows(pb.x, L.ln1_w, L.ln1_b, T, d, pb.n, st);
+        launch_gemm(EPI_QKV, L.qkv, pb.n, pb.qkv, T, nullptr, dv.k_cache, dv.v_cache, slot,
+                    dv.n_slots, dv.n_heads, dv.max_seq, l, d, st);
         attn_prefill_kernel<<<dim3((T + 63) / 64, m.n_heads), 64, 0, st>>>(pb.qkv, T, d, pb.attn);
-        g.W = L.c_proj; g.x = pb.attn; g.y = pb.x;
-        launch_gemm(EPI_RESID, g, st);
-        layernorm_rows_kernel<<<T, 256, 0, st>>>(pb.x, L.ln2_w, L.ln2_b, d, pb.n);
-        g.W = L.c_fc; g.x = pb.n; g.y = pb.u;
-        launch_gemm(EPI_GELU, g, st);
-        g.W = L.mlp_proj; g.x = pb.u; g.y = pb.x;
-        launch_gemm(EPI_RESID, g, st);
+        launch_gemm(EPI_RESID, L.proj, pb.attn, pb.x, T, nullptr, nullptr, nullptr, -1, 0, 0, 0, l,
+                    d, st);
+        launch_layernorm_rows(pb.x, L.ln2_w, L.ln2_b, T, d, pb.n, st);
+        launch_gemm(EPI_GELU, L.fc, pb.n, pb.u, T, nullptr, nullptr, nullptr, -1, 0, 0, 0, l, d, st);
+        launch_gemm(EPI_RESID, L.mlp, pb.u, pb.x, T, nullptr, nullptr, nullptr, -1, 0, 0, 0, l, d,
+                    st);
     }
     // ln_f then final_norm on the last row, then mel_head (gpt.rs:673-692)
-    launch_gemv(m.mel_head, m.sb_half, EPI_PLAIN, 2, m.ln_f_w, m.ln_f_b, m.final_w, m.final_b,
-                pb.x + (size_t)(T - 1) * d, logits_row, 1, nullptr, 0, st);
+    const float *last = pb.x + (size_t)(T - 1) * d;
+    launch_layernorm_rows(last, m.ln_f_w, m.ln_f_b, 1, d, pb.n, st);
+    launch_layernorm_rows(pb.n, m.final_w, m.final_b, 1, d, pb.n + d, st);
+    launch_gemm(EPI_PLAIN, m.mel_head, pb.n + d, logits_row, 1, nullptr, nullptr, nullptr, -1, 0, 0,
+                0, 0, d, st);
 }
 
 }  // namespace itts

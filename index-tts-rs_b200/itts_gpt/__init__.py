@@ -17,6 +17,7 @@ host fallback.
 from __future__ import annotations
 
 import ctypes as C
+import weakref
 from dataclasses import dataclass, field
 from typing import Sequence
 
@@ -166,6 +167,7 @@ class Gpt:
     def __init__(self, handle: int, device: int):
         self._h = C.c_void_p(handle)
         self.device = device
+        self._caches: "weakref.WeakSet[KvCache]" = weakref.WeakSet()
         dims = np.zeros(10, np.int32)
         _check(load_lib().itts_gpt_dims(self._h, _ptr(dims)))
         (self.n_layers, self.d, self.n_heads, self.ff, self.mel_vocab, self.text_vocab,
@@ -201,6 +203,10 @@ class Gpt:
         return int(load_lib().itts_gpt_num_layers(self._h))
 
     def close(self) -> None:
+        """Frees the device weights; caches made from this model are freed first (the C
+        ABI requires every itts_kv of a model to be freed before the model)."""
+        for kv in list(self._caches):
+            kv.close()
         if self._h:
             load_lib().itts_gpt_free(self._h)
             self._h = C.c_void_p()
@@ -261,6 +267,7 @@ class KvCache:
         self._h = C.c_void_p()
         self.gpt = gpt
         _check(load_lib().itts_kv_create(gpt._h, int(max_seq), int(max_batch), C.byref(self._h)))
+        gpt._caches.add(self)
 
     def reset(self, slot: int = -1) -> None:
         _check(load_lib().itts_kv_reset(self._h, slot))

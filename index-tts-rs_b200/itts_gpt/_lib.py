@@ -73,8 +73,10 @@ SIGNATURES = [
      [_P, _P, _I32, C.POINTER(CodePromptC), C.POINTER(SamplingParamsC), _P, _P, _I32, _P]),
     ("itts_gpt_last_timing", C.c_int,
      [_P, C.POINTER(C.c_float), C.POINTER(C.c_float), C.POINTER(_I32)]),
-    ("itts_bench_weight_stream", C.c_int,
-     [_P, _P, _I32, _I32, C.POINTER(C.c_float), C.POINTER(_I32)]),
+    ("itts_bench_decode_forward", C.c_int,
+     [_P, _P, _I32, _I32, _I32, C.POINTER(C.c_float), C.POINTER(_I32)]),
+    ("itts_bench_trace", C.c_int,
+     [_P, _P, _I32, _I32, _P, _I32, C.POINTER(_I32), C.POINTER(_I32)]),
 ]
 
 _lib = None
