@@ -290,6 +290,18 @@ def _bench_decode_forward(gpt, kv, kv_len, iters):
     return ms.value, n.value
 
 
+def run_profile_case(args):
+    """A small case for profilers: the full-size decode-step forward alone, 3 warm-up
+    launches then `--profile-iters` timed ones, at KV length `--profile-decode`."""
+    import itts_gpt as ig
+    cfg, w = make_model()
+    gpt = ig.Gpt.from_weights(w)
+    kv = ig.KvCache(gpt, max_seq=args.profile_decode + 8, max_batch=1)
+    ms, n = _bench_decode_forward(gpt, kv, args.profile_decode, iters=args.profile_iters)
+    print(json.dumps({"profile_case": "decode-step forward", "kv_len": args.profile_decode,
+                      "ms_per_launch": ms, "launches_per_step": n}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -297,7 +309,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-decode", type=int, default=0, metavar="KV_LEN",
+                    help="profiler case: only the decode-step forward at this KV length")
+    ap.add_argument("--profile-iters", type=int, default=2)
     args = ap.parse_args()
+    if args.profile_decode > 0:
+        run_profile_case(args)
+        return
     rank, world, local_rank = dist_env()
     if world > 1:
         import datetime

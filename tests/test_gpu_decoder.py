@@ -115,40 +115,84 @@ def test_generate_sampled_matches_checker(small, small_cfg):
     r = ig.SamplerRng(77)
     codes = ig.generate_codes_after(gpt, ig.CodePrompt(text, conds, 1, min_codes=n), kv, p, r)
     assert len(codes) == n
-    okv = om.kv(512)
-    logits = om.prefill(okv, text, conds, 1)
-    seen = ig.SeenTokenBitSet.new_with_initial_tokens()
-    st = ig.SamplerRng(77).state
-    agree = 0
-    for i, c in enumerate(codes):
-        logits[8193] = -np.inf  # min_codes (sampler.rs:372-376)
-        tok, st = orc.sample_next_token(logits, seen.words, orc.params_c(False, 30, 0.8, 0.8, 10.0), st)
-        agree += tok == c
-        seen.insert(c)
-        if i + 1 < n:
-            logits = om.step(okv, c, i + 2)
-    assert agree >= 0.95 * n, agree
+    agree, st, bad = _teacher_forced_agreement(om, ig.CodePrompt(text, conds, 1, min_codes=n),
+                                               p, codes, ig.SamplerRng(77).state)
+    assert not bad, bad  # every differing step is a near-tie within tolerance
+    assert agree >= 0.95, agree
     assert r.state == st
+
+
+# Largest logit difference the parity bound allows (north_star: max-abs 2e-2).
+LOGIT_TOL = 2e-2
+
+
+def _flip_margin(logits, seen_words, params, state, tok):
+    """How far the checker's choice is from `tok` at this step, in the units the logit
+    tolerance bounds.  Greedy: the logit gap between the best token and `tok`.  Sampled:
+    the distance of this step's uniform draw from `tok`'s cumulative-probability interval
+    (as a fraction of the active mass), or inf when `tok` is not a candidate.  Follows
+    sampler.rs:204-283 in float64, which is precise enough for a margin."""
+    lg = np.asarray(logits, np.float64).copy()
+    pen = params.repetition_penalty
+    if abs(pen - 1.0) > 1.1920929e-7:
+        for i in range(min(lg.size, 129 * 64)):
+            if (int(seen_words[i // 64]) >> (i % 64)) & 1:
+                lg[i] = lg[i] * pen if lg[i] < 0 else lg[i] / pen
+    fin = np.isfinite(lg)
+    if params.greedy:
+        return float(lg[fin].max() - lg[tok]) if fin[tok] else np.inf
+    v = np.where(fin, lg / params.temperature, -np.inf)
+    order = sorted(range(v.size), key=lambda i: (-v[i], i))
+    k = v.size if params.top_k == 0 else min(params.top_k, v.size)
+    order = order[:k]
+    mx = v[order[0]] if np.isfinite(v[order[0]]) else 0.0
+    probs = np.array([np.exp(v[i] - mx) if np.isfinite(v[i]) else 0.0 for i in order])
+    norm = probs / probs.sum()
+    active, cum = len(order), 0.0
+    for i in range(len(order)):
+        if i > 0 and cum > params.top_p:
+            active = i
+            break
+        cum += norm[i]
+    if tok not in order[:active]:
+        return np.inf
+    j = order.index(tok)
+    c = np.concatenate([[0.0], np.cumsum(probs[:active])]) / probs[:active].sum()
+    u = ig.SamplerRng.from_state(state).next_f32()
+    return float(max(c[j] - u, u - c[j + 1], 0.0))
+
+
+def _flip_allowed(params, margin):
+    """A different token is within tolerance when the margin is inside the band a logit
+    error of LOGIT_TOL can move: 2*tol for a greedy gap, exp(2*tol/T) - 1 for a sampled draw."""
+    band = 2 * LOGIT_TOL if params.greedy else np.expm1(2 * LOGIT_TOL / params.temperature)
+    return margin <= band
 
 
 def _teacher_forced_agreement(om, prompt, params, codes, rng_state):
     """Checker's sampler along the device's code path: fraction of steps where it picks
-    the device's token, and the SamplerRng state after the same draws."""
+    the device's token, the SamplerRng state after the same draws, and the steps where
+    the two differ by more than the logit tolerance can explain."""
     okv = om.kv(1024)
     logits = om.prefill(okv, prompt.text_tokens, prompt.conds, prompt.lang_id, prompt.prior_codes)
     seen = ig.SeenTokenBitSet.new_with_initial_tokens()
     pc = orc.params_c(params.greedy, params.top_k, params.top_p, params.temperature,
                       params.repetition_penalty)
-    st, agree = rng_state, 0
+    st, agree, bad = rng_state, 0, []
     for i, c in enumerate(codes):
         if i < prompt.min_codes:
             logits[8193] = -np.inf
+        before, st0, words = logits.copy(), st, np.array(seen.words, np.uint64)
         tok, st = orc.sample_next_token(logits, seen.words, pc, st)
         agree += tok == c
+        if tok != c:
+            m = _flip_margin(before, words, params, st0, c)
+            if not _flip_allowed(params, m):
+                bad.append((i, tok, c, m))
         seen.insert(c)
         if i + 1 < len(codes):
             logits = om.step(okv, c, len(prompt.prior_codes) + i + 2)
-    return agree / max(1, len(codes)), st
+    return agree / max(1, len(codes)), st, bad
 
 
 @pytest.mark.parametrize("n_req", [3, 6])
@@ -169,9 +213,10 @@ def test_generate_batch_matches_checker(small, small_cfg, n_req):
     batch = ig.generate_batch(gpt, prompts, kvb, params, rb)
     for i in range(n_req):
         assert len(batch[i]) == params[i].max_mel_tokens
-        agree, st = _teacher_forced_agreement(om, prompts[i], params[i], batch[i],
-                                              ig.SamplerRng(100 + i).state)
-        assert agree >= 0.95, (i, agree)
+        agree, st, bad = _teacher_forced_agreement(om, prompts[i], params[i], batch[i],
+                                                   ig.SamplerRng(100 + i).state)
+        assert not bad, (i, bad)  # every differing step is a near-tie within tolerance
+        assert agree >= 0.9, (i, agree)
         assert rb[i].state == st
 
 
