@@ -165,6 +165,26 @@ int itts_sample_next_token(itts_gpt *gpt, float *logits, int32_t n_logits,
                            const itts_sampling_params *params, uint64_t *rng_state,
                            int32_t *token_out);
 
+/* No counterpart in the reference.  itts_sample_next_token for callers that cannot
+ * allocate device memory: a process whose GPU memory belongs to another runtime (a
+ * serving framework's allocator, or a fixed budget that must not grow), or a real-time
+ * thread, where cudaMalloc / cudaFree would synchronize the device.  It needs no handle
+ * and allocates nothing: it runs on the calling thread's current device, on `stream` (a
+ * cudaStream_t; NULL is the default stream), and returns once that stream has
+ * synchronized.  Its device working set lives in one static array per device (67,072
+ * bytes, held by every GPU that loads the library until exit), so
+ * 1 <= n_logits <= ITTS_STATIC_SAMPLE_MAX_LOGITS; a longer slice is rejected with
+ * ITTS_E_VALIDATION.  The first call on a device does the set-up (it looks up the array's
+ * device address and sets the kernel's shared-memory limit); make it before any stream
+ * capture.  All calls on one device share the array: calls that overlap on the GPU (from
+ * several host threads, or on several streams) race and return wrong results, so
+ * serialize them. */
+#define ITTS_STATIC_SAMPLE_MAX_LOGITS 16384
+int itts_sample_next_token_static(float *logits, int32_t n_logits,
+                                  const uint64_t seen_words[ITTS_BITSET_WORDS],
+                                  const itts_sampling_params *params, uint64_t *rng_state,
+                                  int32_t *token_out, void *stream);
+
 /* generate_codes_after (sampler.rs:340-392); generate_codes (sampler.rs:309-326) is the
  * case n_prior == 0, min_codes == 0.  Prefill, then a CUDA-graph decode step per token
  * with sampling on the device; only the codes return to the host.  codes_out must hold

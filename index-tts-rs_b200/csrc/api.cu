@@ -17,6 +17,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <thread>
 #include <unordered_map>
@@ -1207,4 +1208,103 @@ extern "C" int itts_bench_trace(itts_gpt *g, itts_kv *kv, int32_t nb, int32_t kv
     *grid = kv->db.mk_grid;
     *events_per_cta = MK_TRACE_EVENTS;
     return rc;
+}
+
+
+// ------------------------------------------------------------------------------
+// Sampling without allocation.
+//
+// Some callers of the sampler cannot allocate device memory: a process whose GPU memory
+// belongs to another runtime (a serving framework's caching allocator, or a fixed memory
+// budget that must never grow), and a real-time audio thread, where cudaMalloc and
+// cudaFree synchronize the whole device and would stall playback.  Such a caller cannot
+// create an itts_gpt either, since loading allocates.  itts_sample_next_token_static runs
+// the same on-device sampler as itts_sample_next_token, with the device-side working set
+// of that kernel (its state block, the batch index, the token word and the logits it
+// penalizes in place) in the file-scope array below instead of buffers of a handle.
+// Every GPU that loads this library holds the array (67,072 bytes) until the process
+// exits.
+// ------------------------------------------------------------------------------
+namespace {
+constexpr size_t kStaticIdxOff = (sizeof(SlotState) + 255) / 256 * 256;  // state block at 0
+constexpr size_t kStaticLogitsOff = kStaticIdxOff + 256;
+constexpr size_t kStaticBytes = kStaticLogitsOff + sizeof(float) * ITTS_STATIC_SAMPLE_MAX_LOGITS;
+constexpr int kStaticMaxDevices = 64;
+std::mutex g_static_mu;
+unsigned char *g_static_base[kStaticMaxDevices];  // device address of the array, per device
+}  // namespace
+
+// Host code never uses this name as an address: in host code it only stands for the
+// symbol, whose device address per device comes from cudaGetSymbolAddress below.
+static __device__ __align__(256) unsigned char g_static_sample_scratch[kStaticBytes];
+
+// Set-up, once per device, with that device current: the array's device address and the
+// sampler kernel's shared-memory attribute.
+static int static_sample_setup(int dev, unsigned char **base) {
+    if (dev < 0 || dev >= kStaticMaxDevices) return validation("device", "ordinal out of range");
+    std::lock_guard<std::mutex> lock(g_static_mu);
+    if (!g_static_base[dev]) {
+        unsigned char *ptr = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress((void **)&ptr, g_static_sample_scratch);
+        if (e != cudaSuccess)
+            return set_err(ITTS_E_CUDA, std::string("device error: cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+        kernels_init_sample();
+        CUDA_TRY(cudaGetLastError());
+        g_static_base[dev] = ptr;
+    }
+    *base = g_static_base[dev];
+    return ITTS_OK;
+}
+
+extern "C" int itts_sample_next_token_static(float *logits, int32_t n, const uint64_t *seen,
+                                             const itts_sampling_params *params,
+                                             uint64_t *rng_state, int32_t *token_out,
+                                             void *stream) {
+    if (!logits || !seen || !rng_state || !token_out) return validation("logits", "null pointer");
+    if (n <= 0) return validation("logits", "logits slice must not be empty");
+    if (n > ITTS_STATIC_SAMPLE_MAX_LOGITS)
+        return validation("logits", "at most " + std::to_string(ITTS_STATIC_SAMPLE_MAX_LOGITS) +
+                                        " logits fit the static scratch of itts_sample_next_token_static (got " +
+                                        std::to_string(n) + ")");
+    TRY(itts_sampling_params_validate(params));
+    int dev = 0;
+    CUDA_TRY(cudaGetDevice(&dev));
+    unsigned char *base = nullptr;
+    TRY(static_sample_setup(dev, &base));
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    // Every field the kernel reads is rewritten here, so nothing of an earlier call is
+    // read: the whole state block, batch column 0 -> state 0, and the token word cleared.
+    SlotState s = blank_slot(0x7FFFFFFF);
+    fill_params(s, params);
+    s.active = 1;
+    s.max_steps = 0x7FFFFFFF;
+    s.rng = *rng_state;
+    std::memcpy(s.seen, seen, sizeof(s.seen));
+    int32_t idx[2] = {0, -1};
+    SlotState *d_state = reinterpret_cast<SlotState *>(base);
+    int32_t *d_idx = reinterpret_cast<int32_t *>(base + kStaticIdxOff);
+    float *d_logits = reinterpret_cast<float *>(base + kStaticLogitsOff);
+    CUDA_TRY(cudaMemcpyAsync(d_state, &s, sizeof(SlotState), cudaMemcpyHostToDevice, st));
+    CUDA_TRY(cudaMemcpyAsync(d_idx, idx, sizeof(idx), cudaMemcpyHostToDevice, st));
+    CUDA_TRY(cudaMemcpyAsync(d_logits, logits, sizeof(float) * n, cudaMemcpyHostToDevice, st));
+    SampleArgs a{};
+    a.slots = d_state;
+    a.batch_slot = d_idx;
+    a.nb = 1;
+    a.logits = d_logits;
+    a.ld_logits = n;
+    a.n_logits = n;
+    a.after_forward = 0;
+    a.write_back = 1;
+    a.codes = nullptr;
+    a.token_out = d_idx + 1;
+    launch_sample(a, st);
+    CUDA_TRY(cudaGetLastError());
+    CUDA_TRY(cudaMemcpyAsync(logits, d_logits, sizeof(float) * n, cudaMemcpyDeviceToHost, st));
+    CUDA_TRY(cudaMemcpyAsync(&s, d_state, sizeof(SlotState), cudaMemcpyDeviceToHost, st));
+    CUDA_TRY(cudaMemcpyAsync(idx + 1, d_idx + 1, sizeof(int32_t), cudaMemcpyDeviceToHost, st));
+    CUDA_TRY(cudaStreamSynchronize(st));
+    *rng_state = s.rng;
+    *token_out = idx[1];
+    return ITTS_OK;
 }

@@ -66,6 +66,8 @@ SIGNATURES = [
     ("itts_gpt_step", C.c_int, [_P, _P, _I32, _P, _P, _P, _P]),
     ("itts_sample_next_token", C.c_int,
      [_P, _P, _I32, _P, C.POINTER(SamplingParamsC), C.POINTER(C.c_uint64), C.POINTER(_I32)]),
+    ("itts_sample_next_token_static", C.c_int,
+     [_P, _I32, _P, C.POINTER(SamplingParamsC), C.POINTER(C.c_uint64), C.POINTER(_I32), _P]),
     ("itts_generate_codes_after", C.c_int,
      [_P, _P, _I32, C.POINTER(CodePromptC), C.POINTER(SamplingParamsC), C.POINTER(C.c_uint64),
       _P, _I32, C.POINTER(_I32)]),
