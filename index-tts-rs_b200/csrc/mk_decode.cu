@@ -202,6 +202,18 @@ struct StepShape {
 };
 
 __device__ __forceinline__ int lin_units(const MkLin &L) { return L.n_rb * L.n_kc; }
+// Attention unit u (0 <= u < attn_units) of the step -> column n, head h, unit a of the
+// head.  Units are numbered column-major over the active columns, then head, then unit.
+__device__ __forceinline__ void attn_unit_of(const StepShape *S, int H, int u, int &n, int &h, int &a) {
+    n = 0;
+    for (int c = 0; c < MK_MAX_NB; ++c) {
+        const int cnt = S->active[c] ? H * S->units[c] : 0;
+        if (u < cnt) { n = c; break; }
+        u -= cnt;
+    }
+    h = u / S->units[n];
+    a = u - h * S->units[n];
+}
 __device__ __forceinline__ int first_owned(uint32_t ubase, int cta, int G) {
     return (int)((cta - (int)(ubase % (uint32_t)G) + G) % G);
 }
@@ -247,22 +259,19 @@ struct MkProducer {
     }
     __device__ __forceinline__ void stream_attn(int l) {
         const MkParams &p = *pp;
-        int u = 0;
-        for (int n = 0; n < MK_MAX_NB; ++n) {
-            if (n >= p.nb || !S->active[n]) continue;
-            const int units = S->units[n], upt = S->upt, kvt = S->kv_tiles[n], lold = S->lold[n];
-            for (int h = 0; h < p.H; ++h)
-                for (int a = 0; a < units; ++a, ++u) {
-                    if ((int)((ubase + u) % (uint32_t)G) != cta) continue;
-                    const int t1 = min(kvt, (a + 1) * upt);
-                    for (int t = a * upt; t < t1; ++t) {
-                        const int p0 = t * MK_KVPOS, np = min(MK_KVPOS, lold - p0);
-                        const size_t off = kv_index(l, S->slot[n], h, p0, p.n_slots, p.H, p.max_seq);
-                        issue(p.kc + off, (uint32_t)np * 128u, p.vc + off, (uint32_t)np * 128u);
-                    }
-                }
+        const int total = S->attn_units, upt = S->upt;
+        for (int u = first_owned(ubase, cta, G); u < total; u += G) {
+            int n, h, a;
+            attn_unit_of(S, p.H, u, n, h, a);
+            const int kvt = S->kv_tiles[n], lold = S->lold[n];
+            const int t1 = min(kvt, (a + 1) * upt);
+            for (int t = a * upt; t < t1; ++t) {
+                const int p0 = t * MK_KVPOS, np = min(MK_KVPOS, lold - p0);
+                const size_t off = kv_index(l, S->slot[n], h, p0, p.n_slots, p.H, p.max_seq);
+                issue(p.kc + off, (uint32_t)np * 128u, p.vc + off, (uint32_t)np * 128u);
+            }
         }
-        ubase += S->attn_units;
+        ubase += total;
     }
     __device__ __forceinline__ void run() {
         const MkParams &p = *pp;
@@ -893,20 +902,16 @@ struct MkConsumer {
     // ---- stage B: attention units of this CTA ----
     __device__ __forceinline__ void stage_b(int l) {
         const MkParams &p = *pp;
-        int u = 0;
         const uint32_t t0 = tag(l, 0), t1 = tag(l, 1);
-        for (int n = 0; n < MK_MAX_NB; ++n) {
-            if (n >= nb || !S->active[n]) continue;
-            const int units = S->units[n];
-            for (int h = 0; h < p.H; ++h)
-                for (int a = 0; a < units; ++a, ++u)
-                    if ((int)((ubase + u) % (uint32_t)G) == cta) {
-                        int okf = ok ? 1 : 0;
-                        seq = mk_attn_unit(pp, S, ring, full, empty, ared, cmb, nslot, seq, &okf, l, n, h, a, t0, t1);
-                        ok = okf != 0;
-                    }
+        const int total = S->attn_units;
+        for (int u = first_owned(ubase, cta, G); u < total; u += G) {
+            int n, h, a;
+            attn_unit_of(S, p.H, u, n, h, a);
+            int okf = ok ? 1 : 0;
+            seq = mk_attn_unit(pp, S, ring, full, empty, ared, cmb, nslot, seq, &okf, l, n, h, a, t0, t1);
+            ok = okf != 0;
         }
-        ubase += S->attn_units;
+        ubase += total;
         trace();
     }
     // ---- stage C: attention output -> c_proj + residual -> h ----
