@@ -30,7 +30,7 @@ namespace itts {
 
 constexpr int MK_CWARPS = 8;
 constexpr int MK_NTHR = MK_CWARPS * 32;
-constexpr int MK_THREADS = MK_NTHR;  // no separate producer warp: 255 registers per thread
+constexpr int MK_THREADS = MK_NTHR + 32;
 constexpr int MK_KVPOS = 96;  // positions per KV tile: 96 * 128 B * 2 = 24 KB
 constexpr uint32_t MK_SPIN_LIMIT = 1u << 22;
 constexpr int MK_STAGES = 5;  // per layer: qkv, attention, h, u, x
@@ -72,6 +72,24 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *b, uint32_t par, const int *
 // Bulk copy global -> shared completing on `bar`, marked evict-first in L2 so that the
 // streamed weights and K/V rows do not push the small hot data (activations, LayerNorm
 // parameters) out of L2.
+// The producer's wait for a free slot: not latency critical, so it sleeps between polls
+// instead of taking issue slots from the consumer warps.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t *b, uint32_t par, const int *err) {
+    const uint32_t a = smem_u32(b);
+    for (uint32_t it = 0; it < MK_SPIN_LIMIT; ++it) {
+        uint32_t done;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+            " selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done)
+            : "r"(a), "r"(par)
+            : "memory");
+        if (done) return true;
+        if ((it & 1023u) == 1023u && *(volatile const int *)err) return false;
+        __nanosleep(64);
+    }
+    return false;
+}
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar,
                                          uint64_t policy) {
     asm volatile(
@@ -154,7 +172,7 @@ __device__ __forceinline__ int frag_pos(int k) { return frag_pos_host(k); }
 
 // Shared-memory carve-up (byte offsets), identical on host and device.
 struct MkSmem {
-    size_t xs, sx, rs, red, ared, cmb, lay, tbias, ctl, rcnt, cur, bar, total;
+    size_t xs, sx, rs, red, ared, cmb, lay, tbias, ctl, bar, total;
 };
 __host__ __device__ inline MkSmem mk_smem_layout(int nslot, int nb, int xsk, int d, int n_layers) {
     MkSmem L;
@@ -168,9 +186,7 @@ __host__ __device__ inline MkSmem mk_smem_layout(int nslot, int nb, int xsk, int
     L.lay = o; o = (o + (size_t)n_layers * sizeof(MkLayer) + 15) & ~(size_t)15;
     L.tbias = o; o = (o + 16 * 4 + 15) & ~(size_t)15;
     L.ctl = o; o = (o + 64 + 15) & ~(size_t)15;
-    L.rcnt = o; o = (o + 16 * 4 + 15) & ~(size_t)15;
-    L.cur = o; o = (o + 32 + 15) & ~(size_t)15;
-    L.bar = o; o = (o + (size_t)nslot * 8 + 16 + 15) & ~(size_t)15;
+    L.bar = o; o = (o + (size_t)2 * nslot * 8 + 16 + 15) & ~(size_t)15;
     L.total = o;
     return L;
 }
@@ -203,118 +219,76 @@ __device__ __forceinline__ int first_owned(uint32_t ubase, int cta, int G) {
 }
 
 // ------------------------------------------------------------------------------
-// copy stream: every ring item of the step (the CTA's weight tiles and the old K/V rows of
-// its attention units) in consumption order.  The consumers refill the ring themselves:
-// the last warp to finish with a slot issues the item nslot ahead into it, so the copies
-// run up to nslot items ahead of the math, across stage and layer boundaries.
+// producer: streams the CTA's tiles (weights, then old K/V rows) in consumption order
 // ------------------------------------------------------------------------------
-struct MkCursor {
-    int layer, phase, u, sub;
-    uint32_t ubase, issued;
-};
-enum : int { MK_PH_QKV = 0, MK_PH_ATTN, MK_PH_PROJ, MK_PH_FC, MK_PH_MLP, MK_PH_HEAD, MK_PH_DONE };
+struct MkProducer {
+    const MkParams *pp;
+    const StepShape *S;
+    uint8_t *ring;
+    uint64_t *full, *empty;
+    const MkLayer *layers;  // shared-memory copy
+    int nslot, cta, G;
+    uint32_t seq, ubase;
+    bool ok;
+    uint64_t policy;
+    uint32_t armed[16];  // seq + 1 of the last copy into each slot not known to have landed
 
-// The next item of the stream (two copies at most), or false at its end.  Units are dealt
-// exactly as the consumer stages deal them (first_owned + k * grid, unit bases cumulative).
-__device__ __forceinline__ bool mk_next_item(MkCursor &c, const MkParams &p, const StepShape *S,
-                                             const MkLayer *lay, const void *&src0, uint32_t &b0,
-                                             const void *&src1, uint32_t &b1) {
-    const int cta = blockIdx.x, G = gridDim.x;
-    for (;;) {
-        if (c.phase == MK_PH_DONE) return false;
-        const MkLin *L = nullptr;
-        int units;
-        if (c.phase == MK_PH_ATTN) {
-            units = S->attn_units;
-        } else {
-            L = c.phase == MK_PH_QKV    ? &lay[c.layer].qkv
-                : c.phase == MK_PH_PROJ ? &lay[c.layer].proj
-                : c.phase == MK_PH_FC   ? &lay[c.layer].fc
-                : c.phase == MK_PH_MLP  ? &lay[c.layer].mlp
-                                        : &p.head;
-            units = c.phase == MK_PH_MLP ? L->n_rb : L->n_rb * L->n_kc;
-        }
-        if (c.u < 0) {
-            c.u = first_owned(c.ubase, cta, G);
-            c.sub = 0;
-        }
-        if (c.u >= units) {
-            c.ubase += c.phase == MK_PH_ATTN ? (uint32_t)units : (uint32_t)(L->n_rb * L->n_kc);
-            if (c.phase == MK_PH_MLP) {
-                ++c.layer;
-                c.phase = c.layer < p.n_layers ? MK_PH_QKV : MK_PH_HEAD;
-            } else {
-                c.phase = c.phase == MK_PH_HEAD ? MK_PH_DONE : c.phase + 1;
-            }
-            c.u = -1;
-            continue;
-        }
-        if (c.phase == MK_PH_ATTN) {
+    __device__ __forceinline__ void issue(const void *src0, uint32_t b0, const void *src1, uint32_t b1) {
+        const uint32_t slot = seq % nslot, ph = (seq / nslot) & 1u;
+        if (seq >= (uint32_t)nslot && ok) ok = mbar_wait_sleep(&empty[slot], ph ^ 1u, pp->err);
+        if (!ok) { ++seq; return; }
+        armed[slot] = seq + 1;  // the previous copy into this slot was consumed
+        mbar_expect_tx(&full[slot], b0 + b1);
+        uint8_t *dst = ring + (size_t)slot * MK_SLOT_BYTES;
+        bulk_g2s(dst, src0, b0, &full[slot], policy);
+        if (b1) bulk_g2s(dst + MK_SLOT_BYTES / 2, src1, b1, &full[slot], policy);
+        ++seq;
+    }
+    __device__ __forceinline__ void stream_lin(const MkLin &L) {
+        const int n = lin_units(L);
+        for (int t = first_owned(ubase, cta, G); t < n; t += G)
+            issue(L.tiles + (size_t)t * L.tile_bytes, (uint32_t)L.tile_bytes, nullptr, 0);
+        ubase += n;
+    }
+    // dealt by row block: all K chunks of a block to one CTA
+    __device__ __forceinline__ void stream_lin_rb(const MkLin &L) {
+        for (int rb = first_owned(ubase, cta, G); rb < L.n_rb; rb += G)
+            for (int kci = 0; kci < L.n_kc; ++kci)
+                issue(L.tiles + ((size_t)rb * L.n_kc + kci) * L.tile_bytes, (uint32_t)L.tile_bytes, nullptr, 0);
+        ubase += lin_units(L);
+    }
+    __device__ __forceinline__ void stream_attn(int l) {
+        const MkParams &p = *pp;
+        const int total = S->attn_units, upt = S->upt;
+        for (int u = first_owned(ubase, cta, G); u < total; u += G) {
             int n, h, a;
-            attn_unit_of(S, p.H, c.u, n, h, a);
-            const int t = a * S->upt + c.sub, t1 = min(S->kv_tiles[n], (a + 1) * S->upt);
-            if (t >= t1) {
-                c.u += G;
-                c.sub = 0;
-                continue;
+            attn_unit_of(S, p.H, u, n, h, a);
+            const int kvt = S->kv_tiles[n], lold = S->lold[n];
+            const int t1 = min(kvt, (a + 1) * upt);
+            for (int t = a * upt; t < t1; ++t) {
+                const int p0 = t * MK_KVPOS, np = min(MK_KVPOS, lold - p0);
+                const size_t off = kv_index(l, S->slot[n], h, p0, p.n_slots, p.H, p.max_seq);
+                issue(p.kc + off, (uint32_t)np * 128u, p.vc + off, (uint32_t)np * 128u);
             }
-            const int p0 = t * MK_KVPOS, np = min(MK_KVPOS, S->lold[n] - p0);
-            const size_t off = kv_index(c.layer, S->slot[n], h, p0, p.n_slots, p.H, p.max_seq);
-            src0 = p.kc + off;
-            src1 = p.vc + off;
-            b0 = b1 = (uint32_t)np * 128u;
-        } else {
-            const int per_unit = c.phase == MK_PH_MLP ? L->n_kc : 1;
-            if (c.sub >= per_unit) {
-                c.u += G;
-                c.sub = 0;
-                continue;
-            }
-            const int tile = c.phase == MK_PH_MLP ? c.u * L->n_kc + c.sub : c.u;
-            src0 = L->tiles + (size_t)tile * L->tile_bytes;
-            b0 = (uint32_t)L->tile_bytes;
-            src1 = nullptr;
-            b1 = 0;
         }
-        ++c.sub;
-        return true;
+        ubase += total;
     }
-}
-
-// Issues the next stream item (sequence number c.issued) into its ring slot.
-__device__ __forceinline__ void mk_issue_next(MkCursor &c, const MkParams &p, const StepShape *S,
-                                              const MkLayer *lay, uint8_t *ring, uint64_t *full) {
-    const void *s0, *s1;
-    uint32_t b0, b1;
-    if (!mk_next_item(c, p, S, lay, s0, b0, s1, b1)) return;
-    const uint32_t slot = c.issued % (uint32_t)p.nslot;
-    const uint64_t policy = evict_first_policy();
-    mbar_expect_tx(&full[slot], b0 + b1);
-    uint8_t *dst = ring + (size_t)slot * MK_SLOT_BYTES;
-    bulk_g2s(dst, s0, b0, &full[slot], policy);
-    if (b1) bulk_g2s(dst + MK_SLOT_BYTES / 2, s1, b1, &full[slot], policy);
-    ++c.issued;
-}
-
-// Called by lane 0 of every consumer warp once the warp is done with ring slot `slot`:
-// the last of the 8 warps resets the slot's count and refills the slot with the item
-// nslot ahead (the cursor is only ever touched by one thread at a time: the last warp of
-// item k has finished its refill for item k - 1 before it can arrive for item k).
-__device__ __forceinline__ void mk_release(uint32_t slot, int *rcnt, MkCursor *cur, const MkParams &p,
-                                           const StepShape *S, const MkLayer *lay, uint8_t *ring,
-                                           uint64_t *full) {
-    __threadfence_block();
-    if (atomicAdd(&rcnt[slot], 1) == MK_CWARPS - 1) {
-        rcnt[slot] = 0;
-        __threadfence_block();
-        // the warps' reads of the slot (generic proxy) precede the bulk copy into it
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        MkCursor c = *cur;
-        mk_issue_next(c, p, S, lay, ring, full);
-        *cur = c;
-        __threadfence_block();
+    __device__ __forceinline__ void run() {
+        const MkParams &p = *pp;
+        for (int l = 0; l < p.n_layers && ok; ++l) {
+            const MkLayer *Ly = layers + l;
+            stream_lin(Ly->qkv);
+            stream_attn(l);
+            stream_lin(Ly->proj);
+            stream_lin(Ly->fc);
+            stream_lin_rb(Ly->mlp);
+        }
+        if (ok) stream_lin(p.head);
+        // every copy issued must land before the CTA may exit
+        for (int s = 0; s < nslot; ++s)
+            if (armed[s]) mbar_wait(&full[s], ((armed[s] - 1) / nslot) & 1u, p.err);
     }
-}
+};
 
 // ------------------------------------------------------------------------------
 // One attention unit (column n, head h, unit a) on the 8 consumer warps: old positions
@@ -324,8 +298,7 @@ __device__ __forceinline__ void mk_release(uint32_t slot, int *rcnt, MkCursor *c
 // after the unit's tiles; *ok is cleared on a wait timeout.
 // ------------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t mk_attn_unit(const MkParams *pp, const StepShape *S, uint8_t *ring,
-                                              uint64_t *full, int *rcnt, MkCursor *cur, const MkLayer *lay,
-                                              float *ared, float *cmb,
+                                              uint64_t *full, uint64_t *empty, float *ared, float *cmb,
                                               int nslot, uint32_t seq, int *ok_io, int l, int n, int h,
                                               int a, uint32_t tag0, uint32_t tag1) {
     const MkParams &p = *pp;
@@ -393,7 +366,7 @@ __device__ __forceinline__ uint32_t mk_attn_unit(const MkParams *pp, const StepS
             }
         }
         __syncwarp();
-        if (lane == 0) mk_release(slot, rcnt, cur, p, S, lay, ring, full);
+        if (lane == 0) mbar_arrive(&empty[slot]);
         ++seq;
     }
     if (w0) {  // the new position (fp32, from stage A)
@@ -507,9 +480,7 @@ struct MkConsumer {
     float *cmb;    // [MK_MAX_UNITS][68]
     float *tbias;  // [16] bias of the rows of the tile being finished
     const MkLayer *layers;  // shared-memory copy
-    uint64_t *full;
-    int *rcnt;
-    MkCursor *cur;
+    uint64_t *full, *empty;
     int nslot, cta, G, tid, warp, lane, g, c, nb, d, xsk;
     uint32_t seq, ubase, tbase;
     bool ok;
@@ -786,7 +757,7 @@ struct MkConsumer {
                 tbias[lane] = *reinterpret_cast<const float *>(tq + mk_tile_bias_offset(KC, pp->sbb) + lane * 4);
         }
         __syncwarp();
-        if (lane == 0) mk_release(slot, rcnt, cur, *pp, S, layers, ring, full);
+        if (lane == 0) mbar_arrive(&empty[slot]);
         ++seq;
     }
     // Sums the 8 warp partials and runs epi(m, n, v) for rows m < 16, columns n < NB:
@@ -864,8 +835,7 @@ struct MkConsumer {
         tbias = reinterpret_cast<float *>(smem + SL.tbias);
         layers = reinterpret_cast<const MkLayer *>(smem + SL.lay);
         full = reinterpret_cast<uint64_t *>(smem + SL.bar);
-        rcnt = reinterpret_cast<int *>(smem + SL.rcnt);
-        cur = reinterpret_cast<MkCursor *>(smem + SL.cur);
+        empty = full + nslot;
         cta = blockIdx.x;
         G = gridDim.x;
         tid = threadIdx.x;
@@ -938,7 +908,7 @@ struct MkConsumer {
             int n, h, a;
             attn_unit_of(S, p.H, u, n, h, a);
             int okf = ok ? 1 : 0;
-            seq = mk_attn_unit(pp, S, ring, full, rcnt, cur, layers, ared, cmb, nslot, seq, &okf, l, n, h, a, t0, t1);
+            seq = mk_attn_unit(pp, S, ring, full, empty, ared, cmb, nslot, seq, &okf, l, n, h, a, t0, t1);
             ok = okf != 0;
         }
         ubase += total;
@@ -1031,13 +1001,12 @@ template <int NB>
 __global__ void __launch_bounds__(MK_THREADS, 1) mk_decode_kernel(const __grid_constant__ MkParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     __shared__ StepShape S;
-    const int tid = threadIdx.x;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int G = gridDim.x, cta = blockIdx.x;
     const int nslot = p.nslot;
     const MkSmem SL = mk_smem_layout(nslot, NB, p.xsk, p.d, p.n_layers);
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + SL.bar);
-    int *rcnt = reinterpret_cast<int *>(smem + SL.rcnt);
-    MkCursor *cur = reinterpret_cast<MkCursor *>(smem + SL.cur);
+    uint64_t *empty = full + nslot;
     const uint32_t epoch = p.epoch[cta];
 
     MkLayer *lay = reinterpret_cast<MkLayer *>(smem + SL.lay);
@@ -1071,20 +1040,24 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mk_decode_kernel(const __grid_c
             }
         for (int s = 0; s < nslot; ++s) {
             mbar_init(&full[s], 1);
-            rcnt[s] = 0;
+            mbar_init(&empty[s], MK_CWARPS);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         if (p.trace) p.trace[(size_t)cta * MK_TRACE_EVENTS] = globaltimer();
     }
     __syncthreads();
-    if (tid == 0) {
-        // prologue of the copy stream: fill the ring
-        MkCursor c;
-        c.layer = 0; c.phase = MK_PH_QKV; c.u = -1; c.sub = 0; c.ubase = 0; c.issued = 0;
-        for (int s = 0; s < nslot; ++s) mk_issue_next(c, p, &S, lay, smem, full);
-        *cur = c;
-    }
 
+    if (warp == MK_CWARPS) {
+        if (lane != 0) return;
+        MkProducer P;
+        P.pp = &p; P.S = &S; P.ring = smem; P.full = full; P.empty = empty; P.layers = lay;
+        P.policy = evict_first_policy();
+        P.nslot = nslot; P.cta = cta; P.G = G; P.seq = 0; P.ubase = 0; P.ok = true;
+#pragma unroll
+        for (int s = 0; s < 16; ++s) P.armed[s] = 0;
+        P.run();
+        return;
+    }
     {
         using Ctl = typename MkConsumer<NB>::Ctl;
         Ctl *ctl = reinterpret_cast<Ctl *>(smem + SL.ctl);
@@ -1106,14 +1079,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mk_decode_kernel(const __grid_c
     }
     mk_stage<NB, 5>(&p, &S, smem, 0);
     named_sync();
-    if (tid == 0) {
-        // after an error some issued copies may not have been consumed: let them land
-        using Ctl = typename MkConsumer<NB>::Ctl;
-        const Ctl *ctl = reinterpret_cast<const Ctl *>(smem + SL.ctl);
-        for (uint32_t k = ctl->seq; k < cur->issued; ++k)
-            mbar_wait(&full[k % (uint32_t)nslot], (k / (uint32_t)nslot) & 1u, p.err);
-        p.epoch[cta] = epoch + 1;
-    }
+    if (tid == 0) p.epoch[cta] = epoch + 1;
 }
 
 // ------------------------------------------------------------------------------
