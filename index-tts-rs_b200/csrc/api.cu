@@ -28,6 +28,7 @@
 
 namespace itts {
 void kernels_init_sample();
+void kernels_init_gemm_tc();
 }  // namespace itts
 
 using namespace itts;
@@ -369,6 +370,7 @@ extern "C" int itts_gpt_from_tensors(const itts_tensor *tensors, int32_t n_tenso
     static bool inited[64] = {false};
     if (device >= 0 && device < 64 && !inited[device]) {
         kernels_init_sample();
+        kernels_init_gemm_tc();
         inited[device] = true;
     }
     size_t total = 0;

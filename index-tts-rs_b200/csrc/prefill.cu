@@ -5,7 +5,7 @@
 // Reference semantics: Gpt::prefix_embedding / sequence_embedding
 // (crates/core/src/models/gpt.rs:535-627), Gpt::prefill_after (gpt.rs:655-696),
 // Gpt2Block::forward with the causal mask (gpt.rs:325-384).
-#include "kernels.h"
+#include "gemm.cuh"
 
 namespace itts {
 
@@ -92,18 +92,6 @@ void launch_layernorm_rows(const float *x, const float *w, const float *b, int r
 // the weight tile is dequantized once into shared memory (fp32) and reused by
 // all 64 positions.  Thread tile 4 x 4.
 // ---------------------------------------------------------------------------
-struct GemmParams {
-    MkLin W;
-    const float *x;  // [T, K]
-    float *y;        // [T, OUT]
-    int T;
-    // EPI_QKV: prefill writes row t's K/V at position t of kv_slot; decode (slots != null)
-    // writes them at the valid_len of slot batch_slot[t]
-    __half *k_cache, *v_cache;
-    const SlotState *slots;
-    const int *batch_slot;
-    int kv_slot, n_slots, n_heads, max_seq, layer, d;
-};
 
 template <int EPI>
 __global__ void __launch_bounds__(256) gemm_q8_kernel(GemmParams p) {
@@ -173,32 +161,14 @@ __global__ void __launch_bounds__(256) gemm_q8_kernel(GemmParams p) {
         for (int j = 0; j < 4; ++j) {
             const int o = o0 + tx * 4 + j;
             if (o >= OUT) continue;
-            const float v = acc[i][j] + p.W.bias[o];
-            float *yp = p.y + (size_t)t * OUT + o;
-            if (EPI == EPI_PLAIN) *yp = v;
-            else if (EPI == EPI_GELU) *yp = gelu_tanh(v);
-            else if (EPI == EPI_RESID) *yp += v;
-            else {
-                *yp = v;
-                if (o >= p.d) {
-                    const int rr = o - p.d, which = rr / p.d, oo = rr - which * p.d;
-                    __half *cache = which == 0 ? p.k_cache : p.v_cache;
-                    int slot = p.kv_slot, pos = t;
-                    bool write = t < p.max_seq;
-                    if (p.slots) {
-                        slot = p.batch_slot[t];
-                        const SlotState &st = p.slots[slot];
-                        pos = st.valid_len;
-                        write = st.active && pos < p.max_seq;
-                    }
-                    if (write)
-                        cache[kv_index(p.layer, slot, oo >> 6, pos, p.n_slots, p.n_heads, p.max_seq) +
-                              (oo & 63)] = __float2half_rn(v);
-                }
-            }
+            gemm_store<EPI>(p, t, o, acc[i][j] + p.W.bias[o]);
         }
     }
 }
+
+// Row counts from which the tensor-core GEMM is used (below it the CUDA-core tile wastes
+// less of a 128-row MMA tile).
+constexpr int kGemmTcMinRows = 16;
 
 void launch_gemm(int epi, const MkLin &W, const float *x, float *y, int T, const DecodeView *dv,
                  __half *k_cache, __half *v_cache, int kv_slot, int n_slots, int n_heads,
@@ -219,6 +189,10 @@ void launch_gemm(int epi, const MkLin &W, const float *x, float *y, int T, const
     if (dv) {
         p.slots = dv->slots;
         p.batch_slot = dv->batch_slot;
+    }
+    if (T >= kGemmTcMinRows) {
+        launch_gemm_tc(epi, p, st);
+        return;
     }
     dim3 grid((W.out + 63) / 64, (T + 63) / 64);
     switch (epi) {
