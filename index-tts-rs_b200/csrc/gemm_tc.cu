@@ -93,7 +93,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_q8_tc_kernel(GemmParams p)
         const bool okw = kb < 2 || tc_wait(&bar[s], (uint32_t)((kb - 2) >> 1) & 1u);
         if (okw) {
             // activations: 128 positions x 64 inputs, 8 per 16-byte chunk
-    #pragma unroll
+#pragma unroll
             for (int i = 0; i < 4; ++i) {
                 const int c = tid + i * TC_THREADS, r = c >> 3, ch = c & 7, t = m0 + r;
                 uint4 h = make_uint4(0u, 0u, 0u, 0u);
@@ -107,7 +107,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_q8_tc_kernel(GemmParams p)
             }
             // weights: 128 rows x 64 inputs; a row's group is 4 chunks of 16 bytes in fragment
             // order (chunk c holds inputs 16b + 8hi + 2c + lo), dequantized as s * q + b
-    #pragma unroll
+#pragma unroll
             for (int i = 0; i < 2; ++i) {
                 const int c = tid + i * TC_THREADS, r = c >> 2, fc = c & 3, o = o0 + r;
                 uint32_t hv[8];
@@ -123,17 +123,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_q8_tc_kernel(GemmParams p)
                         sc = f.x; zo = f.y;
                     }
                     const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-    #pragma unroll
+#pragma unroll
                     for (int b = 0; b < 4; ++b) {
                         hv[2 * b] = pack_half2(fmaf(sc, byte_to_float(ww[b], 0), zo), fmaf(sc, byte_to_float(ww[b], 1), zo));
                         hv[2 * b + 1] =
                             pack_half2(fmaf(sc, byte_to_float(ww[b], 2), zo), fmaf(sc, byte_to_float(ww[b], 3), zo));
                     }
                 } else {
-    #pragma unroll
+#pragma unroll
                     for (int e = 0; e < 8; ++e) hv[e] = 0u;
                 }
-    #pragma unroll
+#pragma unroll
                 for (int b = 0; b < 4; ++b) {
                     const int k0 = b * 16 + 2 * fc;  // bytes 0, 1 of word b
                     *reinterpret_cast<uint32_t *>(sb + tc_swz(r, k0)) = hv[2 * b];
