@@ -154,6 +154,25 @@ int itts_gpt_prefill(itts_gpt *gpt, itts_kv *kv, int32_t slot, const int32_t *te
 int itts_gpt_step(itts_gpt *gpt, itts_kv *kv, int32_t n, const int32_t *slots,
                   const int32_t *toks, const int32_t *pos, float *logits_out);
 
+/* Gpt::teacher_forced / Gpt::code_log_probs (gpt.rs:766-797, replay :800-861): replays
+ * `codes` with teacher forcing after the prompt and writes log p(codes[i] | conds, text,
+ * codes[..i]) to log_probs_out[i] (may be NULL).  With attention_out != NULL also the text
+ * attention of heads (layer 4, head 10) and (5, 10) (align/mod.rs:37) averaged, row-major
+ * [n_codes, n_text + 2] (columns <BOS>, text..., <EOS>); the model needs 6 layers and 11
+ * heads for it.  `slot` of kv is scratch and is left reset. */
+int itts_gpt_teacher_forced(itts_gpt *gpt, itts_kv *kv, int32_t slot, const int32_t *text_tokens,
+                            int32_t n_text, const float *conds, int32_t n_conds, int32_t lang_id,
+                            const int32_t *codes, int32_t n_codes, float *log_probs_out,
+                            float *attention_out);
+
+/* Gpt::alignment_attention (gpt.rs:875-915): the same attention for `codes` generated after
+ * prior_codes, replaying only the first 6 layers (align/mod.rs:40); attention_out is
+ * [n_codes, n_text + 2].  `slot` of kv is scratch and is left reset. */
+int itts_gpt_alignment_attention(itts_gpt *gpt, itts_kv *kv, int32_t slot, const int32_t *text_tokens,
+                                 int32_t n_text, const float *conds, int32_t n_conds, int32_t lang_id,
+                                 const int32_t *prior_codes, int32_t n_prior, const int32_t *codes,
+                                 int32_t n_codes, float *attention_out);
+
 /* ---- sampling and the decode loop --------------------------------------------------- */
 
 /* sample_next_token (sampler.rs:191-284), run by the on-device sampler: applies the

@@ -796,7 +796,7 @@ static int validate_prompt(const ModelView &m, const int32_t *text, int n_text, 
 
 static int prefill_impl(itts_gpt *g, itts_kv *kv, int slot, const int32_t *text, int n_text,
                         const float *conds, int n_conds, int lang, const int32_t *prior,
-                        int n_prior, float *d_logits_row) {
+                        int n_prior, float *d_logits_row, const PrefillHooks *hooks = nullptr) {
     const ModelView &m = g->m;
     int T = 0;
     TRY(validate_prompt(m, text, n_text, conds, n_conds, lang, prior, n_prior, kv->max_seq, &T));
@@ -818,7 +818,7 @@ static int prefill_impl(itts_gpt *g, itts_kv *kv, int slot, const int32_t *text,
     launch_embed_prefix(m, kv->d_text, n_text + 2, kv->d_conds, n_conds, lang, kv->d_prior, n_prior,
                         kv->pb.x, st);
     DecodeView dv = decode_view(kv, 1);
-    prefill_forward(m, dv, slot, T, kv->pb, d_logits_row, st);
+    prefill_forward(m, dv, slot, T, kv->pb, d_logits_row, st, hooks);
     CUDA_TRY(cudaGetLastError());
     kv->h_state[slot].valid_len = T;
     return ITTS_OK;
@@ -839,6 +839,109 @@ extern "C" int itts_gpt_prefill(itts_gpt *g, itts_kv *kv, int32_t slot, const in
                                  sizeof(float) * g->m.mel_vocab, cudaMemcpyDeviceToHost, g->stream));
     CUDA_TRY(cudaStreamSynchronize(g->stream));
     return ITTS_OK;
+}
+
+// ------------------------------------------------------------------------------
+// teacher-forced replay (gpt.rs:756-915)
+// ------------------------------------------------------------------------------
+// (layer, head) pairs whose text attention is averaged, and the layers alignment replays
+// (crates/core/src/align/mod.rs:37-40).
+static const int kAlignHeads[2][2] = {{4, 10}, {5, 10}};
+static const int kAlignLayers = 6;
+
+// Gpt::replay (gpt.rs:800-861) when alignment_only is false, Gpt::alignment_attention
+// (gpt.rs:875-915) when it is true.  The codes fed after <START_MEL> are prior ++
+// codes[..n-1]; query rows start at the <START_MEL> row plus n_prior, and row i scores
+// codes[i].  `slot` of the cache is scratch and is left reset.
+static int replay_impl(itts_gpt *g, itts_kv *kv, int slot, const int32_t *text, int n_text,
+                       const float *conds, int n_conds, int lang, const int32_t *prior, int n_prior,
+                       const int32_t *codes, int n_codes, bool alignment_only, float *log_probs_out,
+                       float *attention_out) {
+    if (!g || !kv || kv->gpt != g) return validation("gpt", "null pointer or cache of another model");
+    if (slot < 0 || slot >= kv->max_batch) return validation("slot", "out of range");
+    if (!codes || n_codes <= 0) return validation("codes", "codes must not be empty");
+    if (n_prior < 0 || (n_prior > 0 && !prior)) return validation("prior_codes", "null pointer");
+    const ModelView &m = g->m;
+    for (int i = 0; i < n_codes; ++i)
+        if (codes[i] < 0 || codes[i] >= m.mel_vocab) return validation("codes", "token id out of range");
+    if (attention_out && (m.n_layers < kAlignLayers || m.n_heads <= kAlignHeads[0][1]))
+        return validation("attention", "the model has no alignment heads (needs 6 layers and 11 heads)");
+    std::vector<int32_t> fed(prior, prior + n_prior);
+    fed.insert(fed.end(), codes, codes + n_codes - 1);
+    CUDA_TRY(cudaSetDevice(g->device));
+    const int text_lo = n_conds, text_hi = n_conds + n_text + 2, q0 = text_hi + n_prior;
+    const int nk = n_text + 2;
+    int32_t *d_targets = nullptr;
+    float *d_lp = nullptr, *d_logits = nullptr, *d_maps = nullptr;
+    auto release = [&]() { cudaFree(d_targets); cudaFree(d_lp); cudaFree(d_logits); cudaFree(d_maps); };
+    cudaError_t e = cudaSuccess;
+    const bool want_lp = !alignment_only && log_probs_out;
+    if (want_lp) {
+        e = cudaMalloc(&d_targets, sizeof(int32_t) * n_codes);
+        if (e == cudaSuccess) e = cudaMalloc(&d_lp, sizeof(float) * n_codes);
+        if (e == cudaSuccess) e = cudaMalloc(&d_logits, sizeof(float) * (size_t)n_codes * m.mel_vocab);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(d_targets, codes, sizeof(int32_t) * n_codes, cudaMemcpyHostToDevice, g->stream);
+    }
+    if (e == cudaSuccess && attention_out) e = cudaMalloc(&d_maps, sizeof(float) * (size_t)n_codes * nk);
+    if (e != cudaSuccess) {
+        release();
+        return set_err(ITTS_E_CUDA, std::string("device error: replay buffers: ") + cudaGetErrorString(e));
+    }
+    PrefillHooks hk;
+    if (attention_out) {
+        hk.map_layers[0] = kAlignHeads[0][0];
+        hk.map_layers[1] = kAlignHeads[1][0];
+        hk.map_head = kAlignHeads[0][1];
+        hk.map_q0 = q0;
+        hk.map_k0 = text_lo;
+        hk.map_k1 = text_hi;
+        hk.maps = d_maps;
+    }
+    if (alignment_only) hk.stop_layer = kAlignLayers - 1;
+    if (want_lp) {
+        hk.lp_q0 = q0;
+        hk.lp_targets = d_targets;
+        hk.lp_logits = d_logits;
+        hk.lp_out = d_lp;
+    }
+    kv->h_state[slot].valid_len = 0;
+    const int rc = prefill_impl(g, kv, slot, text, n_text, conds, n_conds, lang, fed.data(), (int)fed.size(),
+                                kv->db.logits + (size_t)slot * m.mel_vocab, &hk);
+    kv->h_state[slot].valid_len = 0;  // cache.reset() (gpt.rs:839, 912)
+    if (rc != ITTS_OK) {
+        cudaStreamSynchronize(g->stream);
+        release();
+        return rc;
+    }
+    e = cudaSuccess;
+    if (want_lp) e = cudaMemcpyAsync(log_probs_out, d_lp, sizeof(float) * n_codes, cudaMemcpyDeviceToHost, g->stream);
+    if (e == cudaSuccess && attention_out)
+        e = cudaMemcpyAsync(attention_out, d_maps, sizeof(float) * (size_t)n_codes * nk, cudaMemcpyDeviceToHost,
+                            g->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(g->stream);
+    release();
+    if (e != cudaSuccess) return set_err(ITTS_E_CUDA, std::string("device error: replay: ") + cudaGetErrorString(e));
+    TRY(push_slots(kv, &slot, 1));
+    CUDA_TRY(cudaStreamSynchronize(g->stream));
+    return ITTS_OK;
+}
+
+extern "C" int itts_gpt_teacher_forced(itts_gpt *g, itts_kv *kv, int32_t slot, const int32_t *text,
+                                       int32_t n_text, const float *conds, int32_t n_conds, int32_t lang,
+                                       const int32_t *codes, int32_t n_codes, float *log_probs_out,
+                                       float *attention_out) {
+    return replay_impl(g, kv, slot, text, n_text, conds, n_conds, lang, nullptr, 0, codes, n_codes, false,
+                       log_probs_out, attention_out);
+}
+
+extern "C" int itts_gpt_alignment_attention(itts_gpt *g, itts_kv *kv, int32_t slot, const int32_t *text,
+                                            int32_t n_text, const float *conds, int32_t n_conds, int32_t lang,
+                                            const int32_t *prior, int32_t n_prior, const int32_t *codes,
+                                            int32_t n_codes, float *attention_out) {
+    if (!attention_out) return validation("attention", "null pointer");
+    return replay_impl(g, kv, slot, text, n_text, conds, n_conds, lang, prior, n_prior, codes, n_codes, true,
+                       nullptr, attention_out);
 }
 
 // The persistent decode-step kernel's error word is cleared before a run of steps; a

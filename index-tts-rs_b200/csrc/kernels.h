@@ -70,10 +70,23 @@ cudaError_t decode_forward(const ModelView &m, const DecodeView &dv, DecodeBufs 
 // Number of kernels decode_forward launches for nb columns.
 int decode_forward_launches(const ModelView &m, const DecodeBufs &b, int nb);
 
+// Optional extras of a prefill for the teacher-forced replay (gpt.rs:800-915).
+struct PrefillHooks {
+    int stop_layer = -1;      // >= 0: run layers below it, then only its LN1 + QKV
+    int map_layers[2] = {-1, -1}, map_head = 0;  // alignment heads (layer, head)
+    int map_q0 = 0, map_k0 = 0, map_k1 = 0;  // query rows map_q0.., key columns [k0, k1)
+    float *maps = nullptr;    // [T - map_q0][k1 - k0], the mean of the two heads' maps
+    int lp_q0 = -1;           // >= 0: log-probabilities of rows lp_q0.. instead of last logits
+    const int *lp_targets = nullptr;  // [T - lp_q0] target code of each row
+    float *lp_logits = nullptr;       // [T - lp_q0][mel_vocab] scratch
+    float *lp_out = nullptr;          // [T - lp_q0]
+};
+
 // Prefill of one request already embedded in pb.x[0..T): all layers; K/V of every
-// position written to `slot`; logits of position T-1 into logits_row.
+// position written to `slot`; logits of position T-1 into logits_row (unless hooks ask
+// for per-row log-probabilities instead).
 void prefill_forward(const ModelView &m, const DecodeView &dv, int slot, int T, PrefillBufs &pb,
-                     float *logits_row, cudaStream_t st);
+                     float *logits_row, cudaStream_t st, const PrefillHooks *hk = nullptr);
 
 void launch_embed_prefix(const ModelView &m, const int *full_text, int n_full, const float *conds,
                          int n_conds, int lang, const int *prior, int n_prior, float *x,

@@ -254,14 +254,91 @@ __global__ void __launch_bounds__(64) attn_prefill_kernel(const float *qkv, int 
     }
 }
 
+// Gpt2Block::head_attention (gpt.rs:391-427) on the prefill's QKV of one layer: for
+// query row t = q0 + blockIdx.x, softmax over keys 0..t of head `head` at scale 0.125
+// (the prefix and the Mel positions up to the query), keeping key columns [k0, k1).
+// accumulate: maps = (maps + p) / 2, the mean of two heads' maps.
+__global__ void __launch_bounds__(128) head_probs_kernel(const float *qkv, int T, int d, int head, int q0,
+                                                         int k0, int k1, float *maps, int accumulate) {
+    extern __shared__ float hp_sc[];  // [t + 1] scores, then [32] reduction scratch
+    __shared__ float q[64];
+    __shared__ float red[4];
+    const int t = q0 + blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid < 64) q[tid] = qkv[(size_t)t * 3 * d + head * 64 + tid];
+    __syncthreads();
+    float mx = -INFINITY;
+    for (int j = tid; j <= t; j += blockDim.x) {
+        const float *k = qkv + (size_t)j * 3 * d + d + head * 64;
+        float s = 0.f;
+        for (int e = 0; e < 64; ++e) s = fmaf(q[e], k[e], s);
+        s *= kAttnScale;
+        hp_sc[j] = s;
+        mx = fmaxf(mx, s);
+    }
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    __syncthreads();
+    float den = 0.f;
+    for (int j = tid; j <= t; j += blockDim.x) {
+        const float e = expf(hp_sc[j] - mx);
+        hp_sc[j] = e;
+        den += e;
+    }
+    den = warp_sum(den);
+    if (lane == 0) red[warp] = den;
+    __syncthreads();
+    den = (red[0] + red[1]) + (red[2] + red[3]);
+    const int nk = k1 - k0;
+    float *row = maps + (size_t)blockIdx.x * nk;
+    for (int j = k0 + tid; j < k1; j += blockDim.x) {
+        const float pj = j <= t ? hp_sc[j] / den : 0.f;
+        row[j - k0] = accumulate ? (row[j - k0] + pj) / 2.0f : pj;
+    }
+}
+
+// log_softmax of each logits row, taken at the row's target (gpt.rs:850-852).
+__global__ void __launch_bounds__(256) log_softmax_pick_kernel(const float *logits, int V, const int *targets,
+                                                               float *out) {
+    __shared__ float red[8];
+    const float *row = logits + (size_t)blockIdx.x * V;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    float mx = -INFINITY;
+    for (int v = tid; v < V; v += blockDim.x) mx = fmaxf(mx, row[v]);
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    mx = red[0];
+    for (int w = 1; w < 8; ++w) mx = fmaxf(mx, red[w]);
+    __syncthreads();
+    float s = 0.f;
+    for (int v = tid; v < V; v += blockDim.x) s += expf(row[v] - mx);
+    s = warp_sum(s);
+    if (lane == 0) red[warp] = s;
+    __syncthreads();
+    if (tid == 0) {
+        float tot = 0.f;
+        for (int w = 0; w < 8; ++w) tot += red[w];
+        out[blockIdx.x] = (row[targets[blockIdx.x]] - mx) - logf(tot);
+    }
+}
+
 void prefill_forward(const ModelView &m, const DecodeView &dv, int slot, int T, PrefillBufs &pb,
-                     float *logits_row, cudaStream_t st) {
+                     float *logits_row, cudaStream_t st, const PrefillHooks *hk) {
     const int d = m.d;
+    int map_done = 0;
     for (int l = 0; l < m.n_layers; ++l) {
         const MkLayer &L = m.layers[l];
         launch_layernorm_rows(pb.x, L.ln1_w, L.ln1_b, T, d, pb.n, st);
         launch_gemm(EPI_QKV, L.qkv, pb.n, pb.qkv, T, nullptr, dv.k_cache, dv.v_cache, slot,
                     dv.n_slots, dv.n_heads, dv.max_seq, l, d, st);
+        if (hk && hk->maps && (l == hk->map_layers[0] || l == hk->map_layers[1])) {
+            const int rows = T - hk->map_q0;
+            head_probs_kernel<<<rows, 128, (size_t)T * sizeof(float), st>>>(
+                pb.qkv, T, d, hk->map_head, hk->map_q0, hk->map_k0, hk->map_k1, hk->maps, map_done++ > 0);
+        }
+        if (hk && l == hk->stop_layer) return;
         attn_prefill_kernel<<<dim3((T + 63) / 64, m.n_heads), 64, 0, st>>>(pb.qkv, T, d, pb.attn);
         launch_gemm(EPI_RESID, L.proj, pb.attn, pb.x, T, nullptr, nullptr, nullptr, -1, 0, 0, 0, l,
                     d, st);
@@ -269,6 +346,16 @@ void prefill_forward(const ModelView &m, const DecodeView &dv, int slot, int T, 
         launch_gemm(EPI_GELU, L.fc, pb.n, pb.u, T, nullptr, nullptr, nullptr, -1, 0, 0, 0, l, d, st);
         launch_gemm(EPI_RESID, L.mlp, pb.u, pb.x, T, nullptr, nullptr, nullptr, -1, 0, 0, 0, l, d,
                     st);
+    }
+    if (hk && hk->lp_q0 >= 0) {
+        // every row from lp_q0: ln_f, final_norm, mel_head, log_softmax at its target
+        const int rows = T - hk->lp_q0;
+        launch_layernorm_rows(pb.x + (size_t)hk->lp_q0 * d, m.ln_f_w, m.ln_f_b, rows, d, pb.n, st);
+        launch_layernorm_rows(pb.n, m.final_w, m.final_b, rows, d, pb.attn, st);
+        launch_gemm(EPI_PLAIN, m.mel_head, pb.attn, hk->lp_logits, rows, nullptr, nullptr, nullptr, -1, 0, 0, 0,
+                    0, d, st);
+        log_softmax_pick_kernel<<<rows, 256, 0, st>>>(hk->lp_logits, m.mel_vocab, hk->lp_targets, hk->lp_out);
+        return;
     }
     // ln_f then final_norm on the last row, then mel_head (gpt.rs:673-692)
     const float *last = pb.x + (size_t)(T - 1) * d;

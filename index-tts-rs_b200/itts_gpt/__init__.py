@@ -254,6 +254,43 @@ class Gpt:
                                         _ptr(out)))
         return out
 
+    def teacher_forced(self, text_tokens, conds, lang_id: int, codes, cache: "KvCache",
+                       slot: int = 0) -> "TeacherForced":
+        """Gpt::teacher_forced (gpt.rs:766-776): every code's log-probability and the text
+        attention of the alignment heads, [len(codes), len(text) + 2]."""
+        return self._replay(text_tokens, conds, lang_id, codes, cache, slot, True)
+
+    def code_log_probs(self, text_tokens, conds, lang_id: int, codes, cache: "KvCache",
+                       slot: int = 0) -> np.ndarray:
+        """Gpt::code_log_probs (gpt.rs:785-797)."""
+        return self._replay(text_tokens, conds, lang_id, codes, cache, slot, False).log_probs
+
+    def _replay(self, text_tokens, conds, lang_id, codes, cache, slot, attention):
+        t = np.ascontiguousarray(np.asarray(text_tokens, np.int32).reshape(-1))
+        k = np.ascontiguousarray(np.asarray(codes, np.int32).reshape(-1))
+        c = self._conds(conds)
+        lp = np.empty(max(1, k.size), np.float32)
+        att = np.empty((k.size, t.size + 2), np.float32) if attention else None
+        _check(load_lib().itts_gpt_teacher_forced(
+            self._h, cache._h, slot, _ptr(t), t.size, _ptr(c), c.shape[0], int(lang_id),
+            _ptr(k) if k.size else None, k.size, _ptr(lp),
+            _ptr(att) if att is not None and att.size else None))
+        return TeacherForced(attention=att if att is not None else np.zeros((0,), np.float32),
+                             log_probs=lp[:k.size])
+
+    def alignment_attention(self, text_tokens, conds, lang_id: int, prior_codes, codes,
+                            cache: "KvCache", slot: int = 0) -> np.ndarray:
+        """Gpt::alignment_attention (gpt.rs:875-915): [len(codes), len(text) + 2]."""
+        t = np.ascontiguousarray(np.asarray(text_tokens, np.int32).reshape(-1))
+        p = np.ascontiguousarray(np.asarray(prior_codes, np.int32).reshape(-1))
+        k = np.ascontiguousarray(np.asarray(codes, np.int32).reshape(-1))
+        c = self._conds(conds)
+        att = np.empty((max(1, k.size), t.size + 2), np.float32)
+        _check(load_lib().itts_gpt_alignment_attention(
+            self._h, cache._h, slot, _ptr(t), t.size, _ptr(c), c.shape[0], int(lang_id),
+            _ptr(p) if p.size else None, p.size, _ptr(k) if k.size else None, k.size, _ptr(att)))
+        return att[:k.size]
+
     def last_timing(self) -> tuple[float, float, int]:
         a, b, n = C.c_float(), C.c_float(), C.c_int32()
         _check(load_lib().itts_gpt_last_timing(self._h, C.byref(a), C.byref(b), C.byref(n)))
@@ -312,6 +349,15 @@ def sample_next_token(gpt: Gpt, logits: np.ndarray, seen: SeenTokenBitSet,
                                              C.byref(p), C.byref(st), C.byref(tok)))
     rng.state = st.value
     return tok.value
+
+
+@dataclass
+class TeacherForced:
+    """TeacherForced (gpt.rs:428-434): row-major attention [codes, text + 2] (empty when not
+    requested) and the log-probability of every code."""
+
+    attention: np.ndarray
+    log_probs: np.ndarray
 
 
 @dataclass

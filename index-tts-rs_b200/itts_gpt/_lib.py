@@ -64,6 +64,10 @@ SIGNATURES = [
     ("itts_kv_max_batch", _I32, [_P]),
     ("itts_gpt_prefill", C.c_int, [_P, _P, _I32, _P, _I32, _P, _I32, _I32, _P, _I32, _P]),
     ("itts_gpt_step", C.c_int, [_P, _P, _I32, _P, _P, _P, _P]),
+    ("itts_gpt_teacher_forced", C.c_int,
+     [_P, _P, _I32, _P, _I32, _P, _I32, _I32, _P, _I32, _P, _P]),
+    ("itts_gpt_alignment_attention", C.c_int,
+     [_P, _P, _I32, _P, _I32, _P, _I32, _I32, _P, _I32, _P, _I32, _P]),
     ("itts_sample_next_token", C.c_int,
      [_P, _P, _I32, _P, C.POINTER(SamplingParamsC), C.POINTER(C.c_uint64), C.POINTER(_I32)]),
     ("itts_sample_next_token_static", C.c_int,

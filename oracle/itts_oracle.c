@@ -506,6 +506,98 @@ int orc_prefill(const orc_model *m, orc_kv *kv, const int32_t *text, int n_text,
     return ORC_OK;
 }
 
+/* Alignment heads and the number of leading layers alignment replays
+ * (crates/core/src/align/mod.rs:37-40). */
+static const int ALIGN_HEADS[2][2] = {{4, 10}, {5, 10}};
+#define ALIGN_LAYERS 6
+#define MASK_FILL 1e9f /* gpt.rs:72 */
+
+/* Gpt2Block::head_attention (gpt.rs:391-427): softmax attention of one head of the layer
+ * whose input is x [T, d] (LN1 -> c_attn), for query rows qs..T-1, each seeing the
+ * whole prefix 0..qs-1 and the positions qs..itself; keeps key columns klo..khi-1.
+ * out: [T - qs][khi - klo]. */
+static void head_attention(const orc_model *m, int li, const float *x, int T, int head, int qs,
+                           int klo, int khi, float *out) {
+    const orc_layer *L = &m->layers[li];
+    const int d = m->d, nk = khi - klo;
+    float *n1 = (float *)malloc((size_t)T * d * sizeof(float));
+    float *qkv = (float *)malloc((size_t)T * 3 * d * sizeof(float));
+    layer_norm(x, L->ln1_w, L->ln1_b, T, d, n1);
+    linear_fwd(m, &L->c_attn, n1, T, qkv);
+#pragma omp parallel
+    {
+        float *sc = (float *)malloc((size_t)T * sizeof(float));
+#pragma omp for schedule(static)
+        for (int t = qs; t < T; ++t) {
+            const float *q = qkv + (size_t)t * 3 * d + head * HEAD_DIM;
+            float mx = -INFINITY;
+            for (int j = 0; j < T; ++j) {
+                const float *k = qkv + (size_t)j * 3 * d + d + head * HEAD_DIM;
+                float s = 0.0f;
+                for (int e = 0; e < HEAD_DIM; ++e) s += q[e] * k[e];
+                s *= ATTN_SCALE;
+                if (j > t) s += -MASK_FILL; /* (tri - 1) * MASK_FILL on the Mel part */
+                sc[j] = s;
+                if (s > mx) mx = s;
+            }
+            float den = 0.0f;
+            for (int j = 0; j < T; ++j) { sc[j] = expf(sc[j] - mx); den += sc[j]; }
+            for (int j = klo; j < khi; ++j) out[(size_t)(t - qs) * nk + (j - klo)] = sc[j] / den;
+        }
+        free(sc);
+    }
+    free(n1); free(qkv);
+}
+
+/* Gpt::replay (gpt.rs:800-861) and Gpt::alignment_attention (gpt.rs:875-915).
+ * fed: the codes fed after <START_MEL> (codes[..n-1], or prior ++ codes[..n-1]).
+ * mode 0: all layers; log_probs[i] = log_softmax(head(row qs + i))[targets[i]] for i < n_targets
+ *         (log_probs may be NULL); maps (may be NULL) = alignment attention from rows qs..
+ * mode 1: alignment only, the first ALIGN_LAYERS layers (the last one not run past its
+ *         attention map).  maps: [T - qs][n_text + 2], averaged over ALIGN_HEADS. */
+int orc_replay(const orc_model *m, orc_kv *kv, const int32_t *text, int n_text, const float *conds,
+               int n_conds, int lang, const int32_t *fed, int n_fed, int qs, int mode,
+               const int32_t *targets, int n_targets, float *log_probs, float *maps) {
+    int T = 0, rc = orc_sequence_embedding(m, text, n_text, conds, n_conds, lang, fed, n_fed, NULL, &T);
+    if (rc) return rc;
+    if (qs < 0 || qs >= T) return fail(ORC_E_VALIDATION, "codes: query start out of range");
+    const int want_maps = maps != NULL;
+    if (want_maps && (m->n_layers < ALIGN_LAYERS || m->n_heads <= ALIGN_HEADS[0][1]))
+        return fail(ORC_E_VALIDATION, "attention: the model has no alignment heads");
+    const int d = m->d, klo = n_conds, khi = n_conds + n_text + 2, rows = T - qs, nk = khi - klo;
+    float *x = (float *)malloc((size_t)T * d * sizeof(float));
+    orc_sequence_embedding(m, text, n_text, conds, n_conds, lang, fed, n_fed, x, &T);
+    orc_kv_reset(kv);
+    float *map_b = want_maps ? (float *)malloc((size_t)rows * nk * sizeof(float)) : NULL;
+    const int n_run = mode == 1 ? ALIGN_LAYERS : m->n_layers;
+    for (int l = 0; l < n_run; ++l) {
+        if (want_maps)
+            for (int a = 0; a < 2; ++a)
+                if (ALIGN_HEADS[a][0] == l)
+                    head_attention(m, l, x, T, ALIGN_HEADS[a][1], qs, klo, khi, a == 0 ? maps : map_b);
+        if (mode == 1 && l + 1 >= ALIGN_LAYERS) break;
+        rc = block_fwd(m, l, kv, x, T, T, 1);
+        if (rc) { free(x); free(map_b); return rc; }
+    }
+    orc_kv_reset(kv);
+    if (want_maps) /* stack(maps).mean(0) */
+        for (size_t i = 0; i < (size_t)rows * nk; ++i) maps[i] = (maps[i] + map_b[i]) / 2.0f;
+    if (mode == 0 && log_probs) {
+        float *lg = (float *)malloc((size_t)m->mel_vocab * sizeof(float));
+        for (int i = 0; i < n_targets && qs + i < T; ++i) {
+            head_fwd(m, x + (size_t)(qs + i) * d, lg);
+            float mx = -INFINITY;
+            for (int v = 0; v < m->mel_vocab; ++v) if (lg[v] > mx) mx = lg[v];
+            double den = 0.0;
+            for (int v = 0; v < m->mel_vocab; ++v) den += exp((double)(lg[v] - mx));
+            log_probs[i] = (lg[targets[i]] - mx) - (float)log(den); /* log_softmax, take_along_axis */
+        }
+        free(lg);
+    }
+    free(x); free(map_b);
+    return ORC_OK;
+}
+
 /* Gpt::step (gpt.rs:706-754) */
 int orc_step(const orc_model *m, orc_kv *kv, int tok, int pos, float *logits) {
     if (tok < 0 || tok >= m->mel_vocab) return fail(ORC_E_VALIDATION, "mel_token_id: out of range");

@@ -67,6 +67,7 @@ def lib() -> C.CDLL:
         L.orc_kv_reset.argtypes = [P]
         L.orc_kv_valid_len.argtypes = [P]
         L.orc_prefill.argtypes = [P, P, P, I, P, I, I, P, I, P]
+        L.orc_replay.argtypes = [P, P, P, I, P, I, I, P, I, I, I, P, I, P, P]
         L.orc_step.argtypes = [P, P, I, I, P]
         L.orc_generate.argtypes = [P, P, P, I, P, I, I, P, I, I, C.POINTER(ParamsC),
                                    C.POINTER(C.c_uint64), P, I, C.POINTER(I)]
@@ -162,6 +163,25 @@ class OracleModel:
                                  conds.shape[0], lang, prior.ctypes.data if prior.size else None,
                                  prior.size, out.ctypes.data))
         return out
+
+    def replay(self, kv: "OracleKv", text, conds, lang: int, fed, qs: int, mode: int = 0,
+               targets=(), want_maps: bool = False):
+        """Teacher-forced replay (gpt.rs:800-915): per-target log-probabilities of rows
+        qs.. (mode 0) and the alignment attention of those rows (mode 1: the first six
+        layers only).  Returns (log_probs or None, maps [rows, n_text + 2] or None)."""
+        text = np.ascontiguousarray(np.asarray(text, np.int32))
+        conds = np.ascontiguousarray(np.asarray(conds, np.float32).reshape(-1, self.d))
+        fed = np.ascontiguousarray(np.asarray(fed, np.int32))
+        targets = np.ascontiguousarray(np.asarray(targets, np.int32))
+        T = conds.shape[0] + text.size + 3 + fed.size
+        lp = np.empty(max(1, targets.size), np.float32) if targets.size else None
+        maps = np.empty((T - qs, text.size + 2), np.float32) if want_maps else None
+        _check(lib().orc_replay(self.h, kv.h, text.ctypes.data, text.size, conds.ctypes.data,
+                                conds.shape[0], lang, fed.ctypes.data if fed.size else None,
+                                fed.size, qs, mode, targets.ctypes.data if targets.size else None,
+                                targets.size, lp.ctypes.data if lp is not None else None,
+                                maps.ctypes.data if maps is not None else None))
+        return (lp[:targets.size] if lp is not None else None), maps
 
     def step(self, kv: "OracleKv", tok: int, pos: int) -> np.ndarray:
         out = np.empty(self.mel_vocab, np.float32)
