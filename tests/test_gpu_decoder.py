@@ -195,12 +195,13 @@ def _teacher_forced_agreement(om, prompt, params, codes, rng_state):
     return agree / max(1, len(codes)), st, bad
 
 
-@pytest.mark.parametrize("n_req", [3, 6])
+@pytest.mark.parametrize("n_req", [3, 6, 20])
 def test_generate_batch_matches_checker(small, small_cfg, n_req):
-    """Ragged batched generation (3 requests: the persistent kernel; 6: the GEMM path):
-    every request's codes agree with the checker teacher-forced, with the same draws."""
+    """Ragged batched generation (3 requests: the persistent kernel; 6: the CUDA-core GEMM
+    path; 20: the tensor-core GEMM path): every request's codes agree with the checker
+    teacher-forced, with the same draws."""
     gpt, om = small
-    lens = [5, 40, 17, 60, 9, 33][:n_req]
+    lens = ([5, 40, 17, 60, 9, 33] * 4)[:n_req]
     prompts, params = [], []
     for i, n in enumerate(lens):
         steps = 12 + 5 * i
