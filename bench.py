@@ -322,6 +322,22 @@ def run_profile_case(args):
                       "ms_per_launch": ms, "launches_per_step": n}), flush=True)
 
 
+def run_profile_prefill(args):
+    """A small case for profilers: cfg2 prefills (635 positions) of one request, repeated."""
+    import itts_gpt as ig
+    cfg, w = make_model()
+    gpt = ig.Gpt.from_weights(w)
+    text, conds = make_prompt(cfg, 0)
+    kv = ig.KvCache(gpt, max_seq=N_CONDS + N_TEXT + 3 + 8, max_batch=1)
+    import time
+    for i in range(args.profile_prefill):
+        t0 = time.perf_counter()
+        gpt.prefill(text, conds, LANG, kv)
+        dt = time.perf_counter() - t0
+    print(json.dumps({"profile_case": "cfg2 prefill", "positions": N_CONDS + N_TEXT + 3,
+                      "repeats": args.profile_prefill, "last_wall_ms": 1000.0 * dt}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -332,9 +348,14 @@ def main():
     ap.add_argument("--profile-decode", type=int, default=0, metavar="KV_LEN",
                     help="profiler case: only the decode-step forward at this KV length")
     ap.add_argument("--profile-iters", type=int, default=2)
+    ap.add_argument("--profile-prefill", type=int, default=0, metavar="REPEATS",
+                    help="profiler case: only cfg2 prefills, this many")
     args = ap.parse_args()
     if args.profile_decode > 0:
         run_profile_case(args)
+        return
+    if args.profile_prefill > 0:
+        run_profile_prefill(args)
         return
     rank, world, local_rank = dist_env()
     if world > 1:

@@ -41,7 +41,7 @@ void launch_embed_step(const ModelView &m, const DecodeView &dv, float *x, cudaS
 struct AttnParams {
     const float *q;
     int q_stride;
-    float *out;
+    __half *out;  // [nb][d] fp16 (the input of the c_proj GEMM)
     const __half *k_cache, *v_cache;
     const SlotState *slots;
     const int *batch_slot;
@@ -152,7 +152,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnParams p) {
             a += sm_acc[w][e] * f;
         }
         if (n_used == 1) {
-            p.out[(size_t)col * p.d + h * kHeadDim + e] = a / l;
+            p.out[(size_t)col * p.d + h * kHeadDim + e] = __float2half_rn(a / l);
         } else {
             part_out[2 + e] = a;
             if (e == 0) { part_out[0] = M; part_out[1] = l; }
@@ -181,7 +181,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnParams p) {
             l += __ldcg(pp + s * 66 + 1) * f;
             a += __ldcg(pp + s * 66 + 2 + e) * f;
         }
-        p.out[(size_t)col * p.d + h * kHeadDim + e] = a / l;
+        p.out[(size_t)col * p.d + h * kHeadDim + e] = __float2half_rn(a / l);
         if (e == 0) p.counters[col * p.n_heads + h] = 0;
     }
 }
@@ -191,7 +191,7 @@ void launch_attn_decode(const DecodeView &dv, int layer, const float *q, int q_s
     AttnParams p{};
     p.q = q;
     p.q_stride = q_stride;
-    p.out = b.attn;
+    p.out = reinterpret_cast<__half *>(b.attn);
     p.k_cache = dv.k_cache;
     p.v_cache = dv.v_cache;
     p.slots = dv.slots;
@@ -260,22 +260,24 @@ cudaError_t decode_forward(const ModelView &m, const DecodeView &dv, DecodeBufs 
     if (use_mk(b, dv.nb)) return mk_launch(mk_params(m, dv, b), st);
     const int d = m.d;
     launch_embed_step(m, dv, b.x, st);
+    __half *n16 = reinterpret_cast<__half *>(b.n), *attn16 = reinterpret_cast<__half *>(b.attn),
+           *u16 = reinterpret_cast<__half *>(b.u), *fin16 = reinterpret_cast<__half *>(b.n2);
     for (int l = 0; l < m.n_layers; ++l) {
         const MkLayer &L = m.layers[l];
-        launch_layernorm_rows(b.x, L.ln1_w, L.ln1_b, dv.nb, d, b.n, st);
-        launch_gemm(EPI_QKV, L.qkv, b.n, b.q, dv.nb, &dv, dv.k_cache, dv.v_cache, -1, dv.n_slots,
+        launch_layernorm_rows_h(b.x, L.ln1_w, L.ln1_b, dv.nb, d, n16, st);
+        launch_gemm(EPI_QKV, L.qkv, n16, b.q, dv.nb, &dv, dv.k_cache, dv.v_cache, -1, dv.n_slots,
                     dv.n_heads, dv.max_seq, l, d, st);
         launch_attn_decode(dv, l, b.q, 3 * d, b, st);
-        launch_gemm(EPI_RESID, L.proj, b.attn, b.x, dv.nb, nullptr, nullptr, nullptr, -1, 0, 0, 0, l,
+        launch_gemm(EPI_RESID, L.proj, attn16, b.x, dv.nb, nullptr, nullptr, nullptr, -1, 0, 0, 0, l,
                     d, st);
-        launch_layernorm_rows(b.x, L.ln2_w, L.ln2_b, dv.nb, d, b.n, st);
-        launch_gemm(EPI_GELU, L.fc, b.n, b.u, dv.nb, nullptr, nullptr, nullptr, -1, 0, 0, 0, l, d, st);
-        launch_gemm(EPI_RESID, L.mlp, b.u, b.x, dv.nb, nullptr, nullptr, nullptr, -1, 0, 0, 0, l, d,
+        launch_layernorm_rows_h(b.x, L.ln2_w, L.ln2_b, dv.nb, d, n16, st);
+        launch_gemm(EPI_GELU, L.fc, n16, b.u, dv.nb, nullptr, nullptr, nullptr, -1, 0, 0, 0, l, d, st);
+        launch_gemm(EPI_RESID, L.mlp, u16, b.x, dv.nb, nullptr, nullptr, nullptr, -1, 0, 0, 0, l, d,
                     st);
     }
     launch_layernorm_rows(b.x, m.ln_f_w, m.ln_f_b, dv.nb, d, b.n, st);
-    launch_layernorm_rows(b.n, m.final_w, m.final_b, dv.nb, d, b.n2, st);
-    launch_gemm(EPI_PLAIN, m.mel_head, b.n2, b.logits, dv.nb, nullptr, nullptr, nullptr, -1, 0, 0, 0,
+    launch_layernorm_rows_h(b.n, m.final_w, m.final_b, dv.nb, d, fin16, st);
+    launch_gemm(EPI_PLAIN, m.mel_head, fin16, b.logits, dv.nb, nullptr, nullptr, nullptr, -1, 0, 0, 0,
                 0, d, st);
     return cudaGetLastError();
 }

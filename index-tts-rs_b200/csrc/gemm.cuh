@@ -7,8 +7,8 @@ namespace itts {
 
 struct GemmParams {
     MkLin W;
-    const float *x;  // [T, K]
-    float *y;        // [T, OUT]
+    const __half *x;  // [T, K] fp16 activations
+    float *y;         // [T, OUT] (fp16 [T, OUT] for EPI_GELU, whose output feeds the next GEMM)
     int T;
     // EPI_QKV: prefill writes row t's K/V at position t of kv_slot; decode (slots != null)
     // writes them at the valid_len of slot batch_slot[t]
@@ -18,39 +18,50 @@ struct GemmParams {
     int kv_slot, n_slots, n_heads, max_seq, layer, d;
 };
 
-// Output (t, o) with value v = accumulator + bias[o], per epilogue.
+// Where row t's new K/V go (EPI_QKV): position t of kv_slot in prefill; the valid_len of
+// slot batch_slot[t] in decode, unless that slot is inactive or full.
+struct QkvDest {
+    int slot, pos;
+    bool write;
+};
+__device__ __forceinline__ QkvDest qkv_dest(const GemmParams &p, int t) {
+    QkvDest q{p.kv_slot, t, t < p.max_seq};
+    if (p.slots) {
+        q.slot = p.batch_slot[t];
+        const SlotState &st = p.slots[q.slot];
+        q.pos = st.valid_len;
+        q.write = st.active && q.pos < p.max_seq;
+    }
+    return q;
+}
+
+// Output (t, o) with value v = accumulator + bias[o], per epilogue (qd: row t's K/V
+// destination, used by EPI_QKV).
 template <int EPI>
-__device__ __forceinline__ void gemm_store(const GemmParams &p, int t, int o, float v) {
+__device__ __forceinline__ void gemm_store(const GemmParams &p, int t, int o, float v, const QkvDest &qd) {
     const int OUT = p.W.out;
     float *yp = p.y + (size_t)t * OUT + o;
     if (EPI == EPI_PLAIN) {
         *yp = v;
     } else if (EPI == EPI_GELU) {
-        *yp = gelu_tanh(v);
+        reinterpret_cast<__half *>(p.y)[(size_t)t * OUT + o] = __float2half_rn(gelu_tanh(v));
     } else if (EPI == EPI_RESID) {
         *yp += v;
     } else {
         *yp = v;
-        if (o >= p.d) {
+        if (o >= p.d && qd.write) {
             const int rr = o - p.d, which = rr / p.d, oo = rr - which * p.d;
             __half *cache = which == 0 ? p.k_cache : p.v_cache;
-            int slot = p.kv_slot, pos = t;
-            bool write = t < p.max_seq;
-            if (p.slots) {
-                slot = p.batch_slot[t];
-                const SlotState &st = p.slots[slot];
-                pos = st.valid_len;
-                write = st.active && pos < p.max_seq;
-            }
-            if (write)
-                cache[kv_index(p.layer, slot, oo >> 6, pos, p.n_slots, p.n_heads, p.max_seq) + (oo & 63)] =
-                    __float2half_rn(v);
+            cache[kv_index(p.layer, qd.slot, oo >> 6, qd.pos, p.n_slots, p.n_heads, p.max_seq) + (oo & 63)] =
+                __float2half_rn(v);
         }
     }
 }
 
 // Tensor-core version (gemm_tc.cu): tcgen05 MMA on 128 x 128 tiles, TMEM accumulators.
-void launch_gemm_tc(int epi, const GemmParams &p, cudaStream_t st);
+// False when the activation tensor map could not be built (the caller then uses the
+// CUDA-core kernel).
+bool launch_gemm_tc(int epi, const GemmParams &p, cudaStream_t st);
 void kernels_init_gemm_tc();
 
 }  // namespace itts

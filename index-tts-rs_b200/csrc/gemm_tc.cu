@@ -5,19 +5,33 @@
 //
 // One CTA computes a 128-row (positions) x 128-column (weight rows) tile with an fp32
 // accumulator in tensor memory.  The K loop runs over the 64-input quantization groups:
-// the 8 warps stage the group's activations (fp32 -> fp16) and its weights (int8 ->
-// s * q + b in fp32 -> fp16) into shared memory in the 128-byte-swizzled K-major layout
-// the MMA reads, and one thread issues the 4 tcgen05.mma (K = 16 each) of the group and
-// commits them to the stage's mbarrier.  Two stages: the next group is staged while the
-// tensor core runs the current one.  Every wait is bounded; on expiry the kernel records
-// an error, skips the rest, frees its tensor memory and returns.
+//  * the fp16 activation tile of a group (128 rows x 128 bytes) arrives by one TMA tensor
+//    copy straight into one of four A stages, already in the 128-byte-swizzled K-major
+//    layout the MMA reads;
+//  * the group's int8 weight bytes and (scale, offset) pairs arrive by cp.async into one of
+//    three raw stages, and the 8 warps dequantize them (s * q + b in fp32, then fp16) into
+//    one of two B stages in the same swizzled layout;
+//  * one thread issues the group's 4 tcgen05.mma (K = 16 each) and commits them to the B
+//    stage's mbarrier.
+// Copies run two groups ahead, so copies, dequantization and tensor-core work overlap.
+// Every wait is bounded; on expiry the kernel records an error, skips the rest, lets its
+// copies land, frees its tensor memory and returns.
+#include <cuda.h>
+
+#include <mutex>
+
 #include "gemm.cuh"
 
 namespace itts {
 
 constexpr int TC_BM = 128, TC_BN = 128, TC_BK = 64, TC_THREADS = 256;
-constexpr int TC_TILE_BYTES = TC_BM * TC_BK * 2;  // one operand of one stage: 16 KB
-constexpr int TC_SMEM = 2 * 2 * TC_TILE_BYTES + 1024;
+constexpr int TC_TILE_BYTES = TC_BM * TC_BK * 2;  // one operand stage: 16 KB
+constexpr int TC_A_STAGES = 4, TC_B_STAGES = 2, TC_RAW_STAGES = 3;
+// raw weight stage: weight bytes (128 rows x 64) and (scale, offset) pairs (8 B per row)
+constexpr int TC_RAW_B = TC_BN * TC_BK, TC_RAW_S = TC_BN * 8, TC_RAW_STAGE = TC_RAW_B + TC_RAW_S;
+constexpr int TC_OFF_B = TC_A_STAGES * TC_TILE_BYTES;
+constexpr int TC_OFF_RAW = TC_OFF_B + TC_B_STAGES * TC_TILE_BYTES;
+constexpr int TC_SMEM = TC_OFF_RAW + TC_RAW_STAGES * TC_RAW_STAGE + 1024;
 constexpr uint32_t TC_TMEM_COLS = 128;
 constexpr long TC_SPIN = 1L << 24;
 // instruction descriptor (kind::f16): D f32, A and B f16, both K-major, N = 128, M = 128
@@ -28,8 +42,8 @@ __device__ int g_gemm_tc_error;  // nonzero once a bounded wait gave up
 __device__ __forceinline__ uint32_t tc_su32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
 // Byte offset of element (r, k), k < 64, in a K-major tile of 64 fp16 per row with the
-// 128-byte swizzle: 8-row groups of 1024 B; in row r the 16-byte chunk k/8 sits at chunk
-// position (k/8) ^ (r % 8).
+// 128-byte swizzle (the layout TMA writes with CU_TENSOR_MAP_SWIZZLE_128B): 8-row groups of
+// 1024 B; in row r the 16-byte chunk k/8 sits at chunk position (k/8) ^ (r % 8).
 __device__ __forceinline__ uint32_t tc_swz(int r, int k) {
     return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + (((k >> 3) ^ (r & 7)) << 4) + (k & 7) * 2);
 }
@@ -57,20 +71,66 @@ __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
     const __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<const uint32_t *>(&h);
 }
+// 16-byte (or 4 / 8-byte) asynchronous global -> shared copies, zero-filled past src_bytes.
+__device__ __forceinline__ void cp_async16(void *dst, const void *src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(tc_su32(dst)), "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async4(void *dst, const void *src, uint32_t src_bytes) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(tc_su32(dst)), "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async8(void *dst, const void *src, uint32_t src_bytes) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(tc_su32(dst)), "l"(src), "r"(src_bytes)
+                 : "memory");
+}
+// The fp16 activation tile of group kb (x = kb * 64, rows m0.. ; rows past T read as zero)
+// into an A stage, completing on `bar` (no multicast).
+__device__ __forceinline__ void tc_load_a(const CUtensorMap *tmap, void *dst, int kb, int m0, uint64_t *bar) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc_su32(bar)), "r"(TC_TILE_BYTES)
+                 : "memory");
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(tc_su32(dst)),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(kb * TC_BK), "r"(m0), "r"(tc_su32(bar))
+        : "memory");
+}
+// The weight bytes (128 rows x 64 in fragment order) and (scale, offset) pairs of group kb
+// into a raw stage; rows past the weight's rows are zero-filled.
+__device__ __forceinline__ void tc_issue_raw_b(const GemmParams &p, uint8_t *raw, int kb, int o0, int rows_alloc) {
+    const int tid = threadIdx.x, OUT = p.W.out;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const int c = tid + i * TC_THREADS, r = c >> 2, fc = c & 3, o = o0 + r;
+        const bool in = o < OUT && o < rows_alloc;
+        cp_async16(raw + r * 64 + fc * 16,
+                   in ? (const void *)(p.W.tiles + mk_q_offset(p.W, o, kb * TC_BK) + fc * 16) : (const void *)p.W.tiles,
+                   in ? 16u : 0u);
+    }
+    if (tid < TC_BN) {
+        const int o = o0 + tid;
+        const bool in = o < OUT && o < rows_alloc;
+        const void *src = in ? (const void *)(p.W.tiles + mk_sb_offset(p.W, o, kb * TC_BK)) : (const void *)p.W.tiles;
+        if (p.W.sbb == 4) cp_async4(raw + TC_RAW_B + tid * 8, src, in ? 4u : 0u);
+        else cp_async8(raw + TC_RAW_B + tid * 8, src, in ? 8u : 0u);
+    }
+}
 
 template <int EPI>
-__global__ void __launch_bounds__(TC_THREADS, 1) gemm_q8_tc_kernel(GemmParams p) {
+__global__ void __launch_bounds__(TC_THREADS, 1) gemm_q8_tc_kernel(GemmParams p, const __grid_constant__ CUtensorMap tmap_a) {
     extern __shared__ uint8_t tc_smem_raw[];
-    __shared__ uint64_t bar[2];
+    __shared__ uint64_t mma_bar[TC_B_STAGES], a_bar[TC_A_STAGES];
     __shared__ uint32_t tmem_base;
+    __shared__ float bias_s[TC_BN];  // the tile's output-row biases, read once
     uint8_t *smem = tc_smem_raw + ((1024u - (tc_su32(tc_smem_raw) & 1023u)) & 1023u);
+    uint8_t *sA = smem, *sB = smem + TC_OFF_B, *sR = smem + TC_OFF_RAW;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int K = p.W.in, OUT = p.W.out, T = p.T, rows_alloc = p.W.n_rb * 16;
     const int m0 = blockIdx.y * TC_BM, o0 = blockIdx.x * TC_BN;
     const int nkb = K / TC_BK;
     if (tid == 0) {
-        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(tc_su32(&bar[0])));
-        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(tc_su32(&bar[1])));
+        for (int s = 0; s < TC_B_STAGES; ++s) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(tc_su32(&mma_bar[s])));
+        for (int s = 0; s < TC_A_STAGES; ++s) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(tc_su32(&a_bar[s])));
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 0) {
@@ -78,71 +138,74 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_q8_tc_kernel(GemmParams p)
                      "r"(TC_TMEM_COLS));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
+    if (tid < TC_BN) bias_s[tid] = o0 + tid < OUT ? p.W.bias[o0 + tid] : 0.f;
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = tmem_base;
+    // prologue: the copies of the first two groups
+    int a_issued = 0, a_waited = 0;  // A tiles issued / waited for (meaningful in thread 0)
+#pragma unroll 1
+    for (int s = 0; s < 2; ++s) {
+        if (s < nkb) {
+            if (tid == 0) { tc_load_a(&tmap_a, sA + s * TC_TILE_BYTES, s, m0, &a_bar[s]); ++a_issued; }
+            tc_issue_raw_b(p, sR + s * TC_RAW_STAGE, s, o0, rows_alloc);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    }
     const bool half_sb = p.W.sbb == 4;
 
     bool ok = true;
     int last = -1;  // last group whose MMAs were committed
     for (int kb = 0; kb < nkb; ++kb) {
-        const int s = kb & 1;
-        uint8_t *sa = smem + s * 2 * TC_TILE_BYTES, *sb = sa + TC_TILE_BYTES;
-        // the MMAs of group kb - 2 read this stage: wait for them before overwriting it
-        const bool okw = kb < 2 || tc_wait(&bar[s], (uint32_t)((kb - 2) >> 1) & 1u);
-        if (okw) {
-            // activations: 128 positions x 64 inputs, 8 per 16-byte chunk
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int c = tid + i * TC_THREADS, r = c >> 3, ch = c & 7, t = m0 + r;
-                uint4 h = make_uint4(0u, 0u, 0u, 0u);
-                if (t < T) {
-                    const float *src = p.x + (size_t)t * K + kb * TC_BK + ch * 8;
-                    const float4 a = *reinterpret_cast<const float4 *>(src);
-                    const float4 b = *reinterpret_cast<const float4 *>(src + 4);
-                    h = make_uint4(pack_half2(a.x, a.y), pack_half2(a.z, a.w), pack_half2(b.x, b.y), pack_half2(b.z, b.w));
-                }
-                *reinterpret_cast<uint4 *>(sa + tc_swz(r, ch * 8)) = h;
+        const int bs = kb & 1, as = kb % TC_A_STAGES;
+        uint8_t *bt = sB + bs * TC_TILE_BYTES;
+        const uint8_t *raw = sR + (kb % TC_RAW_STAGES) * TC_RAW_STAGE;
+        // this thread's weight copies of group kb have landed (group kb + 1 may be pending)
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+        // the MMAs of group kb - 2 are done: B stage bs and A stage (kb + 2) % 4 are free
+        const bool okw = kb < 2 || tc_wait(&mma_bar[bs], (uint32_t)((kb - 2) >> 1) & 1u);
+        // every thread's copies of group kb are visible and every thread is done with the raw
+        // stage of group kb - 1, which now receives group kb + 2
+        __syncthreads();
+        if (kb + 2 < nkb) {
+            if (tid == 0 && okw) {
+                tc_load_a(&tmap_a, sA + ((kb + 2) % TC_A_STAGES) * TC_TILE_BYTES, kb + 2, m0,
+                          &a_bar[(kb + 2) % TC_A_STAGES]);
+                ++a_issued;
             }
-            // weights: 128 rows x 64 inputs; a row's group is 4 chunks of 16 bytes in fragment
-            // order (chunk c holds inputs 16b + 8hi + 2c + lo), dequantized as s * q + b
+            tc_issue_raw_b(p, sR + ((kb + 2) % TC_RAW_STAGES) * TC_RAW_STAGE, kb + 2, o0, rows_alloc);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        if (okw) {
+            // weights: a row's group is 4 chunks of 16 bytes in fragment order (chunk c holds
+            // inputs 16b + 8hi + 2c + lo), dequantized as s * q + b in fp32, then fp16
 #pragma unroll
             for (int i = 0; i < 2; ++i) {
-                const int c = tid + i * TC_THREADS, r = c >> 2, fc = c & 3, o = o0 + r;
-                uint32_t hv[8];
-                if (o < OUT && o < rows_alloc) {
-                    const uint4 w = ld_stream(p.W.tiles + mk_q_offset(p.W, o, kb * TC_BK) + fc * 16);
-                    const uint8_t *sbp = p.W.tiles + mk_sb_offset(p.W, o, kb * TC_BK);
-                    float sc, zo;
-                    if (half_sb) {
-                        const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(sbp));
-                        sc = f.x; zo = f.y;
-                    } else {
-                        const float2 f = *reinterpret_cast<const float2 *>(sbp);
-                        sc = f.x; zo = f.y;
-                    }
-                    const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-                    for (int b = 0; b < 4; ++b) {
-                        hv[2 * b] = pack_half2(fmaf(sc, byte_to_float(ww[b], 0), zo), fmaf(sc, byte_to_float(ww[b], 1), zo));
-                        hv[2 * b + 1] =
-                            pack_half2(fmaf(sc, byte_to_float(ww[b], 2), zo), fmaf(sc, byte_to_float(ww[b], 3), zo));
-                    }
+                const int c = tid + i * TC_THREADS, r = c >> 2, fc = c & 3;
+                const uint4 w = *reinterpret_cast<const uint4 *>(raw + r * 64 + fc * 16);
+                const uint8_t *sbp = raw + TC_RAW_B + r * 8;
+                float sc, zo;
+                if (half_sb) {
+                    const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(sbp));
+                    sc = f.x; zo = f.y;
                 } else {
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) hv[e] = 0u;
+                    const float2 f = *reinterpret_cast<const float2 *>(sbp);
+                    sc = f.x; zo = f.y;
                 }
+                const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
                 for (int b = 0; b < 4; ++b) {
-                    const int k0 = b * 16 + 2 * fc;  // bytes 0, 1 of word b
-                    *reinterpret_cast<uint32_t *>(sb + tc_swz(r, k0)) = hv[2 * b];
-                    *reinterpret_cast<uint32_t *>(sb + tc_swz(r, k0 + 8)) = hv[2 * b + 1];  // bytes 2, 3
+                    const int k0 = b * 16 + 2 * fc;  // bytes 0, 1 of word b; bytes 2, 3 are k0 + 8, + 9
+                    *reinterpret_cast<uint32_t *>(bt + tc_swz(r, k0)) =
+                        pack_half2(fmaf(sc, byte_to_float(ww[b], 0), zo), fmaf(sc, byte_to_float(ww[b], 1), zo));
+                    *reinterpret_cast<uint32_t *>(bt + tc_swz(r, k0 + 8)) =
+                        pack_half2(fmaf(sc, byte_to_float(ww[b], 2), zo), fmaf(sc, byte_to_float(ww[b], 3), zo));
                 }
             }
         }
-        // make the staged tiles visible to the tensor core, agree on success, then issue
-        // the group's MMAs
+        // make the dequantized weights visible to the tensor core, agree on success, then
+        // issue the group's MMAs once its activation tile has landed
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
         ok = __syncthreads_and(okw ? 1 : 0) != 0;
@@ -150,28 +213,33 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_q8_tc_kernel(GemmParams p)
         if (!ok) break;
         last = kb;
         if (tid == 0) {
+            const bool oka = tc_wait(&a_bar[as], (uint32_t)(kb / TC_A_STAGES) & 1u);
+            ++a_waited;
+            if (oka) {
+                const uint32_t at = tc_su32(sA + as * TC_TILE_BYTES), btu = tc_su32(bt);
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const uint64_t da = tc_desc(tc_su32(sa) + k * 32), db = tc_desc(tc_su32(sb) + k * 32);
-                const uint32_t accumulate = (kb > 0 || k > 0) ? 1u : 0u;
-                asm volatile(
-                    "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-                    " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
-                    "l"(da), "l"(db), "r"(TC_IDESC), "r"(accumulate));
+                for (int k = 0; k < 4; ++k) {
+                    const uint32_t accumulate = (kb > 0 || k > 0) ? 1u : 0u;
+                    asm volatile(
+                        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
+                        "l"(tc_desc(at + k * 32)), "l"(tc_desc(btu + k * 32)), "r"(TC_IDESC), "r"(accumulate));
+                }
+                asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                                 tc_su32(&mma_bar[bs]))
+                             : "memory");
             }
-            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                             tc_su32(&bar[s]))
-                         : "memory");
         }
     }
     // the last committed group's commit covers every MMA issued for the tile (also after a
     // failed wait, so that no MMA still writes the tensor memory when it is freed)
-    const bool okl = last < 0 || tc_wait(&bar[last & 1], (uint32_t)(last >> 1) & 1u);
+    const bool okl = last < 0 || tc_wait(&mma_bar[last & 1], (uint32_t)(last >> 1) & 1u);
     ok = __syncthreads_and((ok && okl) ? 1 : 0) != 0;
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     if (ok && last == nkb - 1 && nkb > 0) {
         // warp w reads TMEM lanes 32 (w % 4) .. (its 32 positions), columns 64 (w / 4) ..
         const int q = warp & 3, half = warp >> 2, t = m0 + q * 32 + lane;
+        const QkvDest qd = EPI == EPI_QKV && t < T ? qkv_dest(p, t) : QkvDest{0, 0, false};
 #pragma unroll 1
         for (int cc = 0; cc < 64; cc += 16) {
             uint32_t v[16];
@@ -184,14 +252,32 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_q8_tc_kernel(GemmParams p)
                   "=r"(v[15])
                 : "r"(ta));
             asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-            if (t < T) {
+            const int ob = o0 + half * 64 + cc;
+            if (t < T && ob < OUT) {
+                const int nj = min(16, OUT - ob);
+                const int cb = half * 64 + cc;
+                if (EPI == EPI_RESID) {
+                    // read the 16 residual values first so their loads overlap
+                    float *yp = p.y + (size_t)t * OUT + ob;
+                    float old[16];
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int o = o0 + half * 64 + cc + j;
-                    if (o < OUT) gemm_store<EPI>(p, t, o, __uint_as_float(v[j]) + p.W.bias[o]);
+                    for (int j = 0; j < 16; ++j) old[j] = j < nj ? yp[j] : 0.f;
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        if (j < nj) yp[j] = old[j] + (__uint_as_float(v[j]) + bias_s[cb + j]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 16; ++j)
+                        if (j < nj) gemm_store<EPI>(p, t, ob + j, __uint_as_float(v[j]) + bias_s[cb + j], qd);
                 }
             }
         }
+    }
+    // teardown: this thread's weight copies have landed, and every activation tile that was
+    // issued but not waited for (a loop that stopped early) has landed too
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    if (tid == 0) {
+        for (int i = a_waited; i < a_issued; ++i) tc_wait(&a_bar[i % TC_A_STAGES], (uint32_t)(i / TC_A_STAGES) & 1u);
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
@@ -199,14 +285,49 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_q8_tc_kernel(GemmParams p)
     if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_TMEM_COLS));
 }
 
-void launch_gemm_tc(int epi, const GemmParams &p, cudaStream_t st) {
+namespace {
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_tiled() {
+    static std::once_flag once;
+    static EncodeTiledFn fn = nullptr;
+    std::call_once(once, [] {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(f);
+        else
+            cudaGetLastError();
+    });
+    return fn;
+}
+}  // namespace
+
+bool launch_gemm_tc(int epi, const GemmParams &p, cudaStream_t st) {
+    const int K = p.W.in;
+    // the activation rows must be 16-byte aligned for the tensor map; K a multiple of 64
+    if (K % TC_BK != 0 || (reinterpret_cast<uintptr_t>(p.x) & 15) != 0 || p.T <= 0) return false;
+    EncodeTiledFn enc = encode_tiled();
+    if (!enc) return false;
+    CUtensorMap map;
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)p.T};
+    const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)TC_BK, (cuuint32_t)TC_BM};
+    const cuuint32_t estr[2] = {1, 1};
+    if (enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half *>(p.x), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return false;
     const dim3 grid((p.W.out + TC_BN - 1) / TC_BN, (p.T + TC_BM - 1) / TC_BM);
     switch (epi) {
-    case EPI_PLAIN: gemm_q8_tc_kernel<EPI_PLAIN><<<grid, TC_THREADS, TC_SMEM, st>>>(p); break;
-    case EPI_GELU: gemm_q8_tc_kernel<EPI_GELU><<<grid, TC_THREADS, TC_SMEM, st>>>(p); break;
-    case EPI_RESID: gemm_q8_tc_kernel<EPI_RESID><<<grid, TC_THREADS, TC_SMEM, st>>>(p); break;
-    default: gemm_q8_tc_kernel<EPI_QKV><<<grid, TC_THREADS, TC_SMEM, st>>>(p); break;
+    case EPI_PLAIN: gemm_q8_tc_kernel<EPI_PLAIN><<<grid, TC_THREADS, TC_SMEM, st>>>(p, map); break;
+    case EPI_GELU: gemm_q8_tc_kernel<EPI_GELU><<<grid, TC_THREADS, TC_SMEM, st>>>(p, map); break;
+    case EPI_RESID: gemm_q8_tc_kernel<EPI_RESID><<<grid, TC_THREADS, TC_SMEM, st>>>(p, map); break;
+    default: gemm_q8_tc_kernel<EPI_QKV><<<grid, TC_THREADS, TC_SMEM, st>>>(p, map); break;
     }
+    return true;
 }
 
 void kernels_init_gemm_tc() {
@@ -214,6 +335,7 @@ void kernels_init_gemm_tc() {
     cudaFuncSetAttribute(gemm_q8_tc_kernel<EPI_GELU>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM);
     cudaFuncSetAttribute(gemm_q8_tc_kernel<EPI_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM);
     cudaFuncSetAttribute(gemm_q8_tc_kernel<EPI_QKV>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM);
+    encode_tiled();
 }
 
 }  // namespace itts

@@ -55,11 +55,15 @@ void launch_attn_decode(const DecodeView &dv, int layer, const float *q, int q_s
 
 void launch_layernorm_rows(const float *x, const float *w, const float *b, int rows, int d,
                            float *y, cudaStream_t st);
+// The same with an fp16 output (the input of a GEMM).
+void launch_layernorm_rows_h(const float *x, const float *w, const float *b, int rows, int d,
+                             __half *y, cudaStream_t st);
 
-// y[t, :] = x[t, :] . W^T + bias with an epilogue, for t < T.  In decode mode (dv != null)
-// the QKV epilogue appends row t's K/V to slot batch_slot[t] at its valid_len; in prefill
-// mode (dv == null, kv_slot >= 0) row t's K/V go to position t of kv_slot.
-void launch_gemm(int epi, const MkLin &W, const float *x, float *y, int T, const DecodeView *dv,
+// y[t, :] = x[t, :] . W^T + bias with an epilogue, for t < T; x is fp16, y is fp32 (fp16
+// for EPI_GELU).  In decode mode (dv != null) the QKV epilogue appends row t's K/V to slot
+// batch_slot[t] at its valid_len; in prefill mode (dv == null, kv_slot >= 0) row t's K/V go
+// to position t of kv_slot.
+void launch_gemm(int epi, const MkLin &W, const __half *x, void *y, int T, const DecodeView *dv,
                  __half *k_cache, __half *v_cache, int kv_slot, int n_slots, int n_heads,
                  int max_seq, int layer, int d, cudaStream_t st);
 

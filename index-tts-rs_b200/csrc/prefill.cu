@@ -42,8 +42,9 @@ void launch_embed_prefix(const ModelView &m, const int *full_text, int n_full, c
 }
 
 // y[t] = LayerNorm(x[t]) * w + b, one CTA per row, two-pass statistics.
+template <typename TY>
 __global__ void __launch_bounds__(256) layernorm_rows_kernel(const float *x, const float *w,
-                                                             const float *b, int d, float *y) {
+                                                             const float *b, int d, TY *y) {
     const int t = blockIdx.x;
     const float *row = x + (size_t)t * d;
     __shared__ float red[8];
@@ -77,13 +78,20 @@ __global__ void __launch_bounds__(256) layernorm_rows_kernel(const float *x, con
     }
     __syncthreads();
     const float rstd = stat;
-    for (int i = threadIdx.x; i < d; i += blockDim.x)
-        y[(size_t)t * d + i] = (row[i] - mean) * rstd * w[i] + b[i];
+    for (int i = threadIdx.x; i < d; i += blockDim.x) {
+        const float v = (row[i] - mean) * rstd * w[i] + b[i];
+        if constexpr (sizeof(TY) == 2) y[(size_t)t * d + i] = __float2half_rn(v);
+        else y[(size_t)t * d + i] = v;
+    }
 }
 
 void launch_layernorm_rows(const float *x, const float *w, const float *b, int rows, int d,
                            float *y, cudaStream_t st) {
-    layernorm_rows_kernel<<<rows, 256, 0, st>>>(x, w, b, d, y);
+    layernorm_rows_kernel<float><<<rows, 256, 0, st>>>(x, w, b, d, y);
+}
+void launch_layernorm_rows_h(const float *x, const float *w, const float *b, int rows, int d,
+                             __half *y, cudaStream_t st) {
+    layernorm_rows_kernel<__half><<<rows, 256, 0, st>>>(x, w, b, d, y);
 }
 
 // ---------------------------------------------------------------------------
@@ -109,7 +117,12 @@ __global__ void __launch_bounds__(256) gemm_q8_kernel(GemmParams p) {
 #pragma unroll
             for (int j = 0; j < 16; j += 4) {
                 float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (tt < p.T) v = *reinterpret_cast<const float4 *>(p.x + (size_t)tt * K + k0 + kq + j);
+                if (tt < p.T) {
+                    const uint2 h = *reinterpret_cast<const uint2 *>(p.x + (size_t)tt * K + k0 + kq + j);
+                    const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&h.x));
+                    const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&h.y));
+                    v = make_float4(a.x, a.y, b.x, b.y);
+                }
                 Xs[kq + j][t] = v.x;
                 Xs[kq + j + 1][t] = v.y;
                 Xs[kq + j + 2][t] = v.z;
@@ -161,7 +174,7 @@ __global__ void __launch_bounds__(256) gemm_q8_kernel(GemmParams p) {
         for (int j = 0; j < 4; ++j) {
             const int o = o0 + tx * 4 + j;
             if (o >= OUT) continue;
-            gemm_store<EPI>(p, t, o, acc[i][j] + p.W.bias[o]);
+            gemm_store<EPI>(p, t, o, acc[i][j] + p.W.bias[o], qkv_dest(p, t));
         }
     }
 }
@@ -170,13 +183,13 @@ __global__ void __launch_bounds__(256) gemm_q8_kernel(GemmParams p) {
 // less of a 128-row MMA tile).
 constexpr int kGemmTcMinRows = 16;
 
-void launch_gemm(int epi, const MkLin &W, const float *x, float *y, int T, const DecodeView *dv,
+void launch_gemm(int epi, const MkLin &W, const __half *x, void *y, int T, const DecodeView *dv,
                  __half *k_cache, __half *v_cache, int kv_slot, int n_slots, int n_heads,
                  int max_seq, int layer, int d, cudaStream_t st) {
     GemmParams p{};
     p.W = W;
     p.x = x;
-    p.y = y;
+    p.y = static_cast<float *>(y);
     p.T = T;
     p.k_cache = k_cache;
     p.v_cache = v_cache;
@@ -190,10 +203,7 @@ void launch_gemm(int epi, const MkLin &W, const float *x, float *y, int T, const
         p.slots = dv->slots;
         p.batch_slot = dv->batch_slot;
     }
-    if (T >= kGemmTcMinRows) {
-        launch_gemm_tc(epi, p, st);
-        return;
-    }
+    if (T >= kGemmTcMinRows && launch_gemm_tc(epi, p, st)) return;
     dim3 grid((W.out + 63) / 64, (T + 63) / 64);
     switch (epi) {
     case EPI_PLAIN: gemm_q8_kernel<EPI_PLAIN><<<grid, 256, 0, st>>>(p); break;
@@ -209,7 +219,7 @@ void launch_gemm(int epi, const MkLin &W, const float *x, float *y, int T, const
 // QKV output); online softmax.  Query t sees keys 0..t.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(64) attn_prefill_kernel(const float *qkv, int T, int d,
-                                                          float *out) {
+                                                          __half *out) {
     __shared__ float Ks[64][65];
     __shared__ float Vs[64][65];
     const int h = blockIdx.y, q0 = blockIdx.x * 64, t = q0 + threadIdx.x;
@@ -250,7 +260,7 @@ __global__ void __launch_bounds__(64) attn_prefill_kernel(const float *qkv, int 
     if (t < T) {
         const float inv = 1.0f / l;
 #pragma unroll
-        for (int e = 0; e < 64; ++e) out[(size_t)t * d + h * 64 + e] = acc[e] * inv;
+        for (int e = 0; e < 64; ++e) out[(size_t)t * d + h * 64 + e] = __float2half_rn(acc[e] * inv);
     }
 }
 
@@ -330,8 +340,10 @@ void prefill_forward(const ModelView &m, const DecodeView &dv, int slot, int T, 
     int map_done = 0;
     for (int l = 0; l < m.n_layers; ++l) {
         const MkLayer &L = m.layers[l];
-        launch_layernorm_rows(pb.x, L.ln1_w, L.ln1_b, T, d, pb.n, st);
-        launch_gemm(EPI_QKV, L.qkv, pb.n, pb.qkv, T, nullptr, dv.k_cache, dv.v_cache, slot,
+        __half *n16 = reinterpret_cast<__half *>(pb.n), *attn16 = reinterpret_cast<__half *>(pb.attn),
+               *u16 = reinterpret_cast<__half *>(pb.u);
+        launch_layernorm_rows_h(pb.x, L.ln1_w, L.ln1_b, T, d, n16, st);
+        launch_gemm(EPI_QKV, L.qkv, n16, pb.qkv, T, nullptr, dv.k_cache, dv.v_cache, slot,
                     dv.n_slots, dv.n_heads, dv.max_seq, l, d, st);
         if (hk && hk->maps && (l == hk->map_layers[0] || l == hk->map_layers[1])) {
             const int rows = T - hk->map_q0;
@@ -339,20 +351,20 @@ void prefill_forward(const ModelView &m, const DecodeView &dv, int slot, int T, 
                 pb.qkv, T, d, hk->map_head, hk->map_q0, hk->map_k0, hk->map_k1, hk->maps, map_done++ > 0);
         }
         if (hk && l == hk->stop_layer) return;
-        attn_prefill_kernel<<<dim3((T + 63) / 64, m.n_heads), 64, 0, st>>>(pb.qkv, T, d, pb.attn);
-        launch_gemm(EPI_RESID, L.proj, pb.attn, pb.x, T, nullptr, nullptr, nullptr, -1, 0, 0, 0, l,
+        attn_prefill_kernel<<<dim3((T + 63) / 64, m.n_heads), 64, 0, st>>>(pb.qkv, T, d, attn16);
+        launch_gemm(EPI_RESID, L.proj, attn16, pb.x, T, nullptr, nullptr, nullptr, -1, 0, 0, 0, l,
                     d, st);
-        launch_layernorm_rows(pb.x, L.ln2_w, L.ln2_b, T, d, pb.n, st);
-        launch_gemm(EPI_GELU, L.fc, pb.n, pb.u, T, nullptr, nullptr, nullptr, -1, 0, 0, 0, l, d, st);
-        launch_gemm(EPI_RESID, L.mlp, pb.u, pb.x, T, nullptr, nullptr, nullptr, -1, 0, 0, 0, l, d,
+        launch_layernorm_rows_h(pb.x, L.ln2_w, L.ln2_b, T, d, n16, st);
+        launch_gemm(EPI_GELU, L.fc, n16, pb.u, T, nullptr, nullptr, nullptr, -1, 0, 0, 0, l, d, st);
+        launch_gemm(EPI_RESID, L.mlp, u16, pb.x, T, nullptr, nullptr, nullptr, -1, 0, 0, 0, l, d,
                     st);
     }
     if (hk && hk->lp_q0 >= 0) {
         // every row from lp_q0: ln_f, final_norm, mel_head, log_softmax at its target
         const int rows = T - hk->lp_q0;
         launch_layernorm_rows(pb.x + (size_t)hk->lp_q0 * d, m.ln_f_w, m.ln_f_b, rows, d, pb.n, st);
-        launch_layernorm_rows(pb.n, m.final_w, m.final_b, rows, d, pb.attn, st);
-        launch_gemm(EPI_PLAIN, m.mel_head, pb.attn, hk->lp_logits, rows, nullptr, nullptr, nullptr, -1, 0, 0, 0,
+        launch_layernorm_rows_h(pb.n, m.final_w, m.final_b, rows, d, reinterpret_cast<__half *>(pb.attn), st);
+        launch_gemm(EPI_PLAIN, m.mel_head, reinterpret_cast<const __half *>(pb.attn), hk->lp_logits, rows, nullptr, nullptr, nullptr, -1, 0, 0, 0,
                     0, d, st);
         log_softmax_pick_kernel<<<rows, 256, 0, st>>>(hk->lp_logits, m.mel_vocab, hk->lp_targets, hk->lp_out);
         return;
@@ -360,8 +372,9 @@ void prefill_forward(const ModelView &m, const DecodeView &dv, int slot, int T, 
     // ln_f then final_norm on the last row, then mel_head (gpt.rs:673-692)
     const float *last = pb.x + (size_t)(T - 1) * d;
     launch_layernorm_rows(last, m.ln_f_w, m.ln_f_b, 1, d, pb.n, st);
-    launch_layernorm_rows(pb.n, m.final_w, m.final_b, 1, d, pb.n + d, st);
-    launch_gemm(EPI_PLAIN, m.mel_head, pb.n + d, logits_row, 1, nullptr, nullptr, nullptr, -1, 0, 0,
+    __half *fin16 = reinterpret_cast<__half *>(pb.n + d);
+    launch_layernorm_rows_h(pb.n, m.final_w, m.final_b, 1, d, fin16, st);
+    launch_gemm(EPI_PLAIN, m.mel_head, fin16, logits_row, 1, nullptr, nullptr, nullptr, -1, 0, 0,
                 0, 0, d, st);
 }
 
