@@ -148,6 +148,14 @@ int itts_gpt_prefill(itts_gpt *gpt, itts_kv *kv, int32_t slot, const int32_t *te
                      int32_t n_text, const float *conds, int32_t n_conds, int32_t lang_id,
                      const int32_t *prior_codes, int32_t n_prior, float *logits_out);
 
+/* Gpt::prefill_after (gpt.rs:655-696) for n requests at once: request r resets slot r
+ * and is prefilled from prompts[r] (text, conds, lang, prior codes; min_codes unused),
+ * all n in one packed forward (every linear runs once over all positions).  logits_out
+ * is [n, mel_vocab] (may be NULL).  The reference prefills one request per call; this
+ * entry point gives the same logits and cache contents as n itts_gpt_prefill calls. */
+int itts_gpt_prefill_batch(itts_gpt *gpt, itts_kv *kv, int32_t n, const itts_code_prompt *prompts,
+                           float *logits_out);
+
 /* Gpt::step (gpt.rs:706-754), batched: for i in 0..n, feeds mel token toks[i] at mel
  * position pos[i] into slot slots[i] (slots distinct), appending one KV position each.
  * logits_out is [n, mel_vocab] (may be NULL). */

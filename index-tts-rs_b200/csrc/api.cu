@@ -100,7 +100,23 @@ struct itts_kv {
     std::vector<cudaGraph_t> graph_defs;
     std::vector<char> graph_failed;       // capture unsupported: launch directly
     size_t ll_bytes = 0;
+    // packed prefill of several requests (grown on demand)
+    PrefillBatch pbb{};
+    int *d_text_b = nullptr, *d_prior_b = nullptr;
+    float *d_conds_b = nullptr;
+    size_t cap_text_b = 0, cap_prior_b = 0, cap_conds_b = 0;
 };
+
+static void free_prefill_batch(itts_kv *kv) {
+    void *dev[] = {kv->pbb.x, kv->pbb.n, kv->pbb.qkv, kv->pbb.attn, kv->pbb.u, kv->pbb.row_slot,
+                   kv->pbb.row_pos, kv->pbb.tiles, kv->pbb.last_row, kv->d_text_b, kv->d_prior_b,
+                   kv->d_conds_b};
+    for (void *p : dev) cudaFree(p);
+    kv->pbb = PrefillBatch{};
+    kv->d_text_b = kv->d_prior_b = nullptr;
+    kv->d_conds_b = nullptr;
+    kv->cap_text_b = kv->cap_prior_b = kv->cap_conds_b = 0;
+}
 
 // ------------------------------------------------------------------------------
 // errors, params, host-side sampler helpers
@@ -587,6 +603,7 @@ static void kv_destroy(itts_kv *kv) {
                    kv->pb.x, kv->pb.n, kv->pb.qkv, kv->pb.attn,
                    kv->pb.u, kv->d_codes, kv->d_text, kv->d_prior, kv->d_conds};
     for (void *p : dev) cudaFree(p);
+    free_prefill_batch(kv);
     cudaFreeHost(kv->h_pinned);
     cudaFreeHost(kv->h_i32);
     cudaFreeHost(kv->h_f32);
@@ -824,6 +841,105 @@ static int prefill_impl(itts_gpt *g, itts_kv *kv, int slot, const int32_t *text,
     return ITTS_OK;
 }
 
+// Prefill of n requests into their slots in one packed forward (prefill_batch.cu): the
+// same results as n calls of prefill_impl, with every linear run once over all positions.
+// Prompts must have been validated (Ts[r] = positions of request r).
+static int prefill_batch_impl(itts_gpt *g, itts_kv *kv, int n, const int *slots, const itts_code_prompt *prompts,
+                              const int *Ts, float *d_logits) {
+    const ModelView &m = g->m;
+    cudaStream_t st = g->stream;
+    size_t total = 0, n_tiles = 0, n_text = 0, n_prior = 0, n_conds = 0;
+    for (int r = 0; r < n; ++r) {
+        total += Ts[r];
+        n_tiles += (Ts[r] + 63) / 64;
+        n_text += prompts[r].n_text + 2;
+        n_prior += prompts[r].n_prior;
+        n_conds += (size_t)prompts[r].n_conds * m.d;
+    }
+    CUDA_TRY(cudaStreamSynchronize(st));  // the scratch may be reallocated
+    PrefillBatch &pb = kv->pbb;
+    if (total > pb.cap_rows || n_tiles > pb.cap_tiles || (size_t)n > pb.cap_req || n_text > kv->cap_text_b ||
+        n_prior > kv->cap_prior_b || n_conds > kv->cap_conds_b) {
+        const size_t rows = std::max(total, pb.cap_rows), tiles = std::max(n_tiles, pb.cap_tiles);
+        const size_t req = std::max((size_t)n, pb.cap_req), nt = std::max(n_text, kv->cap_text_b);
+        const size_t np = std::max(n_prior, kv->cap_prior_b) + 1, nc = std::max(n_conds, kv->cap_conds_b);
+        free_prefill_batch(kv);
+        cudaError_t e = cudaSuccess;
+        auto A = [&](void **p, size_t bytes) { if (e == cudaSuccess) e = cudaMalloc(p, bytes); };
+        const size_t qrows = std::max(rows, req);
+        A((void **)&pb.x, sizeof(float) * rows * m.d);
+        A((void **)&pb.n, sizeof(float) * qrows * m.d);
+        A((void **)&pb.qkv, sizeof(float) * qrows * 3 * m.d);
+        A((void **)&pb.attn, sizeof(float) * qrows * m.d);
+        A((void **)&pb.u, sizeof(float) * rows * m.ff);
+        A((void **)&pb.row_slot, sizeof(int) * rows);
+        A((void **)&pb.row_pos, sizeof(int) * rows);
+        A((void **)&pb.tiles, sizeof(AttnTile) * tiles);
+        A((void **)&pb.last_row, sizeof(int) * req);
+        A((void **)&kv->d_text_b, sizeof(int) * nt);
+        A((void **)&kv->d_prior_b, sizeof(int) * np);
+        A((void **)&kv->d_conds_b, sizeof(float) * nc);
+        if (e != cudaSuccess) {
+            free_prefill_batch(kv);
+            cudaGetLastError();
+            return set_err(ITTS_E_CUDA, std::string("device error: batched prefill scratch: ") + cudaGetErrorString(e));
+        }
+        pb.cap_rows = rows;
+        pb.cap_tiles = tiles;
+        pb.cap_req = req;
+        kv->cap_text_b = nt;
+        kv->cap_prior_b = np;
+        kv->cap_conds_b = nc;
+    }
+    // host tables: tokens (START, text, STOP), prior codes, conds, row destinations, tiles
+    std::vector<int> text(n_text), prior(n_prior + 1), row_slot(total), row_pos(total), last(n);
+    std::vector<float> conds(n_conds);
+    std::vector<AttnTile> tiles;
+    tiles.reserve(n_tiles);
+    size_t ot = 0, op = 0, oc = 0, row = 0;
+    for (int r = 0; r < n; ++r) {
+        const itts_code_prompt &pr = prompts[r];
+        text[ot] = kStartText;
+        for (int i = 0; i < pr.n_text; ++i) text[ot + 1 + i] = pr.text_tokens[i];
+        text[ot + pr.n_text + 1] = kStopText;
+        for (int i = 0; i < pr.n_prior; ++i) prior[op + i] = pr.prior_codes[i];
+        std::memcpy(conds.data() + oc, pr.conds, sizeof(float) * pr.n_conds * m.d);
+        for (int t = 0; t < Ts[r]; ++t) {
+            row_slot[row + t] = slots[r];
+            row_pos[row + t] = t;
+        }
+        for (int q0 = 0; q0 < Ts[r]; q0 += 64) tiles.push_back(AttnTile{(int)row, q0, Ts[r], slots[r]});
+        last[r] = (int)(row + Ts[r] - 1);
+        ot += pr.n_text + 2;
+        op += pr.n_prior;
+        oc += (size_t)pr.n_conds * m.d;
+        row += Ts[r];
+    }
+    CUDA_TRY(cudaMemcpy(kv->d_text_b, text.data(), sizeof(int) * n_text, cudaMemcpyHostToDevice));
+    if (n_prior) CUDA_TRY(cudaMemcpy(kv->d_prior_b, prior.data(), sizeof(int) * n_prior, cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemcpy(kv->d_conds_b, conds.data(), sizeof(float) * n_conds, cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemcpy(pb.row_slot, row_slot.data(), sizeof(int) * total, cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemcpy(pb.row_pos, row_pos.data(), sizeof(int) * total, cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemcpy(pb.tiles, tiles.data(), sizeof(AttnTile) * tiles.size(), cudaMemcpyHostToDevice));
+    CUDA_TRY(cudaMemcpy(pb.last_row, last.data(), sizeof(int) * n, cudaMemcpyHostToDevice));
+    pb.n_tiles = (int)tiles.size();
+    ot = op = oc = row = 0;
+    for (int r = 0; r < n; ++r) {  // embeddings (gpt.rs:535-627), each request at its rows
+        const itts_code_prompt &pr = prompts[r];
+        launch_embed_prefix(m, kv->d_text_b + ot, pr.n_text + 2, kv->d_conds_b + oc, pr.n_conds, pr.lang_id,
+                            kv->d_prior_b + op, pr.n_prior, pb.x + row * m.d, st);
+        ot += pr.n_text + 2;
+        op += pr.n_prior;
+        oc += (size_t)pr.n_conds * m.d;
+        row += Ts[r];
+    }
+    DecodeView dv = decode_view(kv, 1);
+    prefill_batch_forward(m, dv, pb, n, (int)total, d_logits, st);
+    CUDA_TRY(cudaGetLastError());
+    for (int r = 0; r < n; ++r) kv->h_state[slots[r]].valid_len = Ts[r];
+    return ITTS_OK;
+}
+
 extern "C" int itts_gpt_prefill(itts_gpt *g, itts_kv *kv, int32_t slot, const int32_t *text,
                                 int32_t n_text, const float *conds, int32_t n_conds, int32_t lang,
                                 const int32_t *prior, int32_t n_prior, float *logits_out) {
@@ -837,6 +953,29 @@ extern "C" int itts_gpt_prefill(itts_gpt *g, itts_kv *kv, int32_t slot, const in
     if (logits_out)
         CUDA_TRY(cudaMemcpyAsync(logits_out, kv->db.logits + (size_t)slot * g->m.mel_vocab,
                                  sizeof(float) * g->m.mel_vocab, cudaMemcpyDeviceToHost, g->stream));
+    CUDA_TRY(cudaStreamSynchronize(g->stream));
+    return ITTS_OK;
+}
+
+extern "C" int itts_gpt_prefill_batch(itts_gpt *g, itts_kv *kv, int32_t n, const itts_code_prompt *prompts,
+                                      float *logits_out) {
+    if (!g || !kv || kv->gpt != g) return validation("gpt", "null pointer or cache of another model");
+    if (n <= 0 || n > kv->max_batch || !prompts) return validation("n", "batch size out of range");
+    const ModelView &m = g->m;
+    std::vector<int> Ts(n), slots(n);
+    for (int r = 0; r < n; ++r) {
+        const itts_code_prompt &pr = prompts[r];
+        TRY(validate_prompt(m, pr.text_tokens, pr.n_text, pr.conds, pr.n_conds, pr.lang_id, pr.prior_codes,
+                            pr.n_prior, kv->max_seq, &Ts[r]));
+        slots[r] = r;
+    }
+    CUDA_TRY(cudaSetDevice(g->device));
+    for (int r = 0; r < n; ++r) kv->h_state[r].valid_len = 0;  // cache.reset() (gpt.rs:664)
+    TRY(prefill_batch_impl(g, kv, n, slots.data(), prompts, Ts.data(), kv->db.logits));
+    TRY(push_slots(kv, slots.data(), n));
+    if (logits_out)
+        CUDA_TRY(cudaMemcpyAsync(logits_out, kv->db.logits, sizeof(float) * n * m.mel_vocab, cudaMemcpyDeviceToHost,
+                                 g->stream));
     CUDA_TRY(cudaStreamSynchronize(g->stream));
     return ITTS_OK;
 }
@@ -1128,11 +1267,13 @@ static int generate_impl(itts_gpt *g, itts_kv *kv, int n, const int *slots,
     CUDA_TRY(cudaSetDevice(g->device));
     cudaStream_t st = g->stream;
     CUDA_TRY(cudaEventRecord(g->ev[0], st));
-    for (int r = 0; r < n; ++r) {
-        const itts_code_prompt &pr = prompts[r];
-        kv->h_state[slots[r]].valid_len = 0;
-        TRY(prefill_impl(g, kv, slots[r], pr.text_tokens, pr.n_text, pr.conds, pr.n_conds,
-                         pr.lang_id, pr.prior_codes, pr.n_prior, kv->db.logits + (size_t)r * m.mel_vocab));
+    for (int r = 0; r < n; ++r) kv->h_state[slots[r]].valid_len = 0;
+    if (n > 1) {  // one packed prefill of all requests
+        TRY(prefill_batch_impl(g, kv, n, slots, prompts, Ts.data(), kv->db.logits));
+    } else {
+        const itts_code_prompt &pr = prompts[0];
+        TRY(prefill_impl(g, kv, slots[0], pr.text_tokens, pr.n_text, pr.conds, pr.n_conds,
+                         pr.lang_id, pr.prior_codes, pr.n_prior, kv->db.logits));
     }
     CUDA_TRY(cudaEventRecord(g->ev[1], st));
     for (int r = 0; r < n; ++r) {

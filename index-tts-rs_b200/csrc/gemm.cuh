@@ -15,18 +15,25 @@ struct GemmParams {
     __half *k_cache, *v_cache;
     const SlotState *slots;
     const int *batch_slot;
+    // packed prefill of several requests: row t's K/V go to (row_slot[t], row_pos[t])
+    const int *row_slot, *row_pos;
     int kv_slot, n_slots, n_heads, max_seq, layer, d;
 };
 
-// Where row t's new K/V go (EPI_QKV): position t of kv_slot in prefill; the valid_len of
-// slot batch_slot[t] in decode, unless that slot is inactive or full.
+// Where row t's new K/V go (EPI_QKV): position t of kv_slot in prefill; (row_slot[t],
+// row_pos[t]) in a packed prefill of several requests; the valid_len of slot
+// batch_slot[t] in decode, unless that slot is inactive or full.
 struct QkvDest {
     int slot, pos;
     bool write;
 };
 __device__ __forceinline__ QkvDest qkv_dest(const GemmParams &p, int t) {
     QkvDest q{p.kv_slot, t, t < p.max_seq};
-    if (p.slots) {
+    if (p.row_slot) {
+        q.slot = p.row_slot[t];
+        q.pos = p.row_pos[t];
+        q.write = q.pos < p.max_seq;
+    } else if (p.slots) {
         q.slot = p.batch_slot[t];
         const SlotState &st = p.slots[q.slot];
         q.pos = st.valid_len;

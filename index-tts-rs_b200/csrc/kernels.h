@@ -46,6 +46,24 @@ struct PrefillBufs {
     int max_tokens;
 };
 
+// One 64-query tile of the packed prefill attention.
+struct AttnTile {
+    int row0;  // the request's first row in the packed buffers
+    int q0;    // first query (position) of the tile
+    int T;     // the request's positions
+    int slot;  // its KV-cache slot
+};
+
+// Scratch of a packed prefill of several requests (rows = all their positions).
+struct PrefillBatch {
+    float *x = nullptr, *n = nullptr, *qkv = nullptr, *attn = nullptr, *u = nullptr;
+    int *row_slot = nullptr, *row_pos = nullptr;  // [rows] KV destination of each row
+    AttnTile *tiles = nullptr;                     // [n_tiles]
+    int *last_row = nullptr;                       // [requests] row of each request's last position
+    int n_tiles = 0;
+    size_t cap_rows = 0, cap_tiles = 0, cap_req = 0;
+};
+
 void kernels_init();  // one-time function attributes (dynamic shared memory)
 
 void launch_embed_step(const ModelView &m, const DecodeView &dv, float *x, cudaStream_t st);
@@ -91,6 +109,16 @@ struct PrefillHooks {
 // for per-row log-probabilities instead).
 void prefill_forward(const ModelView &m, const DecodeView &dv, int slot, int T, PrefillBufs &pb,
                      float *logits_row, cudaStream_t st, const PrefillHooks *hk = nullptr);
+
+// Packed prefill of n_req requests (pb filled: rows, tables; pb.x embedded): all layers,
+// each row's K/V into its request's slot, logits of request r into row r of `logits`.
+void prefill_batch_forward(const ModelView &m, const DecodeView &dv, const PrefillBatch &pb, int n_req,
+                           int total, float *logits, cudaStream_t st);
+// launch_gemm for a packed prefill: the QKV epilogue writes row t's K/V to
+// (row_slot[t], row_pos[t]).
+void launch_gemm_rows(int epi, const MkLin &W, const __half *x, void *y, int T, const int *row_slot,
+                      const int *row_pos, __half *k_cache, __half *v_cache, int n_slots, int n_heads,
+                      int max_seq, int layer, int d, cudaStream_t st);
 
 void launch_embed_prefix(const ModelView &m, const int *full_text, int n_full, const float *conds,
                          int n_conds, int lang, const int *prior, int n_prior, float *x,

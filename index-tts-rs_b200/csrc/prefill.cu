@@ -213,6 +213,34 @@ void launch_gemm(int epi, const MkLin &W, const __half *x, void *y, int T, const
     }
 }
 
+void launch_gemm_rows(int epi, const MkLin &W, const __half *x, void *y, int T, const int *row_slot,
+                      const int *row_pos, __half *k_cache, __half *v_cache, int n_slots, int n_heads,
+                      int max_seq, int layer, int d, cudaStream_t st) {
+    GemmParams p{};
+    p.W = W;
+    p.x = x;
+    p.y = static_cast<float *>(y);
+    p.T = T;
+    p.k_cache = k_cache;
+    p.v_cache = v_cache;
+    p.row_slot = row_slot;
+    p.row_pos = row_pos;
+    p.kv_slot = -1;
+    p.n_slots = n_slots;
+    p.n_heads = n_heads;
+    p.max_seq = max_seq;
+    p.layer = layer;
+    p.d = d;
+    if (T >= kGemmTcMinRows && launch_gemm_tc(epi, p, st)) return;
+    dim3 grid((W.out + 63) / 64, (T + 63) / 64);
+    switch (epi) {
+    case EPI_PLAIN: gemm_q8_kernel<EPI_PLAIN><<<grid, 256, 0, st>>>(p); break;
+    case EPI_GELU: gemm_q8_kernel<EPI_GELU><<<grid, 256, 0, st>>>(p); break;
+    case EPI_RESID: gemm_q8_kernel<EPI_RESID><<<grid, 256, 0, st>>>(p); break;
+    default: gemm_q8_kernel<EPI_QKV><<<grid, 256, 0, st>>>(p); break;
+    }
+}
+
 // ---------------------------------------------------------------------------
 // Causal attention over the prompt: one thread per query, 64 queries x one head
 // per CTA; K/V tiles of 64 positions staged in shared memory (fp32, from the

@@ -381,6 +381,17 @@ def _prompt_c(gpt: Gpt, pr: CodePrompt, keep: list) -> CodePromptC:
                        int(pr.min_codes))
 
 
+def prefill_batch(gpt: Gpt, prompts: Sequence[CodePrompt], cache: KvCache) -> np.ndarray:
+    """Gpt::prefill_after for several requests in one packed forward: request r resets and
+    fills slot r; returns the [n, mel_vocab] logits of each request's last position."""
+    n = len(prompts)
+    keep: list = []
+    pcs = (CodePromptC * n)(*[_prompt_c(gpt, pr, keep) for pr in prompts])
+    out = np.empty((n, gpt.mel_vocab), np.float32)
+    _check(load_lib().itts_gpt_prefill_batch(gpt._h, cache._h, n, pcs, _ptr(out)))
+    return out
+
+
 def generate_codes(gpt: Gpt, text_tokens, conds, lang_id: int, cache: KvCache,
                    params: SamplingParams, rng: SamplerRng, slot: int = 0) -> list[int]:
     return generate_codes_after(gpt, CodePrompt(text_tokens, conds, lang_id), cache, params, rng,

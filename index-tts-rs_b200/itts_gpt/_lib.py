@@ -75,6 +75,7 @@ SIGNATURES = [
     ("itts_generate_codes_after", C.c_int,
      [_P, _P, _I32, C.POINTER(CodePromptC), C.POINTER(SamplingParamsC), C.POINTER(C.c_uint64),
       _P, _I32, C.POINTER(_I32)]),
+    ("itts_gpt_prefill_batch", C.c_int, [_P, _P, _I32, C.POINTER(CodePromptC), _P]),
     ("itts_generate_batch", C.c_int,
      [_P, _P, _I32, C.POINTER(CodePromptC), C.POINTER(SamplingParamsC), _P, _P, _I32, _P]),
     ("itts_gpt_last_timing", C.c_int,

@@ -221,6 +221,31 @@ def test_generate_batch_matches_checker(small, small_cfg, n_req):
         assert rb[i].state == st
 
 
+def _batch_prompts(cfg, lens, seed0=0):
+    return [ig.CodePrompt(make_text(n, cfg.text_vocab, seed=seed0 + n),
+                          make_conds(cfg.d, 3 if i % 2 else 32, seed=seed0 + i), 1 + i % 3,
+                          prior_codes=[7, 8190, 2, 511][: i % 4] if i % 3 == 2 else ())
+            for i, n in enumerate(lens)]
+
+
+def test_prefill_batch_matches_checker(small, small_cfg):
+    """Packed prefill of ragged requests (tensor-core GEMMs over all positions, flash
+    attention per request): every request's logits and KV cache equal a prefill of its
+    own (the checker), and a decode step after it matches too."""
+    gpt, om = small
+    lens = [1, 29, 64, 7, 100, 33]
+    prompts = _batch_prompts(small_cfg, lens)
+    kv = ig.KvCache(gpt, max_seq=512, max_batch=len(lens))
+    got = ig.prefill_batch(gpt, prompts, kv)
+    for r, pr in enumerate(prompts):
+        okv = om.kv(512)
+        ref = om.prefill(okv, pr.text_tokens, pr.conds, pr.lang_id, list(pr.prior_codes))
+        check_logits(got[r], ref, f"packed prefill request {r}")
+        assert kv.valid_len(r) == okv.valid_len()
+        step = gpt.step(kv, 4000 + r, len(pr.prior_codes) + 2, slot=r)
+        check_logits(step, om.step(okv, 4000 + r, len(pr.prior_codes) + 2), f"step after request {r}")
+
+
 def test_load_from_path_and_f32_scales(tmp_path, small_cfg, small_weights):
     path = tmp_path / "gpt_int8.safetensors"
     save_safetensors(str(path), small_weights)
@@ -293,6 +318,21 @@ def test_full_size_teacher_forced(full):
     agree = np.mean(np.argmax(g, 1) == np.argmax(r, 1))
     assert agree >= 0.99, agree
     print(f"full-size teacher-forced: max |dlogit| {max(errs):.2e}, argmax agreement {agree:.3f}")
+
+
+def test_full_size_prefill_batch(full):
+    """Full-size packed prefill (prompts of 99, 163 and 226 positions: the 64-position
+    attention tiles end inside and at the edge of a prompt) against the checker."""
+    cfg, gpt, om = full
+    prompts = [ig.CodePrompt(make_text(n, cfg.text_vocab, seed=n), make_conds(cfg.d, 32, seed=n + 1), 1)
+               for n in (64, 128, 191)]
+    kv = ig.KvCache(gpt, max_seq=512, max_batch=3)
+    got = ig.prefill_batch(gpt, prompts, kv)
+    for r, pr in enumerate(prompts):
+        ref = om.prefill(om.kv(512), pr.text_tokens, pr.conds, pr.lang_id)
+        err = check_logits(got[r], ref, f"full-size packed prefill {r}")
+        assert np.argmax(got[r]) == np.argmax(ref)
+        print(f"full-size packed prefill T={kv.valid_len(r)}: max |dlogit| {err:.2e}")
 
 
 def test_full_size_greedy_generate(full):
