@@ -338,6 +338,29 @@ def run_profile_prefill(args):
                       "repeats": args.profile_prefill, "last_wall_ms": 1000.0 * dt}), flush=True)
 
 
+def run_profile_prefill_batch(args):
+    """A case for profilers: the cfg4 prefill, N_REQ prompts of 32 conditioning latents +
+    600 text tokens (635 positions each) in one packed prefill, run twice."""
+    import itts_gpt as ig
+    import torch
+    cfg, w = make_model()
+    gpt = ig.Gpt.from_weights(w)
+    n = args.profile_prefill_batch
+    prompts = []
+    for r in range(n):
+        text, conds = make_prompt(cfg, r)
+        prompts.append(ig.CodePrompt(text, conds, LANG))
+    kv = ig.KvCache(gpt, max_seq=N_CONDS + N_TEXT + 3 + 8, max_batch=n)
+    for i in range(2):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        ig.prefill_batch(gpt, prompts, kv)
+        torch.cuda.synchronize()
+        dt = time.perf_counter() - t0
+    print(json.dumps({"profile_case": "cfg4 packed prefill", "requests": n,
+                      "positions": n * (N_CONDS + N_TEXT + 3), "last_wall_ms": 1000.0 * dt}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -350,12 +373,17 @@ def main():
     ap.add_argument("--profile-iters", type=int, default=2)
     ap.add_argument("--profile-prefill", type=int, default=0, metavar="REPEATS",
                     help="profiler case: only cfg2 prefills, this many")
+    ap.add_argument("--profile-prefill-batch", type=int, default=0, metavar="N_REQ",
+                    help="profiler case: the cfg4 packed prefill of N_REQ prompts, twice")
     args = ap.parse_args()
     if args.profile_decode > 0:
         run_profile_case(args)
         return
     if args.profile_prefill > 0:
         run_profile_prefill(args)
+        return
+    if args.profile_prefill_batch > 0:
+        run_profile_prefill_batch(args)
         return
     rank, world, local_rank = dist_env()
     if world > 1:

@@ -67,6 +67,8 @@ struct itts_gpt {
     std::vector<MkLayer> layers;
     MkLayer *d_layers = nullptr;
     void *arena = nullptr;
+    __half *w16_arena = nullptr;  // fp16 copies of the layer weights (long prefills), made once
+    bool w16_tried = false;
     cudaStream_t stream = nullptr;
     cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
     float last_prefill_ms = 0.f, last_decode_ms = 0.f;
@@ -216,6 +218,7 @@ static void gpt_destroy(itts_gpt *g) {
     for (auto &e : g->ev)
         if (e) cudaEventDestroy(e);
     cudaFree(g->arena);
+    cudaFree(g->w16_arena);
     cudaFree(g->d_layers);
     cudaFree(g->d_sstate);
     cudaFree(g->d_slogits);
@@ -811,6 +814,41 @@ static int validate_prompt(const ModelView &m, const int32_t *text, int n_text, 
     return ITTS_OK;
 }
 
+// fp16 copies of the four linears of every layer (not the head, which only ever sees a
+// few rows), made once, on the first prefill long enough to use them: a long prompt's
+// GEMMs then stream fp16 weights by TMA instead of dequantizing int8 tiles in every CTA.
+// They take 2 bytes per weight (0.94 GB for the IndexTTS-2.5 decoder); without memory for
+// them the int8 GEMMs run instead.
+static void ensure_weights_f16(itts_gpt *g) {
+    if (g->w16_tried) return;
+    g->w16_tried = true;
+    size_t total = 0;
+    for (const MkLayer &L : g->layers)
+        for (const MkLin *W : {&L.qkv, &L.proj, &L.fc, &L.mlp}) total += (size_t)W->out * W->in;
+    __half *a = nullptr;
+    if (cudaMalloc(&a, total * sizeof(__half)) != cudaSuccess) {
+        cudaGetLastError();
+        return;
+    }
+    size_t off = 0;
+    cudaError_t e = cudaSuccess;
+    for (MkLayer &L : g->layers)
+        for (MkLin *W : {&L.qkv, &L.proj, &L.fc, &L.mlp}) {
+            if (e == cudaSuccess) e = make_weights_f16(*W, a + off, g->stream);
+            W->w16 = a + off;
+            off += (size_t)W->out * W->in;
+        }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(g->stream);
+    if (e != cudaSuccess) {  // keep the int8 path
+        cudaGetLastError();
+        for (MkLayer &L : g->layers)
+            for (MkLin *W : {&L.qkv, &L.proj, &L.fc, &L.mlp}) W->w16 = nullptr;
+        cudaFree(a);
+        return;
+    }
+    g->w16_arena = a;
+}
+
 static int prefill_impl(itts_gpt *g, itts_kv *kv, int slot, const int32_t *text, int n_text,
                         const float *conds, int n_conds, int lang, const int32_t *prior,
                         int n_prior, float *d_logits_row, const PrefillHooks *hooks = nullptr) {
@@ -832,6 +870,7 @@ static int prefill_impl(itts_gpt *g, itts_kv *kv, int slot, const int32_t *text,
     if (n_prior)
         CUDA_TRY(cudaMemcpyAsync(kv->d_prior, hp, sizeof(int) * n_prior, cudaMemcpyHostToDevice, st));
     CUDA_TRY(cudaMemcpyAsync(kv->d_conds, kv->h_f32, nc * sizeof(float), cudaMemcpyHostToDevice, st));
+    if (T >= kGemmF16MinRows) ensure_weights_f16(g);
     launch_embed_prefix(m, kv->d_text, n_text + 2, kv->d_conds, n_conds, lang, kv->d_prior, n_prior,
                         kv->pb.x, st);
     DecodeView dv = decode_view(kv, 1);
@@ -857,6 +896,7 @@ static int prefill_batch_impl(itts_gpt *g, itts_kv *kv, int n, const int *slots,
         n_conds += (size_t)prompts[r].n_conds * m.d;
     }
     CUDA_TRY(cudaStreamSynchronize(st));  // the scratch may be reallocated
+    if (total >= (size_t)kGemmF16MinRows) ensure_weights_f16(g);
     PrefillBatch &pb = kv->pbb;
     if (total > pb.cap_rows || n_tiles > pb.cap_tiles || (size_t)n > pb.cap_req || n_text > kv->cap_text_b ||
         n_prior > kv->cap_prior_b || n_conds > kv->cap_conds_b) {

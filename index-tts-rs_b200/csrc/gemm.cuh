@@ -69,6 +69,9 @@ __device__ __forceinline__ void gemm_store(const GemmParams &p, int t, int o, fl
 // False when the activation tensor map could not be built (the caller then uses the
 // CUDA-core kernel).
 bool launch_gemm_tc(int epi, const GemmParams &p, cudaStream_t st);
+// fp16 x fp16 tensor-core GEMM over an fp16 copy of the weights (long prefills); false
+// when it cannot run (no copy, misaligned operands, no tensor-map encoder).
+bool launch_gemm_f16(int epi, const GemmParams &p, const __half *w16, cudaStream_t st);
 void kernels_init_gemm_tc();
 
 }  // namespace itts

@@ -18,6 +18,7 @@
 // copies land, frees its tensor memory and returns.
 #include <cuda.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "gemm.cuh"
@@ -32,6 +33,10 @@ constexpr int TC_RAW_B = TC_BN * TC_BK, TC_RAW_S = TC_BN * 8, TC_RAW_STAGE = TC_
 constexpr int TC_OFF_B = TC_A_STAGES * TC_TILE_BYTES;
 constexpr int TC_OFF_RAW = TC_OFF_B + TC_B_STAGES * TC_TILE_BYTES;
 constexpr int TC_SMEM = TC_OFF_RAW + TC_RAW_STAGES * TC_RAW_STAGE + 1024;
+// epilogue staging of the fp32 accumulator tile over the A and B stages (row stride in
+// floats, padded by 4)
+constexpr int TC_STG_LD = TC_BN + 4;
+static_assert(TC_BM * TC_STG_LD * 4 <= TC_OFF_RAW, "epilogue staging exceeds the operand stages");
 constexpr uint32_t TC_TMEM_COLS = 128;
 constexpr long TC_SPIN = 1L << 24;
 // instruction descriptor (kind::f16): D f32, A and B f16, both K-major, N = 128, M = 128
@@ -237,38 +242,79 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_q8_tc_kernel(GemmParams p,
     ok = __syncthreads_and((ok && okl) ? 1 : 0) != 0;
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     if (ok && last == nkb - 1 && nkb > 0) {
-        // warp w reads TMEM lanes 32 (w % 4) .. (its 32 positions), columns 64 (w / 4) ..
-        const int q = warp & 3, half = warp >> 2, t = m0 + q * 32 + lane;
-        const QkvDest qd = EPI == EPI_QKV && t < T ? qkv_dest(p, t) : QkvDest{0, 0, false};
+        // 1) accumulators TMEM -> shared memory, fp32 [128 rows][TC_STG_LD] over the operand
+        //    stages (free now): warp w reads TMEM lanes 32 (w % 4) .. (its 32 rows), columns
+        //    64 (w / 4) ..; the 4-float row padding keeps a quarter-warp's 16-byte stores on
+        //    distinct banks
+        float *stg = reinterpret_cast<float *>(smem);
+        {
+            const int q = warp & 3, half = warp >> 2, r = q * 32 + lane;
 #pragma unroll 1
-        for (int cc = 0; cc < 64; cc += 16) {
-            uint32_t v[16];
-            const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(half * 64 + cc);
-            asm volatile(
-                "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, "
-                "[%16];"
-                : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
-                  "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
-                  "=r"(v[15])
-                : "r"(ta));
-            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-            const int ob = o0 + half * 64 + cc;
-            if (t < T && ob < OUT) {
-                const int nj = min(16, OUT - ob);
-                const int cb = half * 64 + cc;
-                if (EPI == EPI_RESID) {
-                    // read the 16 residual values first so their loads overlap
-                    float *yp = p.y + (size_t)t * OUT + ob;
-                    float old[16];
+            for (int cc = 0; cc < 64; cc += 16) {
+                uint32_t v[16];
+                const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(half * 64 + cc);
+                asm volatile(
+                    "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, "
+                    "[%16];"
+                    : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+                      "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
+                      "=r"(v[15])
+                    : "r"(ta));
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                float4 *dst = reinterpret_cast<float4 *>(stg + r * TC_STG_LD + half * 64 + cc);
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) old[j] = j < nj ? yp[j] : 0.f;
-#pragma unroll
-                    for (int j = 0; j < 16; ++j)
-                        if (j < nj) yp[j] = old[j] + (__uint_as_float(v[j]) + bias_s[cb + j]);
+                for (int j = 0; j < 4; ++j)
+                    dst[j] = make_float4(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1]),
+                                         __uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3]));
+            }
+        }
+        __syncthreads();
+        // 2) row-wise write-out: warp w finishes rows w, w + 8, ...; lane j columns 4j .. 4j+3,
+        //    so a warp's stores (and residual loads) cover whole rows
+        const int c0 = 4 * lane, o = o0 + c0;
+        const float4 bias4 = make_float4(bias_s[c0], bias_s[c0 + 1], bias_s[c0 + 2], bias_s[c0 + 3]);
+        const bool vec = o + 3 < OUT && (OUT & 3) == 0;
+#pragma unroll 1
+        for (int r = warp; r < TC_BM; r += TC_THREADS / 32) {
+            const int t = m0 + r;
+            if (t >= T || o >= OUT) continue;
+            const float4 a = *reinterpret_cast<const float4 *>(stg + r * TC_STG_LD + c0);
+            float v4[4] = {a.x + bias4.x, a.y + bias4.y, a.z + bias4.z, a.w + bias4.w};
+            float *yp = p.y + (size_t)t * OUT + o;
+            if (EPI == EPI_RESID) {
+                if (vec) {
+                    const float4 old = *reinterpret_cast<const float4 *>(yp);
+                    *reinterpret_cast<float4 *>(yp) = make_float4(old.x + v4[0], old.y + v4[1], old.z + v4[2], old.w + v4[3]);
                 } else {
-#pragma unroll
-                    for (int j = 0; j < 16; ++j)
-                        if (j < nj) gemm_store<EPI>(p, t, ob + j, __uint_as_float(v[j]) + bias_s[cb + j], qd);
+                    for (int j = 0; j < 4 && o + j < OUT; ++j) yp[j] += v4[j];
+                }
+            } else if (EPI == EPI_GELU) {
+                __half *hp = reinterpret_cast<__half *>(p.y) + (size_t)t * OUT + o;
+                if (vec) {
+                    uint2 hv;
+                    hv.x = pack_half2(gelu_tanh(v4[0]), gelu_tanh(v4[1]));
+                    hv.y = pack_half2(gelu_tanh(v4[2]), gelu_tanh(v4[3]));
+                    *reinterpret_cast<uint2 *>(hp) = hv;
+                } else {
+                    for (int j = 0; j < 4 && o + j < OUT; ++j) hp[j] = __float2half_rn(gelu_tanh(v4[j]));
+                }
+            } else {
+                if (vec) *reinterpret_cast<float4 *>(yp) = make_float4(v4[0], v4[1], v4[2], v4[3]);
+                else
+                    for (int j = 0; j < 4 && o + j < OUT; ++j) yp[j] = v4[j];
+                if (EPI == EPI_QKV && o >= p.d) {
+                    // 4 consecutive dims of one head: 8 contiguous bytes of the cache row
+                    const QkvDest qd = qkv_dest(p, t);
+                    if (qd.write) {
+                        const int rr = o - p.d, which = rr / p.d, oo = rr - which * p.d;
+                        __half *cache = which == 0 ? p.k_cache : p.v_cache;
+                        uint2 hv;
+                        hv.x = pack_half2(v4[0], v4[1]);
+                        hv.y = pack_half2(v4[2], v4[3]);
+                        *reinterpret_cast<uint2 *>(
+                            cache + kv_index(p.layer, qd.slot, oo >> 6, qd.pos, p.n_slots, p.n_heads, p.max_seq) +
+                            (oo & 63)) = hv;
+                    }
                 }
             }
         }
@@ -330,7 +376,305 @@ bool launch_gemm_tc(int epi, const GemmParams &p, cudaStream_t st) {
     return true;
 }
 
+// ------------------------------------------------------------------------------
+// fp16 weight copies and the fp16 x fp16 GEMM for long prompts (prefill with many rows).
+//
+// With many rows per weight tile, dequantizing the int8 weights inside every CTA costs
+// more than the MMAs (each 128-row tile of the prompt would dequantize the whole weight
+// again).  So the weights of a model are dequantized once, exactly as the int8 kernel does
+// (s * q + b in fp32, rounded to fp16), into a row-major fp16 copy [out][in], and the
+// GEMM streams both operands with TMA:
+//  * persistent CTAs (one per SM) walk 128 x 256 output tiles, row tiles fastest, so the
+//    CTAs of a wave share one 256-row weight slab in L2;
+//  * warp 0 (one thread) issues the TMA copies of A (128 x 64) and B (256 x 64) into a
+//    4-stage ring (128-byte swizzle, no multicast); warp 1 (one thread) issues 4
+//    tcgen05.mma (K = 16) per stage into one of two 256-column TMEM accumulators and
+//    commits each stage back to the ring; warps 2-5 read a finished accumulator with
+//    tcgen05.ld (warp w reads TMEM lanes 32 (w % 4) ..) and run the epilogue while the
+//    MMAs of the next tile proceed in the other accumulator.
+// Every wait is bounded; on expiry the kernel records an error and the roles stop.
+// ------------------------------------------------------------------------------
+constexpr int HB_BM = 128, HB_BN = 256, HB_BK = 64, HB_STAGES = 4, HB_THREADS = 192;
+constexpr int HB_A_BYTES = HB_BM * HB_BK * 2, HB_B_BYTES = HB_BN * HB_BK * 2;
+constexpr int HB_STAGE = HB_A_BYTES + HB_B_BYTES;
+constexpr int HB_SMEM = HB_STAGES * HB_STAGE + 1024;
+constexpr uint32_t HB_TMEM_COLS = 512;  // two accumulators of 256 fp32 columns
+// instruction descriptor (kind::f16): D f32, A and B f16, both K-major, N = 256, M = 128
+constexpr uint32_t HB_IDESC = (1u << 4) | ((uint32_t)(HB_BN >> 3) << 17) | ((uint32_t)(HB_BM >> 4) << 24);
+
+__device__ __forceinline__ void hb_arrive_expect(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(tc_su32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void hb_tma(const CUtensorMap *map, void *dst, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(tc_su32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(tc_su32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void hb_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(tc_su32(bar))
+                 : "memory");
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(HB_THREADS, 1)
+    gemm_f16_tc_kernel(GemmParams p, const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b) {
+    extern __shared__ uint8_t hb_smem_raw[];
+    __shared__ uint64_t full[HB_STAGES], empty[HB_STAGES], acc_full[2], acc_empty[2], mma_done;
+    __shared__ uint32_t tmem_base;
+    __shared__ int stop;
+    uint8_t *smem = hb_smem_raw + ((1024u - (tc_su32(hb_smem_raw) & 1023u)) & 1023u);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int K = p.W.in, OUT = p.W.out, T = p.T;
+    const int mt = (T + HB_BM - 1) / HB_BM, ntile = (OUT + HB_BN - 1) / HB_BN, tiles = mt * ntile, nk = K / HB_BK;
+    if (tid == 0) {
+        for (int s = 0; s < HB_STAGES; ++s) {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(tc_su32(&full[s])));
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(tc_su32(&empty[s])));
+        }
+        for (int b = 0; b < 2; ++b) {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(tc_su32(&acc_full[b])));
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 128;" ::"r"(tc_su32(&acc_empty[b])));
+        }
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(tc_su32(&mma_done)));
+        stop = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(tc_su32(&tmem_base)),
+                     "r"(HB_TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = tmem_base;
+    volatile int *vstop = &stop;
+
+    if (warp == 0) {
+        if (lane == 0) {  // ---- TMA producer ----
+            int stage = 0, it = 0;
+            uint32_t phase = 0;
+            for (int tile = blockIdx.x; tile < tiles && !*vstop; tile += gridDim.x) {
+                const int m0 = (tile % mt) * HB_BM, n0 = (tile / mt) * HB_BN;
+                for (int kb = 0; kb < nk; ++kb) {
+                    if (it >= HB_STAGES && !tc_wait(&empty[stage], phase ^ 1u)) { *vstop = 1; break; }
+                    uint8_t *st = smem + stage * HB_STAGE;
+                    hb_arrive_expect(&full[stage], HB_STAGE);
+                    hb_tma(&tmap_a, st, kb * HB_BK, m0, &full[stage]);
+                    hb_tma(&tmap_b, st + HB_A_BYTES, kb * HB_BK, n0, &full[stage]);
+                    ++it;
+                    if (++stage == HB_STAGES) { stage = 0; phase ^= 1u; }
+                }
+            }
+            // the copies in flight land before the CTA may exit: the last HB_STAGES stages
+            for (int i = 0; i < HB_STAGES && i < it; ++i) {
+                const int k = it - 1 - i, s2 = k % HB_STAGES;
+                tc_wait(&full[s2], (uint32_t)(k / HB_STAGES) & 1u);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {  // ---- MMA issuer ----
+            int stage = 0, tl = 0;
+            uint32_t phase = 0;
+            for (int tile = blockIdx.x; tile < tiles && !*vstop; tile += gridDim.x, ++tl) {
+                const int ab = tl & 1;
+                if (tl >= 2 && !tc_wait(&acc_empty[ab], (uint32_t)((tl >> 1) - 1) & 1u)) { *vstop = 1; break; }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t acc = tmem + (uint32_t)(ab * HB_BN);
+                bool okt = true;
+                for (int kb = 0; kb < nk; ++kb) {
+                    if (!tc_wait(&full[stage], phase)) { okt = false; break; }
+                    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                    const uint32_t at = tc_su32(smem + stage * HB_STAGE), bt = at + HB_A_BYTES;
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const uint32_t accumulate = (kb > 0 || k > 0) ? 1u : 0u;
+                        asm volatile(
+                            "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                            " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(acc),
+                            "l"(tc_desc(at + k * 32)), "l"(tc_desc(bt + k * 32)), "r"(HB_IDESC), "r"(accumulate));
+                    }
+                    hb_commit(&empty[stage]);  // the stage is free once these MMAs are done
+                    if (++stage == HB_STAGES) { stage = 0; phase ^= 1u; }
+                }
+                hb_commit(&acc_full[ab]);  // the accumulator is final once every MMA is done
+                if (!okt) { *vstop = 1; break; }
+            }
+            // no MMA may still write the tensor memory when it is freed
+            hb_commit(&mma_done);
+            tc_wait(&mma_done, 0);
+        }
+    } else {  // ---- epilogue: warps 2..5 ----
+        const int q = warp & 3, r = q * 32 + lane;
+        int tl = 0;
+        for (int tile = blockIdx.x; tile < tiles && !*vstop; tile += gridDim.x, ++tl) {
+            const int ab = tl & 1;
+            const bool okw = tc_wait(&acc_full[ab], (uint32_t)(tl >> 1) & 1u);
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+            if (!okw || *vstop) { *vstop = 1; break; }
+            const int m0 = (tile % mt) * HB_BM, n0 = (tile / mt) * HB_BN, t = m0 + r;
+            const QkvDest qd = EPI == EPI_QKV && t < T ? qkv_dest(p, t) : QkvDest{0, 0, false};
+#pragma unroll 1
+            for (int cc = 0; cc < HB_BN; cc += 16) {
+                uint32_t v[16];
+                const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ab * HB_BN + cc);
+                asm volatile(
+                    "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, "
+                    "[%16];"
+                    : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+                      "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
+                      "=r"(v[15])
+                    : "r"(ta));
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                const int o = n0 + cc;
+                if (t >= T || o >= OUT) continue;
+                float f[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) f[j] = __uint_as_float(v[j]) + (o + j < OUT ? __ldg(p.W.bias + o + j) : 0.f);
+                const bool full16 = o + 16 <= OUT && (OUT & 3) == 0;
+                float *yp = p.y + (size_t)t * OUT + o;
+                if (EPI == EPI_GELU) {
+                    __half *hp = reinterpret_cast<__half *>(p.y) + (size_t)t * OUT + o;
+                    if (full16 && (OUT & 7) == 0) {
+#pragma unroll
+                        for (int j = 0; j < 16; j += 8) {
+                            uint4 hv;
+                            hv.x = pack_half2(gelu_tanh(f[j]), gelu_tanh(f[j + 1]));
+                            hv.y = pack_half2(gelu_tanh(f[j + 2]), gelu_tanh(f[j + 3]));
+                            hv.z = pack_half2(gelu_tanh(f[j + 4]), gelu_tanh(f[j + 5]));
+                            hv.w = pack_half2(gelu_tanh(f[j + 6]), gelu_tanh(f[j + 7]));
+                            *reinterpret_cast<uint4 *>(hp + j) = hv;
+                        }
+                    } else {
+                        for (int j = 0; j < 16 && o + j < OUT; ++j) hp[j] = __float2half_rn(gelu_tanh(f[j]));
+                    }
+                } else if (EPI == EPI_RESID) {
+                    if (full16) {
+#pragma unroll
+                        for (int j = 0; j < 16; j += 4) {
+                            const float4 old = *reinterpret_cast<const float4 *>(yp + j);
+                            *reinterpret_cast<float4 *>(yp + j) =
+                                make_float4(old.x + f[j], old.y + f[j + 1], old.z + f[j + 2], old.w + f[j + 3]);
+                        }
+                    } else {
+                        for (int j = 0; j < 16 && o + j < OUT; ++j) yp[j] += f[j];
+                    }
+                } else {
+                    if (full16) {
+#pragma unroll
+                        for (int j = 0; j < 16; j += 4)
+                            *reinterpret_cast<float4 *>(yp + j) = make_float4(f[j], f[j + 1], f[j + 2], f[j + 3]);
+                    } else {
+                        for (int j = 0; j < 16 && o + j < OUT; ++j) yp[j] = f[j];
+                    }
+                    if (EPI == EPI_QKV && o >= p.d && qd.write) {
+                        // 16 consecutive dims of one head: 32 contiguous bytes of the cache row
+                        const int rr = o - p.d, which = rr / p.d, oo = rr - which * p.d;
+                        __half *cache = (which == 0 ? p.k_cache : p.v_cache) +
+                                        kv_index(p.layer, qd.slot, oo >> 6, qd.pos, p.n_slots, p.n_heads, p.max_seq) +
+                                        (oo & 63);
+#pragma unroll
+                        for (int j = 0; j < 16; j += 8) {
+                            uint4 hv;
+                            hv.x = pack_half2(f[j], f[j + 1]);
+                            hv.y = pack_half2(f[j + 2], f[j + 3]);
+                            hv.z = pack_half2(f[j + 4], f[j + 5]);
+                            hv.w = pack_half2(f[j + 6], f[j + 7]);
+                            *reinterpret_cast<uint4 *>(cache + j) = hv;
+                        }
+                    }
+                }
+            }
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(tc_su32(&acc_empty[ab])) : "memory");
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(HB_TMEM_COLS));
+}
+
+// fp16 copy of a tiled int8 linear: w16[o][k] = fp16(s * q + b), the value the int8
+// GEMMs compute in registers or shared memory (rows past `out` are not written).
+__global__ void dequant_f16_kernel(MkLin W, __half *w16) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;  // one thread per 8 inputs
+    const int per = W.in / 8;
+    if (i >= (size_t)W.out * per) return;
+    const int o = (int)(i / per), k0 = (int)(i - (size_t)o * per) * 8;
+    const uint8_t *sb = W.tiles + mk_sb_offset(W, o, k0);
+    float sc, zo;
+    if (W.sbb == 4) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(sb));
+        sc = f.x; zo = f.y;
+    } else {
+        const float2 f = *reinterpret_cast<const float2 *>(sb);
+        sc = f.x; zo = f.y;
+    }
+    uint32_t hv[4];
+#pragma unroll
+    for (int j = 0; j < 8; j += 2) {
+        const float a = fmaf(sc, (float)W.tiles[mk_q_offset(W, o, k0 + j)], zo);
+        const float b = fmaf(sc, (float)W.tiles[mk_q_offset(W, o, k0 + j + 1)], zo);
+        hv[j / 2] = pack_half2(a, b);
+    }
+    *reinterpret_cast<uint4 *>(w16 + (size_t)o * W.in + k0) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+}
+
+cudaError_t make_weights_f16(const MkLin &W, __half *w16, cudaStream_t st) {
+    const size_t n = (size_t)W.out * (W.in / 8);
+    dequant_f16_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(W, w16);
+    return cudaGetLastError();
+}
+
+bool launch_gemm_f16(int epi, const GemmParams &p, const __half *w16, cudaStream_t st) {
+    const int K = p.W.in;
+    if (!w16 || K % HB_BK != 0 || (reinterpret_cast<uintptr_t>(p.x) & 15) != 0 ||
+        (reinterpret_cast<uintptr_t>(w16) & 15) != 0 || p.T <= 0)
+        return false;
+    EncodeTiledFn enc = encode_tiled();
+    if (!enc) return false;
+    CUtensorMap ma, mb;
+    const cuuint32_t estr[2] = {1, 1};
+    {
+        const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)p.T};
+        const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+        const cuuint32_t box[2] = {(cuuint32_t)HB_BK, (cuuint32_t)HB_BM};
+        if (enc(&ma, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half *>(p.x), dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return false;
+    }
+    {
+        const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)p.W.out};
+        const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+        const cuuint32_t box[2] = {(cuuint32_t)HB_BK, (cuuint32_t)HB_BN};
+        if (enc(&mb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half *>(w16), dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return false;
+    }
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int tiles = ((p.T + HB_BM - 1) / HB_BM) * ((p.W.out + HB_BN - 1) / HB_BN);
+    const dim3 grid((unsigned)std::min(tiles, sms));
+    switch (epi) {
+    case EPI_PLAIN: gemm_f16_tc_kernel<EPI_PLAIN><<<grid, HB_THREADS, HB_SMEM, st>>>(p, ma, mb); break;
+    case EPI_GELU: gemm_f16_tc_kernel<EPI_GELU><<<grid, HB_THREADS, HB_SMEM, st>>>(p, ma, mb); break;
+    case EPI_RESID: gemm_f16_tc_kernel<EPI_RESID><<<grid, HB_THREADS, HB_SMEM, st>>>(p, ma, mb); break;
+    default: gemm_f16_tc_kernel<EPI_QKV><<<grid, HB_THREADS, HB_SMEM, st>>>(p, ma, mb); break;
+    }
+    return true;
+}
+
 void kernels_init_gemm_tc() {
+    cudaFuncSetAttribute(gemm_f16_tc_kernel<EPI_PLAIN>, cudaFuncAttributeMaxDynamicSharedMemorySize, HB_SMEM);
+    cudaFuncSetAttribute(gemm_f16_tc_kernel<EPI_GELU>, cudaFuncAttributeMaxDynamicSharedMemorySize, HB_SMEM);
+    cudaFuncSetAttribute(gemm_f16_tc_kernel<EPI_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, HB_SMEM);
+    cudaFuncSetAttribute(gemm_f16_tc_kernel<EPI_QKV>, cudaFuncAttributeMaxDynamicSharedMemorySize, HB_SMEM);
     cudaFuncSetAttribute(gemm_q8_tc_kernel<EPI_PLAIN>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM);
     cudaFuncSetAttribute(gemm_q8_tc_kernel<EPI_GELU>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM);
     cudaFuncSetAttribute(gemm_q8_tc_kernel<EPI_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM);

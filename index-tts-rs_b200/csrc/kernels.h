@@ -120,6 +120,11 @@ void launch_gemm_rows(int epi, const MkLin &W, const __half *x, void *y, int T, 
                       const int *row_pos, __half *k_cache, __half *v_cache, int n_slots, int n_heads,
                       int max_seq, int layer, int d, cudaStream_t st);
 
+// fp16 copy of a linear's weights (dequantized exactly as the int8 GEMMs do).
+cudaError_t make_weights_f16(const MkLin &W, __half *w16, cudaStream_t st);
+// Rows from which prefill GEMMs use the fp16 weight copy (made on the first such prefill).
+constexpr int kGemmF16MinRows = 256;
+
 void launch_embed_prefix(const ModelView &m, const int *full_text, int n_full, const float *conds,
                          int n_conds, int lang, const int *prior, int n_prior, float *x,
                          cudaStream_t st);

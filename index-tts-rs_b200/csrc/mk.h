@@ -24,6 +24,7 @@ struct MkLin {
     const uint8_t *tiles;
     const float *bias;
     int out, in, n_rb, n_kc, kc, tile_bytes, sbb;
+    const __half *w16;  // optional fp16 copy [out][in] for long prefills (null until made)
 };
 
 struct MkLayer {

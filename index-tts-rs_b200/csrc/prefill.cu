@@ -203,6 +203,7 @@ void launch_gemm(int epi, const MkLin &W, const __half *x, void *y, int T, const
         p.slots = dv->slots;
         p.batch_slot = dv->batch_slot;
     }
+    if (T >= kGemmF16MinRows && W.w16 && launch_gemm_f16(epi, p, W.w16, st)) return;
     if (T >= kGemmTcMinRows && launch_gemm_tc(epi, p, st)) return;
     dim3 grid((W.out + 63) / 64, (T + 63) / 64);
     switch (epi) {
@@ -231,6 +232,7 @@ void launch_gemm_rows(int epi, const MkLin &W, const __half *x, void *y, int T, 
     p.max_seq = max_seq;
     p.layer = layer;
     p.d = d;
+    if (T >= kGemmF16MinRows && W.w16 && launch_gemm_f16(epi, p, W.w16, st)) return;
     if (T >= kGemmTcMinRows && launch_gemm_tc(epi, p, st)) return;
     dim3 grid((W.out + 63) / 64, (T + 63) / 64);
     switch (epi) {
