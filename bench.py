@@ -291,12 +291,53 @@ def run_ours(args, rank, world, local_rank):
                      "ms_per_launch": ws_ms, "traffic": None},
         "clocks": clk,
     }
+    try:
+        line["prefill_cfg4"] = bench_prefill_cfg4(cfg, gpt, peaks)
+    except Exception as e:  # never blocks the headline line
+        line["prefill_cfg4"] = {"error": str(e)[:200]}
     if not args.no_cpu_baseline:
         try:
             line["cpu_baseline"] = cpu_baseline(cfg, w, text, conds, 8, os.cpu_count() or 1)
         except Exception as e:  # the baseline never blocks the GPU line
             line["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
     print(json.dumps(line), flush=True)
+
+
+def prefill_flops(cfg, lens) -> float:
+    """FLOPs of a prefill of requests with `lens` positions: the 24 layers' linears on
+    every position, the head on each request's last position, causal attention
+    (QK^T and PV over keys 0..t of each query t)."""
+    per_pos = 2.0 * cfg.n_layers * (3 * cfg.d * cfg.d + cfg.d * cfg.d + 2 * cfg.d * cfg.ff)
+    head = 2.0 * cfg.d * cfg.mel_vocab
+    attn = sum(2.0 * 2 * cfg.d * cfg.n_layers * T * (T + 1) / 2 for T in lens)
+    return per_pos * sum(lens) + head * len(lens) + attn
+
+
+def bench_prefill_cfg4(cfg, gpt, peaks, n_req=32, reps=3) -> dict:
+    """configs[3]'s prefill: 32 prompts of 32 conditioning latents + 600 text tokens in
+    one packed prefill (device time of the forward, CUDA events)."""
+    import itts_gpt as ig
+    prompts = []
+    for r in range(n_req):
+        text, conds = make_prompt(cfg, r)
+        prompts.append(ig.CodePrompt(text, conds, LANG))
+    T = N_CONDS + N_TEXT + 3
+    kv = ig.KvCache(gpt, max_seq=T + 40, max_batch=n_req)
+    ms = []
+    for i in range(2 + reps):
+        ig.prefill_batch(gpt, prompts, kv)
+        if i >= 2:
+            ms.append(gpt.last_timing()[0])
+    kv.close()
+    dev_ms = statistics.median(ms)
+    flops = prefill_flops(cfg, [T] * n_req)
+    peak = float(peaks.get("bf16_tflops_sustained", 1404.5))
+    tf = flops / (dev_ms * 1e-3) / 1e12
+    return {"workload": f"cfg4 prefill: {n_req} prompts x {T} positions in one packed prefill",
+            "device_ms": dev_ms, "positions_per_s": n_req * T / (dev_ms * 1e-3),
+            "tflops": tf, "flops": flops, "peak_tflops": peak,
+            "peak_source": "measured sustained bf16" if "bf16_tflops_sustained" in peaks else "fallback",
+            "frac": tf / peak}
 
 
 def _bench_decode_forward(gpt, kv, kv_len, iters):

@@ -232,7 +232,8 @@ int itts_generate_batch(itts_gpt *gpt, itts_kv *kv, int32_t n_req,
 
 /* Device time (CUDA events on the handle's stream) of the last generate call:
  * prefill_ms (all prefills) and decode_ms (first sample through the last step), and the
- * number of decode-step graph launches it made. */
+ * number of decode-step graph launches it made.  After itts_gpt_prefill_batch: prefill_ms
+ * is the packed forward (embedded prompts to logits), decode_ms and launches are 0. */
 int itts_gpt_last_timing(const itts_gpt *gpt, float *prefill_ms, float *decode_ms,
                          int32_t *decode_launches);
 

@@ -71,6 +71,7 @@ struct itts_gpt {
     bool w16_tried = false;
     cudaStream_t stream = nullptr;
     cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
+    cudaEvent_t evp[2] = {nullptr, nullptr};  // around the forward of a packed prefill
     float last_prefill_ms = 0.f, last_decode_ms = 0.f;
     int last_launches = 0;
     // standalone sampler scratch
@@ -216,6 +217,8 @@ static void gpt_destroy(itts_gpt *g) {
     cudaSetDevice(g->device);
     if (g->stream) cudaStreamSynchronize(g->stream);
     for (auto &e : g->ev)
+        if (e) cudaEventDestroy(e);
+    for (auto &e : g->evp)
         if (e) cudaEventDestroy(e);
     cudaFree(g->arena);
     cudaFree(g->w16_arena);
@@ -402,6 +405,8 @@ extern "C" int itts_gpt_from_tensors(const itts_tensor *tensors, int32_t n_tenso
     cudaError_t e;
     if ((e = cudaStreamCreateWithFlags(&g->stream, cudaStreamNonBlocking)) != cudaSuccess) return fail(e, "stream");
     for (auto &ev : g->ev)
+        if ((e = cudaEventCreate(&ev)) != cudaSuccess) return fail(e, "event");
+    for (auto &ev : g->evp)
         if ((e = cudaEventCreate(&ev)) != cudaSuccess) return fail(e, "event");
     if ((e = cudaMalloc(&g->arena, total)) != cudaSuccess) return fail(e, "weights");
     char *base = (char *)g->arena;
@@ -974,7 +979,9 @@ static int prefill_batch_impl(itts_gpt *g, itts_kv *kv, int n, const int *slots,
         row += Ts[r];
     }
     DecodeView dv = decode_view(kv, 1);
+    CUDA_TRY(cudaEventRecord(g->evp[0], st));
     prefill_batch_forward(m, dv, pb, n, (int)total, d_logits, st);
+    CUDA_TRY(cudaEventRecord(g->evp[1], st));
     CUDA_TRY(cudaGetLastError());
     for (int r = 0; r < n; ++r) kv->h_state[slots[r]].valid_len = Ts[r];
     return ITTS_OK;
@@ -1017,6 +1024,10 @@ extern "C" int itts_gpt_prefill_batch(itts_gpt *g, itts_kv *kv, int32_t n, const
         CUDA_TRY(cudaMemcpyAsync(logits_out, kv->db.logits, sizeof(float) * n * m.mel_vocab, cudaMemcpyDeviceToHost,
                                  g->stream));
     CUDA_TRY(cudaStreamSynchronize(g->stream));
+    // device time of the packed forward (embedded prompts to logits)
+    CUDA_TRY(cudaEventElapsedTime(&g->last_prefill_ms, g->evp[0], g->evp[1]));
+    g->last_decode_ms = 0.f;
+    g->last_launches = 0;
     return ITTS_OK;
 }
 

@@ -114,6 +114,10 @@ void prefill_forward(const ModelView &m, const DecodeView &dv, int slot, int T, 
 // each row's K/V into its request's slot, logits of request r into row r of `logits`.
 void prefill_batch_forward(const ModelView &m, const DecodeView &dv, const PrefillBatch &pb, int n_req,
                            int total, float *logits, cudaStream_t st);
+// Causal attention of one request's prompt (T positions of QKV rows; K/V from the cache
+// slot the QKV epilogue filled): tensor-core flash attention, fp16 output [T][d].
+void launch_attn_prefill_fa(const float *qkv, int T, int slot, const DecodeView &dv, int layer, int d,
+                            __half *out, cudaStream_t st);
 // launch_gemm for a packed prefill: the QKV epilogue writes row t's K/V to
 // (row_slot[t], row_pos[t]).
 void launch_gemm_rows(int epi, const MkLin &W, const __half *x, void *y, int T, const int *row_slot,

@@ -243,57 +243,6 @@ void launch_gemm_rows(int epi, const MkLin &W, const __half *x, void *y, int T, 
     }
 }
 
-// ---------------------------------------------------------------------------
-// Causal attention over the prompt: one thread per query, 64 queries x one head
-// per CTA; K/V tiles of 64 positions staged in shared memory (fp32, from the
-// QKV output); online softmax.  Query t sees keys 0..t.
-// ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(64) attn_prefill_kernel(const float *qkv, int T, int d,
-                                                          __half *out) {
-    __shared__ float Ks[64][65];
-    __shared__ float Vs[64][65];
-    const int h = blockIdx.y, q0 = blockIdx.x * 64, t = q0 + threadIdx.x;
-    const int ld = 3 * d;
-    float q[64], acc[64];
-    float m = -INFINITY, l = 0.f;
-    if (t < T) {
-#pragma unroll
-        for (int e = 0; e < 64; ++e) q[e] = qkv[(size_t)t * ld + h * 64 + e] * kAttnScale;
-    }
-#pragma unroll
-    for (int e = 0; e < 64; ++e) acc[e] = 0.f;
-    const int last = min(T - 1, q0 + 63);
-    for (int k0 = 0; k0 <= last; k0 += 64) {
-        __syncthreads();
-        for (int i = threadIdx.x; i < 64 * 64; i += 64) {
-            const int r = i >> 6, e = i & 63, kk = k0 + r;
-            Ks[r][e] = kk < T ? qkv[(size_t)kk * ld + d + h * 64 + e] : 0.f;
-            Vs[r][e] = kk < T ? qkv[(size_t)kk * ld + 2 * d + h * 64 + e] : 0.f;
-        }
-        __syncthreads();
-        if (t < T) {
-            const int jn = min(64, t - k0 + 1);
-            for (int j = 0; j < jn; ++j) {
-                float s = 0.f;
-#pragma unroll
-                for (int e = 0; e < 64; ++e) s = fmaf(q[e], Ks[j][e], s);
-                const float mn = fmaxf(m, s);
-                const float corr = m == -INFINITY ? 0.f : expf(m - mn);
-                const float pj = expf(s - mn);
-                l = l * corr + pj;
-#pragma unroll
-                for (int e = 0; e < 64; ++e) acc[e] = acc[e] * corr + pj * Vs[j][e];
-                m = mn;
-            }
-        }
-    }
-    if (t < T) {
-        const float inv = 1.0f / l;
-#pragma unroll
-        for (int e = 0; e < 64; ++e) out[(size_t)t * d + h * 64 + e] = __float2half_rn(acc[e] * inv);
-    }
-}
-
 // Gpt2Block::head_attention (gpt.rs:391-427) on the prefill's QKV of one layer: for
 // query row t = q0 + blockIdx.x, softmax over keys 0..t of head `head` at scale 0.125
 // (the prefix and the Mel positions up to the query), keeping key columns [k0, k1).
@@ -381,7 +330,7 @@ void prefill_forward(const ModelView &m, const DecodeView &dv, int slot, int T, 
                 pb.qkv, T, d, hk->map_head, hk->map_q0, hk->map_k0, hk->map_k1, hk->maps, map_done++ > 0);
         }
         if (hk && l == hk->stop_layer) return;
-        attn_prefill_kernel<<<dim3((T + 63) / 64, m.n_heads), 64, 0, st>>>(pb.qkv, T, d, attn16);
+        launch_attn_prefill_fa(pb.qkv, T, slot, dv, l, d, attn16, st);
         launch_gemm(EPI_RESID, L.proj, attn16, pb.x, T, nullptr, nullptr, nullptr, -1, 0, 0, 0, l,
                     d, st);
         launch_layernorm_rows_h(pb.x, L.ln2_w, L.ln2_b, T, d, n16, st);

@@ -51,13 +51,14 @@ __device__ __forceinline__ void fa_cp16(__half *dst, const __half *src) {
                  : "memory");
 }
 
-__global__ void __launch_bounds__(128) attn_prefill_fa_kernel(const float *qkv, const AttnTile *tiles,
-                                                              const __half *kc, const __half *vc, int layer,
-                                                              int n_slots, int H, int max_seq, int d,
+// tiles == null: one request of T1 positions in slot1 at row 0, tile blockIdx.x
+__global__ void __launch_bounds__(128) attn_prefill_fa_kernel(const float *qkv, const AttnTile *tiles, int T1,
+                                                              int slot1, const __half *kc, const __half *vc,
+                                                              int layer, int n_slots, int H, int max_seq, int d,
                                                               __half *out) {
     __shared__ __align__(16) __half Ks[64 * FA_ROW];
     __shared__ __align__(16) __half Vs[64 * FA_ROW];
-    const AttnTile tl = tiles[blockIdx.x];
+    const AttnTile tl = tiles ? tiles[blockIdx.x] : AttnTile{0, (int)blockIdx.x * 64, T1, slot1};
     const int h = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
     const int T = tl.T, q0 = tl.q0;
     const int qa_row = q0 + warp * 16 + g, qb_row = qa_row + 8;  // this thread's two query rows
@@ -180,6 +181,12 @@ __global__ void __launch_bounds__(128) attn_prefill_fa_kernel(const float *qkv, 
     }
 }
 
+void launch_attn_prefill_fa(const float *qkv, int T, int slot, const DecodeView &dv, int layer, int d,
+                            __half *out, cudaStream_t st) {
+    attn_prefill_fa_kernel<<<dim3((T + 63) / 64, dv.n_heads), 128, 0, st>>>(
+        qkv, nullptr, T, slot, dv.k_cache, dv.v_cache, layer, dv.n_slots, dv.n_heads, dv.max_seq, d, out);
+}
+
 // rows[r] = x[last row of request r]
 __global__ void gather_rows_kernel(const float *x, const int *row_idx, int d, float *rows) {
     const int r = blockIdx.x;
@@ -198,7 +205,7 @@ void prefill_batch_forward(const ModelView &m, const DecodeView &dv, const Prefi
         launch_gemm_rows(EPI_QKV, L.qkv, n16, pb.qkv, total, pb.row_slot, pb.row_pos, dv.k_cache, dv.v_cache,
                          dv.n_slots, dv.n_heads, dv.max_seq, l, d, st);
         attn_prefill_fa_kernel<<<dim3(pb.n_tiles, m.n_heads), 128, 0, st>>>(
-            pb.qkv, pb.tiles, dv.k_cache, dv.v_cache, l, dv.n_slots, dv.n_heads, dv.max_seq, d, attn16);
+            pb.qkv, pb.tiles, 0, 0, dv.k_cache, dv.v_cache, l, dv.n_slots, dv.n_heads, dv.max_seq, d, attn16);
         launch_gemm(EPI_RESID, L.proj, attn16, pb.x, total, nullptr, nullptr, nullptr, -1, 0, 0, 0, l, d, st);
         launch_layernorm_rows_h(pb.x, L.ln2_w, L.ln2_b, total, d, n16, st);
         launch_gemm(EPI_GELU, L.fc, n16, pb.u, total, nullptr, nullptr, nullptr, -1, 0, 0, 0, l, d, st);
