@@ -340,11 +340,11 @@ def bench_prefill_cfg4(cfg, gpt, peaks, n_req=32, reps=3) -> dict:
             "frac": tf / peak}
 
 
-def _bench_decode_forward(gpt, kv, kv_len, iters):
+def _bench_decode_forward(gpt, kv, kv_len, iters, nb=1):
     import ctypes as C
     from itts_gpt import _lib
     ms, n = C.c_float(), C.c_int32()
-    rc = _lib.load_lib().itts_bench_decode_forward(gpt._h, kv._h, 1, kv_len, iters, C.byref(ms),
+    rc = _lib.load_lib().itts_bench_decode_forward(gpt._h, kv._h, nb, kv_len, iters, C.byref(ms),
                                                    C.byref(n))
     if rc != 0:
         raise RuntimeError(_lib.last_error())
@@ -357,10 +357,11 @@ def run_profile_case(args):
     import itts_gpt as ig
     cfg, w = make_model()
     gpt = ig.Gpt.from_weights(w)
-    kv = ig.KvCache(gpt, max_seq=args.profile_decode + 8, max_batch=1)
-    ms, n = _bench_decode_forward(gpt, kv, args.profile_decode, iters=args.profile_iters)
-    print(json.dumps({"profile_case": "decode-step forward", "kv_len": args.profile_decode,
-                      "ms_per_launch": ms, "launches_per_step": n}), flush=True)
+    nb = args.profile_nb
+    kv = ig.KvCache(gpt, max_seq=args.profile_decode + 8, max_batch=nb)
+    ms, n = _bench_decode_forward(gpt, kv, args.profile_decode, iters=args.profile_iters, nb=nb)
+    print(json.dumps({"profile_case": "decode-step forward", "kv_len": args.profile_decode, "columns": nb,
+                      "ms_per_step": ms, "launches_per_step": n}), flush=True)
 
 
 def run_profile_prefill(args):
@@ -412,6 +413,7 @@ def main():
     ap.add_argument("--profile-decode", type=int, default=0, metavar="KV_LEN",
                     help="profiler case: only the decode-step forward at this KV length")
     ap.add_argument("--profile-iters", type=int, default=2)
+    ap.add_argument("--profile-nb", type=int, default=1, help="batch columns of --profile-decode")
     ap.add_argument("--profile-prefill", type=int, default=0, metavar="REPEATS",
                     help="profiler case: only cfg2 prefills, this many")
     ap.add_argument("--profile-prefill-batch", type=int, default=0, metavar="N_REQ",

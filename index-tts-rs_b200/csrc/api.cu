@@ -607,7 +607,7 @@ static void kv_destroy(itts_kv *kv) {
         if (g) cudaGraphDestroy(g);
     void *dev[] = {kv->k, kv->v, kv->d_slots, kv->d_batch_slot, kv->db.x, kv->db.n, kv->db.n2,
                    kv->db.q, kv->db.attn, kv->db.u, kv->db.logits, kv->db.partials,
-                   kv->db.counters, kv->db.qkv_ll, kv->db.epoch, kv->db.err, kv->db.trace,
+                   kv->db.counters, kv->db.qkv_ll, kv->db.epoch, kv->db.err, kv->db.trace, kv->db.ws,
                    kv->pb.x, kv->pb.n, kv->pb.qkv, kv->pb.attn,
                    kv->pb.u, kv->d_codes, kv->d_text, kv->d_prior, kv->d_conds};
     for (void *p : dev) cudaFree(p);
@@ -661,6 +661,10 @@ extern "C" int itts_kv_create(itts_gpt *g, int32_t max_seq, int32_t max_batch, i
     A((void **)&kv->db.logits, sizeof(float) * max_batch * m.mel_vocab);
     A((void **)&kv->db.partials, sizeof(float) * max_batch * m.n_heads * kv->db.max_splits * 66);
     A((void **)&kv->db.counters, sizeof(int) * max_batch * m.n_heads);
+    kv->db.ws_splits = max_batch > MK_MAX_NB ? 16 : 0;  // split-K of the fp16 GEMM (wide steps)
+    kv->db.ws = nullptr;
+    if (kv->db.ws_splits)
+        A((void **)&kv->db.ws, sizeof(float) * kv->db.ws_splits * max_batch * std::max(3 * m.d, m.ff));
     // persistent decode-step kernel
     {
         int nsl = 0, grid = 0;
@@ -1182,6 +1186,7 @@ extern "C" int itts_gpt_step(itts_gpt *g, itts_kv *kv, int32_t n, const int32_t 
     TRY(push_slots(kv, slots, n));
     TRY(set_batch_slots(kv, slots, n));
     TRY(reset_step_sync(kv));
+    if (n > MK_MAX_NB) ensure_weights_f16(g);  // wide steps run the fp16 GEMM
     DecodeView dv = decode_view(kv, n);
     CUDA_TRY(decode_forward(m, dv, kv->db, g->stream));
     CUDA_TRY(cudaStreamSynchronize(g->stream));
@@ -1342,6 +1347,7 @@ static int generate_impl(itts_gpt *g, itts_kv *kv, int n, const int *slots,
     TRY(push_slots(kv, slots, n));
     TRY(set_batch_slots(kv, slots, n));
     TRY(reset_step_sync(kv));
+    if (n > MK_MAX_NB) ensure_weights_f16(g);  // wide steps run the fp16 GEMM (made before capture)
     cudaGraphExec_t graph = nullptr;
     if (!kv->graph_failed[n] && get_graph(kv, n, &graph) != ITTS_OK) {
         kv->graph_failed[n] = 1;  // e.g. a cooperative launch the driver cannot capture
@@ -1464,6 +1470,7 @@ extern "C" int itts_bench_decode_forward(itts_gpt *g, itts_kv *kv, int32_t nb, i
     TRY(push_slots(kv, slots.data(), nb));
     TRY(set_batch_slots(kv, slots.data(), nb));
     TRY(reset_step_sync(kv));
+    if (nb > MK_MAX_NB) ensure_weights_f16(g);
     DecodeView dv = decode_view(kv, nb);
     for (int i = 0; i < 3; ++i) CUDA_TRY(decode_forward(g->m, dv, kv->db, st));
     CUDA_TRY(cudaEventRecord(g->ev[0], st));

@@ -266,14 +266,15 @@ cudaError_t decode_forward(const ModelView &m, const DecodeView &dv, DecodeBufs 
         const MkLayer &L = m.layers[l];
         launch_layernorm_rows_h(b.x, L.ln1_w, L.ln1_b, dv.nb, d, n16, st);
         launch_gemm(EPI_QKV, L.qkv, n16, b.q, dv.nb, &dv, dv.k_cache, dv.v_cache, -1, dv.n_slots,
-                    dv.n_heads, dv.max_seq, l, d, st);
+                    dv.n_heads, dv.max_seq, l, d, st, b.ws, b.ws_splits);
         launch_attn_decode(dv, l, b.q, 3 * d, b, st);
         launch_gemm(EPI_RESID, L.proj, attn16, b.x, dv.nb, nullptr, nullptr, nullptr, -1, 0, 0, 0, l,
-                    d, st);
+                    d, st, b.ws, b.ws_splits);
         launch_layernorm_rows_h(b.x, L.ln2_w, L.ln2_b, dv.nb, d, n16, st);
-        launch_gemm(EPI_GELU, L.fc, n16, b.u, dv.nb, nullptr, nullptr, nullptr, -1, 0, 0, 0, l, d, st);
+        launch_gemm(EPI_GELU, L.fc, n16, b.u, dv.nb, nullptr, nullptr, nullptr, -1, 0, 0, 0, l, d, st, b.ws,
+                    b.ws_splits);
         launch_gemm(EPI_RESID, L.mlp, u16, b.x, dv.nb, nullptr, nullptr, nullptr, -1, 0, 0, 0, l, d,
-                    st);
+                    st, b.ws, b.ws_splits);
     }
     launch_layernorm_rows(b.x, m.ln_f_w, m.ln_f_b, dv.nb, d, b.n, st);
     launch_layernorm_rows_h(b.n, m.final_w, m.final_b, dv.nb, d, fin16, st);

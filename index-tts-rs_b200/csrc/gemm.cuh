@@ -17,6 +17,10 @@ struct GemmParams {
     const int *batch_slot;
     // packed prefill of several requests: row t's K/V go to (row_slot[t], row_pos[t])
     const int *row_slot, *row_pos;
+    // split-K of the fp16 GEMM (few rows): partial sums [ksplit][T][OUT] in ws, which holds
+    // ws_splits of them; the epilogue then runs on their sum
+    float *ws;
+    int ksplit, ws_splits;
     int kv_slot, n_slots, n_heads, max_seq, layer, d;
 };
 

@@ -427,7 +427,17 @@ __global__ void __launch_bounds__(HB_THREADS, 1)
     uint8_t *smem = hb_smem_raw + ((1024u - (tc_su32(hb_smem_raw) & 1023u)) & 1023u);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int K = p.W.in, OUT = p.W.out, T = p.T;
-    const int mt = (T + HB_BM - 1) / HB_BM, ntile = (OUT + HB_BN - 1) / HB_BN, tiles = mt * ntile, nk = K / HB_BK;
+    const int ks = p.ksplit > 1 ? p.ksplit : 1;  // K splits (tile index / (mt * ntile))
+    const int mt = (T + HB_BM - 1) / HB_BM, ntile = (OUT + HB_BN - 1) / HB_BN, tiles = mt * ntile * ks, nk = K / HB_BK;
+    // tile -> row tile m (fastest), column tile n, K split ksp covering k blocks [kb0, kb1)
+    auto tile_of = [&](int tile, int &m0, int &n0, int &kb0, int &kb1, int &ksp) {
+        const int mn = tile % (mt * ntile);
+        ksp = tile / (mt * ntile);
+        m0 = (mn % mt) * HB_BM;
+        n0 = (mn / mt) * HB_BN;
+        kb0 = ksp * nk / ks;
+        kb1 = (ksp + 1) * nk / ks;
+    };
     if (tid == 0) {
         for (int s = 0; s < HB_STAGES; ++s) {
             asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(tc_su32(&full[s])));
@@ -457,8 +467,9 @@ __global__ void __launch_bounds__(HB_THREADS, 1)
             int stage = 0, it = 0;
             uint32_t phase = 0;
             for (int tile = blockIdx.x; tile < tiles && !*vstop; tile += gridDim.x) {
-                const int m0 = (tile % mt) * HB_BM, n0 = (tile / mt) * HB_BN;
-                for (int kb = 0; kb < nk; ++kb) {
+                int m0, n0, kb0, kb1, ksp;
+                tile_of(tile, m0, n0, kb0, kb1, ksp);
+                for (int kb = kb0; kb < kb1; ++kb) {
                     if (it >= HB_STAGES && !tc_wait(&empty[stage], phase ^ 1u)) { *vstop = 1; break; }
                     uint8_t *st = smem + stage * HB_STAGE;
                     hb_arrive_expect(&full[stage], HB_STAGE);
@@ -483,14 +494,16 @@ __global__ void __launch_bounds__(HB_THREADS, 1)
                 if (tl >= 2 && !tc_wait(&acc_empty[ab], (uint32_t)((tl >> 1) - 1) & 1u)) { *vstop = 1; break; }
                 asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                 const uint32_t acc = tmem + (uint32_t)(ab * HB_BN);
+                int m0, n0, kb0, kb1, ksp;
+                tile_of(tile, m0, n0, kb0, kb1, ksp);
                 bool okt = true;
-                for (int kb = 0; kb < nk; ++kb) {
+                for (int kb = kb0; kb < kb1; ++kb) {
                     if (!tc_wait(&full[stage], phase)) { okt = false; break; }
                     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
                     const uint32_t at = tc_su32(smem + stage * HB_STAGE), bt = at + HB_A_BYTES;
 #pragma unroll
                     for (int k = 0; k < 4; ++k) {
-                        const uint32_t accumulate = (kb > 0 || k > 0) ? 1u : 0u;
+                        const uint32_t accumulate = (kb > kb0 || k > 0) ? 1u : 0u;
                         asm volatile(
                             "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
                             " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(acc),
@@ -514,8 +527,10 @@ __global__ void __launch_bounds__(HB_THREADS, 1)
             const bool okw = tc_wait(&acc_full[ab], (uint32_t)(tl >> 1) & 1u);
             asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             if (!okw || *vstop) { *vstop = 1; break; }
-            const int m0 = (tile % mt) * HB_BM, n0 = (tile / mt) * HB_BN, t = m0 + r;
-            const QkvDest qd = EPI == EPI_QKV && t < T ? qkv_dest(p, t) : QkvDest{0, 0, false};
+            int m0, n0, kb0, kb1, ksp;
+            tile_of(tile, m0, n0, kb0, kb1, ksp);
+            const int t = m0 + r;
+            const QkvDest qd = EPI == EPI_QKV && t < T && ks == 1 ? qkv_dest(p, t) : QkvDest{0, 0, false};
 #pragma unroll 1
             for (int cc = 0; cc < HB_BN; cc += 16) {
                 uint32_t v[16];
@@ -530,6 +545,19 @@ __global__ void __launch_bounds__(HB_THREADS, 1)
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
                 const int o = n0 + cc;
                 if (t >= T || o >= OUT) continue;
+                if (ks > 1) {  // split K: this split's partial sums (no bias), finished by gemm_splitk_epilogue
+                    float *wp = p.ws + ((size_t)ksp * T + t) * OUT + o;
+                    if (o + 16 <= OUT && (OUT & 3) == 0) {
+#pragma unroll
+                        for (int j = 0; j < 16; j += 4)
+                            *reinterpret_cast<float4 *>(wp + j) =
+                                make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]), __uint_as_float(v[j + 2]),
+                                            __uint_as_float(v[j + 3]));
+                    } else {
+                        for (int j = 0; j < 16 && o + j < OUT; ++j) wp[j] = __uint_as_float(v[j]);
+                    }
+                    continue;
+                }
                 float f[16];
 #pragma unroll
                 for (int j = 0; j < 16; ++j) f[j] = __uint_as_float(v[j]) + (o + j < OUT ? __ldg(p.W.bias + o + j) : 0.f);
@@ -597,6 +625,21 @@ __global__ void __launch_bounds__(HB_THREADS, 1)
     if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(HB_TMEM_COLS));
 }
 
+// The epilogue of a split-K fp16 GEMM: y[t, o] = sum of the splits' partials (in split
+// order) + bias[o], stored per epilogue (gemm_store); one thread per output.
+template <int EPI>
+__global__ void gemm_splitk_epilogue(GemmParams p) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int OUT = p.W.out;
+    if (i >= (size_t)p.T * OUT) return;
+    const int t = (int)(i / OUT), o = (int)(i - (size_t)t * OUT);
+    float v = 0.f;
+    for (int s = 0; s < p.ksplit; ++s) v += p.ws[(size_t)s * p.T * OUT + i];
+    v += p.W.bias[o];
+    const QkvDest qd = EPI == EPI_QKV ? qkv_dest(p, t) : QkvDest{0, 0, false};
+    gemm_store<EPI>(p, t, o, v, qd);
+}
+
 // fp16 copy of a tiled int8 linear: w16[o][k] = fp16(s * q + b), the value the int8
 // GEMMs compute in registers or shared memory (rows past `out` are not written).
 __global__ void dequant_f16_kernel(MkLin W, __half *w16) {
@@ -659,13 +702,28 @@ bool launch_gemm_f16(int epi, const GemmParams &p, const __half *w16, cudaStream
     int dev = 0, sms = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    GemmParams q = p;
     const int tiles = ((p.T + HB_BM - 1) / HB_BM) * ((p.W.out + HB_BN - 1) / HB_BN);
-    const dim3 grid((unsigned)std::min(tiles, sms));
+    // few output tiles (a decode step of many columns): split K so that every SM streams
+    // part of the weights; the partial sums meet in the workspace
+    q.ksplit = 1;
+    if (tiles < sms && p.ws && p.ws_splits > 1)
+        q.ksplit = std::min({(sms + tiles - 1) / tiles, K / HB_BK, p.ws_splits});
+    const dim3 grid((unsigned)std::min(tiles * q.ksplit, sms));
     switch (epi) {
-    case EPI_PLAIN: gemm_f16_tc_kernel<EPI_PLAIN><<<grid, HB_THREADS, HB_SMEM, st>>>(p, ma, mb); break;
-    case EPI_GELU: gemm_f16_tc_kernel<EPI_GELU><<<grid, HB_THREADS, HB_SMEM, st>>>(p, ma, mb); break;
-    case EPI_RESID: gemm_f16_tc_kernel<EPI_RESID><<<grid, HB_THREADS, HB_SMEM, st>>>(p, ma, mb); break;
-    default: gemm_f16_tc_kernel<EPI_QKV><<<grid, HB_THREADS, HB_SMEM, st>>>(p, ma, mb); break;
+    case EPI_PLAIN: gemm_f16_tc_kernel<EPI_PLAIN><<<grid, HB_THREADS, HB_SMEM, st>>>(q, ma, mb); break;
+    case EPI_GELU: gemm_f16_tc_kernel<EPI_GELU><<<grid, HB_THREADS, HB_SMEM, st>>>(q, ma, mb); break;
+    case EPI_RESID: gemm_f16_tc_kernel<EPI_RESID><<<grid, HB_THREADS, HB_SMEM, st>>>(q, ma, mb); break;
+    default: gemm_f16_tc_kernel<EPI_QKV><<<grid, HB_THREADS, HB_SMEM, st>>>(q, ma, mb); break;
+    }
+    if (q.ksplit > 1) {
+        const unsigned blocks = (unsigned)(((size_t)p.T * p.W.out + 255) / 256);
+        switch (epi) {
+        case EPI_PLAIN: gemm_splitk_epilogue<EPI_PLAIN><<<blocks, 256, 0, st>>>(q); break;
+        case EPI_GELU: gemm_splitk_epilogue<EPI_GELU><<<blocks, 256, 0, st>>>(q); break;
+        case EPI_RESID: gemm_splitk_epilogue<EPI_RESID><<<blocks, 256, 0, st>>>(q); break;
+        default: gemm_splitk_epilogue<EPI_QKV><<<blocks, 256, 0, st>>>(q); break;
+        }
     }
     return true;
 }

@@ -38,6 +38,8 @@ struct DecodeBufs {
     int *err;
     unsigned long long *trace;  // optional per-CTA stage timestamps
     int mk_grid, mk_nslot[MK_MAX_NB + 1];
+    float *ws;      // split-K partial sums of the fp16 GEMM: [ws_splits][max_batch][max(3d, ff)]
+    int ws_splits;
 };
 
 // Prefill scratch for one request of up to max_tokens positions.
@@ -81,9 +83,11 @@ void launch_layernorm_rows_h(const float *x, const float *w, const float *b, int
 // for EPI_GELU).  In decode mode (dv != null) the QKV epilogue appends row t's K/V to slot
 // batch_slot[t] at its valid_len; in prefill mode (dv == null, kv_slot >= 0) row t's K/V go
 // to position t of kv_slot.
+// ws / ws_splits: split-K workspace for the fp16 GEMM on few rows (decode steps of many
+// columns), used when the weight's fp16 copy exists.
 void launch_gemm(int epi, const MkLin &W, const __half *x, void *y, int T, const DecodeView *dv,
                  __half *k_cache, __half *v_cache, int kv_slot, int n_slots, int n_heads,
-                 int max_seq, int layer, int d, cudaStream_t st);
+                 int max_seq, int layer, int d, cudaStream_t st, float *ws = nullptr, int ws_splits = 0);
 
 // Decode forward for dv.nb columns: the persistent kernel when nb <= MK_MAX_NB (one
 // launch), else the GEMM path (embedding, 7 launches per layer, head).

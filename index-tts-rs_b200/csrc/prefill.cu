@@ -85,13 +85,68 @@ __global__ void __launch_bounds__(256) layernorm_rows_kernel(const float *x, con
     }
 }
 
+// The same with one warp per row (d a multiple of 128, at most 128 * LNW_CH): the row
+// stays in registers (float4 chunks c * 128 + 4 lane), two-pass statistics over them.
+constexpr int LNW_CH = 16;
+template <typename TY>
+__global__ void __launch_bounds__(256) layernorm_rows_warp_kernel(const float *x, const float *w,
+                                                                  const float *b, int rows, int d, TY *y) {
+    const int t = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (t >= rows) return;
+    const int nch = d / 128;
+    const float4 *row = reinterpret_cast<const float4 *>(x + (size_t)t * d);
+    float4 v[LNW_CH];
+    float s = 0.f;
+#pragma unroll
+    for (int c = 0; c < LNW_CH; ++c) {
+        if (c >= nch) break;
+        v[c] = row[c * 32 + lane];
+        s += (v[c].x + v[c].y) + (v[c].z + v[c].w);
+    }
+    const float mean = warp_sum(s) / (float)d;
+    float q = 0.f;
+#pragma unroll
+    for (int c = 0; c < LNW_CH; ++c) {
+        if (c >= nch) break;
+        const float a0 = v[c].x - mean, a1 = v[c].y - mean, a2 = v[c].z - mean, a3 = v[c].w - mean;
+        q += (a0 * a0 + a1 * a1) + (a2 * a2 + a3 * a3);
+    }
+    const float rstd = 1.0f / sqrtf(warp_sum(q) / (float)d + kNormEps);
+#pragma unroll
+    for (int c = 0; c < LNW_CH; ++c) {
+        if (c >= nch) break;
+        const int k = c * 128 + 4 * lane;
+        const float4 ww = *reinterpret_cast<const float4 *>(w + k), bb = *reinterpret_cast<const float4 *>(b + k);
+        const float o0 = (v[c].x - mean) * rstd * ww.x + bb.x, o1 = (v[c].y - mean) * rstd * ww.y + bb.y;
+        const float o2 = (v[c].z - mean) * rstd * ww.z + bb.z, o3 = (v[c].w - mean) * rstd * ww.w + bb.w;
+        if constexpr (sizeof(TY) == 2) {
+            const __half2 h01 = __floats2half2_rn(o0, o1), h23 = __floats2half2_rn(o2, o3);
+            uint2 hv;
+            hv.x = *reinterpret_cast<const uint32_t *>(&h01);
+            hv.y = *reinterpret_cast<const uint32_t *>(&h23);
+            *reinterpret_cast<uint2 *>(y + (size_t)t * d + k) = hv;
+        } else {
+            *reinterpret_cast<float4 *>(y + (size_t)t * d + k) = make_float4(o0, o1, o2, o3);
+        }
+    }
+}
+
+template <typename TY>
+static void launch_ln(const float *x, const float *w, const float *b, int rows, int d, TY *y, cudaStream_t st) {
+    const bool aligned = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) |
+                           reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(b)) & 15) == 0;
+    if (d % 128 == 0 && d <= 128 * LNW_CH && aligned)
+        layernorm_rows_warp_kernel<TY><<<(rows + 7) / 8, 256, 0, st>>>(x, w, b, rows, d, y);
+    else
+        layernorm_rows_kernel<TY><<<rows, 256, 0, st>>>(x, w, b, d, y);
+}
 void launch_layernorm_rows(const float *x, const float *w, const float *b, int rows, int d,
                            float *y, cudaStream_t st) {
-    layernorm_rows_kernel<float><<<rows, 256, 0, st>>>(x, w, b, d, y);
+    launch_ln<float>(x, w, b, rows, d, y, st);
 }
 void launch_layernorm_rows_h(const float *x, const float *w, const float *b, int rows, int d,
                              __half *y, cudaStream_t st) {
-    layernorm_rows_kernel<__half><<<rows, 256, 0, st>>>(x, w, b, d, y);
+    launch_ln<__half>(x, w, b, rows, d, y, st);
 }
 
 // ---------------------------------------------------------------------------
@@ -185,7 +240,7 @@ constexpr int kGemmTcMinRows = 16;
 
 void launch_gemm(int epi, const MkLin &W, const __half *x, void *y, int T, const DecodeView *dv,
                  __half *k_cache, __half *v_cache, int kv_slot, int n_slots, int n_heads,
-                 int max_seq, int layer, int d, cudaStream_t st) {
+                 int max_seq, int layer, int d, cudaStream_t st, float *ws, int ws_splits) {
     GemmParams p{};
     p.W = W;
     p.x = x;
@@ -203,7 +258,9 @@ void launch_gemm(int epi, const MkLin &W, const __half *x, void *y, int T, const
         p.slots = dv->slots;
         p.batch_slot = dv->batch_slot;
     }
-    if (T >= kGemmF16MinRows && W.w16 && launch_gemm_f16(epi, p, W.w16, st)) return;
+    p.ws = ws;
+    p.ws_splits = ws_splits;
+    if (W.w16 && (T >= kGemmF16MinRows || (ws && T >= kGemmTcMinRows)) && launch_gemm_f16(epi, p, W.w16, st)) return;
     if (T >= kGemmTcMinRows && launch_gemm_tc(epi, p, st)) return;
     dim3 grid((W.out + 63) / 64, (T + 63) / 64);
     switch (epi) {
