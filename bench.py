@@ -380,6 +380,23 @@ def run_profile_prefill(args):
                       "repeats": args.profile_prefill, "last_wall_ms": 1000.0 * dt}), flush=True)
 
 
+def run_profile_generate(args):
+    """A case for profilers: cfg2's prompt and sampling, `--profile-generate` tokens (the
+    decode step and the sampler launch once per token)."""
+    import itts_gpt as ig
+    cfg, w = make_model()
+    gpt = ig.Gpt.from_weights(w)
+    text, conds = make_prompt(cfg, 0)
+    n = args.profile_generate
+    kv = ig.KvCache(gpt, max_seq=N_CONDS + N_TEXT + 3 + n + 8, max_batch=1)
+    params = ig.SamplingParams(max_mel_tokens=n, **SAMPLING)
+    codes = ig.generate_codes_after(gpt, ig.CodePrompt(text, conds, LANG, min_codes=n), kv, params,
+                                    ig.SamplerRng(1))
+    pf, dc, nl = gpt.last_timing()
+    print(json.dumps({"profile_case": "cfg2 generate", "tokens": len(codes), "prefill_ms": pf,
+                      "decode_ms": dc, "ms_per_step": dc / max(1, len(codes) - 1)}), flush=True)
+
+
 def run_profile_prefill_batch(args):
     """A case for profilers: the cfg4 prefill, N_REQ prompts of 32 conditioning latents +
     600 text tokens (635 positions each) in one packed prefill, run twice."""
@@ -416,6 +433,8 @@ def main():
     ap.add_argument("--profile-nb", type=int, default=1, help="batch columns of --profile-decode")
     ap.add_argument("--profile-prefill", type=int, default=0, metavar="REPEATS",
                     help="profiler case: only cfg2 prefills, this many")
+    ap.add_argument("--profile-generate", type=int, default=0, metavar="TOKENS",
+                    help="profiler case: one cfg2 generate of this many tokens")
     ap.add_argument("--profile-prefill-batch", type=int, default=0, metavar="N_REQ",
                     help="profiler case: the cfg4 packed prefill of N_REQ prompts, twice")
     args = ap.parse_args()
@@ -427,6 +446,9 @@ def main():
         return
     if args.profile_prefill_batch > 0:
         run_profile_prefill_batch(args)
+        return
+    if args.profile_generate > 0:
+        run_profile_generate(args)
         return
     rank, world, local_rank = dist_env()
     if world > 1:

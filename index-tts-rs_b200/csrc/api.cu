@@ -28,6 +28,7 @@
 
 namespace itts {
 void kernels_init_sample();
+bool sample_small_ok(const itts_sampling_params &p, int n_logits);  // sample.cu
 void kernels_init_gemm_tc();
 }  // namespace itts
 
@@ -719,9 +720,9 @@ extern "C" int itts_kv_create(itts_gpt *g, int32_t max_seq, int32_t max_batch, i
         kv_destroy(kv);
         return set_err(ITTS_E_CUDA, msg);
     }
-    kv->graphs.assign(max_batch + 1, nullptr);
-    kv->graph_defs.assign(max_batch + 1, nullptr);
-    kv->graph_failed.assign(max_batch + 1, 0);
+    kv->graphs.assign(2 * (max_batch + 1), nullptr);
+    kv->graph_defs.assign(2 * (max_batch + 1), nullptr);
+    kv->graph_failed.assign(2 * (max_batch + 1), 0);
     *out = kv;
     return ITTS_OK;
 }
@@ -1243,6 +1244,7 @@ extern "C" int itts_sample_next_token(itts_gpt *g, float *logits, int32_t n,
     a.write_back = 1;
     a.codes = nullptr;
     a.token_out = g->d_sidx + 1;
+    a.small_k = sample_small_ok(*params, n);
     launch_sample(a, st);
     CUDA_TRY(cudaGetLastError());
     CUDA_TRY(cudaMemcpyAsync(logits, g->d_slogits, sizeof(float) * n, cudaMemcpyDeviceToHost, st));
@@ -1258,7 +1260,7 @@ extern "C" int itts_sample_next_token(itts_gpt *g, float *logits, int32_t n,
 // decode loop (sampler.rs:340-392): prefill every request, sample, then replay the
 // captured decode step until every request stopped.
 // ------------------------------------------------------------------------------
-static void launch_step_sample(itts_kv *kv, int nb, cudaStream_t st) {
+static void launch_step_sample(itts_kv *kv, int nb, int small_k, cudaStream_t st) {
     itts_gpt *g = kv->gpt;
     SampleArgs a{};
     a.slots = kv->d_slots;
@@ -1271,19 +1273,22 @@ static void launch_step_sample(itts_kv *kv, int nb, cudaStream_t st) {
     a.write_back = 0;
     a.codes = kv->d_codes;
     a.codes_stride = kv->codes_stride;
+    a.small_k = small_k;
     launch_sample(a, st);
 }
 
-// One decode step (forward + sampler) captured as a CUDA graph per batch size.
-static int get_graph(itts_kv *kv, int nb, cudaGraphExec_t *out) {
-    if (kv->graphs[nb]) { *out = kv->graphs[nb]; return ITTS_OK; }
+// One decode step (forward + sampler) captured as a CUDA graph per batch size and sampler
+// variant (small_k: the top-k <= 64 kernel), cached at index 2 nb + small_k.
+static int get_graph(itts_kv *kv, int nb, int small_k, cudaGraphExec_t *out) {
+    const int gi = 2 * nb + small_k;
+    if (kv->graphs[gi]) { *out = kv->graphs[gi]; return ITTS_OK; }
     itts_gpt *g = kv->gpt;
     cudaStream_t st = g->stream;
     cudaGraph_t graph = nullptr;
     CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
     DecodeView dv = decode_view(kv, nb);
     const cudaError_t fe = decode_forward(g->m, dv, kv->db, st);
-    launch_step_sample(kv, nb, st);
+    launch_step_sample(kv, nb, small_k, st);
     const cudaError_t ce = cudaStreamEndCapture(st, &graph);
     if (fe != cudaSuccess || ce != cudaSuccess) {
         if (graph) cudaGraphDestroy(graph);
@@ -1293,8 +1298,8 @@ static int get_graph(itts_kv *kv, int nb, cudaGraphExec_t *out) {
     }
     cudaGraphExec_t exec = nullptr;
     CUDA_TRY(cudaGraphInstantiate(&exec, graph, 0));
-    kv->graph_defs[nb] = graph;
-    kv->graphs[nb] = exec;
+    kv->graph_defs[gi] = graph;
+    kv->graphs[gi] = exec;
     *out = exec;
     return ITTS_OK;
 }
@@ -1348,9 +1353,11 @@ static int generate_impl(itts_gpt *g, itts_kv *kv, int n, const int *slots,
     TRY(set_batch_slots(kv, slots, n));
     TRY(reset_step_sync(kv));
     if (n > MK_MAX_NB) ensure_weights_f16(g);  // wide steps run the fp16 GEMM (made before capture)
+    int small_k = 1;  // every request greedy or with top_k <= 64: the small-k sampler
+    for (int r = 0; r < n; ++r) small_k &= sample_small_ok(params[(size_t)r * params_stride], m.mel_vocab) ? 1 : 0;
     cudaGraphExec_t graph = nullptr;
-    if (!kv->graph_failed[n] && get_graph(kv, n, &graph) != ITTS_OK) {
-        kv->graph_failed[n] = 1;  // e.g. a cooperative launch the driver cannot capture
+    if (!kv->graph_failed[2 * n + small_k] && get_graph(kv, n, small_k, &graph) != ITTS_OK) {
+        kv->graph_failed[2 * n + small_k] = 1;  // e.g. a cooperative launch the driver cannot capture
         graph = nullptr;
     }
     DecodeView step_dv = decode_view(kv, n);
@@ -1365,6 +1372,7 @@ static int generate_impl(itts_gpt *g, itts_kv *kv, int n, const int *slots,
     a.write_back = 0;
     a.codes = kv->d_codes;
     a.codes_stride = kv->codes_stride;
+    a.small_k = small_k;
     launch_sample(a, st);
     CUDA_TRY(cudaGetLastError());
     int launched = 0, chunk = 8;
@@ -1379,7 +1387,7 @@ static int generate_impl(itts_gpt *g, itts_kv *kv, int n, const int *slots,
                 CUDA_TRY(cudaGraphLaunch(graph, st));
             } else {
                 CUDA_TRY(decode_forward(m, step_dv, kv->db, st));
-                launch_step_sample(kv, n, st);
+                launch_step_sample(kv, n, small_k, st);
             }
         }
         launched += todo;
@@ -1602,6 +1610,7 @@ extern "C" int itts_sample_next_token_static(float *logits, int32_t n, const uin
     a.write_back = 1;
     a.codes = nullptr;
     a.token_out = d_idx + 1;
+    a.small_k = sample_small_ok(*params, n);
     launch_sample(a, st);
     CUDA_TRY(cudaGetLastError());
     CUDA_TRY(cudaMemcpyAsync(logits, d_logits, sizeof(float) * n, cudaMemcpyDeviceToHost, st));

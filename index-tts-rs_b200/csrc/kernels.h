@@ -150,6 +150,7 @@ struct SampleArgs {
     int32_t *codes;     // [n_slots][codes_stride]
     int codes_stride;
     int32_t *token_out; // optional [nb]
+    int small_k;        // every column is greedy or has top_k in 1..64 (below n_logits)
 };
 void launch_sample(const SampleArgs &a, cudaStream_t st);
 
