@@ -694,6 +694,7 @@ extern "C" int itts_kv_create(itts_gpt *g, int32_t max_seq, int32_t max_batch, i
         if (e == cudaSuccess) e = cudaMemsetAsync(kv->db.epoch, 0, sizeof(uint32_t) * std::max(grid, 1024), g->stream);
         A((void **)&kv->db.err, sizeof(int) * 4);
         kv->db.trace = nullptr;
+        kv->db.ck_rt = ck_config(m);
     }
     A((void **)&kv->pb.x, sizeof(float) * (size_t)max_seq * m.d);
     A((void **)&kv->pb.n, sizeof(float) * (size_t)max_seq * m.d);
@@ -746,6 +747,12 @@ extern "C" int itts_kv_valid_len(const itts_kv *kv, int32_t slot, int32_t *out) 
 
 extern "C" int32_t itts_kv_max_seq(const itts_kv *kv) { return kv ? kv->max_seq : 0; }
 extern "C" int32_t itts_kv_max_batch(const itts_kv *kv) { return kv ? kv->max_batch : 0; }
+extern "C" int32_t itts_kv_decode_kernel(const itts_kv *kv, int32_t n_columns) {
+    if (!kv || n_columns < 1 || n_columns > kv->max_batch) return 0;
+    if (n_columns == 1 && kv->db.ck_rt > 0) return 1;
+    if (n_columns <= MK_MAX_NB && kv->db.mk_grid > 0 && kv->db.mk_nslot[n_columns] >= 2) return 2;
+    return 3;
+}
 
 static DecodeView decode_view(itts_kv *kv, int nb) {
     const ModelView &m = kv->gpt->m;

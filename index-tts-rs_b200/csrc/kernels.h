@@ -40,6 +40,7 @@ struct DecodeBufs {
     int mk_grid, mk_nslot[MK_MAX_NB + 1];
     float *ws;      // split-K partial sums of the fp16 GEMM: [ws_splits][max_batch][max(3d, ff)]
     int ws_splits;
+    int ck_rt;      // > 0: batch-1 steps run on one 16-CTA cluster (ck_decode.cu)
 };
 
 // Prefill scratch for one request of up to max_tokens positions.
@@ -93,6 +94,10 @@ void launch_gemm(int epi, const MkLin &W, const __half *x, void *y, int T, const
 // launch), else the GEMM path (embedding, 7 launches per layer, head).
 cudaError_t decode_forward(const ModelView &m, const DecodeView &dv, DecodeBufs &b,
                            cudaStream_t st);
+// Decode step of one batch column on one 16-CTA thread-block cluster: returns the
+// partial-sum size it needs (> 0) or -1 when the model or the device does not fit it.
+int ck_config(const ModelView &m);
+cudaError_t ck_launch(const MkParams &p, int rt, cudaStream_t st);
 // Number of kernels decode_forward launches for nb columns.
 int decode_forward_launches(const ModelView &m, const DecodeBufs &b, int nb);
 

@@ -62,6 +62,7 @@ SIGNATURES = [
     ("itts_kv_valid_len", C.c_int, [_P, _I32, C.POINTER(_I32)]),
     ("itts_kv_max_seq", _I32, [_P]),
     ("itts_kv_max_batch", _I32, [_P]),
+    ("itts_kv_decode_kernel", _I32, [_P, _I32]),
     ("itts_gpt_prefill", C.c_int, [_P, _P, _I32, _P, _I32, _P, _I32, _I32, _P, _I32, _P]),
     ("itts_gpt_step", C.c_int, [_P, _P, _I32, _P, _P, _P, _P]),
     ("itts_gpt_teacher_forced", C.c_int,
