@@ -607,36 +607,58 @@ struct CkConsumer {
                     wait_slot(slot, 3);
                     const __half *kt = reinterpret_cast<const __half *>(smem + slot * SLOT);
                     const __half *vt = kt + np * 64;
-                    for (int gi = warp; gi * 4 < np; gi += CW) {
-                        const int pos = gi * 4 + grp;
-                        const bool in = pos < np;
-                        const int pc = in ? pos : 0;
-                        const uint4 kk = *reinterpret_cast<const uint4 *>(kt + pc * 64 + d8 * 8);
-                        const __half2 *k2 = reinterpret_cast<const __half2 *>(&kk);
-                        float s = 0.f;
+                    // this warp's position groups gi = warp + 8 q (4 positions each, 8 lanes
+                    // per position): scores first, then one rescale per tile
+                    constexpr int QG = (KVPOS / 4 + CW - 1) / CW;
+                    float sc[QG];
+                    uint4 vv[QG];
 #pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const float2 kf = __half22float2(k2[e]);
-                            s = fmaf(qv[2 * e], kf.x, s);
-                            s = fmaf(qv[2 * e + 1], kf.y, s);
+                    for (int q = 0; q < QG; ++q) {
+                        const int pos = (warp + q * CW) * 4 + grp;
+                        const int pc = pos < np ? pos : 0;
+                        const uint4 kk = *reinterpret_cast<const uint4 *>(kt + pc * 64 + d8 * 8);
+                        vv[q] = *reinterpret_cast<const uint4 *>(vt + pc * 64 + d8 * 8);
+                        const __half2 *k2 = reinterpret_cast<const __half2 *>(&kk);
+                        float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+                        for (int e = 0; e < 4; e += 2) {
+                            const float2 ka = __half22float2(k2[e]), kb = __half22float2(k2[e + 1]);
+                            s0 = fmaf(qv[2 * e], ka.x, s0);
+                            s1 = fmaf(qv[2 * e + 1], ka.y, s1);
+                            s0 = fmaf(qv[2 * e + 2], kb.x, s0);
+                            s1 = fmaf(qv[2 * e + 3], kb.y, s1);
                         }
-                        s += __shfl_xor_sync(0xffffffffu, s, 1);
-                        s += __shfl_xor_sync(0xffffffffu, s, 2);
-                        s += __shfl_xor_sync(0xffffffffu, s, 4);
-                        if (in) {
-                            const uint4 vv = *reinterpret_cast<const uint4 *>(vt + pc * 64 + d8 * 8);
-                            const __half2 *v2 = reinterpret_cast<const __half2 *>(&vv);
-                            const float mn = fmaxf(m, s);
-                            const float corr = exp2f(m - mn);  // m = -inf gives 0
-                            const float pj = exp2f(s - mn);
-                            ls = ls * corr + pj;
+                        sc[q] = s0 + s1;
+                    }
+#pragma unroll
+                    for (int q = 0; q < QG; ++q) sc[q] += __shfl_xor_sync(0xffffffffu, sc[q], 1);
+#pragma unroll
+                    for (int q = 0; q < QG; ++q) sc[q] += __shfl_xor_sync(0xffffffffu, sc[q], 2);
+#pragma unroll
+                    for (int q = 0; q < QG; ++q) sc[q] += __shfl_xor_sync(0xffffffffu, sc[q], 4);
+                    float mt = m;
+#pragma unroll
+                    for (int q = 0; q < QG; ++q)
+                        if ((warp + q * CW) * 4 + grp < np) mt = fmaxf(mt, sc[q]);
+                    if (mt != m) {  // a new maximum (m = -inf gives corr 0)
+                        const float corr = exp2f(m - mt);
+                        ls *= corr;
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) acc[e] *= corr;
+                        m = mt;
+                    }
+#pragma unroll
+                    for (int q = 0; q < QG; ++q) {
+                        if ((warp + q * CW) * 4 + grp < np) {
+                            const float pj = exp2f(sc[q] - m);
+                            ls += pj;
+                            const __half2 *v2 = reinterpret_cast<const __half2 *>(&vv[q]);
 #pragma unroll
                             for (int e = 0; e < 4; ++e) {
                                 const float2 f = __half22float2(v2[e]);
-                                acc[2 * e] = acc[2 * e] * corr + pj * f.x;
-                                acc[2 * e + 1] = acc[2 * e + 1] * corr + pj * f.y;
+                                acc[2 * e] = fmaf(pj, f.x, acc[2 * e]);
+                                acc[2 * e + 1] = fmaf(pj, f.y, acc[2 * e + 1]);
                             }
-                            m = mn;
                         }
                     }
                     __syncwarp();
@@ -933,7 +955,10 @@ __global__ void __launch_bounds__(NT, 1) ck_decode_kernel(const __grid_constant_
 static int ck_rt_of(const MkLin &L) { return (L.n_rb + CS - 1) / CS * L.n_kc; }
 
 int ck_config(const ModelView &m) {
-    if (getenv("ITTS_NO_CLUSTER")) return -1;
+    // opt-in: on B200 this kernel is slower than the grid-wide one (16 SMs do not issue the
+    // dequantization instructions of a step fast enough), so it runs only on request
+    const char *on = getenv("ITTS_CLUSTER");
+    if (!on || on[0] != '1') return -1;
     if (m.n_layers < 1 || m.d > MK_MAX_D || m.d % 64 || m.ff % 64 || m.n_heads * 64 != m.d ||
         m.n_heads > MAXHC * CS / 2)
         return -1;

@@ -94,8 +94,9 @@ void launch_gemm(int epi, const MkLin &W, const __half *x, void *y, int T, const
 // launch), else the GEMM path (embedding, 7 launches per layer, head).
 cudaError_t decode_forward(const ModelView &m, const DecodeView &dv, DecodeBufs &b,
                            cudaStream_t st);
-// Decode step of one batch column on one 16-CTA thread-block cluster: returns the
-// partial-sum size it needs (> 0) or -1 when the model or the device does not fit it.
+// Decode step of one batch column on one 16-CTA thread-block cluster (opt-in with
+// ITTS_CLUSTER=1 at cache creation): returns the partial-sum size it needs (> 0) or -1 when
+// it is not requested or the model or the device does not fit it.
 int ck_config(const ModelView &m);
 cudaError_t ck_launch(const MkParams &p, int rt, cudaStream_t st);
 // Number of kernels decode_forward launches for nb columns.

@@ -59,33 +59,27 @@ def _teacher_forced(gpt, om, cfg, n_text, n_conds, steps, seed, max_seq=1024):
     return np.stack(g), np.stack(r)
 
 
-def test_decode_kernel_selection(small):
+def test_decode_kernel_selection(small, monkeypatch):
     gpt, _ = small
-    kv1 = ig.KvCache(gpt, max_seq=256, max_batch=1)
-    assert kv1.decode_kernel(1) == "ck_decode_kernel"
     kv4 = ig.KvCache(gpt, max_seq=256, max_batch=8)
-    assert kv4.decode_kernel(1) == "ck_decode_kernel"
+    assert kv4.decode_kernel(1) == "mk_decode_kernel"
     assert kv4.decode_kernel(2) == "mk_decode_kernel"
     assert kv4.decode_kernel(5) == "gemm path"
+    monkeypatch.setenv("ITTS_CLUSTER", "1")
+    assert ig.KvCache(gpt, max_seq=256, max_batch=1).decode_kernel(1) == "ck_decode_kernel"
 
 
+@pytest.mark.parametrize("cluster", [False, True], ids=["grid", "cluster"])
 @pytest.mark.parametrize("n_text,steps", [(52, 70), (140, 60)])
-def test_teacher_forced_across_kv_tiles(small, small_cfg, n_text, steps):
-    """Decode steps whose KV length crosses the cluster kernel's 84-position K/V tiles
-    (and, for 4 heads on 16 CTAs, attention ranges with idle CTAs between a head's)."""
+def test_teacher_forced_across_kv_tiles(small, small_cfg, monkeypatch, cluster, n_text, steps):
+    """Decode steps whose KV length crosses 84-position K/V tiles (the cluster kernel's
+    tile; for 4 heads on 16 CTAs its attention ranges have idle CTAs between a head's),
+    on the grid-wide kernel and on the opt-in 16-CTA cluster kernel."""
     gpt, om = small
+    if cluster:
+        monkeypatch.setenv("ITTS_CLUSTER", "1")
+        assert ig.KvCache(gpt, max_seq=64).decode_kernel(1) == "ck_decode_kernel"
     g, r = _teacher_forced(gpt, om, small_cfg, n_text, 3, steps, seed=n_text)
-    for i in range(len(g)):
-        check_logits(g[i], r[i], f"step {i}")
-
-
-def test_teacher_forced_grid_kernel_small(small, small_cfg, monkeypatch):
-    """Batch-1 steps on the persistent grid-wide kernel (the path when no 16-CTA cluster
-    fits the device or the model)."""
-    gpt, om = small
-    monkeypatch.setenv("ITTS_NO_CLUSTER", "1")
-    assert ig.KvCache(gpt, max_seq=64).decode_kernel(1) == "mk_decode_kernel"
-    g, r = _teacher_forced(gpt, om, small_cfg, 20, 3, 30, seed=5)
     for i in range(len(g)):
         check_logits(g[i], r[i], f"step {i}")
 
@@ -342,9 +336,13 @@ def full():
     g.close()
 
 
-def test_full_size_teacher_forced(full):
+@pytest.mark.parametrize("cluster", [False, True], ids=["grid", "cluster"])
+def test_full_size_teacher_forced(full, monkeypatch, cluster):
     cfg, gpt, om = full
-    assert ig.KvCache(gpt, max_seq=512).decode_kernel(1) == "ck_decode_kernel"
+    if cluster:
+        monkeypatch.setenv("ITTS_CLUSTER", "1")
+    want = "ck_decode_kernel" if cluster else "mk_decode_kernel"
+    assert ig.KvCache(gpt, max_seq=512).decode_kernel(1) == want
     g, r = _teacher_forced(gpt, om, cfg, 64, 32, 24, seed=41, max_seq=512)
     errs = [check_logits(g[i], r[i], f"full step {i}") for i in range(len(g))]
     agree = np.mean(np.argmax(g, 1) == np.argmax(r, 1))
