@@ -609,6 +609,7 @@ static void kv_destroy(itts_kv *kv) {
     void *dev[] = {kv->k, kv->v, kv->d_slots, kv->d_batch_slot, kv->db.x, kv->db.n, kv->db.n2,
                    kv->db.q, kv->db.attn, kv->db.u, kv->db.logits, kv->db.partials,
                    kv->db.counters, kv->db.qkv_ll, kv->db.epoch, kv->db.err, kv->db.trace, kv->db.ws,
+                   kv->db.xkb.qkv_ll,
                    kv->pb.x, kv->pb.n, kv->pb.qkv, kv->pb.attn,
                    kv->pb.u, kv->d_codes, kv->d_text, kv->d_prior, kv->d_conds};
     for (void *p : dev) cudaFree(p);
@@ -695,6 +696,24 @@ extern "C" int itts_kv_create(itts_gpt *g, int32_t max_seq, int32_t max_batch, i
         A((void **)&kv->db.err, sizeof(int) * 4);
         kv->db.trace = nullptr;
         kv->db.ck_rt = ck_config(m);
+        kv->db.xk = XkConfig{};
+        XkConfig xc;
+        if (e == cudaSuccess && xk_config(m, &xc) > 0) {
+            const size_t L = m.n_layers;
+            const size_t words = L * (3 * (size_t)m.d + (size_t)xc.rec_stride * 68 + m.d + m.ff + (size_t)xc.nkc * m.d);
+            const size_t bytes = words * 8 + sizeof(uint32_t) * xc.grid;
+            A((void **)&kv->db.xkb.qkv_ll, bytes);
+            if (e == cudaSuccess) {
+                XkBufs &x = kv->db.xkb;
+                x.rec_ll = x.qkv_ll + L * 3 * m.d;
+                x.pv_ll = x.rec_ll + L * xc.rec_stride * 68;
+                x.u_ll = x.pv_ll + L * m.d;
+                x.mp_ll = x.u_ll + L * m.ff;
+                x.epoch = reinterpret_cast<uint32_t *>(x.mp_ll + L * xc.nkc * m.d);
+                e = cudaMemsetAsync(x.qkv_ll, 0, bytes, g->stream);
+                kv->db.xk = xc;
+            }
+        }
     }
     A((void **)&kv->pb.x, sizeof(float) * (size_t)max_seq * m.d);
     A((void **)&kv->pb.n, sizeof(float) * (size_t)max_seq * m.d);
@@ -750,6 +769,7 @@ extern "C" int32_t itts_kv_max_batch(const itts_kv *kv) { return kv ? kv->max_ba
 extern "C" int32_t itts_kv_decode_kernel(const itts_kv *kv, int32_t n_columns) {
     if (!kv || n_columns < 1 || n_columns > kv->max_batch) return 0;
     if (n_columns == 1 && kv->db.ck_rt > 0) return 1;
+    if (n_columns == 1 && kv->db.xk.grid > 0) return 4;
     if (n_columns <= MK_MAX_NB && kv->db.mk_grid > 0 && kv->db.mk_nslot[n_columns] >= 2) return 2;
     return 3;
 }

@@ -26,6 +26,16 @@ struct ModelView {
     const MkLayer *d_layers;  // the same, in device memory (persistent kernel)
 };
 
+// The clustered all-SM decode step of one column (xk_decode.cu): launch shape and its
+// global exchange buffers (LL words, tags unique per launch).
+struct XkConfig {
+    int grid = 0, rt = 0, nkc = 0, coop = 0, rec_stride = 0;
+};
+struct XkBufs {
+    uint64_t *qkv_ll = nullptr, *rec_ll = nullptr, *pv_ll = nullptr, *u_ll = nullptr, *mp_ll = nullptr;
+    uint32_t *epoch = nullptr;
+};
+
 // Decode-step scratch (sized for max_batch columns).
 struct DecodeBufs {
     float *x, *n, *n2, *q, *attn, *u, *logits;  // q holds [max_batch][3d] (QKV output)
@@ -41,6 +51,8 @@ struct DecodeBufs {
     float *ws;      // split-K partial sums of the fp16 GEMM: [ws_splits][max_batch][max(3d, ff)]
     int ws_splits;
     int ck_rt;      // > 0: batch-1 steps run on one 16-CTA cluster (ck_decode.cu)
+    XkConfig xk;    // grid > 0: batch-1 steps run on the clustered all-SM kernel (xk_decode.cu)
+    XkBufs xkb;
 };
 
 // Prefill scratch for one request of up to max_tokens positions.
@@ -98,6 +110,11 @@ cudaError_t decode_forward(const ModelView &m, const DecodeView &dv, DecodeBufs 
 // ITTS_CLUSTER=1 at cache creation): returns the partial-sum size it needs (> 0) or -1 when
 // it is not requested or the model or the device does not fit it.
 int ck_config(const ModelView &m);
+// Decode step of one column on (nearly) all SMs as 8-CTA clusters that gather each stage's
+// input once per cluster (default for batch 1; ITTS_XK=0 at cache creation turns it off).
+// Fills `out` and returns the grid size, or -1 when the model or the device does not fit it.
+int xk_config(const ModelView &m, XkConfig *out);
+cudaError_t xk_launch(const MkParams &p, const XkConfig &xc, const XkBufs &b, cudaStream_t st);
 cudaError_t ck_launch(const MkParams &p, int rt, cudaStream_t st);
 // Number of kernels decode_forward launches for nb columns.
 int decode_forward_launches(const ModelView &m, const DecodeBufs &b, int nb);

@@ -1,0 +1,1254 @@
+// xk_decode.cu -- the decode step of one request (batch column) on (almost) every SM,
+// launched as 8-CTA thread-block clusters (crates/core/src/models/gpt.rs:706-754): step
+// embedding, n_layers x [LN1 -> QKV -> KV append -> attention -> c_proj + residual -> LN2 ->
+// c_fc + GELU -> mlp c_proj + residual], ln_f -> final_norm -> mel_head.
+//
+// Each stage's output rows go to global memory as 64-bit LL words {fp32 value, stage tag}
+// (the tag is unique per launch, layer and stage, so no buffer is ever reset).  The next
+// stage's input vector is gathered ONCE per cluster instead of once per CTA: cluster rank k
+// polls the k-th eighth of the vector (finishing it on the way: residual add, K-split sum,
+// attention-partial merge, fp16 conversion) and pushes it into the shared memory of all 8
+// CTAs of its cluster with st.async; each CTA's mbarrier counts the bytes.  So a stage
+// boundary costs one L2 round trip for 1/8 of the vector plus one distributed-shared-memory
+// hop, and every SM keeps issuing the dequantization work of its 1-4 tiles per stage.
+//
+// Per CTA: 8 consumer warps + 1 producer warp.  The producer lane streams the CTA's weight
+// tiles (tile t of every linear belongs to CTA t % grid) and its range of old K/V rows into
+// an 8-slot cp.async.bulk ring (no multicast) ahead of the stages; consumers dequantize in
+// registers and run mma.sync m16n8k16 with the activation (the same arithmetic as the other
+// decode kernels), per-warp partial sums reduced once per tile.
+//
+// Buffer reuse: four vectors arrive per layer (x, attention output, h, u) into three
+// landing buffers (x and h share one).  A cluster peer can be at most one exchange ahead
+// of a CTA (finishing exchange e needs every peer's slice of e, sent only after that peer
+// finished exchange e-1), and each landing buffer is reused only two exchanges later, after
+// its previous contents were consumed.
+//
+// Every wait and poll is bounded; on a timeout the kernel records an error code in p.err
+// (read by the host as ITTS_E_TIMEOUT), skips the remaining waits and exits cleanly.
+#include <algorithm>
+#include <cstdio>
+#include <cstdlib>
+
+#include "kernels.h"
+#include "mk.h"
+
+namespace itts {
+namespace {
+
+constexpr int CS = 8;              // CTAs per cluster
+constexpr int CW = 8;              // consumer warps
+constexpr int CT = CW * 32;        // consumer threads
+constexpr int NT = CT + 32;        // + the producer warp
+constexpr int NSLOT = 8;           // ring slots (power of two)
+constexpr int SLOT = 21888;        // bytes per slot: a 16 x 1280 tile with fp16 pairs, or 84 K/V rows
+constexpr int KVPOS = 84;          // positions per K/V tile: 2 x 84 x 128 B = 21,504 B
+constexpr int MAXHC = 4;           // heads one CTA's attention range may touch
+constexpr int REC = 68;            // floats per attention record: m, l, 0, 0, acc[64]
+constexpr int MAXNR = 160;         // CTAs of the grid (SM count bound)
+constexpr int RCH = 32;            // attention records merged per round
+static_assert(MAXNR % 32 == 0, "scan layout");
+constexpr int NWS = 5;             // LL-writing stages per layer: qkv, records, c_proj, u, mlp
+constexpr uint32_t SPIN = 1u << 22;
+constexpr float kLog2e = 1.4426950408889634f;
+
+enum { B0 = 0, BAO, BU, NSTB };  // landing barriers: x/h (fp32), attention output, u (fp16)
+
+// ---------------------------------------------------------------------------
+// PTX helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t su32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mb_init(uint64_t *b, uint32_t n) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(n));
+}
+__device__ __forceinline__ void mb_expect(uint64_t *b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mb_arrive(uint64_t *b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
+}
+template <bool CLUSTER>
+__device__ __forceinline__ bool mb_try(uint32_t a, uint32_t par) {
+    uint32_t done;
+    if (CLUSTER)
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+            " selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done)
+            : "r"(a), "r"(par)
+            : "memory");
+    else
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done)
+            : "r"(a), "r"(par)
+            : "memory");
+    return done != 0;
+}
+template <bool CLUSTER>
+__device__ __forceinline__ bool mb_wait(uint64_t *b, uint32_t par, const int *err) {
+    const uint32_t a = su32(b);
+    for (uint32_t it = 0; it < SPIN; ++it) {
+        if (mb_try<CLUSTER>(a, par)) return true;
+        if ((it & 4095u) == 4095u && *(volatile const int *)err) return false;
+    }
+    return false;
+}
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar, uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(dst),
+        "l"(src), "r"(bytes), "r"(bar), "l"(pol)
+        : "memory");
+}
+__device__ __forceinline__ uint32_t mapa(uint32_t a, int rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void st_async_v4(uint32_t raddr, uint4 v, uint32_t rbar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(raddr),
+                 "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "r"(rbar)
+                 : "memory");
+}
+// the same 16 bytes into every CTA of the cluster
+__device__ __forceinline__ void bcast_v4(uint32_t laddr, uint4 v, uint32_t lbar) {
+#pragma unroll
+    for (int r = 0; r < CS; ++r) st_async_v4(mapa(laddr, r), v, mapa(lbar, r));
+}
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"n"(CT) : "memory"); }
+__device__ __forceinline__ bool csync_and(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, 1, %2, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+        : "=r"(r)
+        : "r"((uint32_t)v), "n"(CT)
+        : "memory");
+    return r != 0;
+}
+__device__ __forceinline__ void mma16816(float *d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t lo_h(uint32_t w) { return __byte_perm(w, 0x64646464u, 0x4140u); }
+__device__ __forceinline__ uint32_t hi_h(uint32_t w) { return __byte_perm(w, 0x64646464u, 0x4342u); }
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+// LL words: low 32 bits the fp32 value, high 32 bits the tag of the writing stage
+__device__ __forceinline__ uint64_t ll_word(float v, uint32_t tag) {
+    return ((uint64_t)tag << 32) | (uint64_t)__float_as_uint(v);
+}
+__device__ __forceinline__ void ll_st2(uint64_t *p, float a, float b, uint32_t tag) {
+    asm volatile("st.relaxed.gpu.global.v2.b64 [%0], {%1, %2};" ::"l"(p), "l"(ll_word(a, tag)), "l"(ll_word(b, tag))
+                 : "memory");
+}
+__device__ __forceinline__ void ll_ld2(const uint64_t *p, uint64_t &a, uint64_t &b) {
+    asm volatile("ld.relaxed.gpu.global.v2.b64 {%0,%1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+__device__ __forceinline__ float ll_val(uint64_t w) { return __uint_as_float((uint32_t)w); }
+__device__ __forceinline__ bool ll_ok(uint64_t w, uint32_t tag) { return (uint32_t)(w >> 32) == tag; }
+
+// Polls up to N pairs of LL words (16-byte aligned; ptr(j) == nullptr: none) until every
+// tag equals `tag`; out(j, a, b) receives each pair.  All loads of a round are issued
+// before any check.  False on timeout or when another CTA raised the error word.
+template <int N, class P, class O>
+__device__ __forceinline__ bool poll_pairs(P ptr, uint32_t tag, O out, const int *err) {
+    uint32_t pending = 0;
+#pragma unroll
+    for (int j = 0; j < N; ++j)
+        if (ptr(j)) pending |= 1u << j;
+    for (uint32_t it = 0; pending; ++it) {
+        uint64_t w[N][2];
+#pragma unroll
+        for (int j = 0; j < N; ++j)
+            if ((pending >> j) & 1u) ll_ld2(ptr(j), w[j][0], w[j][1]);
+#pragma unroll
+        for (int j = 0; j < N; ++j)
+            if (((pending >> j) & 1u) && ll_ok(w[j][0], tag) && ll_ok(w[j][1], tag)) {
+                out(j, ll_val(w[j][0]), ll_val(w[j][1]));
+                pending &= ~(1u << j);
+            }
+        if (pending) {
+            if (it >= SPIN || ((it & 255u) == 255u && *(volatile const int *)err)) return false;
+            __nanosleep(it < 4 ? 32u : (it < 16 ? 64u : 128u));
+        }
+    }
+    return true;
+}
+
+// A list of runs of LL word pairs: pair i (flattened over the runs) of run r lives at
+// src + 2 (i - start).  One out-of-line routine polls them all, so the many exchanges of a
+// layer share one copy of the polling code.
+struct PollRun {
+    const uint64_t *src;
+    int start, pad;
+};
+constexpr int MAXRUN = 16;
+constexpr int PPJ = 4;  // pairs per thread per round
+
+// Polls pairs [0, total) until every tag equals `tag`; pair i's values go to stage[2i],
+// stage[2i + 1].  Called by all consumer threads; false on a timeout or a raised error word.
+__device__ __noinline__ bool poll_runs(const PollRun *runs, int nruns, int total, uint32_t tag, float *stage,
+                                       const int *err) {
+    const int tid = threadIdx.x;
+    for (int base = 0; base < total; base += CT * PPJ) {
+        const uint64_t *adr[PPJ];
+        uint32_t pending = 0;
+#pragma unroll
+        for (int j = 0; j < PPJ; ++j) {
+            const int i = base + tid + j * CT;
+            adr[j] = nullptr;
+            if (i < total) {
+                int r = 0;
+                while (r + 1 < nruns && i >= runs[r + 1].start) ++r;
+                adr[j] = runs[r].src + 2 * (i - runs[r].start);
+                pending |= 1u << j;
+            }
+        }
+        for (uint32_t it = 0; pending; ++it) {
+            uint64_t w[PPJ][2];
+#pragma unroll
+            for (int j = 0; j < PPJ; ++j)
+                if ((pending >> j) & 1u) ll_ld2(adr[j], w[j][0], w[j][1]);
+#pragma unroll
+            for (int j = 0; j < PPJ; ++j)
+                if (((pending >> j) & 1u) && ll_ok(w[j][0], tag) && ll_ok(w[j][1], tag)) {
+                    const int i = base + tid + j * CT;
+                    stage[2 * i] = ll_val(w[j][0]);
+                    stage[2 * i + 1] = ll_val(w[j][1]);
+                    pending &= ~(1u << j);
+                }
+            if (pending) {
+                if (it >= SPIN || ((it & 255u) == 255u && *(volatile const int *)err)) return false;
+                __nanosleep(it < 4 ? 32u : (it < 16 ? 64u : 128u));
+            }
+        }
+    }
+    return true;
+}
+
+// ---------------------------------------------------------------------------
+// shared-memory carve-up (identical on host and device)
+// ---------------------------------------------------------------------------
+struct XkSmem {
+    uint32_t land, xln, xao, xu, sxln, sxao, sxu, red, qkvh, stat, tab, bar, total;
+};
+__host__ __device__ inline uint32_t xk_red_bytes(int rt) {
+    const uint32_t lin = (uint32_t)rt * CW * 16 * 4;
+    const uint32_t att = (uint32_t)(MAXHC * CW * REC + MAXHC * REC) * 4;
+    const uint32_t mrg = (uint32_t)(RCH * REC + MAXHC * 32) * 4 + 128;
+    uint32_t m = lin > att ? lin : att;
+    return m > mrg ? m : mrg;
+}
+struct XkTab {
+    int active, lold, kvt, units, slot, tok, pos, u_lo, u_hi, hlo, nh, seg0, nseg, pad[3];
+    int hs0[33];                 // first attention segment of head h (hs0[H] = total)
+    int cnt[MAXNR], hl[MAXNR];   // per CTA of the grid: heads its range touches, first head
+    PollRun runs[MAXRUN];        // the current poll list
+};
+__host__ __device__ inline XkSmem xk_layout(int d, int ff, int rt) {
+    XkSmem L;
+    uint32_t o = NSLOT * SLOT;
+    auto take = [&](uint32_t bytes) {
+        const uint32_t at = o;
+        o = (o + bytes + 127u) & ~127u;
+        return at;
+    };
+    L.land = take(d * 4);
+    L.xln = take(d * 2);
+    L.xao = take(d * 2);
+    L.xu = take(ff * 2);
+    L.sxln = take(d / 64 * 4);
+    L.sxao = take(d / 64 * 4);
+    L.sxu = take(ff / 64 * 4);
+    L.red = take(xk_red_bytes(rt));
+    L.qkvh = take(MAXHC * 3 * 64 * 4);
+    L.stat = take(64 * 4);
+    L.tab = take(sizeof(XkTab));
+    L.bar = take((2 * NSLOT + NSTB) * 8);
+    L.total = o;
+    return L;
+}
+
+struct XkParams {
+    MkParams p;          // model, slots, KV cache, logits, err, trace
+    uint64_t *qkv_ll;    // [L][3d]
+    uint64_t *rec_ll;    // [L][rec_stride][REC]
+    uint64_t *pv_ll;     // [L][d]     c_proj output + bias
+    uint64_t *u_ll;      // [L][ff]    GELU(c_fc)
+    uint64_t *mp_ll;     // [L][nkc][d] mlp c_proj K-chunk partial sums
+    uint32_t *epoch;     // [grid] launches completed per CTA
+    int rt, nkc, rec_stride, dry;
+};
+
+// ---------------------------------------------------------------------------
+// producer (one lane)
+// ---------------------------------------------------------------------------
+struct XkProducer {
+    uint32_t ring, full;
+    uint64_t *fullp, *emptyp;
+    const int *err;
+    uint64_t pol;
+    uint32_t seq;
+    int R, NR;
+    bool ok;
+
+    __device__ __forceinline__ void issue(const void *s0, uint32_t b0, const void *s1, uint32_t b1) {
+        const uint32_t slot = seq & (NSLOT - 1);
+        if (seq >= (uint32_t)NSLOT && ok) {
+            ok = mb_wait<false>(emptyp + slot, ((seq / NSLOT) & 1u) ^ 1u, err);
+            if (!ok) atomicExch(const_cast<int *>(err), 1);
+        }
+        ++seq;
+        if (!ok) return;
+        const uint32_t bar = full + slot * 8;
+        mb_expect(fullp + slot, b0 + b1);
+        const uint32_t dst = ring + slot * SLOT;
+        bulk_g2s(dst, s0, b0, bar, pol);
+        if (b1) bulk_g2s(dst + b0, s1, b1, bar, pol);
+    }
+    // tiles t = R, R + NR, ... of a linear (tile index = rb * n_kc + kc)
+    __device__ __forceinline__ void lin(const uint8_t *tiles, int n_tiles, uint32_t tb) {
+        const uint8_t *t = tiles + (size_t)R * tb;
+        const size_t step = (size_t)NR * tb;
+        for (int i = R; i < n_tiles; i += NR, t += step) issue(t, tb, nullptr, 0);
+    }
+    __device__ __forceinline__ void lin(const MkLin *L) { lin(L->tiles, L->n_rb * L->n_kc, (uint32_t)L->tile_bytes); }
+    __device__ __forceinline__ void attn(const __half *kc, const __half *vc, size_t base, size_t head_stride, int u_lo,
+                                         int u_hi, int kvt, int lold) {
+        int h = u_lo / kvt, t = u_lo - h * kvt;
+        base += (size_t)h * head_stride;
+        for (int u = u_lo; u < u_hi; ++u) {
+            const int np = min(KVPOS, lold - t * KVPOS);
+            if (np > 0) {
+                const size_t off = base + (size_t)t * KVPOS * kHeadDim;
+                issue(kc + off, (uint32_t)np * 128u, vc + off, (uint32_t)np * 128u);
+            }
+            if (++t == kvt) { t = 0; base += head_stride; }
+        }
+    }
+    __device__ __forceinline__ void run(const MkParams &p, const XkTab &T) {
+        const int u_lo = T.u_lo, u_hi = T.u_hi, kvt = T.kvt, lold = T.lold, slot = T.slot;
+        const size_t head_stride = (size_t)p.max_seq * kHeadDim;
+        for (int l = 0; l < p.n_layers && ok; ++l) {
+            const MkLayer *Ly = p.layers + l;
+            lin(&Ly->qkv);
+            if (u_hi > u_lo)
+                attn(p.kc, p.vc, kv_index(l, slot, 0, 0, p.n_slots, p.H, p.max_seq), head_stride, u_lo, u_hi, kvt, lold);
+            lin(&Ly->proj);
+            lin(&Ly->fc);
+            lin(&Ly->mlp);
+        }
+        if (ok) lin(&p.head);
+        for (uint32_t s = 0; s < NSLOT && s < seq; ++s) {  // every copy lands before exit
+            const uint32_t last = ((seq - 1 - s) / NSLOT) * NSLOT + s;
+            mb_wait<false>(fullp + s, (last / NSLOT) & 1u, err);
+        }
+    }
+};
+
+// ---------------------------------------------------------------------------
+// consumers (8 warps)
+// ---------------------------------------------------------------------------
+struct XkConsumer {
+    const XkParams *xp;
+    const MkParams *pp;
+    XkTab *T;
+    uint8_t *smem;
+    float *land, *sxln, *sxao, *sxu, *red, *qkvh, *stat;
+    __half *xln, *xao, *xu;
+    uint64_t *fullp, *emptyp, *stb;
+    int tid, warp, lane, g, c, rank, R, NR, d, ff, H, rt;
+    uint32_t seq, tbase;
+    uint32_t ph[NSTB];
+    uint32_t exp_bytes[NSTB];
+    bool ok;
+    int ev;
+
+    __device__ __forceinline__ uint32_t tag(int l, int st) const { return tbase + (uint32_t)(l * NWS + st) + 1u; }
+    __device__ __forceinline__ void trace() {
+        if (pp->trace && tid == 0 && ev < MK_TRACE_EVENTS) {
+            unsigned long long t;
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+            pp->trace[(size_t)R * MK_TRACE_EVENTS + ev] = t;
+        }
+        ++ev;
+    }
+    __device__ __forceinline__ void fail(int code) {
+        if (ok) atomicExch(pp->err, code);
+        ok = false;
+    }
+    // every consumer thread learns whether any of them failed
+    __device__ __forceinline__ void agree(bool good, int code) {
+        good = csync_and(good);
+        if (!good) fail(code);
+    }
+    __device__ __forceinline__ void wait_land(int b, int code) {
+        bool good = !ok || mb_wait<true>(stb + b, ph[b] & 1u, pp->err);
+        ++ph[b];
+        agree(good, code);
+        if (tid == 0) mb_expect(stb + b, exp_bytes[b]);
+        trace();
+    }
+    __device__ __forceinline__ void put_x(__half *xs, int k, float v) {
+        xs[(k & ~63) + frag_pos_host(k & 63)] = __float2half_rn(v);
+    }
+    __device__ __forceinline__ float block_sum(float v) {
+        v = warp_sum(v);
+        if (lane == 0) stat[warp] = v;
+        csync();
+        float t = 0.f;
+#pragma unroll
+        for (int w = 0; w < CW; ++w) t += stat[w];
+        csync();
+        return t;
+    }
+    __device__ __forceinline__ void group_sums(const __half *xs, float *sx, int K) {
+        csync();
+        const int total = K / 64 * 8;
+        for (int i0 = 0; i0 < total; i0 += CT) {
+            const int i = i0 + tid;
+            float s = 0.f;
+            if (i < total) {
+                const uint4 v = *reinterpret_cast<const uint4 *>(xs + (i >> 3) * 64 + (i & 7) * 8);
+                const __half2 *h2 = reinterpret_cast<const __half2 *>(&v);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 f = __half22float2(h2[e]);
+                    s += f.x + f.y;
+                }
+            }
+            s += __shfl_xor_sync(0xffffffffu, s, 1);
+            s += __shfl_xor_sync(0xffffffffu, s, 2);
+            s += __shfl_xor_sync(0xffffffffu, s, 4);
+            if (i < total && (i & 7) == 0) sx[i >> 3] = s;
+        }
+        csync();
+    }
+    static constexpr int LNC = (MK_MAX_D / 4 + CT - 1) / CT;
+    struct LnRegs {
+        float4 w[LNC], b[LNC];
+    };
+    __device__ __forceinline__ LnRegs ln_prefetch(const float *w, const float *b) const {
+        LnRegs r;
+#pragma unroll
+        for (int j = 0; j < LNC; ++j) {
+            const int k4 = tid + j * CT;
+            if (k4 * 4 < d) {
+                r.w[j] = __ldg(reinterpret_cast<const float4 *>(w) + k4);
+                r.b[j] = __ldg(reinterpret_cast<const float4 *>(b) + k4);
+            } else {
+                r.w[j] = r.b[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
+        return r;
+    }
+    // LayerNorm(land) * w + b (two-pass statistics) into xln (fp16, fragment order) or back
+    // into land (inplace)
+    __device__ __forceinline__ void layernorm(const LnRegs &P, bool inplace) {
+        float4 x[LNC];
+        float s = 0.f;
+#pragma unroll
+        for (int j = 0; j < LNC; ++j) {
+            const int k4 = tid + j * CT;
+            x[j] = k4 * 4 < d ? *reinterpret_cast<const float4 *>(land + k4 * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+            s += (x[j].x + x[j].y) + (x[j].z + x[j].w);
+        }
+        const float mean = block_sum(s) / (float)d;
+        float v = 0.f;
+#pragma unroll
+        for (int j = 0; j < LNC; ++j) {
+            const int k4 = tid + j * CT;
+            if (k4 * 4 < d) {
+                const float a = x[j].x - mean, b = x[j].y - mean, cc = x[j].z - mean, e = x[j].w - mean;
+                v += (a * a + b * b) + (cc * cc + e * e);
+            }
+        }
+        const float rstd = 1.0f / sqrtf(block_sum(v) / (float)d + kNormEps);
+#pragma unroll
+        for (int j = 0; j < LNC; ++j) {
+            const int k4 = tid + j * CT;
+            if (k4 * 4 >= d) continue;
+            float4 y;
+            y.x = (x[j].x - mean) * rstd * P.w[j].x + P.b[j].x;
+            y.y = (x[j].y - mean) * rstd * P.w[j].y + P.b[j].y;
+            y.z = (x[j].z - mean) * rstd * P.w[j].z + P.b[j].z;
+            y.w = (x[j].w - mean) * rstd * P.w[j].w + P.b[j].w;
+            if (inplace) {
+                *reinterpret_cast<float4 *>(land + k4 * 4) = y;
+            } else {
+                put_x(xln, k4 * 4, y.x);
+                put_x(xln, k4 * 4 + 1, y.y);
+                put_x(xln, k4 * 4 + 2, y.z);
+                put_x(xln, k4 * 4 + 3, y.w);
+            }
+        }
+        if (inplace) csync();
+        else group_sums(xln, sxln, d);
+        trace();
+    }
+
+    // ---- GEMV tiles ----
+    __device__ __forceinline__ void group(const uint8_t *tq, const uint8_t *tsb, int KC, int G64, int j, int gg,
+                                          const __half *xs, const float *sx, bool half_sb, float &a0, float &a1) {
+        const int jj = j ^ (g & 1);
+        const uint4 wa = *reinterpret_cast<const uint4 *>(tq + g * KC + jj * 64 + c * 16);
+        const uint4 wb = *reinterpret_cast<const uint4 *>(tq + (g + 8) * KC + jj * 64 + c * 16);
+        const uint4 x0 = *reinterpret_cast<const uint4 *>(xs + gg * 64 + c * 16);
+        const uint4 x1 = *reinterpret_cast<const uint4 *>(xs + gg * 64 + c * 16 + 8);
+        float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+        mma16816(d0, lo_h(wa.x), lo_h(wb.x), hi_h(wa.x), hi_h(wb.x), x0.x, x0.y);
+        mma16816(d1, lo_h(wa.y), lo_h(wb.y), hi_h(wa.y), hi_h(wb.y), x0.z, x0.w);
+        mma16816(d0, lo_h(wa.z), lo_h(wb.z), hi_h(wa.z), hi_h(wb.z), x1.x, x1.y);
+        mma16816(d1, lo_h(wa.w), lo_h(wb.w), hi_h(wa.w), hi_h(wb.w), x1.z, x1.w);
+        float s0, z0, s1, z1;
+        if (half_sb) {
+            const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(tsb + (g * G64 + j) * 4));
+            const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(tsb + ((g + 8) * G64 + j) * 4));
+            s0 = f0.x; z0 = f0.y; s1 = f1.x; z1 = f1.y;
+        } else {
+            const float2 f0 = *reinterpret_cast<const float2 *>(tsb + (g * G64 + j) * 8);
+            const float2 f1 = *reinterpret_cast<const float2 *>(tsb + ((g + 8) * G64 + j) * 8);
+            s0 = f0.x; z0 = f0.y; s1 = f1.x; z1 = f1.y;
+        }
+        const float sxg = sx[gg];
+        a0 += fmaf(s0, d0[0] + d1[0], fmaf(-1024.0f, s0, z0) * sxg);
+        a1 += fmaf(s1, d0[2] + d1[2], fmaf(-1024.0f, s1, z1) * sxg);
+    }
+    __device__ __forceinline__ void wait_slot(uint32_t slot, int code) {
+        bool good = !ok || mb_wait<false>(fullp + slot, (seq / NSLOT) & 1u, pp->err);
+        good = __all_sync(0xffffffffu, good);
+        if (!good) fail(code);
+    }
+    // This CTA's tiles t = R + NR i of linear L, i in [i0, i1), from the ring: per-warp
+    // partial sums to red[i - i0] (group j of a tile goes to warp (tile * G64 + j) % 8).
+    __device__ __forceinline__ void tiles(const MkLin &L, const __half *xs, const float *sx, int i0, int i1) {
+        const int KC = L.kc, G64 = KC / 64, nkc = L.n_kc;
+        const bool half_sb = pp->sbb == 4;
+        int w0 = 0;
+        for (int i = i0; i < i1; ++i) {
+            const int kci = nkc == 1 ? 0 : (R + i * NR) % nkc;
+            const uint32_t slot = seq & (NSLOT - 1);
+            wait_slot(slot, 2);
+            const uint8_t *tq = smem + slot * SLOT;
+            const uint8_t *tsb = tq + 16 * KC;
+            float a0 = 0.f, a1 = 0.f;
+            {
+                int j = (warp - w0) & (CW - 1);
+                for (; j + CW < G64; j += 2 * CW) {
+                    group(tq, tsb, KC, G64, j, kci * G64 + j, xs, sx, half_sb, a0, a1);
+                    group(tq, tsb, KC, G64, j + CW, kci * G64 + j + CW, xs, sx, half_sb, a0, a1);
+                }
+                if (j < G64) group(tq, tsb, KC, G64, j, kci * G64 + j, xs, sx, half_sb, a0, a1);
+            }
+            __syncwarp();
+            if (lane == 0) mb_arrive(emptyp + slot);
+            ++seq;
+            if (c == 0) {
+                float *r = red + ((i - i0) * CW + warp) * 16;
+                r[g] = a0;
+                r[g + 8] = a1;
+            }
+            w0 = (w0 + G64) & (CW - 1);
+        }
+        csync();
+    }
+    __device__ __forceinline__ int own_tiles(const MkLin &L) const {
+        const int n = L.n_rb * L.n_kc;
+        return R < n ? (n - 1 - R) / NR + 1 : 0;
+    }
+    // rows [4q, 4q+4) of local tile i: the 8 warps' partial sums in a fixed order
+    __device__ __forceinline__ float4 rows4(int i, int q) const {
+        float v[4] = {0.f, 0.f, 0.f, 0.f};
+        const float *r = red + (i * CW) * 16 + q * 4;
+#pragma unroll
+        for (int w = 0; w < CW; ++w) {
+            const float4 x = *reinterpret_cast<const float4 *>(r + w * 16);
+            v[0] += x.x; v[1] += x.y; v[2] += x.z; v[3] += x.w;
+        }
+        return make_float4(v[0], v[1], v[2], v[3]);
+    }
+    // Tiles of one linear, then per 4-row chunk epi(o, kc, v) (o: first output row,
+    // kc: K chunk of the tile).  Rows past L.out are skipped.
+    template <class Epi>
+    __device__ __forceinline__ void run_lin(const MkLin &L, const __half *xs, const float *sx, Epi epi) {
+        const int n = own_tiles(L);
+        for (int i0 = 0; i0 < n; i0 += rt) {
+            const int i1 = min(n, i0 + rt);
+            tiles(L, xs, sx, i0, i1);
+            if (i0 == 0) trace();
+            for (int q = tid; q < (i1 - i0) * 4; q += CT) {
+                const int il = q >> 2, t = R + (i0 + il) * NR, rb = t / L.n_kc, kci = t - rb * L.n_kc;
+                const int o = rb * 16 + (q & 3) * 4;
+                if (o < L.out) epi(o, kci, rows4(il, q & 3));
+            }
+            csync();
+        }
+        trace();
+    }
+
+    // ---- exchanges (cluster rank k gathers slice k and pushes it to the cluster) ----
+    // Runs are set by thread 0, polled by every consumer thread into `stage`.
+    __device__ __forceinline__ bool poll(int nruns, int total, uint32_t tg, float *stage) {
+        csync();  // the run table is written
+        return !ok || poll_runs(T->runs, nruns, total, tg, stage, pp->err);
+    }
+    // x_l = h + mlp bias + sum over K chunks of the mlp partials (layer l - 1) -> land
+    __device__ __forceinline__ void exchange_x(int lprev, int code) {
+        const MkParams &p = *pp;
+        const int per = d / CS, o0 = rank * per;
+        const MkLin &Lm = p.layers[lprev].mlp;
+        const int nkc = Lm.n_kc;
+        const uint64_t *mp = xp->mp_ll + (size_t)lprev * xp->nkc * d;
+        if (tid == 0)
+            for (int k = 0; k < nkc; ++k) T->runs[k] = PollRun{mp + (size_t)k * d + o0, k * (per / 2), 0};
+        const bool good = poll(nkc, nkc * per / 2, tag(lprev, 4), red);
+        agree(good, code);
+        const uint32_t land_a = su32(land), bar_a = su32(stb + B0);
+        for (int i = tid; i < per / 4; i += CT) {
+            const int o = o0 + i * 4;
+            float4 acc = *reinterpret_cast<const float4 *>(land + o);
+            const float4 bb = __ldg(reinterpret_cast<const float4 *>(Lm.bias + o));
+            acc.x += bb.x; acc.y += bb.y; acc.z += bb.z; acc.w += bb.w;
+            for (int k = 0; k < nkc; ++k) {  // fixed order over the K chunks
+                const float4 s4 = *reinterpret_cast<const float4 *>(red + k * per + i * 4);
+                acc.x += s4.x; acc.y += s4.y; acc.z += s4.z; acc.w += s4.w;
+            }
+            bcast_v4(land_a + o * 4, make_uint4(__float_as_uint(acc.x), __float_as_uint(acc.y),
+                                                __float_as_uint(acc.z), __float_as_uint(acc.w)), bar_a);
+        }
+        trace();
+        wait_land(B0, code + 1);
+    }
+    // h = x + (c_proj + bias) -> land
+    __device__ __forceinline__ void exchange_h(int l, int code) {
+        const int per = d / CS, o0 = rank * per;
+        if (tid == 0) T->runs[0] = PollRun{xp->pv_ll + (size_t)l * d + o0, 0, 0};
+        const bool good = poll(1, per / 2, tag(l, 2), red);
+        agree(good, code);
+        const uint32_t land_a = su32(land), bar_a = su32(stb + B0);
+        for (int i = tid; i < per / 4; i += CT) {
+            const int o = o0 + i * 4;
+            const float4 x = *reinterpret_cast<const float4 *>(land + o);
+            const float4 v = *reinterpret_cast<const float4 *>(red + i * 4);
+            bcast_v4(land_a + o * 4, make_uint4(__float_as_uint(x.x + v.x), __float_as_uint(x.y + v.y),
+                                                __float_as_uint(x.z + v.z), __float_as_uint(x.w + v.w)), bar_a);
+        }
+        trace();
+        wait_land(B0, code + 1);
+    }
+    // u -> fp16 fragment order -> xu; thread (group, c) sends the 32 contiguous bytes of rows
+    // {16 b + 2c, 16 b + 2c + 1, 16 b + 2c + 8, 16 b + 2c + 9 : b < 4}
+    __device__ __forceinline__ void exchange_u(int l, int code) {
+        const int per = ff / CS, k0 = rank * per;
+        if (tid == 0) T->runs[0] = PollRun{xp->u_ll + (size_t)l * ff + k0, 0, 0};
+        const bool good = poll(1, per / 2, tag(l, 3), red);
+        agree(good, code);
+        const uint32_t xu_a = su32(xu), bar_a = su32(stb + BU);
+        for (int i = tid; i < per / 16; i += CT) {
+            const int gl = (i >> 2) * 64, cc = i & 3;
+            const float *s = red + gl + 2 * cc;
+            uint4 v0, v1;
+            v0.x = pack_h2(s[0], s[1]);   v0.y = pack_h2(s[8], s[9]);
+            v0.z = pack_h2(s[16], s[17]); v0.w = pack_h2(s[24], s[25]);
+            v1.x = pack_h2(s[32], s[33]); v1.y = pack_h2(s[40], s[41]);
+            v1.z = pack_h2(s[48], s[49]); v1.w = pack_h2(s[56], s[57]);
+            const uint32_t dst = xu_a + (k0 + gl + cc * 16) * 2;
+            bcast_v4(dst, v0, bar_a);
+            bcast_v4(dst + 16, v1, bar_a);
+        }
+        trace();
+        wait_land(BU, code + 1);
+    }
+    // attention output of the heads h = rank + CS i: their partial records (contiguous per
+    // head) staged together (at most RCH, checked at configuration), thread (i, e) merges dim
+    // e of head i; fp16 fragment order -> xao of every CTA of the cluster
+    __device__ __forceinline__ void exchange_ao(int l, int code) {
+        const uint64_t *recs = xp->rec_ll + (size_t)l * xp->rec_stride * REC;
+        float *stg = red;                                            // [RCH][REC]
+        __half *hout = reinterpret_cast<__half *>(red + RCH * REC);  // [MAXHC][64] fragment order
+        const int nmy = rank < H ? (H - 1 - rank) / CS + 1 : 0;
+        const bool act = T->active != 0;
+        if (tid == 0) {
+            int start = 0;
+            for (int i = 0; i < nmy; ++i) {
+                const int h = rank + i * CS;
+                T->runs[i] = PollRun{recs + (size_t)T->hs0[h] * REC, start, 0};
+                start += act ? (T->hs0[h + 1] - T->hs0[h]) * (REC / 2) : 0;
+            }
+            T->runs[MAXHC].start = start;  // total pairs
+        }
+        csync();
+        const int total = T->runs[MAXHC].start;
+        const bool good = poll(nmy, total, tag(l, 1), stg);
+        agree(good, code);
+        const int mi = tid >> 6, e = tid & 63;
+        if (mi < nmy) {
+            const int h = rank + mi * CS;
+            const int r0 = T->runs[mi].start / (REC / 2), nr = act ? T->hs0[h + 1] - T->hs0[h] : 0;
+            float M = -INFINITY, Lsum = 0.f, A = 0.f;
+            for (int s = r0; s < r0 + nr; ++s) {
+                const float *rec = stg + s * REC;
+                const float ms = rec[0], Mn = fmaxf(M, ms);
+                const float fa = exp2f(M - Mn), fb = exp2f(ms - Mn);  // M = -inf gives 0
+                Lsum = Lsum * fa + rec[1] * fb;
+                A = A * fa + rec[4 + e] * fb;
+                M = Mn;
+            }
+            hout[mi * 64 + frag_pos_host(e)] = __float2half_rn(nr > 0 ? A / Lsum : 0.f);
+        }
+        csync();
+        const uint32_t xao_a = su32(xao), bar_a = su32(stb + BAO);
+        if (tid < nmy * 8) {
+            const int h = rank + (tid >> 3) * CS;
+            bcast_v4(xao_a + (h * 64 + (tid & 7) * 8) * 2, reinterpret_cast<const uint4 *>(hout)[tid], bar_a);
+        }
+        trace();
+        wait_land(BAO, code + 1);
+    }
+
+    // ---- stages ----
+    __device__ __forceinline__ void stage_qkv(int l) {
+        const MkParams &p = *pp;
+        const MkLayer &Ly = p.layers[l];
+        const LnRegs ln1 = ln_prefetch(Ly.ln1_w, Ly.ln1_b);
+        if (l == 0) {
+            const float *e = p.mel_emb + (size_t)T->tok * d, *ps = p.mel_pos + (size_t)T->pos * d;
+            for (int k = tid; k < d; k += CT) land[k] = e[k] + ps[k];
+            csync();
+            trace();
+        } else {
+            exchange_x(l - 1, 20);
+        }
+        layernorm(ln1, false);
+        const MkLin &L = Ly.qkv;
+        uint64_t *q = xp->qkv_ll + (size_t)l * 3 * d;
+        const uint32_t tg = tag(l, 0);
+        const int active = T->active, slot = T->slot, lold = T->lold;
+        run_lin(L, xln, sxln, [&](int o, int, float4 v) {
+            const float4 bb = __ldg(reinterpret_cast<const float4 *>(L.bias + o));
+            v.x += bb.x; v.y += bb.y; v.z += bb.z; v.w += bb.w;
+            ll_st2(q + o, v.x, v.y, tg);
+            ll_st2(q + o + 2, v.z, v.w, tg);
+            const int which = o / d, oo = o - which * d;
+            if (which > 0 && active) {
+                __half *cache = which == 1 ? p.kc : p.vc;
+                uint2 hv;
+                hv.x = pack_h2(v.x, v.y);
+                hv.y = pack_h2(v.z, v.w);
+                *reinterpret_cast<uint2 *>(cache + kv_index(l, slot, oo >> 6, lold, p.n_slots, p.H, p.max_seq) +
+                                           (oo & 63)) = hv;
+            }
+        });
+    }
+    __device__ __forceinline__ void stage_attn(int l) {
+        const MkParams &p = *pp;
+        const int grp = lane >> 3, d8 = lane & 7;
+        const int nh = T->nh;
+        // q, k, v of this CTA's heads from the QKV stage
+        {
+            const uint64_t *q = xp->qkv_ll + (size_t)l * 3 * d;
+            if (tid == 0)
+                for (int i = 0; i < nh * 3; ++i)
+                    T->runs[i] = PollRun{q + (i % 3) * d + (T->hlo + i / 3) * 64, i * 32, 0};
+            const bool good = poll(nh * 3, nh * 96, tag(l, 0), qkvh);
+            agree(good, 30);
+        }
+        float *ascr = red;                     // [MAXHC][CW][REC] warp states
+        const float qscale = kAttnScale * kLog2e;
+        int k = -1, hcur = -1;
+        float qv[8], m = -INFINITY, ls = 0.f, acc[8];
+        auto close = [&]() {
+#pragma unroll
+            for (int off = 8; off <= 16; off <<= 1) {
+                const float m2 = __shfl_xor_sync(0xffffffffu, m, off);
+                const float l2 = __shfl_xor_sync(0xffffffffu, ls, off);
+                const float M = fmaxf(m, m2);
+                const float fa = m == -INFINITY ? 0.f : exp2f(m - M);
+                const float fb = m2 == -INFINITY ? 0.f : exp2f(m2 - M);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const float a2 = __shfl_xor_sync(0xffffffffu, acc[e], off);
+                    acc[e] = acc[e] * fa + a2 * fb;
+                }
+                ls = ls * fa + l2 * fb;
+                m = M;
+            }
+            if (grp == 0) {
+                float *s = ascr + (k * CW + warp) * REC;
+                if (d8 == 0) { s[0] = m; s[1] = ls; }
+#pragma unroll
+                for (int e = 0; e < 8; ++e) s[4 + d8 * 8 + e] = acc[e];
+            }
+        };
+        if (T->u_hi > T->u_lo) {
+            const int kvt = T->kvt, lold = T->lold, hlo = T->hlo;
+            int h = T->u_lo / kvt, t = T->u_lo - h * kvt;
+            for (int u = T->u_lo; u < T->u_hi; ++u) {
+                if (h != hcur) {
+                    if (k >= 0) close();
+                    ++k;
+                    hcur = h;
+                    const float *qh = qkvh + ((h - hlo) * 3) * 64 + d8 * 8;
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) { qv[e] = qh[e] * qscale; acc[e] = 0.f; }
+                    m = -INFINITY;
+                    ls = 0.f;
+                }
+                const int np = min(KVPOS, lold - t * KVPOS);
+                if (np > 0) {
+                    const uint32_t slot = seq & (NSLOT - 1);
+                    wait_slot(slot, 3);
+                    const __half *kt = reinterpret_cast<const __half *>(smem + slot * SLOT);
+                    const __half *vt = kt + np * 64;
+                    constexpr int QG = (KVPOS / 4 + CW - 1) / CW;
+                    float sc[QG];
+                    uint4 vv[QG];
+#pragma unroll
+                    for (int q = 0; q < QG; ++q) {
+                        const int pos = (warp + q * CW) * 4 + grp;
+                        const int pc = pos < np ? pos : 0;
+                        const uint4 kk = *reinterpret_cast<const uint4 *>(kt + pc * 64 + d8 * 8);
+                        vv[q] = *reinterpret_cast<const uint4 *>(vt + pc * 64 + d8 * 8);
+                        const __half2 *k2 = reinterpret_cast<const __half2 *>(&kk);
+                        float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+                        for (int e = 0; e < 4; e += 2) {
+                            const float2 ka = __half22float2(k2[e]), kb = __half22float2(k2[e + 1]);
+                            s0 = fmaf(qv[2 * e], ka.x, s0);
+                            s1 = fmaf(qv[2 * e + 1], ka.y, s1);
+                            s0 = fmaf(qv[2 * e + 2], kb.x, s0);
+                            s1 = fmaf(qv[2 * e + 3], kb.y, s1);
+                        }
+                        sc[q] = s0 + s1;
+                    }
+#pragma unroll
+                    for (int q = 0; q < QG; ++q) sc[q] += __shfl_xor_sync(0xffffffffu, sc[q], 1);
+#pragma unroll
+                    for (int q = 0; q < QG; ++q) sc[q] += __shfl_xor_sync(0xffffffffu, sc[q], 2);
+#pragma unroll
+                    for (int q = 0; q < QG; ++q) sc[q] += __shfl_xor_sync(0xffffffffu, sc[q], 4);
+                    float mt = m;
+#pragma unroll
+                    for (int q = 0; q < QG; ++q)
+                        if ((warp + q * CW) * 4 + grp < np) mt = fmaxf(mt, sc[q]);
+                    if (mt != m) {
+                        const float corr = exp2f(m - mt);
+                        ls *= corr;
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) acc[e] *= corr;
+                        m = mt;
+                    }
+#pragma unroll
+                    for (int q = 0; q < QG; ++q) {
+                        if ((warp + q * CW) * 4 + grp < np) {
+                            const float pj = exp2f(sc[q] - m);
+                            ls += pj;
+                            const __half2 *v2 = reinterpret_cast<const __half2 *>(&vv[q]);
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                const float2 f = __half22float2(v2[e]);
+                                acc[2 * e] = fmaf(pj, f.x, acc[2 * e]);
+                                acc[2 * e + 1] = fmaf(pj, f.y, acc[2 * e + 1]);
+                            }
+                        }
+                    }
+                    __syncwarp();
+                    if (lane == 0) mb_arrive(emptyp + slot);
+                    ++seq;
+                }
+                if (t == kvt - 1 && warp == CW - 1) {  // the new position (fp32, from the QKV stage)
+                    const float *kn = qkvh + ((h - hlo) * 3 + 1) * 64 + d8 * 8;
+                    const float *vn = kn + 64;
+                    float s = 0.f;
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) s = fmaf(qv[e], kn[e], s);
+                    s += __shfl_xor_sync(0xffffffffu, s, 1);
+                    s += __shfl_xor_sync(0xffffffffu, s, 2);
+                    s += __shfl_xor_sync(0xffffffffu, s, 4);
+                    if (grp == 0) {
+                        const float mn = fmaxf(m, s);
+                        const float corr = exp2f(m - mn);
+                        const float pj = exp2f(s - mn);
+                        ls = ls * corr + pj;
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) acc[e] = acc[e] * corr + pj * vn[e];
+                        m = mn;
+                    }
+                }
+                if (++t == kvt) { t = 0; ++h; }
+            }
+            close();
+        }
+        csync();
+        // merge the warps per segment, records to global memory
+        uint64_t *rdst = xp->rec_ll + ((size_t)l * xp->rec_stride + T->seg0) * REC;
+        const uint32_t tg = tag(l, 1);
+        for (int i = tid; i < nh * 32; i += CT) {
+            const int kk = i >> 5, e2 = (i & 31) * 2;  // dims e2, e2 + 1
+            const float *s = ascr + kk * CW * REC;
+            float M = -INFINITY;
+#pragma unroll
+            for (int w = 0; w < CW; ++w) M = fmaxf(M, s[w * REC]);
+            float L2 = 0.f, A0 = 0.f, A1 = 0.f;
+#pragma unroll
+            for (int w = 0; w < CW; ++w) {
+                const float f = exp2f(s[w * REC] - M);
+                L2 += s[w * REC + 1] * f;
+                A0 += s[w * REC + 4 + e2] * f;
+                A1 += s[w * REC + 5 + e2] * f;
+            }
+            ll_st2(rdst + kk * REC + 4 + e2, A0, A1, tg);
+            if (e2 == 0) {
+                ll_st2(rdst + kk * REC, M, L2, tg);
+                ll_st2(rdst + kk * REC + 2, 0.f, 0.f, tg);
+            }
+        }
+        trace();
+    }
+    __device__ __forceinline__ void stage_proj(int l) {
+        exchange_ao(l, 40);
+        group_sums(xao, sxao, d);
+        const MkLin &L = pp->layers[l].proj;
+        uint64_t *pv = xp->pv_ll + (size_t)l * d;
+        const uint32_t tg = tag(l, 2);
+        run_lin(L, xao, sxao, [&](int o, int, float4 v) {
+            const float4 bb = __ldg(reinterpret_cast<const float4 *>(L.bias + o));
+            ll_st2(pv + o, v.x + bb.x, v.y + bb.y, tg);
+            ll_st2(pv + o + 2, v.z + bb.z, v.w + bb.w, tg);
+        });
+    }
+    __device__ __forceinline__ void stage_fc(int l) {
+        const MkLayer &Ly = pp->layers[l];
+        const LnRegs ln2 = ln_prefetch(Ly.ln2_w, Ly.ln2_b);
+        exchange_h(l, 50);
+        layernorm(ln2, false);
+        const MkLin &L = Ly.fc;
+        uint64_t *u = xp->u_ll + (size_t)l * ff;
+        const uint32_t tg = tag(l, 3);
+        run_lin(L, xln, sxln, [&](int o, int, float4 v) {
+            const float4 bb = __ldg(reinterpret_cast<const float4 *>(L.bias + o));
+            ll_st2(u + o, gelu_tanh(v.x + bb.x), gelu_tanh(v.y + bb.y), tg);
+            ll_st2(u + o + 2, gelu_tanh(v.z + bb.z), gelu_tanh(v.w + bb.w), tg);
+        });
+    }
+    __device__ __forceinline__ void stage_mlp(int l) {
+        exchange_u(l, 60);
+        group_sums(xu, sxu, ff);
+        const MkLin &L = pp->layers[l].mlp;
+        uint64_t *mp = xp->mp_ll + (size_t)l * xp->nkc * d;
+        const uint32_t tg = tag(l, 4);
+        const int dd = d;
+        run_lin(L, xu, sxu, [&](int o, int kci, float4 v) {
+            ll_st2(mp + (size_t)kci * dd + o, v.x, v.y, tg);
+            ll_st2(mp + (size_t)kci * dd + o + 2, v.z, v.w, tg);
+        });
+    }
+    __device__ __forceinline__ void stage_head() {
+        const MkParams &p = *pp;
+        const LnRegs lnf = ln_prefetch(p.lnf_w, p.lnf_b);
+        const LnRegs fin = ln_prefetch(p.fin_w, p.fin_b);
+        exchange_x(p.n_layers - 1, 70);
+        layernorm(lnf, true);
+        layernorm(fin, false);
+        const MkLin &L = p.head;
+        const int V = p.mel_vocab;
+        run_lin(L, xln, sxln, [&](int o, int, float4 v) {
+            const float vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                if (o + e < V) p.logits[o + e] = vv[e] + __ldg(L.bias + o + e);
+        });
+    }
+};
+
+// ---------------------------------------------------------------------------
+// kernel
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(NT, 1) xk_decode_kernel(const __grid_constant__ XkParams xp) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    if (xp.dry) {  // launch-configuration probe
+        cluster_sync_all();
+        return;
+    }
+    const MkParams &p = xp.p;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    uint32_t rank_u;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank_u));
+    const int rank = (int)rank_u, R = blockIdx.x, NR = gridDim.x;
+    const XkSmem SL = xk_layout(p.d, p.ff, xp.rt);
+    XkTab *T = reinterpret_cast<XkTab *>(smem + SL.tab);
+    uint64_t *fullp = reinterpret_cast<uint64_t *>(smem + SL.bar);
+    uint64_t *emptyp = fullp + NSLOT;
+    uint64_t *stb = emptyp + NSLOT;
+
+    // step shape: every CTA computes the same tables; thread r < NR does CTA r's range
+    const int slot = p.batch_slot[0];
+    const SlotState &st = p.slots[slot];
+    const int active = st.active && st.valid_len < p.max_seq;
+    const int lold = active ? st.valid_len : 0;
+    const int kvt = active ? max(1, (lold + KVPOS - 1) / KVPOS) : 0;
+    const int units = p.H * kvt;
+    if (tid < NR) {
+        const int a = (int)((long long)tid * units / NR), b = (int)((long long)(tid + 1) * units / NR);
+        T->hl[tid] = b > a ? a / kvt : 0;
+        T->cnt[tid] = b > a ? (b - 1) / kvt - a / kvt + 1 : 0;
+        if (tid == R) {
+            T->u_lo = a;
+            T->u_hi = b;
+            T->hlo = T->hl[tid];
+            T->nh = T->cnt[tid];
+        }
+    }
+    if (tid <= p.H) T->hs0[tid] = 0x7fffffff;
+    if (tid == 0) {
+        for (int s = 0; s < NSLOT; ++s) {
+            mb_init(fullp + s, 1);
+            mb_init(emptyp + s, CW);
+        }
+        for (int b = 0; b < NSTB; ++b) mb_init(stb + b, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        mb_expect(stb + B0, (uint32_t)p.d * 4);
+        mb_expect(stb + BAO, (uint32_t)p.d * 2);
+        mb_expect(stb + BU, (uint32_t)p.ff * 2);
+        T->active = active;
+        T->lold = lold;
+        T->kvt = kvt;
+        T->units = units;
+        T->slot = slot;
+        T->tok = min(max(st.tok, 0), p.mel_vocab - 1);
+        T->pos = min(max(st.pos, 0), p.mel_pos_len - 1);
+    }
+    __syncthreads();
+    if (warp == 0) {  // segments: a scan of the per-CTA head counts (5 CTAs per lane)
+        constexpr int PL = MAXNR / 32;
+        int cnt[PL], sum = 0;
+#pragma unroll
+        for (int k = 0; k < PL; ++k) {
+            const int r = lane * PL + k;
+            cnt[k] = r < NR ? T->cnt[r] : 0;
+            sum += cnt[k];
+        }
+        int inc = sum;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, inc, off);
+            if (lane >= off) inc += y;
+        }
+        int base = inc - sum;
+#pragma unroll
+        for (int k = 0; k < PL; ++k) {
+            const int r = lane * PL + k;
+            if (r < NR) {
+                if (r == R) T->seg0 = base;
+                for (int kk = 0; kk < cnt[k]; ++kk) atomicMin(&T->hs0[T->hl[r] + kk], base + kk);
+            }
+            base += cnt[k];
+        }
+        const int total = __shfl_sync(0xffffffffu, inc, 31);
+        __syncwarp();
+        if (lane == 0) T->nseg = total;
+        for (int h = lane; h <= p.H; h += 32)  // heads without segments (inactive column), end mark
+            if (h == p.H || T->hs0[h] == 0x7fffffff) T->hs0[h] = total;
+    }
+    __syncthreads();
+    const uint32_t epoch = xp.epoch[R];
+    // every CTA's barriers are armed before any CTA pushes into them
+    cluster_sync_all();
+
+    if (warp == CW) {
+        if (lane == 0) {
+            XkProducer P;
+            P.ring = su32(smem);
+            P.full = su32(fullp);
+            P.fullp = fullp;
+            P.emptyp = emptyp;
+            P.err = p.err;
+            asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(P.pol));
+            P.seq = 0;
+            P.R = R;
+            P.NR = NR;
+            P.ok = true;
+            P.run(p, *T);
+        }
+        __syncwarp();
+    } else {
+        XkConsumer C;
+        C.xp = &xp;
+        C.pp = &p;
+        C.T = T;
+        C.smem = smem;
+        C.land = reinterpret_cast<float *>(smem + SL.land);
+        C.xln = reinterpret_cast<__half *>(smem + SL.xln);
+        C.xao = reinterpret_cast<__half *>(smem + SL.xao);
+        C.xu = reinterpret_cast<__half *>(smem + SL.xu);
+        C.sxln = reinterpret_cast<float *>(smem + SL.sxln);
+        C.sxao = reinterpret_cast<float *>(smem + SL.sxao);
+        C.sxu = reinterpret_cast<float *>(smem + SL.sxu);
+        C.red = reinterpret_cast<float *>(smem + SL.red);
+        C.qkvh = reinterpret_cast<float *>(smem + SL.qkvh);
+        C.stat = reinterpret_cast<float *>(smem + SL.stat);
+        C.fullp = fullp;
+        C.emptyp = emptyp;
+        C.stb = stb;
+        C.tid = tid;
+        C.warp = warp;
+        C.lane = lane;
+        C.g = lane >> 2;
+        C.c = lane & 3;
+        C.rank = rank;
+        C.R = R;
+        C.NR = NR;
+        C.d = p.d;
+        C.ff = p.ff;
+        C.H = p.H;
+        C.rt = xp.rt;
+        C.seq = 0;
+        C.tbase = epoch * (uint32_t)(NWS * p.n_layers);
+        C.ok = true;
+        C.ev = 0;
+        C.ph[B0] = C.ph[BAO] = C.ph[BU] = 0;
+        C.exp_bytes[B0] = (uint32_t)p.d * 4;
+        C.exp_bytes[BAO] = (uint32_t)p.d * 2;
+        C.exp_bytes[BU] = (uint32_t)p.ff * 2;
+        for (int l = 0; l < p.n_layers; ++l) {
+            C.stage_qkv(l);
+            C.stage_attn(l);
+            C.stage_proj(l);
+            C.stage_fc(l);
+            C.stage_mlp(l);
+        }
+        C.stage_head();
+    }
+    __syncwarp();
+    cluster_sync_all();  // no CTA leaves while a peer may still push into its shared memory
+    if (tid == 0) xp.epoch[R] = epoch + 1;
+}
+
+cudaError_t xk_launch_cfg(const XkParams &xp, int grid, size_t smem, bool coop, cudaStream_t st) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(NT);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[2];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = CS;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    at[1].id = cudaLaunchAttributeCooperative;
+    at[1].val.cooperative = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = coop ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, xk_decode_kernel, xp);
+}
+
+}  // namespace
+
+static int xk_tiles_of(const MkLin &L, int nr) { return (L.n_rb * L.n_kc + nr - 1) / nr; }
+
+int xk_config(const ModelView &m, XkConfig *out) {
+    *out = XkConfig{};
+    const char *off = getenv("ITTS_XK");
+    if (off && off[0] == '0') return -1;
+    if (m.n_layers < 1 || m.d > MK_MAX_KC || m.d % (4 * CS) || m.d % 64 || m.ff % (64 * CS) ||
+        m.n_heads * 64 != m.d || m.n_heads > 32)
+        return -1;
+    int dev = 0, optin = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    int nkc = 0;
+    for (int l = 0; l < m.n_layers; ++l) {
+        const MkLayer &L = m.layers[l];
+        for (const MkLin *x : {&L.qkv, &L.proj, &L.fc, &L.mlp})
+            if (x->tile_bytes > SLOT || x->kc % 64) return -1;
+        if (L.qkv.n_kc != 1 || L.proj.n_kc != 1 || L.fc.n_kc != 1 || L.mlp.n_kc > 4) return -1;
+        if (L.qkv.out != 3 * m.d || L.proj.out != m.d || L.fc.out != m.ff || L.mlp.out != m.d) return -1;
+        nkc = std::max(nkc, L.mlp.n_kc);
+    }
+    if (m.mel_head.tile_bytes > SLOT || m.mel_head.n_kc != 1) return -1;
+    // grid: as many 8-CTA clusters as fit at once
+    const int rt_guess = 8;
+    size_t smem = xk_layout(m.d, m.ff, rt_guess).total;
+    if ((int)smem > optin) return -1;
+    if (cudaFuncSetAttribute(xk_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
+        cudaGetLastError();
+        return -1;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(CS);
+    cfg.blockDim = dim3(NT);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = CS;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    int ncl = 0;
+    if (cudaOccupancyMaxActiveClusters(&ncl, xk_decode_kernel, &cfg) != cudaSuccess || ncl < 1) {
+        cudaGetLastError();
+        return -1;
+    }
+    const int grid = std::min(ncl * CS, (std::min(sms, MAXNR) / CS) * CS);
+    int rt = 1;
+    for (int l = 0; l < m.n_layers; ++l) {
+        const MkLayer &L = m.layers[l];
+        for (const MkLin *x : {&L.qkv, &L.proj, &L.fc, &L.mlp}) rt = std::max(rt, xk_tiles_of(*x, grid));
+    }
+    rt = std::min(rt, rt_guess);
+    smem = xk_layout(m.d, m.ff, rt).total;
+    cudaFuncSetAttribute(xk_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    // probe the launch form: cooperative (co-residency guaranteed) with clusters, else plain
+    XkParams probe{};
+    probe.dry = 1;
+    bool coop = true;
+    cudaError_t e = xk_launch_cfg(probe, grid, smem, true, 0);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        coop = false;
+        e = xk_launch_cfg(probe, grid, smem, false, 0);
+        if (e == cudaSuccess) e = cudaDeviceSynchronize();
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return -1;
+        }
+    }
+    out->grid = grid;
+    out->rt = rt;
+    out->nkc = nkc;
+    out->coop = coop ? 1 : 0;
+    out->rec_stride = m.n_heads + grid;
+    if (getenv("ITTS_DEBUG"))
+        fprintf(stderr, "[itts] clustered decode kernel: grid %d (%d-CTA clusters, %s), %zu B shared memory, rt %d\n",
+                grid, CS, coop ? "cooperative" : "plain", smem, rt);
+    return grid;
+}
+
+cudaError_t xk_launch(const MkParams &p, const XkConfig &xc, const XkBufs &b, cudaStream_t st) {
+    XkParams xp{};
+    xp.p = p;
+    xp.qkv_ll = b.qkv_ll;
+    xp.rec_ll = b.rec_ll;
+    xp.pv_ll = b.pv_ll;
+    xp.u_ll = b.u_ll;
+    xp.mp_ll = b.mp_ll;
+    xp.epoch = b.epoch;
+    xp.rt = xc.rt;
+    xp.nkc = xc.nkc;
+    xp.rec_stride = xc.rec_stride;
+    xp.dry = 0;
+    return xk_launch_cfg(xp, xc.grid, xk_layout(p.d, p.ff, xc.rt).total, xc.coop != 0, st);
+}
+
+}  // namespace itts

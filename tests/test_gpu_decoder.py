@@ -59,26 +59,38 @@ def _teacher_forced(gpt, om, cfg, n_text, n_conds, steps, seed, max_seq=1024):
     return np.stack(g), np.stack(r)
 
 
+# batch-1 decode kernels: the default clustered all-SM kernel, the persistent grid-wide
+# kernel (ITTS_XK=0), the single-cluster kernel (ITTS_CLUSTER=1)
+KERNELS = {"xk": ({}, "xk_decode_kernel"), "grid": ({"ITTS_XK": "0"}, "mk_decode_kernel"),
+           "cluster": ({"ITTS_CLUSTER": "1"}, "ck_decode_kernel")}
+
+
+def _use_kernel(monkeypatch, gpt, name):
+    env, want = KERNELS[name]
+    for k, v in env.items():
+        monkeypatch.setenv(k, v)
+    assert ig.KvCache(gpt, max_seq=64).decode_kernel(1) == want
+
+
 def test_decode_kernel_selection(small, monkeypatch):
     gpt, _ = small
     kv4 = ig.KvCache(gpt, max_seq=256, max_batch=8)
-    assert kv4.decode_kernel(1) == "mk_decode_kernel"
+    assert kv4.decode_kernel(1) == "xk_decode_kernel"
     assert kv4.decode_kernel(2) == "mk_decode_kernel"
     assert kv4.decode_kernel(5) == "gemm path"
-    monkeypatch.setenv("ITTS_CLUSTER", "1")
-    assert ig.KvCache(gpt, max_seq=256, max_batch=1).decode_kernel(1) == "ck_decode_kernel"
+    for name in KERNELS:
+        with monkeypatch.context() as mp:
+            _use_kernel(mp, gpt, name)
 
 
-@pytest.mark.parametrize("cluster", [False, True], ids=["grid", "cluster"])
+@pytest.mark.parametrize("kernel", list(KERNELS))
 @pytest.mark.parametrize("n_text,steps", [(52, 70), (140, 60)])
-def test_teacher_forced_across_kv_tiles(small, small_cfg, monkeypatch, cluster, n_text, steps):
-    """Decode steps whose KV length crosses 84-position K/V tiles (the cluster kernel's
-    tile; for 4 heads on 16 CTAs its attention ranges have idle CTAs between a head's),
-    on the grid-wide kernel and on the opt-in 16-CTA cluster kernel."""
+def test_teacher_forced_across_kv_tiles(small, small_cfg, monkeypatch, kernel, n_text, steps):
+    """Decode steps whose KV length crosses 84-position K/V tiles (the tile of the cluster
+    kernels; for 4 heads on many CTAs their attention ranges have idle CTAs between a
+    head's), on every batch-1 decode kernel."""
     gpt, om = small
-    if cluster:
-        monkeypatch.setenv("ITTS_CLUSTER", "1")
-        assert ig.KvCache(gpt, max_seq=64).decode_kernel(1) == "ck_decode_kernel"
+    _use_kernel(monkeypatch, gpt, kernel)
     g, r = _teacher_forced(gpt, om, small_cfg, n_text, 3, steps, seed=n_text)
     for i in range(len(g)):
         check_logits(g[i], r[i], f"step {i}")
@@ -336,13 +348,10 @@ def full():
     g.close()
 
 
-@pytest.mark.parametrize("cluster", [False, True], ids=["grid", "cluster"])
-def test_full_size_teacher_forced(full, monkeypatch, cluster):
+@pytest.mark.parametrize("kernel", list(KERNELS))
+def test_full_size_teacher_forced(full, monkeypatch, kernel):
     cfg, gpt, om = full
-    if cluster:
-        monkeypatch.setenv("ITTS_CLUSTER", "1")
-    want = "ck_decode_kernel" if cluster else "mk_decode_kernel"
-    assert ig.KvCache(gpt, max_seq=512).decode_kernel(1) == want
+    _use_kernel(monkeypatch, gpt, kernel)
     g, r = _teacher_forced(gpt, om, cfg, 64, 32, 24, seed=41, max_seq=512)
     errs = [check_logits(g[i], r[i], f"full step {i}") for i in range(len(g))]
     agree = np.mean(np.argmax(g, 1) == np.argmax(r, 1))
