@@ -292,7 +292,10 @@ def run_ours(args, rank, world, local_rank):
                      "algorithmic_bytes_per_launch": step_bytes,
                      "bytes_formula": "514,144,936 weight B + 122,880 B x KV positions (fp16 K+V)",
                      "kv_positions": L_avg + 1, "launches_per_step": ws_launches,
-                     "ms_per_launch": ws_ms, "traffic": None},
+                     "ms_per_launch": ws_ms,
+                     # dram__bytes_read.sum + dram__bytes_write.sum of one launch at this KV
+                     # length (ncu capture summarised in profiles/xk_decode_kernel_cfg2.md)
+                     "traffic": 692909056 if kname == "xk_decode_kernel" else None},
         "clocks": clk,
     }
     try:

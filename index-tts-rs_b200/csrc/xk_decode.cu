@@ -1211,8 +1211,11 @@ int xk_config(const ModelView &m, XkConfig *out) {
     // probe the launch form: cooperative (co-residency guaranteed) with clusters, else plain
     XkParams probe{};
     probe.dry = 1;
-    bool coop = true;
-    cudaError_t e = xk_launch_cfg(probe, grid, smem, true, 0);
+    // ITTS_XK_COOP=0: plain cluster launch (co-residency then rests on the grid fitting the
+    // device at once, which the cluster count above ensures; profilers replay it)
+    const char *cp = getenv("ITTS_XK_COOP");
+    bool coop = !(cp && cp[0] == '0');
+    cudaError_t e = coop ? xk_launch_cfg(probe, grid, smem, true, 0) : cudaErrorNotSupported;
     if (e == cudaSuccess) e = cudaDeviceSynchronize();
     if (e != cudaSuccess) {
         cudaGetLastError();
