@@ -238,7 +238,7 @@ __device__ __noinline__ bool poll_runs(const PollRun *runs, int nruns, int total
 // shared-memory carve-up (identical on host and device)
 // ---------------------------------------------------------------------------
 struct XkSmem {
-    uint32_t land, xln, xao, xu, sxln, sxao, sxu, red, qkvh, stat, tab, bar, total;
+    uint32_t land, xln, xao, xu, sxln, sxao, sxu, red, qkvh, stat, tab, lay, bar, total;
 };
 __host__ __device__ inline uint32_t xk_red_bytes(int rt) {
     const uint32_t lin = (uint32_t)rt * CW * 16 * 4;
@@ -253,7 +253,7 @@ struct XkTab {
     int cnt[MAXNR], hl[MAXNR];   // per CTA of the grid: heads its range touches, first head
     PollRun runs[MAXRUN];        // the current poll list
 };
-__host__ __device__ inline XkSmem xk_layout(int d, int ff, int rt) {
+__host__ __device__ inline XkSmem xk_layout(int d, int ff, int rt, int n_layers) {
     XkSmem L;
     uint32_t o = NSLOT * SLOT;
     auto take = [&](uint32_t bytes) {
@@ -272,6 +272,7 @@ __host__ __device__ inline XkSmem xk_layout(int d, int ff, int rt) {
     L.qkvh = take(MAXHC * 3 * 64 * 4);
     L.stat = take(64 * 4);
     L.tab = take(sizeof(XkTab));
+    L.lay = take(n_layers * sizeof(MkLayer));  // the layer table (pointers, shapes) in shared memory
     L.bar = take((2 * NSLOT + NSTB) * 8);
     L.total = o;
     return L;
@@ -334,11 +335,11 @@ struct XkProducer {
             if (++t == kvt) { t = 0; base += head_stride; }
         }
     }
-    __device__ __forceinline__ void run(const MkParams &p, const XkTab &T) {
+    __device__ __forceinline__ void run(const MkParams &p, const XkTab &T, const MkLayer *lay) {
         const int u_lo = T.u_lo, u_hi = T.u_hi, kvt = T.kvt, lold = T.lold, slot = T.slot;
         const size_t head_stride = (size_t)p.max_seq * kHeadDim;
         for (int l = 0; l < p.n_layers && ok; ++l) {
-            const MkLayer *Ly = p.layers + l;
+            const MkLayer *Ly = lay + l;
             lin(&Ly->qkv);
             if (u_hi > u_lo)
                 attn(p.kc, p.vc, kv_index(l, slot, 0, 0, p.n_slots, p.H, p.max_seq), head_stride, u_lo, u_hi, kvt, lold);
@@ -361,6 +362,7 @@ struct XkConsumer {
     const XkParams *xp;
     const MkParams *pp;
     XkTab *T;
+    const MkLayer *lay;  // shared-memory copy of the layer table
     uint8_t *smem;
     float *land, *sxln, *sxao, *sxu, *red, *qkvh, *stat;
     __half *xln, *xao, *xu;
@@ -575,19 +577,34 @@ struct XkConsumer {
         }
         return make_float4(v[0], v[1], v[2], v[3]);
     }
-    // Tiles of one linear, then per 4-row chunk epi(o, kc, v) (o: first output row,
+    // bias of output rows [o, o + 4) (rows past L.out read as 0)
+    __device__ __forceinline__ float4 bias4(const MkLin &L, int o) const {
+        if (o + 4 <= L.out) return __ldg(reinterpret_cast<const float4 *>(L.bias + o));
+        float b[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) b[e] = o + e < L.out ? __ldg(L.bias + o + e) : 0.f;
+        return make_float4(b[0], b[1], b[2], b[3]);
+    }
+    // This thread's epilogue chunk of the first round of run_lin: its bias, loaded before the
+    // stage's input wait so that the L2 latency is off the critical path.
+    __device__ __forceinline__ float4 bias_pre(const MkLin &L) const {
+        const int n = min(own_tiles(L), rt);
+        if (tid >= n * 4) return make_float4(0.f, 0.f, 0.f, 0.f);
+        const int t = R + (tid >> 2) * NR, rb = t / L.n_kc, o = rb * 16 + (tid & 3) * 4;
+        return o < L.out ? bias4(L, o) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    // Tiles of one linear, then per 4-row chunk epi(o, kc, v, bias) (o: first output row,
     // kc: K chunk of the tile).  Rows past L.out are skipped.
     template <class Epi>
-    __device__ __forceinline__ void run_lin(const MkLin &L, const __half *xs, const float *sx, Epi epi) {
+    __device__ __forceinline__ void run_lin(const MkLin &L, const __half *xs, const float *sx, float4 bpre, Epi epi) {
         const int n = own_tiles(L);
         for (int i0 = 0; i0 < n; i0 += rt) {
             const int i1 = min(n, i0 + rt);
             tiles(L, xs, sx, i0, i1);
-            if (i0 == 0) trace();
             for (int q = tid; q < (i1 - i0) * 4; q += CT) {
                 const int il = q >> 2, t = R + (i0 + il) * NR, rb = t / L.n_kc, kci = t - rb * L.n_kc;
                 const int o = rb * 16 + (q & 3) * 4;
-                if (o < L.out) epi(o, kci, rows4(il, q & 3));
+                if (o < L.out) epi(o, kci, rows4(il, q & 3), i0 == 0 ? bpre : bias4(L, o));
             }
             csync();
         }
@@ -604,9 +621,11 @@ struct XkConsumer {
     __device__ __forceinline__ void exchange_x(int lprev, int code) {
         const MkParams &p = *pp;
         const int per = d / CS, o0 = rank * per;
-        const MkLin &Lm = p.layers[lprev].mlp;
+        const MkLin &Lm = lay[lprev].mlp;
         const int nkc = Lm.n_kc;
         const uint64_t *mp = xp->mp_ll + (size_t)lprev * xp->nkc * d;
+        const float4 bpre = tid < per / 4 ? __ldg(reinterpret_cast<const float4 *>(Lm.bias + o0 + tid * 4))
+                                          : make_float4(0.f, 0.f, 0.f, 0.f);
         if (tid == 0)
             for (int k = 0; k < nkc; ++k) T->runs[k] = PollRun{mp + (size_t)k * d + o0, k * (per / 2), 0};
         const bool good = poll(nkc, nkc * per / 2, tag(lprev, 4), red);
@@ -615,7 +634,7 @@ struct XkConsumer {
         for (int i = tid; i < per / 4; i += CT) {
             const int o = o0 + i * 4;
             float4 acc = *reinterpret_cast<const float4 *>(land + o);
-            const float4 bb = __ldg(reinterpret_cast<const float4 *>(Lm.bias + o));
+            const float4 bb = i == tid ? bpre : __ldg(reinterpret_cast<const float4 *>(Lm.bias + o));
             acc.x += bb.x; acc.y += bb.y; acc.z += bb.z; acc.w += bb.w;
             for (int k = 0; k < nkc; ++k) {  // fixed order over the K chunks
                 const float4 s4 = *reinterpret_cast<const float4 *>(red + k * per + i * 4);
@@ -717,8 +736,9 @@ struct XkConsumer {
     // ---- stages ----
     __device__ __forceinline__ void stage_qkv(int l) {
         const MkParams &p = *pp;
-        const MkLayer &Ly = p.layers[l];
+        const MkLayer &Ly = lay[l];
         const LnRegs ln1 = ln_prefetch(Ly.ln1_w, Ly.ln1_b);
+        const float4 bpre = bias_pre(Ly.qkv);
         if (l == 0) {
             const float *e = p.mel_emb + (size_t)T->tok * d, *ps = p.mel_pos + (size_t)T->pos * d;
             for (int k = tid; k < d; k += CT) land[k] = e[k] + ps[k];
@@ -732,8 +752,7 @@ struct XkConsumer {
         uint64_t *q = xp->qkv_ll + (size_t)l * 3 * d;
         const uint32_t tg = tag(l, 0);
         const int active = T->active, slot = T->slot, lold = T->lold;
-        run_lin(L, xln, sxln, [&](int o, int, float4 v) {
-            const float4 bb = __ldg(reinterpret_cast<const float4 *>(L.bias + o));
+        run_lin(L, xln, sxln, bpre, [&](int o, int, float4 v, float4 bb) {
             v.x += bb.x; v.y += bb.y; v.z += bb.z; v.w += bb.w;
             ll_st2(q + o, v.x, v.y, tg);
             ll_st2(q + o + 2, v.z, v.w, tg);
@@ -914,27 +933,27 @@ struct XkConsumer {
         trace();
     }
     __device__ __forceinline__ void stage_proj(int l) {
+        const float4 bpre = bias_pre(lay[l].proj);
         exchange_ao(l, 40);
         group_sums(xao, sxao, d);
-        const MkLin &L = pp->layers[l].proj;
+        const MkLin &L = lay[l].proj;
         uint64_t *pv = xp->pv_ll + (size_t)l * d;
         const uint32_t tg = tag(l, 2);
-        run_lin(L, xao, sxao, [&](int o, int, float4 v) {
-            const float4 bb = __ldg(reinterpret_cast<const float4 *>(L.bias + o));
+        run_lin(L, xao, sxao, bpre, [&](int o, int, float4 v, float4 bb) {
             ll_st2(pv + o, v.x + bb.x, v.y + bb.y, tg);
             ll_st2(pv + o + 2, v.z + bb.z, v.w + bb.w, tg);
         });
     }
     __device__ __forceinline__ void stage_fc(int l) {
-        const MkLayer &Ly = pp->layers[l];
+        const MkLayer &Ly = lay[l];
         const LnRegs ln2 = ln_prefetch(Ly.ln2_w, Ly.ln2_b);
+        const float4 bpre = bias_pre(Ly.fc);
         exchange_h(l, 50);
         layernorm(ln2, false);
         const MkLin &L = Ly.fc;
         uint64_t *u = xp->u_ll + (size_t)l * ff;
         const uint32_t tg = tag(l, 3);
-        run_lin(L, xln, sxln, [&](int o, int, float4 v) {
-            const float4 bb = __ldg(reinterpret_cast<const float4 *>(L.bias + o));
+        run_lin(L, xln, sxln, bpre, [&](int o, int, float4 v, float4 bb) {
             ll_st2(u + o, gelu_tanh(v.x + bb.x), gelu_tanh(v.y + bb.y), tg);
             ll_st2(u + o + 2, gelu_tanh(v.z + bb.z), gelu_tanh(v.w + bb.w), tg);
         });
@@ -942,11 +961,11 @@ struct XkConsumer {
     __device__ __forceinline__ void stage_mlp(int l) {
         exchange_u(l, 60);
         group_sums(xu, sxu, ff);
-        const MkLin &L = pp->layers[l].mlp;
+        const MkLin &L = lay[l].mlp;
         uint64_t *mp = xp->mp_ll + (size_t)l * xp->nkc * d;
         const uint32_t tg = tag(l, 4);
         const int dd = d;
-        run_lin(L, xu, sxu, [&](int o, int kci, float4 v) {
+        run_lin(L, xu, sxu, make_float4(0.f, 0.f, 0.f, 0.f), [&](int o, int kci, float4 v, float4) {
             ll_st2(mp + (size_t)kci * dd + o, v.x, v.y, tg);
             ll_st2(mp + (size_t)kci * dd + o + 2, v.z, v.w, tg);
         });
@@ -955,16 +974,17 @@ struct XkConsumer {
         const MkParams &p = *pp;
         const LnRegs lnf = ln_prefetch(p.lnf_w, p.lnf_b);
         const LnRegs fin = ln_prefetch(p.fin_w, p.fin_b);
+        const float4 bpre = bias_pre(p.head);
         exchange_x(p.n_layers - 1, 70);
         layernorm(lnf, true);
         layernorm(fin, false);
         const MkLin &L = p.head;
         const int V = p.mel_vocab;
-        run_lin(L, xln, sxln, [&](int o, int, float4 v) {
-            const float vv[4] = {v.x, v.y, v.z, v.w};
+        run_lin(L, xln, sxln, bpre, [&](int o, int, float4 v, float4 bb) {
+            const float vv[4] = {v.x + bb.x, v.y + bb.y, v.z + bb.z, v.w + bb.w};
 #pragma unroll
             for (int e = 0; e < 4; ++e)
-                if (o + e < V) p.logits[o + e] = vv[e] + __ldg(L.bias + o + e);
+                if (o + e < V) p.logits[o + e] = vv[e];
         });
     }
 };
@@ -983,7 +1003,7 @@ __global__ void __launch_bounds__(NT, 1) xk_decode_kernel(const __grid_constant_
     uint32_t rank_u;
     asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(rank_u));
     const int rank = (int)rank_u, R = blockIdx.x, NR = gridDim.x;
-    const XkSmem SL = xk_layout(p.d, p.ff, xp.rt);
+    const XkSmem SL = xk_layout(p.d, p.ff, xp.rt, p.n_layers);
     XkTab *T = reinterpret_cast<XkTab *>(smem + SL.tab);
     uint64_t *fullp = reinterpret_cast<uint64_t *>(smem + SL.bar);
     uint64_t *emptyp = fullp + NSLOT;
@@ -1008,6 +1028,12 @@ __global__ void __launch_bounds__(NT, 1) xk_decode_kernel(const __grid_constant_
         }
     }
     if (tid <= p.H) T->hs0[tid] = 0x7fffffff;
+    {
+        const int words = (int)(p.n_layers * sizeof(MkLayer) / 4);
+        const uint32_t *src = reinterpret_cast<const uint32_t *>(p.layers);
+        uint32_t *dst = reinterpret_cast<uint32_t *>(smem + SL.lay);
+        for (int i = tid; i < words; i += NT) dst[i] = src[i];
+    }
     if (tid == 0) {
         for (int s = 0; s < NSLOT; ++s) {
             mb_init(fullp + s, 1);
@@ -1076,7 +1102,7 @@ __global__ void __launch_bounds__(NT, 1) xk_decode_kernel(const __grid_constant_
             P.R = R;
             P.NR = NR;
             P.ok = true;
-            P.run(p, *T);
+            P.run(p, *T, reinterpret_cast<const MkLayer *>(smem + SL.lay));
         }
         __syncwarp();
     } else {
@@ -1084,6 +1110,7 @@ __global__ void __launch_bounds__(NT, 1) xk_decode_kernel(const __grid_constant_
         C.xp = &xp;
         C.pp = &p;
         C.T = T;
+        C.lay = reinterpret_cast<const MkLayer *>(smem + SL.lay);
         C.smem = smem;
         C.land = reinterpret_cast<float *>(smem + SL.land);
         C.xln = reinterpret_cast<__half *>(smem + SL.xln);
@@ -1177,7 +1204,7 @@ int xk_config(const ModelView &m, XkConfig *out) {
     if (m.mel_head.tile_bytes > SLOT || m.mel_head.n_kc != 1) return -1;
     // grid: as many 8-CTA clusters as fit at once
     const int rt_guess = 8;
-    size_t smem = xk_layout(m.d, m.ff, rt_guess).total;
+    size_t smem = xk_layout(m.d, m.ff, rt_guess, m.n_layers).total;
     if ((int)smem > optin) return -1;
     if (cudaFuncSetAttribute(xk_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) {
         cudaGetLastError();
@@ -1206,7 +1233,7 @@ int xk_config(const ModelView &m, XkConfig *out) {
         for (const MkLin *x : {&L.qkv, &L.proj, &L.fc, &L.mlp}) rt = std::max(rt, xk_tiles_of(*x, grid));
     }
     rt = std::min(rt, rt_guess);
-    smem = xk_layout(m.d, m.ff, rt).total;
+    smem = xk_layout(m.d, m.ff, rt, m.n_layers).total;
     cudaFuncSetAttribute(xk_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     // probe the launch form: cooperative (co-residency guaranteed) with clusters, else plain
     XkParams probe{};
@@ -1251,7 +1278,7 @@ cudaError_t xk_launch(const MkParams &p, const XkConfig &xc, const XkBufs &b, cu
     xp.nkc = xc.nkc;
     xp.rec_stride = xc.rec_stride;
     xp.dry = 0;
-    return xk_launch_cfg(xp, xc.grid, xk_layout(p.d, p.ff, xc.rt).total, xc.coop != 0, st);
+    return xk_launch_cfg(xp, xc.grid, xk_layout(p.d, p.ff, xc.rt, p.n_layers).total, xc.coop != 0, st);
 }
 
 }  // namespace itts
