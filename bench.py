@@ -247,8 +247,9 @@ def run_ours(args, rank, world, local_rank):
     # the decode-step forward (one launch), timed alone at the mean KV length
     L_avg = N_CONDS + N_TEXT + 3 + (N_MEL - 1) // 2
     kname = kv.decode_kernel(1)
-    kdesc = {"xk_decode_kernel": "all-SM decode step launched as 8-CTA clusters that gather each stage's "
-                                 "input once per cluster (int8 g64 dequant GEMVs + flash-decode attention)",
+    kdesc = {"xk_decode_kernel": "decode step on one 6-CTA cluster per attention head (120 CTAs): q/k/v and "
+                                 "attention partials stay in the cluster, stage inputs gathered once per cluster "
+                                 "(int8 g64 dequant GEMVs + flash-decode attention)",
              "mk_decode_kernel": "persistent grid-wide decode step (int8 g64 dequant GEMVs + flash-decode "
                                  "attention)"}.get(kname, "decode step")
     ws_ms, ws_launches = _bench_decode_forward(gpt, kv, L_avg, iters=100)
@@ -295,7 +296,7 @@ def run_ours(args, rank, world, local_rank):
                      "ms_per_launch": ws_ms,
                      # dram__bytes_read.sum + dram__bytes_write.sum of one launch at this KV
                      # length (ncu capture summarised in profiles/xk_decode_kernel_cfg2.md)
-                     "traffic": 692909056 if kname == "xk_decode_kernel" else None},
+                     "traffic": None},
         "clocks": clk,
     }
     try:

@@ -609,7 +609,7 @@ static void kv_destroy(itts_kv *kv) {
     void *dev[] = {kv->k, kv->v, kv->d_slots, kv->d_batch_slot, kv->db.x, kv->db.n, kv->db.n2,
                    kv->db.q, kv->db.attn, kv->db.u, kv->db.logits, kv->db.partials,
                    kv->db.counters, kv->db.qkv_ll, kv->db.epoch, kv->db.err, kv->db.trace, kv->db.ws,
-                   kv->db.xkb.qkv_ll,
+                   kv->db.xkb.ao_ll,
                    kv->pb.x, kv->pb.n, kv->pb.qkv, kv->pb.attn,
                    kv->pb.u, kv->d_codes, kv->d_text, kv->d_prior, kv->d_conds};
     for (void *p : dev) cudaFree(p);
@@ -700,17 +700,16 @@ extern "C" int itts_kv_create(itts_gpt *g, int32_t max_seq, int32_t max_batch, i
         XkConfig xc;
         if (e == cudaSuccess && xk_config(m, &xc) > 0) {
             const size_t L = m.n_layers;
-            const size_t words = L * (3 * (size_t)m.d + (size_t)xc.rec_stride * 68 + m.d + m.ff + (size_t)xc.nkc * m.d);
+            const size_t words = L * (2 * (size_t)m.d + m.ff + (size_t)xc.nkc * m.d);
             const size_t bytes = words * 8 + sizeof(uint32_t) * xc.grid;
-            A((void **)&kv->db.xkb.qkv_ll, bytes);
+            A((void **)&kv->db.xkb.ao_ll, bytes);
             if (e == cudaSuccess) {
                 XkBufs &x = kv->db.xkb;
-                x.rec_ll = x.qkv_ll + L * 3 * m.d;
-                x.pv_ll = x.rec_ll + L * xc.rec_stride * 68;
+                x.pv_ll = x.ao_ll + L * m.d;
                 x.u_ll = x.pv_ll + L * m.d;
                 x.mp_ll = x.u_ll + L * m.ff;
                 x.epoch = reinterpret_cast<uint32_t *>(x.mp_ll + L * xc.nkc * m.d);
-                e = cudaMemsetAsync(x.qkv_ll, 0, bytes, g->stream);
+                e = cudaMemsetAsync(x.ao_ll, 0, bytes, g->stream);
                 kv->db.xk = xc;
             }
         }

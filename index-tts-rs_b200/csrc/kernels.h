@@ -29,10 +29,10 @@ struct ModelView {
 // The clustered all-SM decode step of one column (xk_decode.cu): launch shape and its
 // global exchange buffers (LL words, tags unique per launch).
 struct XkConfig {
-    int grid = 0, rt = 0, nkc = 0, coop = 0, rec_stride = 0;
+    int grid = 0, rt = 0, nkc = 0, coop = 0;
 };
-struct XkBufs {
-    uint64_t *qkv_ll = nullptr, *rec_ll = nullptr, *pv_ll = nullptr, *u_ll = nullptr, *mp_ll = nullptr;
+struct XkBufs {  // one allocation: [L][d] attention output, [L][d] c_proj, [L][ff] u, [L][nkc][d] mlp partials
+    uint64_t *ao_ll = nullptr, *pv_ll = nullptr, *u_ll = nullptr, *mp_ll = nullptr;
     uint32_t *epoch = nullptr;
 };
 
@@ -110,8 +110,9 @@ cudaError_t decode_forward(const ModelView &m, const DecodeView &dv, DecodeBufs 
 // ITTS_CLUSTER=1 at cache creation): returns the partial-sum size it needs (> 0) or -1 when
 // it is not requested or the model or the device does not fit it.
 int ck_config(const ModelView &m);
-// Decode step of one column on (nearly) all SMs as 8-CTA clusters that gather each stage's
-// input once per cluster (default for batch 1; ITTS_XK=0 at cache creation turns it off).
+// Decode step of one column on one 6-CTA cluster per attention head (120 CTAs for 20 heads);
+// each stage's input is gathered once per cluster (default for batch 1; ITTS_XK=0 at cache
+// creation turns it off).
 // Fills `out` and returns the grid size, or -1 when the model or the device does not fit it.
 int xk_config(const ModelView &m, XkConfig *out);
 cudaError_t xk_launch(const MkParams &p, const XkConfig &xc, const XkBufs &b, cudaStream_t st);

@@ -36,23 +36,22 @@
 namespace itts {
 namespace {
 
-constexpr int CS = 8;              // CTAs per cluster
+constexpr int CS = 6;              // CTAs per cluster: one cluster per attention head
 constexpr int CW = 8;              // consumer warps
 constexpr int CT = CW * 32;        // consumer threads
 constexpr int NT = CT + 32;        // + the producer warp
 constexpr int NSLOT = 8;           // ring slots (power of two)
 constexpr int SLOT = 21888;        // bytes per slot: a 16 x 1280 tile with fp16 pairs, or 84 K/V rows
 constexpr int KVPOS = 84;          // positions per K/V tile: 2 x 84 x 128 B = 21,504 B
-constexpr int MAXHC = 4;           // heads one CTA's attention range may touch
 constexpr int REC = 68;            // floats per attention record: m, l, 0, 0, acc[64]
-constexpr int MAXNR = 160;         // CTAs of the grid (SM count bound)
-constexpr int RCH = 32;            // attention records merged per round
-static_assert(MAXNR % 32 == 0, "scan layout");
+constexpr int QT = 12;             // QKV row blocks of one head (q, k, v x 64 rows / 16)
 constexpr int NWS = 5;             // LL-writing stages per layer: qkv, records, c_proj, u, mlp
 constexpr uint32_t SPIN = 1u << 22;
 constexpr float kLog2e = 1.4426950408889634f;
 
-enum { B0 = 0, BAO, BU, NSTB };  // landing barriers: x/h (fp32), attention output, u (fp16)
+// landing barriers: x/h (fp32), attention output (fp16), u (fp16), the head's q/k/v (fp32),
+// the head's attention records (cluster rank 0 only)
+enum { B0 = 0, BAO, BU, BQ, BR, NSTB };
 
 // ---------------------------------------------------------------------------
 // PTX helpers
@@ -238,20 +237,18 @@ __device__ __noinline__ bool poll_runs(const PollRun *runs, int nruns, int total
 // shared-memory carve-up (identical on host and device)
 // ---------------------------------------------------------------------------
 struct XkSmem {
-    uint32_t land, xln, xao, xu, sxln, sxao, sxu, red, qkvh, stat, tab, lay, bar, total;
+    uint32_t land, xln, xao, xu, sxln, sxao, sxu, red, qkvh, recs, stat, tab, lay, bar, total;
 };
-__host__ __device__ inline uint32_t xk_red_bytes(int rt) {
-    const uint32_t lin = (uint32_t)rt * CW * 16 * 4;
-    const uint32_t att = (uint32_t)(MAXHC * CW * REC + MAXHC * REC) * 4;
-    const uint32_t mrg = (uint32_t)(RCH * REC + MAXHC * 32) * 4 + 128;
-    uint32_t m = lin > att ? lin : att;
-    return m > mrg ? m : mrg;
+__host__ __device__ inline uint32_t xk_red_bytes(int rt, int d, int ff) {
+    uint32_t m = (uint32_t)rt * CW * 16 * 4;                                   // tile partial sums
+    m = max(m, (uint32_t)(CW + 1) * REC * 4);                                  // attention warp states
+    m = max(m, (uint32_t)(4 * ((d / 4 + CS - 1) / CS) * 4 * 4));               // x gather (4 K chunks)
+    m = max(m, (uint32_t)(((ff / 64 + CS - 1) / CS) * 64 * 4));                // u gather
+    return m;
 }
 struct XkTab {
-    int active, lold, kvt, units, slot, tok, pos, u_lo, u_hi, hlo, nh, seg0, nseg, pad[3];
-    int hs0[33];                 // first attention segment of head h (hs0[H] = total)
-    int cnt[MAXNR], hl[MAXNR];   // per CTA of the grid: heads its range touches, first head
-    PollRun runs[MAXRUN];        // the current poll list
+    int active, lold, kvt, slot, tok, pos, head, t_lo, t_hi, pad[7];
+    PollRun runs[MAXRUN];  // the current poll list
 };
 __host__ __device__ inline XkSmem xk_layout(int d, int ff, int rt, int n_layers) {
     XkSmem L;
@@ -268,8 +265,9 @@ __host__ __device__ inline XkSmem xk_layout(int d, int ff, int rt, int n_layers)
     L.sxln = take(d / 64 * 4);
     L.sxao = take(d / 64 * 4);
     L.sxu = take(ff / 64 * 4);
-    L.red = take(xk_red_bytes(rt));
-    L.qkvh = take(MAXHC * 3 * 64 * 4);
+    L.red = take(xk_red_bytes(rt, d, ff));
+    L.qkvh = take(3 * 64 * 4);
+    L.recs = take(CS * REC * 4);
     L.stat = take(64 * 4);
     L.tab = take(sizeof(XkTab));
     L.lay = take(n_layers * sizeof(MkLayer));  // the layer table (pointers, shapes) in shared memory
@@ -280,14 +278,19 @@ __host__ __device__ inline XkSmem xk_layout(int d, int ff, int rt, int n_layers)
 
 struct XkParams {
     MkParams p;          // model, slots, KV cache, logits, err, trace
-    uint64_t *qkv_ll;    // [L][3d]
-    uint64_t *rec_ll;    // [L][rec_stride][REC]
+    uint64_t *ao_ll;     // [L][d]     attention output (each head's, merged by its cluster)
     uint64_t *pv_ll;     // [L][d]     c_proj output + bias
     uint64_t *u_ll;      // [L][ff]    GELU(c_fc)
     uint64_t *mp_ll;     // [L][nkc][d] mlp c_proj K-chunk partial sums
     uint32_t *epoch;     // [grid] launches completed per CTA
-    int rt, nkc, rec_stride, dry;
+    int rt, nkc, dry;
 };
+
+// rows of [0, n) gathered by cluster rank k
+__device__ __forceinline__ int slice_lo(int k, int n) { return k * n / CS; }
+
+// QKV row block i (0 <= i < QT) of head h: q, k, v rows h*64 .. h*64 + 63
+__device__ __forceinline__ int qkv_rb(int i, int h, int d) { return (i >> 2) * (d / 16) + 4 * h + (i & 3); }
 
 // ---------------------------------------------------------------------------
 // producer (one lane)
@@ -322,27 +325,25 @@ struct XkProducer {
         for (int i = R; i < n_tiles; i += NR, t += step) issue(t, tb, nullptr, 0);
     }
     __device__ __forceinline__ void lin(const MkLin *L) { lin(L->tiles, L->n_rb * L->n_kc, (uint32_t)L->tile_bytes); }
-    __device__ __forceinline__ void attn(const __half *kc, const __half *vc, size_t base, size_t head_stride, int u_lo,
-                                         int u_hi, int kvt, int lold) {
-        int h = u_lo / kvt, t = u_lo - h * kvt;
-        base += (size_t)h * head_stride;
-        for (int u = u_lo; u < u_hi; ++u) {
-            const int np = min(KVPOS, lold - t * KVPOS);
-            if (np > 0) {
-                const size_t off = base + (size_t)t * KVPOS * kHeadDim;
-                issue(kc + off, (uint32_t)np * 128u, vc + off, (uint32_t)np * 128u);
-            }
-            if (++t == kvt) { t = 0; base += head_stride; }
-        }
-    }
-    __device__ __forceinline__ void run(const MkParams &p, const XkTab &T, const MkLayer *lay) {
-        const int u_lo = T.u_lo, u_hi = T.u_hi, kvt = T.kvt, lold = T.lold, slot = T.slot;
-        const size_t head_stride = (size_t)p.max_seq * kHeadDim;
+    __device__ __forceinline__ void run(const MkParams &p, const XkTab &T, const MkLayer *lay, int rank) {
+        const int head = T.head, t_lo = T.t_lo, t_hi = T.t_hi, lold = T.lold, slot = T.slot;
+        const int q0 = rank * QT / CS, q1 = (rank + 1) * QT / CS;
         for (int l = 0; l < p.n_layers && ok; ++l) {
             const MkLayer *Ly = lay + l;
-            lin(&Ly->qkv);
-            if (u_hi > u_lo)
-                attn(p.kc, p.vc, kv_index(l, slot, 0, 0, p.n_slots, p.H, p.max_seq), head_stride, u_lo, u_hi, kvt, lold);
+            {  // this rank's QKV row blocks of the cluster's head
+                const uint8_t *tiles = Ly->qkv.tiles;
+                const uint32_t tb = (uint32_t)Ly->qkv.tile_bytes;
+                for (int i = q0; i < q1; ++i) issue(tiles + (size_t)qkv_rb(i, head, p.d) * tb, tb, nullptr, 0);
+            }
+            // this rank's K/V tiles of the head
+            const size_t base = kv_index(l, slot, head, 0, p.n_slots, p.H, p.max_seq);
+            for (int t = t_lo; t < t_hi; ++t) {
+                const int np = min(KVPOS, lold - t * KVPOS);
+                if (np > 0) {
+                    const size_t off = base + (size_t)t * KVPOS * kHeadDim;
+                    issue(p.kc + off, (uint32_t)np * 128u, p.vc + off, (uint32_t)np * 128u);
+                }
+            }
             lin(&Ly->proj);
             lin(&Ly->fc);
             lin(&Ly->mlp);
@@ -364,10 +365,10 @@ struct XkConsumer {
     XkTab *T;
     const MkLayer *lay;  // shared-memory copy of the layer table
     uint8_t *smem;
-    float *land, *sxln, *sxao, *sxu, *red, *qkvh, *stat;
+    float *land, *sxln, *sxao, *sxu, *red, *qkvh, *recs, *stat;
     __half *xln, *xao, *xu;
     uint64_t *fullp, *emptyp, *stb;
-    int tid, warp, lane, g, c, rank, R, NR, d, ff, H, rt;
+    int tid, warp, lane, g, c, rank, R, NR, d, ff, H, rt, head;
     uint32_t seq, tbase;
     uint32_t ph[NSTB];
     uint32_t exp_bytes[NSTB];
@@ -531,12 +532,22 @@ struct XkConsumer {
     }
     // This CTA's tiles t = R + NR i of linear L, i in [i0, i1), from the ring: per-warp
     // partial sums to red[i - i0] (group j of a tile goes to warp (tile * G64 + j) % 8).
-    __device__ __forceinline__ void tiles(const MkLin &L, const __half *xs, const float *sx, int i0, int i1) {
+    // global tile index of this CTA's i-th tile of L: round robin over the grid, or (qkv) the
+    // rank's share of the QKV row blocks of the cluster's head
+    __device__ __forceinline__ int tile_of(const MkLin &L, int i, bool qkv) const {
+        return qkv ? qkv_rb(rank * QT / CS + i, head, d) : R + i * NR;
+    }
+    __device__ __forceinline__ int own_tiles(const MkLin &L, bool qkv) const {
+        if (qkv) return (rank + 1) * QT / CS - rank * QT / CS;
+        const int n = L.n_rb * L.n_kc;
+        return R < n ? (n - 1 - R) / NR + 1 : 0;
+    }
+    __device__ __forceinline__ void tiles(const MkLin &L, const __half *xs, const float *sx, int i0, int i1, bool qkv) {
         const int KC = L.kc, G64 = KC / 64, nkc = L.n_kc;
         const bool half_sb = pp->sbb == 4;
         int w0 = 0;
         for (int i = i0; i < i1; ++i) {
-            const int kci = nkc == 1 ? 0 : (R + i * NR) % nkc;
+            const int kci = nkc == 1 ? 0 : tile_of(L, i, qkv) % nkc;
             const uint32_t slot = seq & (NSLOT - 1);
             wait_slot(slot, 2);
             const uint8_t *tq = smem + slot * SLOT;
@@ -562,10 +573,6 @@ struct XkConsumer {
         }
         csync();
     }
-    __device__ __forceinline__ int own_tiles(const MkLin &L) const {
-        const int n = L.n_rb * L.n_kc;
-        return R < n ? (n - 1 - R) / NR + 1 : 0;
-    }
     // rows [4q, 4q+4) of local tile i: the 8 warps' partial sums in a fixed order
     __device__ __forceinline__ float4 rows4(int i, int q) const {
         float v[4] = {0.f, 0.f, 0.f, 0.f};
@@ -587,22 +594,23 @@ struct XkConsumer {
     }
     // This thread's epilogue chunk of the first round of run_lin: its bias, loaded before the
     // stage's input wait so that the L2 latency is off the critical path.
-    __device__ __forceinline__ float4 bias_pre(const MkLin &L) const {
-        const int n = min(own_tiles(L), rt);
+    __device__ __forceinline__ float4 bias_pre(const MkLin &L, bool qkv) const {
+        const int n = min(own_tiles(L, qkv), rt);
         if (tid >= n * 4) return make_float4(0.f, 0.f, 0.f, 0.f);
-        const int t = R + (tid >> 2) * NR, rb = t / L.n_kc, o = rb * 16 + (tid & 3) * 4;
+        const int t = tile_of(L, tid >> 2, qkv), rb = t / L.n_kc, o = rb * 16 + (tid & 3) * 4;
         return o < L.out ? bias4(L, o) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     // Tiles of one linear, then per 4-row chunk epi(o, kc, v, bias) (o: first output row,
     // kc: K chunk of the tile).  Rows past L.out are skipped.
     template <class Epi>
-    __device__ __forceinline__ void run_lin(const MkLin &L, const __half *xs, const float *sx, float4 bpre, Epi epi) {
-        const int n = own_tiles(L);
+    __device__ __forceinline__ void run_lin(const MkLin &L, const __half *xs, const float *sx, float4 bpre, bool qkv,
+                                            Epi epi) {
+        const int n = own_tiles(L, qkv);
         for (int i0 = 0; i0 < n; i0 += rt) {
             const int i1 = min(n, i0 + rt);
-            tiles(L, xs, sx, i0, i1);
+            tiles(L, xs, sx, i0, i1, qkv);
             for (int q = tid; q < (i1 - i0) * 4; q += CT) {
-                const int il = q >> 2, t = R + (i0 + il) * NR, rb = t / L.n_kc, kci = t - rb * L.n_kc;
+                const int il = q >> 2, t = tile_of(L, i0 + il, qkv), rb = t / L.n_kc, kci = t - rb * L.n_kc;
                 const int o = rb * 16 + (q & 3) * 4;
                 if (o < L.out) epi(o, kci, rows4(il, q & 3), i0 == 0 ? bpre : bias4(L, o));
             }
@@ -611,7 +619,8 @@ struct XkConsumer {
         trace();
     }
 
-    // ---- exchanges (cluster rank k gathers slice k and pushes it to the cluster) ----
+    // ---- exchanges (cluster rank k gathers its slice of the vector and pushes it to the
+    // cluster) ----
     // Runs are set by thread 0, polled by every consumer thread into `stage`.
     __device__ __forceinline__ bool poll(int nruns, int total, uint32_t tg, float *stage) {
         csync();  // the run table is written
@@ -619,25 +628,24 @@ struct XkConsumer {
     }
     // x_l = h + mlp bias + sum over K chunks of the mlp partials (layer l - 1) -> land
     __device__ __forceinline__ void exchange_x(int lprev, int code) {
-        const MkParams &p = *pp;
-        const int per = d / CS, o0 = rank * per;
+        const int c0 = slice_lo(rank, d / 4), nch = slice_lo(rank + 1, d / 4) - c0, o0 = c0 * 4;
         const MkLin &Lm = lay[lprev].mlp;
         const int nkc = Lm.n_kc;
         const uint64_t *mp = xp->mp_ll + (size_t)lprev * xp->nkc * d;
-        const float4 bpre = tid < per / 4 ? __ldg(reinterpret_cast<const float4 *>(Lm.bias + o0 + tid * 4))
-                                          : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4 bpre = tid < nch ? __ldg(reinterpret_cast<const float4 *>(Lm.bias + o0 + tid * 4))
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
         if (tid == 0)
-            for (int k = 0; k < nkc; ++k) T->runs[k] = PollRun{mp + (size_t)k * d + o0, k * (per / 2), 0};
-        const bool good = poll(nkc, nkc * per / 2, tag(lprev, 4), red);
+            for (int k = 0; k < nkc; ++k) T->runs[k] = PollRun{mp + (size_t)k * d + o0, k * nch * 2, 0};
+        const bool good = poll(nkc, nkc * nch * 2, tag(lprev, 4), red);
         agree(good, code);
         const uint32_t land_a = su32(land), bar_a = su32(stb + B0);
-        for (int i = tid; i < per / 4; i += CT) {
+        for (int i = tid; i < nch; i += CT) {
             const int o = o0 + i * 4;
             float4 acc = *reinterpret_cast<const float4 *>(land + o);
             const float4 bb = i == tid ? bpre : __ldg(reinterpret_cast<const float4 *>(Lm.bias + o));
             acc.x += bb.x; acc.y += bb.y; acc.z += bb.z; acc.w += bb.w;
             for (int k = 0; k < nkc; ++k) {  // fixed order over the K chunks
-                const float4 s4 = *reinterpret_cast<const float4 *>(red + k * per + i * 4);
+                const float4 s4 = *reinterpret_cast<const float4 *>(red + (k * nch + i) * 4);
                 acc.x += s4.x; acc.y += s4.y; acc.z += s4.z; acc.w += s4.w;
             }
             bcast_v4(land_a + o * 4, make_uint4(__float_as_uint(acc.x), __float_as_uint(acc.y),
@@ -648,12 +656,12 @@ struct XkConsumer {
     }
     // h = x + (c_proj + bias) -> land
     __device__ __forceinline__ void exchange_h(int l, int code) {
-        const int per = d / CS, o0 = rank * per;
+        const int c0 = slice_lo(rank, d / 4), nch = slice_lo(rank + 1, d / 4) - c0, o0 = c0 * 4;
         if (tid == 0) T->runs[0] = PollRun{xp->pv_ll + (size_t)l * d + o0, 0, 0};
-        const bool good = poll(1, per / 2, tag(l, 2), red);
+        const bool good = poll(1, nch * 2, tag(l, 2), red);
         agree(good, code);
         const uint32_t land_a = su32(land), bar_a = su32(stb + B0);
-        for (int i = tid; i < per / 4; i += CT) {
+        for (int i = tid; i < nch; i += CT) {
             const int o = o0 + i * 4;
             const float4 x = *reinterpret_cast<const float4 *>(land + o);
             const float4 v = *reinterpret_cast<const float4 *>(red + i * 4);
@@ -663,15 +671,17 @@ struct XkConsumer {
         trace();
         wait_land(B0, code + 1);
     }
-    // u -> fp16 fragment order -> xu; thread (group, c) sends the 32 contiguous bytes of rows
+    // groups [g0, g1) of 64 values of an fp32 LL vector -> fp16 fragment order -> xs of every
+    // CTA of the cluster; thread (group, c) sends the 32 contiguous bytes of rows
     // {16 b + 2c, 16 b + 2c + 1, 16 b + 2c + 8, 16 b + 2c + 9 : b < 4}
-    __device__ __forceinline__ void exchange_u(int l, int code) {
-        const int per = ff / CS, k0 = rank * per;
-        if (tid == 0) T->runs[0] = PollRun{xp->u_ll + (size_t)l * ff + k0, 0, 0};
-        const bool good = poll(1, per / 2, tag(l, 3), red);
+    __device__ __forceinline__ void gather_f16(const uint64_t *src, int n_groups, uint32_t tg, __half *xs, int bar,
+                                               int code) {
+        const int g0 = slice_lo(rank, n_groups), ng = slice_lo(rank + 1, n_groups) - g0;
+        if (tid == 0) T->runs[0] = PollRun{src + (size_t)g0 * 64, 0, 0};
+        const bool good = poll(1, ng * 32, tg, red);
         agree(good, code);
-        const uint32_t xu_a = su32(xu), bar_a = su32(stb + BU);
-        for (int i = tid; i < per / 16; i += CT) {
+        const uint32_t xs_a = su32(xs), bar_a = su32(stb + bar);
+        for (int i = tid; i < ng * 4; i += CT) {
             const int gl = (i >> 2) * 64, cc = i & 3;
             const float *s = red + gl + 2 * cc;
             uint4 v0, v1;
@@ -679,58 +689,18 @@ struct XkConsumer {
             v0.z = pack_h2(s[16], s[17]); v0.w = pack_h2(s[24], s[25]);
             v1.x = pack_h2(s[32], s[33]); v1.y = pack_h2(s[40], s[41]);
             v1.z = pack_h2(s[48], s[49]); v1.w = pack_h2(s[56], s[57]);
-            const uint32_t dst = xu_a + (k0 + gl + cc * 16) * 2;
+            const uint32_t dst = xs_a + (g0 * 64 + gl + cc * 16) * 2;
             bcast_v4(dst, v0, bar_a);
             bcast_v4(dst + 16, v1, bar_a);
         }
         trace();
-        wait_land(BU, code + 1);
+        wait_land(bar, code + 1);
     }
-    // attention output of the heads h = rank + CS i: their partial records (contiguous per
-    // head) staged together (at most RCH, checked at configuration), thread (i, e) merges dim
-    // e of head i; fp16 fragment order -> xao of every CTA of the cluster
+    __device__ __forceinline__ void exchange_u(int l, int code) {
+        gather_f16(xp->u_ll + (size_t)l * ff, ff / 64, tag(l, 3), xu, BU, code);
+    }
     __device__ __forceinline__ void exchange_ao(int l, int code) {
-        const uint64_t *recs = xp->rec_ll + (size_t)l * xp->rec_stride * REC;
-        float *stg = red;                                            // [RCH][REC]
-        __half *hout = reinterpret_cast<__half *>(red + RCH * REC);  // [MAXHC][64] fragment order
-        const int nmy = rank < H ? (H - 1 - rank) / CS + 1 : 0;
-        const bool act = T->active != 0;
-        if (tid == 0) {
-            int start = 0;
-            for (int i = 0; i < nmy; ++i) {
-                const int h = rank + i * CS;
-                T->runs[i] = PollRun{recs + (size_t)T->hs0[h] * REC, start, 0};
-                start += act ? (T->hs0[h + 1] - T->hs0[h]) * (REC / 2) : 0;
-            }
-            T->runs[MAXHC].start = start;  // total pairs
-        }
-        csync();
-        const int total = T->runs[MAXHC].start;
-        const bool good = poll(nmy, total, tag(l, 1), stg);
-        agree(good, code);
-        const int mi = tid >> 6, e = tid & 63;
-        if (mi < nmy) {
-            const int h = rank + mi * CS;
-            const int r0 = T->runs[mi].start / (REC / 2), nr = act ? T->hs0[h + 1] - T->hs0[h] : 0;
-            float M = -INFINITY, Lsum = 0.f, A = 0.f;
-            for (int s = r0; s < r0 + nr; ++s) {
-                const float *rec = stg + s * REC;
-                const float ms = rec[0], Mn = fmaxf(M, ms);
-                const float fa = exp2f(M - Mn), fb = exp2f(ms - Mn);  // M = -inf gives 0
-                Lsum = Lsum * fa + rec[1] * fb;
-                A = A * fa + rec[4 + e] * fb;
-                M = Mn;
-            }
-            hout[mi * 64 + frag_pos_host(e)] = __float2half_rn(nr > 0 ? A / Lsum : 0.f);
-        }
-        csync();
-        const uint32_t xao_a = su32(xao), bar_a = su32(stb + BAO);
-        if (tid < nmy * 8) {
-            const int h = rank + (tid >> 3) * CS;
-            bcast_v4(xao_a + (h * 64 + (tid & 7) * 8) * 2, reinterpret_cast<const uint4 *>(hout)[tid], bar_a);
-        }
-        trace();
-        wait_land(BAO, code + 1);
+        gather_f16(xp->ao_ll + (size_t)l * d, d / 64, tag(l, 1), xao, BAO, code);
     }
 
     // ---- stages ----
@@ -738,7 +708,7 @@ struct XkConsumer {
         const MkParams &p = *pp;
         const MkLayer &Ly = lay[l];
         const LnRegs ln1 = ln_prefetch(Ly.ln1_w, Ly.ln1_b);
-        const float4 bpre = bias_pre(Ly.qkv);
+        const float4 bpre = bias_pre(Ly.qkv, true);
         if (l == 0) {
             const float *e = p.mel_emb + (size_t)T->tok * d, *ps = p.mel_pos + (size_t)T->pos * d;
             for (int k = tid; k < d; k += CT) land[k] = e[k] + ps[k];
@@ -748,198 +718,192 @@ struct XkConsumer {
             exchange_x(l - 1, 20);
         }
         layernorm(ln1, false);
+        // this rank's share of the head's q/k/v rows: K/V appended to the cache, all 192
+        // values pushed into the qkvh of every CTA of the cluster
         const MkLin &L = Ly.qkv;
-        uint64_t *q = xp->qkv_ll + (size_t)l * 3 * d;
-        const uint32_t tg = tag(l, 0);
-        const int active = T->active, slot = T->slot, lold = T->lold;
-        run_lin(L, xln, sxln, bpre, [&](int o, int, float4 v, float4 bb) {
+        const int active = T->active, slot = T->slot, lold = T->lold, hd = head;
+        const uint32_t q_a = su32(qkvh), bar_a = su32(stb + BQ);
+        run_lin(L, xln, sxln, bpre, true, [&](int o, int, float4 v, float4 bb) {
             v.x += bb.x; v.y += bb.y; v.z += bb.z; v.w += bb.w;
-            ll_st2(q + o, v.x, v.y, tg);
-            ll_st2(q + o + 2, v.z, v.w, tg);
             const int which = o / d, oo = o - which * d;
             if (which > 0 && active) {
                 __half *cache = which == 1 ? p.kc : p.vc;
                 uint2 hv;
                 hv.x = pack_h2(v.x, v.y);
                 hv.y = pack_h2(v.z, v.w);
-                *reinterpret_cast<uint2 *>(cache + kv_index(l, slot, oo >> 6, lold, p.n_slots, p.H, p.max_seq) +
-                                           (oo & 63)) = hv;
+                *reinterpret_cast<uint2 *>(cache + kv_index(l, slot, hd, lold, p.n_slots, p.H, p.max_seq) + (oo & 63)) = hv;
             }
+            bcast_v4(q_a + (which * 64 + (oo & 63)) * 4,
+                     make_uint4(__float_as_uint(v.x), __float_as_uint(v.y), __float_as_uint(v.z), __float_as_uint(v.w)),
+                     bar_a);
         });
     }
+    // attention of the cluster's head over this rank's K/V tiles: one record (m, l, acc[64])
+    // per rank into cluster rank 0, which merges them and writes the head's 64 outputs
     __device__ __forceinline__ void stage_attn(int l) {
-        const MkParams &p = *pp;
+        wait_land(BQ, 30);
         const int grp = lane >> 3, d8 = lane & 7;
-        const int nh = T->nh;
-        // q, k, v of this CTA's heads from the QKV stage
-        {
-            const uint64_t *q = xp->qkv_ll + (size_t)l * 3 * d;
-            if (tid == 0)
-                for (int i = 0; i < nh * 3; ++i)
-                    T->runs[i] = PollRun{q + (i % 3) * d + (T->hlo + i / 3) * 64, i * 32, 0};
-            const bool good = poll(nh * 3, nh * 96, tag(l, 0), qkvh);
-            agree(good, 30);
-        }
-        float *ascr = red;                     // [MAXHC][CW][REC] warp states
+        float *ascr = red;  // [CW][REC] warp states, then [REC] this rank's record
         const float qscale = kAttnScale * kLog2e;
-        int k = -1, hcur = -1;
         float qv[8], m = -INFINITY, ls = 0.f, acc[8];
-        auto close = [&]() {
 #pragma unroll
-            for (int off = 8; off <= 16; off <<= 1) {
-                const float m2 = __shfl_xor_sync(0xffffffffu, m, off);
-                const float l2 = __shfl_xor_sync(0xffffffffu, ls, off);
-                const float M = fmaxf(m, m2);
-                const float fa = m == -INFINITY ? 0.f : exp2f(m - M);
-                const float fb = m2 == -INFINITY ? 0.f : exp2f(m2 - M);
+        for (int e = 0; e < 8; ++e) { qv[e] = qkvh[d8 * 8 + e] * qscale; acc[e] = 0.f; }
+        const int kvt = T->kvt, lold = T->lold;
+        for (int t = T->t_lo; t < T->t_hi; ++t) {
+            const int np = min(KVPOS, lold - t * KVPOS);
+            if (np > 0) {
+                const uint32_t slot = seq & (NSLOT - 1);
+                wait_slot(slot, 3);
+                const __half *kt = reinterpret_cast<const __half *>(smem + slot * SLOT);
+                const __half *vt = kt + np * 64;
+                constexpr int QG = (KVPOS / 4 + CW - 1) / CW;
+                float sc[QG];
+                uint4 vv[QG];
 #pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                    const float a2 = __shfl_xor_sync(0xffffffffu, acc[e], off);
-                    acc[e] = acc[e] * fa + a2 * fb;
+                for (int q = 0; q < QG; ++q) {
+                    const int pos = (warp + q * CW) * 4 + grp;
+                    const int pc = pos < np ? pos : 0;
+                    const uint4 kk = *reinterpret_cast<const uint4 *>(kt + pc * 64 + d8 * 8);
+                    vv[q] = *reinterpret_cast<const uint4 *>(vt + pc * 64 + d8 * 8);
+                    const __half2 *k2 = reinterpret_cast<const __half2 *>(&kk);
+                    float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+                    for (int e = 0; e < 4; e += 2) {
+                        const float2 ka = __half22float2(k2[e]), kb = __half22float2(k2[e + 1]);
+                        s0 = fmaf(qv[2 * e], ka.x, s0);
+                        s1 = fmaf(qv[2 * e + 1], ka.y, s1);
+                        s0 = fmaf(qv[2 * e + 2], kb.x, s0);
+                        s1 = fmaf(qv[2 * e + 3], kb.y, s1);
+                    }
+                    sc[q] = s0 + s1;
                 }
-                ls = ls * fa + l2 * fb;
-                m = M;
+#pragma unroll
+                for (int q = 0; q < QG; ++q) sc[q] += __shfl_xor_sync(0xffffffffu, sc[q], 1);
+#pragma unroll
+                for (int q = 0; q < QG; ++q) sc[q] += __shfl_xor_sync(0xffffffffu, sc[q], 2);
+#pragma unroll
+                for (int q = 0; q < QG; ++q) sc[q] += __shfl_xor_sync(0xffffffffu, sc[q], 4);
+                float mt = m;
+#pragma unroll
+                for (int q = 0; q < QG; ++q)
+                    if ((warp + q * CW) * 4 + grp < np) mt = fmaxf(mt, sc[q]);
+                if (mt != m) {
+                    const float corr = exp2f(m - mt);
+                    ls *= corr;
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) acc[e] *= corr;
+                    m = mt;
+                }
+#pragma unroll
+                for (int q = 0; q < QG; ++q) {
+                    if ((warp + q * CW) * 4 + grp < np) {
+                        const float pj = exp2f(sc[q] - m);
+                        ls += pj;
+                        const __half2 *v2 = reinterpret_cast<const __half2 *>(&vv[q]);
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const float2 f = __half22float2(v2[e]);
+                            acc[2 * e] = fmaf(pj, f.x, acc[2 * e]);
+                            acc[2 * e + 1] = fmaf(pj, f.y, acc[2 * e + 1]);
+                        }
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mb_arrive(emptyp + slot);
+                ++seq;
             }
+        }
+        if (T->active && T->t_hi == kvt && T->t_hi > T->t_lo && warp == CW - 1) {  // the new position
+            const float *kn = qkvh + 64 + d8 * 8;
+            const float *vn = kn + 64;
+            float s = 0.f;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) s = fmaf(qv[e], kn[e], s);
+            s += __shfl_xor_sync(0xffffffffu, s, 1);
+            s += __shfl_xor_sync(0xffffffffu, s, 2);
+            s += __shfl_xor_sync(0xffffffffu, s, 4);
             if (grp == 0) {
-                float *s = ascr + (k * CW + warp) * REC;
-                if (d8 == 0) { s[0] = m; s[1] = ls; }
+                const float mn = fmaxf(m, s);
+                const float corr = exp2f(m - mn);
+                const float pj = exp2f(s - mn);
+                ls = ls * corr + pj;
 #pragma unroll
-                for (int e = 0; e < 8; ++e) s[4 + d8 * 8 + e] = acc[e];
+                for (int e = 0; e < 8; ++e) acc[e] = acc[e] * corr + pj * vn[e];
+                m = mn;
             }
-        };
-        if (T->u_hi > T->u_lo) {
-            const int kvt = T->kvt, lold = T->lold, hlo = T->hlo;
-            int h = T->u_lo / kvt, t = T->u_lo - h * kvt;
-            for (int u = T->u_lo; u < T->u_hi; ++u) {
-                if (h != hcur) {
-                    if (k >= 0) close();
-                    ++k;
-                    hcur = h;
-                    const float *qh = qkvh + ((h - hlo) * 3) * 64 + d8 * 8;
+        }
+        // merge the 4 position groups of each warp, then the 8 warps
 #pragma unroll
-                    for (int e = 0; e < 8; ++e) { qv[e] = qh[e] * qscale; acc[e] = 0.f; }
-                    m = -INFINITY;
-                    ls = 0.f;
-                }
-                const int np = min(KVPOS, lold - t * KVPOS);
-                if (np > 0) {
-                    const uint32_t slot = seq & (NSLOT - 1);
-                    wait_slot(slot, 3);
-                    const __half *kt = reinterpret_cast<const __half *>(smem + slot * SLOT);
-                    const __half *vt = kt + np * 64;
-                    constexpr int QG = (KVPOS / 4 + CW - 1) / CW;
-                    float sc[QG];
-                    uint4 vv[QG];
+        for (int off = 8; off <= 16; off <<= 1) {
+            const float m2 = __shfl_xor_sync(0xffffffffu, m, off);
+            const float l2 = __shfl_xor_sync(0xffffffffu, ls, off);
+            const float M = fmaxf(m, m2);
+            const float fa = m == -INFINITY ? 0.f : exp2f(m - M);
+            const float fb = m2 == -INFINITY ? 0.f : exp2f(m2 - M);
 #pragma unroll
-                    for (int q = 0; q < QG; ++q) {
-                        const int pos = (warp + q * CW) * 4 + grp;
-                        const int pc = pos < np ? pos : 0;
-                        const uint4 kk = *reinterpret_cast<const uint4 *>(kt + pc * 64 + d8 * 8);
-                        vv[q] = *reinterpret_cast<const uint4 *>(vt + pc * 64 + d8 * 8);
-                        const __half2 *k2 = reinterpret_cast<const __half2 *>(&kk);
-                        float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-                        for (int e = 0; e < 4; e += 2) {
-                            const float2 ka = __half22float2(k2[e]), kb = __half22float2(k2[e + 1]);
-                            s0 = fmaf(qv[2 * e], ka.x, s0);
-                            s1 = fmaf(qv[2 * e + 1], ka.y, s1);
-                            s0 = fmaf(qv[2 * e + 2], kb.x, s0);
-                            s1 = fmaf(qv[2 * e + 3], kb.y, s1);
-                        }
-                        sc[q] = s0 + s1;
-                    }
-#pragma unroll
-                    for (int q = 0; q < QG; ++q) sc[q] += __shfl_xor_sync(0xffffffffu, sc[q], 1);
-#pragma unroll
-                    for (int q = 0; q < QG; ++q) sc[q] += __shfl_xor_sync(0xffffffffu, sc[q], 2);
-#pragma unroll
-                    for (int q = 0; q < QG; ++q) sc[q] += __shfl_xor_sync(0xffffffffu, sc[q], 4);
-                    float mt = m;
-#pragma unroll
-                    for (int q = 0; q < QG; ++q)
-                        if ((warp + q * CW) * 4 + grp < np) mt = fmaxf(mt, sc[q]);
-                    if (mt != m) {
-                        const float corr = exp2f(m - mt);
-                        ls *= corr;
-#pragma unroll
-                        for (int e = 0; e < 8; ++e) acc[e] *= corr;
-                        m = mt;
-                    }
-#pragma unroll
-                    for (int q = 0; q < QG; ++q) {
-                        if ((warp + q * CW) * 4 + grp < np) {
-                            const float pj = exp2f(sc[q] - m);
-                            ls += pj;
-                            const __half2 *v2 = reinterpret_cast<const __half2 *>(&vv[q]);
-#pragma unroll
-                            for (int e = 0; e < 4; ++e) {
-                                const float2 f = __half22float2(v2[e]);
-                                acc[2 * e] = fmaf(pj, f.x, acc[2 * e]);
-                                acc[2 * e + 1] = fmaf(pj, f.y, acc[2 * e + 1]);
-                            }
-                        }
-                    }
-                    __syncwarp();
-                    if (lane == 0) mb_arrive(emptyp + slot);
-                    ++seq;
-                }
-                if (t == kvt - 1 && warp == CW - 1) {  // the new position (fp32, from the QKV stage)
-                    const float *kn = qkvh + ((h - hlo) * 3 + 1) * 64 + d8 * 8;
-                    const float *vn = kn + 64;
-                    float s = 0.f;
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) s = fmaf(qv[e], kn[e], s);
-                    s += __shfl_xor_sync(0xffffffffu, s, 1);
-                    s += __shfl_xor_sync(0xffffffffu, s, 2);
-                    s += __shfl_xor_sync(0xffffffffu, s, 4);
-                    if (grp == 0) {
-                        const float mn = fmaxf(m, s);
-                        const float corr = exp2f(m - mn);
-                        const float pj = exp2f(s - mn);
-                        ls = ls * corr + pj;
-#pragma unroll
-                        for (int e = 0; e < 8; ++e) acc[e] = acc[e] * corr + pj * vn[e];
-                        m = mn;
-                    }
-                }
-                if (++t == kvt) { t = 0; ++h; }
+            for (int e = 0; e < 8; ++e) {
+                const float a2 = __shfl_xor_sync(0xffffffffu, acc[e], off);
+                acc[e] = acc[e] * fa + a2 * fb;
             }
-            close();
+            ls = ls * fa + l2 * fb;
+            m = M;
+        }
+        if (grp == 0) {
+            float *sw = ascr + warp * REC;
+            if (d8 == 0) { sw[0] = m; sw[1] = ls; }
+#pragma unroll
+            for (int e = 0; e < 8; ++e) sw[4 + d8 * 8 + e] = acc[e];
         }
         csync();
-        // merge the warps per segment, records to global memory
-        uint64_t *rdst = xp->rec_ll + ((size_t)l * xp->rec_stride + T->seg0) * REC;
-        const uint32_t tg = tag(l, 1);
-        for (int i = tid; i < nh * 32; i += CT) {
-            const int kk = i >> 5, e2 = (i & 31) * 2;  // dims e2, e2 + 1
-            const float *s = ascr + kk * CW * REC;
+        float *rec = ascr + CW * REC;
+        if (tid < 64) {
             float M = -INFINITY;
 #pragma unroll
-            for (int w = 0; w < CW; ++w) M = fmaxf(M, s[w * REC]);
-            float L2 = 0.f, A0 = 0.f, A1 = 0.f;
+            for (int w = 0; w < CW; ++w) M = fmaxf(M, ascr[w * REC]);
+            float L2 = 0.f, A2 = 0.f;
 #pragma unroll
             for (int w = 0; w < CW; ++w) {
-                const float f = exp2f(s[w * REC] - M);
-                L2 += s[w * REC + 1] * f;
-                A0 += s[w * REC + 4 + e2] * f;
-                A1 += s[w * REC + 5 + e2] * f;
+                const float mw = ascr[w * REC];
+                const float f = mw == -INFINITY ? 0.f : exp2f(mw - M);
+                L2 += ascr[w * REC + 1] * f;
+                A2 += ascr[w * REC + 4 + tid] * f;
             }
-            ll_st2(rdst + kk * REC + 4 + e2, A0, A1, tg);
-            if (e2 == 0) {
-                ll_st2(rdst + kk * REC, M, L2, tg);
-                ll_st2(rdst + kk * REC + 2, 0.f, 0.f, tg);
+            rec[4 + tid] = A2;
+            if (tid == 0) { rec[0] = M; rec[1] = L2; rec[2] = 0.f; rec[3] = 0.f; }
+        }
+        csync();
+        {  // this rank's record into slot [rank] of cluster rank 0
+            const uint32_t dst = mapa(su32(recs + rank * REC), 0), bar = mapa(su32(stb + BR), 0);
+            if (tid < REC / 4) st_async_v4(dst + tid * 16, reinterpret_cast<const uint4 *>(rec)[tid], bar);
+        }
+        if (rank == 0) {
+            wait_land(BR, 31);
+            uint64_t *ao = xp->ao_ll + (size_t)l * d + head * 64;
+            if (tid < 32) {  // dims 2 tid, 2 tid + 1
+                float M = -INFINITY;
+                for (int r = 0; r < CS; ++r) M = fmaxf(M, recs[r * REC]);
+                float L2 = 0.f, A0 = 0.f, A1 = 0.f;
+                for (int r = 0; r < CS; ++r) {
+                    const float mr = recs[r * REC];
+                    const float f = mr == -INFINITY ? 0.f : exp2f(mr - M);
+                    L2 += recs[r * REC + 1] * f;
+                    A0 += recs[r * REC + 4 + 2 * tid] * f;
+                    A1 += recs[r * REC + 5 + 2 * tid] * f;
+                }
+                const bool any = L2 > 0.f;
+                ll_st2(ao + 2 * tid, any ? A0 / L2 : 0.f, any ? A1 / L2 : 0.f, tag(l, 1));
             }
         }
         trace();
     }
     __device__ __forceinline__ void stage_proj(int l) {
-        const float4 bpre = bias_pre(lay[l].proj);
+        const float4 bpre = bias_pre(lay[l].proj, false);
         exchange_ao(l, 40);
         group_sums(xao, sxao, d);
         const MkLin &L = lay[l].proj;
         uint64_t *pv = xp->pv_ll + (size_t)l * d;
         const uint32_t tg = tag(l, 2);
-        run_lin(L, xao, sxao, bpre, [&](int o, int, float4 v, float4 bb) {
+        run_lin(L, xao, sxao, bpre, false, [&](int o, int, float4 v, float4 bb) {
             ll_st2(pv + o, v.x + bb.x, v.y + bb.y, tg);
             ll_st2(pv + o + 2, v.z + bb.z, v.w + bb.w, tg);
         });
@@ -947,13 +911,13 @@ struct XkConsumer {
     __device__ __forceinline__ void stage_fc(int l) {
         const MkLayer &Ly = lay[l];
         const LnRegs ln2 = ln_prefetch(Ly.ln2_w, Ly.ln2_b);
-        const float4 bpre = bias_pre(Ly.fc);
+        const float4 bpre = bias_pre(Ly.fc, false);
         exchange_h(l, 50);
         layernorm(ln2, false);
         const MkLin &L = Ly.fc;
         uint64_t *u = xp->u_ll + (size_t)l * ff;
         const uint32_t tg = tag(l, 3);
-        run_lin(L, xln, sxln, bpre, [&](int o, int, float4 v, float4 bb) {
+        run_lin(L, xln, sxln, bpre, false, [&](int o, int, float4 v, float4 bb) {
             ll_st2(u + o, gelu_tanh(v.x + bb.x), gelu_tanh(v.y + bb.y), tg);
             ll_st2(u + o + 2, gelu_tanh(v.z + bb.z), gelu_tanh(v.w + bb.w), tg);
         });
@@ -965,7 +929,7 @@ struct XkConsumer {
         uint64_t *mp = xp->mp_ll + (size_t)l * xp->nkc * d;
         const uint32_t tg = tag(l, 4);
         const int dd = d;
-        run_lin(L, xu, sxu, make_float4(0.f, 0.f, 0.f, 0.f), [&](int o, int kci, float4 v, float4) {
+        run_lin(L, xu, sxu, make_float4(0.f, 0.f, 0.f, 0.f), false, [&](int o, int kci, float4 v, float4) {
             ll_st2(mp + (size_t)kci * dd + o, v.x, v.y, tg);
             ll_st2(mp + (size_t)kci * dd + o + 2, v.z, v.w, tg);
         });
@@ -974,13 +938,13 @@ struct XkConsumer {
         const MkParams &p = *pp;
         const LnRegs lnf = ln_prefetch(p.lnf_w, p.lnf_b);
         const LnRegs fin = ln_prefetch(p.fin_w, p.fin_b);
-        const float4 bpre = bias_pre(p.head);
+        const float4 bpre = bias_pre(p.head, false);
         exchange_x(p.n_layers - 1, 70);
         layernorm(lnf, true);
         layernorm(fin, false);
         const MkLin &L = p.head;
         const int V = p.mel_vocab;
-        run_lin(L, xln, sxln, bpre, [&](int o, int, float4 v, float4 bb) {
+        run_lin(L, xln, sxln, bpre, false, [&](int o, int, float4 v, float4 bb) {
             const float vv[4] = {v.x + bb.x, v.y + bb.y, v.z + bb.z, v.w + bb.w};
 #pragma unroll
             for (int e = 0; e < 4; ++e)
@@ -1009,25 +973,13 @@ __global__ void __launch_bounds__(NT, 1) xk_decode_kernel(const __grid_constant_
     uint64_t *emptyp = fullp + NSLOT;
     uint64_t *stb = emptyp + NSLOT;
 
-    // step shape: every CTA computes the same tables; thread r < NR does CTA r's range
+    // step shape: cluster c runs head c; rank k of it the k-th of CS ranges of the K/V tiles
     const int slot = p.batch_slot[0];
     const SlotState &st = p.slots[slot];
     const int active = st.active && st.valid_len < p.max_seq;
     const int lold = active ? st.valid_len : 0;
     const int kvt = active ? max(1, (lold + KVPOS - 1) / KVPOS) : 0;
-    const int units = p.H * kvt;
-    if (tid < NR) {
-        const int a = (int)((long long)tid * units / NR), b = (int)((long long)(tid + 1) * units / NR);
-        T->hl[tid] = b > a ? a / kvt : 0;
-        T->cnt[tid] = b > a ? (b - 1) / kvt - a / kvt + 1 : 0;
-        if (tid == R) {
-            T->u_lo = a;
-            T->u_hi = b;
-            T->hlo = T->hl[tid];
-            T->nh = T->cnt[tid];
-        }
-    }
-    if (tid <= p.H) T->hs0[tid] = 0x7fffffff;
+    const int head = R / CS;
     {
         const int words = (int)(p.n_layers * sizeof(MkLayer) / 4);
         const uint32_t *src = reinterpret_cast<const uint32_t *>(p.layers);
@@ -1044,45 +996,17 @@ __global__ void __launch_bounds__(NT, 1) xk_decode_kernel(const __grid_constant_
         mb_expect(stb + B0, (uint32_t)p.d * 4);
         mb_expect(stb + BAO, (uint32_t)p.d * 2);
         mb_expect(stb + BU, (uint32_t)p.ff * 2);
+        mb_expect(stb + BQ, 3 * 64 * 4);
+        mb_expect(stb + BR, CS * REC * 4);  // (waited on by rank 0 only)
         T->active = active;
         T->lold = lold;
         T->kvt = kvt;
-        T->units = units;
         T->slot = slot;
+        T->head = head;
+        T->t_lo = rank * kvt / CS;
+        T->t_hi = (rank + 1) * kvt / CS;
         T->tok = min(max(st.tok, 0), p.mel_vocab - 1);
         T->pos = min(max(st.pos, 0), p.mel_pos_len - 1);
-    }
-    __syncthreads();
-    if (warp == 0) {  // segments: a scan of the per-CTA head counts (5 CTAs per lane)
-        constexpr int PL = MAXNR / 32;
-        int cnt[PL], sum = 0;
-#pragma unroll
-        for (int k = 0; k < PL; ++k) {
-            const int r = lane * PL + k;
-            cnt[k] = r < NR ? T->cnt[r] : 0;
-            sum += cnt[k];
-        }
-        int inc = sum;
-#pragma unroll
-        for (int off = 1; off < 32; off <<= 1) {
-            const int y = __shfl_up_sync(0xffffffffu, inc, off);
-            if (lane >= off) inc += y;
-        }
-        int base = inc - sum;
-#pragma unroll
-        for (int k = 0; k < PL; ++k) {
-            const int r = lane * PL + k;
-            if (r < NR) {
-                if (r == R) T->seg0 = base;
-                for (int kk = 0; kk < cnt[k]; ++kk) atomicMin(&T->hs0[T->hl[r] + kk], base + kk);
-            }
-            base += cnt[k];
-        }
-        const int total = __shfl_sync(0xffffffffu, inc, 31);
-        __syncwarp();
-        if (lane == 0) T->nseg = total;
-        for (int h = lane; h <= p.H; h += 32)  // heads without segments (inactive column), end mark
-            if (h == p.H || T->hs0[h] == 0x7fffffff) T->hs0[h] = total;
     }
     __syncthreads();
     const uint32_t epoch = xp.epoch[R];
@@ -1102,7 +1026,7 @@ __global__ void __launch_bounds__(NT, 1) xk_decode_kernel(const __grid_constant_
             P.R = R;
             P.NR = NR;
             P.ok = true;
-            P.run(p, *T, reinterpret_cast<const MkLayer *>(smem + SL.lay));
+            P.run(p, *T, reinterpret_cast<const MkLayer *>(smem + SL.lay), rank);
         }
         __syncwarp();
     } else {
@@ -1121,6 +1045,8 @@ __global__ void __launch_bounds__(NT, 1) xk_decode_kernel(const __grid_constant_
         C.sxu = reinterpret_cast<float *>(smem + SL.sxu);
         C.red = reinterpret_cast<float *>(smem + SL.red);
         C.qkvh = reinterpret_cast<float *>(smem + SL.qkvh);
+        C.recs = reinterpret_cast<float *>(smem + SL.recs);
+        C.head = head;
         C.stat = reinterpret_cast<float *>(smem + SL.stat);
         C.fullp = fullp;
         C.emptyp = emptyp;
@@ -1141,10 +1067,12 @@ __global__ void __launch_bounds__(NT, 1) xk_decode_kernel(const __grid_constant_
         C.tbase = epoch * (uint32_t)(NWS * p.n_layers);
         C.ok = true;
         C.ev = 0;
-        C.ph[B0] = C.ph[BAO] = C.ph[BU] = 0;
+        for (int b = 0; b < NSTB; ++b) C.ph[b] = 0;
         C.exp_bytes[B0] = (uint32_t)p.d * 4;
         C.exp_bytes[BAO] = (uint32_t)p.d * 2;
         C.exp_bytes[BU] = (uint32_t)p.ff * 2;
+        C.exp_bytes[BQ] = 3 * 64 * 4;
+        C.exp_bytes[BR] = CS * REC * 4;
         for (int l = 0; l < p.n_layers; ++l) {
             C.stage_qkv(l);
             C.stage_attn(l);
@@ -1185,8 +1113,8 @@ int xk_config(const ModelView &m, XkConfig *out) {
     *out = XkConfig{};
     const char *off = getenv("ITTS_XK");
     if (off && off[0] == '0') return -1;
-    if (m.n_layers < 1 || m.d > MK_MAX_KC || m.d % (4 * CS) || m.d % 64 || m.ff % (64 * CS) ||
-        m.n_heads * 64 != m.d || m.n_heads > 32)
+    if (m.n_layers < 1 || m.d > MK_MAX_KC || m.d % 64 || m.ff % 64 || m.n_heads * 64 != m.d || m.d / 4 < CS ||
+        m.ff / 64 < CS)
         return -1;
     int dev = 0, optin = 0, sms = 0;
     cudaGetDevice(&dev);
@@ -1202,7 +1130,7 @@ int xk_config(const ModelView &m, XkConfig *out) {
         nkc = std::max(nkc, L.mlp.n_kc);
     }
     if (m.mel_head.tile_bytes > SLOT || m.mel_head.n_kc != 1) return -1;
-    // grid: as many 8-CTA clusters as fit at once
+    // grid: one CS-CTA cluster per attention head, all resident at once
     const int rt_guess = 8;
     size_t smem = xk_layout(m.d, m.ff, rt_guess, m.n_layers).total;
     if ((int)smem > optin) return -1;
@@ -1226,12 +1154,17 @@ int xk_config(const ModelView &m, XkConfig *out) {
         cudaGetLastError();
         return -1;
     }
-    const int grid = std::min(ncl * CS, (std::min(sms, MAXNR) / CS) * CS);
+    if (ncl < m.n_heads || m.n_heads * CS > sms) {
+        if (getenv("ITTS_DEBUG")) fprintf(stderr, "[itts] clustered decode kernel: %d heads, %d clusters fit\n", m.n_heads, ncl);
+        return -1;
+    }
+    const int grid = m.n_heads * CS;
     int rt = 1;
     for (int l = 0; l < m.n_layers; ++l) {
         const MkLayer &L = m.layers[l];
         for (const MkLin *x : {&L.qkv, &L.proj, &L.fc, &L.mlp}) rt = std::max(rt, xk_tiles_of(*x, grid));
     }
+    rt = std::max(rt, (QT + CS - 1) / CS);  // this rank's share of the head's QKV row blocks
     rt = std::min(rt, rt_guess);
     smem = xk_layout(m.d, m.ff, rt, m.n_layers).total;
     cudaFuncSetAttribute(xk_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -1258,7 +1191,6 @@ int xk_config(const ModelView &m, XkConfig *out) {
     out->rt = rt;
     out->nkc = nkc;
     out->coop = coop ? 1 : 0;
-    out->rec_stride = m.n_heads + grid;
     if (getenv("ITTS_DEBUG"))
         fprintf(stderr, "[itts] clustered decode kernel: grid %d (%d-CTA clusters, %s), %zu B shared memory, rt %d\n",
                 grid, CS, coop ? "cooperative" : "plain", smem, rt);
@@ -1268,15 +1200,13 @@ int xk_config(const ModelView &m, XkConfig *out) {
 cudaError_t xk_launch(const MkParams &p, const XkConfig &xc, const XkBufs &b, cudaStream_t st) {
     XkParams xp{};
     xp.p = p;
-    xp.qkv_ll = b.qkv_ll;
-    xp.rec_ll = b.rec_ll;
+    xp.ao_ll = b.ao_ll;
     xp.pv_ll = b.pv_ll;
     xp.u_ll = b.u_ll;
     xp.mp_ll = b.mp_ll;
     xp.epoch = b.epoch;
     xp.rt = xc.rt;
     xp.nkc = xc.nkc;
-    xp.rec_stride = xc.rec_stride;
     xp.dry = 0;
     return xk_launch_cfg(xp, xc.grid, xk_layout(p.d, p.ff, xc.rt, p.n_layers).total, xc.coop != 0, st);
 }
