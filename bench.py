@@ -296,7 +296,9 @@ def run_ours(args, rank, world, local_rank):
                      "ms_per_launch": ws_ms,
                      # dram__bytes_read.sum + dram__bytes_write.sum of one launch at this KV
                      # length (ncu capture summarised in profiles/xk_decode_kernel_cfg2.md)
-                     "traffic": None},
+                     # dram__bytes_read.sum + dram__bytes_write.sum of one launch at this KV
+                     # length (ncu capture summarised in profiles/xk_decode_kernel_cfg2.md)
+                     "traffic": 691946752 if kname == "xk_decode_kernel" else None},
         "clocks": clk,
     }
     try:
