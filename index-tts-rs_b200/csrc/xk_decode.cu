@@ -1,28 +1,35 @@
-// xk_decode.cu -- the decode step of one request (batch column) on (almost) every SM,
-// launched as 8-CTA thread-block clusters (crates/core/src/models/gpt.rs:706-754): step
-// embedding, n_layers x [LN1 -> QKV -> KV append -> attention -> c_proj + residual -> LN2 ->
-// c_fc + GELU -> mlp c_proj + residual], ln_f -> final_norm -> mel_head.
+// xk_decode.cu -- the decode step of one request (batch column) on one 6-CTA thread-block
+// cluster per attention head (120 CTAs for the 20 heads of IndexTTS-2.5;
+// crates/core/src/models/gpt.rs:706-754): step embedding, n_layers x [LN1 -> QKV -> KV append
+// -> attention -> c_proj + residual -> LN2 -> c_fc + GELU -> mlp c_proj + residual], ln_f ->
+// final_norm -> mel_head.
 //
-// Each stage's output rows go to global memory as 64-bit LL words {fp32 value, stage tag}
-// (the tag is unique per launch, layer and stage, so no buffer is ever reset).  The next
-// stage's input vector is gathered ONCE per cluster instead of once per CTA: cluster rank k
-// polls the k-th eighth of the vector (finishing it on the way: residual add, K-split sum,
-// attention-partial merge, fp16 conversion) and pushes it into the shared memory of all 8
-// CTAs of its cluster with st.async; each CTA's mbarrier counts the bytes.  So a stage
-// boundary costs one L2 round trip for 1/8 of the vector plus one distributed-shared-memory
-// hop, and every SM keeps issuing the dequantization work of its 1-4 tiles per stage.
+// Cluster c owns head c: its ranks compute the 12 QKV row blocks of the head (q, k, v rows
+// 64c .. 64c + 63), append K/V to the cache and push the 192 values into every CTA of the
+// cluster with st.async; each rank then attends over its range of the head's 84-position
+// K/V tiles and pushes one (m, l, acc[64]) record into cluster rank 0, which merges them
+// and writes the head's 64 outputs.  So q/k/v and the attention partials never leave the
+// cluster.
+//
+// Everything else crosses clusters as 64-bit LL words {fp32 value, stage tag} in global
+// memory (the tag is unique per launch, layer and stage, so no buffer is ever reset), and
+// each stage input vector (x, attention output, h, u) is gathered ONCE per cluster: rank k
+// polls the k-th sixth of the vector (finishing it on the way: residual add, K-split sum,
+// fp16 conversion) and pushes it into all 6 CTAs with st.async; each CTA's mbarrier counts
+// the bytes.  The c_proj, c_fc, mlp and head tiles are dealt round-robin over the grid
+// (tile t on CTA t % grid; the mlp projection is K-split and the gathering rank sums its
+// four chunk partials in a fixed order).
 //
 // Per CTA: 8 consumer warps + 1 producer warp.  The producer lane streams the CTA's weight
-// tiles (tile t of every linear belongs to CTA t % grid) and its range of old K/V rows into
-// an 8-slot cp.async.bulk ring (no multicast) ahead of the stages; consumers dequantize in
-// registers and run mma.sync m16n8k16 with the activation (the same arithmetic as the other
-// decode kernels), per-warp partial sums reduced once per tile.
+// tiles and K/V rows into an 8-slot cp.async.bulk ring (no multicast) ahead of the stages;
+// consumers dequantize in registers and run mma.sync m16n8k16 with the activation (the same
+// arithmetic as the other decode kernels), per-warp partial sums reduced once per tile.
 //
-// Buffer reuse: four vectors arrive per layer (x, attention output, h, u) into three
-// landing buffers (x and h share one).  A cluster peer can be at most one exchange ahead
-// of a CTA (finishing exchange e needs every peer's slice of e, sent only after that peer
-// finished exchange e-1), and each landing buffer is reused only two exchanges later, after
-// its previous contents were consumed.
+// Buffer reuse: the landing buffers (x/h, attention output, u, the head's q/k/v, rank 0's
+// records) are rewritten once per layer without double buffering.  A cluster peer can be
+// at most one exchange ahead of a CTA (finishing exchange e needs every peer's part of e,
+// sent only after that peer finished exchange e-1), and each buffer is rewritten only after
+// every CTA of the cluster has consumed its previous contents.
 //
 // Every wait and poll is bounded; on a timeout the kernel records an error code in p.err
 // (read by the host as ITTS_E_TIMEOUT), skips the remaining waits and exits cleanly.
