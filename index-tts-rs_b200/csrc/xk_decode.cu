@@ -116,6 +116,11 @@ __device__ __forceinline__ void st_async_v4(uint32_t raddr, uint4 v, uint32_t rb
                  "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "r"(rbar)
                  : "memory");
 }
+__device__ __forceinline__ void st_async_b32(uint32_t raddr, uint32_t v, uint32_t rbar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(raddr), "r"(v),
+                 "r"(rbar)
+                 : "memory");
+}
 // the same 16 bytes into every CTA of the cluster
 __device__ __forceinline__ void bcast_v4(uint32_t laddr, uint4 v, uint32_t lbar) {
 #pragma unroll
@@ -233,7 +238,7 @@ __device__ __noinline__ bool poll_runs(const PollRun *runs, int nruns, int total
                 }
             if (pending) {
                 if (it >= SPIN || ((it & 255u) == 255u && *(volatile const int *)err)) return false;
-                __nanosleep(it < 4 ? 32u : (it < 16 ? 64u : 128u));
+                if (it >= 8) __nanosleep(it < 32 ? 32u : 128u);
             }
         }
     }
@@ -407,41 +412,6 @@ struct XkConsumer {
         if (tid == 0) mb_expect(stb + b, exp_bytes[b]);
         trace();
     }
-    __device__ __forceinline__ void put_x(__half *xs, int k, float v) {
-        xs[(k & ~63) + frag_pos_host(k & 63)] = __float2half_rn(v);
-    }
-    __device__ __forceinline__ float block_sum(float v) {
-        v = warp_sum(v);
-        if (lane == 0) stat[warp] = v;
-        csync();
-        float t = 0.f;
-#pragma unroll
-        for (int w = 0; w < CW; ++w) t += stat[w];
-        csync();
-        return t;
-    }
-    __device__ __forceinline__ void group_sums(const __half *xs, float *sx, int K) {
-        csync();
-        const int total = K / 64 * 8;
-        for (int i0 = 0; i0 < total; i0 += CT) {
-            const int i = i0 + tid;
-            float s = 0.f;
-            if (i < total) {
-                const uint4 v = *reinterpret_cast<const uint4 *>(xs + (i >> 3) * 64 + (i & 7) * 8);
-                const __half2 *h2 = reinterpret_cast<const __half2 *>(&v);
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float2 f = __half22float2(h2[e]);
-                    s += f.x + f.y;
-                }
-            }
-            s += __shfl_xor_sync(0xffffffffu, s, 1);
-            s += __shfl_xor_sync(0xffffffffu, s, 2);
-            s += __shfl_xor_sync(0xffffffffu, s, 4);
-            if (i < total && (i & 7) == 0) sx[i >> 3] = s;
-        }
-        csync();
-    }
     static constexpr int LNC = (MK_MAX_D / 4 + CT - 1) / CT;
     struct LnRegs {
         float4 w[LNC], b[LNC];
@@ -460,48 +430,63 @@ struct XkConsumer {
         }
         return r;
     }
-    // LayerNorm(land) * w + b (two-pass statistics) into xln (fp16, fragment order) or back
-    // into land (inplace)
+    // LayerNorm(land) * w + b into xln (fp16, fragment order, with its group sums) or back
+    // into land (inplace).  Statistics in one pass over x - x[0] (the shift keeps
+    // E[y^2] - E[y]^2 well conditioned); a group's 64 inputs are the float4 chunks of 16
+    // consecutive lanes, so its fp16 sum takes 4 shuffles.
     __device__ __forceinline__ void layernorm(const LnRegs &P, bool inplace) {
         float4 x[LNC];
-        float s = 0.f;
+        const float sh = land[0];
+        float s1 = 0.f, s2 = 0.f;
 #pragma unroll
         for (int j = 0; j < LNC; ++j) {
             const int k4 = tid + j * CT;
-            x[j] = k4 * 4 < d ? *reinterpret_cast<const float4 *>(land + k4 * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
-            s += (x[j].x + x[j].y) + (x[j].z + x[j].w);
+            x[j] = k4 * 4 < d ? *reinterpret_cast<const float4 *>(land + k4 * 4) : make_float4(sh, sh, sh, sh);
+            const float a = x[j].x - sh, b = x[j].y - sh, cc = x[j].z - sh, e = x[j].w - sh;
+            s1 += (a + b) + (cc + e);
+            s2 += (a * a + b * b) + (cc * cc + e * e);
         }
-        const float mean = block_sum(s) / (float)d;
-        float v = 0.f;
+        s1 = warp_sum(s1);
+        s2 = warp_sum(s2);
+        if (lane == 0) { stat[2 * warp] = s1; stat[2 * warp + 1] = s2; }
+        csync();
+        float t1 = 0.f, t2 = 0.f;
+#pragma unroll
+        for (int w = 0; w < CW; ++w) { t1 += stat[2 * w]; t2 += stat[2 * w + 1]; }
+        const float m1 = t1 / (float)d;
+        const float mean = sh + m1;
+        const float rstd = 1.0f / sqrtf(fmaxf(t2 / (float)d - m1 * m1, 0.f) + kNormEps);
 #pragma unroll
         for (int j = 0; j < LNC; ++j) {
+            if (j * CT >= d / 4) break;  // (uniform: no thread of this round has inputs)
             const int k4 = tid + j * CT;
-            if (k4 * 4 < d) {
-                const float a = x[j].x - mean, b = x[j].y - mean, cc = x[j].z - mean, e = x[j].w - mean;
-                v += (a * a + b * b) + (cc * cc + e * e);
-            }
-        }
-        const float rstd = 1.0f / sqrtf(block_sum(v) / (float)d + kNormEps);
-#pragma unroll
-        for (int j = 0; j < LNC; ++j) {
-            const int k4 = tid + j * CT;
-            if (k4 * 4 >= d) continue;
+            const bool in = k4 * 4 < d;
             float4 y;
             y.x = (x[j].x - mean) * rstd * P.w[j].x + P.b[j].x;
             y.y = (x[j].y - mean) * rstd * P.w[j].y + P.b[j].y;
             y.z = (x[j].z - mean) * rstd * P.w[j].z + P.b[j].z;
             y.w = (x[j].w - mean) * rstd * P.w[j].w + P.b[j].w;
             if (inplace) {
-                *reinterpret_cast<float4 *>(land + k4 * 4) = y;
+                if (in) *reinterpret_cast<float4 *>(land + k4 * 4) = y;
             } else {
-                put_x(xln, k4 * 4, y.x);
-                put_x(xln, k4 * 4 + 1, y.y);
-                put_x(xln, k4 * 4 + 2, y.z);
-                put_x(xln, k4 * 4 + 3, y.w);
+                const __half hx = __float2half_rn(y.x), hy = __float2half_rn(y.y), hz = __float2half_rn(y.z),
+                             hw = __float2half_rn(y.w);
+                float gs = in ? (__half2float(hx) + __half2float(hy)) + (__half2float(hz) + __half2float(hw)) : 0.f;
+                gs += __shfl_xor_sync(0xffffffffu, gs, 1);
+                gs += __shfl_xor_sync(0xffffffffu, gs, 2);
+                gs += __shfl_xor_sync(0xffffffffu, gs, 4);
+                gs += __shfl_xor_sync(0xffffffffu, gs, 8);
+                if (in) {
+                    const int k = k4 * 4, base = k & ~63;
+                    xln[base + frag_pos_host(k & 63)] = hx;
+                    xln[base + frag_pos_host((k + 1) & 63)] = hy;
+                    xln[base + frag_pos_host((k + 2) & 63)] = hz;
+                    xln[base + frag_pos_host((k + 3) & 63)] = hw;
+                    if ((k4 & 15) == 0) sxln[k4 >> 4] = gs;
+                }
             }
         }
-        if (inplace) csync();
-        else group_sums(xln, sxln, d);
+        csync();
         trace();
     }
 
@@ -681,33 +666,51 @@ struct XkConsumer {
     // groups [g0, g1) of 64 values of an fp32 LL vector -> fp16 fragment order -> xs of every
     // CTA of the cluster; thread (group, c) sends the 32 contiguous bytes of rows
     // {16 b + 2c, 16 b + 2c + 1, 16 b + 2c + 8, 16 b + 2c + 9 : b < 4}
-    __device__ __forceinline__ void gather_f16(const uint64_t *src, int n_groups, uint32_t tg, __half *xs, int bar,
-                                               int code) {
+    __device__ __forceinline__ void gather_f16(const uint64_t *src, int n_groups, uint32_t tg, __half *xs, float *sx,
+                                               int bar, int code) {
         const int g0 = slice_lo(rank, n_groups), ng = slice_lo(rank + 1, n_groups) - g0;
         if (tid == 0) T->runs[0] = PollRun{src + (size_t)g0 * 64, 0, 0};
         const bool good = poll(1, ng * 32, tg, red);
         agree(good, code);
-        const uint32_t xs_a = su32(xs), bar_a = su32(stb + bar);
-        for (int i = tid; i < ng * 4; i += CT) {
+        const uint32_t xs_a = su32(xs), sx_a = su32(sx), bar_a = su32(stb + bar);
+        for (int i0 = 0; i0 < ng * 4; i0 += CT) {  // (threads of one group are 4 consecutive lanes)
+            const int i = i0 + tid;
+            const bool in = i < ng * 4;
             const int gl = (i >> 2) * 64, cc = i & 3;
-            const float *s = red + gl + 2 * cc;
-            uint4 v0, v1;
-            v0.x = pack_h2(s[0], s[1]);   v0.y = pack_h2(s[8], s[9]);
-            v0.z = pack_h2(s[16], s[17]); v0.w = pack_h2(s[24], s[25]);
-            v1.x = pack_h2(s[32], s[33]); v1.y = pack_h2(s[40], s[41]);
-            v1.z = pack_h2(s[48], s[49]); v1.w = pack_h2(s[56], s[57]);
-            const uint32_t dst = xs_a + (g0 * 64 + gl + cc * 16) * 2;
-            bcast_v4(dst, v0, bar_a);
-            bcast_v4(dst + 16, v1, bar_a);
+            float gs = 0.f;
+            if (in) {
+                const float *s = red + gl + 2 * cc;
+                uint4 v0, v1;
+                v0.x = pack_h2(s[0], s[1]);   v0.y = pack_h2(s[8], s[9]);
+                v0.z = pack_h2(s[16], s[17]); v0.w = pack_h2(s[24], s[25]);
+                v1.x = pack_h2(s[32], s[33]); v1.y = pack_h2(s[40], s[41]);
+                v1.z = pack_h2(s[48], s[49]); v1.w = pack_h2(s[56], s[57]);
+                const __half2 *h0 = reinterpret_cast<const __half2 *>(&v0), *h1 = reinterpret_cast<const __half2 *>(&v1);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 a = __half22float2(h0[e]), b = __half22float2(h1[e]);
+                    gs += (a.x + a.y) + (b.x + b.y);
+                }
+                const uint32_t dst = xs_a + (g0 * 64 + gl + cc * 16) * 2;
+                bcast_v4(dst, v0, bar_a);
+                bcast_v4(dst + 16, v1, bar_a);
+            }
+            gs += __shfl_xor_sync(0xffffffffu, gs, 1);
+            gs += __shfl_xor_sync(0xffffffffu, gs, 2);
+            if (in && cc == 0) {  // the group's fp16 sum
+                const uint32_t sa = sx_a + (g0 + (i >> 2)) * 4;
+#pragma unroll
+                for (int r = 0; r < CS; ++r) st_async_b32(mapa(sa, r), __float_as_uint(gs), mapa(bar_a, r));
+            }
         }
         trace();
         wait_land(bar, code + 1);
     }
     __device__ __forceinline__ void exchange_u(int l, int code) {
-        gather_f16(xp->u_ll + (size_t)l * ff, ff / 64, tag(l, 3), xu, BU, code);
+        gather_f16(xp->u_ll + (size_t)l * ff, ff / 64, tag(l, 3), xu, sxu, BU, code);
     }
     __device__ __forceinline__ void exchange_ao(int l, int code) {
-        gather_f16(xp->ao_ll + (size_t)l * d, d / 64, tag(l, 1), xao, BAO, code);
+        gather_f16(xp->ao_ll + (size_t)l * d, d / 64, tag(l, 1), xao, sxao, BAO, code);
     }
 
     // ---- stages ----
@@ -906,7 +909,6 @@ struct XkConsumer {
     __device__ __forceinline__ void stage_proj(int l) {
         const float4 bpre = bias_pre(lay[l].proj, false);
         exchange_ao(l, 40);
-        group_sums(xao, sxao, d);
         const MkLin &L = lay[l].proj;
         uint64_t *pv = xp->pv_ll + (size_t)l * d;
         const uint32_t tg = tag(l, 2);
@@ -931,7 +933,6 @@ struct XkConsumer {
     }
     __device__ __forceinline__ void stage_mlp(int l) {
         exchange_u(l, 60);
-        group_sums(xu, sxu, ff);
         const MkLin &L = lay[l].mlp;
         uint64_t *mp = xp->mp_ll + (size_t)l * xp->nkc * d;
         const uint32_t tg = tag(l, 4);
@@ -1001,8 +1002,8 @@ __global__ void __launch_bounds__(NT, 1) xk_decode_kernel(const __grid_constant_
         for (int b = 0; b < NSTB; ++b) mb_init(stb + b, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         mb_expect(stb + B0, (uint32_t)p.d * 4);
-        mb_expect(stb + BAO, (uint32_t)p.d * 2);
-        mb_expect(stb + BU, (uint32_t)p.ff * 2);
+        mb_expect(stb + BAO, (uint32_t)p.d * 2 + p.d / 64 * 4);  // fp16 values + group sums
+        mb_expect(stb + BU, (uint32_t)p.ff * 2 + p.ff / 64 * 4);
         mb_expect(stb + BQ, 3 * 64 * 4);
         mb_expect(stb + BR, CS * REC * 4);  // (waited on by rank 0 only)
         T->active = active;
@@ -1076,8 +1077,8 @@ __global__ void __launch_bounds__(NT, 1) xk_decode_kernel(const __grid_constant_
         C.ev = 0;
         for (int b = 0; b < NSTB; ++b) C.ph[b] = 0;
         C.exp_bytes[B0] = (uint32_t)p.d * 4;
-        C.exp_bytes[BAO] = (uint32_t)p.d * 2;
-        C.exp_bytes[BU] = (uint32_t)p.ff * 2;
+        C.exp_bytes[BAO] = (uint32_t)p.d * 2 + p.d / 64 * 4;
+        C.exp_bytes[BU] = (uint32_t)p.ff * 2 + p.ff / 64 * 4;
         C.exp_bytes[BQ] = 3 * 64 * 4;
         C.exp_bytes[BR] = CS * REC * 4;
         for (int l = 0; l < p.n_layers; ++l) {
