@@ -430,6 +430,47 @@ def run_profile_prefill_batch(args):
                       "positions": n * (N_CONDS + N_TEXT + 3), "last_wall_ms": 1000.0 * dt}), flush=True)
 
 
+# stage timeline events of xk_decode_kernel per layer (l >= 1) on cluster ranks other than 0
+XK_EVENTS = ["x sent", "x gathered", "LayerNorm 1", "QKV tiles + push", "q/k/v in cluster", "attention",
+             "attention output sent", "attention output gathered", "c_proj tile", "h sent", "h gathered",
+             "LayerNorm 2", "c_fc tiles", "u sent", "u gathered", "mlp tiles"]
+
+
+def run_profile_trace(args):
+    """Stage timeline of one batch-1 decode step at KV length `--profile-trace`: per-CTA
+    globaltimer stamps (itts_bench_trace), medians over CTAs and layers, µs after the
+    layer's first x arrival."""
+    import ctypes as C
+    import numpy as np
+    import itts_gpt as ig
+    from itts_gpt import _lib
+    cfg, w = make_model()
+    gpt = ig.Gpt.from_weights(w)
+    L = args.profile_trace
+    kv = ig.KvCache(gpt, max_seq=L + 8, max_batch=1)
+    if kv.decode_kernel(1) != "xk_decode_kernel":
+        raise SystemExit("--profile-trace reads the event layout of xk_decode_kernel")
+    lib = _lib.load_lib()
+    n = 148 * 256
+    out = np.zeros(n, np.uint64)
+    g, e = C.c_int32(), C.c_int32()
+    for _ in range(3):
+        if lib.itts_bench_trace(gpt._h, kv._h, 1, L, out.ctypes.data, n, C.byref(g), C.byref(e)) != 0:
+            raise RuntimeError(_lib.last_error())
+    t = out.reshape(-1, e.value).astype(np.int64)
+    nr = int((t[:, 0] > 0).sum())
+    ev = (t[:nr] - t[:nr, 0].min()) / 1000.0
+    sel = [r for r in range(nr) if r % 6 != 0]  # rank 0 of each cluster records one event more
+    E, first, nl = len(XK_EVENTS), 15, 14  # layer 0 has no x exchange (15 events); 256 events hold 14 layers
+    lay = ev[sel, first:first + (nl - 1) * E].reshape(len(sel), nl - 1, E)
+    rel = lay[:, 1:, :] - lay[:, 1:, 1].min(0)[None, :, None]
+    per_layer = (lay[:, -1, 0].min() - lay[:, 0, 0].min()) / (nl - 2)
+    print(json.dumps({"profile_case": "decode-step stage timeline", "kv_len": L, "ctas": nr,
+                      "us_per_layer": round(float(per_layer), 2),
+                      "median_us_after_x_arrival": {nm: round(float(np.median(np.median(rel[:, :, i], 0))), 2)
+                                                    for i, nm in enumerate(XK_EVENTS)}}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -447,7 +488,12 @@ def main():
                     help="profiler case: one cfg2 generate of this many tokens")
     ap.add_argument("--profile-prefill-batch", type=int, default=0, metavar="N_REQ",
                     help="profiler case: the cfg4 packed prefill of N_REQ prompts, twice")
+    ap.add_argument("--profile-trace", type=int, default=0, metavar="KV_LEN",
+                    help="stage timeline of one batch-1 decode step at this KV length")
     args = ap.parse_args()
+    if args.profile_trace > 0:
+        run_profile_trace(args)
+        return
     if args.profile_decode > 0:
         run_profile_case(args)
         return
