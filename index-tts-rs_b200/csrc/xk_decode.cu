@@ -20,7 +20,7 @@
 // (tile t on CTA t % grid; the mlp projection is K-split and the gathering rank sums its
 // four chunk partials in a fixed order).
 //
-// Per CTA: 8 consumer warps + 1 producer warp.  The producer lane streams the CTA's weight
+// Per CTA: 10 consumer warps + 1 producer warp.  The producer lane streams the CTA's weight
 // tiles and K/V rows into an 8-slot cp.async.bulk ring (no multicast) ahead of the stages;
 // consumers dequantize in registers and run mma.sync m16n8k16 with the activation (the same
 // arithmetic as the other decode kernels), per-warp partial sums reduced once per tile.
@@ -44,7 +44,7 @@ namespace itts {
 namespace {
 
 constexpr int CS = 6;              // CTAs per cluster: one cluster per attention head
-constexpr int CW = 8;              // consumer warps
+constexpr int CW = 10;             // consumer warps (20 quantization groups of a tile: 2 each)
 constexpr int CT = CW * 32;        // consumer threads
 constexpr int NT = CT + 32;        // + the producer warp
 constexpr int NSLOT = 8;           // ring slots (power of two)
@@ -546,7 +546,8 @@ struct XkConsumer {
             const uint8_t *tsb = tq + 16 * KC;
             float a0 = 0.f, a1 = 0.f;
             {
-                int j = (warp - w0) & (CW - 1);
+                int j = warp - w0;
+                if (j < 0) j += CW;
                 for (; j + CW < G64; j += 2 * CW) {
                     group(tq, tsb, KC, G64, j, kci * G64 + j, xs, sx, half_sb, a0, a1);
                     group(tq, tsb, KC, G64, j + CW, kci * G64 + j + CW, xs, sx, half_sb, a0, a1);
@@ -561,7 +562,7 @@ struct XkConsumer {
                 r[g] = a0;
                 r[g + 8] = a1;
             }
-            w0 = (w0 + G64) & (CW - 1);
+            w0 = (w0 + G64) % CW;
         }
         csync();
     }
