@@ -20,7 +20,7 @@
 // (tile t on CTA t % grid; the mlp projection is K-split and the gathering rank sums its
 // four chunk partials in a fixed order).
 //
-// Per CTA: 10 consumer warps + 1 producer warp.  The producer lane streams the CTA's weight
+// Per CTA: 11 consumer warps + 1 producer warp.  The producer lane streams the CTA's weight
 // tiles and K/V rows into an 8-slot cp.async.bulk ring (no multicast) ahead of the stages;
 // consumers dequantize in registers and run mma.sync m16n8k16 with the activation (the same
 // arithmetic as the other decode kernels), per-warp partial sums reduced once per tile.
@@ -44,7 +44,7 @@ namespace itts {
 namespace {
 
 constexpr int CS = 6;              // CTAs per cluster: one cluster per attention head
-constexpr int CW = 10;             // consumer warps (20 quantization groups of a tile: 2 each)
+constexpr int CW = 11;             // consumer warps (20 quantization groups of a tile: at most 2 each)
 constexpr int CT = CW * 32;        // consumer threads
 constexpr int NT = CT + 32;        // + the producer warp
 constexpr int NSLOT = 8;           // ring slots (power of two)
@@ -1012,8 +1012,10 @@ __global__ void __launch_bounds__(NT, 1) xk_decode_kernel(const __grid_constant_
         T->kvt = kvt;
         T->slot = slot;
         T->head = head;
-        T->t_lo = rank * kvt / CS;
-        T->t_hi = (rank + 1) * kvt / CS;
+        // ranges rounded up, so the last rank (which also takes the new position) has the
+        // smaller share
+        T->t_lo = (rank * kvt + CS - 1) / CS;
+        T->t_hi = ((rank + 1) * kvt + CS - 1) / CS;
         T->tok = min(max(st.tok, 0), p.mel_vocab - 1);
         T->pos = min(max(st.pos, 0), p.mel_pos_len - 1);
     }
