@@ -298,7 +298,7 @@ def run_ours(args, rank, world, local_rank):
                      # length (ncu capture summarised in profiles/xk_decode_kernel_cfg2.md)
                      # dram__bytes_read.sum + dram__bytes_write.sum of one launch at this KV
                      # length (ncu capture summarised in profiles/xk_decode_kernel_cfg2.md)
-                     "traffic": 691946752 if kname == "xk_decode_kernel" else None},
+                     "traffic": 692219904 if kname == "xk_decode_kernel" else None},
         "clocks": clk,
     }
     try:
