@@ -194,21 +194,20 @@ __device__ __forceinline__ bool poll_pairs(P ptr, uint32_t tag, O out, const int
     return true;
 }
 
-// A list of runs of LL word pairs: pair i (flattened over the runs) of run r lives at
-// src + 2 (i - start).  One out-of-line routine polls them all, so the many exchanges of a
-// layer share one copy of the polling code.
-struct PollRun {
+// The LL word pairs a gather polls: nruns runs of ppr pairs each, run r starting at
+// src + r * stride words (pair i: run i / ppr, pair i % ppr of it).  One out-of-line routine
+// polls every gather, so the exchanges of a layer share one copy of the polling code.
+struct PollRuns {
     const uint64_t *src;
-    int start, pad;
+    int stride, ppr, nruns;
 };
-constexpr int MAXRUN = 16;
 constexpr int PPJ = 4;  // pairs per thread per round
 
-// Polls pairs [0, total) until every tag equals `tag`; pair i's values go to stage[2i],
-// stage[2i + 1].  Called by all consumer threads; false on a timeout or a raised error word.
-__device__ __noinline__ bool poll_runs(const PollRun *runs, int nruns, int total, uint32_t tag, float *stage,
-                                       const int *err) {
-    const int tid = threadIdx.x;
+// Polls pairs [0, nruns * ppr) until every tag equals `tag`; pair i's values go to
+// stage[2i], stage[2i + 1].  Called by all consumer threads; false on a timeout or a raised
+// error word.
+__device__ __noinline__ bool poll_runs(PollRuns pr, uint32_t tag, float *stage, const int *err) {
+    const int tid = threadIdx.x, total = pr.nruns * pr.ppr;
     for (int base = 0; base < total; base += CT * PPJ) {
         const uint64_t *adr[PPJ];
         uint32_t pending = 0;
@@ -217,9 +216,8 @@ __device__ __noinline__ bool poll_runs(const PollRun *runs, int nruns, int total
             const int i = base + tid + j * CT;
             adr[j] = nullptr;
             if (i < total) {
-                int r = 0;
-                while (r + 1 < nruns && i >= runs[r + 1].start) ++r;
-                adr[j] = runs[r].src + 2 * (i - runs[r].start);
+                const int r = i / pr.ppr;
+                adr[j] = pr.src + (size_t)r * pr.stride + 2 * (i - r * pr.ppr);
                 pending |= 1u << j;
             }
         }
@@ -260,7 +258,6 @@ __host__ __device__ inline uint32_t xk_red_bytes(int rt, int d, int ff) {
 }
 struct XkTab {
     int active, lold, kvt, slot, tok, pos, head, t_lo, t_hi, pad[7];
-    PollRun runs[MAXRUN];  // the current poll list
 };
 __host__ __device__ inline XkSmem xk_layout(int d, int ff, int rt, int n_layers) {
     XkSmem L;
@@ -614,10 +611,8 @@ struct XkConsumer {
 
     // ---- exchanges (cluster rank k gathers its slice of the vector and pushes it to the
     // cluster) ----
-    // Runs are set by thread 0, polled by every consumer thread into `stage`.
-    __device__ __forceinline__ bool poll(int nruns, int total, uint32_t tg, float *stage) {
-        csync();  // the run table is written
-        return !ok || poll_runs(T->runs, nruns, total, tg, stage, pp->err);
+    __device__ __forceinline__ bool poll(PollRuns pr, uint32_t tg, float *stage) {
+        return !ok || poll_runs(pr, tg, stage, pp->err);
     }
     // x_l = h + mlp bias + sum over K chunks of the mlp partials (layer l - 1) -> land
     __device__ __forceinline__ void exchange_x(int lprev, int code) {
@@ -627,9 +622,7 @@ struct XkConsumer {
         const uint64_t *mp = xp->mp_ll + (size_t)lprev * xp->nkc * d;
         const float4 bpre = tid < nch ? __ldg(reinterpret_cast<const float4 *>(Lm.bias + o0 + tid * 4))
                                       : make_float4(0.f, 0.f, 0.f, 0.f);
-        if (tid == 0)
-            for (int k = 0; k < nkc; ++k) T->runs[k] = PollRun{mp + (size_t)k * d + o0, k * nch * 2, 0};
-        const bool good = poll(nkc, nkc * nch * 2, tag(lprev, 4), red);
+        const bool good = poll(PollRuns{mp + o0, d, nch * 2, nkc}, tag(lprev, 4), red);
         agree(good, code);
         const uint32_t land_a = su32(land), bar_a = su32(stb + B0);
         for (int i = tid; i < nch; i += CT) {
@@ -650,8 +643,7 @@ struct XkConsumer {
     // h = x + (c_proj + bias) -> land
     __device__ __forceinline__ void exchange_h(int l, int code) {
         const int c0 = slice_lo(rank, d / 4), nch = slice_lo(rank + 1, d / 4) - c0, o0 = c0 * 4;
-        if (tid == 0) T->runs[0] = PollRun{xp->pv_ll + (size_t)l * d + o0, 0, 0};
-        const bool good = poll(1, nch * 2, tag(l, 2), red);
+        const bool good = poll(PollRuns{xp->pv_ll + (size_t)l * d + o0, 0, nch * 2, 1}, tag(l, 2), red);
         agree(good, code);
         const uint32_t land_a = su32(land), bar_a = su32(stb + B0);
         for (int i = tid; i < nch; i += CT) {
@@ -670,8 +662,7 @@ struct XkConsumer {
     __device__ __forceinline__ void gather_f16(const uint64_t *src, int n_groups, uint32_t tg, __half *xs, float *sx,
                                                int bar, int code) {
         const int g0 = slice_lo(rank, n_groups), ng = slice_lo(rank + 1, n_groups) - g0;
-        if (tid == 0) T->runs[0] = PollRun{src + (size_t)g0 * 64, 0, 0};
-        const bool good = poll(1, ng * 32, tg, red);
+        const bool good = poll(PollRuns{src + (size_t)g0 * 64, 0, ng * 32, 1}, tg, red);
         agree(good, code);
         const uint32_t xs_a = su32(xs), sx_a = su32(sx), bar_a = su32(stb + bar);
         for (int i0 = 0; i0 < ng * 4; i0 += CT) {  // (threads of one group are 4 consecutive lanes)
