@@ -514,6 +514,30 @@ struct XkConsumer {
         a0 += fmaf(s0, d0[0] + d1[0], fmaf(-1024.0f, s0, z0) * sxg);
         a1 += fmaf(s1, d0[2] + d1[2], fmaf(-1024.0f, s1, z1) * sxg);
     }
+    // the same with the activation fragment (x0, x1) and its group sum already in registers
+    __device__ __forceinline__ void group_x(const uint8_t *tq, const uint8_t *tsb, int KC, int G64, int j, uint4 x0,
+                                            uint4 x1, float sxg, bool half_sb, float &a0, float &a1) {
+        const int jj = j ^ (g & 1);
+        const uint4 wa = *reinterpret_cast<const uint4 *>(tq + g * KC + jj * 64 + c * 16);
+        const uint4 wb = *reinterpret_cast<const uint4 *>(tq + (g + 8) * KC + jj * 64 + c * 16);
+        float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+        mma16816(d0, lo_h(wa.x), lo_h(wb.x), hi_h(wa.x), hi_h(wb.x), x0.x, x0.y);
+        mma16816(d1, lo_h(wa.y), lo_h(wb.y), hi_h(wa.y), hi_h(wb.y), x0.z, x0.w);
+        mma16816(d0, lo_h(wa.z), lo_h(wb.z), hi_h(wa.z), hi_h(wb.z), x1.x, x1.y);
+        mma16816(d1, lo_h(wa.w), lo_h(wb.w), hi_h(wa.w), hi_h(wb.w), x1.z, x1.w);
+        float s0, z0, s1, z1;
+        if (half_sb) {
+            const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(tsb + (g * G64 + j) * 4));
+            const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(tsb + ((g + 8) * G64 + j) * 4));
+            s0 = f0.x; z0 = f0.y; s1 = f1.x; z1 = f1.y;
+        } else {
+            const float2 f0 = *reinterpret_cast<const float2 *>(tsb + (g * G64 + j) * 8);
+            const float2 f1 = *reinterpret_cast<const float2 *>(tsb + ((g + 8) * G64 + j) * 8);
+            s0 = f0.x; z0 = f0.y; s1 = f1.x; z1 = f1.y;
+        }
+        a0 += fmaf(s0, d0[0] + d1[0], fmaf(-1024.0f, s0, z0) * sxg);
+        a1 += fmaf(s1, d0[2] + d1[2], fmaf(-1024.0f, s1, z1) * sxg);
+    }
     __device__ __forceinline__ void wait_slot(uint32_t slot, int code) {
         bool good = !ok || mb_wait<false>(fullp + slot, (seq / NSLOT) & 1u, pp->err);
         good = __all_sync(0xffffffffu, good);
@@ -531,25 +555,42 @@ struct XkConsumer {
         const int n = L.n_rb * L.n_kc;
         return R < n ? (n - 1 - R) / NR + 1 : 0;
     }
+    // Warp w takes groups w and w + CW of every tile (CW >= 10: at most 2 of the <= 20
+    // groups); with one K chunk the two activation fragments stay in registers for the
+    // whole stage, otherwise (the K-split mlp projection) they are loaded per tile.
     __device__ __forceinline__ void tiles(const MkLin &L, const __half *xs, const float *sx, int i0, int i1, bool qkv) {
+        static_assert(2 * CW >= MK_MAX_KC / 64, "two groups per warp cover a tile");
         const int KC = L.kc, G64 = KC / 64, nkc = L.n_kc;
         const bool half_sb = pp->sbb == 4;
-        int w0 = 0;
+        const int j0 = warp, j1 = warp + CW;
+        const bool h0 = j0 < G64, h1 = j1 < G64;
+        uint4 xa0 = make_uint4(0, 0, 0, 0), xa1 = xa0, xb0 = xa0, xb1 = xa0;
+        float sa = 0.f, sb = 0.f;
+        if (nkc == 1) {
+            if (h0) {
+                xa0 = *reinterpret_cast<const uint4 *>(xs + j0 * 64 + c * 16);
+                xa1 = *reinterpret_cast<const uint4 *>(xs + j0 * 64 + c * 16 + 8);
+                sa = sx[j0];
+            }
+            if (h1) {
+                xb0 = *reinterpret_cast<const uint4 *>(xs + j1 * 64 + c * 16);
+                xb1 = *reinterpret_cast<const uint4 *>(xs + j1 * 64 + c * 16 + 8);
+                sb = sx[j1];
+            }
+        }
         for (int i = i0; i < i1; ++i) {
-            const int kci = nkc == 1 ? 0 : tile_of(L, i, qkv) % nkc;
             const uint32_t slot = seq & (NSLOT - 1);
             wait_slot(slot, 2);
             const uint8_t *tq = smem + slot * SLOT;
             const uint8_t *tsb = tq + 16 * KC;
             float a0 = 0.f, a1 = 0.f;
-            {
-                int j = warp - w0;
-                if (j < 0) j += CW;
-                for (; j + CW < G64; j += 2 * CW) {
-                    group(tq, tsb, KC, G64, j, kci * G64 + j, xs, sx, half_sb, a0, a1);
-                    group(tq, tsb, KC, G64, j + CW, kci * G64 + j + CW, xs, sx, half_sb, a0, a1);
-                }
-                if (j < G64) group(tq, tsb, KC, G64, j, kci * G64 + j, xs, sx, half_sb, a0, a1);
+            if (nkc == 1) {
+                if (h0) group_x(tq, tsb, KC, G64, j0, xa0, xa1, sa, half_sb, a0, a1);
+                if (h1) group_x(tq, tsb, KC, G64, j1, xb0, xb1, sb, half_sb, a0, a1);
+            } else {
+                const int kci = tile_of(L, i, qkv) % nkc;
+                if (h0) group(tq, tsb, KC, G64, j0, kci * G64 + j0, xs, sx, half_sb, a0, a1);
+                if (h1) group(tq, tsb, KC, G64, j1, kci * G64 + j1, xs, sx, half_sb, a0, a1);
             }
             __syncwarp();
             if (lane == 0) mb_arrive(emptyp + slot);
@@ -559,7 +600,6 @@ struct XkConsumer {
                 r[g] = a0;
                 r[g + 8] = a1;
             }
-            w0 = (w0 + G64) % CW;
         }
         csync();
     }
