@@ -166,34 +166,6 @@ __device__ __forceinline__ void ll_ld2(const uint64_t *p, uint64_t &a, uint64_t 
 __device__ __forceinline__ float ll_val(uint64_t w) { return __uint_as_float((uint32_t)w); }
 __device__ __forceinline__ bool ll_ok(uint64_t w, uint32_t tag) { return (uint32_t)(w >> 32) == tag; }
 
-// Polls up to N pairs of LL words (16-byte aligned; ptr(j) == nullptr: none) until every
-// tag equals `tag`; out(j, a, b) receives each pair.  All loads of a round are issued
-// before any check.  False on timeout or when another CTA raised the error word.
-template <int N, class P, class O>
-__device__ __forceinline__ bool poll_pairs(P ptr, uint32_t tag, O out, const int *err) {
-    uint32_t pending = 0;
-#pragma unroll
-    for (int j = 0; j < N; ++j)
-        if (ptr(j)) pending |= 1u << j;
-    for (uint32_t it = 0; pending; ++it) {
-        uint64_t w[N][2];
-#pragma unroll
-        for (int j = 0; j < N; ++j)
-            if ((pending >> j) & 1u) ll_ld2(ptr(j), w[j][0], w[j][1]);
-#pragma unroll
-        for (int j = 0; j < N; ++j)
-            if (((pending >> j) & 1u) && ll_ok(w[j][0], tag) && ll_ok(w[j][1], tag)) {
-                out(j, ll_val(w[j][0]), ll_val(w[j][1]));
-                pending &= ~(1u << j);
-            }
-        if (pending) {
-            if (it >= SPIN || ((it & 255u) == 255u && *(volatile const int *)err)) return false;
-            __nanosleep(it < 4 ? 32u : (it < 16 ? 64u : 128u));
-        }
-    }
-    return true;
-}
-
 // The LL word pairs a gather polls: nruns runs of ppr pairs each, run r starting at
 // src + r * stride words (pair i: run i / ppr, pair i % ppr of it).  One out-of-line routine
 // polls every gather, so the exchanges of a layer share one copy of the polling code.
