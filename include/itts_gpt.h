@@ -254,9 +254,11 @@ int itts_gpt_last_timing(const itts_gpt *gpt, float *prefill_ms, float *decode_m
 int itts_bench_decode_forward(itts_gpt *gpt, itts_kv *kv, int32_t nb, int32_t kv_len,
                               int32_t iters, float *ms_per_step, int32_t *launches_per_step);
 
-/* The same for one step of the persistent decode-step kernel (nb <= 4), with per-CTA
- * stage timestamps (device globaltimer, ns): out[cta * events_per_cta + i], 0 where a CTA
- * recorded nothing.  out_len must be at least grid * 256. */
+/* The same for one step of nb <= 4 columns with per-CTA stage timestamps (device
+ * globaltimer, ns) recorded by whichever single-launch decode-step kernel the cache runs for
+ * nb (itts_kv_decode_kernel): out[cta * events_per_cta + i], 0 where a CTA recorded nothing
+ * (the cluster kernels use fewer CTAs than the reported grid).  out_len must be at least
+ * grid * 256.  No reference counterpart (a profiling aid). */
 int itts_bench_trace(itts_gpt *gpt, itts_kv *kv, int32_t nb, int32_t kv_len,
                      unsigned long long *out, int32_t out_len, int32_t *grid,
                      int32_t *events_per_cta);
