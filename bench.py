@@ -432,8 +432,8 @@ def run_profile_prefill_batch(args):
 
 # stage timeline events of xk_decode_kernel per layer (l >= 1) on cluster ranks other than 0
 XK_EVENTS = ["x sent", "x gathered", "LayerNorm 1", "QKV tiles + push", "q/k/v in cluster", "attention",
-             "attention output sent", "attention output gathered", "c_proj tile", "h sent", "h gathered",
-             "LayerNorm 2", "c_fc tiles", "u sent", "u gathered", "mlp tiles"]
+             "head output in cluster", "c_proj partials added", "h sent", "h gathered", "LayerNorm 2",
+             "c_fc tiles", "u sent", "u gathered", "mlp tiles"]
 
 
 def run_profile_trace(args):
@@ -461,7 +461,7 @@ def run_profile_trace(args):
     nr = int((t[:, 0] > 0).sum())
     ev = (t[:nr] - t[:nr, 0].min()) / 1000.0
     sel = [r for r in range(nr) if r % 6 != 0]  # rank 0 of each cluster records one event more
-    E, first, nl = len(XK_EVENTS), 15, 14  # layer 0 has no x exchange (15 events); 256 events hold 14 layers
+    E, first, nl = len(XK_EVENTS), 14, 15  # layer 0 has no x exchange (14 events); 256 events hold 15 layers
     lay = ev[sel, first:first + (nl - 1) * E].reshape(len(sel), nl - 1, E)
     rel = lay[:, 1:, :] - lay[:, 1:, 1].min(0)[None, :, None]
     per_layer = (lay[:, -1, 0].min() - lay[:, 0, 0].min()) / (nl - 2)

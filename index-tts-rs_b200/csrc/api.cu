@@ -69,6 +69,7 @@ struct itts_gpt {
     MkLayer *d_layers = nullptr;
     void *arena = nullptr;
     __half *w16_arena = nullptr;  // fp16 copies of the layer weights (long prefills), made once
+    void *projh_arena = nullptr;  // head-major c_proj copies (batch-1 cluster decode step)
     bool w16_tried = false;
     cudaStream_t stream = nullptr;
     cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
@@ -223,6 +224,7 @@ static void gpt_destroy(itts_gpt *g) {
         if (e) cudaEventDestroy(e);
     cudaFree(g->arena);
     cudaFree(g->w16_arena);
+    cudaFree(g->projh_arena);
     cudaFree(g->d_layers);
     cudaFree(g->d_sstate);
     cudaFree(g->d_slogits);
@@ -429,6 +431,23 @@ extern "C" int itts_gpt_from_tensors(const itts_tensor *tensors, int32_t n_tenso
         L.ln1_w = F(li[i].l1w); L.ln1_b = F(li[i].l1b); L.ln2_w = F(li[i].l2w); L.ln2_b = F(li[i].l2b);
         L.qkv = mk(li[i].a); L.proj = mk(li[i].p); L.fc = mk(li[i].fc); L.mlp = mk(li[i].mp);
     }
+    // head-major copies of the c_proj weights (batch-1 cluster decode step), made once here
+    {
+        const MkLin &P0 = g->layers[0].proj;
+        const size_t per = (size_t)(d / 64) * P0.n_rb * mk_projh_chunk_bytes(P0.sbb);
+        if (d % 64 == 0 && P0.n_kc == 1 && P0.kc == (int)d && cudaMalloc(&g->projh_arena, per * n_layers) == cudaSuccess) {
+            for (int i = 0; i < n_layers && e == cudaSuccess; ++i) {
+                uint8_t *dst = (uint8_t *)g->projh_arena + per * i;
+                e = make_proj_by_head(g->layers[i].proj, (int)(d / 64), dst, g->stream);
+                g->layers[i].proj_h = dst;
+            }
+            if (e == cudaSuccess) e = cudaStreamSynchronize(g->stream);
+            if (e != cudaSuccess) return fail(e, "c_proj copy");
+        } else {
+            cudaGetLastError();
+            for (int i = 0; i < n_layers; ++i) g->layers[i].proj_h = nullptr;
+        }
+    }
     if ((e = cudaMalloc(&g->d_layers, sizeof(MkLayer) * n_layers)) != cudaSuccess) return fail(e, "layers");
     if ((e = cudaMemcpy(g->d_layers, g->layers.data(), sizeof(MkLayer) * n_layers, cudaMemcpyHostToDevice)) != cudaSuccess)
         return fail(e, "layers");
@@ -609,7 +628,7 @@ static void kv_destroy(itts_kv *kv) {
     void *dev[] = {kv->k, kv->v, kv->d_slots, kv->d_batch_slot, kv->db.x, kv->db.n, kv->db.n2,
                    kv->db.q, kv->db.attn, kv->db.u, kv->db.logits, kv->db.partials,
                    kv->db.counters, kv->db.qkv_ll, kv->db.epoch, kv->db.err, kv->db.trace, kv->db.ws,
-                   kv->db.xkb.ao_ll,
+                   kv->db.xkb.hacc,
                    kv->pb.x, kv->pb.n, kv->pb.qkv, kv->pb.attn,
                    kv->pb.u, kv->d_codes, kv->d_text, kv->d_prior, kv->d_conds};
     for (void *p : dev) cudaFree(p);
@@ -701,15 +720,15 @@ extern "C" int itts_kv_create(itts_gpt *g, int32_t max_seq, int32_t max_batch, i
         if (e == cudaSuccess && xk_config(m, &xc) > 0) {
             const size_t L = m.n_layers;
             const size_t words = L * (2 * (size_t)m.d + m.ff + (size_t)xc.nkc * m.d);
-            const size_t bytes = words * 8 + sizeof(uint32_t) * xc.grid;
-            A((void **)&kv->db.xkb.ao_ll, bytes);
+            const size_t bytes = words * 8 + sizeof(uint32_t) * (2 * L + xc.grid);
+            A((void **)&kv->db.xkb.hacc, bytes);
             if (e == cudaSuccess) {
                 XkBufs &x = kv->db.xkb;
-                x.pv_ll = x.ao_ll + L * m.d;
-                x.u_ll = x.pv_ll + L * m.d;
+                x.u_ll = reinterpret_cast<uint64_t *>(x.hacc + 2 * L * m.d);
                 x.mp_ll = x.u_ll + L * m.ff;
-                x.epoch = reinterpret_cast<uint32_t *>(x.mp_ll + L * xc.nkc * m.d);
-                e = cudaMemsetAsync(x.ao_ll, 0, bytes, g->stream);
+                x.hcnt = reinterpret_cast<uint32_t *>(x.mp_ll + L * xc.nkc * m.d);
+                x.epoch = x.hcnt + 2 * L;
+                e = cudaMemsetAsync(x.hacc, 0, bytes, g->stream);
                 kv->db.xk = xc;
             }
         }

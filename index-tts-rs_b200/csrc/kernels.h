@@ -31,8 +31,10 @@ struct ModelView {
 struct XkConfig {
     int grid = 0, rt = 0, nkc = 0, coop = 0;
 };
-struct XkBufs {  // one allocation: [L][d] attention output, [L][d] c_proj, [L][ff] u, [L][nkc][d] mlp partials
-    uint64_t *ao_ll = nullptr, *pv_ll = nullptr, *u_ll = nullptr, *mp_ll = nullptr;
+struct XkBufs {  // one allocation: [2][L][d] c_proj accumulators, [L][ff] u, [L][nkc][d] mlp partials, counters
+    unsigned long long *hacc = nullptr;  // fixed-point (2^-32) sums of the heads' c_proj partials, by step parity
+    uint64_t *u_ll = nullptr, *mp_ll = nullptr;
+    uint32_t *hcnt = nullptr;   // [2][L] CTAs that added their c_proj partials
     uint32_t *epoch = nullptr;
 };
 
@@ -116,6 +118,8 @@ int ck_config(const ModelView &m);
 // Fills `out` and returns the grid size, or -1 when the model or the device does not fit it.
 int xk_config(const ModelView &m, XkConfig *out);
 cudaError_t xk_launch(const MkParams &p, const XkConfig &xc, const XkBufs &b, cudaStream_t st);
+// The head-major copy of a c_proj (MkLayer::proj_h) from its tiles: n_heads * n_rb chunks.
+cudaError_t make_proj_by_head(const MkLin &W, int n_heads, uint8_t *dst, cudaStream_t st);
 cudaError_t ck_launch(const MkParams &p, int rt, cudaStream_t st);
 // Number of kernels decode_forward launches for nb columns.
 int decode_forward_launches(const ModelView &m, const DecodeBufs &b, int nb);

@@ -30,7 +30,13 @@ struct MkLin {
 struct MkLayer {
     const float *ln1_w, *ln1_b, *ln2_w, *ln2_b;
     MkLin qkv, proj, fc, mlp;
+    // c_proj re-tiled by attention head (null when not made): for head h and row block rb
+    // the chunk (h * n_rb + rb) of 16 rows x the head's 64 inputs (int8 bytes in fragment
+    // order, row m at 64 m, no swizzle) followed by the 16 rows' (scale, offset) pairs of
+    // that group; the batch-1 cluster decode step reads c_proj from here
+    const uint8_t *proj_h;
 };
+__host__ __device__ inline int mk_projh_chunk_bytes(int sbb) { return 16 * 64 + 16 * sbb; }
 
 constexpr int MK_MAX_D = 2048;      // model dim limit of the persistent kernel
 constexpr int MK_MAX_UNITS = 8;     // attention units per (column, head)

@@ -56,9 +56,9 @@ constexpr int NWS = 5;             // LL-writing stages per layer: qkv, records,
 constexpr uint32_t SPIN = 1u << 22;
 constexpr float kLog2e = 1.4426950408889634f;
 
-// landing barriers: x/h (fp32), attention output (fp16), u (fp16), the head's q/k/v (fp32),
-// the head's attention records (cluster rank 0 only)
-enum { B0 = 0, BAO, BU, BQ, BR, NSTB };
+// landing barriers: x/h (fp32), the head's attention output (fp16 + its sum), u (fp16), the
+// head's q/k/v (fp32), the head's attention records (cluster rank 0 only)
+enum { B0 = 0, BA, BU, BQ, BR, NSTB };
 
 // ---------------------------------------------------------------------------
 // PTX helpers
@@ -219,7 +219,7 @@ __device__ __noinline__ bool poll_runs(PollRuns pr, uint32_t tag, float *stage, 
 // shared-memory carve-up (identical on host and device)
 // ---------------------------------------------------------------------------
 struct XkSmem {
-    uint32_t land, xln, xao, xu, sxln, sxao, sxu, red, qkvh, recs, stat, tab, lay, bar, total;
+    uint32_t land, xln, xh, xu, sxln, sxu, red, qkvh, recs, stat, tab, lay, bar, total;
 };
 __host__ __device__ inline uint32_t xk_red_bytes(int rt, int d, int ff) {
     uint32_t m = (uint32_t)rt * CW * 16 * 4;                                   // tile partial sums
@@ -241,10 +241,9 @@ __host__ __device__ inline XkSmem xk_layout(int d, int ff, int rt, int n_layers)
     };
     L.land = take(d * 4);
     L.xln = take(d * 2);
-    L.xao = take(d * 2);
+    L.xh = take(64 * 2 + 16);  // the head's attention output (fp16, fragment order) + its sum
     L.xu = take(ff * 2);
     L.sxln = take(d / 64 * 4);
-    L.sxao = take(d / 64 * 4);
     L.sxu = take(ff / 64 * 4);
     L.red = take(xk_red_bytes(rt, d, ff));
     L.qkvh = take(3 * 64 * 4);
@@ -259,8 +258,9 @@ __host__ __device__ inline XkSmem xk_layout(int d, int ff, int rt, int n_layers)
 
 struct XkParams {
     MkParams p;          // model, slots, KV cache, logits, err, trace
-    uint64_t *ao_ll;     // [L][d]     attention output (each head's, merged by its cluster)
-    uint64_t *pv_ll;     // [L][d]     c_proj output + bias
+    unsigned long long *hacc;  // [2][L][d] sums of the heads' c_proj partials, fixed point 2^-32,
+                               // by step parity (this step's buffer p = epoch & 1; 1 - p zeroed)
+    uint32_t *hcnt;            // [2][L] CTAs that added their partials
     uint64_t *u_ll;      // [L][ff]    GELU(c_fc)
     uint64_t *mp_ll;     // [L][nkc][d] mlp c_proj K-chunk partial sums
     uint32_t *epoch;     // [grid] launches completed per CTA
@@ -325,7 +325,11 @@ struct XkProducer {
                     issue(p.kc + off, (uint32_t)np * 128u, p.vc + off, (uint32_t)np * 128u);
                 }
             }
-            lin(&Ly->proj);
+            {  // this rank's head-major c_proj chunks of the head (one copy)
+                const int nrb = Ly->proj.n_rb, r0 = rank * nrb / CS, nc = (rank + 1) * nrb / CS - r0;
+                const uint32_t cb = (uint32_t)mk_projh_chunk_bytes(Ly->proj.sbb);
+                if (nc > 0) issue(Ly->proj_h + ((size_t)head * nrb + r0) * cb, (uint32_t)nc * cb, nullptr, 0);
+            }
             lin(&Ly->fc);
             lin(&Ly->mlp);
         }
@@ -346,8 +350,9 @@ struct XkConsumer {
     XkTab *T;
     const MkLayer *lay;  // shared-memory copy of the layer table
     uint8_t *smem;
-    float *land, *sxln, *sxao, *sxu, *red, *qkvh, *recs, *stat;
-    __half *xln, *xao, *xu;
+    float *land, *sxln, *sxu, *red, *qkvh, *recs, *stat;
+    __half *xln, *xh, *xu;  // xh: the head's attention output (fp16, fragment order), sum after it
+    uint32_t par;           // this step's accumulator buffer
     uint64_t *fullp, *emptyp, *stb;
     int tid, warp, lane, g, c, rank, R, NR, d, ff, H, rt, head;
     uint32_t seq, tbase;
@@ -652,18 +657,37 @@ struct XkConsumer {
         trace();
         wait_land(B0, code + 1);
     }
-    // h = x + (c_proj + bias) -> land
-    __device__ __forceinline__ void exchange_h(int l, int code) {
+    // h = x + c_proj bias + the fixed-point sum of the heads' c_proj partials -> land, once
+    // every CTA of the grid has added its partials (counter)
+    __device__ __forceinline__ void exchange_h(int l, float4 bpre, int code) {
         const int c0 = slice_lo(rank, d / 4), nch = slice_lo(rank + 1, d / 4) - c0, o0 = c0 * 4;
-        const bool good = poll(PollRuns{xp->pv_ll + (size_t)l * d + o0, 0, nch * 2, 1}, tag(l, 2), red);
+        const uint32_t *cnt = xp->hcnt + par * pp->n_layers + l;
+        const unsigned long long *acc = xp->hacc + ((size_t)par * pp->n_layers + l) * d;
+        bool good = true;
+        if (tid < nch && ok) {
+            good = false;
+            for (uint32_t it = 0; it < SPIN; ++it) {
+                uint32_t v;
+                asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(cnt) : "memory");
+                if (v >= (uint32_t)NR) { good = true; break; }
+                if ((it & 255u) == 255u && *(volatile const int *)pp->err) break;
+                if (it >= 8) __nanosleep(it < 32 ? 32u : 128u);
+            }
+        }
         agree(good, code);
         const uint32_t land_a = su32(land), bar_a = su32(stb + B0);
         for (int i = tid; i < nch; i += CT) {
             const int o = o0 + i * 4;
+            unsigned long long q0, q1, q2, q3;
+            asm volatile("ld.relaxed.gpu.global.v2.b64 {%0,%1}, [%2];" : "=l"(q0), "=l"(q1) : "l"(acc + o) : "memory");
+            asm volatile("ld.relaxed.gpu.global.v2.b64 {%0,%1}, [%2];" : "=l"(q2), "=l"(q3) : "l"(acc + o + 2) : "memory");
             const float4 x = *reinterpret_cast<const float4 *>(land + o);
-            const float4 v = *reinterpret_cast<const float4 *>(red + i * 4);
-            bcast_v4(land_a + o * 4, make_uint4(__float_as_uint(x.x + v.x), __float_as_uint(x.y + v.y),
-                                                __float_as_uint(x.z + v.z), __float_as_uint(x.w + v.w)), bar_a);
+            const float sc = 2.3283064365386963e-10f;  // 2^-32
+            const float4 v = make_float4((float)(long long)q0 * sc, (float)(long long)q1 * sc,
+                                         (float)(long long)q2 * sc, (float)(long long)q3 * sc);
+            bcast_v4(land_a + o * 4, make_uint4(__float_as_uint(x.x + bpre.x + v.x), __float_as_uint(x.y + bpre.y + v.y),
+                                                __float_as_uint(x.z + bpre.z + v.z), __float_as_uint(x.w + bpre.w + v.w)),
+                     bar_a);
         }
         trace();
         wait_land(B0, code + 1);
@@ -713,9 +737,7 @@ struct XkConsumer {
     __device__ __forceinline__ void exchange_u(int l, int code) {
         gather_f16(xp->u_ll + (size_t)l * ff, ff / 64, tag(l, 3), xu, sxu, BU, code);
     }
-    __device__ __forceinline__ void exchange_ao(int l, int code) {
-        gather_f16(xp->ao_ll + (size_t)l * d, d / 64, tag(l, 1), xao, sxao, BAO, code);
-    }
+
 
     // ---- stages ----
     __device__ __forceinline__ void stage_qkv(int l) {
@@ -892,40 +914,98 @@ struct XkConsumer {
         }
         if (rank == 0) {
             wait_land(BR, 31);
-            uint64_t *ao = xp->ao_ll + (size_t)l * d + head * 64;
-            if (tid < 32) {  // dims 2 tid, 2 tid + 1
+            __half *ho = reinterpret_cast<__half *>(red);  // [64] fragment order
+            if (tid < 64) {
                 float M = -INFINITY;
                 for (int r = 0; r < CS; ++r) M = fmaxf(M, recs[r * REC]);
-                float L2 = 0.f, A0 = 0.f, A1 = 0.f;
+                float L2 = 0.f, A = 0.f;
                 for (int r = 0; r < CS; ++r) {
                     const float mr = recs[r * REC];
                     const float f = mr == -INFINITY ? 0.f : exp2f(mr - M);
                     L2 += recs[r * REC + 1] * f;
-                    A0 += recs[r * REC + 4 + 2 * tid] * f;
-                    A1 += recs[r * REC + 5 + 2 * tid] * f;
+                    A += recs[r * REC + 4 + tid] * f;
                 }
-                const bool any = L2 > 0.f;
-                ll_st2(ao + 2 * tid, any ? A0 / L2 : 0.f, any ? A1 / L2 : 0.f, tag(l, 1));
+                const __half hv = __float2half_rn(L2 > 0.f ? A / L2 : 0.f);
+                ho[frag_pos_host(tid)] = hv;
+                const float hs = warp_sum(__half2float(hv));  // (warps 0 and 1, all lanes)
+                if (lane == 0) stat[warp] = hs;
+            }
+            csync();
+            const uint32_t xh_a = su32(xh), bar_a = su32(stb + BA);
+            if (tid < 8) bcast_v4(xh_a + tid * 16, reinterpret_cast<const uint4 *>(ho)[tid], bar_a);
+            if (tid == 8) {
+                const float hs = stat[0] + stat[1];
+#pragma unroll
+                for (int r = 0; r < CS; ++r) st_async_b32(mapa(xh_a + 128, r), __float_as_uint(hs), mapa(bar_a, r));
             }
         }
         trace();
     }
+    // c_proj of the cluster's head: this rank's range of the head-major chunks (16 rows x the
+    // head's 64 inputs, one chunk per warp at a time); each row's partial is added to the
+    // step's fixed-point accumulator (64-bit integer adds: the sum does not depend on their
+    // order), then the CTA counts itself in
     __device__ __forceinline__ void stage_proj(int l) {
-        const float4 bpre = bias_pre(lay[l].proj, false);
-        exchange_ao(l, 40);
-        const MkLin &L = lay[l].proj;
-        uint64_t *pv = xp->pv_ll + (size_t)l * d;
-        const uint32_t tg = tag(l, 2);
-        run_lin(L, xao, sxao, bpre, false, [&](int o, int, float4 v, float4 bb) {
-            ll_st2(pv + o, v.x + bb.x, v.y + bb.y, tg);
-            ll_st2(pv + o + 2, v.z + bb.z, v.w + bb.w, tg);
-        });
+        wait_land(BA, 40);
+        const MkLin &P = lay[l].proj;
+        const int nrb = P.n_rb, r0 = rank * nrb / CS, nc = (rank + 1) * nrb / CS - r0;
+        const bool half_sb = pp->sbb == 4;
+        const int cb = mk_projh_chunk_bytes(pp->sbb);
+        const float hsum = reinterpret_cast<const float *>(xh + 64)[0];
+        unsigned long long *acc = xp->hacc + ((size_t)par * pp->n_layers + l) * d;
+        if (nc > 0) {
+            const uint32_t slot = seq & (NSLOT - 1);
+            wait_slot(slot, 4);
+            const uint8_t *base = smem + slot * SLOT;
+            const uint4 x0 = *reinterpret_cast<const uint4 *>(xh + c * 16);
+            const uint4 x1 = *reinterpret_cast<const uint4 *>(xh + c * 16 + 8);
+            for (int i = warp; i < nc; i += CW) {
+                const uint8_t *tq = base + i * cb, *tsb = tq + 16 * 64;
+                const uint4 wa = *reinterpret_cast<const uint4 *>(tq + g * 64 + c * 16);
+                const uint4 wb = *reinterpret_cast<const uint4 *>(tq + (g + 8) * 64 + c * 16);
+                float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+                mma16816(d0, lo_h(wa.x), lo_h(wb.x), hi_h(wa.x), hi_h(wb.x), x0.x, x0.y);
+                mma16816(d1, lo_h(wa.y), lo_h(wb.y), hi_h(wa.y), hi_h(wb.y), x0.z, x0.w);
+                mma16816(d0, lo_h(wa.z), lo_h(wb.z), hi_h(wa.z), hi_h(wb.z), x1.x, x1.y);
+                mma16816(d1, lo_h(wa.w), lo_h(wb.w), hi_h(wa.w), hi_h(wb.w), x1.z, x1.w);
+                float s0, z0, s1, z1;
+                if (half_sb) {
+                    const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(tsb + g * 4));
+                    const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(tsb + (g + 8) * 4));
+                    s0 = f0.x; z0 = f0.y; s1 = f1.x; z1 = f1.y;
+                } else {
+                    const float2 f0 = *reinterpret_cast<const float2 *>(tsb + g * 8);
+                    const float2 f1 = *reinterpret_cast<const float2 *>(tsb + (g + 8) * 8);
+                    s0 = f0.x; z0 = f0.y; s1 = f1.x; z1 = f1.y;
+                }
+                const float y0 = fmaf(s0, d0[0] + d1[0], fmaf(-1024.0f, s0, z0) * hsum);
+                const float y1 = fmaf(s1, d0[2] + d1[2], fmaf(-1024.0f, s1, z1) * hsum);
+                if (c == 0) {
+                    const int o = (r0 + i) * 16;
+                    atomicAdd(acc + o + g, (unsigned long long)__float2ll_rn(y0 * 4294967296.0f));
+                    atomicAdd(acc + o + g + 8, (unsigned long long)__float2ll_rn(y1 * 4294967296.0f));
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mb_arrive(emptyp + slot);
+            ++seq;
+        }
+        __threadfence();
+        csync();
+        if (tid == 0) {
+            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(xp->hcnt + par * pp->n_layers + l) : "memory");
+        }
+        trace();
     }
     __device__ __forceinline__ void stage_fc(int l) {
         const MkLayer &Ly = lay[l];
         const LnRegs ln2 = ln_prefetch(Ly.ln2_w, Ly.ln2_b);
         const float4 bpre = bias_pre(Ly.fc, false);
-        exchange_h(l, 50);
+        const int hc0 = slice_lo(rank, d / 4) * 4;
+        const float4 hbias = tid < slice_lo(rank + 1, d / 4) - slice_lo(rank, d / 4)
+                                 ? __ldg(reinterpret_cast<const float4 *>(Ly.proj.bias + hc0 + tid * 4))
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+        exchange_h(l, hbias, 50);
         layernorm(ln2, false);
         const MkLin &L = Ly.fc;
         uint64_t *u = xp->u_ll + (size_t)l * ff;
@@ -1006,7 +1086,7 @@ __global__ void __launch_bounds__(NT, 1) xk_decode_kernel(const __grid_constant_
         for (int b = 0; b < NSTB; ++b) mb_init(stb + b, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         mb_expect(stb + B0, (uint32_t)p.d * 4);
-        mb_expect(stb + BAO, (uint32_t)p.d * 2 + p.d / 64 * 4);  // fp16 values + group sums
+        mb_expect(stb + BA, 64 * 2 + 4);  // the head's output: fp16 values + their sum
         mb_expect(stb + BU, (uint32_t)p.ff * 2 + p.ff / 64 * 4);
         mb_expect(stb + BQ, 3 * 64 * 4);
         mb_expect(stb + BR, CS * REC * 4);  // (waited on by rank 0 only)
@@ -1024,6 +1104,13 @@ __global__ void __launch_bounds__(NT, 1) xk_decode_kernel(const __grid_constant_
     }
     __syncthreads();
     const uint32_t epoch = xp.epoch[R];
+    {  // the next step's c_proj accumulators and counters (this step's were zeroed by the last)
+        const uint32_t q = (epoch & 1u) ^ 1u;
+        const size_t n = (size_t)p.n_layers * p.d;
+        unsigned long long *a = xp.hacc + q * n;
+        for (size_t i = (size_t)R * NT + tid; i < n; i += (size_t)NR * NT) a[i] = 0ull;
+        if (R == 0 && tid < p.n_layers) xp.hcnt[q * p.n_layers + tid] = 0u;
+    }
     // every CTA's barriers are armed before any CTA pushes into them
     cluster_sync_all();
 
@@ -1052,10 +1139,10 @@ __global__ void __launch_bounds__(NT, 1) xk_decode_kernel(const __grid_constant_
         C.smem = smem;
         C.land = reinterpret_cast<float *>(smem + SL.land);
         C.xln = reinterpret_cast<__half *>(smem + SL.xln);
-        C.xao = reinterpret_cast<__half *>(smem + SL.xao);
+        C.xh = reinterpret_cast<__half *>(smem + SL.xh);
+        C.par = epoch & 1u;
         C.xu = reinterpret_cast<__half *>(smem + SL.xu);
         C.sxln = reinterpret_cast<float *>(smem + SL.sxln);
-        C.sxao = reinterpret_cast<float *>(smem + SL.sxao);
         C.sxu = reinterpret_cast<float *>(smem + SL.sxu);
         C.red = reinterpret_cast<float *>(smem + SL.red);
         C.qkvh = reinterpret_cast<float *>(smem + SL.qkvh);
@@ -1083,7 +1170,7 @@ __global__ void __launch_bounds__(NT, 1) xk_decode_kernel(const __grid_constant_
         C.ev = 0;
         for (int b = 0; b < NSTB; ++b) C.ph[b] = 0;
         C.exp_bytes[B0] = (uint32_t)p.d * 4;
-        C.exp_bytes[BAO] = (uint32_t)p.d * 2 + p.d / 64 * 4;
+        C.exp_bytes[BA] = 64 * 2 + 4;
         C.exp_bytes[BU] = (uint32_t)p.ff * 2 + p.ff / 64 * 4;
         C.exp_bytes[BQ] = 3 * 64 * 4;
         C.exp_bytes[BR] = CS * REC * 4;
@@ -1140,6 +1227,7 @@ int xk_config(const ModelView &m, XkConfig *out) {
         for (const MkLin *x : {&L.qkv, &L.proj, &L.fc, &L.mlp})
             if (x->tile_bytes > SLOT || x->kc % 64) return -1;
         if (L.qkv.n_kc != 1 || L.proj.n_kc != 1 || L.fc.n_kc != 1 || L.mlp.n_kc > 4) return -1;
+        if (!L.proj_h || (L.proj.n_rb + CS - 1) / CS * mk_projh_chunk_bytes(L.proj.sbb) > SLOT) return -1;
         if (L.qkv.out != 3 * m.d || L.proj.out != m.d || L.fc.out != m.ff || L.mlp.out != m.d) return -1;
         nkc = std::max(nkc, L.mlp.n_kc);
     }
@@ -1214,8 +1302,8 @@ int xk_config(const ModelView &m, XkConfig *out) {
 cudaError_t xk_launch(const MkParams &p, const XkConfig &xc, const XkBufs &b, cudaStream_t st) {
     XkParams xp{};
     xp.p = p;
-    xp.ao_ll = b.ao_ll;
-    xp.pv_ll = b.pv_ll;
+    xp.hacc = b.hacc;
+    xp.hcnt = b.hcnt;
     xp.u_ll = b.u_ll;
     xp.mp_ll = b.mp_ll;
     xp.epoch = b.epoch;
@@ -1223,6 +1311,31 @@ cudaError_t xk_launch(const MkParams &p, const XkConfig &xc, const XkBufs &b, cu
     xp.nkc = xc.nkc;
     xp.dry = 0;
     return xk_launch_cfg(xp, xc.grid, xk_layout(p.d, p.ff, xc.rt, p.n_layers).total, xc.coop != 0, st);
+}
+
+// chunk (h, rb) of the head-major c_proj copy from tile rb (n_kc == 1): row m's bytes of group h
+// (stored at group slot h ^ (m & 1) in the tile) to 64 m, then the 16 rows' (scale, offset)
+// pairs of group h
+__global__ void proj_by_head_kernel(const uint8_t *tiles, int tile_bytes, int kc, int sbb, uint8_t *dst) {
+    const int rb = blockIdx.x, h = blockIdx.y, n_rb = gridDim.x, G64 = kc / 64;
+    const uint8_t *t = tiles + (size_t)rb * tile_bytes;
+    uint8_t *o = dst + ((size_t)h * n_rb + rb) * mk_projh_chunk_bytes(sbb);
+    for (int i = threadIdx.x; i < 16 * 16; i += blockDim.x) {  // 16 rows x 16 words
+        const int m = i >> 4, w = i & 15;
+        reinterpret_cast<uint32_t *>(o + m * 64)[w] =
+            reinterpret_cast<const uint32_t *>(t + (size_t)m * kc + (h ^ (m & 1)) * 64)[w];
+    }
+    for (int i = threadIdx.x; i < 16 * sbb / 4; i += blockDim.x) {
+        const int m = i / (sbb / 4), w = i - m * (sbb / 4);
+        reinterpret_cast<uint32_t *>(o + 16 * 64 + m * sbb)[w] =
+            reinterpret_cast<const uint32_t *>(t + 16 * kc + (size_t)(m * G64 + h) * sbb)[w];
+    }
+}
+
+cudaError_t make_proj_by_head(const MkLin &W, int n_heads, uint8_t *dst, cudaStream_t st) {
+    if (W.n_kc != 1 || W.kc != n_heads * 64) return cudaErrorInvalidValue;
+    proj_by_head_kernel<<<dim3(W.n_rb, n_heads), 128, 0, st>>>(W.tiles, W.tile_bytes, W.kc, W.sbb, dst);
+    return cudaGetLastError();
 }
 
 }  // namespace itts
