@@ -7,18 +7,22 @@
 // Cluster c owns head c: its ranks compute the 12 QKV row blocks of the head (q, k, v rows
 // 64c .. 64c + 63), append K/V to the cache and push the 192 values into every CTA of the
 // cluster with st.async; each rank then attends over its range of the head's 84-position
-// K/V tiles and pushes one (m, l, acc[64]) record into cluster rank 0, which merges them
-// and writes the head's 64 outputs.  So q/k/v and the attention partials never leave the
-// cluster.
+// K/V tiles and pushes one (m, l, acc[64]) record into cluster rank 0, which merges them and
+// pushes the head's 64 outputs (fp16) back into the cluster.  The cluster then applies the
+// head's 64 columns of c_proj (a head-major copy of its weights made at load) to them and
+// adds each row's partial into a per-step accumulator with 64-bit fixed-point (2^-32)
+// atomics, whose sum does not depend on the order of the adds; a counter tells the h gather
+// when all CTAs have added theirs.  So q/k/v, the attention partials and the attention
+// output never cross clusters.
 //
-// Everything else crosses clusters as 64-bit LL words {fp32 value, stage tag} in global
-// memory (the tag is unique per launch, layer and stage, so no buffer is ever reset), and
-// each stage input vector (x, attention output, h, u) is gathered ONCE per cluster: rank k
-// polls the k-th sixth of the vector (finishing it on the way: residual add, K-split sum,
-// fp16 conversion) and pushes it into all 6 CTAs with st.async; each CTA's mbarrier counts
-// the bytes.  The c_proj, c_fc, mlp and head tiles are dealt round-robin over the grid
-// (tile t on CTA t % grid; the mlp projection is K-split and the gathering rank sums its
-// four chunk partials in a fixed order).
+// x, h and u cross clusters as 64-bit LL words {fp32 value, stage tag} in global memory (the
+// tag is unique per launch, layer and stage, so no buffer is ever reset) or, for h, through
+// the accumulator, and each of them is gathered ONCE per cluster: rank k reads the k-th sixth
+// of the vector (finishing it on the way: residual add, K-split sum, fp16 conversion) and
+// pushes it into all 6 CTAs with st.async; each CTA's mbarrier counts the bytes.  The c_fc,
+// mlp and head tiles are dealt round-robin over the grid (tile t on CTA t % grid; the mlp
+// projection is K-split and the gathering rank sums its four chunk partials in a fixed
+// order).
 //
 // Per CTA: 11 consumer warps + 1 producer warp.  The producer lane streams the CTA's weight
 // tiles and K/V rows into an 8-slot cp.async.bulk ring (no multicast) ahead of the stages;
