@@ -5,7 +5,7 @@
  * (crates/core/src/models/mod.rs:41-59 re-exports; the implementations are in
  * crates/core/src/models/gpt.rs and crates/core/src/models/sampler.rs).  Each entry
  * point below names the Rust item it replaces.  A Rust `-sys` crate binds this
- * header one to one; see INTEGRATION.md.
+ * header one to one.
  *
  * Conventions
  *  - Every call returns an int status: ITTS_OK or one of the ITTS_E_* codes, which
@@ -138,10 +138,9 @@ int itts_kv_valid_len(const itts_kv *kv, int32_t slot, int32_t *out);
 int32_t itts_kv_max_seq(const itts_kv *kv);
 int32_t itts_kv_max_batch(const itts_kv *kv);
 /* Which decode-step kernel runs a step of `n_columns` batch columns on this cache:
- * 1 = one 16-CTA thread-block cluster (batch 1, only when the environment variable
- * ITTS_CLUSTER=1 was set at itts_kv_create), 2 = the persistent grid-wide kernel (up to
- * 4 columns), 3 = the multi-launch GEMM path, 4 = one 6-CTA cluster per attention head
- * (batch 1 by default; ITTS_XK=0 at itts_kv_create turns it off).  No reference counterpart (the
+ * 2 = the persistent grid-wide kernel (up to 4 columns), 3 = the multi-launch GEMM path,
+ * 4 = one 6-CTA cluster per attention head (batch 1 by default; ITTS_XK=0 at
+ * itts_kv_create turns it off).  No reference counterpart (the
  * reference has one MLX code path); used by tests and the benchmark to name the kernel. */
 int32_t itts_kv_decode_kernel(const itts_kv *kv, int32_t n_columns);
 

@@ -714,20 +714,20 @@ extern "C" int itts_kv_create(itts_gpt *g, int32_t max_seq, int32_t max_batch, i
         if (e == cudaSuccess) e = cudaMemsetAsync(kv->db.epoch, 0, sizeof(uint32_t) * std::max(grid, 1024), g->stream);
         A((void **)&kv->db.err, sizeof(int) * 4);
         kv->db.trace = nullptr;
-        kv->db.ck_rt = ck_config(m);
         kv->db.xk = XkConfig{};
         XkConfig xc;
         if (e == cudaSuccess && xk_config(m, &xc) > 0) {
             const size_t L = m.n_layers;
             const size_t words = L * (2 * (size_t)m.d + m.ff + (size_t)xc.nkc * m.d);
-            const size_t bytes = words * 8 + sizeof(uint32_t) * (2 * L + xc.grid);
+            const size_t bytes = words * 8 + sizeof(uint32_t) * (4 * L + xc.grid);
             A((void **)&kv->db.xkb.hacc, bytes);
             if (e == cudaSuccess) {
                 XkBufs &x = kv->db.xkb;
                 x.u_ll = reinterpret_cast<uint64_t *>(x.hacc + 2 * L * m.d);
                 x.mp_ll = x.u_ll + L * m.ff;
                 x.hcnt = reinterpret_cast<uint32_t *>(x.mp_ll + L * xc.nkc * m.d);
-                x.epoch = x.hcnt + 2 * L;
+                x.hflag = x.hcnt + 2 * L;
+                x.epoch = x.hflag + 2 * L;
                 e = cudaMemsetAsync(x.hacc, 0, bytes, g->stream);
                 kv->db.xk = xc;
             }
@@ -786,7 +786,6 @@ extern "C" int32_t itts_kv_max_seq(const itts_kv *kv) { return kv ? kv->max_seq 
 extern "C" int32_t itts_kv_max_batch(const itts_kv *kv) { return kv ? kv->max_batch : 0; }
 extern "C" int32_t itts_kv_decode_kernel(const itts_kv *kv, int32_t n_columns) {
     if (!kv || n_columns < 1 || n_columns > kv->max_batch) return 0;
-    if (n_columns == 1 && kv->db.ck_rt > 0) return 1;
     if (n_columns == 1 && kv->db.xk.grid > 0) return 4;
     if (n_columns <= MK_MAX_NB && kv->db.mk_grid > 0 && kv->db.mk_nslot[n_columns] >= 2) return 2;
     return 3;
@@ -1193,8 +1192,12 @@ static int reset_step_sync(itts_kv *kv) {
 }
 
 static int check_step_sync(itts_kv *kv) {
-    int err = 0;
-    CUDA_TRY(cudaMemcpy(&err, kv->db.err, sizeof(int), cudaMemcpyDeviceToHost));
+    int errw[2] = {0, 0};
+    CUDA_TRY(cudaMemcpy(errw, kv->db.err, sizeof(errw), cudaMemcpyDeviceToHost));
+    const int err = errw[0] ? errw[0] : errw[1];  // [0]: a bounded wait gave up; [1]: range
+    if (err == MK_ERR_RANGE)
+        return set_err(ITTS_E_CUDA, "device error: a c_proj partial of the decode step is finite but "
+                                    "outside the fixed-point accumulator's range (|y| >= 2^30)");
     if (err != 0)
         return set_err(ITTS_E_TIMEOUT, "device wait timed out in the decode-step kernel (code " +
                                            std::to_string(err) + ")");

@@ -251,13 +251,12 @@ static bool use_mk(const DecodeBufs &b, int nb) {
 }
 
 int decode_forward_launches(const ModelView &m, const DecodeBufs &b, int nb) {
-    if ((nb == 1 && (b.xk.grid > 0 || b.ck_rt > 0)) || use_mk(b, nb)) return 1;
+    if ((nb == 1 && b.xk.grid > 0) || use_mk(b, nb)) return 1;
     return 1 + 7 * m.n_layers + 3;
 }
 
 cudaError_t decode_forward(const ModelView &m, const DecodeView &dv, DecodeBufs &b,
                            cudaStream_t st) {
-    if (dv.nb == 1 && b.ck_rt > 0) return ck_launch(mk_params(m, dv, b), b.ck_rt, st);
     if (dv.nb == 1 && b.xk.grid > 0) return xk_launch(mk_params(m, dv, b), b.xk, b.xkb, st);
     if (use_mk(b, dv.nb)) return mk_launch(mk_params(m, dv, b), st);
     const int d = m.d;

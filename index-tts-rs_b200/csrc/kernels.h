@@ -35,6 +35,8 @@ struct XkBufs {  // one allocation: [2][L][d] c_proj accumulators, [L][ff] u, [L
     unsigned long long *hacc = nullptr;  // fixed-point (2^-32) sums of the heads' c_proj partials, by step parity
     uint64_t *u_ll = nullptr, *mp_ll = nullptr;
     uint32_t *hcnt = nullptr;   // [2][L] CTAs that added their c_proj partials
+    uint32_t *hflag = nullptr;  // [2][L] bit 0: a partial was not finite; bit 1: one was finite
+                                // but outside the fixed-point range (|y| >= 2^30)
     uint32_t *epoch = nullptr;
 };
 
@@ -52,7 +54,6 @@ struct DecodeBufs {
     int mk_grid, mk_nslot[MK_MAX_NB + 1];
     float *ws;      // split-K partial sums of the fp16 GEMM: [ws_splits][max_batch][max(3d, ff)]
     int ws_splits;
-    int ck_rt;      // > 0: batch-1 steps run on one 16-CTA cluster (ck_decode.cu)
     XkConfig xk;    // grid > 0: batch-1 steps run on the clustered all-SM kernel (xk_decode.cu)
     XkBufs xkb;
 };
@@ -108,10 +109,6 @@ void launch_gemm(int epi, const MkLin &W, const __half *x, void *y, int T, const
 // launch), else the GEMM path (embedding, 7 launches per layer, head).
 cudaError_t decode_forward(const ModelView &m, const DecodeView &dv, DecodeBufs &b,
                            cudaStream_t st);
-// Decode step of one batch column on one 16-CTA thread-block cluster (opt-in with
-// ITTS_CLUSTER=1 at cache creation): returns the partial-sum size it needs (> 0) or -1 when
-// it is not requested or the model or the device does not fit it.
-int ck_config(const ModelView &m);
 // Decode step of one column on one 6-CTA cluster per attention head (120 CTAs for 20 heads);
 // each stage's input is gathered once per cluster (default for batch 1; ITTS_XK=0 at cache
 // creation turns it off).
@@ -120,7 +117,6 @@ int xk_config(const ModelView &m, XkConfig *out);
 cudaError_t xk_launch(const MkParams &p, const XkConfig &xc, const XkBufs &b, cudaStream_t st);
 // The head-major copy of a c_proj (MkLayer::proj_h) from its tiles: n_heads * n_rb chunks.
 cudaError_t make_proj_by_head(const MkLin &W, int n_heads, uint8_t *dst, cudaStream_t st);
-cudaError_t ck_launch(const MkParams &p, int rt, cudaStream_t st);
 // Number of kernels decode_forward launches for nb columns.
 int decode_forward_launches(const ModelView &m, const DecodeBufs &b, int nb);
 

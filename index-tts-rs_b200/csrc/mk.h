@@ -69,6 +69,9 @@ struct MkParams {
     unsigned long long *trace;  // optional [grid][MK_TRACE_EVENTS] globaltimer stamps
 };
 constexpr int MK_TRACE_EVENTS = 256;
+// Error word value of a decode step whose fixed-point c_proj sum would overflow (any other
+// nonzero value names a bounded wait that gave up).
+constexpr int MK_ERR_RANGE = 1000;
 
 __host__ __device__ inline int frag_pos_host(int k) {
     const int b = k >> 4, kk = k & 15, c = (kk & 7) >> 1, hi = kk >> 3, lo = kk & 1;

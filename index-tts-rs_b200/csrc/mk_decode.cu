@@ -1046,6 +1046,14 @@ __global__ void __launch_bounds__(MK_THREADS, 1) mk_decode_kernel(const __grid_c
         if (p.trace) p.trace[(size_t)cta * MK_TRACE_EVENTS] = globaltimer();
     }
     __syncthreads();
+    // No column left generating (each stopped, sampler.rs:378, or failed): the step does
+    // nothing.  S is the same in every CTA, so the whole grid leaves before any copy,
+    // exchange or write; the launch counter stays, so no LL tag repeats.
+    {
+        int any = 0;
+        for (int n = 0; n < MK_MAX_NB; ++n) any |= S.active[n];
+        if (!any) return;
+    }
 
     if (warp == MK_CWARPS) {
         if (lane != 0) return;

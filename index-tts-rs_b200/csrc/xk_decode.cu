@@ -58,6 +58,7 @@ constexpr int REC = 68;            // floats per attention record: m, l, 0, 0, a
 constexpr int QT = 12;             // QKV row blocks of one head (q, k, v x 64 rows / 16)
 constexpr int NWS = 5;             // LL-writing stages per layer: qkv, records, c_proj, u, mlp
 constexpr uint32_t SPIN = 1u << 22;
+constexpr int kXkRangeCode = MK_ERR_RANGE;  // error word: a c_proj partial outside the fixed-point range
 constexpr float kLog2e = 1.4426950408889634f;
 
 // landing barriers: x/h (fp32), the head's attention output (fp16 + its sum), u (fp16), the
@@ -100,7 +101,7 @@ __device__ __forceinline__ bool mb_wait(uint64_t *b, uint32_t par, const int *er
     const uint32_t a = su32(b);
     for (uint32_t it = 0; it < SPIN; ++it) {
         if (mb_try<CLUSTER>(a, par)) return true;
-        if ((it & 4095u) == 4095u && *(volatile const int *)err) return false;
+        if (err && (it & 4095u) == 4095u && *(volatile const int *)err) return false;
     }
     return false;
 }
@@ -265,6 +266,8 @@ struct XkParams {
     unsigned long long *hacc;  // [2][L][d] sums of the heads' c_proj partials, fixed point 2^-32,
                                // by step parity (this step's buffer p = epoch & 1; 1 - p zeroed)
     uint32_t *hcnt;            // [2][L] CTAs that added their partials
+    uint32_t *hflag;           // [2][L] partials left out of the sum: bit 0 not finite, bit 1
+                               // finite but |y| >= 2^30 (the sum of 20 heads could wrap)
     uint64_t *u_ll;      // [L][ff]    GELU(c_fc)
     uint64_t *mp_ll;     // [L][nkc][d] mlp c_proj K-chunk partial sums
     uint32_t *epoch;     // [grid] launches completed per CTA
@@ -289,14 +292,18 @@ struct XkProducer {
     int R, NR;
     bool ok;
 
+    // seq counts the copies actually issued, so the drain below waits for exactly those
     __device__ __forceinline__ void issue(const void *s0, uint32_t b0, const void *s1, uint32_t b1) {
+        if (!ok) return;
         const uint32_t slot = seq & (NSLOT - 1);
-        if (seq >= (uint32_t)NSLOT && ok) {
+        if (seq >= (uint32_t)NSLOT) {
             ok = mb_wait<false>(emptyp + slot, ((seq / NSLOT) & 1u) ^ 1u, err);
-            if (!ok) atomicExch(const_cast<int *>(err), 1);
+            if (!ok) {
+                atomicExch(const_cast<int *>(err), 1);
+                return;
+            }
         }
         ++seq;
-        if (!ok) return;
         const uint32_t bar = full + slot * 8;
         mb_expect(fullp + slot, b0 + b1);
         const uint32_t dst = ring + slot * SLOT;
@@ -338,9 +345,12 @@ struct XkProducer {
             lin(&Ly->mlp);
         }
         if (ok) lin(&p.head);
-        for (uint32_t s = 0; s < NSLOT && s < seq; ++s) {  // every copy lands before exit
+        // every issued copy lands before exit (the last one of each slot; the earlier ones
+        // were consumed before the slot was reused).  Copies always complete, so this wait
+        // ignores the error word and is bounded by SPIN only.
+        for (uint32_t s = 0; s < NSLOT && s < seq; ++s) {
             const uint32_t last = ((seq - 1 - s) / NSLOT) * NSLOT + s;
-            mb_wait<false>(fullp + s, (last / NSLOT) & 1u, err);
+            mb_wait<false>(fullp + s, (last / NSLOT) & 1u, nullptr);
         }
     }
 };
@@ -668,7 +678,7 @@ struct XkConsumer {
         const uint32_t *cnt = xp->hcnt + par * pp->n_layers + l;
         const unsigned long long *acc = xp->hacc + ((size_t)par * pp->n_layers + l) * d;
         bool good = true;
-        if (tid < nch && ok) {
+        if (tid == 0 && ok) {  // one poller per CTA; the barrier in agree() orders the rest
             good = false;
             for (uint32_t it = 0; it < SPIN; ++it) {
                 uint32_t v;
@@ -679,6 +689,11 @@ struct XkConsumer {
             }
         }
         agree(good, code);
+        uint32_t flag;
+        asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(flag) : "l"(xp->hflag + par * pp->n_layers + l) : "memory");
+        // reported in its own error word: the step itself runs to the end on the normal path
+        if ((flag & 2u) && tid == 0) atomicExch(pp->err + 1, kXkRangeCode);
+        const float fnan = flag ? __int_as_float(0x7fc00000) : 0.f;
         const uint32_t land_a = su32(land), bar_a = su32(stb + B0);
         for (int i = tid; i < nch; i += CT) {
             const int o = o0 + i * 4;
@@ -689,8 +704,8 @@ struct XkConsumer {
             const float sc = 2.3283064365386963e-10f;  // 2^-32
             const float4 v = make_float4((float)(long long)q0 * sc, (float)(long long)q1 * sc,
                                          (float)(long long)q2 * sc, (float)(long long)q3 * sc);
-            bcast_v4(land_a + o * 4, make_uint4(__float_as_uint(x.x + bpre.x + v.x), __float_as_uint(x.y + bpre.y + v.y),
-                                                __float_as_uint(x.z + bpre.z + v.z), __float_as_uint(x.w + bpre.w + v.w)),
+            bcast_v4(land_a + o * 4, make_uint4(__float_as_uint(x.x + bpre.x + v.x + fnan), __float_as_uint(x.y + bpre.y + v.y + fnan),
+                                                __float_as_uint(x.z + bpre.z + v.z + fnan), __float_as_uint(x.w + bpre.w + v.w + fnan)),
                      bar_a);
         }
         trace();
@@ -986,8 +1001,16 @@ struct XkConsumer {
                 const float y1 = fmaf(s1, d0[2] + d1[2], fmaf(-1024.0f, s1, z1) * hsum);
                 if (c == 0) {
                     const int o = (r0 + i) * 16;
-                    atomicAdd(acc + o + g, (unsigned long long)__float2ll_rn(y0 * 4294967296.0f));
-                    atomicAdd(acc + o + g + 8, (unsigned long long)__float2ll_rn(y1 * 4294967296.0f));
+                    // |y| < 2^30 keeps the sum of the 20 heads' partials inside int64 at 2^-32
+                    // units; a NaN, an infinity or a larger value is flagged instead of added
+                    // (the h gather then yields NaN, as the reference's fp32 sum would for a
+                    // non-finite partial, and reports the out-of-range case as an error)
+                    const bool f0 = fabsf(y0) < 1073741824.0f, f1 = fabsf(y1) < 1073741824.0f;
+                    if (f0) atomicAdd(acc + o + g, (unsigned long long)__float2ll_rn(y0 * 4294967296.0f));
+                    if (f1) atomicAdd(acc + o + g + 8, (unsigned long long)__float2ll_rn(y1 * 4294967296.0f));
+                    if (!(f0 && f1))
+                        atomicOr(xp->hflag + par * pp->n_layers + l,
+                                 (f0 || isfinite(y0)) && (f1 || isfinite(y1)) ? 2u : 1u);
                 }
             }
             __syncwarp();
@@ -1076,6 +1099,10 @@ __global__ void __launch_bounds__(NT, 1) xk_decode_kernel(const __grid_constant_
     const int lold = active ? st.valid_len : 0;
     const int kvt = active ? max(1, (lold + KVPOS - 1) / KVPOS) : 0;
     const int head = R / CS;
+    // A step of a request that has stopped (sampler.rs:378) or failed does nothing: every
+    // CTA reads the same slot state, so all of them leave here, before any barrier, copy or
+    // write (the launch counter and the accumulators stay as the last real step left them).
+    if (!active) return;
     {
         const int words = (int)(p.n_layers * sizeof(MkLayer) / 4);
         const uint32_t *src = reinterpret_cast<const uint32_t *>(p.layers);
@@ -1113,7 +1140,10 @@ __global__ void __launch_bounds__(NT, 1) xk_decode_kernel(const __grid_constant_
         const size_t n = (size_t)p.n_layers * p.d;
         unsigned long long *a = xp.hacc + q * n;
         for (size_t i = (size_t)R * NT + tid; i < n; i += (size_t)NR * NT) a[i] = 0ull;
-        if (R == 0 && tid < p.n_layers) xp.hcnt[q * p.n_layers + tid] = 0u;
+        if (R == 0 && tid < p.n_layers) {
+            xp.hcnt[q * p.n_layers + tid] = 0u;
+            xp.hflag[q * p.n_layers + tid] = 0u;
+        }
     }
     // every CTA's barriers are armed before any CTA pushes into them
     cluster_sync_all();
@@ -1308,6 +1338,7 @@ cudaError_t xk_launch(const MkParams &p, const XkConfig &xc, const XkBufs &b, cu
     xp.p = p;
     xp.hacc = b.hacc;
     xp.hcnt = b.hcnt;
+    xp.hflag = b.hflag;
     xp.u_ll = b.u_ll;
     xp.mp_ll = b.mp_ll;
     xp.epoch = b.epoch;

@@ -323,7 +323,7 @@ class KvCache:
     def decode_kernel(self, n_columns: int = 1) -> str:
         """Name of the decode-step kernel a step of `n_columns` columns runs."""
         k = int(load_lib().itts_kv_decode_kernel(self._h, int(n_columns)))
-        return {1: "ck_decode_kernel", 2: "mk_decode_kernel", 3: "gemm path",
+        return {2: "mk_decode_kernel", 3: "gemm path",
                 4: "xk_decode_kernel"}.get(k, "none")
 
     def close(self) -> None:

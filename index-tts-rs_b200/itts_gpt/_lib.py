@@ -88,7 +88,7 @@ SIGNATURES = [
 ]
 
 _lib = None
-_synth = None
+_synth: dict = {}
 
 
 def load_lib() -> C.CDLL:
@@ -107,12 +107,14 @@ def load_lib() -> C.CDLL:
     return _lib
 
 
-def load_synth() -> C.CDLL:
+def load_synth(path=None) -> C.CDLL:
+    """The seeded input generator; `path` picks another build of the same source."""
     global _synth
-    if _synth is None:
-        if not SYNTH_PATH.exists():
-            raise RuntimeError(f"{SYNTH_PATH} is missing: run index-tts-rs_b200/build.py")
-        s = C.CDLL(str(SYNTH_PATH))
+    key = str(path or SYNTH_PATH)
+    if key not in _synth:
+        if not Path(key).exists():
+            raise RuntimeError(f"{key} is missing: run index-tts-rs_b200/build.py")
+        s = C.CDLL(key)
         s.itts_synth_tag.restype = C.c_uint64
         s.itts_synth_tag.argtypes = [C.c_char_p]
         for fn in (s.itts_synth_normal_f32, s.itts_synth_normal_f16_as_f32):
@@ -121,8 +123,8 @@ def load_synth() -> C.CDLL:
         s.itts_synth_quant_linear.restype = C.c_int
         s.itts_synth_quant_linear.argtypes = [C.c_uint64, C.c_uint64, C.c_int, C.c_int, C.c_float,
                                               C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]
-        _synth = s
-    return _synth
+        _synth[key] = s
+    return _synth[key]
 
 
 def last_error() -> str:

@@ -74,9 +74,11 @@ def linear_specs(cfg: ModelConfig):
 
 
 def make_weights(cfg: ModelConfig, seed: int = 1234, w_std: float = 0.02,
-                 ln_beta_std: float = 0.0, bias_std: float = 0.02) -> dict[str, np.ndarray]:
-    """All decoder tensors by reference name."""
-    lib = load_synth()
+                 ln_beta_std: float = 0.0, bias_std: float = 0.02,
+                 synth_path=None) -> dict[str, np.ndarray]:
+    """All decoder tensors by reference name (`synth_path`: another build of the
+    generator library, same values)."""
+    lib = load_synth(synth_path)
     t: dict[str, np.ndarray] = {}
 
     def normal(name, shape, mean, std):
@@ -118,9 +120,9 @@ def make_weights(cfg: ModelConfig, seed: int = 1234, w_std: float = 0.02,
     return t
 
 
-def make_conds(d: int, n_conds: int, seed: int) -> np.ndarray:
+def make_conds(d: int, n_conds: int, seed: int, synth_path=None) -> np.ndarray:
     """``[n_conds, d]`` f32 conditioning latents drawn N(0,1) and rounded through fp16."""
-    lib = load_synth()
+    lib = load_synth(synth_path)
     a = np.empty((n_conds, d), np.float32)
     lib.itts_synth_normal_f16_as_f32(seed, lib.itts_synth_tag(b"conds"), a.ctypes.data, a.size,
                                      0.0, 1.0)

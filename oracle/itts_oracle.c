@@ -363,6 +363,26 @@ void orc_kv_free(orc_kv *kv) { if (kv) { free(kv->k); free(kv->v); free(kv); } }
 void orc_kv_reset(orc_kv *kv) { kv->valid_len = 0; }
 int orc_kv_valid_len(const orc_kv *kv) { return kv->valid_len; }
 
+static inline float *kv_ptr(float *base, const orc_kv *kv, int layer, int head, int pos);
+
+/* Timing aid for the CPU baseline (no reference counterpart): extends every layer's
+ * cache from valid_len to n positions by repeating the filled positions cyclically, so a
+ * following orc_step costs what a step at KV length n costs (the work of a step depends
+ * only on the length).  Needs valid_len >= 1 and n <= max_seq. */
+int orc_kv_fill(orc_kv *kv, int n) {
+    if (kv->valid_len < 1 || n > kv->max_seq || n < kv->valid_len)
+        return fail(ORC_E_VALIDATION, "kv_fill: need 1 <= valid_len <= n <= max_seq");
+    const int v0 = kv->valid_len;
+    for (int l = 0; l < kv->n_layers; ++l)
+        for (int h = 0; h < kv->n_heads; ++h)
+            for (int p = v0; p < n; ++p) {
+                memcpy(kv_ptr(kv->k, kv, l, h, p), kv_ptr(kv->k, kv, l, h, p % v0), HEAD_DIM * sizeof(float));
+                memcpy(kv_ptr(kv->v, kv, l, h, p), kv_ptr(kv->v, kv, l, h, p % v0), HEAD_DIM * sizeof(float));
+            }
+    kv->valid_len = n;
+    return ORC_OK;
+}
+
 static inline float *kv_ptr(float *base, const orc_kv *kv, int layer, int head, int pos) {
     return base + (((size_t)layer * kv->n_heads + head) * kv->max_seq + pos) * HEAD_DIM;
 }

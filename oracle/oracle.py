@@ -14,6 +14,7 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 LIB = HERE / "libitts_oracle.so"
+SYNTH_LIB = HERE / "libitts_oracle_synth.so"
 BITSET_WORDS = 129
 STOP_MEL = 8193
 
@@ -66,6 +67,7 @@ def lib() -> C.CDLL:
         L.orc_kv_free.argtypes = [P]
         L.orc_kv_reset.argtypes = [P]
         L.orc_kv_valid_len.argtypes = [P]
+        L.orc_kv_fill.argtypes = [P, I]
         L.orc_prefill.argtypes = [P, P, P, I, P, I, I, P, I, P]
         L.orc_replay.argtypes = [P, P, P, I, P, I, I, P, I, I, I, P, I, P, P]
         L.orc_step.argtypes = [P, P, I, I, P]
@@ -74,6 +76,14 @@ def lib() -> C.CDLL:
         L.orc_set_num_threads.argtypes = [I]
         _lib = L
     return _lib
+
+
+def synth_lib_path() -> Path:
+    """The seeded input generator built by this directory's Makefile (the same source as
+    the package's generator, so both benchmark arms see identical weights and prompts)."""
+    if not SYNTH_LIB.exists():
+        build()
+    return SYNTH_LIB
 
 
 def error() -> str:
@@ -211,6 +221,11 @@ class OracleKv:
 
     def valid_len(self) -> int:
         return lib().orc_kv_valid_len(self.h)
+
+    def fill(self, n: int) -> None:
+        """Timing aid: extends the cache to n positions (cyclic copies of the filled ones),
+        so the next step costs what a step at KV length n costs."""
+        _check(lib().orc_kv_fill(self.h, int(n)))
 
     def __del__(self):
         try:

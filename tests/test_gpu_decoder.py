@@ -59,10 +59,9 @@ def _teacher_forced(gpt, om, cfg, n_text, n_conds, steps, seed, max_seq=1024):
     return np.stack(g), np.stack(r)
 
 
-# batch-1 decode kernels: the default clustered all-SM kernel, the persistent grid-wide
-# kernel (ITTS_XK=0), the single-cluster kernel (ITTS_CLUSTER=1)
-KERNELS = {"xk": ({}, "xk_decode_kernel"), "grid": ({"ITTS_XK": "0"}, "mk_decode_kernel"),
-           "cluster": ({"ITTS_CLUSTER": "1"}, "ck_decode_kernel")}
+# batch-1 decode kernels: the default clustered all-SM kernel and the persistent grid-wide
+# kernel (ITTS_XK=0)
+KERNELS = {"xk": ({}, "xk_decode_kernel"), "grid": ({"ITTS_XK": "0"}, "mk_decode_kernel")}
 
 
 def _use_kernel(monkeypatch, gpt, name):
@@ -383,3 +382,97 @@ def test_full_size_greedy_generate(full):
     ref, _ = om.generate(om.kv(512), text, conds, 1, orc.params_c(greedy=True, max_mel_tokens=32), 0)
     n = min(len(codes), len(ref))
     assert n > 0 and np.mean(np.array(codes[:n]) == np.array(ref[:n])) >= 0.99
+
+
+# ---------------------------------------------------------------------------
+# non-finite and out-of-range values in the batch-1 cluster kernel's c_proj, whose
+# per-head partials are summed as 64-bit fixed-point integers
+# ---------------------------------------------------------------------------
+def test_nonfinite_cproj_partial_propagates(small_weights, small_cfg):
+    """A NaN scale in one c_proj row makes that row's partial NaN.  The reference's fp32 sum
+    carries it into h, and the LayerNorm after it spreads it to every logit; the device
+    step must give all-NaN logits too, not a finite value from a wrapped integer sum."""
+    w = dict(small_weights)
+    sc = w["gpt.h.1.attn.c_proj.scales"].copy()
+    sc[5, 2] = np.float16(np.nan)
+    w["gpt.h.1.attn.c_proj.scales"] = sc
+    gpt = ig.Gpt.from_weights(w, device=0)
+    try:
+        om = orc.OracleModel(w)
+        kv = ig.KvCache(gpt, max_seq=128)
+        assert kv.decode_kernel(1) == "xk_decode_kernel"
+        text = make_text(11, small_cfg.text_vocab, seed=4)
+        conds = make_conds(small_cfg.d, 3, seed=5)
+        okv = om.kv(128)
+        gpt.prefill(text, conds, 1, kv)
+        om.prefill(okv, text, conds, 1)
+        got = gpt.step(kv, 77, 2)
+        ref = om.step(okv, 77, 2)
+        assert np.isnan(ref).all()
+        assert np.isnan(got).all(), int(np.isfinite(got).sum())
+    finally:
+        gpt.close()
+
+
+def test_cproj_partial_out_of_fixed_point_range_is_an_error():
+    """A finite c_proj partial of 2^30 or more cannot be summed exactly in the 2^-32 fixed
+    point: the step reports a device error instead of a wrapped value, and the next steps
+    on a sound model in the same process are correct."""
+    cfg32 = ModelConfig(n_layers=2, d=256, ff=1024, text_vocab=500, sb_half=False)
+    w = make_weights(cfg32, seed=3, ln_beta_std=0.02)
+    w["gpt.h.0.attn.c_proj.scales"] = w["gpt.h.0.attn.c_proj.scales"].copy()
+    w["gpt.h.0.attn.c_proj.scales"][3, 1] = 1e12
+    text = make_text(9, cfg32.text_vocab, seed=1)
+    conds = make_conds(cfg32.d, 3, seed=2)
+    bad = ig.Gpt.from_weights(w, device=0)
+    try:
+        kv = ig.KvCache(bad, max_seq=64)
+        assert kv.decode_kernel(1) == "xk_decode_kernel"
+        bad.prefill(text, conds, 1, kv)
+        with pytest.raises(ig.DeviceError, match="fixed-point"):
+            bad.step(kv, 5, 2)
+    finally:
+        bad.close()
+    good_w = make_weights(cfg32, seed=3, ln_beta_std=0.02)
+    good = ig.Gpt.from_weights(good_w, device=0)
+    try:
+        om = orc.OracleModel(good_w)
+        kv, okv = ig.KvCache(good, max_seq=64), om.kv(64)
+        check_logits(good.prefill(text, conds, 1, kv), om.prefill(okv, text, conds, 1), "prefill after the error")
+        for i in range(3):
+            check_logits(good.step(kv, 5 + i, 2 + i), om.step(okv, 5 + i, 2 + i), f"step {i} after the error")
+    finally:
+        good.close()
+
+
+def test_generate_stops_early_and_skips_idle_steps(small_weights, small_cfg):
+    """A request that stops at STOP (sampler.rs:378) leaves the rest of the replayed
+    decode-step chunk idle: the batch-1 kernel returns at once for a slot that is no longer
+    generating, so the decode time of a run that stops after 3 codes is far below that of
+    a run of all its steps, and the codes match the checker."""
+    w = dict(small_weights)
+    w["mel_head.bias"] = w["mel_head.bias"].copy()
+    w["mel_head.bias"][8193] = 40.0  # STOP wins every draw once it is no longer masked
+    gpt = ig.Gpt.from_weights(w, device=0)
+    try:
+        om = orc.OracleModel(w)
+        text = make_text(20, small_cfg.text_vocab, seed=6)
+        conds = make_conds(small_cfg.d, 3, seed=7)
+        kv = ig.KvCache(gpt, max_seq=512)
+        assert kv.decode_kernel(1) == "xk_decode_kernel"
+        p = ig.SamplingParams(greedy=True, max_mel_tokens=300)
+        full = ig.generate_codes_after(gpt, ig.CodePrompt(text, conds, 1, min_codes=300), kv, p, ig.SamplerRng(0))
+        assert len(full) == 300
+        _, t_full, n_full = gpt.last_timing()
+        early = ig.generate_codes_after(gpt, ig.CodePrompt(text, conds, 1, min_codes=3), kv, p, ig.SamplerRng(0))
+        _, t_early, n_early = gpt.last_timing()
+        ref, _ = om.generate(om.kv(512), text, conds, 1, orc.params_c(greedy=True, max_mel_tokens=300), 0,
+                             min_codes=3)
+        assert early == ref and len(early) == 3, (early, ref)
+        # the first chunk replays 8 steps; all but 2 of them find the slot stopped
+        assert n_early >= 8
+        per_step_full = t_full / n_full
+        assert t_early < 6 * per_step_full, (t_early, per_step_full)
+        print(f"early stop: {n_early} replays in {t_early:.3f} ms; full run {per_step_full:.4f} ms per step")
+    finally:
+        gpt.close()

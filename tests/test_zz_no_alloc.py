@@ -6,6 +6,7 @@ shares, so the checks run two calls in a row with different slice lengths and
 parameters: the second call must not see anything the first left behind.  The sampler
 is bit-exact, so token, RNG state and penalized logits must be identical."""
 import ctypes as C
+import gc
 
 import numpy as np
 import pytest
@@ -18,16 +19,32 @@ pytestmark = pytest.mark.gpu
 MAX_LOGITS = 16384
 
 
-def _static_sample(logits, seen, params, state):
-    """Calls the C entry point directly (host buffers, default stream)."""
+def _static_sample(logits, seen, params, state, stream=None):
+    """Calls the C entry point directly (host buffers; the default stream unless given)."""
     lib = _lib.load_lib()
     p = params.to_c()
     st = C.c_uint64(state)
     tok = C.c_int32(-7)
     words = np.ascontiguousarray(seen.words, np.uint64)
     rc = lib.itts_sample_next_token_static(logits.ctypes.data, int(logits.size), words.ctypes.data,
-                                           C.byref(p), C.byref(st), C.byref(tok), None)
+                                           C.byref(p), C.byref(st), C.byref(tok), stream)
     return rc, tok.value, st.value
+
+
+def _cudart():
+    """The CUDA runtime the library itself loaded (same soname), for memory queries and
+    a stream of our own."""
+    rt = C.CDLL("libcudart.so.12")
+    rt.cudaMemGetInfo.argtypes = [C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]
+    rt.cudaStreamCreate.argtypes = [C.POINTER(C.c_void_p)]
+    rt.cudaStreamDestroy.argtypes = [C.c_void_p]
+    return rt
+
+
+def _free_bytes(rt):
+    free, total = C.c_size_t(), C.c_size_t()
+    assert rt.cudaMemGetInfo(C.byref(free), C.byref(total)) == 0
+    return free.value
 
 
 def _case(seed, n, params):
@@ -40,10 +57,15 @@ def _case(seed, n, params):
     return x, seen, params, int(rng.integers(0, 2**63))
 
 
+# The first three select the top-k <= 64 kernel; the last three the full-sort kernel (top_k 0,
+# i.e. every logit a candidate, or top_k above 64).
 CASES = [
     (31, MAX_LOGITS, ig.SamplingParams(top_k=50, top_p=0.9, temperature=0.7, repetition_penalty=1.3)),
     (32, 8194, ig.SamplingParams()),
     (33, 8194, ig.SamplingParams(greedy=True, repetition_penalty=10.0)),
+    (34, 8194, ig.SamplingParams(top_k=0, top_p=0.9, temperature=0.8)),
+    (35, MAX_LOGITS, ig.SamplingParams(top_k=500, top_p=0.95, temperature=1.1, repetition_penalty=2.0)),
+    (36, MAX_LOGITS, ig.SamplingParams(top_k=0, top_p=1.0, temperature=0.5)),
 ]
 
 
@@ -91,3 +113,35 @@ def test_static_sampler_rejects_oversize_slices():
     x, seen, p, state = _case(41, 1000, ig.SamplingParams(top_k=0, top_p=1.0))
     rc, tok, st = _static_sample(x.copy(), seen, p, state)
     assert rc == 0 and 0 <= tok < 1000
+
+
+def test_static_sampler_allocates_nothing_and_takes_a_stream():
+    """After the first call (which sets the device up), further calls leave the device's
+    free memory unchanged, and a call on a stream the caller created gives the same
+    result as one on the default stream."""
+    rt = _cudart()
+    x, seen, p, state = _case(50, 8194, ig.SamplingParams(top_k=30, top_p=0.8))
+    rc, tok0, st0 = _static_sample(x.copy(), seen, p, state)
+    assert rc == 0, _lib.last_error()
+    stream = C.c_void_p()
+    assert rt.cudaStreamCreate(C.byref(stream)) == 0
+    try:
+        # one pass first: the CUDA runtime loads each kernel's code on its first launch
+        # (lazy module loading), which takes device memory that is not the sampler's
+        for seed, n, params in CASES:
+            _static_sample(*_case(seed, n, params))
+        _static_sample(x.copy(), seen, p, state, stream)
+        gc.collect()  # handles of earlier tests freed now, not during the measurement
+        before = _free_bytes(rt)
+        for seed, n, params in CASES:
+            xc, sc, pc, stc = _case(seed, n, params)
+            assert _static_sample(xc, sc, pc, stc)[0] == 0, _lib.last_error()
+        assert _free_bytes(rt) == before
+        for _ in range(2):
+            xs = x.copy()
+            rc, tok, st = _static_sample(xs, seen, p, state, stream)
+            assert rc == 0, _lib.last_error()
+            assert (tok, st) == (tok0, st0)
+        assert _free_bytes(rt) == before
+    finally:
+        rt.cudaStreamDestroy(stream)
