@@ -293,6 +293,10 @@ def run_ours(args, rank, world, local_rank):
     times = max_over_ranks([dev_ms / 1000.0, wall], world)
     dev_s, wall_s = float(times[0]), float(times[1])
     tokens = N_MEL * args.steps * world
+    cfg5 = None
+    if not args.no_extra:
+        kv.close()
+        cfg5 = bench_cfg5(cfg, w, rank, world, local_rank)
     if rank != 0:
         return
     # kernels of ours per generate: prefill (embed + 7 per layer + 2 LN + head GEMM),
@@ -335,16 +339,145 @@ def run_ours(args, rank, world, local_rank):
                      "traffic": 692219904 if kname == "xk_decode_kernel" else None},
         "clocks": clk,
     }
-    try:
-        line["prefill_cfg4"] = bench_prefill_cfg4(cfg, gpt, peaks)
-    except Exception as e:  # never blocks the headline line
-        line["prefill_cfg4"] = {"error": str(e)[:200]}
+    if cfg5 is not None:
+        line["cfg5"] = cfg5
+    if world == 1 and not args.no_extra:
+        for key, fn in (("cfg1", lambda: bench_cfg1(cfg, gpt, w)),
+                        ("prefill_cfg4", lambda: bench_prefill_cfg4(cfg, gpt, peaks)),
+                        ("cfg3", lambda: bench_cfg3(cfg, gpt, peaks))):
+            try:
+                line[key] = fn()
+            except Exception as e:  # never blocks the headline line
+                line[key] = {"error": str(e)[:300]}
     if not args.no_cpu_baseline:
         try:
             line["cpu_baseline"] = cpu_baseline(cfg, w, text, conds, os.cpu_count() or 1)
         except Exception as e:  # the baseline never blocks the GPU line
             line["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
     print(json.dumps(line), flush=True)
+
+
+def bench_cfg1(cfg, gpt, w) -> dict:
+    """batch 1, 32 conditioning latents + 64 text tokens (99 positions), 256
+    greedy steps (repetition penalty 10); device time of prefill + decode."""
+    import itts_gpt as ig
+    from itts_gpt.synth import make_conds, make_text
+    text = make_text(64, cfg.text_vocab, seed=11)
+    conds = make_conds(cfg.d, N_CONDS, seed=12)
+    kv = ig.KvCache(gpt, max_seq=N_CONDS + 64 + 3 + 256 + 8)
+    p = ig.SamplingParams(greedy=True, max_mel_tokens=256)
+    runs = []
+    for i in range(4):
+        codes = ig.generate_codes_after(gpt, ig.CodePrompt(text, conds, LANG, min_codes=256), kv, p,
+                                        ig.SamplerRng(i))
+        assert len(codes) == 256
+        runs.append(gpt.last_timing())
+    kv.close()
+    pf, dc, nl = [statistics.median(x) for x in zip(*runs[1:])]
+    return {"workload": "cfg1: batch 1, 32 conds + 64 text tokens, 256 greedy mel tokens (rep 10)",
+            "ms_per_mel_token": (pf + dc) / 256, "decode_ms_per_step": dc / 255, "prefill_ms": pf,
+            "mel_tokens_per_s": 256 / ((pf + dc) * 1e-3)}
+
+
+def bench_cfg3(cfg, gpt, peaks, n_req=64, n_mel=600) -> dict:
+    """64 requests (32 conds + text uniform in [16, 600]) in one batched
+    generate of 600 sampled steps each (STOP masked, so every request runs all of them).
+    Roofline: per decode step the int8 weights once plus the fp16 K/V of every live
+    request, over the mean step time."""
+    import itts_gpt as ig
+    from itts_gpt.synth import make_conds, make_text
+    lens = np.random.default_rng(3).integers(16, 601, n_req)
+    prompts = [ig.CodePrompt(make_text(int(n), cfg.text_vocab, seed=900 + r),
+                             make_conds(cfg.d, N_CONDS, seed=950 + r), LANG, min_codes=n_mel)
+               for r, n in enumerate(lens)]
+    params = ig.SamplingParams(max_mel_tokens=n_mel, **SAMPLING)
+    kv = ig.KvCache(gpt, max_seq=int(lens.max()) + N_CONDS + 3 + n_mel + 8, max_batch=n_req)
+    runs = []
+    for i in range(3):
+        out = ig.generate_batch(gpt, prompts, kv, params, [ig.SamplerRng(i * 100 + r) for r in range(n_req)])
+        assert all(len(c) == n_mel for c in out)
+        runs.append(gpt.last_timing())
+    kv.close()
+    pf, dc, nl = [statistics.median(x) for x in zip(*runs[1:])]
+    T0 = lens + N_CONDS + 3
+    steps = n_mel - 1
+    kv_bytes = sum(kv_bytes_per_step(cfg, int(t) + s + 1) for t in T0 for s in range(0, steps, 50)) * 50 / steps
+    step_bytes = cfg.weight_bytes() + kv_bytes
+    ms_step = dc / steps
+    achieved = step_bytes / (ms_step * 1e-3) / 1e9
+    peak = float(peaks.get("hbm_gbs", 6650.0))
+    return {"workload": f"cfg3: {n_req} requests, text U[16,600], {n_mel} sampled steps each (T 0.8, top-k 30, "
+                        "top-p 0.8, rep 10), one batched generate",
+            "mel_tokens_per_s": n_req * n_mel / ((pf + dc) * 1e-3), "prefill_ms": pf,
+            "decode_ms_per_step": ms_step,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak,
+                         "algorithmic_bytes_per_step": step_bytes,
+                         "bytes_formula": "514,144,936 int8 weight B + 122,880 B x KV positions of the 64 "
+                                          "live requests (mean over the steps)"}}
+
+
+def cfg5_requests(cfg, synth_path=None, n=1024, seed=5):
+    """configs[4]'s queue: text lengths log-normal with median 80 (sigma 0.6, the spread the
+    config leaves open), clipped to [8, 600]; mel length 3.5 x text clipped to 1800 (STOP
+    masked until then, so every sentence yields exactly that many codes); cfg2's sampling."""
+    import itts_gpt as ig
+    from itts_gpt.serve import Request
+    from itts_gpt.synth import make_conds, make_text
+    rng = np.random.default_rng(seed)
+    lens = np.clip(np.round(np.exp(np.log(80.0) + 0.6 * rng.standard_normal(n))), 8, 600).astype(int)
+    reqs = []
+    for i, L in enumerate(lens):
+        mel = int(min(round(3.5 * L), 1800))
+        prompt = ig.CodePrompt(make_text(int(L), cfg.text_vocab, seed=20000 + i),
+                               make_conds(cfg.d, N_CONDS, seed=30000 + i, synth_path=synth_path), LANG,
+                               min_codes=mel)
+        reqs.append(Request(i, prompt, ig.SamplingParams(max_mel_tokens=mel, **SAMPLING), seed=40000 + i))
+    return reqs
+
+
+def bench_cfg5(cfg, w, rank, world, local_rank, max_batch=64, chunk=8) -> dict:
+    """the 1,024-sentence queue served by one worker per GPU with continuous
+    batching (itts_gpt.serve; up to 64 live requests per GPU), the queue shared by all ranks
+    through the torch.distributed store.  Wall clock around the whole queue (synchronized
+    on both sides; max over ranks), tokens summed over ranks."""
+    import torch
+    from itts_gpt.serve import Dispatcher, RequestQueue, StoreQueue, gpu_engine_factory
+    reqs = cfg5_requests(cfg)
+    max_seq = N_CONDS + 600 + 3 + 1800 + 8
+    make = gpu_engine_factory(w, local_rank, max_batch=max_batch, max_seq=max_seq, chunk=chunk)
+    # warm-up on this rank's own short queue: graphs, fp16 weight copies, allocations; the
+    # worker keeps its engine (model replica and cache) for the timed queue
+    d = Dispatcher([make], keep_engines=True)
+    warm = d.run(RequestQueue(sorted(reqs, key=lambda r: r.prompt.min_codes)[:2 * max_batch]))
+    assert all(r.error is None for r in warm.values()), d.workers[0].error
+    if world > 1:
+        import torch.distributed as dist
+        store = dist.distributed_c10d._get_default_store()
+        dist.barrier()
+        queue = StoreQueue(store, "bench/cfg5/next", reqs)
+    else:
+        queue = RequestQueue(reqs)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    res = d.run(queue)
+    torch.cuda.synchronize()
+    secs = time.perf_counter() - t0
+    d.close()
+    sums = [sum(len(r.codes) for r in res.values()), len(res), sum(1 for r in res.values() if r.error)]
+    secs_max = float(max_over_ranks([secs], world)[0])
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor(sums, dtype=torch.float64)
+        dist.all_reduce(t)
+        sums = [int(x) for x in t.tolist()]
+    return {"workload": "cfg5: 1,024 sentences, text log-normal (median 80, sigma 0.6, [8, 600]), mel = "
+                        "min(3.5 x text, 1800), cfg2 sampling; continuous batching, <= 64 live requests per "
+                        "GPU, one shared queue",
+            "mel_tokens_per_s": sums[0] / secs_max, "unit": "mel tokens/s (aggregate over GPUs)",
+            "seconds": secs_max, "mel_tokens": sums[0], "sentences": sums[1], "errors": sums[2],
+            "n_gpus": world, "timing": "wall clock around the queue, synchronized, max over ranks",
+            "scaling": "strong (fixed 1,024-sentence queue)"}
 
 
 def prefill_flops(cfg, lens) -> float:
@@ -372,8 +505,18 @@ def bench_prefill_cfg4(cfg, gpt, peaks, n_req=32, reps=3) -> dict:
         ig.prefill_batch(gpt, prompts, kv)
         if i >= 2:
             ms.append(gpt.last_timing()[0])
+    # then configs[3]'s 32 decode steps of the 32 requests (a batched generate of 33 codes:
+    # the first from the prefill, 32 from decode steps)
+    params = ig.SamplingParams(max_mel_tokens=33, **SAMPLING)
+    dec = []
+    for i in range(3):
+        out = ig.generate_batch(gpt, [ig.CodePrompt(p.text_tokens, p.conds, LANG, min_codes=33) for p in prompts],
+                                kv, params, [ig.SamplerRng(i * 100 + r) for r in range(n_req)])
+        assert all(len(c) == 33 for c in out)
+        dec.append(gpt.last_timing()[1])
     kv.close()
     dev_ms = statistics.median(ms)
+    dec_ms = statistics.median(dec[1:])
     flops = prefill_flops(cfg, [T] * n_req)
     peak = float(peaks.get("bf16_tflops_sustained", 1404.5))
     tf = flops / (dev_ms * 1e-3) / 1e12
@@ -381,7 +524,10 @@ def bench_prefill_cfg4(cfg, gpt, peaks, n_req=32, reps=3) -> dict:
             "device_ms": dev_ms, "positions_per_s": n_req * T / (dev_ms * 1e-3),
             "tflops": tf, "flops": flops, "peak_tflops": peak,
             "peak_source": "measured sustained bf16" if "bf16_tflops_sustained" in peaks else "fallback",
-            "frac": tf / peak}
+            "frac": tf / peak,
+            "decode_32_steps_ms": dec_ms, "decode_ms_per_step": dec_ms / 32,
+            "decode_note": "32 decode steps of the 32 requests after the prefill (batched generate, "
+                           "device time first sample through the last step)"}
 
 
 def _bench_decode_forward(gpt, kv, kv_len, iters, nb=1):
@@ -512,6 +658,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="only the cfg2 headline (no cfg1/cfg3/cfg4/cfg5 keys)")
     ap.add_argument("--profile-decode", type=int, default=0, metavar="KV_LEN",
                     help="profiler case: only the decode-step forward at this KV length")
     ap.add_argument("--profile-iters", type=int, default=2)

@@ -236,6 +236,39 @@ int itts_generate_batch(itts_gpt *gpt, itts_kv *kv, int32_t n_req,
                         uint64_t *rng_states, int32_t *codes_out, int32_t codes_stride,
                         int32_t *n_codes_out);
 
+/* ---- continuous batching ------------------------------------------------------------ */
+/* The reference serves one request at a time on its single engine actor
+ * (crates/core/src/engine/actor.rs:1227-1277), each through generate_codes_after
+ * (sampler.rs:340-392).  These three calls run that loop for many requests at once on
+ * one itts_kv: each of its max_batch slots holds at most one request, requests enter
+ * free slots between decode chunks and leave at their own STOP, and every decode step
+ * (one CUDA graph over all slots) advances all live requests.  Each request's codes are
+ * those of its own generate_codes_after call, within the decoder's tolerances.  A slot
+ * holding a live request is rejected by the other slot-taking entry points until it is
+ * collected; itts_kv_reset on it cancels the request. */
+
+/* Starts n requests in the given free slots: one packed prefill of their prompts, then
+ * each one's first sample (min_codes from the prompt, params[r], rng_states[r]).  The
+ * requests already in other slots are not disturbed. */
+int itts_batch_admit(itts_gpt *gpt, itts_kv *kv, int32_t n, const int32_t *slots,
+                     const itts_code_prompt *prompts, const itts_sampling_params *params,
+                     const uint64_t *rng_states);
+
+/* Replays decode steps over all slots, `chunk` at a time, until a live request has
+ * finished (STOP, its step limit, or an outgrown KV cache) or max_steps steps ran.
+ * finished_out (max_batch entries) receives the slots whose requests finished since the
+ * last call, *n_finished their number and *n_live the number still generating.  A
+ * request that finished at its first sample (admission) is reported without a step. */
+int itts_batch_decode(itts_gpt *gpt, itts_kv *kv, int32_t max_steps, int32_t chunk,
+                      int32_t *finished_out, int32_t *n_finished, int32_t *n_live);
+
+/* Takes a finished request out of `slot` and frees the slot: its codes (what
+ * generate_codes_after would return; codes_out holds max_codes), the SamplerRng state
+ * after its last draw, and *status_out = ITTS_OK or ITTS_E_VALIDATION when the request
+ * outgrew the KV cache (gpt.rs:157-165). */
+int itts_batch_collect(itts_kv *kv, int32_t slot, int32_t *codes_out, int32_t max_codes,
+                       int32_t *n_codes_out, uint64_t *rng_state_out, int32_t *status_out);
+
 /* Device time (CUDA events on the handle's stream) of the last generate call:
  * prefill_ms (all prefills) and decode_ms (first sample through the last step), and the
  * number of decode-step graph launches it made.  After itts_gpt_prefill_batch: prefill_ms

@@ -110,6 +110,10 @@ struct itts_kv {
     int *d_text_b = nullptr, *d_prior_b = nullptr;
     float *d_conds_b = nullptr;
     size_t cap_text_b = 0, cap_prior_b = 0, cap_conds_b = 0;
+    // continuous batching (itts_batch_*): per slot, a request admitted and not yet collected
+    // (live) and, among those, finished; the slots of an admission's first sample
+    std::vector<char> live, finished;
+    int *d_admit = nullptr;
 };
 
 static void free_prefill_batch(itts_kv *kv) {
@@ -630,7 +634,7 @@ static void kv_destroy(itts_kv *kv) {
                    kv->db.counters, kv->db.qkv_ll, kv->db.epoch, kv->db.err, kv->db.trace, kv->db.ws,
                    kv->db.xkb.hacc,
                    kv->pb.x, kv->pb.n, kv->pb.qkv, kv->pb.attn,
-                   kv->pb.u, kv->d_codes, kv->d_text, kv->d_prior, kv->d_conds};
+                   kv->pb.u, kv->d_codes, kv->d_text, kv->d_prior, kv->d_conds, kv->d_admit};
     for (void *p : dev) cudaFree(p);
     free_prefill_batch(kv);
     cudaFreeHost(kv->h_pinned);
@@ -742,6 +746,7 @@ extern "C" int itts_kv_create(itts_gpt *g, int32_t max_seq, int32_t max_batch, i
     A((void **)&kv->d_text, sizeof(int) * (m.text_pos_len + 2));
     A((void **)&kv->d_prior, sizeof(int) * (m.mel_pos_len + 2));
     A((void **)&kv->d_conds, sizeof(float) * (size_t)max_seq * m.d);
+    A((void **)&kv->d_admit, sizeof(int) * max_batch);
     if (e == cudaSuccess) e = cudaMallocHost((void **)&kv->h_pinned, sizeof(SlotState) * max_batch);
     if (e == cudaSuccess) e = cudaMallocHost((void **)&kv->h_i32, sizeof(int32_t) * (m.text_pos_len + m.mel_pos_len + 4 * max_batch + 8));
     kv->h_f32_cap = (size_t)max_seq * m.d;
@@ -758,6 +763,8 @@ extern "C" int itts_kv_create(itts_gpt *g, int32_t max_seq, int32_t max_batch, i
         kv_destroy(kv);
         return set_err(ITTS_E_CUDA, msg);
     }
+    kv->live.assign(max_batch, 0);
+    kv->finished.assign(max_batch, 0);
     kv->graphs.assign(2 * (max_batch + 1), nullptr);
     kv->graph_defs.assign(2 * (max_batch + 1), nullptr);
     kv->graph_failed.assign(2 * (max_batch + 1), 0);
@@ -767,11 +774,26 @@ extern "C" int itts_kv_create(itts_gpt *g, int32_t max_seq, int32_t max_batch, i
 
 extern "C" void itts_kv_free(itts_kv *kv) { kv_destroy(kv); }
 
+static int push_slots(itts_kv *kv, const int *slots, int n);
+
 extern "C" int itts_kv_reset(itts_kv *kv, int32_t slot) {
     if (!kv) return validation("kv", "null pointer");
     if (slot >= kv->max_batch) return validation("slot", "out of range");
+    std::vector<int> dropped;  // requests of the continuous batch in these slots are cancelled
     for (int s = 0; s < kv->max_batch; ++s)
-        if (slot < 0 || s == slot) kv->h_state[s].valid_len = 0;
+        if (slot < 0 || s == slot) {
+            kv->h_state[s].valid_len = 0;
+            if (kv->live[s]) {
+                kv->h_state[s].active = 0;
+                kv->live[s] = kv->finished[s] = 0;
+                dropped.push_back(s);
+            }
+        }
+    if (!dropped.empty()) {
+        CUDA_TRY(cudaSetDevice(kv->gpt->device));
+        TRY(push_slots(kv, dropped.data(), (int)dropped.size()));
+        CUDA_TRY(cudaStreamSynchronize(kv->gpt->stream));
+    }
     return ITTS_OK;
 }
 
@@ -836,6 +858,15 @@ static int set_batch_slots(itts_kv *kv, const int *slots, int n) {
     for (int i = 0; i < n; ++i) h[i] = slots[i];
     CUDA_TRY(cudaMemcpyAsync(kv->d_batch_slot, h, sizeof(int) * n, cudaMemcpyHostToDevice, st));
     CUDA_TRY(cudaStreamSynchronize(st));
+    return ITTS_OK;
+}
+
+// A slot that holds a request of the continuous batch (itts_batch_*) belongs to it until
+// the request is collected or the slot is reset.
+static int check_not_live(const itts_kv *kv, int slot) {
+    if (slot >= 0 && slot < kv->max_batch && kv->live[slot])
+        return validation("slot", "slot " + std::to_string(slot) +
+                                      " holds a request of the continuous batch (collect it or reset the slot first)");
     return ITTS_OK;
 }
 
@@ -1041,6 +1072,7 @@ extern "C" int itts_gpt_prefill(itts_gpt *g, itts_kv *kv, int32_t slot, const in
                                 const int32_t *prior, int32_t n_prior, float *logits_out) {
     if (!g || !kv || kv->gpt != g) return validation("gpt", "null pointer or cache of another model");
     if (slot < 0 || slot >= kv->max_batch) return validation("slot", "out of range");
+    TRY(check_not_live(kv, slot));
     CUDA_TRY(cudaSetDevice(g->device));
     kv->h_state[slot].valid_len = 0;  // cache.reset() (gpt.rs:664)
     TRY(prefill_impl(g, kv, slot, text, n_text, conds, n_conds, lang, prior, n_prior,
@@ -1098,6 +1130,7 @@ static int replay_impl(itts_gpt *g, itts_kv *kv, int slot, const int32_t *text, 
                        float *attention_out) {
     if (!g || !kv || kv->gpt != g) return validation("gpt", "null pointer or cache of another model");
     if (slot < 0 || slot >= kv->max_batch) return validation("slot", "out of range");
+    TRY(check_not_live(kv, slot));
     if (!codes || n_codes <= 0) return validation("codes", "codes must not be empty");
     if (n_prior < 0 || (n_prior > 0 && !prior)) return validation("prior_codes", "null pointer");
     const ModelView &m = g->m;
@@ -1215,6 +1248,7 @@ extern "C" int itts_gpt_step(itts_gpt *g, itts_kv *kv, int32_t n, const int32_t 
     std::vector<char> seen_slot(kv->max_batch, 0);
     for (int i = 0; i < n; ++i) {
         if (slots[i] < 0 || slots[i] >= kv->max_batch || seen_slot[slots[i]]) return validation("slots", "slots must be distinct and in range");
+        TRY(check_not_live(kv, slots[i]));
         seen_slot[slots[i]] = 1;
         if (toks[i] < 0 || toks[i] >= m.mel_vocab)
             return validation("mel_token_id", "mel_token_id " + std::to_string(toks[i]) + " out of range 0.." + std::to_string(m.mel_vocab));
@@ -1360,6 +1394,7 @@ static int generate_impl(itts_gpt *g, itts_kv *kv, int n, const int *slots,
     if (n <= 0 || n > kv->max_batch) return validation("n_req", "batch size out of range");
     std::vector<int> max_steps(n), Ts(n);
     int max_replays = 0;
+    for (int r = 0; r < n; ++r) TRY(check_not_live(kv, slots[r]));
     for (int r = 0; r < n; ++r) {
         const itts_sampling_params *p = params + (size_t)r * params_stride;
         TRY(itts_sampling_params_validate(p));
@@ -1492,6 +1527,181 @@ extern "C" int itts_generate_batch(itts_gpt *g, itts_kv *kv, int32_t n_req,
                          codes_stride, n_codes_out);
 }
 
+// ------------------------------------------------------------------------------
+// continuous batching: requests enter free slots between decode chunks and leave at
+// their own STOP, so a worker keeps up to max_batch requests in every decode step
+// (replaces the engine actor's one-request-at-a-time loop, actor.rs:1227-1277, around
+// generate_codes_after, sampler.rs:340-392)
+// ------------------------------------------------------------------------------
+static bool slot_small_k(const SlotState &s, int n_logits) {
+    itts_sampling_params p{};
+    p.greedy = s.greedy;
+    p.top_k = s.top_k;
+    p.top_p = s.top_p;
+    p.temperature = s.temperature;
+    p.repetition_penalty = s.rep_penalty;
+    p.max_mel_tokens = 1;
+    return sample_small_ok(p, n_logits);
+}
+
+extern "C" int itts_batch_admit(itts_gpt *g, itts_kv *kv, int32_t n, const int32_t *slots,
+                                const itts_code_prompt *prompts, const itts_sampling_params *params,
+                                const uint64_t *rng_states) {
+    if (!g || !kv || kv->gpt != g || !slots || !prompts || !params || !rng_states)
+        return validation("gpt", "null pointer or cache of another model");
+    if (n <= 0 || n > kv->max_batch) return validation("n", "number of requests out of range");
+    const ModelView &m = g->m;
+    std::vector<char> seen_slot(kv->max_batch, 0);
+    std::vector<int> Ts(n), max_steps(n), sl(slots, slots + n);
+    for (int r = 0; r < n; ++r) {
+        const int s = slots[r];
+        if (s < 0 || s >= kv->max_batch || seen_slot[s]) return validation("slots", "slots must be distinct and in range");
+        seen_slot[s] = 1;
+        if (kv->live[s]) return validation("slots", "slot " + std::to_string(s) + " holds a request that was not collected");
+        TRY(itts_sampling_params_validate(params + r));
+        const itts_code_prompt &pr = prompts[r];
+        const int cap = std::max(0, m.mel_pos_len - 3 - pr.n_prior);
+        max_steps[r] = std::min((int)params[r].max_mel_tokens, cap);  // sampler.rs:348-349
+        if (max_steps[r] == 0)
+            return validation("max_mel_tokens", "no Mel positions left to generate (max_mel_tokens is 0 or the prior codes fill the capacity)");
+        TRY(validate_prompt(m, pr.text_tokens, pr.n_text, pr.conds, pr.n_conds, pr.lang_id, pr.prior_codes,
+                            pr.n_prior, kv->max_seq, &Ts[r]));
+    }
+    CUDA_TRY(cudaSetDevice(g->device));
+    cudaStream_t st = g->stream;
+    for (int r = 0; r < n; ++r) kv->h_state[slots[r]].valid_len = 0;
+    TRY(prefill_batch_impl(g, kv, n, sl.data(), prompts, Ts.data(), kv->db.logits));
+    for (int r = 0; r < n; ++r) {
+        SlotState s = blank_slot(kv->max_seq);
+        fill_params(s, params + r);
+        s.valid_len = Ts[r];
+        s.active = 1;
+        s.max_steps = max_steps[r];
+        s.min_codes = prompts[r].min_codes;
+        s.n_prior = prompts[r].n_prior;
+        s.rng = rng_states[r];
+        itts_seen_initial(s.seen);  // sampler.rs:368: prior codes are not penalised
+        kv->h_state[slots[r]] = s;
+    }
+    TRY(push_slots(kv, sl.data(), n));
+    {
+        int32_t *h = kv->h_i32;  // staging is free: push_slots synchronized the stream
+        for (int r = 0; r < n; ++r) h[r] = slots[r];
+        CUDA_TRY(cudaMemcpyAsync(kv->d_admit, h, sizeof(int) * n, cudaMemcpyHostToDevice, st));
+    }
+    int small_k = 1;
+    for (int r = 0; r < n; ++r) small_k &= sample_small_ok(params[r], m.mel_vocab) ? 1 : 0;
+    SampleArgs a{};  // the first sample of each new request, from its prefill logits (row r)
+    a.slots = kv->d_slots;
+    a.batch_slot = kv->d_admit;
+    a.nb = n;
+    a.logits = kv->db.logits;
+    a.ld_logits = m.mel_vocab;
+    a.n_logits = m.mel_vocab;
+    a.after_forward = 0;
+    a.write_back = 0;
+    a.codes = kv->d_codes;
+    a.codes_stride = kv->codes_stride;
+    a.small_k = small_k;
+    launch_sample(a, st);
+    CUDA_TRY(cudaGetLastError());
+    CUDA_TRY(cudaStreamSynchronize(st));  // the staging buffer is reused by the next call
+    for (int r = 0; r < n; ++r) {
+        kv->live[slots[r]] = 1;
+        kv->finished[slots[r]] = 0;
+    }
+    return ITTS_OK;
+}
+
+extern "C" int itts_batch_decode(itts_gpt *g, itts_kv *kv, int32_t max_steps, int32_t chunk,
+                                 int32_t *finished_out, int32_t *n_finished, int32_t *n_live) {
+    if (!g || !kv || kv->gpt != g || !finished_out || !n_finished || !n_live)
+        return validation("gpt", "null pointer or cache of another model");
+    if (max_steps < 0 || chunk <= 0) return validation("max_steps", "max_steps >= 0 and chunk >= 1 required");
+    const ModelView &m = g->m;
+    const int nb = kv->max_batch;
+    *n_finished = 0;
+    *n_live = 0;
+    std::vector<int> all(nb), live_slots;
+    for (int i = 0; i < nb; ++i) {
+        all[i] = i;
+        if (kv->live[i] && !kv->finished[i]) live_slots.push_back(i);
+    }
+    if (live_slots.empty()) return ITTS_OK;
+    CUDA_TRY(cudaSetDevice(g->device));
+    cudaStream_t st = g->stream;
+    {  // the step runs every column: slots without a live request must not generate
+        std::vector<int> idle;
+        for (int i = 0; i < nb; ++i)
+            if (!kv->live[i] && kv->h_state[i].active) {
+                kv->h_state[i].active = 0;
+                idle.push_back(i);
+            }
+        if (!idle.empty()) TRY(push_slots(kv, idle.data(), (int)idle.size()));
+    }
+    int small_k = 1;
+    for (int s : live_slots) small_k &= slot_small_k(kv->h_state[s], m.mel_vocab) ? 1 : 0;
+    TRY(set_batch_slots(kv, all.data(), nb));  // column i = slot i: one graph for any mix
+    TRY(reset_step_sync(kv));
+    if (nb > MK_MAX_NB) ensure_weights_f16(g);  // before the capture
+    cudaGraphExec_t graph = nullptr;
+    if (!kv->graph_failed[2 * nb + small_k] && get_graph(kv, nb, small_k, &graph) != ITTS_OK) {
+        kv->graph_failed[2 * nb + small_k] = 1;
+        graph = nullptr;
+    }
+    DecodeView dv = decode_view(kv, nb);
+    int steps = 0;
+    for (;;) {
+        TRY(pull_slots(kv, live_slots.data(), (int)live_slots.size()));
+        int nf = 0, nl = 0;
+        for (int s : live_slots) {
+            if (kv->h_state[s].active) {
+                ++nl;
+            } else {
+                kv->finished[s] = 1;
+                finished_out[nf++] = s;
+            }
+        }
+        *n_finished = nf;
+        *n_live = nl;
+        if (nf > 0 || nl == 0 || steps >= max_steps) break;
+        const int todo = std::min(chunk, max_steps - steps);
+        for (int i = 0; i < todo; ++i) {
+            if (graph) {
+                CUDA_TRY(cudaGraphLaunch(graph, st));
+            } else {
+                CUDA_TRY(decode_forward(m, dv, kv->db, st));
+                launch_step_sample(kv, nb, small_k, st);
+            }
+        }
+        steps += todo;
+    }
+    TRY(check_step_sync(kv));
+    g->last_launches = steps;
+    return ITTS_OK;
+}
+
+extern "C" int itts_batch_collect(itts_kv *kv, int32_t slot, int32_t *codes_out, int32_t max_codes,
+                                  int32_t *n_codes_out, uint64_t *rng_state_out, int32_t *status_out) {
+    if (!kv || !n_codes_out || !rng_state_out || !status_out) return validation("kv", "null pointer");
+    if (slot < 0 || slot >= kv->max_batch) return validation("slot", "out of range");
+    if (!kv->live[slot] || !kv->finished[slot])
+        return validation("slot", "slot " + std::to_string(slot) + " holds no finished request");
+    const SlotState &s = kv->h_state[slot];
+    if (s.n_codes > 0 && (!codes_out || max_codes < s.n_codes))
+        return validation("codes_out", "buffer smaller than the request's " + std::to_string(s.n_codes) + " codes");
+    CUDA_TRY(cudaSetDevice(kv->gpt->device));
+    if (s.n_codes > 0)
+        CUDA_TRY(cudaMemcpy(codes_out, kv->d_codes + (size_t)slot * kv->codes_stride, sizeof(int32_t) * s.n_codes,
+                            cudaMemcpyDeviceToHost));
+    *n_codes_out = s.n_codes;
+    *rng_state_out = s.rng;
+    *status_out = s.error ? ITTS_E_VALIDATION : ITTS_OK;
+    kv->live[slot] = 0;
+    kv->finished[slot] = 0;
+    return ITTS_OK;
+}
+
 extern "C" int itts_gpt_last_timing(const itts_gpt *g, float *prefill_ms, float *decode_ms,
                                     int32_t *launches) {
     if (!g) return validation("gpt", "null pointer");
@@ -1513,6 +1723,7 @@ extern "C" int itts_bench_decode_forward(itts_gpt *g, itts_kv *kv, int32_t nb, i
     cudaStream_t st = g->stream;
     std::vector<int> slots(nb);
     std::vector<SlotState> saved(nb);
+    for (int i = 0; i < nb; ++i) TRY(check_not_live(kv, i));
     for (int i = 0; i < nb; ++i) {
         slots[i] = i;
         saved[i] = kv->h_state[i];

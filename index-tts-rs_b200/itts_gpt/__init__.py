@@ -438,3 +438,40 @@ def generate_batch(gpt: Gpt, prompts: Sequence[CodePrompt], cache: KvCache,
     for r, s in zip(rngs, states):
         r.state = int(s)
     return [codes[i, : counts[i]].tolist() for i in range(n)]
+
+
+# ---------------------------------------------------------------------------
+# continuous batching (include/itts_gpt.h itts_batch_*): requests enter free slots of a
+# cache between decode chunks and leave at their own STOP
+# ---------------------------------------------------------------------------
+def batch_admit(gpt: Gpt, cache: KvCache, slots: Sequence[int], prompts: Sequence[CodePrompt],
+                params: Sequence[SamplingParams], rngs: Sequence[SamplerRng]) -> None:
+    """Starts requests r in slots[r] (free slots): packed prefill + first sample."""
+    n = len(prompts)
+    keep: list = []
+    pcs = (CodePromptC * n)(*[_prompt_c(gpt, pr, keep) for pr in prompts])
+    ps = (SamplingParamsC * n)(*[p.to_c() for p in params])
+    sl = np.ascontiguousarray(np.asarray(slots, np.int32))
+    states = np.array([r.state for r in rngs], np.uint64)
+    _check(load_lib().itts_batch_admit(gpt._h, cache._h, n, _ptr(sl), pcs, ps, _ptr(states)))
+
+
+def batch_decode(gpt: Gpt, cache: KvCache, max_steps: int, chunk: int = 8) -> tuple[list[int], int]:
+    """Decode steps over all slots until a request finishes (or max_steps): returns the
+    finished slots and the number of requests still generating."""
+    out = np.zeros(max(1, cache.max_batch()), np.int32)
+    nf, nl = C.c_int32(), C.c_int32()
+    _check(load_lib().itts_batch_decode(gpt._h, cache._h, int(max_steps), int(chunk), _ptr(out),
+                                        C.byref(nf), C.byref(nl)))
+    return out[: nf.value].tolist(), nl.value
+
+
+def batch_collect(gpt: Gpt, cache: KvCache, slot: int) -> tuple[list[int], int, int]:
+    """Codes, final SamplerRng state and status (0, or the Validation code when the request
+    outgrew the cache) of the finished request in `slot`; frees the slot."""
+    cap = max(1, gpt.mel_pos_len)
+    codes = np.zeros(cap, np.int32)
+    n, st, status = C.c_int32(), C.c_uint64(), C.c_int32()
+    _check(load_lib().itts_batch_collect(cache._h, int(slot), _ptr(codes), cap, C.byref(n), C.byref(st),
+                                         C.byref(status)))
+    return codes[: n.value].tolist(), st.value, status.value

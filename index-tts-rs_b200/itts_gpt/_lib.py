@@ -79,6 +79,11 @@ SIGNATURES = [
     ("itts_gpt_prefill_batch", C.c_int, [_P, _P, _I32, C.POINTER(CodePromptC), _P]),
     ("itts_generate_batch", C.c_int,
      [_P, _P, _I32, C.POINTER(CodePromptC), C.POINTER(SamplingParamsC), _P, _P, _I32, _P]),
+    ("itts_batch_admit", C.c_int,
+     [_P, _P, _I32, _P, C.POINTER(CodePromptC), C.POINTER(SamplingParamsC), _P]),
+    ("itts_batch_decode", C.c_int, [_P, _P, _I32, _I32, _P, C.POINTER(_I32), C.POINTER(_I32)]),
+    ("itts_batch_collect", C.c_int,
+     [_P, _I32, _P, _I32, C.POINTER(_I32), C.POINTER(C.c_uint64), C.POINTER(_I32)]),
     ("itts_gpt_last_timing", C.c_int,
      [_P, C.POINTER(C.c_float), C.POINTER(C.c_float), C.POINTER(_I32)]),
     ("itts_bench_decode_forward", C.c_int,
