@@ -23,6 +23,8 @@
 #include <unordered_map>
 #include <vector>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "../../include/itts_gpt.h"
 #include "kernels.h"
 
@@ -35,6 +37,16 @@ void kernels_init_gemm_tc();
 using namespace itts;
 
 static thread_local std::string t_err;
+
+// Host-side NVTX range over one entry point or decode chunk (profilers show the reference's
+// per-stage spans, crates/core/src/engine/stream.rs:20-27, as named ranges; nothing is
+// recorded unless a profiler is attached).
+struct NvtxRange {
+    explicit NvtxRange(const char *name) { nvtxRangePushA(name); }
+    ~NvtxRange() { nvtxRangePop(); }
+    NvtxRange(const NvtxRange &) = delete;
+    NvtxRange &operator=(const NvtxRange &) = delete;
+};
 
 static int set_err(int code, const std::string &msg) {
     t_err = msg;
@@ -436,19 +448,28 @@ extern "C" int itts_gpt_from_tensors(const itts_tensor *tensors, int32_t n_tenso
         L.qkv = mk(li[i].a); L.proj = mk(li[i].p); L.fc = mk(li[i].fc); L.mlp = mk(li[i].mp);
     }
     // head-major copies of the c_proj weights (batch-1 cluster decode step), made once here
+    // (about 42 MB for the IndexTTS-2.5 decoder).  Every layer's c_proj must have layer 0's
+    // shape; otherwise, or when the copy cannot be made, no layer gets one and batch-1 steps
+    // run on the grid-wide kernel instead (xk_config declines a model without the copies).
     {
         const MkLin &P0 = g->layers[0].proj;
         const size_t per = (size_t)(d / 64) * P0.n_rb * mk_projh_chunk_bytes(P0.sbb);
-        if (d % 64 == 0 && P0.n_kc == 1 && P0.kc == (int)d && cudaMalloc(&g->projh_arena, per * n_layers) == cudaSuccess) {
-            for (int i = 0; i < n_layers && e == cudaSuccess; ++i) {
-                uint8_t *dst = (uint8_t *)g->projh_arena + per * i;
-                e = make_proj_by_head(g->layers[i].proj, (int)(d / 64), dst, g->stream);
-                g->layers[i].proj_h = dst;
-            }
-            if (e == cudaSuccess) e = cudaStreamSynchronize(g->stream);
-            if (e != cudaSuccess) return fail(e, "c_proj copy");
-        } else {
+        bool fits = d % 64 == 0 && P0.n_kc == 1 && P0.kc == (int)d;
+        for (int i = 1; i < n_layers && fits; ++i) {
+            const MkLin &Pi = g->layers[i].proj;
+            fits = Pi.n_kc == P0.n_kc && Pi.kc == P0.kc && Pi.n_rb == P0.n_rb && Pi.sbb == P0.sbb;
+        }
+        cudaError_t pe = fits ? cudaMalloc(&g->projh_arena, per * n_layers) : cudaErrorInvalidValue;
+        for (int i = 0; i < n_layers && pe == cudaSuccess; ++i) {
+            uint8_t *dst = (uint8_t *)g->projh_arena + per * i;
+            pe = make_proj_by_head(g->layers[i].proj, (int)(d / 64), dst, g->stream);
+            g->layers[i].proj_h = dst;
+        }
+        if (pe == cudaSuccess && fits) pe = cudaStreamSynchronize(g->stream);
+        if (pe != cudaSuccess) {
             cudaGetLastError();
+            cudaFree(g->projh_arena);
+            g->projh_arena = nullptr;
             for (int i = 0; i < n_layers; ++i) g->layers[i].proj_h = nullptr;
         }
     }
@@ -1070,6 +1091,7 @@ static int prefill_batch_impl(itts_gpt *g, itts_kv *kv, int n, const int *slots,
 extern "C" int itts_gpt_prefill(itts_gpt *g, itts_kv *kv, int32_t slot, const int32_t *text,
                                 int32_t n_text, const float *conds, int32_t n_conds, int32_t lang,
                                 const int32_t *prior, int32_t n_prior, float *logits_out) {
+    NvtxRange nvtx("itts prefill");
     if (!g || !kv || kv->gpt != g) return validation("gpt", "null pointer or cache of another model");
     if (slot < 0 || slot >= kv->max_batch) return validation("slot", "out of range");
     TRY(check_not_live(kv, slot));
@@ -1087,6 +1109,7 @@ extern "C" int itts_gpt_prefill(itts_gpt *g, itts_kv *kv, int32_t slot, const in
 
 extern "C" int itts_gpt_prefill_batch(itts_gpt *g, itts_kv *kv, int32_t n, const itts_code_prompt *prompts,
                                       float *logits_out) {
+    NvtxRange nvtx("itts prefill batch");
     if (!g || !kv || kv->gpt != g) return validation("gpt", "null pointer or cache of another model");
     if (n <= 0 || n > kv->max_batch || !prompts) return validation("n", "batch size out of range");
     const ModelView &m = g->m;
@@ -1128,6 +1151,7 @@ static int replay_impl(itts_gpt *g, itts_kv *kv, int slot, const int32_t *text, 
                        const float *conds, int n_conds, int lang, const int32_t *prior, int n_prior,
                        const int32_t *codes, int n_codes, bool alignment_only, float *log_probs_out,
                        float *attention_out) {
+    NvtxRange nvtx("itts teacher-forced replay");
     if (!g || !kv || kv->gpt != g) return validation("gpt", "null pointer or cache of another model");
     if (slot < 0 || slot >= kv->max_batch) return validation("slot", "out of range");
     TRY(check_not_live(kv, slot));
@@ -1242,6 +1266,7 @@ static int check_step_sync(itts_kv *kv) {
 // ------------------------------------------------------------------------------
 extern "C" int itts_gpt_step(itts_gpt *g, itts_kv *kv, int32_t n, const int32_t *slots,
                              const int32_t *toks, const int32_t *pos, float *logits_out) {
+    NvtxRange nvtx("itts step");
     if (!g || !kv || kv->gpt != g) return validation("gpt", "null pointer or cache of another model");
     if (n <= 0 || n > kv->max_batch || !slots || !toks || !pos) return validation("n", "batch size out of range");
     const ModelView &m = g->m;
@@ -1390,6 +1415,7 @@ static int generate_impl(itts_gpt *g, itts_kv *kv, int n, const int *slots,
                          const itts_code_prompt *prompts, const itts_sampling_params *params,
                          int params_stride, uint64_t *rngs, int32_t *codes_out, int stride,
                          int32_t *n_out) {
+    NvtxRange nvtx("itts generate");
     const ModelView &m = g->m;
     if (n <= 0 || n > kv->max_batch) return validation("n_req", "batch size out of range");
     std::vector<int> max_steps(n), Ts(n);
@@ -1465,6 +1491,7 @@ static int generate_impl(itts_gpt *g, itts_kv *kv, int n, const int *slots,
         for (int r = 0; r < n; ++r) any |= kv->h_state[slots[r]].active != 0;
         if (!any || launched >= max_replays) break;
         const int todo = std::min(chunk, max_replays - launched);
+        NvtxRange nvtx_chunk("itts decode chunk");
         for (int i = 0; i < todo; ++i) {
             if (graph) {
                 CUDA_TRY(cudaGraphLaunch(graph, st));
@@ -1547,6 +1574,7 @@ static bool slot_small_k(const SlotState &s, int n_logits) {
 extern "C" int itts_batch_admit(itts_gpt *g, itts_kv *kv, int32_t n, const int32_t *slots,
                                 const itts_code_prompt *prompts, const itts_sampling_params *params,
                                 const uint64_t *rng_states) {
+    NvtxRange nvtx("itts batch admit");
     if (!g || !kv || kv->gpt != g || !slots || !prompts || !params || !rng_states)
         return validation("gpt", "null pointer or cache of another model");
     if (n <= 0 || n > kv->max_batch) return validation("n", "number of requests out of range");
@@ -1615,6 +1643,7 @@ extern "C" int itts_batch_admit(itts_gpt *g, itts_kv *kv, int32_t n, const int32
 
 extern "C" int itts_batch_decode(itts_gpt *g, itts_kv *kv, int32_t max_steps, int32_t chunk,
                                  int32_t *finished_out, int32_t *n_finished, int32_t *n_live) {
+    NvtxRange nvtx("itts batch decode");
     if (!g || !kv || kv->gpt != g || !finished_out || !n_finished || !n_live)
         return validation("gpt", "null pointer or cache of another model");
     if (max_steps < 0 || chunk <= 0) return validation("max_steps", "max_steps >= 0 and chunk >= 1 required");
@@ -1666,6 +1695,7 @@ extern "C" int itts_batch_decode(itts_gpt *g, itts_kv *kv, int32_t max_steps, in
         *n_live = nl;
         if (nf > 0 || nl == 0 || steps >= max_steps) break;
         const int todo = std::min(chunk, max_steps - steps);
+        NvtxRange nvtx_chunk("itts decode chunk");
         for (int i = 0; i < todo; ++i) {
             if (graph) {
                 CUDA_TRY(cudaGraphLaunch(graph, st));

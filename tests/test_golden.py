@@ -100,3 +100,18 @@ def test_device_matches_golden_decoder(golden, golden_weights):
                 ref.max() - ref[int(np.argmax(g))] <= 4e-2
     finally:
         gpt.close()
+
+
+def test_reference_gpt_fixture_shapes():
+    """The Stage-1 tensors extracted from the reference's golden fixture
+    (crates/core/fixtures/golden_ref.safetensors) have the shapes its CP-10 / CP-11 tests
+    use: conds [1, 3, 1280] (gpt.rs:549-553), 8,194 prefill logits, 32 greedy codes."""
+    import numpy as np
+    from pathlib import Path
+    f = dict(np.load(Path(__file__).resolve().parent / "golden" / "reference_gpt_fixture.npz"))
+    assert f["conds"].shape == (1, 3, 1280) and f["conds"].dtype == np.float32
+    assert f["prefill_logits"].shape == (8194,) and np.isfinite(f["prefill_logits"]).all()
+    assert f["greedy_codes"].shape == (32,) and ((0 <= f["greedy_codes"]) & (f["greedy_codes"] < 8193)).all()
+    for i in range(6):
+        t = f[f"token_ids_{i}"]
+        assert t.dtype == np.int32 and 0 < t.size <= 600 and (t >= 0).all() and (t < 60510).all()
