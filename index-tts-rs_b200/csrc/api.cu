@@ -412,6 +412,7 @@ extern "C" int itts_gpt_from_tensors(const itts_tensor *tensors, int32_t n_tenso
     if (device >= 0 && device < 64 && !inited[device]) {
         kernels_init_sample();
         kernels_init_gemm_tc();
+        kernels_init_wide();
         inited[device] = true;
     }
     size_t total = 0;
@@ -459,6 +460,7 @@ extern "C" int itts_gpt_from_tensors(const itts_tensor *tensors, int32_t n_tenso
             const MkLin &Pi = g->layers[i].proj;
             fits = Pi.n_kc == P0.n_kc && Pi.kc == P0.kc && Pi.n_rb == P0.n_rb && Pi.sbb == P0.sbb;
         }
+        cudaGetLastError();  // a stale error from an earlier call must not read as this copy failing
         cudaError_t pe = fits ? cudaMalloc(&g->projh_arena, per * n_layers) : cudaErrorInvalidValue;
         for (int i = 0; i < n_layers && pe == cudaSuccess; ++i) {
             uint8_t *dst = (uint8_t *)g->projh_arena + per * i;
@@ -653,7 +655,7 @@ static void kv_destroy(itts_kv *kv) {
     void *dev[] = {kv->k, kv->v, kv->d_slots, kv->d_batch_slot, kv->db.x, kv->db.n, kv->db.n2,
                    kv->db.q, kv->db.attn, kv->db.u, kv->db.logits, kv->db.partials,
                    kv->db.counters, kv->db.qkv_ll, kv->db.epoch, kv->db.err, kv->db.trace, kv->db.ws,
-                   kv->db.xkb.hacc,
+                   kv->db.xkb.hacc, kv->db.sk_counters,
                    kv->pb.x, kv->pb.n, kv->pb.qkv, kv->pb.attn,
                    kv->pb.u, kv->d_codes, kv->d_text, kv->d_prior, kv->d_conds, kv->d_admit};
     for (void *p : dev) cudaFree(p);
@@ -707,7 +709,13 @@ extern "C" int itts_kv_create(itts_gpt *g, int32_t max_seq, int32_t max_batch, i
     A((void **)&kv->db.logits, sizeof(float) * max_batch * m.mel_vocab);
     A((void **)&kv->db.partials, sizeof(float) * max_batch * m.n_heads * kv->db.max_splits * 66);
     A((void **)&kv->db.counters, sizeof(int) * max_batch * m.n_heads);
-    kv->db.ws_splits = max_batch > MK_MAX_NB ? 16 : 0;  // split-K of the fp16 GEMM (wide steps)
+    kv->db.ws_splits = max_batch > MK_MAX_NB ? 16 : 0;  // split-K partials of the wide steps
+    kv->db.sk_counters = nullptr;
+    {  // steps of 5..64 columns on the int8 tiles (ITTS_WIDE_F16=1: the fp16-copy GEMMs instead)
+        const char *f16 = getenv("ITTS_WIDE_F16");
+        kv->db.wide_int8 = !(f16 && f16[0] == '1');
+    }
+    if (max_batch > MK_MAX_NB) A((void **)&kv->db.sk_counters, sizeof(int) * 4096);
     kv->db.ws = nullptr;
     if (kv->db.ws_splits)
         A((void **)&kv->db.ws, sizeof(float) * kv->db.ws_splits * max_batch * std::max(3 * m.d, m.ff));
@@ -773,6 +781,7 @@ extern "C" int itts_kv_create(itts_gpt *g, int32_t max_seq, int32_t max_batch, i
     kv->h_f32_cap = (size_t)max_seq * m.d;
     if (e == cudaSuccess) e = cudaMallocHost((void **)&kv->h_f32, sizeof(float) * kv->h_f32_cap);
     if (e == cudaSuccess) e = cudaMemsetAsync(kv->db.counters, 0, sizeof(int) * max_batch * m.n_heads, g->stream);
+    if (e == cudaSuccess && kv->db.sk_counters) e = cudaMemsetAsync(kv->db.sk_counters, 0, sizeof(int) * 4096, g->stream);
     kv->h_state.assign(max_batch, blank_slot(max_seq));
     if (e == cudaSuccess) {
         std::memcpy(kv->h_pinned, kv->h_state.data(), sizeof(SlotState) * max_batch);
@@ -1294,7 +1303,7 @@ extern "C" int itts_gpt_step(itts_gpt *g, itts_kv *kv, int32_t n, const int32_t 
     TRY(push_slots(kv, slots, n));
     TRY(set_batch_slots(kv, slots, n));
     TRY(reset_step_sync(kv));
-    if (n > MK_MAX_NB) ensure_weights_f16(g);  // wide steps run the fp16 GEMM
+    if (decode_uses_f16_weights(m, kv->db, n)) ensure_weights_f16(g);  // steps above 64 columns
     DecodeView dv = decode_view(kv, n);
     CUDA_TRY(decode_forward(m, dv, kv->db, g->stream));
     CUDA_TRY(cudaStreamSynchronize(g->stream));
@@ -1461,7 +1470,7 @@ static int generate_impl(itts_gpt *g, itts_kv *kv, int n, const int *slots,
     TRY(push_slots(kv, slots, n));
     TRY(set_batch_slots(kv, slots, n));
     TRY(reset_step_sync(kv));
-    if (n > MK_MAX_NB) ensure_weights_f16(g);  // wide steps run the fp16 GEMM (made before capture)
+    if (decode_uses_f16_weights(m, kv->db, n)) ensure_weights_f16(g);  // made before the capture
     int small_k = 1;  // every request greedy or with top_k <= 64: the small-k sampler
     for (int r = 0; r < n; ++r) small_k &= sample_small_ok(params[(size_t)r * params_stride], m.mel_vocab) ? 1 : 0;
     cudaGraphExec_t graph = nullptr;
@@ -1672,7 +1681,7 @@ extern "C" int itts_batch_decode(itts_gpt *g, itts_kv *kv, int32_t max_steps, in
     for (int s : live_slots) small_k &= slot_small_k(kv->h_state[s], m.mel_vocab) ? 1 : 0;
     TRY(set_batch_slots(kv, all.data(), nb));  // column i = slot i: one graph for any mix
     TRY(reset_step_sync(kv));
-    if (nb > MK_MAX_NB) ensure_weights_f16(g);  // before the capture
+    if (decode_uses_f16_weights(m, kv->db, nb)) ensure_weights_f16(g);  // before the capture
     cudaGraphExec_t graph = nullptr;
     if (!kv->graph_failed[2 * nb + small_k] && get_graph(kv, nb, small_k, &graph) != ITTS_OK) {
         kv->graph_failed[2 * nb + small_k] = 1;
@@ -1767,7 +1776,7 @@ extern "C" int itts_bench_decode_forward(itts_gpt *g, itts_kv *kv, int32_t nb, i
     TRY(push_slots(kv, slots.data(), nb));
     TRY(set_batch_slots(kv, slots.data(), nb));
     TRY(reset_step_sync(kv));
-    if (nb > MK_MAX_NB) ensure_weights_f16(g);
+    if (decode_uses_f16_weights(g->m, kv->db, nb)) ensure_weights_f16(g);
     DecodeView dv = decode_view(kv, nb);
     for (int i = 0; i < 3; ++i) CUDA_TRY(decode_forward(g->m, dv, kv->db, st));
     CUDA_TRY(cudaEventRecord(g->ev[0], st));

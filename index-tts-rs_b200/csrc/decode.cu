@@ -49,7 +49,15 @@ struct AttnParams {
     float *partials;
     int *counters;
     int split_len, max_splits;
+    int frag;  // write the output in fragment order (the skinny GEMM's activation layout)
 };
+
+// position of head element e (0..63) in the attention output: natural, or fragment order
+__device__ __forceinline__ int attn_out_pos(int e, int frag) {
+    if (!frag) return e;
+    const int b = e >> 4, kk = e & 15, c = (kk & 7) >> 1, hi = kk >> 3, lo = kk & 1;
+    return c * 16 + b * 4 + hi * 2 + lo;
+}
 
 struct SoftmaxPart {
     float m, l, acc[8];
@@ -90,38 +98,49 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnParams p) {
     part.l = 0.f;
 #pragma unroll
     for (int e = 0; e < 8; ++e) part.acc[e] = 0.f;
-    for (int j0 = s0 + warp * 4; j0 < s1; j0 += 16) {
-        const int j = j0 + grp;
-        const bool ok = j < s1;
-        float s = 0.f;
-        uint4 kr = make_uint4(0, 0, 0, 0), vr = make_uint4(0, 0, 0, 0);
-        if (ok) {
-            kr = *reinterpret_cast<const uint4 *>(Kb + (size_t)j * kHeadDim + d8 * 8);
-            vr = *reinterpret_cast<const uint4 *>(Vb + (size_t)j * kHeadDim + d8 * 8);
-        }
-        const __half2 *k2 = reinterpret_cast<const __half2 *>(&kr);
+    // each trip: positions j0 + grp and j0 + 16 + grp (two 16-position rows of the warp's
+    // range); all four K/V loads are issued before the first is used
+    for (int j0 = s0 + warp * 4; j0 < s1; j0 += 32) {
+        uint4 kr[2], vr[2];
+        bool ok[2];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const float2 kf = __half22float2(k2[e]);
-            s = fmaf(qv[2 * e], kf.x, s);
-            s = fmaf(qv[2 * e + 1], kf.y, s);
+        for (int u = 0; u < 2; ++u) {
+            const int j = j0 + 16 * u + grp;
+            ok[u] = j < s1;
+            kr[u] = make_uint4(0, 0, 0, 0);
+            vr[u] = kr[u];
+            if (ok[u]) {
+                kr[u] = *reinterpret_cast<const uint4 *>(Kb + (size_t)j * kHeadDim + d8 * 8);
+                vr[u] = *reinterpret_cast<const uint4 *>(Vb + (size_t)j * kHeadDim + d8 * 8);
+            }
         }
-        s += __shfl_xor_sync(0xffffffffu, s, 1);
-        s += __shfl_xor_sync(0xffffffffu, s, 2);
-        s += __shfl_xor_sync(0xffffffffu, s, 4);
-        if (ok) {
-            const float mn = fmaxf(part.m, s);
-            const float corr = part.m == -INFINITY ? 0.f : expf(part.m - mn);
-            const float pj = expf(s - mn);
-            part.l = part.l * corr + pj;
-            const __half2 *v2 = reinterpret_cast<const __half2 *>(&vr);
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            float s = 0.f;
+            const __half2 *k2 = reinterpret_cast<const __half2 *>(&kr[u]);
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                const float2 vf = __half22float2(v2[e]);
-                part.acc[2 * e] = part.acc[2 * e] * corr + pj * vf.x;
-                part.acc[2 * e + 1] = part.acc[2 * e + 1] * corr + pj * vf.y;
+                const float2 kf = __half22float2(k2[e]);
+                s = fmaf(qv[2 * e], kf.x, s);
+                s = fmaf(qv[2 * e + 1], kf.y, s);
             }
-            part.m = mn;
+            s += __shfl_xor_sync(0xffffffffu, s, 1);
+            s += __shfl_xor_sync(0xffffffffu, s, 2);
+            s += __shfl_xor_sync(0xffffffffu, s, 4);
+            if (ok[u]) {
+                const float mn = fmaxf(part.m, s);
+                const float corr = part.m == -INFINITY ? 0.f : expf(part.m - mn);
+                const float pj = expf(s - mn);
+                part.l = part.l * corr + pj;
+                const __half2 *v2 = reinterpret_cast<const __half2 *>(&vr[u]);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 vf = __half22float2(v2[e]);
+                    part.acc[2 * e] = part.acc[2 * e] * corr + pj * vf.x;
+                    part.acc[2 * e + 1] = part.acc[2 * e + 1] * corr + pj * vf.y;
+                }
+                part.m = mn;
+            }
         }
     }
 #pragma unroll
@@ -152,7 +171,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnParams p) {
             a += sm_acc[w][e] * f;
         }
         if (n_used == 1) {
-            p.out[(size_t)col * p.d + h * kHeadDim + e] = __float2half_rn(a / l);
+            p.out[(size_t)col * p.d + h * kHeadDim + attn_out_pos(e, p.frag)] = __float2half_rn(a / l);
         } else {
             part_out[2 + e] = a;
             if (e == 0) { part_out[0] = M; part_out[1] = l; }
@@ -181,14 +200,15 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(AttnParams p) {
             l += __ldcg(pp + s * 66 + 1) * f;
             a += __ldcg(pp + s * 66 + 2 + e) * f;
         }
-        p.out[(size_t)col * p.d + h * kHeadDim + e] = __float2half_rn(a / l);
+        p.out[(size_t)col * p.d + h * kHeadDim + attn_out_pos(e, p.frag)] = __float2half_rn(a / l);
         if (e == 0) p.counters[col * p.n_heads + h] = 0;
     }
 }
 
 void launch_attn_decode(const DecodeView &dv, int layer, const float *q, int q_stride,
-                        DecodeBufs &b, cudaStream_t st) {
+                        DecodeBufs &b, cudaStream_t st, int frag) {
     AttnParams p{};
+    p.frag = frag;
     p.q = q;
     p.q_stride = q_stride;
     p.out = reinterpret_cast<__half *>(b.attn);
@@ -250,15 +270,53 @@ static bool use_mk(const DecodeBufs &b, int nb) {
     return nb <= MK_MAX_NB && b.mk_grid > 0 && b.mk_nslot[nb] >= 2;
 }
 
+static bool use_wide(const ModelView &m, const DecodeBufs &b, int nb) {
+    if (!b.wide_int8 || nb > SK_MAX_NB || m.d > MK_MAX_D || m.d % 128 || m.ff % 64) return false;
+    const MkLayer &L = m.layers[0];
+    return skinny_ok(L.qkv, nb) && skinny_ok(L.proj, nb) && skinny_ok(L.fc, nb) && skinny_ok(L.mlp, nb) &&
+           skinny_ok(m.mel_head, nb);
+}
+
 int decode_forward_launches(const ModelView &m, const DecodeBufs &b, int nb) {
     if ((nb == 1 && b.xk.grid > 0) || use_mk(b, nb)) return 1;
+    if (use_wide(m, b, nb)) return 1 + 6 * m.n_layers + 3;
     return 1 + 7 * m.n_layers + 3;
+}
+
+bool decode_uses_f16_weights(const ModelView &m, const DecodeBufs &b, int nb) {
+    return !((nb == 1 && b.xk.grid > 0) || use_mk(b, nb) || use_wide(m, b, nb));
+}
+
+// Steps of 5..SK_MAX_NB columns: LayerNorms into fragment order, the skinny int8 GEMMs, the
+// split-K flash-decode attention with fragment-order output (6 launches per layer).
+static cudaError_t decode_forward_wide(const ModelView &m, const DecodeView &dv, DecodeBufs &b, cudaStream_t st) {
+    const int d = m.d, nb = dv.nb;
+    launch_embed_step(m, dv, b.x, st);
+    __half *n16 = reinterpret_cast<__half *>(b.n), *attn16 = reinterpret_cast<__half *>(b.attn),
+           *u16 = reinterpret_cast<__half *>(b.u), *fin16 = reinterpret_cast<__half *>(b.n2);
+    cudaError_t e = cudaSuccess;
+    auto ok = [&](cudaError_t r) { if (e == cudaSuccess) e = r; };
+    for (int l = 0; l < m.n_layers; ++l) {
+        const MkLayer &L = m.layers[l];
+        launch_ln_frag(b.x, L.ln1_w, L.ln1_b, nb, d, n16, st);
+        ok(launch_skinny(EPI_QKV, L.qkv, n16, nb, b.q, &dv, l, d, b.ws, b.sk_counters, st));
+        launch_attn_decode(dv, l, b.q, 3 * d, b, st, 1);
+        ok(launch_skinny(EPI_RESID, L.proj, attn16, nb, b.x, nullptr, l, d, b.ws, b.sk_counters, st));
+        launch_ln_frag(b.x, L.ln2_w, L.ln2_b, nb, d, n16, st);
+        ok(launch_skinny(EPI_GELU, L.fc, n16, nb, b.u, nullptr, l, d, b.ws, b.sk_counters, st, L.mlp.kc));
+        ok(launch_skinny(EPI_RESID, L.mlp, u16, nb, b.x, nullptr, l, d, b.ws, b.sk_counters, st));
+    }
+    launch_layernorm_rows(b.x, m.ln_f_w, m.ln_f_b, nb, d, b.n, st);   // gpt.ln_f, then final_norm
+    launch_ln_frag(b.n, m.final_w, m.final_b, nb, d, fin16, st);
+    ok(launch_skinny(EPI_PLAIN, m.mel_head, fin16, nb, b.logits, nullptr, 0, d, b.ws, b.sk_counters, st));
+    return e != cudaSuccess ? e : cudaGetLastError();
 }
 
 cudaError_t decode_forward(const ModelView &m, const DecodeView &dv, DecodeBufs &b,
                            cudaStream_t st) {
     if (dv.nb == 1 && b.xk.grid > 0) return xk_launch(mk_params(m, dv, b), b.xk, b.xkb, st);
     if (use_mk(b, dv.nb)) return mk_launch(mk_params(m, dv, b), st);
+    if (use_wide(m, b, dv.nb)) return decode_forward_wide(m, dv, b, st);
     const int d = m.d;
     launch_embed_step(m, dv, b.x, st);
     __half *n16 = reinterpret_cast<__half *>(b.n), *attn16 = reinterpret_cast<__half *>(b.attn),
@@ -268,7 +326,7 @@ cudaError_t decode_forward(const ModelView &m, const DecodeView &dv, DecodeBufs 
         launch_layernorm_rows_h(b.x, L.ln1_w, L.ln1_b, dv.nb, d, n16, st);
         launch_gemm(EPI_QKV, L.qkv, n16, b.q, dv.nb, &dv, dv.k_cache, dv.v_cache, -1, dv.n_slots,
                     dv.n_heads, dv.max_seq, l, d, st, b.ws, b.ws_splits);
-        launch_attn_decode(dv, l, b.q, 3 * d, b, st);
+        launch_attn_decode(dv, l, b.q, 3 * d, b, st, 0);
         launch_gemm(EPI_RESID, L.proj, attn16, b.x, dv.nb, nullptr, nullptr, nullptr, -1, 0, 0, 0, l,
                     d, st, b.ws, b.ws_splits);
         launch_layernorm_rows_h(b.x, L.ln2_w, L.ln2_b, dv.nb, d, n16, st);

@@ -56,6 +56,8 @@ struct DecodeBufs {
     int ws_splits;
     XkConfig xk;    // grid > 0: batch-1 steps run on the clustered all-SM kernel (xk_decode.cu)
     XkBufs xkb;
+    int *sk_counters;  // split-K counters of the skinny decode GEMMs (zero between launches)
+    bool wide_int8;    // steps of 5..SK_MAX_NB columns run the skinny int8 GEMMs
 };
 
 // Prefill scratch for one request of up to max_tokens positions.
@@ -87,7 +89,7 @@ void kernels_init();  // one-time function attributes (dynamic shared memory)
 void launch_embed_step(const ModelView &m, const DecodeView &dv, float *x, cudaStream_t st);
 
 void launch_attn_decode(const DecodeView &dv, int layer, const float *q, int q_stride,
-                        DecodeBufs &b, cudaStream_t st);
+                        DecodeBufs &b, cudaStream_t st, int frag);
 
 void launch_layernorm_rows(const float *x, const float *w, const float *b, int rows, int d,
                            float *y, cudaStream_t st);
@@ -117,6 +119,22 @@ int xk_config(const ModelView &m, XkConfig *out);
 cudaError_t xk_launch(const MkParams &p, const XkConfig &xc, const XkBufs &b, cudaStream_t st);
 // The head-major copy of a c_proj (MkLayer::proj_h) from its tiles: n_heads * n_rb chunks.
 cudaError_t make_proj_by_head(const MkLin &W, int n_heads, uint8_t *dst, cudaStream_t st);
+// Decode steps of 5..SK_MAX_NB columns on the int8 tiles (decode_wide.cu): the skinny GEMM
+// of one linear for nb columns whose activations x are fp16 [n_kc][nb][kc] (K chunk-major,
+// [nb][in] for one chunk) in fragment order (each group of 64 inputs permuted like the weight
+// bytes); epilogue as launch_gemm's, except EPI_GELU, whose fp16 output is written in that
+// layout for the next GEMM, whose K chunk is y_kc.  ws /
+// counters: partial sums of linears with several K chunks ([n_kc][nb][out] floats, and
+// n_rb counters that are zero between launches).
+constexpr int SK_MAX_NB = 64;
+bool skinny_ok(const MkLin &W, int nb);
+cudaError_t launch_skinny(int epi, const MkLin &W, const __half *x, int nb, void *y, const DecodeView *dv,
+                          int layer, int d, float *ws, int *counters, cudaStream_t st, int y_kc = 0);
+// LayerNorm of rows into fp16 fragment order (the skinny GEMM's input).
+void launch_ln_frag(const float *x, const float *w, const float *b, int rows, int d, __half *y, cudaStream_t st);
+void kernels_init_wide();
+// Whether a step of nb columns reads the fp16 weight copies (made before its first launch).
+bool decode_uses_f16_weights(const ModelView &m, const DecodeBufs &b, int nb);
 // Number of kernels decode_forward launches for nb columns.
 int decode_forward_launches(const ModelView &m, const DecodeBufs &b, int nb);
 

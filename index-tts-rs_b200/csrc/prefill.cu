@@ -98,11 +98,10 @@ __global__ void __launch_bounds__(256) layernorm_rows_warp_kernel(const float *x
     float4 v[LNW_CH];
     float s = 0.f;
 #pragma unroll
-    for (int c = 0; c < LNW_CH; ++c) {
-        if (c >= nch) break;
-        v[c] = row[c * 32 + lane];
-        s += (v[c].x + v[c].y) + (v[c].z + v[c].w);
-    }
+    for (int c = 0; c < LNW_CH; ++c)  // every load issued before the first use (no early exit)
+        v[c] = c < nch ? row[c * 32 + lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int c = 0; c < LNW_CH; ++c) s += (v[c].x + v[c].y) + (v[c].z + v[c].w);
     const float mean = warp_sum(s) / (float)d;
     float q = 0.f;
 #pragma unroll

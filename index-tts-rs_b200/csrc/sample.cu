@@ -296,17 +296,17 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleArgs a) {
 }
 
 // ---------------------------------------------------------------------------
-// The same sampler for top_k in 1..kSmallK (and greedy columns), 256 threads.  The k-th
+// The same sampler for top_k in 1..kSmallK (and greedy columns), 1,024 threads.  The k-th
 // largest scaled logit is found by a 4-pass radix select over 32-bit order keys (kept in
-// shared memory; per-warp histograms); the candidates are the keys above it and the ties
-// at it, the lowest ids first (when a tie group straddles the k-th place, one warp scans
+// shared memory; one histogram, updated once per distinct bin of a warp); the candidates are
+// the keys above it and the ties at it, the lowest ids first (when a tie group straddles the k-th place, one warp scans
 // the ids in order); one warp sorts the candidates (bitonic, in registers) into the
 // reference's order (value descending, id ascending).  The tail is the general kernel's.
 // The code is kept small (plain loops): it runs once per decode step from cold
 // instruction memory.
 // ---------------------------------------------------------------------------
 constexpr int kSmallK = 64;
-constexpr int kSmallThreads = 256;
+constexpr int kSmallThreads = 1024;
 
 __device__ __forceinline__ uint32_t order_key(float v) {
     const uint32_t b = v == 0.0f ? 0u : __float_as_uint(v);
@@ -315,7 +315,7 @@ __device__ __forceinline__ uint32_t order_key(float v) {
 
 __global__ void __launch_bounds__(kSmallThreads) sample_small_kernel(SampleArgs a) {
     extern __shared__ __align__(16) float lgs[];  // [n] logits, then [n] order keys
-    __shared__ uint32_t hist[kSmallThreads / 32][256];
+    __shared__ uint32_t hist[256];
     __shared__ uint32_t s_bin, s_above, s_count, s_eq;
     __shared__ uint64_t cand[kSmallK];
     __shared__ int s_ids[kSmallK];
@@ -381,21 +381,25 @@ __global__ void __launch_bounds__(kSmallThreads) sample_small_kernel(SampleArgs 
         const int k = min(kSmallK, (raw_k == 0 || raw_k >= (uint32_t)n) ? n : (int)raw_k);  // :221-226
         uint32_t prefix = 0, pmask = 0, remaining = (uint32_t)k;
         for (int shift = 24; shift >= 0; shift -= 8) {  // radix select of the k-th largest key
-            for (int b = lane; b < 256; b += 32) hist[warp][b] = 0;
+            if (tid < 256) hist[tid] = 0;
             __syncthreads();  // also: keys written / the previous pass's s_bin read
-            for (int i = tid; i < n; i += kSmallThreads) {
-                const uint32_t key = keys[i];
-                if ((key & pmask) == prefix) atomicAdd(&hist[warp][(key >> shift) & 0xFFu], 1u);
+            for (int i0 = 0; i0 < n; i0 += kSmallThreads) {  // (uniform trip count: warp-wide match)
+                const int i = i0 + tid;
+                uint32_t bin = 0x100u;  // no bin: out of range or outside the prefix
+                if (i < n) {
+                    const uint32_t key = keys[i];
+                    if ((key & pmask) == prefix) bin = (key >> shift) & 0xFFu;
+                }
+                // one shared-memory atomic per distinct bin of the warp (most keys share a few
+                // bins in the first passes)
+                const unsigned peers = __match_any_sync(0xffffffffu, bin);
+                if (bin != 0x100u && lane == __ffs(peers) - 1) atomicAdd(&hist[bin], (uint32_t)__popc(peers));
             }
-            __syncthreads();
-            uint32_t t = 0;
-            for (int w = 0; w < kSmallThreads / 32; ++w) t += hist[w][tid];
-            hist[0][tid] = t;  // each thread reads and writes only bin tid
             __syncthreads();
             if (warp == 0) {  // lane L holds bins 255-8L .. 248-8L (top-down order)
                 uint32_t c[8], sum = 0;
 #pragma unroll
-                for (int j = 0; j < 8; ++j) { c[j] = hist[0][255 - 8 * lane - j]; sum += c[j]; }
+                for (int j = 0; j < 8; ++j) { c[j] = hist[255 - 8 * lane - j]; sum += c[j]; }
                 uint32_t incl = sum;
                 for (int off = 1; off < 32; off <<= 1) {
                     const uint32_t o = __shfl_up_sync(0xffffffffu, incl, off);

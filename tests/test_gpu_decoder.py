@@ -191,7 +191,17 @@ def _flip_margin(logits, seen_words, params, state, tok):
             break
         cum += norm[i]
     if tok not in order[:active]:
-        return np.inf
+        if not np.isfinite(v[tok]):
+            return np.inf
+        if tok not in order:
+            # outside the checker's top-k: allowed when a logit error within the bound could
+            # swap it with the k-th candidate (returned in the units of a greedy gap)
+            return ("logit", float((v[order[-1]] - v[tok]) * params.temperature))
+        # inside the top-k but cut by top-p: allowed when the cumulative probability before
+        # it is within the band of the top-p threshold
+        j = order.index(tok)
+        before = float(norm[:j].sum())
+        return float(max(before - params.top_p, 0.0))
     j = order.index(tok)
     c = np.concatenate([[0.0], np.cumsum(probs[:active])]) / probs[:active].sum()
     u = ig.SamplerRng.from_state(state).next_f32()
@@ -200,7 +210,10 @@ def _flip_margin(logits, seen_words, params, state, tok):
 
 def _flip_allowed(params, margin):
     """A different token is within tolerance when the margin is inside the band a logit
-    error of LOGIT_TOL can move: 2*tol for a greedy gap, exp(2*tol/T) - 1 for a sampled draw."""
+    error of LOGIT_TOL can move: 2*tol for a greedy gap (or a swap across the top-k
+    boundary), exp(2*tol/T) - 1 for a sampled draw or the top-p cut."""
+    if isinstance(margin, tuple):  # ("logit", gap)
+        return margin[1] <= 2 * LOGIT_TOL
     band = 2 * LOGIT_TOL if params.greedy else np.expm1(2 * LOGIT_TOL / params.temperature)
     return margin <= band
 

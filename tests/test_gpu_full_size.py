@@ -277,3 +277,25 @@ def test_teacher_forced_replay_full_size(full):
     got = gpt.alignment_attention(text, conds, 1, prior, codes[10:], kv)
     _, maps2 = om.replay(om.kv(512), text, conds, 1, prior + codes[10:-1], q0 + len(prior), 1, (), True)
     np.testing.assert_allclose(got, maps2, atol=2e-3)
+
+
+def test_wide_steps_on_int8_tiles(full):
+    """Decode steps of 12 columns (the skinny int8 GEMMs, whose mlp projection sums its four
+    K chunks in a second pass) against the checker, column by column, for 4 steps."""
+    gpt, om = full
+    n = 12
+    prompts = [ig.CodePrompt(make_text(10 + 7 * r, CFG.text_vocab, seed=600 + r),
+                             make_conds(CFG.d, N_CONDS if r % 2 else 3, seed=700 + r), 1) for r in range(n)]
+    kv = ig.KvCache(gpt, max_seq=256, max_batch=n)
+    assert kv.decode_kernel(n) == "gemm path"
+    ig.prefill_batch(gpt, prompts, kv)
+    okvs = [om.kv(256) for _ in range(n)]
+    for r, pr in enumerate(prompts):
+        om.prefill(okvs[r], pr.text_tokens, pr.conds, pr.lang_id)
+    codes = np.random.default_rng(8).integers(0, 8192, (4, n))
+    errs = []
+    for s in range(4):
+        got = gpt.step_batch(kv, list(range(n)), codes[s].tolist(), [2 + s] * n)
+        for r in range(n):
+            errs.append(check_logits(got[r], om.step(okvs[r], int(codes[s, r]), 2 + s), f"column {r} step {s}"))
+    print(f"12-column steps on the int8 tiles: max |dlogit| {max(errs):.2e}")
