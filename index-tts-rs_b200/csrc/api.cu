@@ -413,6 +413,8 @@ extern "C" int itts_gpt_from_tensors(const itts_tensor *tensors, int32_t n_tenso
         kernels_init_sample();
         kernels_init_gemm_tc();
         kernels_init_wide();
+        kernels_init_decode();
+        kernels_init_prefill();
         inited[device] = true;
     }
     size_t total = 0;
@@ -1376,7 +1378,7 @@ extern "C" int itts_sample_next_token(itts_gpt *g, float *logits, int32_t n,
 // decode loop (sampler.rs:340-392): prefill every request, sample, then replay the
 // captured decode step until every request stopped.
 // ------------------------------------------------------------------------------
-static void launch_step_sample(itts_kv *kv, int nb, int small_k, cudaStream_t st) {
+static SampleArgs step_sample_args(itts_kv *kv, int nb, int small_k) {
     itts_gpt *g = kv->gpt;
     SampleArgs a{};
     a.slots = kv->d_slots;
@@ -1390,8 +1392,21 @@ static void launch_step_sample(itts_kv *kv, int nb, int small_k, cudaStream_t st
     a.codes = kv->d_codes;
     a.codes_stride = kv->codes_stride;
     a.small_k = small_k;
-    launch_sample(a, st);
+    return a;
 }
+
+// One decode step: the forward, then the sampler.  (A version that ran the small-k sampler
+// inside the batch-1 cluster kernel's last CTA measured slower: one 11-warp CTA after a
+// counter hand-off takes longer than the sampler kernel of 32 warps and its launch.)
+static cudaError_t launch_step(itts_kv *kv, int nb, int small_k, cudaStream_t st) {
+    itts_gpt *g = kv->gpt;
+    DecodeView dv = decode_view(kv, nb);
+    const cudaError_t e = decode_forward(g->m, dv, kv->db, st);
+    if (e != cudaSuccess) return e;
+    launch_sample(step_sample_args(kv, nb, small_k), st);
+    return cudaGetLastError();
+}
+
 
 // One decode step (forward + sampler) captured as a CUDA graph per batch size and sampler
 // variant (small_k: the top-k <= 64 kernel), cached at index 2 nb + small_k.
@@ -1402,9 +1417,7 @@ static int get_graph(itts_kv *kv, int nb, int small_k, cudaGraphExec_t *out) {
     cudaStream_t st = g->stream;
     cudaGraph_t graph = nullptr;
     CUDA_TRY(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
-    DecodeView dv = decode_view(kv, nb);
-    const cudaError_t fe = decode_forward(g->m, dv, kv->db, st);
-    launch_step_sample(kv, nb, small_k, st);
+    const cudaError_t fe = launch_step(kv, nb, small_k, st);
     const cudaError_t ce = cudaStreamEndCapture(st, &graph);
     if (fe != cudaSuccess || ce != cudaSuccess) {
         if (graph) cudaGraphDestroy(graph);
@@ -1478,7 +1491,6 @@ static int generate_impl(itts_gpt *g, itts_kv *kv, int n, const int *slots,
         kv->graph_failed[2 * n + small_k] = 1;  // e.g. a cooperative launch the driver cannot capture
         graph = nullptr;
     }
-    DecodeView step_dv = decode_view(kv, n);
     SampleArgs a{};
     a.slots = kv->d_slots;
     a.batch_slot = kv->d_batch_slot;
@@ -1505,8 +1517,7 @@ static int generate_impl(itts_gpt *g, itts_kv *kv, int n, const int *slots,
             if (graph) {
                 CUDA_TRY(cudaGraphLaunch(graph, st));
             } else {
-                CUDA_TRY(decode_forward(m, step_dv, kv->db, st));
-                launch_step_sample(kv, n, small_k, st);
+                CUDA_TRY(launch_step(kv, n, small_k, st));
             }
         }
         launched += todo;
@@ -1709,8 +1720,7 @@ extern "C" int itts_batch_decode(itts_gpt *g, itts_kv *kv, int32_t max_steps, in
             if (graph) {
                 CUDA_TRY(cudaGraphLaunch(graph, st));
             } else {
-                CUDA_TRY(decode_forward(m, dv, kv->db, st));
-                launch_step_sample(kv, nb, small_k, st);
+                CUDA_TRY(launch_step(kv, nb, small_k, st));
             }
         }
         steps += todo;

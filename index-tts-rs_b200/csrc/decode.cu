@@ -342,4 +342,13 @@ cudaError_t decode_forward(const ModelView &m, const DecodeView &dv, DecodeBufs 
     return cudaGetLastError();
 }
 
+// Every kernel of a decode step asks for the largest shared-memory carve-out: the step's
+// big kernels (the batch-1 cluster kernel, the skinny GEMMs) need it, and an SM whose next
+// kernel prefers another L1 / shared split has to drain and reconfigure between launches.
+void kernels_init_decode() {
+    cudaFuncSetAttribute(embed_step_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    cudaGetLastError();
+}
+
 }  // namespace itts

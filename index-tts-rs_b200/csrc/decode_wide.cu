@@ -112,7 +112,7 @@ __device__ __forceinline__ void skinny_epilogue(const SkinnyParams &p, const SkK
                                                 const float *v) {
     const int OUT = p.W.out, nb = p.nb;
     float *y = p.gp.y;
-    if (EPI == EPI_RESID) {
+    if constexpr (EPI == EPI_RESID) {
         float xv[SK_MAX_NB / 16];
 #pragma unroll
         for (int u = 0; u < SK_MAX_NB / 16; ++u) {
@@ -124,22 +124,22 @@ __device__ __forceinline__ void skinny_epilogue(const SkinnyParams &p, const SkK
             const int n = n0 + 16 * u;
             if (n < nb) y[(size_t)n * OUT + o] = xv[u] + v[u];
         }
-        return;
-    }
+    } else {
 #pragma unroll
-    for (int u = 0; u < SK_MAX_NB / 16; ++u) {
-        const int n = n0 + 16 * u;
-        if (n >= nb) break;
-        if (EPI == EPI_GELU) {
-            const int kc = o / p.y_kc, w = o - kc * p.y_kc;
-            p.y16[((size_t)kc * nb + n) * p.y_kc + (w & ~63) + frag_pos(w & 63)] = __float2half_rn(gelu_tanh(v[u]));
-        } else {
-            y[(size_t)n * OUT + o] = v[u];
-            if (EPI == EPI_QKV && o >= p.gp.d && kd.write[n]) {
-                const int rr = o - p.gp.d, which = rr / p.gp.d, oo = rr - which * p.gp.d;
-                __half *cache = which == 0 ? p.gp.k_cache : p.gp.v_cache;
-                cache[kv_index(p.gp.layer, kd.slot[n], oo >> 6, kd.pos[n], p.gp.n_slots, p.gp.n_heads, p.gp.max_seq) +
-                      (oo & 63)] = __float2half_rn(v[u]);
+        for (int u = 0; u < SK_MAX_NB / 16; ++u) {
+            const int n = n0 + 16 * u;
+            if (n >= nb) break;
+            if (EPI == EPI_GELU) {
+                const int kc = o / p.y_kc, w = o - kc * p.y_kc;
+                p.y16[((size_t)kc * nb + n) * p.y_kc + (w & ~63) + frag_pos(w & 63)] = __float2half_rn(gelu_tanh(v[u]));
+            } else {
+                y[(size_t)n * OUT + o] = v[u];
+                if (EPI == EPI_QKV && o >= p.gp.d && kd.write[n]) {
+                    const int rr = o - p.gp.d, which = rr / p.gp.d, oo = rr - which * p.gp.d;
+                    __half *cache = which == 0 ? p.gp.k_cache : p.gp.v_cache;
+                    cache[kv_index(p.gp.layer, kd.slot[n], oo >> 6, kd.pos[n], p.gp.n_slots, p.gp.n_heads, p.gp.max_seq) +
+                          (oo & 63)] = __float2half_rn(v[u]);
+                }
             }
         }
     }
@@ -356,11 +356,14 @@ bool skinny_ok(const MkLin &W, int nb) {
            W.n_rb <= 4096 && skinny_smem_bytes(W, nb) <= (size_t)SK_MAX_SMEM;
 }
 
+__global__ void ln_frag_kernel(const float *x, const float *w, const float *b, int rows, int d, __half *y);
+
 void kernels_init_wide() {  // once per device, at model load
     cudaFuncSetAttribute(skinny_q8_kernel<EPI_PLAIN>, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_MAX_SMEM);
     cudaFuncSetAttribute(skinny_q8_kernel<EPI_GELU>, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_MAX_SMEM);
     cudaFuncSetAttribute(skinny_q8_kernel<EPI_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_MAX_SMEM);
     cudaFuncSetAttribute(skinny_q8_kernel<EPI_QKV>, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_MAX_SMEM);
+    cudaFuncSetAttribute(ln_frag_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     cudaGetLastError();  // a refusal shows up as skinny_ok() launches failing, never as a stale error
 }
 

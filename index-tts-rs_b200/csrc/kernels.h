@@ -133,10 +133,13 @@ cudaError_t launch_skinny(int epi, const MkLin &W, const __half *x, int nb, void
 // LayerNorm of rows into fp16 fragment order (the skinny GEMM's input).
 void launch_ln_frag(const float *x, const float *w, const float *b, int rows, int d, __half *y, cudaStream_t st);
 void kernels_init_wide();
+void kernels_init_decode();   // shared-memory carve-out of the decode step's small kernels
+void kernels_init_prefill();
 // Whether a step of nb columns reads the fp16 weight copies (made before its first launch).
 bool decode_uses_f16_weights(const ModelView &m, const DecodeBufs &b, int nb);
 // Number of kernels decode_forward launches for nb columns.
 int decode_forward_launches(const ModelView &m, const DecodeBufs &b, int nb);
+
 
 // Optional extras of a prefill for the teacher-forced replay (gpt.rs:800-915).
 struct PrefillHooks {

@@ -413,4 +413,12 @@ void prefill_forward(const ModelView &m, const DecodeView &dv, int slot, int T, 
                 0, 0, d, st);
 }
 
+// The largest shared-memory carve-out for the LayerNorms that run between the decode step's
+// big kernels (see kernels_init_decode).
+void kernels_init_prefill() {
+    cudaFuncSetAttribute(layernorm_rows_warp_kernel<float>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    cudaFuncSetAttribute(layernorm_rows_warp_kernel<__half>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    cudaGetLastError();
+}
+
 }  // namespace itts
