@@ -276,6 +276,29 @@ int itts_batch_collect(itts_kv *kv, int32_t slot, int32_t *codes_out, int32_t ma
 int itts_gpt_last_timing(const itts_gpt *gpt, float *prefill_ms, float *decode_ms,
                          int32_t *decode_launches);
 
+/* ---- SemanticCodec decode (the step after the decoder) -------------------------------- */
+
+typedef struct itts_codec itts_codec; /* replaces `SemanticCodec` (models/codec.rs:104-114) */
+
+/* SemanticCodec::load_from_path (codec.rs:165-175): reads raw/semantic_codec.safetensors
+ * (F32 tensors; the encoder's tensors are ignored) onto `device`. */
+int itts_codec_load(const char *path, int device, itts_codec **out);
+/* SemanticCodec::from_weights (codec.rs:136-162): the same from caller-owned host tensors. */
+int itts_codec_from_tensors(const itts_tensor *tensors, int32_t n_tensors, int device,
+                            itts_codec **out);
+void itts_codec_free(itts_codec *codec);
+/* SemanticCodec::num_layers (codec.rs:178-182). */
+int32_t itts_codec_num_layers(const itts_codec *codec);
+/* Geometry: {n_layers, hidden (1024), backbone dim (384), intermediate (2048), codebook
+ * size (8192)} (codec.rs:27-42). */
+int itts_codec_dims(const itts_codec *codec, int32_t dims[5]);
+/* SemanticCodec::decode (codec.rs:202-239) of one sequence: codes [n_codes] (each in
+ * 0..8191) -> out [2 * n_codes][1024] fp32 (row-major), the features the length regulator
+ * takes (engine/actor.rs:597-615).  n_codes == 0 is a Validation error like codec.rs:211-216.
+ * device_ms (may be NULL) receives the device time of the decode (CUDA events). */
+int itts_codec_decode(itts_codec *codec, const int32_t *codes, int32_t n_codes, float *out,
+                      float *device_ms);
+
 /* ---- measurement (no reference counterpart) ----------------------------------------- */
 
 /* Replays `iters` times the decode-step forward (everything but the sampler) for slots

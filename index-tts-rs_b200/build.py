@@ -20,7 +20,7 @@ CSRC = PKG / "csrc"
 BUILD = PKG / "_build"
 INCLUDE = PKG.parent / "include"
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
-CU_SOURCES = ["decode.cu", "decode_wide.cu", "mk_decode.cu", "xk_decode.cu", "prefill.cu", "prefill_batch.cu", "gemm_tc.cu", "sample.cu", "api.cu"]
+CU_SOURCES = ["decode.cu", "decode_wide.cu", "codec.cu", "mk_decode.cu", "xk_decode.cu", "prefill.cu", "prefill_batch.cu", "gemm_tc.cu", "sample.cu", "api.cu"]
 
 
 def _nvcc() -> str:

@@ -13,6 +13,7 @@
 #include <unistd.h>
 
 #include <algorithm>
+#include <array>
 #include <cerrno>
 #include <cmath>
 #include <cstdio>
@@ -211,9 +212,9 @@ std::string shape_str(const itts_tensor *t) {
 
 // tensor_array_shaped (loader.rs:316-331): presence, rank, extents.
 int expect(const TensorTable &tt, const std::string &name, std::vector<int64_t> shape,
-           const itts_tensor **out) {
+           const itts_tensor **out, const char *artifact = "gpt_int8.safetensors") {
     const itts_tensor *t = tt.get(name);
-    if (!t) return weight_load("gpt_int8.safetensors", "missing tensor `" + name + "`");
+    if (!t) return weight_load(artifact, "missing tensor `" + name + "`");
     bool ok = t->ndim == (int)shape.size();
     for (size_t i = 0; ok && i < shape.size(); ++i) ok = t->shape[i] == shape[i];
     if (!ok) {
@@ -548,9 +549,10 @@ struct JsonCursor {
 };
 }  // namespace
 
-extern "C" int itts_gpt_load(const char *path, int device, itts_gpt **out) {
-    if (!out) return validation("out", "null pointer");
-    *out = nullptr;
+// Maps a safetensors file (8-byte header length, JSON header, raw data) and hands its
+// tensors (F32 / F16 / U32 / I32; others listed with dtype -1) to `use`, then unmaps it.
+template <class Use>
+static int read_safetensors(const char *path, Use use) {
     if (!path) return validation("path", "null pointer");
     const int fd = open(path, O_RDONLY);
     if (fd < 0) return set_err(ITTS_E_IO, std::string("I/O error at `") + path + "`: " + strerror(errno));
@@ -624,10 +626,18 @@ extern "C" int itts_gpt_load(const char *path, int device, itts_gpt **out) {
     }
     if (rc == ITTS_OK) {
         for (size_t i = 0; i < ts.size(); ++i) ts[i].name = names[i].c_str();
-        rc = itts_gpt_from_tensors(ts.data(), (int32_t)ts.size(), device, out);
+        rc = use(ts.data(), (int32_t)ts.size());
     }
     munmap(map, size);
     return rc;
+}
+
+extern "C" int itts_gpt_load(const char *path, int device, itts_gpt **out) {
+    if (!out) return validation("out", "null pointer");
+    *out = nullptr;
+    return read_safetensors(path, [&](const itts_tensor *t, int32_t n) {
+        return itts_gpt_from_tensors(t, n, device, out);
+    });
 }
 
 extern "C" void itts_gpt_free(itts_gpt *g) { gpt_destroy(g); }
@@ -1830,6 +1840,213 @@ extern "C" int itts_bench_trace(itts_gpt *g, itts_kv *kv, int32_t nb, int32_t kv
     return rc;
 }
 
+
+// ------------------------------------------------------------------------------
+// SemanticCodec decode (crates/core/src/models/codec.rs:104-239): the step after the
+// decoder turns its mel codes into the features the length regulator takes
+// (crates/core/src/engine/actor.rs:597-615).
+// ------------------------------------------------------------------------------
+struct itts_codec {
+    int device = 0;
+    CodecView v{};
+    std::vector<CodecBlock> blocks;
+    void *arena = nullptr;
+    cudaStream_t stream = nullptr;
+    cudaEvent_t ev[2] = {nullptr, nullptr};
+    CodecBufs bufs{};
+    int32_t *d_codes = nullptr;
+    float *d_out = nullptr;
+    int cap = 0;
+    float last_ms = 0.f;
+};
+
+static void codec_free_bufs(itts_codec *c) {
+    void *p[] = {c->bufs.x, c->bufs.t, c->bufs.h, c->bufs.u, c->d_codes, c->d_out};
+    for (void *q : p) cudaFree(q);
+    c->bufs = CodecBufs{};
+    c->d_codes = nullptr;
+    c->d_out = nullptr;
+    c->cap = 0;
+}
+
+extern "C" void itts_codec_free(itts_codec *c) {
+    if (!c) return;
+    cudaSetDevice(c->device);
+    if (c->stream) cudaStreamSynchronize(c->stream);
+    codec_free_bufs(c);
+    cudaFree(c->arena);
+    for (cudaEvent_t e : c->ev)
+        if (e) cudaEventDestroy(e);
+    if (c->stream) cudaStreamDestroy(c->stream);
+    delete c;
+}
+
+extern "C" int itts_codec_from_tensors(const itts_tensor *tensors, int32_t n_tensors, int device, itts_codec **out) {
+    if (!out) return validation("out", "null pointer");
+    *out = nullptr;
+    if (!tensors || n_tensors <= 0) return validation("tensors", "no tensors");
+    const char *art = "semantic_codec.safetensors";
+    TensorTable tt;
+    for (int i = 0; i < n_tensors; ++i)
+        if (tensors[i].name) tt.by_name[tensors[i].name] = &tensors[i];
+    // geometry from the tensors (codec.rs:27-42: hidden 1024, dim 384, 2048, codebook 8192 x 8)
+    const itts_tensor *cb = tt.get("quantizer.quantizers.0.codebook.weight");
+    const itts_tensor *pw1 = tt.get("decoder.0.convnext.0.pwconv1.weight");
+    const itts_tensor *emb = tt.get("decoder.0.embed.weight");
+    if (!cb || cb->ndim != 2) return weight_load(art, "missing tensor `quantizer.quantizers.0.codebook.weight`");
+    if (!pw1 || pw1->ndim != 2) return weight_load(art, "missing tensor `decoder.0.convnext.0.pwconv1.weight`");
+    if (!emb || emb->ndim != 3) return weight_load(art, "missing tensor `decoder.0.embed.weight`");
+    const int64_t ncode = cb->shape[0], cdim = cb->shape[1], inter = pw1->shape[0], dim = pw1->shape[1];
+    const int64_t embed_k = emb->shape[1], hidden = emb->shape[2];
+    int n_layers = 0;
+    while (tt.get("decoder.0.convnext." + std::to_string(n_layers) + ".gamma")) ++n_layers;
+    const itts_tensor *upw = tt.get("up.weight");
+    const int64_t up_k = upw && upw->ndim == 3 ? upw->shape[1] : 3;
+    const itts_tensor *dw0 = tt.get("decoder.0.convnext.0.dwconv.weight");
+    const int64_t dw_k = dw0 && dw0->ndim == 3 ? dw0->shape[1] : 7;
+    struct Up { const itts_tensor *t; size_t off; };
+    std::vector<Up> ups;
+    auto f32 = [&](const std::string &name, std::vector<int64_t> shape, int *idx) -> int {
+        const itts_tensor *t = nullptr;
+        TRY(expect(tt, name, shape, &t, art));
+        if (t->dtype != ITTS_DTYPE_F32) return weight_load(name, "expected F32");
+        *idx = (int)ups.size();
+        ups.push_back({t, 0});
+        return ITTS_OK;
+    };
+    int i_cb, i_ow, i_ob, i_ew, i_eb, i_nw, i_nb, i_fw, i_fb, i_pw, i_pb, i_uw, i_ub;
+    TRY(f32("quantizer.quantizers.0.codebook.weight", {ncode, cdim}, &i_cb));
+    TRY(f32("quantizer.quantizers.0.out_project.weight", {hidden, 1, cdim}, &i_ow));
+    TRY(f32("quantizer.quantizers.0.out_project.bias", {hidden}, &i_ob));
+    TRY(f32("decoder.0.embed.weight", {dim, embed_k, hidden}, &i_ew));
+    TRY(f32("decoder.0.embed.bias", {dim}, &i_eb));
+    TRY(f32("decoder.0.norm.weight", {dim}, &i_nw));
+    TRY(f32("decoder.0.norm.bias", {dim}, &i_nb));
+    TRY(f32("decoder.0.final_layer_norm.weight", {dim}, &i_fw));
+    TRY(f32("decoder.0.final_layer_norm.bias", {dim}, &i_fb));
+    TRY(f32("decoder.1.weight", {hidden, dim}, &i_pw));
+    TRY(f32("decoder.1.bias", {hidden}, &i_pb));
+    TRY(f32("up.weight", {hidden, up_k, hidden}, &i_uw));
+    TRY(f32("up.bias", {hidden}, &i_ub));
+    std::vector<std::array<int, 9>> bi(n_layers);
+    for (int l = 0; l < n_layers; ++l) {
+        const std::string pre = "decoder.0.convnext." + std::to_string(l) + ".";
+        TRY(f32(pre + "dwconv.weight", {dim, dw_k, 1}, &bi[l][0]));
+        TRY(f32(pre + "dwconv.bias", {dim}, &bi[l][1]));
+        TRY(f32(pre + "norm.weight", {dim}, &bi[l][2]));
+        TRY(f32(pre + "norm.bias", {dim}, &bi[l][3]));
+        TRY(f32(pre + "pwconv1.weight", {inter, dim}, &bi[l][4]));
+        TRY(f32(pre + "pwconv1.bias", {inter}, &bi[l][5]));
+        TRY(f32(pre + "pwconv2.weight", {dim, inter}, &bi[l][6]));
+        TRY(f32(pre + "pwconv2.bias", {dim}, &bi[l][7]));
+        TRY(f32(pre + "gamma", {dim}, &bi[l][8]));
+    }
+    if (n_layers < 1 || dim % 32 || embed_k % 2 == 0 || up_k % 2 == 0 || dw_k % 2 == 0)
+        return weight_load(art, "unsupported codec geometry");
+    CUDA_TRY(cudaSetDevice(device));
+    itts_codec *c = new itts_codec();
+    c->device = device;
+    size_t total = 0;
+    for (auto &u : ups) {
+        u.off = total;
+        size_t n = 1;
+        for (int k = 0; k < u.t->ndim; ++k) n *= (size_t)u.t->shape[k];
+        total = align256(total + n * 4);
+    }
+    cudaError_t e = cudaMalloc(&c->arena, total);
+    for (size_t k = 0; k < ups.size() && e == cudaSuccess; ++k) {
+        size_t n = 1;
+        for (int j = 0; j < ups[k].t->ndim; ++j) n *= (size_t)ups[k].t->shape[j];
+        e = cudaMemcpy((char *)c->arena + ups[k].off, ups[k].t->data, n * 4, cudaMemcpyHostToDevice);
+    }
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreate(&c->ev[0]);
+    if (e == cudaSuccess) e = cudaEventCreate(&c->ev[1]);
+    if (e != cudaSuccess) {
+        const std::string msg = std::string("device error: codec upload: ") + cudaGetErrorString(e);
+        itts_codec_free(c);
+        return set_err(ITTS_E_CUDA, msg);
+    }
+    auto F = [&](int i) { return (const float *)((const char *)c->arena + ups[i].off); };
+    CodecView &v = c->v;
+    v.n_layers = n_layers; v.hidden = (int)hidden; v.dim = (int)dim; v.inter = (int)inter; v.cdim = (int)cdim;
+    v.n_codes = (int)ncode; v.embed_k = (int)embed_k; v.dw_k = (int)dw_k; v.up_k = (int)up_k;
+    v.eps = 1e-6f;  // CODEC_NORM_EPS (codec.rs:39), convnext.rs:18
+    v.codebook = F(i_cb); v.out_w = F(i_ow); v.out_b = F(i_ob); v.embed_w = F(i_ew); v.embed_b = F(i_eb);
+    v.norm_w = F(i_nw); v.norm_b = F(i_nb); v.fnorm_w = F(i_fw); v.fnorm_b = F(i_fb);
+    v.proj_w = F(i_pw); v.proj_b = F(i_pb); v.up_w = F(i_uw); v.up_b = F(i_ub);
+    c->blocks.resize(n_layers);
+    for (int l = 0; l < n_layers; ++l) {
+        CodecBlock &b = c->blocks[l];
+        b.dw_w = F(bi[l][0]); b.dw_b = F(bi[l][1]); b.norm_w = F(bi[l][2]); b.norm_b = F(bi[l][3]);
+        b.pw1_w = F(bi[l][4]); b.pw1_b = F(bi[l][5]); b.pw2_w = F(bi[l][6]); b.pw2_b = F(bi[l][7]);
+        b.gamma = F(bi[l][8]);
+    }
+    v.blocks = c->blocks.data();
+    *out = c;
+    return ITTS_OK;
+}
+
+extern "C" int itts_codec_load(const char *path, int device, itts_codec **out) {
+    if (!out) return validation("out", "null pointer");
+    *out = nullptr;
+    return read_safetensors(path, [&](const itts_tensor *t, int32_t n) {
+        return itts_codec_from_tensors(t, n, device, out);
+    });
+}
+
+extern "C" int32_t itts_codec_num_layers(const itts_codec *c) { return c ? c->v.n_layers : 0; }
+
+extern "C" int itts_codec_dims(const itts_codec *c, int32_t dims[5]) {
+    if (!c || !dims) return validation("codec", "null pointer");
+    dims[0] = c->v.n_layers;
+    dims[1] = c->v.hidden;
+    dims[2] = c->v.dim;
+    dims[3] = c->v.inter;
+    dims[4] = c->v.n_codes;
+    return ITTS_OK;
+}
+
+extern "C" int itts_codec_decode(itts_codec *c, const int32_t *codes, int32_t n_codes, float *out, float *device_ms) {
+    if (!c || !out) return validation("codec", "null pointer");
+    if (!codes || n_codes <= 0) return validation("codes", "token sequence length T must be >= 1");
+    for (int i = 0; i < n_codes; ++i)
+        if (codes[i] < 0 || codes[i] >= c->v.n_codes)
+            return validation("codes", "code " + std::to_string(codes[i]) + " out of range 0.." +
+                                           std::to_string(c->v.n_codes));
+    NvtxRange nvtx("itts codec decode");
+    CUDA_TRY(cudaSetDevice(c->device));
+    cudaStream_t st = c->stream;
+    if (n_codes > c->cap) {  // work buffers grow with the longest sequence seen
+        CUDA_TRY(cudaStreamSynchronize(st));
+        codec_free_bufs(c);
+        const size_t T = (size_t)n_codes;
+        const CodecView &v = c->v;
+        cudaError_t e = cudaSuccess;
+        auto A = [&](void **p, size_t bytes) { if (e == cudaSuccess) e = cudaMalloc(p, bytes); };
+        A((void **)&c->bufs.x, T * v.hidden * 4);
+        A((void **)&c->bufs.t, T * v.dim * 4);
+        A((void **)&c->bufs.h, T * v.dim * 4);
+        A((void **)&c->bufs.u, T * v.inter * 4);
+        A((void **)&c->d_codes, T * 4);
+        A((void **)&c->d_out, 2 * T * v.hidden * 4);
+        if (e != cudaSuccess) {
+            codec_free_bufs(c);
+            return set_err(ITTS_E_CUDA, std::string("device error: codec buffers: ") + cudaGetErrorString(e));
+        }
+        c->cap = n_codes;
+    }
+    CUDA_TRY(cudaMemcpyAsync(c->d_codes, codes, sizeof(int32_t) * n_codes, cudaMemcpyHostToDevice, st));
+    CUDA_TRY(cudaEventRecord(c->ev[0], st));
+    CUDA_TRY(codec_decode_forward(c->v, c->d_codes, n_codes, c->bufs, c->d_out, st));
+    CUDA_TRY(cudaEventRecord(c->ev[1], st));
+    CUDA_TRY(cudaMemcpyAsync(out, c->d_out, sizeof(float) * 2 * (size_t)n_codes * c->v.hidden,
+                             cudaMemcpyDeviceToHost, st));
+    CUDA_TRY(cudaStreamSynchronize(st));
+    CUDA_TRY(cudaEventElapsedTime(&c->last_ms, c->ev[0], c->ev[1]));
+    if (device_ms) *device_ms = c->last_ms;
+    return ITTS_OK;
+}
 
 // ------------------------------------------------------------------------------
 // Sampling without allocation.

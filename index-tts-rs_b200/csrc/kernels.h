@@ -199,4 +199,23 @@ struct SampleArgs {
 };
 void launch_sample(const SampleArgs &a, cudaStream_t st);
 
+// SemanticCodec decode (codec.cu; crates/core/src/models/codec.rs:202-239): device
+// pointers of the weights (fp32, the checkpoint's layouts) and the work buffers.
+struct CodecBlock {
+    const float *dw_w, *dw_b, *norm_w, *norm_b, *pw1_w, *pw1_b, *pw2_w, *pw2_b, *gamma;
+};
+struct CodecView {
+    int n_layers, hidden, dim, inter, cdim, n_codes, embed_k, dw_k, up_k;
+    float eps;
+    const float *codebook, *out_w, *out_b, *embed_w, *embed_b, *norm_w, *norm_b, *fnorm_w, *fnorm_b;
+    const float *proj_w, *proj_b, *up_w, *up_b;
+    const CodecBlock *blocks;  // host array [n_layers]
+};
+struct CodecBufs {
+    float *x, *t, *h, *u;  // [cap][hidden], [cap][dim] x 2, [cap][inter]
+};
+// codes (device, [T], each < n_codes) -> d_out [2T][hidden]
+cudaError_t codec_decode_forward(const CodecView &c, const int32_t *d_codes, int T, const CodecBufs &b,
+                                 float *d_out, cudaStream_t st);
+
 }  // namespace itts

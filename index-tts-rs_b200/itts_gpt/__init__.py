@@ -475,3 +475,71 @@ def batch_collect(gpt: Gpt, cache: KvCache, slot: int) -> tuple[list[int], int, 
     _check(load_lib().itts_batch_collect(cache._h, int(slot), _ptr(codes), cap, C.byref(n), C.byref(st),
                                          C.byref(status)))
     return codes[: n.value].tolist(), st.value, status.value
+
+
+# ---------------------------------------------------------------------------
+# SemanticCodec decode (crates/core/src/models/codec.rs:104-239)
+# ---------------------------------------------------------------------------
+def _tensor_array(tensors: dict[str, np.ndarray]):
+    arr = (Tensor * len(tensors))()
+    keep = []
+    for i, (name, a) in enumerate(tensors.items()):
+        a = np.ascontiguousarray(a)
+        nb = name.encode()
+        keep += [a, nb]
+        arr[i].name = nb
+        arr[i].dtype = _NP_DTYPE[a.dtype]
+        arr[i].ndim = a.ndim
+        for j, sz in enumerate(a.shape):
+            arr[i].shape[j] = sz
+        arr[i].data = a.ctypes.data
+    return arr, keep
+
+
+class SemanticCodec:
+    """Decoder half of the semantic codec on one GPU: mel codes -> [2T, 1024] features."""
+
+    def __init__(self, handle: int, device: int):
+        self._h = C.c_void_p(handle)
+        self.device = device
+        self.last_device_ms = 0.0
+        dims = np.zeros(5, np.int32)
+        _check(load_lib().itts_codec_dims(self._h, _ptr(dims)))
+        self.n_layers, self.hidden, self.dim, self.inter, self.n_codes = (int(x) for x in dims)
+
+    @classmethod
+    def load_from_path(cls, path: str, device: int = 0) -> "SemanticCodec":
+        h = C.c_void_p()
+        _check(load_lib().itts_codec_load(str(path).encode(), device, C.byref(h)))
+        return cls(h.value, device)
+
+    @classmethod
+    def from_weights(cls, tensors: dict[str, np.ndarray], device: int = 0) -> "SemanticCodec":
+        arr, keep = _tensor_array(tensors)
+        h = C.c_void_p()
+        _check(load_lib().itts_codec_from_tensors(arr, len(tensors), device, C.byref(h)))
+        return cls(h.value, device)
+
+    def num_layers(self) -> int:
+        return int(load_lib().itts_codec_num_layers(self._h))
+
+    def decode(self, codes) -> np.ndarray:
+        """SemanticCodec::decode for one sequence: [T] codes -> [2T, 1024] float32."""
+        k = np.ascontiguousarray(np.asarray(codes, np.int32).reshape(-1))
+        out = np.empty((2 * max(1, k.size), self.hidden), np.float32)
+        ms = C.c_float()
+        _check(load_lib().itts_codec_decode(self._h, _ptr(k) if k.size else None, k.size, _ptr(out),
+                                            C.byref(ms)))
+        self.last_device_ms = ms.value
+        return out
+
+    def close(self) -> None:
+        if self._h:
+            load_lib().itts_codec_free(self._h)
+            self._h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -84,6 +84,12 @@ SIGNATURES = [
     ("itts_batch_decode", C.c_int, [_P, _P, _I32, _I32, _P, C.POINTER(_I32), C.POINTER(_I32)]),
     ("itts_batch_collect", C.c_int,
      [_P, _I32, _P, _I32, C.POINTER(_I32), C.POINTER(C.c_uint64), C.POINTER(_I32)]),
+    ("itts_codec_load", C.c_int, [C.c_char_p, C.c_int, C.POINTER(_P)]),
+    ("itts_codec_from_tensors", C.c_int, [C.POINTER(Tensor), _I32, C.c_int, C.POINTER(_P)]),
+    ("itts_codec_free", None, [_P]),
+    ("itts_codec_num_layers", _I32, [_P]),
+    ("itts_codec_dims", C.c_int, [_P, _P]),
+    ("itts_codec_decode", C.c_int, [_P, _P, _I32, _P, C.POINTER(C.c_float)]),
     ("itts_gpt_last_timing", C.c_int,
      [_P, C.POINTER(C.c_float), C.POINTER(C.c_float), C.POINTER(_I32)]),
     ("itts_bench_decode_forward", C.c_int,

@@ -165,3 +165,45 @@ def save_safetensors(path: str, tensors: dict[str, np.ndarray]) -> None:
         f.write(hb)
         for a in order:
             f.write(a.tobytes())
+
+
+def make_codec_weights(seed: int = 77, n_layers: int = 12, hidden: int = 1024, dim: int = 384,
+                       inter: int = 2048, cdim: int = 8, n_codes: int = 8192, embed_k: int = 7,
+                       dw_k: int = 7, up_k: int = 3, synth_path=None) -> dict[str, np.ndarray]:
+    """Seeded SemanticCodec decoder tensors by the names of raw/semantic_codec.safetensors
+    (crates/core/src/models/codec.rs:136-162, convnext.rs:40-60), F32, MLX conv layouts
+    [C_out, K, C_in].  Weights N(0, 1/fan_in), biases N(0, 0.02), LayerNorm gamma
+    1 + N(0, 0.01) and beta N(0, 0.01), layer scale N(0.1, 0.01), codebook N(0, 1)."""
+    lib = load_synth(synth_path)
+    t: dict[str, np.ndarray] = {}
+
+    def normal(name, shape, mean, std):
+        a = np.empty(shape, np.float32)
+        lib.itts_synth_normal_f32(seed, lib.itts_synth_tag(name.encode()), a.ctypes.data, a.size, mean, std)
+        t[name] = a
+
+    q = "quantizer.quantizers.0."
+    normal(q + "codebook.weight", (n_codes, cdim), 0.0, 1.0)
+    normal(q + "out_project.weight", (hidden, 1, cdim), 0.0, cdim ** -0.5)
+    normal(q + "out_project.bias", (hidden,), 0.0, 0.02)
+    normal("decoder.0.embed.weight", (dim, embed_k, hidden), 0.0, (embed_k * hidden) ** -0.5)
+    normal("decoder.0.embed.bias", (dim,), 0.0, 0.02)
+    for ln in ("decoder.0.norm", "decoder.0.final_layer_norm"):
+        normal(ln + ".weight", (dim,), 1.0, 0.01)
+        normal(ln + ".bias", (dim,), 0.0, 0.01)
+    for l in range(n_layers):
+        p = f"decoder.0.convnext.{l}."
+        normal(p + "dwconv.weight", (dim, dw_k, 1), 0.0, dw_k ** -0.5)
+        normal(p + "dwconv.bias", (dim,), 0.0, 0.02)
+        normal(p + "norm.weight", (dim,), 1.0, 0.01)
+        normal(p + "norm.bias", (dim,), 0.0, 0.01)
+        normal(p + "pwconv1.weight", (inter, dim), 0.0, dim ** -0.5)
+        normal(p + "pwconv1.bias", (inter,), 0.0, 0.02)
+        normal(p + "pwconv2.weight", (dim, inter), 0.0, inter ** -0.5)
+        normal(p + "pwconv2.bias", (dim,), 0.0, 0.02)
+        normal(p + "gamma", (dim,), 0.1, 0.01)
+    normal("decoder.1.weight", (hidden, dim), 0.0, dim ** -0.5)
+    normal("decoder.1.bias", (hidden,), 0.0, 0.02)
+    normal("up.weight", (hidden, up_k, hidden), 0.0, (up_k * hidden) ** -0.5)
+    normal("up.bias", (hidden,), 0.0, 0.02)
+    return t

@@ -685,3 +685,122 @@ void orc_set_num_threads(int n) {
     (void)n;
 #endif
 }
+
+/* ---------------------------------------------------------------------------------------
+ * SemanticCodec decode (crates/core/src/models/codec.rs:202-239, the Vocos backbone
+ * codec.rs:83-102, the ConvNeXt block crates/core/src/models/convnext.rs:66-73), fp32.
+ * MLX conv weights are channels-last [C_out, K, C_in]; conv1d is a cross-correlation:
+ * y[t, o] = b[o] + sum_k sum_i x[t + k - pad, i] w[o, k, i] (zero outside the sequence).
+ * --------------------------------------------------------------------------------------- */
+typedef struct {
+    const float *dw_w, *dw_b, *norm_w, *norm_b, *pw1_w, *pw1_b, *pw2_w, *pw2_b, *gamma;
+} orc_codec_block;
+
+typedef struct {
+    int n_layers, hidden, dim, inter, cdim, n_codes, embed_k, dw_k, up_k;
+    const float *codebook, *out_w, *out_b, *embed_w, *embed_b, *norm_w, *norm_b, *fnorm_w, *fnorm_b;
+    const float *proj_w, *proj_b, *up_w, *up_b;
+    orc_codec_block *blocks;
+} orc_codec;
+
+orc_codec *orc_codec_new(int n_layers, int hidden, int dim, int inter, int cdim, int n_codes, int embed_k,
+                         int dw_k, int up_k) {
+    orc_codec *c = (orc_codec *)calloc(1, sizeof(orc_codec));
+    c->n_layers = n_layers; c->hidden = hidden; c->dim = dim; c->inter = inter; c->cdim = cdim;
+    c->n_codes = n_codes; c->embed_k = embed_k; c->dw_k = dw_k; c->up_k = up_k;
+    c->blocks = (orc_codec_block *)calloc((size_t)n_layers, sizeof(orc_codec_block));
+    return c;
+}
+void orc_codec_free(orc_codec *c) { if (c) { free(c->blocks); free(c); } }
+void orc_codec_set_globals(orc_codec *c, const float *codebook, const float *out_w, const float *out_b,
+                           const float *embed_w, const float *embed_b, const float *norm_w, const float *norm_b,
+                           const float *fnorm_w, const float *fnorm_b, const float *proj_w, const float *proj_b,
+                           const float *up_w, const float *up_b) {
+    c->codebook = codebook; c->out_w = out_w; c->out_b = out_b; c->embed_w = embed_w; c->embed_b = embed_b;
+    c->norm_w = norm_w; c->norm_b = norm_b; c->fnorm_w = fnorm_w; c->fnorm_b = fnorm_b;
+    c->proj_w = proj_w; c->proj_b = proj_b; c->up_w = up_w; c->up_b = up_b;
+}
+void orc_codec_set_block(orc_codec *c, int l, const float *dw_w, const float *dw_b, const float *norm_w,
+                         const float *norm_b, const float *pw1_w, const float *pw1_b, const float *pw2_w,
+                         const float *pw2_b, const float *gamma) {
+    orc_codec_block *b = &c->blocks[l];
+    b->dw_w = dw_w; b->dw_b = dw_b; b->norm_w = norm_w; b->norm_b = norm_b; b->pw1_w = pw1_w;
+    b->pw1_b = pw1_b; b->pw2_w = pw2_w; b->pw2_b = pw2_b; b->gamma = gamma;
+}
+
+/* conv1d over `rows` output rows of x [src_rows][cin] (optionally the x`rep` nearest
+ * repetition of it), kernel k, pad (k-1)/2, weight [cout][k][cin] */
+static void codec_conv(const float *x, int src_rows, int rep, int cin, const float *w, const float *b, int k,
+                       int cout, float *y) {
+    const int pad = (k - 1) / 2, rows = src_rows * rep;
+#pragma omp parallel for schedule(static)
+    for (int t = 0; t < rows; ++t)
+        for (int o = 0; o < cout; ++o) {
+            float acc = 0.f;
+            for (int kk = 0; kk < k; ++kk) {
+                const int r = t + kk - pad;
+                if (r < 0 || r >= rows) continue;
+                const float *xr = x + (size_t)(r / rep) * cin;
+                const float *wr = w + ((size_t)o * k + kk) * cin;
+                for (int i = 0; i < cin; ++i) acc += xr[i] * wr[i];
+            }
+            y[(size_t)t * cout + o] = acc + b[o];
+        }
+}
+
+static void codec_ln(float *x, int rows, int c, const float *w, const float *b) { /* fast::layer_norm, eps 1e-6 */
+    for (int t = 0; t < rows; ++t) {
+        float *xr = x + (size_t)t * c;
+        float mean = 0.f, var = 0.f;
+        for (int i = 0; i < c; ++i) mean += xr[i];
+        mean /= (float)c;
+        for (int i = 0; i < c; ++i) { const float d = xr[i] - mean; var += d * d; }
+        var /= (float)c;
+        const float rstd = 1.0f / sqrtf(var + 1e-6f);
+        for (int i = 0; i < c; ++i) xr[i] = (xr[i] - mean) * rstd * w[i] + b[i];
+    }
+}
+
+int orc_codec_decode(const orc_codec *c, const int32_t *codes, int T, float *out) {
+    if (T <= 0) return fail(ORC_E_VALIDATION, "codes: token sequence length T must be >= 1");
+    for (int t = 0; t < T; ++t)
+        if (codes[t] < 0 || codes[t] >= c->n_codes) return fail(ORC_E_VALIDATION, "codes: out of range");
+    const int H = c->hidden, D = c->dim, F = c->inter;
+    float *x = (float *)malloc((size_t)T * H * sizeof(float));
+    float *h = (float *)malloc((size_t)T * D * sizeof(float));
+    float *t1 = (float *)malloc((size_t)T * D * sizeof(float));
+    float *u = (float *)malloc((size_t)T * F * sizeof(float));
+    for (int t = 0; t < T; ++t) /* codebook lookup + out_project Conv1d(k=1) (codec.rs:219-221) */
+        for (int o = 0; o < H; ++o) {
+            float acc = 0.f;
+            for (int j = 0; j < c->cdim; ++j) acc += c->codebook[(size_t)codes[t] * c->cdim + j] * c->out_w[(size_t)o * c->cdim + j];
+            x[(size_t)t * H + o] = acc + c->out_b[o];
+        }
+    codec_conv(x, T, 1, H, c->embed_w, c->embed_b, c->embed_k, D, h); /* backbone embed + norm (codec.rs:84-91) */
+    codec_ln(h, T, D, c->norm_w, c->norm_b);
+    for (int l = 0; l < c->n_layers; ++l) { /* ConvNeXt blocks (convnext.rs:66-73) */
+        const orc_codec_block *b = &c->blocks[l];
+        const int K = c->dw_k, pad = (K - 1) / 2;
+        for (int t = 0; t < T; ++t)
+            for (int ch = 0; ch < D; ++ch) {
+                float acc = 0.f;
+                for (int k = 0; k < K; ++k) {
+                    const int r = t + k - pad;
+                    if (r >= 0 && r < T) acc += h[(size_t)r * D + ch] * b->dw_w[(size_t)ch * K + k];
+                }
+                t1[(size_t)t * D + ch] = acc + b->dw_b[ch];
+            }
+        codec_ln(t1, T, D, b->norm_w, b->norm_b);
+        codec_conv(t1, T, 1, D, b->pw1_w, b->pw1_b, 1, F, u);
+        for (size_t i = 0; i < (size_t)T * F; ++i) /* nn::gelu: x * (1 + erf(x / sqrt 2)) / 2 */
+            u[i] = 0.5f * u[i] * (1.0f + erff(u[i] * 0.70710678118654752f));
+        codec_conv(u, T, 1, F, b->pw2_w, b->pw2_b, 1, D, t1);
+        for (int t = 0; t < T; ++t)
+            for (int ch = 0; ch < D; ++ch) h[(size_t)t * D + ch] += b->gamma[ch] * t1[(size_t)t * D + ch];
+    }
+    codec_ln(h, T, D, c->fnorm_w, c->fnorm_b);
+    codec_conv(h, T, 1, D, c->proj_w, c->proj_b, 1, H, x); /* decoder.1 (codec.rs:224-230) */
+    codec_conv(x, T, 2, H, c->up_w, c->up_b, c->up_k, H, out); /* x2 repeat + up conv (codec.rs:233-235) */
+    free(x); free(h); free(t1); free(u);
+    return ORC_OK;
+}

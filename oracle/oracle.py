@@ -232,3 +232,54 @@ class OracleKv:
             lib().orc_kv_free(self.h)
         except Exception:
             pass
+
+
+class OracleCodec:
+    """The SemanticCodec decode restatement (orc_codec_decode) over host tensors named as in
+    raw/semantic_codec.safetensors."""
+
+    def __init__(self, t: dict[str, np.ndarray]):
+        L = lib()
+        P, I = C.c_void_p, C.c_int
+        L.orc_codec_new.restype = P
+        L.orc_codec_new.argtypes = [I] * 9
+        L.orc_codec_free.argtypes = [P]
+        L.orc_codec_set_globals.argtypes = [P] * 14
+        L.orc_codec_set_block.argtypes = [P, I] + [P] * 9
+        L.orc_codec_decode.argtypes = [P, P, I, P]
+        self.t = {k: np.ascontiguousarray(v, np.float32) for k, v in t.items()}
+        t = self.t
+        cb = t["quantizer.quantizers.0.codebook.weight"]
+        emb = t["decoder.0.embed.weight"]
+        pw1 = t["decoder.0.convnext.0.pwconv1.weight"]
+        n_layers = 0
+        while f"decoder.0.convnext.{n_layers}.gamma" in t:
+            n_layers += 1
+        self.hidden = emb.shape[2]
+        self.h = L.orc_codec_new(n_layers, emb.shape[2], pw1.shape[1], pw1.shape[0], cb.shape[1], cb.shape[0],
+                                 emb.shape[1], t["decoder.0.convnext.0.dwconv.weight"].shape[1],
+                                 t["up.weight"].shape[1])
+        p = lambda n: t[n].ctypes.data
+        L.orc_codec_set_globals(self.h, p("quantizer.quantizers.0.codebook.weight"),
+                                p("quantizer.quantizers.0.out_project.weight"),
+                                p("quantizer.quantizers.0.out_project.bias"), p("decoder.0.embed.weight"),
+                                p("decoder.0.embed.bias"), p("decoder.0.norm.weight"), p("decoder.0.norm.bias"),
+                                p("decoder.0.final_layer_norm.weight"), p("decoder.0.final_layer_norm.bias"),
+                                p("decoder.1.weight"), p("decoder.1.bias"), p("up.weight"), p("up.bias"))
+        for l in range(n_layers):
+            q = f"decoder.0.convnext.{l}."
+            L.orc_codec_set_block(self.h, l, *[p(q + n) for n in (
+                "dwconv.weight", "dwconv.bias", "norm.weight", "norm.bias", "pwconv1.weight", "pwconv1.bias",
+                "pwconv2.weight", "pwconv2.bias", "gamma")])
+
+    def decode(self, codes) -> np.ndarray:
+        k = np.ascontiguousarray(np.asarray(codes, np.int32).reshape(-1))
+        out = np.empty((2 * max(1, k.size), self.hidden), np.float32)
+        _check(lib().orc_codec_decode(self.h, k.ctypes.data if k.size else None, k.size, out.ctypes.data))
+        return out
+
+    def __del__(self):
+        try:
+            lib().orc_codec_free(self.h)
+        except Exception:
+            pass
