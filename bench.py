@@ -117,6 +117,7 @@ class ClockSampler:
 
 
 METRIC = "mel tokens/s (cfg2 batch-1 decode)"
+XK_TRAFFIC = 686_719_488 + 4_613_120  # DRAM bytes of one batch-1 decode-step launch (ncu)
 DTYPE = "int8 weights (g64 affine, fp16 scales) x fp16 activations and KV, fp32 accumulate"
 
 
@@ -333,16 +334,17 @@ def run_ours(args, rank, world, local_rank):
                      "kv_positions": L_avg + 1, "launches_per_step": ws_launches,
                      "ms_per_launch": ws_ms,
                      # dram__bytes_read.sum + dram__bytes_write.sum of one launch at this KV
-                     # length (ncu capture summarised in profiles/xk_decode_kernel_cfg2.md)
-                     # dram__bytes_read.sum + dram__bytes_write.sum of one launch at this KV
-                     # length (ncu capture summarised in profiles/xk_decode_kernel_cfg2.md)
-                     "traffic": 692219904 if kname == "xk_decode_kernel" else None},
+                     # length, from an ncu capture of this kernel build (not measured here)
+                     "traffic": XK_TRAFFIC if kname == "xk_decode_kernel" else None,
+                     "traffic_source": "ncu --set full capture of one xk_decode_kernel launch at KV 1,384 "
+                                       "(686,719,488 B read + 4,613,120 B written); not measured in this run"},
         "clocks": clk,
     }
     if cfg5 is not None:
         line["cfg5"] = cfg5
     if world == 1 and not args.no_extra:
-        for key, fn in (("cfg1", lambda: bench_cfg1(cfg, gpt, w)),
+        for key, fn in (("codec_decode", lambda: bench_codec(codes)),
+                        ("cfg1", lambda: bench_cfg1(cfg, gpt, w)),
                         ("prefill_cfg4", lambda: bench_prefill_cfg4(cfg, gpt, peaks)),
                         ("cfg3", lambda: bench_cfg3(cfg, gpt, peaks))):
             try:
@@ -355,6 +357,24 @@ def run_ours(args, rank, world, local_rank):
         except Exception as e:  # the baseline never blocks the GPU line
             line["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
     print(json.dumps(line), flush=True)
+
+
+def bench_codec(codes) -> dict:
+    """The step after the decoder: SemanticCodec decode (crates/core/src/models/codec.rs:202-239)
+    of one cfg2 generate's 1,500 codes into [3000, 1024] features, seeded synthetic codec
+    weights of the checkpoint's geometry; device time by CUDA events."""
+    import itts_gpt as ig
+    from itts_gpt.synth import make_codec_weights
+    c = ig.SemanticCodec.from_weights(make_codec_weights(seed=77))
+    ms = []
+    for i in range(4):
+        out = c.decode(codes)
+        if i:
+            ms.append(c.last_device_ms)
+    c.close()
+    dev = statistics.median(ms)
+    return {"workload": f"SemanticCodec decode of {len(codes)} codes -> [{out.shape[0]}, {out.shape[1]}] fp32",
+            "device_ms": dev, "codes_per_s": len(codes) / (dev * 1e-3)}
 
 
 def bench_cfg1(cfg, gpt, w) -> dict:
