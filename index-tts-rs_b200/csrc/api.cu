@@ -83,6 +83,7 @@ struct itts_gpt {
     void *arena = nullptr;
     __half *w16_arena = nullptr;  // fp16 copies of the layer weights (long prefills), made once
     void *projh_arena = nullptr;  // head-major c_proj copies (batch-1 cluster decode step)
+    void *mlpk_arena = nullptr;   // input-sliced mlp copies (the same step)
     bool w16_tried = false;
     cudaStream_t stream = nullptr;
     cudaEvent_t ev[3] = {nullptr, nullptr, nullptr};
@@ -242,6 +243,7 @@ static void gpt_destroy(itts_gpt *g) {
     cudaFree(g->arena);
     cudaFree(g->w16_arena);
     cudaFree(g->projh_arena);
+    cudaFree(g->mlpk_arena);
     cudaFree(g->d_layers);
     cudaFree(g->d_sstate);
     cudaFree(g->d_slogits);
@@ -474,8 +476,36 @@ extern "C" int itts_gpt_from_tensors(const itts_tensor *tensors, int32_t n_tenso
         if (pe != cudaSuccess) {
             cudaGetLastError();
             cudaFree(g->projh_arena);
+    cudaFree(g->mlpk_arena);
             g->projh_arena = nullptr;
             for (int i = 0; i < n_layers; ++i) g->layers[i].proj_h = nullptr;
+        }
+    }
+    // copies of the mlp projections sliced by input (batch-1 cluster decode step: each cluster
+    // applies the rows of its own slice of the c_fc output), made once here (about 160 MB for
+    // the IndexTTS-2.5 decoder).  Same all-or-nothing rule as the c_proj copies.
+    {
+        const int H = (int)(d / 64);
+        const MkLin &M0 = g->layers[0].mlp;
+        const size_t per = mlp_slice_bytes(M0, H);
+        bool fits = mlp_slice_ok(M0, H);
+        for (int i = 1; i < n_layers && fits; ++i) {
+            const MkLin &Mi = g->layers[i].mlp;
+            fits = Mi.in == M0.in && Mi.kc == M0.kc && Mi.n_rb == M0.n_rb && Mi.sbb == M0.sbb;
+        }
+        cudaGetLastError();
+        cudaError_t pe = fits ? cudaMalloc(&g->mlpk_arena, per * n_layers) : cudaErrorInvalidValue;
+        for (int i = 0; i < n_layers && pe == cudaSuccess; ++i) {
+            uint8_t *dst = (uint8_t *)g->mlpk_arena + per * i;
+            pe = make_mlp_by_slice(g->layers[i].mlp, H, dst, g->stream);
+            g->layers[i].mlp_k = dst;
+        }
+        if (pe == cudaSuccess && fits) pe = cudaStreamSynchronize(g->stream);
+        if (pe != cudaSuccess) {
+            cudaGetLastError();
+            cudaFree(g->mlpk_arena);
+            g->mlpk_arena = nullptr;
+            for (int i = 0; i < n_layers; ++i) g->layers[i].mlp_k = nullptr;
         }
     }
     if ((e = cudaMalloc(&g->d_layers, sizeof(MkLayer) * n_layers)) != cudaSuccess) return fail(e, "layers");
@@ -763,16 +793,16 @@ extern "C" int itts_kv_create(itts_gpt *g, int32_t max_seq, int32_t max_batch, i
         XkConfig xc;
         if (e == cudaSuccess && xk_config(m, &xc) > 0) {
             const size_t L = m.n_layers;
-            const size_t words = L * (2 * (size_t)m.d + m.ff + (size_t)xc.nkc * m.d);
-            const size_t bytes = words * 8 + sizeof(uint32_t) * (4 * L + xc.grid);
+            const size_t bytes = sizeof(unsigned long long) * 4 * L * m.d + sizeof(uint32_t) * (8 * L + xc.grid);
             A((void **)&kv->db.xkb.hacc, bytes);
             if (e == cudaSuccess) {
                 XkBufs &x = kv->db.xkb;
-                x.u_ll = reinterpret_cast<uint64_t *>(x.hacc + 2 * L * m.d);
-                x.mp_ll = x.u_ll + L * m.ff;
-                x.hcnt = reinterpret_cast<uint32_t *>(x.mp_ll + L * xc.nkc * m.d);
+                x.xacc = x.hacc + 2 * L * m.d;
+                x.hcnt = reinterpret_cast<uint32_t *>(x.xacc + 2 * L * m.d);
                 x.hflag = x.hcnt + 2 * L;
-                x.epoch = x.hflag + 2 * L;
+                x.xcnt = x.hflag + 2 * L;
+                x.xflag = x.xcnt + 2 * L;
+                x.epoch = x.xflag + 2 * L;
                 e = cudaMemsetAsync(x.hacc, 0, bytes, g->stream);
                 kv->db.xk = xc;
             }

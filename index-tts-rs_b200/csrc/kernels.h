@@ -27,16 +27,17 @@ struct ModelView {
 };
 
 // The clustered all-SM decode step of one column (xk_decode.cu): launch shape and its
-// global exchange buffers (LL words, tags unique per launch).
+// global exchange buffers (fixed-point accumulators and counters, by step parity).
 struct XkConfig {
-    int grid = 0, rt = 0, nkc = 0, coop = 0;
+    int grid = 0, rt = 0, coop = 0;
 };
-struct XkBufs {  // one allocation: [2][L][d] c_proj accumulators, [L][ff] u, [L][nkc][d] mlp partials, counters
+struct XkBufs {  // one allocation: [2][L][d] accumulators for h and for x, then the counters
     unsigned long long *hacc = nullptr;  // fixed-point (2^-32) sums of the heads' c_proj partials, by step parity
-    uint64_t *u_ll = nullptr, *mp_ll = nullptr;
+    unsigned long long *xacc = nullptr;  // the same for the clusters' mlp partials (the next x)
     uint32_t *hcnt = nullptr;   // [2][L] CTAs that added their c_proj partials
     uint32_t *hflag = nullptr;  // [2][L] bit 0: a partial was not finite; bit 1: one was finite
                                 // but outside the fixed-point range (|y| >= 2^30)
+    uint32_t *xcnt = nullptr, *xflag = nullptr;  // [2][L] the same for the mlp partials
     uint32_t *epoch = nullptr;
 };
 
@@ -119,6 +120,11 @@ int xk_config(const ModelView &m, XkConfig *out);
 cudaError_t xk_launch(const MkParams &p, const XkConfig &xc, const XkBufs &b, cudaStream_t st);
 // The head-major copy of a c_proj (MkLayer::proj_h) from its tiles: n_heads * n_rb chunks.
 cudaError_t make_proj_by_head(const MkLin &W, int n_heads, uint8_t *dst, cudaStream_t st);
+// The copy of an mlp projection sliced by input (MkLayer::mlp_k): whether the shape allows it,
+// its size, and the copy itself.
+bool mlp_slice_ok(const MkLin &W, int n_heads);
+size_t mlp_slice_bytes(const MkLin &W, int n_heads);
+cudaError_t make_mlp_by_slice(const MkLin &W, int n_heads, uint8_t *dst, cudaStream_t st);
 // Decode steps of 5..SK_MAX_NB columns on the int8 tiles (decode_wide.cu): the skinny GEMM
 // of one linear for nb columns whose activations x are fp16 [n_kc][nb][kc] (K chunk-major,
 // [nb][in] for one chunk) in fragment order (each group of 64 inputs permuted like the weight

@@ -35,8 +35,22 @@ struct MkLayer {
     // order, row m at 64 m, no swizzle) followed by the 16 rows' (scale, offset) pairs of
     // that group; the batch-1 cluster decode step reads c_proj from here
     const uint8_t *proj_h;
+    // mlp projection re-tiled by input slice (null when not made): for the S = ff / H inputs
+    // [S c, S c + S) of cluster c and row block rb, a sub-tile of 16 rows x S bytes (row m's
+    // group j of the slice at slot j ^ (m & 1), fragment order, as in the tiles) followed by
+    // the 16 rows' (scale, offset) pairs of the slice's S / 64 groups; the sub-tiles of cluster
+    // c that rank k of its cluster applies (row blocks k, k + 6, ...) are contiguous; the
+    // batch-1 cluster decode step reads the mlp projection only from here
+    const uint8_t *mlp_k;
 };
 __host__ __device__ inline int mk_projh_chunk_bytes(int sbb) { return 16 * 64 + 16 * sbb; }
+__host__ __device__ inline int mk_mlpk_sub_bytes(int S, int sbb) { return 16 * S + 16 * (S / 64) * sbb; }
+// byte offset of (cluster c, rank k)'s first sub-tile in a layer's sliced mlp copy (6 ranks)
+__host__ __device__ inline size_t mk_mlpk_rank_offset(int n_rb, int S, int sbb, int c, int k) {
+    size_t before = 0;  // sub-tiles of ranks 0..k-1 of the cluster
+    for (int r = 0; r < k; ++r) before += r < n_rb ? (size_t)((n_rb - 1 - r) / 6 + 1) : 0;
+    return ((size_t)c * n_rb + before) * (size_t)mk_mlpk_sub_bytes(S, sbb);
+}
 
 constexpr int MK_MAX_D = 2048;      // model dim limit of the persistent kernel
 constexpr int MK_MAX_UNITS = 8;     // attention units per (column, head)

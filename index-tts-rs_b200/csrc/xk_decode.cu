@@ -15,14 +15,15 @@
 // when all CTAs have added theirs.  So q/k/v, the attention partials and the attention
 // output never cross clusters.
 //
-// x, h and u cross clusters as 64-bit LL words {fp32 value, stage tag} in global memory (the
-// tag is unique per launch, layer and stage, so no buffer is ever reset) or, for h, through
-// the accumulator, and each of them is gathered ONCE per cluster: rank k reads the k-th sixth
-// of the vector (finishing it on the way: residual add, K-split sum, fp16 conversion) and
-// pushes it into all 6 CTAs with st.async; each CTA's mbarrier counts the bytes.  The c_fc,
-// mlp and head tiles are dealt round-robin over the grid (tile t on CTA t % grid; the mlp
-// projection is K-split and the gathering rank sums its four chunk partials in a fixed
-// order).
+// The MLP runs by slices of its S = ff / H hidden units (256 for IndexTTS-2.5): cluster c
+// computes the c_fc rows [S c, S c + S), pushes GELU of them (fp16) into every CTA of the
+// cluster, and applies the matching S inputs of the mlp projection (a copy of its weights
+// re-tiled by input slice, made at load) for all d outputs, adding the partials into the
+// next x's fixed-point accumulator.  So the only vectors that cross clusters are h and x,
+// each through an accumulator: once every CTA has counted itself in, rank k of every
+// cluster reads the k-th sixth (adding the residual and the bias) and pushes it into all 6
+// CTAs with st.async; each CTA's mbarrier counts the bytes.  The head tiles are dealt
+// round-robin over the grid (tile t on CTA t % grid).
 //
 // Per CTA: 11 consumer warps + 1 producer warp.  The producer lane streams the CTA's weight
 // tiles and K/V rows into an 8-slot cp.async.bulk ring (no multicast) ahead of the stages;
@@ -56,7 +57,6 @@ constexpr int SLOT = 21888;        // bytes per slot: a 16 x 1280 tile with fp16
 constexpr int KVPOS = 84;          // positions per K/V tile: 2 x 84 x 128 B = 21,504 B
 constexpr int REC = 68;            // floats per attention record: m, l, 0, 0, acc[64]
 constexpr int QT = 12;             // QKV row blocks of one head (q, k, v x 64 rows / 16)
-constexpr int NWS = 5;             // LL-writing stages per layer: qkv, records, c_proj, u, mlp
 constexpr uint32_t SPIN = 1u << 22;
 constexpr int kXkRangeCode = MK_ERR_RANGE;  // error word: a c_proj partial outside the fixed-point range
 constexpr float kLog2e = 1.4426950408889634f;
@@ -64,6 +64,7 @@ constexpr float kLog2e = 1.4426950408889634f;
 // landing barriers: x/h (fp32), the head's attention output (fp16 + its sum), u (fp16), the
 // head's q/k/v (fp32), the head's attention records (cluster rank 0 only)
 enum { B0 = 0, BA, BU, BQ, BR, NSTB };
+enum { TM_RR = 0, TM_QKV = 1, TM_FC = 2 };  // tile assignment of a stage (tile_of)
 
 // ---------------------------------------------------------------------------
 // PTX helpers
@@ -157,69 +158,6 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
     const __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<const uint32_t *>(&h);
 }
-// LL words: low 32 bits the fp32 value, high 32 bits the tag of the writing stage
-__device__ __forceinline__ uint64_t ll_word(float v, uint32_t tag) {
-    return ((uint64_t)tag << 32) | (uint64_t)__float_as_uint(v);
-}
-__device__ __forceinline__ void ll_st2(uint64_t *p, float a, float b, uint32_t tag) {
-    asm volatile("st.relaxed.gpu.global.v2.b64 [%0], {%1, %2};" ::"l"(p), "l"(ll_word(a, tag)), "l"(ll_word(b, tag))
-                 : "memory");
-}
-__device__ __forceinline__ void ll_ld2(const uint64_t *p, uint64_t &a, uint64_t &b) {
-    asm volatile("ld.relaxed.gpu.global.v2.b64 {%0,%1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
-}
-__device__ __forceinline__ float ll_val(uint64_t w) { return __uint_as_float((uint32_t)w); }
-__device__ __forceinline__ bool ll_ok(uint64_t w, uint32_t tag) { return (uint32_t)(w >> 32) == tag; }
-
-// The LL word pairs a gather polls: nruns runs of ppr pairs each, run r starting at
-// src + r * stride words (pair i: run i / ppr, pair i % ppr of it).  One out-of-line routine
-// polls every gather, so the exchanges of a layer share one copy of the polling code.
-struct PollRuns {
-    const uint64_t *src;
-    int stride, ppr, nruns;
-};
-constexpr int PPJ = 4;  // pairs per thread per round
-
-// Polls pairs [0, nruns * ppr) until every tag equals `tag`; pair i's values go to
-// stage[2i], stage[2i + 1].  Called by all consumer threads; false on a timeout or a raised
-// error word.
-__device__ __noinline__ bool poll_runs(PollRuns pr, uint32_t tag, float *stage, const int *err) {
-    const int tid = threadIdx.x, total = pr.nruns * pr.ppr;
-    for (int base = 0; base < total; base += CT * PPJ) {
-        const uint64_t *adr[PPJ];
-        uint32_t pending = 0;
-#pragma unroll
-        for (int j = 0; j < PPJ; ++j) {
-            const int i = base + tid + j * CT;
-            adr[j] = nullptr;
-            if (i < total) {
-                const int r = i / pr.ppr;
-                adr[j] = pr.src + (size_t)r * pr.stride + 2 * (i - r * pr.ppr);
-                pending |= 1u << j;
-            }
-        }
-        for (uint32_t it = 0; pending; ++it) {
-            uint64_t w[PPJ][2];
-#pragma unroll
-            for (int j = 0; j < PPJ; ++j)
-                if ((pending >> j) & 1u) ll_ld2(adr[j], w[j][0], w[j][1]);
-#pragma unroll
-            for (int j = 0; j < PPJ; ++j)
-                if (((pending >> j) & 1u) && ll_ok(w[j][0], tag) && ll_ok(w[j][1], tag)) {
-                    const int i = base + tid + j * CT;
-                    stage[2 * i] = ll_val(w[j][0]);
-                    stage[2 * i + 1] = ll_val(w[j][1]);
-                    pending &= ~(1u << j);
-                }
-            if (pending) {
-                if (it >= SPIN || ((it & 255u) == 255u && *(volatile const int *)err)) return false;
-                if (it >= 8) __nanosleep(it < 32 ? 32u : 128u);
-            }
-        }
-    }
-    return true;
-}
-
 // ---------------------------------------------------------------------------
 // shared-memory carve-up (identical on host and device)
 // ---------------------------------------------------------------------------
@@ -229,8 +167,7 @@ struct XkSmem {
 __host__ __device__ inline uint32_t xk_red_bytes(int rt, int d, int ff) {
     uint32_t m = (uint32_t)rt * CW * 16 * 4;                                   // tile partial sums
     m = max(m, (uint32_t)(CW + 1) * REC * 4);                                  // attention warp states
-    m = max(m, (uint32_t)(4 * ((d / 4 + CS - 1) / CS) * 4 * 4));               // x gather (4 K chunks)
-    m = max(m, (uint32_t)(((ff / 64 + CS - 1) / CS) * 64 * 4));                // u gather
+    m = max(m, (uint32_t)2 * CW * 16 * 4);                                     // mlp slice partial sums
     return m;
 }
 struct XkTab {
@@ -247,9 +184,10 @@ __host__ __device__ inline XkSmem xk_layout(int d, int ff, int rt, int n_layers)
     L.land = take(d * 4);
     L.xln = take(d * 2);
     L.xh = take(64 * 2 + 16);  // the head's attention output (fp16, fragment order) + its sum
-    L.xu = take(ff * 2);
+    const int S = ff / (d / 64);  // the cluster's slice of the MLP hidden units
+    L.xu = take(S * 2);
     L.sxln = take(d / 64 * 4);
-    L.sxu = take(ff / 64 * 4);
+    L.sxu = take(S / 64 * 4);
     L.red = take(xk_red_bytes(rt, d, ff));
     L.qkvh = take(3 * 64 * 4);
     L.recs = take(CS * REC * 4);
@@ -268,10 +206,11 @@ struct XkParams {
     uint32_t *hcnt;            // [2][L] CTAs that added their partials
     uint32_t *hflag;           // [2][L] partials left out of the sum: bit 0 not finite, bit 1
                                // finite but |y| >= 2^30 (the sum of 20 heads could wrap)
-    uint64_t *u_ll;      // [L][ff]    GELU(c_fc)
-    uint64_t *mp_ll;     // [L][nkc][d] mlp c_proj K-chunk partial sums
+    unsigned long long *xacc;  // [2][L][d] sums of the clusters' mlp partials (next x), as hacc
+    uint32_t *xcnt;            // [2][L] CTAs that added their mlp partials
+    uint32_t *xflag;           // [2][L] as hflag
     uint32_t *epoch;     // [grid] launches completed per CTA
-    int rt, nkc, dry;
+    int rt, dry;
 };
 
 // rows of [0, n) gathered by cluster rank k
@@ -341,8 +280,21 @@ struct XkProducer {
                 const uint32_t cb = (uint32_t)mk_projh_chunk_bytes(Ly->proj.sbb);
                 if (nc > 0) issue(Ly->proj_h + ((size_t)head * nrb + r0) * cb, (uint32_t)nc * cb, nullptr, 0);
             }
-            lin(&Ly->fc);
-            lin(&Ly->mlp);
+            {  // the cluster's slice of c_fc rows: row blocks S/16 head + rank + CS i
+                const int nrb = p.ff / p.H / 16;
+                const uint32_t tb = (uint32_t)Ly->fc.tile_bytes;
+                for (int rb = rank; rb < nrb; rb += CS) issue(Ly->fc.tiles + (size_t)(head * nrb + rb) * tb, tb, nullptr, 0);
+            }
+            {  // this rank's sub-tiles of the cluster's K-slice of the mlp projection, contiguous
+               // in the sliced copy, as many per ring slot as fit
+                const int S = p.ff / p.H, nrb = Ly->mlp.n_rb, mine = rank < nrb ? (nrb - 1 - rank) / CS + 1 : 0;
+                const uint32_t sub = (uint32_t)mk_mlpk_sub_bytes(S, p.sbb), per = SLOT / sub;
+                const uint8_t *src = Ly->mlp_k + mk_mlpk_rank_offset(nrb, S, p.sbb, head, rank);
+                for (int s0 = 0; s0 < mine; s0 += (int)per) {
+                    const int ns = min((int)per, mine - s0);
+                    issue(src + (size_t)s0 * sub, (uint32_t)ns * sub, nullptr, 0);
+                }
+            }
         }
         if (ok) lin(&p.head);
         // every issued copy lands before exit (the last one of each slot; the earlier ones
@@ -369,13 +321,12 @@ struct XkConsumer {
     uint32_t par;           // this step's accumulator buffer
     uint64_t *fullp, *emptyp, *stb;
     int tid, warp, lane, g, c, rank, R, NR, d, ff, H, rt, head;
-    uint32_t seq, tbase;
+    uint32_t seq;
     uint32_t ph[NSTB];
     uint32_t exp_bytes[NSTB];
     bool ok;
     int ev;
 
-    __device__ __forceinline__ uint32_t tag(int l, int st) const { return tbase + (uint32_t)(l * NWS + st) + 1u; }
     __device__ __forceinline__ void trace() {
         if (pp->trace && tid == 0 && ev < MK_TRACE_EVENTS) {
             unsigned long long t;
@@ -536,20 +487,27 @@ struct XkConsumer {
     }
     // This CTA's tiles t = R + NR i of linear L, i in [i0, i1), from the ring: per-warp
     // partial sums to red[i - i0] (group j of a tile goes to warp (tile * G64 + j) % 8).
-    // global tile index of this CTA's i-th tile of L: round robin over the grid, or (qkv) the
-    // rank's share of the QKV row blocks of the cluster's head
-    __device__ __forceinline__ int tile_of(const MkLin &L, int i, bool qkv) const {
-        return qkv ? qkv_rb(rank * QT / CS + i, head, d) : R + i * NR;
+    // global tile index of this CTA's i-th tile of L: round robin over the grid (TM_RR), the
+    // rank's share of the QKV row blocks of the cluster's head (TM_QKV), or of the c_fc row
+    // blocks of the cluster's slice of the MLP (TM_FC: rows [S head, S head + S), S = ff / H)
+    __device__ __forceinline__ int tile_of(const MkLin &L, int i, int mode) const {
+        if (mode == TM_QKV) return qkv_rb(rank * QT / CS + i, head, d);
+        if (mode == TM_FC) return head * (ff / pp->H / 16) + rank + CS * i;
+        return R + i * NR;
     }
-    __device__ __forceinline__ int own_tiles(const MkLin &L, bool qkv) const {
-        if (qkv) return (rank + 1) * QT / CS - rank * QT / CS;
+    __device__ __forceinline__ int own_tiles(const MkLin &L, int mode) const {
+        if (mode == TM_QKV) return (rank + 1) * QT / CS - rank * QT / CS;
+        if (mode == TM_FC) {
+            const int nrb = ff / pp->H / 16;
+            return rank < nrb ? (nrb - 1 - rank) / CS + 1 : 0;
+        }
         const int n = L.n_rb * L.n_kc;
         return R < n ? (n - 1 - R) / NR + 1 : 0;
     }
     // Warp w takes groups w and w + CW of every tile (CW >= 10: at most 2 of the <= 20
     // groups); with one K chunk the two activation fragments stay in registers for the
     // whole stage, otherwise (the K-split mlp projection) they are loaded per tile.
-    __device__ __forceinline__ void tiles(const MkLin &L, const __half *xs, const float *sx, int i0, int i1, bool qkv) {
+    __device__ __forceinline__ void tiles(const MkLin &L, const __half *xs, const float *sx, int i0, int i1, int mode) {
         static_assert(2 * CW >= MK_MAX_KC / 64, "two groups per warp cover a tile");
         const int KC = L.kc, G64 = KC / 64, nkc = L.n_kc;
         const bool half_sb = pp->sbb == 4;
@@ -579,7 +537,7 @@ struct XkConsumer {
                 if (h0) group_x(tq, tsb, KC, G64, j0, xa0, xa1, sa, half_sb, a0, a1);
                 if (h1) group_x(tq, tsb, KC, G64, j1, xb0, xb1, sb, half_sb, a0, a1);
             } else {
-                const int kci = tile_of(L, i, qkv) % nkc;
+                const int kci = tile_of(L, i, mode) % nkc;
                 if (h0) group(tq, tsb, KC, G64, j0, kci * G64 + j0, xs, sx, half_sb, a0, a1);
                 if (h1) group(tq, tsb, KC, G64, j1, kci * G64 + j1, xs, sx, half_sb, a0, a1);
             }
@@ -615,23 +573,23 @@ struct XkConsumer {
     }
     // This thread's epilogue chunk of the first round of run_lin: its bias, loaded before the
     // stage's input wait so that the L2 latency is off the critical path.
-    __device__ __forceinline__ float4 bias_pre(const MkLin &L, bool qkv) const {
-        const int n = min(own_tiles(L, qkv), rt);
+    __device__ __forceinline__ float4 bias_pre(const MkLin &L, int mode) const {
+        const int n = min(own_tiles(L, mode), rt);
         if (tid >= n * 4) return make_float4(0.f, 0.f, 0.f, 0.f);
-        const int t = tile_of(L, tid >> 2, qkv), rb = t / L.n_kc, o = rb * 16 + (tid & 3) * 4;
+        const int t = tile_of(L, tid >> 2, mode), rb = t / L.n_kc, o = rb * 16 + (tid & 3) * 4;
         return o < L.out ? bias4(L, o) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
     // Tiles of one linear, then per 4-row chunk epi(o, kc, v, bias) (o: first output row,
     // kc: K chunk of the tile).  Rows past L.out are skipped.
     template <class Epi>
-    __device__ __forceinline__ void run_lin(const MkLin &L, const __half *xs, const float *sx, float4 bpre, bool qkv,
+    __device__ __forceinline__ void run_lin(const MkLin &L, const __half *xs, const float *sx, float4 bpre, int mode,
                                             Epi epi) {
-        const int n = own_tiles(L, qkv);
+        const int n = own_tiles(L, mode);
         for (int i0 = 0; i0 < n; i0 += rt) {
             const int i1 = min(n, i0 + rt);
-            tiles(L, xs, sx, i0, i1, qkv);
+            tiles(L, xs, sx, i0, i1, mode);
             for (int q = tid; q < (i1 - i0) * 4; q += CT) {
-                const int il = q >> 2, t = tile_of(L, i0 + il, qkv), rb = t / L.n_kc, kci = t - rb * L.n_kc;
+                const int il = q >> 2, t = tile_of(L, i0 + il, mode), rb = t / L.n_kc, kci = t - rb * L.n_kc;
                 const int o = rb * 16 + (q & 3) * 4;
                 if (o < L.out) epi(o, kci, rows4(il, q & 3), i0 == 0 ? bpre : bias4(L, o));
             }
@@ -642,41 +600,15 @@ struct XkConsumer {
 
     // ---- exchanges (cluster rank k gathers its slice of the vector and pushes it to the
     // cluster) ----
-    __device__ __forceinline__ bool poll(PollRuns pr, uint32_t tg, float *stage) {
-        return !ok || poll_runs(pr, tg, stage, pp->err);
-    }
-    // x_l = h + mlp bias + sum over K chunks of the mlp partials (layer l - 1) -> land
-    __device__ __forceinline__ void exchange_x(int lprev, int code) {
+    // land += bias + the fixed-point sum of an accumulator (2^-32 units) -> land of every CTA of
+    // the cluster, once every CTA of the grid has added its partials (counter == NR).  For h:
+    // land holds x and the partials are the heads' c_proj rows; for the next x: land holds h
+    // and the partials are the clusters' mlp K-slices.  A flagged partial (not finite, or out
+    // of the fixed-point range) makes the whole vector NaN, as the reference's fp32 sum would
+    // after the next LayerNorm; the out-of-range case is also reported in the error word.
+    __device__ __forceinline__ void exchange_acc(const unsigned long long *acc, const uint32_t *cnt,
+                                                 const uint32_t *flagp, float4 bpre, const float *bias, int code) {
         const int c0 = slice_lo(rank, d / 4), nch = slice_lo(rank + 1, d / 4) - c0, o0 = c0 * 4;
-        const MkLin &Lm = lay[lprev].mlp;
-        const int nkc = Lm.n_kc;
-        const uint64_t *mp = xp->mp_ll + (size_t)lprev * xp->nkc * d;
-        const float4 bpre = tid < nch ? __ldg(reinterpret_cast<const float4 *>(Lm.bias + o0 + tid * 4))
-                                      : make_float4(0.f, 0.f, 0.f, 0.f);
-        const bool good = poll(PollRuns{mp + o0, d, nch * 2, nkc}, tag(lprev, 4), red);
-        agree(good, code);
-        const uint32_t land_a = su32(land), bar_a = su32(stb + B0);
-        for (int i = tid; i < nch; i += CT) {
-            const int o = o0 + i * 4;
-            float4 acc = *reinterpret_cast<const float4 *>(land + o);
-            const float4 bb = i == tid ? bpre : __ldg(reinterpret_cast<const float4 *>(Lm.bias + o));
-            acc.x += bb.x; acc.y += bb.y; acc.z += bb.z; acc.w += bb.w;
-            for (int k = 0; k < nkc; ++k) {  // fixed order over the K chunks
-                const float4 s4 = *reinterpret_cast<const float4 *>(red + (k * nch + i) * 4);
-                acc.x += s4.x; acc.y += s4.y; acc.z += s4.z; acc.w += s4.w;
-            }
-            bcast_v4(land_a + o * 4, make_uint4(__float_as_uint(acc.x), __float_as_uint(acc.y),
-                                                __float_as_uint(acc.z), __float_as_uint(acc.w)), bar_a);
-        }
-        trace();
-        wait_land(B0, code + 1);
-    }
-    // h = x + c_proj bias + the fixed-point sum of the heads' c_proj partials -> land, once
-    // every CTA of the grid has added its partials (counter)
-    __device__ __forceinline__ void exchange_h(int l, float4 bpre, int code) {
-        const int c0 = slice_lo(rank, d / 4), nch = slice_lo(rank + 1, d / 4) - c0, o0 = c0 * 4;
-        const uint32_t *cnt = xp->hcnt + par * pp->n_layers + l;
-        const unsigned long long *acc = xp->hacc + ((size_t)par * pp->n_layers + l) * d;
         bool good = true;
         if (tid == 0 && ok) {  // one poller per CTA; the barrier in agree() orders the rest
             good = false;
@@ -690,7 +622,7 @@ struct XkConsumer {
         }
         agree(good, code);
         uint32_t flag;
-        asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(flag) : "l"(xp->hflag + par * pp->n_layers + l) : "memory");
+        asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(flag) : "l"(flagp) : "memory");
         // reported in its own error word: the step itself runs to the end on the normal path
         if ((flag & 2u) && tid == 0) atomicExch(pp->err + 1, kXkRangeCode);
         const float fnan = flag ? __int_as_float(0x7fc00000) : 0.f;
@@ -701,69 +633,37 @@ struct XkConsumer {
             asm volatile("ld.relaxed.gpu.global.v2.b64 {%0,%1}, [%2];" : "=l"(q0), "=l"(q1) : "l"(acc + o) : "memory");
             asm volatile("ld.relaxed.gpu.global.v2.b64 {%0,%1}, [%2];" : "=l"(q2), "=l"(q3) : "l"(acc + o + 2) : "memory");
             const float4 x = *reinterpret_cast<const float4 *>(land + o);
+            const float4 bb = i == tid ? bpre : __ldg(reinterpret_cast<const float4 *>(bias + o));
             const float sc = 2.3283064365386963e-10f;  // 2^-32
             const float4 v = make_float4((float)(long long)q0 * sc, (float)(long long)q1 * sc,
                                          (float)(long long)q2 * sc, (float)(long long)q3 * sc);
-            bcast_v4(land_a + o * 4, make_uint4(__float_as_uint(x.x + bpre.x + v.x + fnan), __float_as_uint(x.y + bpre.y + v.y + fnan),
-                                                __float_as_uint(x.z + bpre.z + v.z + fnan), __float_as_uint(x.w + bpre.w + v.w + fnan)),
+            bcast_v4(land_a + o * 4, make_uint4(__float_as_uint(x.x + bb.x + v.x + fnan), __float_as_uint(x.y + bb.y + v.y + fnan),
+                                                __float_as_uint(x.z + bb.z + v.z + fnan), __float_as_uint(x.w + bb.w + v.w + fnan)),
                      bar_a);
         }
         trace();
         wait_land(B0, code + 1);
     }
-    // groups [g0, g1) of 64 values of an fp32 LL vector -> fp16 fragment order -> xs of every
-    // CTA of the cluster; thread (group, c) sends the 32 contiguous bytes of rows
-    // {16 b + 2c, 16 b + 2c + 1, 16 b + 2c + 8, 16 b + 2c + 9 : b < 4}
-    __device__ __forceinline__ void gather_f16(const uint64_t *src, int n_groups, uint32_t tg, __half *xs, float *sx,
-                                               int bar, int code) {
-        const int g0 = slice_lo(rank, n_groups), ng = slice_lo(rank + 1, n_groups) - g0;
-        const bool good = poll(PollRuns{src + (size_t)g0 * 64, 0, ng * 32, 1}, tg, red);
-        agree(good, code);
-        const uint32_t xs_a = su32(xs), sx_a = su32(sx), bar_a = su32(stb + bar);
-        for (int i0 = 0; i0 < ng * 4; i0 += CT) {  // (threads of one group are 4 consecutive lanes)
-            const int i = i0 + tid;
-            const bool in = i < ng * 4;
-            const int gl = (i >> 2) * 64, cc = i & 3;
-            float gs = 0.f;
-            if (in) {
-                const float *s = red + gl + 2 * cc;
-                uint4 v0, v1;
-                v0.x = pack_h2(s[0], s[1]);   v0.y = pack_h2(s[8], s[9]);
-                v0.z = pack_h2(s[16], s[17]); v0.w = pack_h2(s[24], s[25]);
-                v1.x = pack_h2(s[32], s[33]); v1.y = pack_h2(s[40], s[41]);
-                v1.z = pack_h2(s[48], s[49]); v1.w = pack_h2(s[56], s[57]);
-                const __half2 *h0 = reinterpret_cast<const __half2 *>(&v0), *h1 = reinterpret_cast<const __half2 *>(&v1);
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float2 a = __half22float2(h0[e]), b = __half22float2(h1[e]);
-                    gs += (a.x + a.y) + (b.x + b.y);
-                }
-                const uint32_t dst = xs_a + (g0 * 64 + gl + cc * 16) * 2;
-                bcast_v4(dst, v0, bar_a);
-                bcast_v4(dst + 16, v1, bar_a);
-            }
-            gs += __shfl_xor_sync(0xffffffffu, gs, 1);
-            gs += __shfl_xor_sync(0xffffffffu, gs, 2);
-            if (in && cc == 0) {  // the group's fp16 sum
-                const uint32_t sa = sx_a + (g0 + (i >> 2)) * 4;
-#pragma unroll
-                for (int r = 0; r < CS; ++r) st_async_b32(mapa(sa, r), __float_as_uint(gs), mapa(bar_a, r));
-            }
-        }
-        trace();
-        wait_land(bar, code + 1);
+    __device__ __forceinline__ void exchange_h(int l, float4 bpre, int code) {
+        const size_t li = (size_t)par * pp->n_layers + l;
+        exchange_acc(xp->hacc + li * d, xp->hcnt + li, xp->hflag + li, bpre, lay[l].proj.bias, code);
     }
-    __device__ __forceinline__ void exchange_u(int l, int code) {
-        gather_f16(xp->u_ll + (size_t)l * ff, ff / 64, tag(l, 3), xu, sxu, BU, code);
+    // x of layer lprev + 1 = h + mlp bias + the clusters' mlp partials
+    __device__ __forceinline__ void exchange_x(int lprev, int code) {
+        const size_t li = (size_t)par * pp->n_layers + lprev;
+        const int c0 = slice_lo(rank, d / 4), nch = slice_lo(rank + 1, d / 4) - c0;
+        const float *mb = lay[lprev].mlp.bias;
+        const float4 bpre = tid < nch ? __ldg(reinterpret_cast<const float4 *>(mb + c0 * 4 + tid * 4))
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+        exchange_acc(xp->xacc + li * d, xp->xcnt + li, xp->xflag + li, bpre, mb, code);
     }
-
 
     // ---- stages ----
     __device__ __forceinline__ void stage_qkv(int l) {
         const MkParams &p = *pp;
         const MkLayer &Ly = lay[l];
         const LnRegs ln1 = ln_prefetch(Ly.ln1_w, Ly.ln1_b);
-        const float4 bpre = bias_pre(Ly.qkv, true);
+        const float4 bpre = bias_pre(Ly.qkv, TM_QKV);
         if (l == 0) {
             const float *e = p.mel_emb + (size_t)T->tok * d, *ps = p.mel_pos + (size_t)T->pos * d;
             for (int k = tid; k < d; k += CT) land[k] = e[k] + ps[k];
@@ -778,7 +678,7 @@ struct XkConsumer {
         const MkLin &L = Ly.qkv;
         const int active = T->active, slot = T->slot, lold = T->lold, hd = head;
         const uint32_t q_a = su32(qkvh), bar_a = su32(stb + BQ);
-        run_lin(L, xln, sxln, bpre, true, [&](int o, int, float4 v, float4 bb) {
+        run_lin(L, xln, sxln, bpre, TM_QKV, [&](int o, int, float4 v, float4 bb) {
             v.x += bb.x; v.y += bb.y; v.z += bb.z; v.w += bb.w;
             const int which = o / d, oo = o - which * d;
             if (which > 0 && active) {
@@ -1024,10 +924,16 @@ struct XkConsumer {
         }
         trace();
     }
+    // The MLP by slices: cluster c owns the S = ff / H inputs [S c, S c + S) of the mlp
+    // projection.  Its ranks compute those S c_fc rows (TM_FC) and push GELU of them as fp16
+    // into the xu of every CTA of the cluster (fragment order, one mbarrier: S x 2 bytes); then
+    // each rank applies the K-slice of the mlp projection to them for its share of the d
+    // outputs and adds the partials into the next x's fixed-point accumulator.  No vector of
+    // the MLP crosses clusters except the result.
     __device__ __forceinline__ void stage_fc(int l) {
         const MkLayer &Ly = lay[l];
         const LnRegs ln2 = ln_prefetch(Ly.ln2_w, Ly.ln2_b);
-        const float4 bpre = bias_pre(Ly.fc, false);
+        const float4 bpre = bias_pre(Ly.fc, TM_FC);
         const int hc0 = slice_lo(rank, d / 4) * 4;
         const float4 hbias = tid < slice_lo(rank + 1, d / 4) - slice_lo(rank, d / 4)
                                  ? __ldg(reinterpret_cast<const float4 *>(Ly.proj.bias + hc0 + tid * 4))
@@ -1035,35 +941,86 @@ struct XkConsumer {
         exchange_h(l, hbias, 50);
         layernorm(ln2, false);
         const MkLin &L = Ly.fc;
-        uint64_t *u = xp->u_ll + (size_t)l * ff;
-        const uint32_t tg = tag(l, 3);
-        run_lin(L, xln, sxln, bpre, false, [&](int o, int, float4 v, float4 bb) {
-            ll_st2(u + o, gelu_tanh(v.x + bb.x), gelu_tanh(v.y + bb.y), tg);
-            ll_st2(u + o + 2, gelu_tanh(v.z + bb.z), gelu_tanh(v.w + bb.w), tg);
+        const int S = ff / pp->H, lo0 = head * S;
+        const uint32_t xu_a = su32(xu), bar_a = su32(stb + BU);
+        run_lin(L, xln, sxln, bpre, TM_FC, [&](int o, int, float4 v, float4 bb) {
+            // rows o..o+3 of the slice -> positions frag_pos(k), frag_pos(k) + 1 (k = o & 63)
+            // and frag_pos(k + 2), + 1 of their group: two fp16 pairs
+            const int lo = o - lo0, g = lo >> 6, k = lo & 63;
+            const uint32_t p01 = pack_h2(gelu_tanh(v.x + bb.x), gelu_tanh(v.y + bb.y));
+            const uint32_t p23 = pack_h2(gelu_tanh(v.z + bb.z), gelu_tanh(v.w + bb.w));
+            const uint32_t a01 = xu_a + (g * 64 + frag_pos_host(k)) * 2, a23 = xu_a + (g * 64 + frag_pos_host(k + 2)) * 2;
+#pragma unroll
+            for (int r = 0; r < CS; ++r) {
+                st_async_b32(mapa(a01, r), p01, mapa(bar_a, r));
+                st_async_b32(mapa(a23, r), p23, mapa(bar_a, r));
+            }
         });
     }
     __device__ __forceinline__ void stage_mlp(int l) {
-        exchange_u(l, 60);
+        wait_land(BU, 60);
+        const int S = ff / pp->H, G = S / 64;
+        // the slice's group sums (the dequantization offset term), from the fp16 values
+        if (warp < G) {
+            float a = 0.f;
+            const __half2 *u2 = reinterpret_cast<const __half2 *>(xu + warp * 64);
+            const float2 f = __half22float2(u2[lane]);
+            a = f.x + f.y;
+            sxu[warp] = warp_sum(a);
+        }
+        csync();
         const MkLin &L = lay[l].mlp;
-        uint64_t *mp = xp->mp_ll + (size_t)l * xp->nkc * d;
-        const uint32_t tg = tag(l, 4);
-        const int dd = d;
-        run_lin(L, xu, sxu, make_float4(0.f, 0.f, 0.f, 0.f), false, [&](int o, int kci, float4 v, float4) {
-            ll_st2(mp + (size_t)kci * dd + o, v.x, v.y, tg);
-            ll_st2(mp + (size_t)kci * dd + o + 2, v.z, v.w, tg);
-        });
+        const bool half_sb = pp->sbb == 4;
+        const int sub = mk_mlpk_sub_bytes(S, pp->sbb), per_slot = SLOT / sub;
+        const int nrb = L.n_rb, mine = rank < nrb ? (nrb - 1 - rank) / CS + 1 : 0;
+        unsigned long long *acc = xp->xacc + ((size_t)par * pp->n_layers + l) * d;
+        for (int s0 = 0; s0 < mine; s0 += per_slot) {
+            const int ns = min(per_slot, mine - s0), nvg = ns * G;  // virtual groups: (sub-tile, group)
+            const uint32_t slot = seq & (NSLOT - 1);
+            wait_slot(slot, 4);
+            const uint8_t *base = smem + slot * SLOT;
+            for (int vg = warp; vg < nvg; vg += CW) {
+                const int si = vg / G, j = vg - si * G;
+                const uint8_t *tq = base + si * sub, *tsb = tq + 16 * S;
+                float a0 = 0.f, a1 = 0.f;
+                group(tq, tsb, S, G, j, j, xu, sxu, half_sb, a0, a1);
+                if (c == 0) {
+                    red[vg * 16 + g] = a0;
+                    red[vg * 16 + g + 8] = a1;
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mb_arrive(emptyp + slot);  // (every consumer warp, once per slot)
+            ++seq;
+            csync();  // every warp has written its partials
+            for (int q = tid; q < ns * 16; q += CT) {  // per row: the groups in order, then the sum
+                const int si = q >> 4, m = q & 15;
+                float y = 0.f;
+                for (int j = 0; j < G; ++j) y += red[(si * G + j) * 16 + m];
+                const int o = (rank + CS * (s0 + si)) * 16 + m;
+                const bool fin = fabsf(y) < 1073741824.0f;  // |y| < 2^30: no int64 wrap over the slices
+                if (fin) atomicAdd(acc + o, (unsigned long long)__float2ll_rn(y * 4294967296.0f));
+                else atomicOr(xp->xflag + par * pp->n_layers + l, isfinite(y) ? 2u : 1u);
+            }
+            csync();  // red is rewritten by the next slot
+        }
+        __threadfence();
+        csync();
+        if (tid == 0)
+            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(xp->xcnt + par * pp->n_layers + l) : "memory");
+        trace();
     }
     __device__ __forceinline__ void stage_head() {
         const MkParams &p = *pp;
         const LnRegs lnf = ln_prefetch(p.lnf_w, p.lnf_b);
         const LnRegs fin = ln_prefetch(p.fin_w, p.fin_b);
-        const float4 bpre = bias_pre(p.head, false);
+        const float4 bpre = bias_pre(p.head, TM_RR);
         exchange_x(p.n_layers - 1, 70);
         layernorm(lnf, true);
         layernorm(fin, false);
         const MkLin &L = p.head;
         const int V = p.mel_vocab;
-        run_lin(L, xln, sxln, bpre, false, [&](int o, int, float4 v, float4 bb) {
+        run_lin(L, xln, sxln, bpre, TM_RR, [&](int o, int, float4 v, float4 bb) {
             const float vv[4] = {v.x + bb.x, v.y + bb.y, v.z + bb.z, v.w + bb.w};
 #pragma unroll
             for (int e = 0; e < 4; ++e)
@@ -1118,7 +1075,7 @@ __global__ void __launch_bounds__(NT, 1) xk_decode_kernel(const __grid_constant_
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         mb_expect(stb + B0, (uint32_t)p.d * 4);
         mb_expect(stb + BA, 64 * 2 + 4);  // the head's output: fp16 values + their sum
-        mb_expect(stb + BU, (uint32_t)p.ff * 2 + p.ff / 64 * 4);
+        mb_expect(stb + BU, (uint32_t)(p.ff / p.H) * 2);  // the cluster's slice of GELU(c_fc), fp16
         mb_expect(stb + BQ, 3 * 64 * 4);
         mb_expect(stb + BR, CS * REC * 4);  // (waited on by rank 0 only)
         T->active = active;
@@ -1138,11 +1095,16 @@ __global__ void __launch_bounds__(NT, 1) xk_decode_kernel(const __grid_constant_
     {  // the next step's c_proj accumulators and counters (this step's were zeroed by the last)
         const uint32_t q = (epoch & 1u) ^ 1u;
         const size_t n = (size_t)p.n_layers * p.d;
-        unsigned long long *a = xp.hacc + q * n;
-        for (size_t i = (size_t)R * NT + tid; i < n; i += (size_t)NR * NT) a[i] = 0ull;
+        unsigned long long *a = xp.hacc + q * n, *ax = xp.xacc + q * n;
+        for (size_t i = (size_t)R * NT + tid; i < n; i += (size_t)NR * NT) {
+            a[i] = 0ull;
+            ax[i] = 0ull;
+        }
         if (R == 0 && tid < p.n_layers) {
             xp.hcnt[q * p.n_layers + tid] = 0u;
             xp.hflag[q * p.n_layers + tid] = 0u;
+            xp.xcnt[q * p.n_layers + tid] = 0u;
+            xp.xflag[q * p.n_layers + tid] = 0u;
         }
     }
     // every CTA's barriers are armed before any CTA pushes into them
@@ -1199,13 +1161,12 @@ __global__ void __launch_bounds__(NT, 1) xk_decode_kernel(const __grid_constant_
         C.H = p.H;
         C.rt = xp.rt;
         C.seq = 0;
-        C.tbase = epoch * (uint32_t)(NWS * p.n_layers);
         C.ok = true;
         C.ev = 0;
         for (int b = 0; b < NSTB; ++b) C.ph[b] = 0;
         C.exp_bytes[B0] = (uint32_t)p.d * 4;
         C.exp_bytes[BA] = 64 * 2 + 4;
-        C.exp_bytes[BU] = (uint32_t)p.ff * 2 + p.ff / 64 * 4;
+        C.exp_bytes[BU] = (uint32_t)(p.ff / p.H) * 2;
         C.exp_bytes[BQ] = 3 * 64 * 4;
         C.exp_bytes[BR] = CS * REC * 4;
         for (int l = 0; l < p.n_layers; ++l) {
@@ -1255,15 +1216,14 @@ int xk_config(const ModelView &m, XkConfig *out) {
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    int nkc = 0;
     for (int l = 0; l < m.n_layers; ++l) {
         const MkLayer &L = m.layers[l];
         for (const MkLin *x : {&L.qkv, &L.proj, &L.fc, &L.mlp})
             if (x->tile_bytes > SLOT || x->kc % 64) return -1;
-        if (L.qkv.n_kc != 1 || L.proj.n_kc != 1 || L.fc.n_kc != 1 || L.mlp.n_kc > 4) return -1;
+        if (L.qkv.n_kc != 1 || L.proj.n_kc != 1 || L.fc.n_kc != 1) return -1;
         if (!L.proj_h || (L.proj.n_rb + CS - 1) / CS * mk_projh_chunk_bytes(L.proj.sbb) > SLOT) return -1;
         if (L.qkv.out != 3 * m.d || L.proj.out != m.d || L.fc.out != m.ff || L.mlp.out != m.d) return -1;
-        nkc = std::max(nkc, L.mlp.n_kc);
+        if (!L.mlp_k || !mlp_slice_ok(L.mlp, m.n_heads)) return -1;
     }
     if (m.mel_head.tile_bytes > SLOT || m.mel_head.n_kc != 1) return -1;
     // grid: one CS-CTA cluster per attention head, all resident at once
@@ -1298,7 +1258,7 @@ int xk_config(const ModelView &m, XkConfig *out) {
     int rt = 1;
     for (int l = 0; l < m.n_layers; ++l) {
         const MkLayer &L = m.layers[l];
-        for (const MkLin *x : {&L.qkv, &L.proj, &L.fc, &L.mlp}) rt = std::max(rt, xk_tiles_of(*x, grid));
+        for (const MkLin *x : {&L.qkv, &L.proj, &L.fc}) rt = std::max(rt, xk_tiles_of(*x, grid));
     }
     rt = std::max(rt, (QT + CS - 1) / CS);  // this rank's share of the head's QKV row blocks
     rt = std::min(rt, rt_guess);
@@ -1325,7 +1285,6 @@ int xk_config(const ModelView &m, XkConfig *out) {
     }
     out->grid = grid;
     out->rt = rt;
-    out->nkc = nkc;
     out->coop = coop ? 1 : 0;
     if (getenv("ITTS_DEBUG"))
         fprintf(stderr, "[itts] clustered decode kernel: grid %d (%d-CTA clusters, %s), %zu B shared memory, rt %d\n",
@@ -1339,11 +1298,11 @@ cudaError_t xk_launch(const MkParams &p, const XkConfig &xc, const XkBufs &b, cu
     xp.hacc = b.hacc;
     xp.hcnt = b.hcnt;
     xp.hflag = b.hflag;
-    xp.u_ll = b.u_ll;
-    xp.mp_ll = b.mp_ll;
+    xp.xacc = b.xacc;
+    xp.xcnt = b.xcnt;
+    xp.xflag = b.xflag;
     xp.epoch = b.epoch;
     xp.rt = xc.rt;
-    xp.nkc = xc.nkc;
     xp.dry = 0;
     return xk_launch_cfg(xp, xc.grid, xk_layout(p.d, p.ff, xc.rt, p.n_layers).total, xc.coop != 0, st);
 }
@@ -1365,6 +1324,48 @@ __global__ void proj_by_head_kernel(const uint8_t *tiles, int tile_bytes, int kc
         reinterpret_cast<uint32_t *>(o + 16 * 64 + m * sbb)[w] =
             reinterpret_cast<const uint32_t *>(t + 16 * kc + (size_t)(m * G64 + h) * sbb)[w];
     }
+}
+
+// sub-tile (cluster c, row block rb) of the sliced mlp copy (MkLayer::mlp_k) from tile
+// (rb, kc) with kc = S c / KC: each row's S bytes of the slice (its groups keep their slots:
+// the row-parity swizzle stays inside the slice, whose group count is even), then the rows'
+// (scale, offset) pairs of the slice's groups; placed in the copy so that each rank's
+// sub-tiles (row blocks rank, rank + 6, ...) are contiguous
+__global__ void mlp_by_slice_kernel(const uint8_t *tiles, int tile_bytes, int kc, int n_kc, int sbb, int S,
+                                    uint8_t *dst) {
+    const int rb = blockIdx.x, c = blockIdx.y, n_rb = gridDim.x, G = S / 64, G64 = kc / 64;
+    const int kci = S * c / kc, q = (S * c - kci * kc) / 64;
+    const uint8_t *t = tiles + ((size_t)rb * n_kc + kci) * tile_bytes;
+    const int sub = mk_mlpk_sub_bytes(S, sbb);
+    uint8_t *o = dst + mk_mlpk_rank_offset(n_rb, S, sbb, c, rb % 6) + (size_t)(rb / 6) * sub;
+    const int wpr = S / 4;  // words per row
+    for (int i = threadIdx.x; i < 16 * wpr; i += blockDim.x) {
+        const int m = i / wpr, w = i - m * wpr;
+        reinterpret_cast<uint32_t *>(o + m * S)[w] = reinterpret_cast<const uint32_t *>(t + (size_t)m * kc + q * 64)[w];
+    }
+    const int spw = sbb / 4;  // words per (scale, offset) pair
+    for (int i = threadIdx.x; i < 16 * G * spw; i += blockDim.x) {
+        const int m = i / (G * spw), r = i - m * G * spw, j = r / spw, w = r - j * spw;
+        reinterpret_cast<uint32_t *>(o + 16 * S + (m * G + j) * sbb)[w] =
+            reinterpret_cast<const uint32_t *>(t + 16 * kc + (size_t)(m * G64 + q + j) * sbb)[w];
+    }
+}
+
+bool mlp_slice_ok(const MkLin &W, int n_heads) {
+    const int S = W.in / n_heads;
+    return n_heads > 0 && W.in % n_heads == 0 && S % 128 == 0 && W.kc % S == 0 &&
+           mk_mlpk_sub_bytes(S, W.sbb) <= SLOT && (SLOT / mk_mlpk_sub_bytes(S, W.sbb)) * (S / 64) <= 2 * CW;
+}
+
+size_t mlp_slice_bytes(const MkLin &W, int n_heads) {
+    return (size_t)n_heads * W.n_rb * mk_mlpk_sub_bytes(W.in / n_heads, W.sbb);
+}
+
+cudaError_t make_mlp_by_slice(const MkLin &W, int n_heads, uint8_t *dst, cudaStream_t st) {
+    if (!mlp_slice_ok(W, n_heads)) return cudaErrorInvalidValue;
+    mlp_by_slice_kernel<<<dim3(W.n_rb, n_heads), 128, 0, st>>>(W.tiles, W.tile_bytes, W.kc, W.n_kc, W.sbb,
+                                                               W.in / n_heads, dst);
+    return cudaGetLastError();
 }
 
 cudaError_t make_proj_by_head(const MkLin &W, int n_heads, uint8_t *dst, cudaStream_t st) {
