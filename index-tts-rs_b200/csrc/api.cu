@@ -793,16 +793,12 @@ extern "C" int itts_kv_create(itts_gpt *g, int32_t max_seq, int32_t max_batch, i
         XkConfig xc;
         if (e == cudaSuccess && xk_config(m, &xc) > 0) {
             const size_t L = m.n_layers;
-            const size_t bytes = sizeof(unsigned long long) * 4 * L * m.d + sizeof(uint32_t) * (8 * L + xc.grid);
+            const size_t bytes = sizeof(unsigned long long) * 4 * L * m.d + sizeof(uint32_t) * xc.grid;
             A((void **)&kv->db.xkb.hacc, bytes);
             if (e == cudaSuccess) {
                 XkBufs &x = kv->db.xkb;
                 x.xacc = x.hacc + 2 * L * m.d;
-                x.hcnt = reinterpret_cast<uint32_t *>(x.xacc + 2 * L * m.d);
-                x.hflag = x.hcnt + 2 * L;
-                x.xcnt = x.hflag + 2 * L;
-                x.xflag = x.xcnt + 2 * L;
-                x.epoch = x.xflag + 2 * L;
+                x.epoch = reinterpret_cast<uint32_t *>(x.xacc + 2 * L * m.d);
                 e = cudaMemsetAsync(x.hacc, 0, bytes, g->stream);
                 kv->db.xk = xc;
             }
@@ -1304,8 +1300,8 @@ static int check_step_sync(itts_kv *kv) {
     CUDA_TRY(cudaMemcpy(errw, kv->db.err, sizeof(errw), cudaMemcpyDeviceToHost));
     const int err = errw[0] ? errw[0] : errw[1];  // [0]: a bounded wait gave up; [1]: range
     if (err == MK_ERR_RANGE)
-        return set_err(ITTS_E_CUDA, "device error: a c_proj partial of the decode step is finite but "
-                                    "outside the fixed-point accumulator's range (|y| >= 2^30)");
+        return set_err(ITTS_E_CUDA, "device error: a c_proj or mlp partial of the decode step is finite but "
+                                    "outside the fixed-point accumulator's range (|y| >= 2^18)");
     if (err != 0)
         return set_err(ITTS_E_TIMEOUT, "device wait timed out in the decode-step kernel (code " +
                                            std::to_string(err) + ")");

@@ -27,17 +27,13 @@ struct ModelView {
 };
 
 // The clustered all-SM decode step of one column (xk_decode.cu): launch shape and its
-// global exchange buffers (fixed-point accumulators and counters, by step parity).
+// global exchange buffers (counted fixed-point accumulator words, by step parity).
 struct XkConfig {
     int grid = 0, rt = 0, coop = 0;
 };
-struct XkBufs {  // one allocation: [2][L][d] accumulators for h and for x, then the counters
-    unsigned long long *hacc = nullptr;  // fixed-point (2^-32) sums of the heads' c_proj partials, by step parity
+struct XkBufs {  // one allocation: [2][L][d] accumulator words for h and for x, then [grid] launch counters
+    unsigned long long *hacc = nullptr;  // counted fixed-point sums of the heads' c_proj partials, by step parity
     unsigned long long *xacc = nullptr;  // the same for the clusters' mlp partials (the next x)
-    uint32_t *hcnt = nullptr;   // [2][L] CTAs that added their c_proj partials
-    uint32_t *hflag = nullptr;  // [2][L] bit 0: a partial was not finite; bit 1: one was finite
-                                // but outside the fixed-point range (|y| >= 2^30)
-    uint32_t *xcnt = nullptr, *xflag = nullptr;  // [2][L] the same for the mlp partials
     uint32_t *epoch = nullptr;
 };
 

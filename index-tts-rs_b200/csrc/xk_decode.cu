@@ -10,19 +10,22 @@
 // K/V tiles and pushes one (m, l, acc[64]) record into cluster rank 0, which merges them and
 // pushes the head's 64 outputs (fp16) back into the cluster.  The cluster then applies the
 // head's 64 columns of c_proj (a head-major copy of its weights made at load) to them and
-// adds each row's partial into a per-step accumulator with 64-bit fixed-point (2^-32)
-// atomics, whose sum does not depend on the order of the adds; a counter tells the h gather
-// when all CTAs have added theirs.  So q/k/v, the attention partials and the attention
-// output never cross clusters.
+// adds each row's partial into a per-step accumulator word with a 64-bit integer add.  The
+// word is a counted fixed-point sum: bits 0..51 the sum of the partials in 2^-28 units
+// (signed), bits 52..57 how many partials have been added, bits 58..63 how many were not
+// representable (not finite, or |y| >= 2^18).  Integer adds do not depend on their order, and
+// the count makes each word self-validating: the reader polls the words it needs until
+// every count is complete, with no fence or separate counter between writer and reader.  So
+// q/k/v, the attention partials and the attention output never cross clusters.
 //
 // The MLP runs by slices of its S = ff / H hidden units (256 for IndexTTS-2.5): cluster c
 // computes the c_fc rows [S c, S c + S), pushes GELU of them (fp16) into every CTA of the
 // cluster, and applies the matching S inputs of the mlp projection (a copy of its weights
 // re-tiled by input slice, made at load) for all d outputs, adding the partials into the
-// next x's fixed-point accumulator.  So the only vectors that cross clusters are h and x,
-// each through an accumulator: once every CTA has counted itself in, rank k of every
-// cluster reads the k-th sixth (adding the residual and the bias) and pushes it into all 6
-// CTAs with st.async; each CTA's mbarrier counts the bytes.  The head tiles are dealt
+// next x's accumulator words.  So the only vectors that cross clusters are h and x, each
+// through its accumulator: rank k of every cluster polls the k-th sixth of the words until
+// all H partials of each are in, adds the residual and the bias, and pushes the result into
+// all 6 CTAs with st.async; each CTA's mbarrier counts the bytes.  The head tiles are dealt
 // round-robin over the grid (tile t on CTA t % grid).
 //
 // Per CTA: 11 consumer warps + 1 producer warp.  The producer lane streams the CTA's weight
@@ -58,7 +61,14 @@ constexpr int KVPOS = 84;          // positions per K/V tile: 2 x 84 x 128 B = 2
 constexpr int REC = 68;            // floats per attention record: m, l, 0, 0, acc[64]
 constexpr int QT = 12;             // QKV row blocks of one head (q, k, v x 64 rows / 16)
 constexpr uint32_t SPIN = 1u << 22;
-constexpr int kXkRangeCode = MK_ERR_RANGE;  // error word: a c_proj partial outside the fixed-point range
+constexpr int kXkRangeCode = MK_ERR_RANGE;  // error word: a partial outside the fixed-point range
+// counted fixed-point accumulator words (see the top of the file)
+// (2^-28 resolution: coarser units change the fp16 rounding of some activations downstream)
+constexpr float kFxScale = 268435456.0f;                // 2^28 units
+constexpr float kFxLimit = 262144.0f;                   // |partial| < 2^18: 31 of them stay below 2^51
+constexpr unsigned long long kFxOne = 1ull << 52;       // one partial added
+constexpr unsigned long long kFxBad = 1ull << 58;       // one partial not representable
+constexpr int kFxMaxParts = 31;                         // partials per word (heads)
 constexpr float kLog2e = 1.4426950408889634f;
 
 // landing barriers: x/h (fp32), the head's attention output (fp16 + its sum), u (fp16), the
@@ -201,14 +211,9 @@ __host__ __device__ inline XkSmem xk_layout(int d, int ff, int rt, int n_layers)
 
 struct XkParams {
     MkParams p;          // model, slots, KV cache, logits, err, trace
-    unsigned long long *hacc;  // [2][L][d] sums of the heads' c_proj partials, fixed point 2^-32,
+    unsigned long long *hacc;  // [2][L][d] counted fixed-point sums of the heads' c_proj partials,
                                // by step parity (this step's buffer p = epoch & 1; 1 - p zeroed)
-    uint32_t *hcnt;            // [2][L] CTAs that added their partials
-    uint32_t *hflag;           // [2][L] partials left out of the sum: bit 0 not finite, bit 1
-                               // finite but |y| >= 2^30 (the sum of 20 heads could wrap)
-    unsigned long long *xacc;  // [2][L][d] sums of the clusters' mlp partials (next x), as hacc
-    uint32_t *xcnt;            // [2][L] CTAs that added their mlp partials
-    uint32_t *xflag;           // [2][L] as hflag
+    unsigned long long *xacc;  // [2][L][d] the same for the clusters' mlp partials (next x)
     uint32_t *epoch;     // [grid] launches completed per CTA
     int rt, dry;
 };
@@ -600,45 +605,59 @@ struct XkConsumer {
 
     // ---- exchanges (cluster rank k gathers its slice of the vector and pushes it to the
     // cluster) ----
-    // land += bias + the fixed-point sum of an accumulator (2^-32 units) -> land of every CTA of
-    // the cluster, once every CTA of the grid has added its partials (counter == NR).  For h:
-    // land holds x and the partials are the heads' c_proj rows; for the next x: land holds h
-    // and the partials are the clusters' mlp K-slices.  A flagged partial (not finite, or out
-    // of the fixed-point range) makes the whole vector NaN, as the reference's fp32 sum would
-    // after the next LayerNorm; the out-of-range case is also reported in the error word.
-    __device__ __forceinline__ void exchange_acc(const unsigned long long *acc, const uint32_t *cnt,
-                                                 const uint32_t *flagp, float4 bpre, const float *bias, int code) {
-        const int c0 = slice_lo(rank, d / 4), nch = slice_lo(rank + 1, d / 4) - c0, o0 = c0 * 4;
-        bool good = true;
-        if (tid == 0 && ok) {  // one poller per CTA; the barrier in agree() orders the rest
-            good = false;
-            for (uint32_t it = 0; it < SPIN; ++it) {
-                uint32_t v;
-                asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(cnt) : "memory");
-                if (v >= (uint32_t)NR) { good = true; break; }
-                if ((it & 255u) == 255u && *(volatile const int *)pp->err) break;
-                if (it >= 8) __nanosleep(it < 32 ? 32u : 128u);
-            }
+    // one partial into a counted fixed-point accumulator word; a partial that is not finite or
+    // too large adds only to the count and the "not representable" field (the reader then
+    // yields NaN for the row, as the reference's fp32 sum would give NaN or a value the next
+    // LayerNorm spreads to every output); the finite case is also reported in the error word
+    __device__ __forceinline__ void add_part(unsigned long long *a, float y) const {
+        unsigned long long v = kFxOne;
+        if (fabsf(y) < kFxLimit) {
+            v += (unsigned long long)__float2ll_rn(y * kFxScale);
+        } else {
+            v += kFxBad;
+            if (isfinite(y)) atomicExch(pp->err + 1, kXkRangeCode);
         }
-        agree(good, code);
-        uint32_t flag;
-        asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(flag) : "l"(flagp) : "memory");
-        // reported in its own error word: the step itself runs to the end on the normal path
-        if ((flag & 2u) && tid == 0) atomicExch(pp->err + 1, kXkRangeCode);
-        const float fnan = flag ? __int_as_float(0x7fc00000) : 0.f;
+        asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(a), "l"(v) : "memory");
+    }
+    // land += bias + the accumulated partials -> land of every CTA of the cluster.  Each of the
+    // slice's threads polls its 4 words until all H partials of each are in, then pushes.  For
+    // h: land holds x and the partials are the heads' c_proj rows; for the next x: land holds
+    // h and the partials are the clusters' mlp slices.
+    __device__ __forceinline__ void exchange_acc(const unsigned long long *acc, float4 bpre, const float *bias,
+                                                 int code) {
+        const int c0 = slice_lo(rank, d / 4), nch = slice_lo(rank + 1, d / 4) - c0, o0 = c0 * 4;
         const uint32_t land_a = su32(land), bar_a = su32(stb + B0);
-        for (int i = tid; i < nch; i += CT) {
+        const long long want = pp->H;
+        for (int i = tid; i < nch && ok; i += CT) {
             const int o = o0 + i * 4;
-            unsigned long long q0, q1, q2, q3;
-            asm volatile("ld.relaxed.gpu.global.v2.b64 {%0,%1}, [%2];" : "=l"(q0), "=l"(q1) : "l"(acc + o) : "memory");
-            asm volatile("ld.relaxed.gpu.global.v2.b64 {%0,%1}, [%2];" : "=l"(q2), "=l"(q3) : "l"(acc + o + 2) : "memory");
+            long long q[4];
+            bool done = false;
+            for (uint32_t it = 0; it < SPIN; ++it) {
+                asm volatile("ld.relaxed.gpu.global.v2.b64 {%0,%1}, [%2];" : "=l"(q[0]), "=l"(q[1]) : "l"(acc + o) : "memory");
+                asm volatile("ld.relaxed.gpu.global.v2.b64 {%0,%1}, [%2];" : "=l"(q[2]), "=l"(q[3]) : "l"(acc + o + 2) : "memory");
+                // count field (bits 52..57) of each word, the signed sum below it taken out
+                done = true;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) done &= (((q[e] + (1ll << 51)) >> 52) & 63) == want;
+                if (done) break;
+                if ((it & 255u) == 255u && *(volatile const int *)pp->err) break;
+                if (it >= 4) __nanosleep(it < 64 ? 20u : 100u);
+            }
+            if (!done) {
+                fail(code);
+                break;
+            }
             const float4 x = *reinterpret_cast<const float4 *>(land + o);
             const float4 bb = i == tid ? bpre : __ldg(reinterpret_cast<const float4 *>(bias + o));
-            const float sc = 2.3283064365386963e-10f;  // 2^-32
-            const float4 v = make_float4((float)(long long)q0 * sc, (float)(long long)q1 * sc,
-                                         (float)(long long)q2 * sc, (float)(long long)q3 * sc);
-            bcast_v4(land_a + o * 4, make_uint4(__float_as_uint(x.x + bb.x + v.x + fnan), __float_as_uint(x.y + bb.y + v.y + fnan),
-                                                __float_as_uint(x.z + bb.z + v.z + fnan), __float_as_uint(x.w + bb.w + v.w + fnan)),
+            float v[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const long long m = (q[e] + (1ll << 51)) >> 52;  // count + 64 x not-representable
+                const long long sum = q[e] - (m << 52);
+                v[e] = (m >> 6) ? __int_as_float(0x7fc00000) : (float)sum * (1.0f / kFxScale);
+            }
+            bcast_v4(land_a + o * 4, make_uint4(__float_as_uint(x.x + bb.x + v[0]), __float_as_uint(x.y + bb.y + v[1]),
+                                                __float_as_uint(x.z + bb.z + v[2]), __float_as_uint(x.w + bb.w + v[3])),
                      bar_a);
         }
         trace();
@@ -646,7 +665,7 @@ struct XkConsumer {
     }
     __device__ __forceinline__ void exchange_h(int l, float4 bpre, int code) {
         const size_t li = (size_t)par * pp->n_layers + l;
-        exchange_acc(xp->hacc + li * d, xp->hcnt + li, xp->hflag + li, bpre, lay[l].proj.bias, code);
+        exchange_acc(xp->hacc + li * d, bpre, lay[l].proj.bias, code);
     }
     // x of layer lprev + 1 = h + mlp bias + the clusters' mlp partials
     __device__ __forceinline__ void exchange_x(int lprev, int code) {
@@ -655,7 +674,7 @@ struct XkConsumer {
         const float *mb = lay[lprev].mlp.bias;
         const float4 bpre = tid < nch ? __ldg(reinterpret_cast<const float4 *>(mb + c0 * 4 + tid * 4))
                                       : make_float4(0.f, 0.f, 0.f, 0.f);
-        exchange_acc(xp->xacc + li * d, xp->xcnt + li, xp->xflag + li, bpre, mb, code);
+        exchange_acc(xp->xacc + li * d, bpre, mb, code);
     }
 
     // ---- stages ----
@@ -901,26 +920,13 @@ struct XkConsumer {
                 const float y1 = fmaf(s1, d0[2] + d1[2], fmaf(-1024.0f, s1, z1) * hsum);
                 if (c == 0) {
                     const int o = (r0 + i) * 16;
-                    // |y| < 2^30 keeps the sum of the 20 heads' partials inside int64 at 2^-32
-                    // units; a NaN, an infinity or a larger value is flagged instead of added
-                    // (the h gather then yields NaN, as the reference's fp32 sum would for a
-                    // non-finite partial, and reports the out-of-range case as an error)
-                    const bool f0 = fabsf(y0) < 1073741824.0f, f1 = fabsf(y1) < 1073741824.0f;
-                    if (f0) atomicAdd(acc + o + g, (unsigned long long)__float2ll_rn(y0 * 4294967296.0f));
-                    if (f1) atomicAdd(acc + o + g + 8, (unsigned long long)__float2ll_rn(y1 * 4294967296.0f));
-                    if (!(f0 && f1))
-                        atomicOr(xp->hflag + par * pp->n_layers + l,
-                                 (f0 || isfinite(y0)) && (f1 || isfinite(y1)) ? 2u : 1u);
+                    add_part(acc + o + g, y0);
+                    add_part(acc + o + g + 8, y1);
                 }
             }
             __syncwarp();
             if (lane == 0) mb_arrive(emptyp + slot);
             ++seq;
-        }
-        __threadfence();
-        csync();
-        if (tid == 0) {
-            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(xp->hcnt + par * pp->n_layers + l) : "memory");
         }
         trace();
     }
@@ -997,17 +1003,10 @@ struct XkConsumer {
                 const int si = q >> 4, m = q & 15;
                 float y = 0.f;
                 for (int j = 0; j < G; ++j) y += red[(si * G + j) * 16 + m];
-                const int o = (rank + CS * (s0 + si)) * 16 + m;
-                const bool fin = fabsf(y) < 1073741824.0f;  // |y| < 2^30: no int64 wrap over the slices
-                if (fin) atomicAdd(acc + o, (unsigned long long)__float2ll_rn(y * 4294967296.0f));
-                else atomicOr(xp->xflag + par * pp->n_layers + l, isfinite(y) ? 2u : 1u);
+                add_part(acc + (rank + CS * (s0 + si)) * 16 + m, y);
             }
             csync();  // red is rewritten by the next slot
         }
-        __threadfence();
-        csync();
-        if (tid == 0)
-            asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(xp->xcnt + par * pp->n_layers + l) : "memory");
         trace();
     }
     __device__ __forceinline__ void stage_head() {
@@ -1092,19 +1091,13 @@ __global__ void __launch_bounds__(NT, 1) xk_decode_kernel(const __grid_constant_
     }
     __syncthreads();
     const uint32_t epoch = xp.epoch[R];
-    {  // the next step's c_proj accumulators and counters (this step's were zeroed by the last)
+    {  // the next step's accumulator words (this step's were zeroed by the last)
         const uint32_t q = (epoch & 1u) ^ 1u;
         const size_t n = (size_t)p.n_layers * p.d;
         unsigned long long *a = xp.hacc + q * n, *ax = xp.xacc + q * n;
         for (size_t i = (size_t)R * NT + tid; i < n; i += (size_t)NR * NT) {
             a[i] = 0ull;
             ax[i] = 0ull;
-        }
-        if (R == 0 && tid < p.n_layers) {
-            xp.hcnt[q * p.n_layers + tid] = 0u;
-            xp.hflag[q * p.n_layers + tid] = 0u;
-            xp.xcnt[q * p.n_layers + tid] = 0u;
-            xp.xflag[q * p.n_layers + tid] = 0u;
         }
     }
     // every CTA's barriers are armed before any CTA pushes into them
@@ -1210,7 +1203,7 @@ int xk_config(const ModelView &m, XkConfig *out) {
     const char *off = getenv("ITTS_XK");
     if (off && off[0] == '0') return -1;
     if (m.n_layers < 1 || m.d > MK_MAX_KC || m.d % 64 || m.ff % 64 || m.n_heads * 64 != m.d || m.d / 4 < CS ||
-        m.ff / 64 < CS)
+        m.ff / 64 < CS || m.n_heads > kFxMaxParts)
         return -1;
     int dev = 0, optin = 0, sms = 0;
     cudaGetDevice(&dev);
@@ -1296,11 +1289,7 @@ cudaError_t xk_launch(const MkParams &p, const XkConfig &xc, const XkBufs &b, cu
     XkParams xp{};
     xp.p = p;
     xp.hacc = b.hacc;
-    xp.hcnt = b.hcnt;
-    xp.hflag = b.hflag;
     xp.xacc = b.xacc;
-    xp.xcnt = b.xcnt;
-    xp.xflag = b.xflag;
     xp.epoch = b.epoch;
     xp.rt = xc.rt;
     xp.dry = 0;

@@ -399,16 +399,18 @@ def test_full_size_greedy_generate(full):
 
 # ---------------------------------------------------------------------------
 # non-finite and out-of-range values in the batch-1 cluster kernel's c_proj, whose
-# per-head partials are summed as 64-bit fixed-point integers
+# per-head partials are summed as counted 64-bit fixed-point integers
 # ---------------------------------------------------------------------------
-def test_nonfinite_cproj_partial_propagates(small_weights, small_cfg):
-    """A NaN scale in one c_proj row makes that row's partial NaN.  The reference's fp32 sum
-    carries it into h, and the LayerNorm after it spreads it to every logit; the device
-    step must give all-NaN logits too, not a finite value from a wrapped integer sum."""
+@pytest.mark.parametrize("name", ["gpt.h.1.attn.c_proj.scales", "gpt.h.1.mlp.c_proj.scales"])
+def test_nonfinite_cproj_partial_propagates(small_weights, small_cfg, name):
+    """A NaN scale in one row of the attention's or the MLP's c_proj makes that row's partial
+    NaN.  The reference's fp32 sum carries it into h (or the next x), and the LayerNorm
+    after it spreads it to every logit; the device step must give all-NaN logits too, not a
+    finite value from a wrapped integer sum."""
     w = dict(small_weights)
-    sc = w["gpt.h.1.attn.c_proj.scales"].copy()
+    sc = w[name].copy()
     sc[5, 2] = np.float16(np.nan)
-    w["gpt.h.1.attn.c_proj.scales"] = sc
+    w[name] = sc
     gpt = ig.Gpt.from_weights(w, device=0)
     try:
         om = orc.OracleModel(w)
@@ -428,9 +430,9 @@ def test_nonfinite_cproj_partial_propagates(small_weights, small_cfg):
 
 
 def test_cproj_partial_out_of_fixed_point_range_is_an_error():
-    """A finite c_proj partial of 2^30 or more cannot be summed exactly in the 2^-32 fixed
-    point: the step reports a device error instead of a wrapped value, and the next steps
-    on a sound model in the same process are correct."""
+    """A finite c_proj partial of 2^18 or more does not fit the counted 2^-28 fixed-point
+    accumulator word: the step reports a device error instead of a wrapped value, and the
+    next steps on a sound model in the same process are correct."""
     cfg32 = ModelConfig(n_layers=2, d=256, ff=1024, text_vocab=500, sb_half=False)
     w = make_weights(cfg32, seed=3, ln_beta_std=0.02)
     w["gpt.h.0.attn.c_proj.scales"] = w["gpt.h.0.attn.c_proj.scales"].copy()
