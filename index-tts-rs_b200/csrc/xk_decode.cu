@@ -177,7 +177,6 @@ struct XkSmem {
 __host__ __device__ inline uint32_t xk_red_bytes(int rt, int d, int ff) {
     uint32_t m = (uint32_t)rt * CW * 16 * 4;                                   // tile partial sums
     m = max(m, (uint32_t)(CW + 1) * REC * 4);                                  // attention warp states
-    m = max(m, (uint32_t)2 * CW * 16 * 4);                                     // mlp slice partial sums
     return m;
 }
 struct XkTab {
@@ -963,16 +962,18 @@ struct XkConsumer {
             }
         });
     }
+    // Each warp applies whole sub-tiles (16 rows x the slice's S inputs: sub-tile i of this
+    // rank's run goes to warp i % CW), so a row's partial is complete in one lane and goes
+    // straight into the accumulator word; every warp still waits for each slot before
+    // releasing it, so that its release counts towards the slot's current use.
     __device__ __forceinline__ void stage_mlp(int l) {
         wait_land(BU, 60);
         const int S = ff / pp->H, G = S / 64;
         // the slice's group sums (the dequantization offset term), from the fp16 values
         if (warp < G) {
-            float a = 0.f;
             const __half2 *u2 = reinterpret_cast<const __half2 *>(xu + warp * 64);
             const float2 f = __half22float2(u2[lane]);
-            a = f.x + f.y;
-            sxu[warp] = warp_sum(a);
+            sxu[warp] = warp_sum(f.x + f.y);
         }
         csync();
         const MkLin &L = lay[l].mlp;
@@ -981,31 +982,23 @@ struct XkConsumer {
         const int nrb = L.n_rb, mine = rank < nrb ? (nrb - 1 - rank) / CS + 1 : 0;
         unsigned long long *acc = xp->xacc + ((size_t)par * pp->n_layers + l) * d;
         for (int s0 = 0; s0 < mine; s0 += per_slot) {
-            const int ns = min(per_slot, mine - s0), nvg = ns * G;  // virtual groups: (sub-tile, group)
+            const int ns = min(per_slot, mine - s0);
             const uint32_t slot = seq & (NSLOT - 1);
             wait_slot(slot, 4);
             const uint8_t *base = smem + slot * SLOT;
-            for (int vg = warp; vg < nvg; vg += CW) {
-                const int si = vg / G, j = vg - si * G;
+            for (int si = (warp + CW - s0 % CW) % CW; si < ns; si += CW) {
                 const uint8_t *tq = base + si * sub, *tsb = tq + 16 * S;
                 float a0 = 0.f, a1 = 0.f;
-                group(tq, tsb, S, G, j, j, xu, sxu, half_sb, a0, a1);
+                for (int j = 0; j < G; ++j) group(tq, tsb, S, G, j, j, xu, sxu, half_sb, a0, a1);
                 if (c == 0) {
-                    red[vg * 16 + g] = a0;
-                    red[vg * 16 + g + 8] = a1;
+                    const int o = (rank + CS * (s0 + si)) * 16;
+                    add_part(acc + o + g, a0);
+                    add_part(acc + o + g + 8, a1);
                 }
             }
             __syncwarp();
             if (lane == 0) mb_arrive(emptyp + slot);  // (every consumer warp, once per slot)
             ++seq;
-            csync();  // every warp has written its partials
-            for (int q = tid; q < ns * 16; q += CT) {  // per row: the groups in order, then the sum
-                const int si = q >> 4, m = q & 15;
-                float y = 0.f;
-                for (int j = 0; j < G; ++j) y += red[(si * G + j) * 16 + m];
-                add_part(acc + (rank + CS * (s0 + si)) * 16 + m, y);
-            }
-            csync();  // red is rewritten by the next slot
         }
         trace();
     }
@@ -1342,8 +1335,7 @@ __global__ void mlp_by_slice_kernel(const uint8_t *tiles, int tile_bytes, int kc
 
 bool mlp_slice_ok(const MkLin &W, int n_heads) {
     const int S = W.in / n_heads;
-    return n_heads > 0 && W.in % n_heads == 0 && S % 128 == 0 && W.kc % S == 0 &&
-           mk_mlpk_sub_bytes(S, W.sbb) <= SLOT && (SLOT / mk_mlpk_sub_bytes(S, W.sbb)) * (S / 64) <= 2 * CW;
+    return n_heads > 0 && W.in % n_heads == 0 && S % 128 == 0 && W.kc % S == 0 && mk_mlpk_sub_bytes(S, W.sbb) <= SLOT;
 }
 
 size_t mlp_slice_bytes(const MkLin &W, int n_heads) {
