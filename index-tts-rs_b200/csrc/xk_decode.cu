@@ -434,33 +434,10 @@ struct XkConsumer {
     }
 
     // ---- GEMV tiles ----
-    __device__ __forceinline__ void group(const uint8_t *tq, const uint8_t *tsb, int KC, int G64, int j, int gg,
-                                          const __half *xs, const float *sx, bool half_sb, float &a0, float &a1) {
-        const int jj = j ^ (g & 1);
-        const uint4 wa = *reinterpret_cast<const uint4 *>(tq + g * KC + jj * 64 + c * 16);
-        const uint4 wb = *reinterpret_cast<const uint4 *>(tq + (g + 8) * KC + jj * 64 + c * 16);
-        const uint4 x0 = *reinterpret_cast<const uint4 *>(xs + gg * 64 + c * 16);
-        const uint4 x1 = *reinterpret_cast<const uint4 *>(xs + gg * 64 + c * 16 + 8);
-        float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
-        mma16816(d0, lo_h(wa.x), lo_h(wb.x), hi_h(wa.x), hi_h(wb.x), x0.x, x0.y);
-        mma16816(d1, lo_h(wa.y), lo_h(wb.y), hi_h(wa.y), hi_h(wb.y), x0.z, x0.w);
-        mma16816(d0, lo_h(wa.z), lo_h(wb.z), hi_h(wa.z), hi_h(wb.z), x1.x, x1.y);
-        mma16816(d1, lo_h(wa.w), lo_h(wb.w), hi_h(wa.w), hi_h(wb.w), x1.z, x1.w);
-        float s0, z0, s1, z1;
-        if (half_sb) {
-            const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(tsb + (g * G64 + j) * 4));
-            const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(tsb + ((g + 8) * G64 + j) * 4));
-            s0 = f0.x; z0 = f0.y; s1 = f1.x; z1 = f1.y;
-        } else {
-            const float2 f0 = *reinterpret_cast<const float2 *>(tsb + (g * G64 + j) * 8);
-            const float2 f1 = *reinterpret_cast<const float2 *>(tsb + ((g + 8) * G64 + j) * 8);
-            s0 = f0.x; z0 = f0.y; s1 = f1.x; z1 = f1.y;
-        }
-        const float sxg = sx[gg];
-        a0 += fmaf(s0, d0[0] + d1[0], fmaf(-1024.0f, s0, z0) * sxg);
-        a1 += fmaf(s1, d0[2] + d1[2], fmaf(-1024.0f, s1, z1) * sxg);
-    }
-    // the same with the activation fragment (x0, x1) and its group sum already in registers
+    // one quantization group j (64 inputs) of a 16-row tile (row pitch KC bytes, G64 groups
+    // per row) against the activation fragment (x0, x1) and its group sum: per-row partials
+    // into a0 (row g) and a1 (row g + 8), int8 -> fp16 by byte permutation, y = s acc + (b -
+    // 1024 s) sum(x)
     __device__ __forceinline__ void group_x(const uint8_t *tq, const uint8_t *tsb, int KC, int G64, int j, uint4 x0,
                                             uint4 x1, float sxg, bool half_sb, float &a0, float &a1) {
         const int jj = j ^ (g & 1);
@@ -484,10 +461,20 @@ struct XkConsumer {
         a0 += fmaf(s0, d0[0] + d1[0], fmaf(-1024.0f, s0, z0) * sxg);
         a1 += fmaf(s1, d0[2] + d1[2], fmaf(-1024.0f, s1, z1) * sxg);
     }
-    __device__ __forceinline__ void wait_slot(uint32_t slot, int code) {
-        bool good = !ok || mb_wait<false>(fullp + slot, (seq / NSLOT) & 1u, pp->err);
+    __device__ __forceinline__ void wait_slot(uint32_t slot, int code) { wait_seq(seq, code); }
+    // the copy of ring sequence number sq (slot sq % NSLOT, use sq / NSLOT) has landed
+    __device__ __forceinline__ void wait_seq(uint32_t sq, int code) {
+        bool good = !ok || mb_wait<false>(fullp + (sq & (NSLOT - 1)), (sq / NSLOT) & 1u, pp->err);
         good = __all_sync(0xffffffffu, good);
         if (!good) fail(code);
+    }
+    __device__ __forceinline__ const uint8_t *ring_at(uint32_t sq) const { return smem + (sq & (NSLOT - 1)) * SLOT; }
+    // releases the next n ring entries (after the warp is done with them)
+    __device__ __forceinline__ void release(int n) {
+        __syncwarp();
+        if (lane == 0)
+            for (int i = 0; i < n; ++i) mb_arrive(emptyp + ((seq + i) & (NSLOT - 1)));
+        seq += n;
     }
     // This CTA's tiles t = R + NR i of linear L, i in [i0, i1), from the ring: per-warp
     // partial sums to red[i - i0] (group j of a tile goes to warp (tile * G64 + j) % 8).
@@ -508,48 +495,38 @@ struct XkConsumer {
         const int n = L.n_rb * L.n_kc;
         return R < n ? (n - 1 - R) / NR + 1 : 0;
     }
-    // Warp w takes groups w and w + CW of every tile (CW >= 10: at most 2 of the <= 20
-    // groups); with one K chunk the two activation fragments stay in registers for the
-    // whole stage, otherwise (the K-split mlp projection) they are loaded per tile.
-    __device__ __forceinline__ void tiles(const MkLin &L, const __half *xs, const float *sx, int i0, int i1, int mode) {
+    // This CTA's tiles i in [i0, i1) of a linear with one K chunk (tile_of gives their
+    // index), from the ring: per-warp partial sums to red[i - i0].  Warp w takes groups w and
+    // w + CW of every tile (CW >= 10: at most 2 of the <= 20 groups), its two activation
+    // fragments in registers for the whole stage.  Each tile is computed as soon as it has
+    // landed (the later ones are often still in flight).
+    __device__ __forceinline__ void tiles(const MkLin &L, const __half *xs, const float *sx, int i0, int i1) {
         static_assert(2 * CW >= MK_MAX_KC / 64, "two groups per warp cover a tile");
-        const int KC = L.kc, G64 = KC / 64, nkc = L.n_kc;
+        const int KC = L.kc, G64 = KC / 64, n = i1 - i0;
         const bool half_sb = pp->sbb == 4;
         const int j0 = warp, j1 = warp + CW;
         const bool h0 = j0 < G64, h1 = j1 < G64;
         uint4 xa0 = make_uint4(0, 0, 0, 0), xa1 = xa0, xb0 = xa0, xb1 = xa0;
         float sa = 0.f, sb = 0.f;
-        if (nkc == 1) {
-            if (h0) {
-                xa0 = *reinterpret_cast<const uint4 *>(xs + j0 * 64 + c * 16);
-                xa1 = *reinterpret_cast<const uint4 *>(xs + j0 * 64 + c * 16 + 8);
-                sa = sx[j0];
-            }
-            if (h1) {
-                xb0 = *reinterpret_cast<const uint4 *>(xs + j1 * 64 + c * 16);
-                xb1 = *reinterpret_cast<const uint4 *>(xs + j1 * 64 + c * 16 + 8);
-                sb = sx[j1];
-            }
+        if (h0) {
+            xa0 = *reinterpret_cast<const uint4 *>(xs + j0 * 64 + c * 16);
+            xa1 = *reinterpret_cast<const uint4 *>(xs + j0 * 64 + c * 16 + 8);
+            sa = sx[j0];
         }
-        for (int i = i0; i < i1; ++i) {
-            const uint32_t slot = seq & (NSLOT - 1);
-            wait_slot(slot, 2);
-            const uint8_t *tq = smem + slot * SLOT;
-            const uint8_t *tsb = tq + 16 * KC;
+        if (h1) {
+            xb0 = *reinterpret_cast<const uint4 *>(xs + j1 * 64 + c * 16);
+            xb1 = *reinterpret_cast<const uint4 *>(xs + j1 * 64 + c * 16 + 8);
+            sb = sx[j1];
+        }
+        for (int i = 0; i < n; ++i) {
+            wait_seq(seq, 2);
+            const uint8_t *tq = ring_at(seq);
             float a0 = 0.f, a1 = 0.f;
-            if (nkc == 1) {
-                if (h0) group_x(tq, tsb, KC, G64, j0, xa0, xa1, sa, half_sb, a0, a1);
-                if (h1) group_x(tq, tsb, KC, G64, j1, xb0, xb1, sb, half_sb, a0, a1);
-            } else {
-                const int kci = tile_of(L, i, mode) % nkc;
-                if (h0) group(tq, tsb, KC, G64, j0, kci * G64 + j0, xs, sx, half_sb, a0, a1);
-                if (h1) group(tq, tsb, KC, G64, j1, kci * G64 + j1, xs, sx, half_sb, a0, a1);
-            }
-            __syncwarp();
-            if (lane == 0) mb_arrive(emptyp + slot);
-            ++seq;
+            if (h0) group_x(tq, tq + 16 * KC, KC, G64, j0, xa0, xa1, sa, half_sb, a0, a1);
+            if (h1) group_x(tq, tq + 16 * KC, KC, G64, j1, xb0, xb1, sb, half_sb, a0, a1);
+            release(1);
             if (c == 0) {
-                float *r = red + ((i - i0) * CW + warp) * 16;
+                float *r = red + (i * CW + warp) * 16;
                 r[g] = a0;
                 r[g + 8] = a1;
             }
@@ -575,27 +552,29 @@ struct XkConsumer {
         for (int e = 0; e < 4; ++e) b[e] = o + e < L.out ? __ldg(L.bias + o + e) : 0.f;
         return make_float4(b[0], b[1], b[2], b[3]);
     }
-    // This thread's epilogue chunk of the first round of run_lin: its bias, loaded before the
-    // stage's input wait so that the L2 latency is off the critical path.
+    // This thread's epilogue chunk of the first round of run_lin<P>: its bias, loaded before
+    // the stage's input wait so that the L2 latency is off the critical path.
+    template <int P>
     __device__ __forceinline__ float4 bias_pre(const MkLin &L, int mode) const {
-        const int n = min(own_tiles(L, mode), rt);
-        if (tid >= n * 4) return make_float4(0.f, 0.f, 0.f, 0.f);
-        const int t = tile_of(L, tid >> 2, mode), rb = t / L.n_kc, o = rb * 16 + (tid & 3) * 4;
+        const int n = min(own_tiles(L, mode), rt), ch = tid / P;
+        if (ch >= n * 4) return make_float4(0.f, 0.f, 0.f, 0.f);
+        const int t = tile_of(L, ch >> 2, mode), o = t * 16 + (ch & 3) * 4;
         return o < L.out ? bias4(L, o) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    // Tiles of one linear, then per 4-row chunk epi(o, kc, v, bias) (o: first output row,
-    // kc: K chunk of the tile).  Rows past L.out are skipped.
-    template <class Epi>
+    // Tiles of one linear (one K chunk), then per 4-row chunk and part p < P
+    // epi(o, v, bias, p) (o: first output row; P threads per chunk, each sending one part of
+    // its results).  Rows past L.out are skipped.
+    template <int P, class Epi>
     __device__ __forceinline__ void run_lin(const MkLin &L, const __half *xs, const float *sx, float4 bpre, int mode,
                                             Epi epi) {
         const int n = own_tiles(L, mode);
         for (int i0 = 0; i0 < n; i0 += rt) {
             const int i1 = min(n, i0 + rt);
-            tiles(L, xs, sx, i0, i1, mode);
-            for (int q = tid; q < (i1 - i0) * 4; q += CT) {
-                const int il = q >> 2, t = tile_of(L, i0 + il, mode), rb = t / L.n_kc, kci = t - rb * L.n_kc;
-                const int o = rb * 16 + (q & 3) * 4;
-                if (o < L.out) epi(o, kci, rows4(il, q & 3), i0 == 0 ? bpre : bias4(L, o));
+            tiles(L, xs, sx, i0, i1);
+            for (int q = tid; q < (i1 - i0) * 4 * P; q += CT) {
+                const int ch = q / P, part = q - ch * P, il = ch >> 2, t = tile_of(L, i0 + il, mode);
+                const int o = t * 16 + (ch & 3) * 4;
+                if (o < L.out) epi(o, rows4(il, ch & 3), i0 == 0 ? bpre : bias4(L, o), part);
             }
             csync();
         }
@@ -681,7 +660,7 @@ struct XkConsumer {
         const MkParams &p = *pp;
         const MkLayer &Ly = lay[l];
         const LnRegs ln1 = ln_prefetch(Ly.ln1_w, Ly.ln1_b);
-        const float4 bpre = bias_pre(Ly.qkv, TM_QKV);
+        const float4 bpre = bias_pre<CS>(Ly.qkv, TM_QKV);
         if (l == 0) {
             const float *e = p.mel_emb + (size_t)T->tok * d, *ps = p.mel_pos + (size_t)T->pos * d;
             for (int k = tid; k < d; k += CT) land[k] = e[k] + ps[k];
@@ -696,19 +675,19 @@ struct XkConsumer {
         const MkLin &L = Ly.qkv;
         const int active = T->active, slot = T->slot, lold = T->lold, hd = head;
         const uint32_t q_a = su32(qkvh), bar_a = su32(stb + BQ);
-        run_lin(L, xln, sxln, bpre, TM_QKV, [&](int o, int, float4 v, float4 bb) {
+        run_lin<CS>(L, xln, sxln, bpre, TM_QKV, [&](int o, float4 v, float4 bb, int r) {
             v.x += bb.x; v.y += bb.y; v.z += bb.z; v.w += bb.w;
             const int which = o / d, oo = o - which * d;
-            if (which > 0 && active) {
+            if (r == 0 && which > 0 && active) {
                 __half *cache = which == 1 ? p.kc : p.vc;
                 uint2 hv;
                 hv.x = pack_h2(v.x, v.y);
                 hv.y = pack_h2(v.z, v.w);
                 *reinterpret_cast<uint2 *>(cache + kv_index(l, slot, hd, lold, p.n_slots, p.H, p.max_seq) + (oo & 63)) = hv;
             }
-            bcast_v4(q_a + (which * 64 + (oo & 63)) * 4,
-                     make_uint4(__float_as_uint(v.x), __float_as_uint(v.y), __float_as_uint(v.z), __float_as_uint(v.w)),
-                     bar_a);
+            st_async_v4(mapa(q_a + (which * 64 + (oo & 63)) * 4, r),
+                        make_uint4(__float_as_uint(v.x), __float_as_uint(v.y), __float_as_uint(v.z), __float_as_uint(v.w)),
+                        mapa(bar_a, r));
         });
     }
     // attention of the cluster's head over this rank's K/V tiles: one record (m, l, acc[64])
@@ -896,7 +875,8 @@ struct XkConsumer {
             const uint8_t *base = smem + slot * SLOT;
             const uint4 x0 = *reinterpret_cast<const uint4 *>(xh + c * 16);
             const uint4 x1 = *reinterpret_cast<const uint4 *>(xh + c * 16 + 8);
-            for (int i = warp; i < nc; i += CW) {
+            // chunk i: 16 rows x the head's 64 inputs (one quantization group)
+            auto chunk = [&](int i, float &y0, float &y1) {
                 const uint8_t *tq = base + i * cb, *tsb = tq + 16 * 64;
                 const uint4 wa = *reinterpret_cast<const uint4 *>(tq + g * 64 + c * 16);
                 const uint4 wb = *reinterpret_cast<const uint4 *>(tq + (g + 8) * 64 + c * 16);
@@ -915,12 +895,25 @@ struct XkConsumer {
                     const float2 f1 = *reinterpret_cast<const float2 *>(tsb + (g + 8) * 8);
                     s0 = f0.x; z0 = f0.y; s1 = f1.x; z1 = f1.y;
                 }
-                const float y0 = fmaf(s0, d0[0] + d1[0], fmaf(-1024.0f, s0, z0) * hsum);
-                const float y1 = fmaf(s1, d0[2] + d1[2], fmaf(-1024.0f, s1, z1) * hsum);
+                y0 = fmaf(s0, d0[0] + d1[0], fmaf(-1024.0f, s0, z0) * hsum);
+                y1 = fmaf(s1, d0[2] + d1[2], fmaf(-1024.0f, s1, z1) * hsum);
+            };
+            // two chunks per warp at a time (the second one computed twice when absent), so
+            // that their loads and mma chains overlap
+            for (int i = warp; i < nc; i += 2 * CW) {
+                const int i2 = i + CW < nc ? i + CW : i;
+                float y0, y1, y2, y3;
+                chunk(i, y0, y1);
+                chunk(i2, y2, y3);
                 if (c == 0) {
                     const int o = (r0 + i) * 16;
                     add_part(acc + o + g, y0);
                     add_part(acc + o + g + 8, y1);
+                    if (i2 != i) {
+                        const int o2 = (r0 + i2) * 16;
+                        add_part(acc + o2 + g, y2);
+                        add_part(acc + o2 + g + 8, y3);
+                    }
                 }
             }
             __syncwarp();
@@ -938,7 +931,7 @@ struct XkConsumer {
     __device__ __forceinline__ void stage_fc(int l) {
         const MkLayer &Ly = lay[l];
         const LnRegs ln2 = ln_prefetch(Ly.ln2_w, Ly.ln2_b);
-        const float4 bpre = bias_pre(Ly.fc, TM_FC);
+        const float4 bpre = bias_pre<CS>(Ly.fc, TM_FC);
         const int hc0 = slice_lo(rank, d / 4) * 4;
         const float4 hbias = tid < slice_lo(rank + 1, d / 4) - slice_lo(rank, d / 4)
                                  ? __ldg(reinterpret_cast<const float4 *>(Ly.proj.bias + hc0 + tid * 4))
@@ -948,27 +941,25 @@ struct XkConsumer {
         const MkLin &L = Ly.fc;
         const int S = ff / pp->H, lo0 = head * S;
         const uint32_t xu_a = su32(xu), bar_a = su32(stb + BU);
-        run_lin(L, xln, sxln, bpre, TM_FC, [&](int o, int, float4 v, float4 bb) {
+        run_lin<CS>(L, xln, sxln, bpre, TM_FC, [&](int o, float4 v, float4 bb, int r) {
             // rows o..o+3 of the slice -> positions frag_pos(k), frag_pos(k) + 1 (k = o & 63)
-            // and frag_pos(k + 2), + 1 of their group: two fp16 pairs
+            // and frag_pos(k + 2), + 1 of their group: two fp16 pairs, into cluster rank r
             const int lo = o - lo0, g = lo >> 6, k = lo & 63;
             const uint32_t p01 = pack_h2(gelu_tanh(v.x + bb.x), gelu_tanh(v.y + bb.y));
             const uint32_t p23 = pack_h2(gelu_tanh(v.z + bb.z), gelu_tanh(v.w + bb.w));
             const uint32_t a01 = xu_a + (g * 64 + frag_pos_host(k)) * 2, a23 = xu_a + (g * 64 + frag_pos_host(k + 2)) * 2;
-#pragma unroll
-            for (int r = 0; r < CS; ++r) {
-                st_async_b32(mapa(a01, r), p01, mapa(bar_a, r));
-                st_async_b32(mapa(a23, r), p23, mapa(bar_a, r));
-            }
+            st_async_b32(mapa(a01, r), p01, mapa(bar_a, r));
+            st_async_b32(mapa(a23, r), p23, mapa(bar_a, r));
         });
     }
-    // Each warp applies whole sub-tiles (16 rows x the slice's S inputs: sub-tile i of this
-    // rank's run goes to warp i % CW), so a row's partial is complete in one lane and goes
-    // straight into the accumulator word; every warp still waits for each slot before
-    // releasing it, so that its release counts towards the slot's current use.
+    // Each warp applies whole sub-tiles (16 rows x the slice's S <= 256 inputs), so a row's
+    // partial is complete in one lane and goes straight into the accumulator word.  Slot by
+    // slot as they land, the sub-tiles are dealt to the warps (sub-tile s of this rank's run
+    // to warp s % CW); every warp waits for each slot before releasing it, so that its
+    // release counts towards the slot's current use.
     __device__ __forceinline__ void stage_mlp(int l) {
         wait_land(BU, 60);
-        const int S = ff / pp->H, G = S / 64;
+        const int S = ff / pp->H, G = S / 64;  // G <= 4 (xk_config)
         // the slice's group sums (the dequantization offset term), from the fp16 values
         if (warp < G) {
             const __half2 *u2 = reinterpret_cast<const __half2 *>(xu + warp * 64);
@@ -976,29 +967,40 @@ struct XkConsumer {
             sxu[warp] = warp_sum(f.x + f.y);
         }
         csync();
+        uint4 xf[4][2];
+        float sxf[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            if (j < G) {
+                xf[j][0] = *reinterpret_cast<const uint4 *>(xu + j * 64 + c * 16);
+                xf[j][1] = *reinterpret_cast<const uint4 *>(xu + j * 64 + c * 16 + 8);
+                sxf[j] = sxu[j];
+            } else {
+                xf[j][0] = xf[j][1] = make_uint4(0, 0, 0, 0);
+                sxf[j] = 0.f;
+            }
+        }
         const MkLin &L = lay[l].mlp;
         const bool half_sb = pp->sbb == 4;
         const int sub = mk_mlpk_sub_bytes(S, pp->sbb), per_slot = SLOT / sub;
         const int nrb = L.n_rb, mine = rank < nrb ? (nrb - 1 - rank) / CS + 1 : 0;
         unsigned long long *acc = xp->xacc + ((size_t)par * pp->n_layers + l) * d;
-        for (int s0 = 0; s0 < mine; s0 += per_slot) {
-            const int ns = min(per_slot, mine - s0);
-            const uint32_t slot = seq & (NSLOT - 1);
-            wait_slot(slot, 4);
-            const uint8_t *base = smem + slot * SLOT;
-            for (int si = (warp + CW - s0 % CW) % CW; si < ns; si += CW) {
-                const uint8_t *tq = base + si * sub, *tsb = tq + 16 * S;
+        for (int s_lo = 0; s_lo < mine; s_lo += per_slot) {
+            const int s_hi = min(mine, s_lo + per_slot);
+            wait_seq(seq, 4);
+            for (int s = s_lo + (warp + CW - s_lo % CW) % CW; s < s_hi; s += CW) {
+                const uint8_t *tq = ring_at(seq) + (s - s_lo) * sub, *tsb = tq + 16 * S;
                 float a0 = 0.f, a1 = 0.f;
-                for (int j = 0; j < G; ++j) group(tq, tsb, S, G, j, j, xu, sxu, half_sb, a0, a1);
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (j < G) group_x(tq, tsb, S, G, j, xf[j][0], xf[j][1], sxf[j], half_sb, a0, a1);
                 if (c == 0) {
-                    const int o = (rank + CS * (s0 + si)) * 16;
+                    const int o = (rank + CS * s) * 16;
                     add_part(acc + o + g, a0);
                     add_part(acc + o + g + 8, a1);
                 }
             }
-            __syncwarp();
-            if (lane == 0) mb_arrive(emptyp + slot);  // (every consumer warp, once per slot)
-            ++seq;
+            release(1);  // (every consumer warp, once per slot)
         }
         trace();
     }
@@ -1006,13 +1008,13 @@ struct XkConsumer {
         const MkParams &p = *pp;
         const LnRegs lnf = ln_prefetch(p.lnf_w, p.lnf_b);
         const LnRegs fin = ln_prefetch(p.fin_w, p.fin_b);
-        const float4 bpre = bias_pre(p.head, TM_RR);
+        const float4 bpre = bias_pre<1>(p.head, TM_RR);
         exchange_x(p.n_layers - 1, 70);
         layernorm(lnf, true);
         layernorm(fin, false);
         const MkLin &L = p.head;
         const int V = p.mel_vocab;
-        run_lin(L, xln, sxln, bpre, TM_RR, [&](int o, int, float4 v, float4 bb) {
+        run_lin<1>(L, xln, sxln, bpre, TM_RR, [&](int o, float4 v, float4 bb, int) {
             const float vv[4] = {v.x + bb.x, v.y + bb.y, v.z + bb.z, v.w + bb.w};
 #pragma unroll
             for (int e = 0; e < 4; ++e)
@@ -1335,7 +1337,8 @@ __global__ void mlp_by_slice_kernel(const uint8_t *tiles, int tile_bytes, int kc
 
 bool mlp_slice_ok(const MkLin &W, int n_heads) {
     const int S = W.in / n_heads;
-    return n_heads > 0 && W.in % n_heads == 0 && S % 128 == 0 && W.kc % S == 0 && mk_mlpk_sub_bytes(S, W.sbb) <= SLOT;
+    return n_heads > 0 && W.in % n_heads == 0 && S % 128 == 0 && S <= 256 && W.kc % S == 0 &&
+           mk_mlpk_sub_bytes(S, W.sbb) <= SLOT;
 }
 
 size_t mlp_slice_bytes(const MkLin &W, int n_heads) {
