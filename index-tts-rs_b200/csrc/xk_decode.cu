@@ -7,8 +7,8 @@
 // Cluster c owns head c: its ranks compute the 12 QKV row blocks of the head (q, k, v rows
 // 64c .. 64c + 63), append K/V to the cache and push the 192 values into every CTA of the
 // cluster with st.async; each rank then attends over its range of the head's 84-position
-// K/V tiles and pushes one (m, l, acc[64]) record into cluster rank 0, which merges them and
-// pushes the head's 64 outputs (fp16) back into the cluster.  The cluster then applies the
+// K/V tiles and pushes one (m, l, acc[64]) record into every CTA of the cluster, and each CTA
+// merges the six records into the head's 64 outputs (fp16).  The cluster then applies the
 // head's 64 columns of c_proj (a head-major copy of its weights made at load) to them and
 // adds each row's partial into a per-step accumulator word with a 64-bit integer add.  The
 // word is a counted fixed-point sum: bits 0..51 the sum of the partials in 2^-28 units
@@ -71,9 +71,8 @@ constexpr unsigned long long kFxBad = 1ull << 58;       // one partial not repre
 constexpr int kFxMaxParts = 31;                         // partials per word (heads)
 constexpr float kLog2e = 1.4426950408889634f;
 
-// landing barriers: x/h (fp32), the head's attention output (fp16 + its sum), u (fp16), the
-// head's q/k/v (fp32), the head's attention records (cluster rank 0 only)
-enum { B0 = 0, BA, BU, BQ, BR, NSTB };
+// landing barriers: x/h (fp32), u (fp16), the head's q/k/v (fp32), the head's attention records
+enum { B0 = 0, BU, BQ, BR, NSTB };
 enum { TM_RR = 0, TM_QKV = 1, TM_FC = 2 };  // tile assignment of a stage (tile_of)
 
 // ---------------------------------------------------------------------------
@@ -192,7 +191,7 @@ __host__ __device__ inline XkSmem xk_layout(int d, int ff, int rt, int n_layers)
     };
     L.land = take(d * 4);
     L.xln = take(d * 2);
-    L.xh = take(64 * 2 + 16);  // the head's attention output (fp16, fragment order) + its sum
+    L.xh = take(64 * 2);  // the head's attention output (fp16, fragment order)
     const int S = ff / (d / 64);  // the cluster's slice of the MLP hidden units
     L.xu = take(S * 2);
     L.sxln = take(d / 64 * 4);
@@ -321,7 +320,7 @@ struct XkConsumer {
     const MkLayer *lay;  // shared-memory copy of the layer table
     uint8_t *smem;
     float *land, *sxln, *sxu, *red, *qkvh, *recs, *stat;
-    __half *xln, *xh, *xu;  // xh: the head's attention output (fp16, fragment order), sum after it
+    __half *xln, *xh, *xu;  // xh: the head's attention output (fp16, fragment order)
     uint32_t par;           // this step's accumulator buffer
     uint64_t *fullp, *emptyp, *stb;
     int tid, warp, lane, g, c, rank, R, NR, d, ff, H, rt, head;
@@ -396,9 +395,10 @@ struct XkConsumer {
         float t1 = 0.f, t2 = 0.f;
 #pragma unroll
         for (int w = 0; w < CW; ++w) { t1 += stat[2 * w]; t2 += stat[2 * w + 1]; }
-        const float m1 = t1 / (float)d;
+        const float inv_d = 1.0f / (float)d;  // (a constant of the launch: hoisted by the compiler)
+        const float m1 = t1 * inv_d;
         const float mean = sh + m1;
-        const float rstd = 1.0f / sqrtf(fmaxf(t2 / (float)d - m1 * m1, 0.f) + kNormEps);
+        const float rstd = rsqrtf(fmaxf(t2 * inv_d - m1 * m1, 0.f) + kNormEps);
 #pragma unroll
         for (int j = 0; j < LNC; ++j) {
             if (j * CT >= d / 4) break;  // (uniform: no thread of this round has inputs)
@@ -691,7 +691,8 @@ struct XkConsumer {
         });
     }
     // attention of the cluster's head over this rank's K/V tiles: one record (m, l, acc[64])
-    // per rank into cluster rank 0, which merges them and writes the head's 64 outputs
+    // per rank into every CTA of the cluster, each of which merges them into the head's 64
+    // outputs
     __device__ __forceinline__ void stage_attn(int l) {
         wait_land(BQ, 30);
         const int grp = lane >> 3, d8 = lane & 7;
@@ -701,69 +702,79 @@ struct XkConsumer {
 #pragma unroll
         for (int e = 0; e < 8; ++e) { qv[e] = qkvh[d8 * 8 + e] * qscale; acc[e] = 0.f; }
         const int kvt = T->kvt, lold = T->lold;
-        for (int t = T->t_lo; t < T->t_hi; ++t) {
-            const int np = min(KVPOS, lold - t * KVPOS);
-            if (np > 0) {
-                const uint32_t slot = seq & (NSLOT - 1);
-                wait_slot(slot, 3);
-                const __half *kt = reinterpret_cast<const __half *>(smem + slot * SLOT);
-                const __half *vt = kt + np * 64;
-                constexpr int QG = (KVPOS / 4 + CW - 1) / CW;
-                float sc[QG];
-                uint4 vv[QG];
-#pragma unroll
-                for (int q = 0; q < QG; ++q) {
-                    const int pos = (warp + q * CW) * 4 + grp;
-                    const int pc = pos < np ? pos : 0;
-                    const uint4 kk = *reinterpret_cast<const uint4 *>(kt + pc * 64 + d8 * 8);
-                    vv[q] = *reinterpret_cast<const uint4 *>(vt + pc * 64 + d8 * 8);
-                    const __half2 *k2 = reinterpret_cast<const __half2 *>(&kk);
-                    float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-                    for (int e = 0; e < 4; e += 2) {
-                        const float2 ka = __half22float2(k2[e]), kb = __half22float2(k2[e + 1]);
-                        s0 = fmaf(qv[2 * e], ka.x, s0);
-                        s1 = fmaf(qv[2 * e + 1], ka.y, s1);
-                        s0 = fmaf(qv[2 * e + 2], kb.x, s0);
-                        s1 = fmaf(qv[2 * e + 3], kb.y, s1);
-                    }
-                    sc[q] = s0 + s1;
-                }
-#pragma unroll
-                for (int q = 0; q < QG; ++q) sc[q] += __shfl_xor_sync(0xffffffffu, sc[q], 1);
-#pragma unroll
-                for (int q = 0; q < QG; ++q) sc[q] += __shfl_xor_sync(0xffffffffu, sc[q], 2);
-#pragma unroll
-                for (int q = 0; q < QG; ++q) sc[q] += __shfl_xor_sync(0xffffffffu, sc[q], 4);
-                float mt = m;
-#pragma unroll
-                for (int q = 0; q < QG; ++q)
-                    if ((warp + q * CW) * 4 + grp < np) mt = fmaxf(mt, sc[q]);
-                if (mt != m) {
-                    const float corr = exp2f(m - mt);
-                    ls *= corr;
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) acc[e] *= corr;
-                    m = mt;
-                }
-#pragma unroll
-                for (int q = 0; q < QG; ++q) {
-                    if ((warp + q * CW) * 4 + grp < np) {
-                        const float pj = exp2f(sc[q] - m);
-                        ls += pj;
-                        const __half2 *v2 = reinterpret_cast<const __half2 *>(&vv[q]);
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const float2 f = __half22float2(v2[e]);
-                            acc[2 * e] = fmaf(pj, f.x, acc[2 * e]);
-                            acc[2 * e + 1] = fmaf(pj, f.y, acc[2 * e + 1]);
-                        }
-                    }
-                }
-                __syncwarp();
-                if (lane == 0) mb_arrive(emptyp + slot);
-                ++seq;
+        // two K/V tiles at a time (one online-softmax update per pair): a warp's 8-lane group
+        // scores QG positions of each tile
+        constexpr int QG = (KVPOS / 4 + CW - 1) / CW, QP = 2 * QG;
+        for (int t = T->t_lo; t < T->t_hi;) {
+            const int npa = min(KVPOS, lold - t * KVPOS);
+            if (npa <= 0) {  // (only with no cached positions: nothing was copied)
+                ++t;
+                continue;
             }
+            const bool two = t + 1 < T->t_hi;  // (a later tile of the range is never empty)
+            const int npb = two ? min(KVPOS, lold - (t + 1) * KVPOS) : 0;
+            wait_seq(seq, 3);
+            if (two) wait_seq(seq + 1, 3);
+            const __half *ka = reinterpret_cast<const __half *>(ring_at(seq)), *va = ka + npa * 64;
+            const __half *kb = two ? reinterpret_cast<const __half *>(ring_at(seq + 1)) : ka;
+            const __half *vb = two ? kb + npb * 64 : va;
+            float sc[QP];
+            uint4 vv[QP];
+            bool in[QP];
+#pragma unroll
+            for (int q = 0; q < QP; ++q) {
+                const bool second = q >= QG;
+                const int pos = (warp + (second ? q - QG : q) * CW) * 4 + grp;
+                in[q] = pos < (second ? npb : npa);
+                const int pc = in[q] ? pos : 0;
+                const __half *kt = second ? kb : ka, *vt = second ? vb : va;
+                const uint4 kk = *reinterpret_cast<const uint4 *>(kt + pc * 64 + d8 * 8);
+                vv[q] = *reinterpret_cast<const uint4 *>(vt + pc * 64 + d8 * 8);
+                const __half2 *k2 = reinterpret_cast<const __half2 *>(&kk);
+                float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+                for (int e = 0; e < 4; e += 2) {
+                    const float2 fa = __half22float2(k2[e]), fb = __half22float2(k2[e + 1]);
+                    s0 = fmaf(qv[2 * e], fa.x, s0);
+                    s1 = fmaf(qv[2 * e + 1], fa.y, s1);
+                    s0 = fmaf(qv[2 * e + 2], fb.x, s0);
+                    s1 = fmaf(qv[2 * e + 3], fb.y, s1);
+                }
+                sc[q] = s0 + s1;
+            }
+#pragma unroll
+            for (int q = 0; q < QP; ++q) sc[q] += __shfl_xor_sync(0xffffffffu, sc[q], 1);
+#pragma unroll
+            for (int q = 0; q < QP; ++q) sc[q] += __shfl_xor_sync(0xffffffffu, sc[q], 2);
+#pragma unroll
+            for (int q = 0; q < QP; ++q) sc[q] += __shfl_xor_sync(0xffffffffu, sc[q], 4);
+            float mt = m;
+#pragma unroll
+            for (int q = 0; q < QP; ++q)
+                if (in[q]) mt = fmaxf(mt, sc[q]);
+            if (mt != m) {
+                const float corr = exp2f(m - mt);
+                ls *= corr;
+#pragma unroll
+                for (int e = 0; e < 8; ++e) acc[e] *= corr;
+                m = mt;
+            }
+#pragma unroll
+            for (int q = 0; q < QP; ++q) {
+                if (in[q]) {
+                    const float pj = exp2f(sc[q] - m);
+                    ls += pj;
+                    const __half2 *v2 = reinterpret_cast<const __half2 *>(&vv[q]);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 f = __half22float2(v2[e]);
+                        acc[2 * e] = fmaf(pj, f.x, acc[2 * e]);
+                        acc[2 * e + 1] = fmaf(pj, f.y, acc[2 * e + 1]);
+                    }
+                }
+            }
+            release(two ? 2 : 1);
+            t += two ? 2 : 1;
         }
         if (T->active && T->t_hi == kvt && T->t_hi > T->t_lo && warp == CW - 1) {  // the new position
             const float *kn = qkvh + 64 + d8 * 8;
@@ -824,37 +835,33 @@ struct XkConsumer {
             if (tid == 0) { rec[0] = M; rec[1] = L2; rec[2] = 0.f; rec[3] = 0.f; }
         }
         csync();
-        {  // this rank's record into slot [rank] of cluster rank 0
-            const uint32_t dst = mapa(su32(recs + rank * REC), 0), bar = mapa(su32(stb + BR), 0);
-            if (tid < REC / 4) st_async_v4(dst + tid * 16, reinterpret_cast<const uint4 *>(rec)[tid], bar);
-        }
-        if (rank == 0) {
-            wait_land(BR, 31);
-            __half *ho = reinterpret_cast<__half *>(red);  // [64] fragment order
-            if (tid < 64) {
-                float M = -INFINITY;
-                for (int r = 0; r < CS; ++r) M = fmaxf(M, recs[r * REC]);
-                float L2 = 0.f, A = 0.f;
-                for (int r = 0; r < CS; ++r) {
-                    const float mr = recs[r * REC];
-                    const float f = mr == -INFINITY ? 0.f : exp2f(mr - M);
-                    L2 += recs[r * REC + 1] * f;
-                    A += recs[r * REC + 4 + tid] * f;
-                }
-                const __half hv = __float2half_rn(L2 > 0.f ? A / L2 : 0.f);
-                ho[frag_pos_host(tid)] = hv;
-                const float hs = warp_sum(__half2float(hv));  // (warps 0 and 1, all lanes)
-                if (lane == 0) stat[warp] = hs;
-            }
-            csync();
-            const uint32_t xh_a = su32(xh), bar_a = su32(stb + BA);
-            if (tid < 8) bcast_v4(xh_a + tid * 16, reinterpret_cast<const uint4 *>(ho)[tid], bar_a);
-            if (tid == 8) {
-                const float hs = stat[0] + stat[1];
-#pragma unroll
-                for (int r = 0; r < CS; ++r) st_async_b32(mapa(xh_a + 128, r), __float_as_uint(hs), mapa(bar_a, r));
+        {  // this rank's record into slot [rank] of every CTA of the cluster (one 16-byte push
+           // per thread)
+            const uint32_t dst = su32(recs + rank * REC), bar = su32(stb + BR);
+            if (tid < CS * (REC / 4)) {
+                const int r = tid / (REC / 4), q = tid - r * (REC / 4);
+                st_async_v4(mapa(dst + q * 16, r), reinterpret_cast<const uint4 *>(rec)[q], mapa(bar, r));
             }
         }
+        // every CTA merges the six records itself: the head's 64 outputs (fp16, fragment order)
+        // into xh, their sum into stat[0] + stat[1]
+        wait_land(BR, 31);
+        if (tid < 64) {
+            float M = -INFINITY;
+            for (int r = 0; r < CS; ++r) M = fmaxf(M, recs[r * REC]);
+            float L2 = 0.f, A = 0.f;
+            for (int r = 0; r < CS; ++r) {
+                const float mr = recs[r * REC];
+                const float f = mr == -INFINITY ? 0.f : exp2f(mr - M);
+                L2 += recs[r * REC + 1] * f;
+                A += recs[r * REC + 4 + tid] * f;
+            }
+            const __half hv = __float2half_rn(L2 > 0.f ? A * __frcp_rn(L2) : 0.f);
+            xh[frag_pos_host(tid)] = hv;
+            const float hs = warp_sum(__half2float(hv));  // (warps 0 and 1, all lanes)
+            if (lane == 0) stat[warp] = hs;
+        }
+        csync();
         trace();
     }
     // c_proj of the cluster's head: this rank's range of the head-major chunks (16 rows x the
@@ -862,12 +869,11 @@ struct XkConsumer {
     // step's fixed-point accumulator (64-bit integer adds: the sum does not depend on their
     // order), then the CTA counts itself in
     __device__ __forceinline__ void stage_proj(int l) {
-        wait_land(BA, 40);
         const MkLin &P = lay[l].proj;
         const int nrb = P.n_rb, r0 = rank * nrb / CS, nc = (rank + 1) * nrb / CS - r0;
         const bool half_sb = pp->sbb == 4;
         const int cb = mk_projh_chunk_bytes(pp->sbb);
-        const float hsum = reinterpret_cast<const float *>(xh + 64)[0];
+        const float hsum = stat[0] + stat[1];  // (read before the next LayerNorm rewrites stat)
         unsigned long long *acc = xp->hacc + ((size_t)par * pp->n_layers + l) * d;
         if (nc > 0) {
             const uint32_t slot = seq & (NSLOT - 1);
@@ -1068,7 +1074,6 @@ __global__ void __launch_bounds__(NT, 1) xk_decode_kernel(const __grid_constant_
         for (int b = 0; b < NSTB; ++b) mb_init(stb + b, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         mb_expect(stb + B0, (uint32_t)p.d * 4);
-        mb_expect(stb + BA, 64 * 2 + 4);  // the head's output: fp16 values + their sum
         mb_expect(stb + BU, (uint32_t)(p.ff / p.H) * 2);  // the cluster's slice of GELU(c_fc), fp16
         mb_expect(stb + BQ, 3 * 64 * 4);
         mb_expect(stb + BR, CS * REC * 4);  // (waited on by rank 0 only)
@@ -1153,7 +1158,6 @@ __global__ void __launch_bounds__(NT, 1) xk_decode_kernel(const __grid_constant_
         C.ev = 0;
         for (int b = 0; b < NSTB; ++b) C.ph[b] = 0;
         C.exp_bytes[B0] = (uint32_t)p.d * 4;
-        C.exp_bytes[BA] = 64 * 2 + 4;
         C.exp_bytes[BU] = (uint32_t)(p.ff / p.H) * 2;
         C.exp_bytes[BQ] = 3 * 64 * 4;
         C.exp_bytes[BR] = CS * REC * 4;
