@@ -1301,7 +1301,7 @@ static int check_step_sync(itts_kv *kv) {
     const int err = errw[0] ? errw[0] : errw[1];  // [0]: a bounded wait gave up; [1]: range
     if (err == MK_ERR_RANGE)
         return set_err(ITTS_E_CUDA, "device error: a c_proj or mlp partial of the decode step is finite but "
-                                    "outside the fixed-point accumulator's range (|y| >= 2^18)");
+                                    "outside the fixed-point accumulator's range (|y| >= 2^17)");
     if (err != 0)
         return set_err(ITTS_E_TIMEOUT, "device wait timed out in the decode-step kernel (code " +
                                            std::to_string(err) + ")");

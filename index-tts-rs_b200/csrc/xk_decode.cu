@@ -13,7 +13,7 @@
 // adds each row's partial into a per-step accumulator word with a 64-bit integer add.  The
 // word is a counted fixed-point sum: bits 0..51 the sum of the partials in 2^-28 units
 // (signed), bits 52..57 how many partials have been added, bits 58..63 how many were not
-// representable (not finite, or |y| >= 2^18).  Integer adds do not depend on their order, and
+// representable (not finite, or |y| >= 2^17).  Integer adds do not depend on their order, and
 // the count makes each word self-validating: the reader polls the words it needs until
 // every count is complete, with no fence or separate counter between writer and reader.  So
 // q/k/v, the attention partials and the attention output never cross clusters.
@@ -65,10 +65,10 @@ constexpr int kXkRangeCode = MK_ERR_RANGE;  // error word: a partial outside the
 // counted fixed-point accumulator words (see the top of the file)
 // (2^-28 resolution: coarser units change the fp16 rounding of some activations downstream)
 constexpr float kFxScale = 268435456.0f;                // 2^28 units
-constexpr float kFxLimit = 262144.0f;                   // |partial| < 2^18: 31 of them stay below 2^51
+constexpr float kFxLimit = 131072.0f;                   // |partial| < 2^17: 62 of them stay below 2^51
 constexpr unsigned long long kFxOne = 1ull << 52;       // one partial added
 constexpr unsigned long long kFxBad = 1ull << 58;       // one partial not representable
-constexpr int kFxMaxParts = 31;                         // partials per word (heads)
+constexpr int kFxMaxHeads = 31;                         // partials per word: H (h) or 2H (next x)
 constexpr float kLog2e = 1.4426950408889634f;
 
 // landing barriers: x/h (fp32), u (fp16), the head's q/k/v (fp32), the head's attention records
@@ -602,10 +602,9 @@ struct XkConsumer {
     // h: land holds x and the partials are the heads' c_proj rows; for the next x: land holds
     // h and the partials are the clusters' mlp slices.
     __device__ __forceinline__ void exchange_acc(const unsigned long long *acc, float4 bpre, const float *bias,
-                                                 int code) {
+                                                 int want, int code) {
         const int c0 = slice_lo(rank, d / 4), nch = slice_lo(rank + 1, d / 4) - c0, o0 = c0 * 4;
         const uint32_t land_a = su32(land), bar_a = su32(stb + B0);
-        const long long want = pp->H;
         for (int i = tid; i < nch && ok; i += CT) {
             const int o = o0 + i * 4;
             long long q[4];
@@ -613,10 +612,11 @@ struct XkConsumer {
             for (uint32_t it = 0; it < SPIN; ++it) {
                 asm volatile("ld.relaxed.gpu.global.v2.b64 {%0,%1}, [%2];" : "=l"(q[0]), "=l"(q[1]) : "l"(acc + o) : "memory");
                 asm volatile("ld.relaxed.gpu.global.v2.b64 {%0,%1}, [%2];" : "=l"(q[2]), "=l"(q[3]) : "l"(acc + o + 2) : "memory");
-                // count field (bits 52..57) of each word, the signed sum below it taken out
+                // count field (bits 52..57) of each word, with the signed sum below it biased
+                // to [0, 2^52) so that it does not borrow from the count
                 done = true;
 #pragma unroll
-                for (int e = 0; e < 4; ++e) done &= (((q[e] + (1ll << 51)) >> 52) & 63) == want;
+                for (int e = 0; e < 4; ++e) done &= (int)(((unsigned long long)q[e] + (1ull << 51)) >> 52 & 63) == want;
                 if (done) break;
                 if ((it & 255u) == 255u && *(volatile const int *)pp->err) break;
                 if (it >= 4) __nanosleep(it < 64 ? 20u : 100u);
@@ -630,9 +630,9 @@ struct XkConsumer {
             float v[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                const long long m = (q[e] + (1ll << 51)) >> 52;  // count + 64 x not-representable
-                const long long sum = q[e] - (m << 52);
-                v[e] = (m >> 6) ? __int_as_float(0x7fc00000) : (float)sum * (1.0f / kFxScale);
+                const unsigned long long u = (unsigned long long)q[e] + (1ull << 51);
+                const long long sum = (long long)(u & ((1ull << 52) - 1)) - (1ll << 51);
+                v[e] = (u >> 58) ? __int_as_float(0x7fc00000) : (float)sum * (1.0f / kFxScale);
             }
             bcast_v4(land_a + o * 4, make_uint4(__float_as_uint(x.x + bb.x + v[0]), __float_as_uint(x.y + bb.y + v[1]),
                                                 __float_as_uint(x.z + bb.z + v[2]), __float_as_uint(x.w + bb.w + v[3])),
@@ -643,7 +643,7 @@ struct XkConsumer {
     }
     __device__ __forceinline__ void exchange_h(int l, float4 bpre, int code) {
         const size_t li = (size_t)par * pp->n_layers + l;
-        exchange_acc(xp->hacc + li * d, bpre, lay[l].proj.bias, code);
+        exchange_acc(xp->hacc + li * d, bpre, lay[l].proj.bias, pp->H, code);
     }
     // x of layer lprev + 1 = h + mlp bias + the clusters' mlp partials
     __device__ __forceinline__ void exchange_x(int lprev, int code) {
@@ -652,7 +652,7 @@ struct XkConsumer {
         const float *mb = lay[lprev].mlp.bias;
         const float4 bpre = tid < nch ? __ldg(reinterpret_cast<const float4 *>(mb + c0 * 4 + tid * 4))
                                       : make_float4(0.f, 0.f, 0.f, 0.f);
-        exchange_acc(xp->xacc + li * d, bpre, mb, code);
+        exchange_acc(xp->xacc + li * d, bpre, mb, 2 * pp->H, code);  // (two halves per cluster)
     }
 
     // ---- stages ----
@@ -958,14 +958,14 @@ struct XkConsumer {
             st_async_b32(mapa(a23, r), p23, mapa(bar_a, r));
         });
     }
-    // Each warp applies whole sub-tiles (16 rows x the slice's S <= 256 inputs), so a row's
-    // partial is complete in one lane and goes straight into the accumulator word.  Slot by
-    // slot as they land, the sub-tiles are dealt to the warps (sub-tile s of this rank's run
-    // to warp s % CW); every warp waits for each slot before releasing it, so that its
+    // The sub-tiles (16 rows x the slice's S <= 256 inputs) are applied in halves (S / 2
+    // inputs each): slot by slot as they land, half h of this rank's run goes to warp h % CW,
+    // which adds its rows' partials straight into the accumulator words (two partials per
+    // row and cluster).  Every warp waits for each slot before releasing it, so that its
     // release counts towards the slot's current use.
     __device__ __forceinline__ void stage_mlp(int l) {
         wait_land(BU, 60);
-        const int S = ff / pp->H, G = S / 64;  // G <= 4 (xk_config)
+        const int S = ff / pp->H, G = S / 64;  // G is 2 or 4 (xk_config)
         // the slice's group sums (the dequantization offset term), from the fp16 values
         if (warp < G) {
             const __half2 *u2 = reinterpret_cast<const __half2 *>(xu + warp * 64);
@@ -973,33 +973,27 @@ struct XkConsumer {
             sxu[warp] = warp_sum(f.x + f.y);
         }
         csync();
-        uint4 xf[4][2];
-        float sxf[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            if (j < G) {
-                xf[j][0] = *reinterpret_cast<const uint4 *>(xu + j * 64 + c * 16);
-                xf[j][1] = *reinterpret_cast<const uint4 *>(xu + j * 64 + c * 16 + 8);
-                sxf[j] = sxu[j];
-            } else {
-                xf[j][0] = xf[j][1] = make_uint4(0, 0, 0, 0);
-                sxf[j] = 0.f;
-            }
-        }
+        // group j of a sub-tile against the slice's activation fragment (from shared memory)
+        auto grp_j = [&](const uint8_t *tq, const uint8_t *tsb, int j, bool half_sb, float &a0, float &a1) {
+            const uint4 x0 = *reinterpret_cast<const uint4 *>(xu + j * 64 + c * 16);
+            const uint4 x1 = *reinterpret_cast<const uint4 *>(xu + j * 64 + c * 16 + 8);
+            group_x(tq, tsb, S, G, j, x0, x1, sxu[j], half_sb, a0, a1);
+        };
         const MkLin &L = lay[l].mlp;
         const bool half_sb = pp->sbb == 4;
         const int sub = mk_mlpk_sub_bytes(S, pp->sbb), per_slot = SLOT / sub;
         const int nrb = L.n_rb, mine = rank < nrb ? (nrb - 1 - rank) / CS + 1 : 0;
         unsigned long long *acc = xp->xacc + ((size_t)par * pp->n_layers + l) * d;
         for (int s_lo = 0; s_lo < mine; s_lo += per_slot) {
-            const int s_hi = min(mine, s_lo + per_slot);
+            const int nh = 2 * (min(mine, s_lo + per_slot) - s_lo);
             wait_seq(seq, 4);
-            for (int s = s_lo + (warp + CW - s_lo % CW) % CW; s < s_hi; s += CW) {
-                const uint8_t *tq = ring_at(seq) + (s - s_lo) * sub, *tsb = tq + 16 * S;
+            for (int h = (warp + CW - (2 * s_lo) % CW) % CW; h < nh; h += CW) {
+                const int s = s_lo + (h >> 1);
+                const uint8_t *tq = ring_at(seq) + (h >> 1) * sub, *tsb = tq + 16 * S;
                 float a0 = 0.f, a1 = 0.f;
-#pragma unroll
-                for (int j = 0; j < 4; ++j)
-                    if (j < G) group_x(tq, tsb, S, G, j, xf[j][0], xf[j][1], sxf[j], half_sb, a0, a1);
+                const int j0 = (h & 1) * (G / 2);  // this half's first group
+                grp_j(tq, tsb, j0, half_sb, a0, a1);
+                if (G == 4) grp_j(tq, tsb, j0 + 1, half_sb, a0, a1);
                 if (c == 0) {
                     const int o = (rank + CS * s) * 16;
                     add_part(acc + o + g, a0);
@@ -1202,7 +1196,7 @@ int xk_config(const ModelView &m, XkConfig *out) {
     const char *off = getenv("ITTS_XK");
     if (off && off[0] == '0') return -1;
     if (m.n_layers < 1 || m.d > MK_MAX_KC || m.d % 64 || m.ff % 64 || m.n_heads * 64 != m.d || m.d / 4 < CS ||
-        m.ff / 64 < CS || m.n_heads > kFxMaxParts)
+        m.ff / 64 < CS || m.n_heads > kFxMaxHeads)
         return -1;
     int dev = 0, optin = 0, sms = 0;
     cudaGetDevice(&dev);

@@ -430,7 +430,7 @@ def test_nonfinite_cproj_partial_propagates(small_weights, small_cfg, name):
 
 
 def test_cproj_partial_out_of_fixed_point_range_is_an_error():
-    """A finite c_proj partial of 2^18 or more does not fit the counted 2^-28 fixed-point
+    """A finite c_proj partial of 2^17 or more does not fit the counted 2^-28 fixed-point
     accumulator word: the step reports a device error instead of a wrapped value, and the
     next steps on a sound model in the same process are correct."""
     cfg32 = ModelConfig(n_layers=2, d=256, ff=1024, text_vocab=500, sb_half=False)
