@@ -117,7 +117,7 @@ class ClockSampler:
 
 
 METRIC = "mel tokens/s (cfg2 batch-1 decode)"
-XK_TRAFFIC = 686_719_488 + 4_613_120  # DRAM bytes of one batch-1 decode-step launch (ncu)
+XK_TRAFFIC = 685_748_992 + 8_116_736  # DRAM bytes of one batch-1 decode-step launch (ncu)
 DTYPE = "int8 weights (g64 affine, fp16 scales) x fp16 activations and KV, fp32 accumulate"
 
 
@@ -337,7 +337,7 @@ def run_ours(args, rank, world, local_rank):
                      # length, from an ncu capture of this kernel build (not measured here)
                      "traffic": XK_TRAFFIC if kname == "xk_decode_kernel" else None,
                      "traffic_source": "ncu --set full capture of one xk_decode_kernel launch at KV 1,384 "
-                                       "(686,719,488 B read + 4,613,120 B written); not measured in this run"},
+                                       "(685,748,992 B read + 8,116,736 B written); not measured in this run"},
         "clocks": clk,
     }
     if cfg5 is not None:
@@ -631,15 +631,16 @@ def run_profile_prefill_batch(args):
 
 
 # stage timeline events of xk_decode_kernel per layer (l >= 1) on cluster ranks other than 0
-XK_EVENTS = ["x sent", "x gathered", "LayerNorm 1", "QKV tiles + push", "q/k/v in cluster", "attention",
-             "head output in cluster", "c_proj partials added", "h sent", "h gathered", "LayerNorm 2",
-             "c_fc tiles", "u sent", "u gathered", "mlp tiles"]
+# the batch-1 kernel's stage stamps of one layer after the first (xk_decode.cu: trace())
+XK_EVENTS = ["x pushed", "x gathered", "LayerNorm 1", "QKV tiles + push", "q/k/v in cluster",
+             "attention records in cluster", "attention merged", "c_proj partials added", "h pushed",
+             "h gathered", "LayerNorm 2", "c_fc tiles + push", "u in cluster", "mlp partials added"]
 
 
 def run_profile_trace(args):
     """Stage timeline of one batch-1 decode step at KV length `--profile-trace`: per-CTA
-    globaltimer stamps (itts_bench_trace), medians over CTAs and layers, µs after the
-    layer's first x arrival."""
+    SM-cycle stamps (itts_bench_trace); each stage's duration is the gap to the previous
+    stamp of the same CTA, median over all CTAs and layers 1 .. n_layers - 2."""
     import ctypes as C
     import numpy as np
     import itts_gpt as ig
@@ -651,24 +652,24 @@ def run_profile_trace(args):
     if kv.decode_kernel(1) != "xk_decode_kernel":
         raise SystemExit("--profile-trace reads the event layout of xk_decode_kernel")
     lib = _lib.load_lib()
-    n = 148 * 256
+    n = 160 * 512
     out = np.zeros(n, np.uint64)
     g, e = C.c_int32(), C.c_int32()
     for _ in range(3):
         if lib.itts_bench_trace(gpt._h, kv._h, 1, L, out.ctypes.data, n, C.byref(g), C.byref(e)) != 0:
             raise RuntimeError(_lib.last_error())
-    t = out.reshape(-1, e.value).astype(np.int64)
+    t = out[: g.value * e.value].reshape(g.value, e.value).astype(np.int64)
     nr = int((t[:, 0] > 0).sum())
-    ev = (t[:nr] - t[:nr, 0].min()) / 1000.0
-    sel = [r for r in range(nr) if r % 6 != 0]  # rank 0 of each cluster records one event more
-    E, first, nl = len(XK_EVENTS), 14, 15  # layer 0 has no x exchange (14 events); 256 events hold 15 layers
-    lay = ev[sel, first:first + (nl - 1) * E].reshape(len(sel), nl - 1, E)
-    rel = lay[:, 1:, :] - lay[:, 1:, 1].min(0)[None, :, None]
-    per_layer = (lay[:, -1, 0].min() - lay[:, 0, 0].min()) / (nl - 2)
+    E, first = len(XK_EVENTS), len(XK_EVENTS) - 1  # layer 0 has no x exchange
+    nl = cfg.n_layers
+    assert first + (nl - 1) * E + 5 <= e.value
+    lay = t[:nr, first - 1:first + (nl - 1) * E]  # from layer 0's last stamp on
+    d = np.diff(lay, axis=1).reshape(nr, nl - 1, E)[:, :-1, :]  # layers 1 .. nl - 2
+    med = np.median(d.reshape(-1, E), axis=0)
+    sm_mhz = 1965.0
     print(json.dumps({"profile_case": "decode-step stage timeline", "kv_len": L, "ctas": nr,
-                      "us_per_layer": round(float(per_layer), 2),
-                      "median_us_after_x_arrival": {nm: round(float(np.median(np.median(rel[:, :, i], 0))), 2)
-                                                    for i, nm in enumerate(XK_EVENTS)}}), flush=True)
+                      "cycles_per_layer": int(med.sum()), "us_per_layer_at_1965_mhz": round(float(med.sum()) / sm_mhz, 2),
+                      "median_cycles_per_stage": {nm: int(med[i]) for i, nm in enumerate(XK_EVENTS)}}), flush=True)
 
 
 def main():

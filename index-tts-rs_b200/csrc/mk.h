@@ -80,9 +80,10 @@ struct MkParams {
     float *logits;
     uint32_t *epoch;    // [grid] launches completed, one counter per CTA
     int *err;
-    unsigned long long *trace;  // optional [grid][MK_TRACE_EVENTS] globaltimer stamps
+    unsigned long long *trace;  // optional [grid][MK_TRACE_EVENTS] stage stamps (globaltimer ns in
+                                // the grid-wide kernel, SM clock cycles in the cluster kernel)
 };
-constexpr int MK_TRACE_EVENTS = 256;
+constexpr int MK_TRACE_EVENTS = 512;
 // Error word value of a decode step whose fixed-point c_proj sum would overflow (any other
 // nonzero value names a bounded wait that gave up).
 constexpr int MK_ERR_RANGE = 1000;

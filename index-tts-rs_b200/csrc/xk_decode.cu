@@ -331,9 +331,9 @@ struct XkConsumer {
     int ev;
 
     __device__ __forceinline__ void trace() {
-        if (pp->trace && tid == 0 && ev < MK_TRACE_EVENTS) {
+        if (pp->trace && tid == 0 && ev < MK_TRACE_EVENTS) {  // (SM clock cycles)
             unsigned long long t;
-            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+            asm volatile("mov.u64 %0, %%clock64;" : "=l"(t));
             pp->trace[(size_t)R * MK_TRACE_EVENTS + ev] = t;
         }
         ++ev;
