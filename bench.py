@@ -660,16 +660,26 @@ def run_profile_trace(args):
             raise RuntimeError(_lib.last_error())
     t = out[: g.value * e.value].reshape(g.value, e.value).astype(np.int64)
     nr = int((t[:, 0] > 0).sum())
-    E, first = len(XK_EVENTS), len(XK_EVENTS) - 1  # layer 0 has no x exchange
+    # stamp 0: CTA start; layer 0 (no x exchange) 1 .. E - 1; layers 1 .. nl - 1 from E on; then
+    # x pushed / gathered, ln_f, final_norm, head; the last slot: CTA end
+    E, first = len(XK_EVENTS), len(XK_EVENTS)
     nl = cfg.n_layers
-    assert first + (nl - 1) * E + 5 <= e.value
-    lay = t[:nr, first - 1:first + (nl - 1) * E]  # from layer 0's last stamp on
+    tail = first + (nl - 1) * E
+    assert tail + 5 < e.value - 1
+    lay = t[:nr, first - 1:tail]  # from layer 0's last stamp on
     d = np.diff(lay, axis=1).reshape(nr, nl - 1, E)[:, :-1, :]  # layers 1 .. nl - 2
     med = np.median(d.reshape(-1, E), axis=0)
+    head = np.diff(t[:nr, tail - 1:tail + 5], axis=1)
     sm_mhz = 1965.0
     print(json.dumps({"profile_case": "decode-step stage timeline", "kv_len": L, "ctas": nr,
                       "cycles_per_layer": int(med.sum()), "us_per_layer_at_1965_mhz": round(float(med.sum()) / sm_mhz, 2),
-                      "median_cycles_per_stage": {nm: int(med[i]) for i, nm in enumerate(XK_EVENTS)}}), flush=True)
+                      "median_cycles_per_stage": {nm: int(med[i]) for i, nm in enumerate(XK_EVENTS)},
+                      "median_cycles_start_to_embedding": int(np.median(t[:nr, 1] - t[:nr, 0])),
+                      "median_cycles_layer_0": int(np.median(t[:nr, E - 1] - t[:nr, 1])),
+                      "median_cycles_head": {nm: int(v) for nm, v in zip(
+                          ["x pushed", "x gathered", "ln_f", "final_norm", "head tiles"], np.median(head, axis=0))},
+                      "median_cycles_head_to_end": int(np.median(t[:nr, -1] - t[:nr, tail + 4])),
+                      "median_cycles_start_to_end": int(np.median(t[:nr, -1] - t[:nr, 0]))}), flush=True)
 
 
 def main():

@@ -1054,6 +1054,11 @@ __global__ void __launch_bounds__(NT, 1) xk_decode_kernel(const __grid_constant_
     // CTA reads the same slot state, so all of them leave here, before any barrier, copy or
     // write (the launch counter and the accumulators stay as the last real step left them).
     if (!active) return;
+    if (p.trace && tid == 0) {  // stamp 0: the CTA starts (SM clock cycles, as every stamp)
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%clock64;" : "=l"(t));
+        p.trace[(size_t)R * MK_TRACE_EVENTS] = t;
+    }
     {
         const int words = (int)(p.n_layers * sizeof(MkLayer) / 4);
         const uint32_t *src = reinterpret_cast<const uint32_t *>(p.layers);
@@ -1149,7 +1154,7 @@ __global__ void __launch_bounds__(NT, 1) xk_decode_kernel(const __grid_constant_
         C.rt = xp.rt;
         C.seq = 0;
         C.ok = true;
-        C.ev = 0;
+        C.ev = 1;
         for (int b = 0; b < NSTB; ++b) C.ph[b] = 0;
         C.exp_bytes[B0] = (uint32_t)p.d * 4;
         C.exp_bytes[BU] = (uint32_t)(p.ff / p.H) * 2;
@@ -1167,6 +1172,11 @@ __global__ void __launch_bounds__(NT, 1) xk_decode_kernel(const __grid_constant_
     __syncwarp();
     cluster_sync_all();  // no CTA leaves while a peer may still push into its shared memory
     if (tid == 0) xp.epoch[R] = epoch + 1;
+    if (p.trace && tid == 0) {  // last stamp slot: the CTA ends
+        unsigned long long t;
+        asm volatile("mov.u64 %0, %%clock64;" : "=l"(t));
+        p.trace[(size_t)R * MK_TRACE_EVENTS + MK_TRACE_EVENTS - 1] = t;
+    }
 }
 
 cudaError_t xk_launch_cfg(const XkParams &xp, int grid, size_t smem, bool coop, cudaStream_t st) {
