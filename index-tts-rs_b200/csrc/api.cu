@@ -800,7 +800,9 @@ extern "C" int itts_kv_create(itts_gpt *g, int32_t max_seq, int32_t max_batch, i
                 x.xacc = x.hacc + 2 * L * m.d;
                 x.epoch = reinterpret_cast<uint32_t *>(x.xacc + 2 * L * m.d);
                 e = cudaMemsetAsync(x.hacc, 0, bytes, g->stream);
-                kv->db.xk = xc;
+                // without the K/V tensor maps batch-1 steps use the grid-wide kernel
+                if (e == cudaSuccess && xk_make_kv_maps(m, kv->k, kv->v, max_batch, max_seq, x) == cudaSuccess)
+                    kv->db.xk = xc;
             }
         }
     }

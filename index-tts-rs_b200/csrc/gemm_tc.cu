@@ -331,10 +331,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_q8_tc_kernel(GemmParams p,
     if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TC_TMEM_COLS));
 }
 
-namespace {
-using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
-                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 EncodeTiledFn encode_tiled() {
     static std::once_flag once;
     static EncodeTiledFn fn = nullptr;
@@ -349,7 +345,6 @@ EncodeTiledFn encode_tiled() {
     });
     return fn;
 }
-}  // namespace
 
 bool launch_gemm_tc(int epi, const GemmParams &p, cudaStream_t st) {
     const int K = p.W.in;

@@ -1,5 +1,7 @@
 // kernels.h -- host launchers of the decoder kernels (all on one CUDA stream).
 #pragma once
+#include <cuda.h>
+
 #include "common.cuh"
 #include "mk.h"
 
@@ -35,6 +37,9 @@ struct XkBufs {  // one allocation: [2][L][d] accumulator words for h and for x,
     unsigned long long *hacc = nullptr;  // counted fixed-point sums of the heads' c_proj partials, by step parity
     unsigned long long *xacc = nullptr;  // the same for the clusters' mlp partials (the next x)
     uint32_t *epoch = nullptr;
+    // the K and V caches as 5-D tensors {64, max_seq, heads, slots, layers} for tiled loads of
+    // 84 positions x 64 values with the 128-byte swizzle
+    alignas(64) CUtensorMap kmap, vmap;
 };
 
 // Decode-step scratch (sized for max_batch columns).
@@ -113,6 +118,14 @@ cudaError_t decode_forward(const ModelView &m, const DecodeView &dv, DecodeBufs 
 // creation turns it off).
 // Fills `out` and returns the grid size, or -1 when the model or the device does not fit it.
 int xk_config(const ModelView &m, XkConfig *out);
+// The K/V tensor maps of a cache (XkBufs::kmap / vmap).
+cudaError_t xk_make_kv_maps(const ModelView &m, __half *k_cache, __half *v_cache, int n_slots, int max_seq,
+                            XkBufs &b);
+// cuTensorMapEncodeTiled from the driver (null when the driver does not provide it).
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_tiled();
 cudaError_t xk_launch(const MkParams &p, const XkConfig &xc, const XkBufs &b, cudaStream_t st);
 // The head-major copy of a c_proj (MkLayer::proj_h) from its tiles: n_heads * n_rb chunks.
 cudaError_t make_proj_by_head(const MkLin &W, int n_heads, uint8_t *dst, cudaStream_t st);

@@ -56,8 +56,11 @@ constexpr int CW = 11;             // consumer warps (20 quantization groups of 
 constexpr int CT = CW * 32;        // consumer threads
 constexpr int NT = CT + 32;        // + the producer warp
 constexpr int NSLOT = 8;           // ring slots (power of two)
-constexpr int SLOT = 21888;        // bytes per slot: a 16 x 1280 tile with fp16 pairs, or 84 K/V rows
-constexpr int KVPOS = 84;          // positions per K/V tile: 2 x 84 x 128 B = 21,504 B
+constexpr int SLOT = 22528;        // bytes per slot (a multiple of 1,024): a 16 x 1280 tile with its
+                                   // scale pairs, or one K/V tile
+constexpr int KVPOS = 84;          // positions per K/V tile: K rows at the slot's start, V at KV_VOFF
+constexpr int KV_VOFF = 11264;     // (both 1,024-aligned: the 128-byte swizzle repeats every 1,024 B)
+static_assert(SLOT % 1024 == 0 && KVPOS * 128 <= KV_VOFF && KV_VOFF + KVPOS * 128 <= SLOT, "K/V tile layout");
 constexpr int REC = 68;            // floats per attention record: m, l, 0, 0, acc[64]
 constexpr int QT = 12;             // QKV row blocks of one head (q, k, v x 64 rows / 16)
 constexpr uint32_t SPIN = 1u << 22;
@@ -106,6 +109,15 @@ __device__ __forceinline__ bool mb_try(uint32_t a, uint32_t par) {
             : "memory");
     return done != 0;
 }
+// non-blocking test of a CTA-local barrier's phase (the common case: the copy landed long ago)
+__device__ __forceinline__ bool mb_test(uint32_t a, uint32_t par) {
+    uint32_t done;
+    asm volatile("{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+                 : "=r"(done)
+                 : "r"(a), "r"(par)
+                 : "memory");
+    return done != 0;
+}
 template <bool CLUSTER>
 __device__ __forceinline__ bool mb_wait(uint64_t *b, uint32_t par, const int *err) {
     const uint32_t a = su32(b);
@@ -121,6 +133,31 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t
         "l"(src), "r"(bytes), "r"(bar), "l"(pol)
         : "memory");
 }
+// 84 positions x 64 values of a K or V cache (tensor map {64, max_seq, heads, slots, layers},
+// 128-byte swizzle) into shared memory at dst, completing on bar (no multicast)
+__device__ __forceinline__ void tma_kv(uint32_t dst, const CUtensorMap *map, int pos0, int head, int slot, int layer,
+                                       uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5, "
+        "%6}], [%7];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(pos0), "r"(head), "r"(slot), "r"(layer), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &a0, uint32_t &a1, uint32_t &a2, uint32_t &a3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(a0), "=r"(a1), "=r"(a2), "=r"(a3)
+                 : "r"(addr)
+                 : "memory");
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &a0, uint32_t &a1, uint32_t &a2, uint32_t &a3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(a0), "=r"(a1), "=r"(a2), "=r"(a3)
+                 : "r"(addr)
+                 : "memory");
+}
+// shared address of 16-byte chunk `chunk` of the 128-byte row at `row` (128-byte swizzle: the
+// chunk index is XORed with address bits 7..9)
+__device__ __forceinline__ uint32_t swz(uint32_t row, int chunk) { return row + ((chunk ^ ((row >> 7) & 7)) << 4); }
 __device__ __forceinline__ uint32_t mapa(uint32_t a, int rank) {
     uint32_t r;
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
@@ -208,6 +245,7 @@ __host__ __device__ inline XkSmem xk_layout(int d, int ff, int rt, int n_layers)
 }
 
 struct XkParams {
+    CUtensorMap kmap, vmap;    // the K and V caches (tiled loads of KVPOS x 64 values)
     MkParams p;          // model, slots, KV cache, logits, err, trace
     unsigned long long *hacc;  // [2][L][d] counted fixed-point sums of the heads' c_proj partials,
                                // by step parity (this step's buffer p = epoch & 1; 1 - p zeroed)
@@ -234,23 +272,41 @@ struct XkProducer {
     int R, NR;
     bool ok;
 
-    // seq counts the copies actually issued, so the drain below waits for exactly those
-    __device__ __forceinline__ void issue(const void *s0, uint32_t b0, const void *s1, uint32_t b1) {
-        if (!ok) return;
-        const uint32_t slot = seq & (NSLOT - 1);
+    // the next ring slot, once its consumers have released it (false: a wait gave up); seq
+    // counts the copies actually issued, so the drain below waits for exactly those
+    __device__ __forceinline__ bool acquire(uint32_t &slot) {
+        if (!ok) return false;
+        slot = seq & (NSLOT - 1);
         if (seq >= (uint32_t)NSLOT) {
             ok = mb_wait<false>(emptyp + slot, ((seq / NSLOT) & 1u) ^ 1u, err);
             if (!ok) {
                 atomicExch(const_cast<int *>(err), 1);
-                return;
+                return false;
             }
         }
         ++seq;
+        return true;
+    }
+    __device__ __forceinline__ void issue(const void *s0, uint32_t b0, const void *s1, uint32_t b1) {
+        uint32_t slot;
+        if (!acquire(slot)) return;
         const uint32_t bar = full + slot * 8;
         mb_expect(fullp + slot, b0 + b1);
         const uint32_t dst = ring + slot * SLOT;
         bulk_g2s(dst, s0, b0, bar, pol);
         if (b1) bulk_g2s(dst + b0, s1, b1, bar, pol);
+    }
+    // K/V tile t of (layer, cache slot, head): the full box of KVPOS rows each (rows past the
+    // cache's positions read as zero; rows past the valid length are never used)
+    __device__ __forceinline__ void issue_kv(const CUtensorMap *km, const CUtensorMap *vm, int t, int head,
+                                             int cslot, int layer) {
+        uint32_t slot;
+        if (!acquire(slot)) return;
+        const uint32_t bar = full + slot * 8;
+        mb_expect(fullp + slot, 2 * KVPOS * 128);
+        const uint32_t dst = ring + slot * SLOT;
+        tma_kv(dst, km, t * KVPOS, head, cslot, layer, bar);
+        tma_kv(dst + KV_VOFF, vm, t * KVPOS, head, cslot, layer, bar);
     }
     // tiles t = R, R + NR, ... of a linear (tile index = rb * n_kc + kc)
     __device__ __forceinline__ void lin(const uint8_t *tiles, int n_tiles, uint32_t tb) {
@@ -259,7 +315,8 @@ struct XkProducer {
         for (int i = R; i < n_tiles; i += NR, t += step) issue(t, tb, nullptr, 0);
     }
     __device__ __forceinline__ void lin(const MkLin *L) { lin(L->tiles, L->n_rb * L->n_kc, (uint32_t)L->tile_bytes); }
-    __device__ __forceinline__ void run(const MkParams &p, const XkTab &T, const MkLayer *lay, int rank) {
+    __device__ __forceinline__ void run(const XkParams &xp, const XkTab &T, const MkLayer *lay, int rank) {
+        const MkParams &p = xp.p;
         const int head = T.head, t_lo = T.t_lo, t_hi = T.t_hi, lold = T.lold, slot = T.slot;
         const int q0 = rank * QT / CS, q1 = (rank + 1) * QT / CS;
         for (int l = 0; l < p.n_layers && ok; ++l) {
@@ -270,14 +327,8 @@ struct XkProducer {
                 for (int i = q0; i < q1; ++i) issue(tiles + (size_t)qkv_rb(i, head, p.d) * tb, tb, nullptr, 0);
             }
             // this rank's K/V tiles of the head
-            const size_t base = kv_index(l, slot, head, 0, p.n_slots, p.H, p.max_seq);
-            for (int t = t_lo; t < t_hi; ++t) {
-                const int np = min(KVPOS, lold - t * KVPOS);
-                if (np > 0) {
-                    const size_t off = base + (size_t)t * KVPOS * kHeadDim;
-                    issue(p.kc + off, (uint32_t)np * 128u, p.vc + off, (uint32_t)np * 128u);
-                }
-            }
+            for (int t = t_lo; t < t_hi; ++t)
+                if (lold - t * KVPOS > 0) issue_kv(&xp.kmap, &xp.vmap, t, head, slot, l);
             {  // this rank's head-major c_proj chunks of the head (one copy)
                 const int nrb = Ly->proj.n_rb, r0 = rank * nrb / CS, nc = (rank + 1) * nrb / CS - r0;
                 const uint32_t cb = (uint32_t)mk_projh_chunk_bytes(Ly->proj.sbb);
@@ -464,7 +515,10 @@ struct XkConsumer {
     __device__ __forceinline__ void wait_slot(uint32_t slot, int code) { wait_seq(seq, code); }
     // the copy of ring sequence number sq (slot sq % NSLOT, use sq / NSLOT) has landed
     __device__ __forceinline__ void wait_seq(uint32_t sq, int code) {
-        bool good = !ok || mb_wait<false>(fullp + (sq & (NSLOT - 1)), (sq / NSLOT) & 1u, pp->err);
+        uint64_t *b = fullp + (sq & (NSLOT - 1));
+        const uint32_t par = (sq / NSLOT) & 1u;
+        if (mb_test(su32(b), par)) return;  // (one warp instruction: the same answer in every lane)
+        bool good = !ok || mb_wait<false>(b, par, pp->err);
         good = __all_sync(0xffffffffu, good);
         if (!good) fail(code);
     }
@@ -692,19 +746,35 @@ struct XkConsumer {
     }
     // attention of the cluster's head over this rank's K/V tiles: one record (m, l, acc[64])
     // per rank into every CTA of the cluster, each of which merges them into the head's 64
-    // outputs
+    // outputs.  Two tiles at a time, as one run of n <= 168 positions; warp w takes positions
+    // [16w, 16w + 16) of the run on the tensor cores: S = K q with mma.sync (K rows through
+    // ldmatrix from the swizzled tile; q as the B operand, column 0 its fp16 value and column 1
+    // the fp16 remainder, so the products carry about 22 bits of q), an online softmax per warp,
+    // then O^T = V^T P (ldmatrix.trans; P split the same way into columns 0 and 1).  Rows past
+    // the run read row 0 of the first tile (finite, with weight 0).
     __device__ __forceinline__ void stage_attn(int l) {
         wait_land(BQ, 30);
-        const int grp = lane >> 3, d8 = lane & 7;
         float *ascr = red;  // [CW][REC] warp states, then [REC] this rank's record
         const float qscale = kAttnScale * kLog2e;
-        float qv[8], m = -INFINITY, ls = 0.f, acc[8];
+        uint32_t qb[4][2];  // B fragments of q: k16 step kk, dims 16 kk + 2c (+1) and + 8
 #pragma unroll
-        for (int e = 0; e < 8; ++e) { qv[e] = qkvh[d8 * 8 + e] * qscale; acc[e] = 0.f; }
+        for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int k0 = 16 * kk + 2 * c + 8 * h;
+                const float q0 = qkvh[k0] * qscale, q1 = qkvh[k0 + 1] * qscale;
+                const __half2 qh = __floats2half2_rn(q0, q1);
+                const float2 qf = __half22float2(qh);
+                const uint32_t hi = *reinterpret_cast<const uint32_t *>(&qh);
+                const uint32_t lo = pack_h2(q0 - qf.x, q1 - qf.y);
+                qb[kk][h] = g == 0 ? hi : g == 1 ? lo : 0u;
+            }
+        float m = -INFINITY, ls = 0.f;  // the warp's running max (uniform) and this lane's part of the sum
+        float o[4][4];                  // O^T accumulators: dims 16 dt + g (+8), columns 2c, 2c + 1
+#pragma unroll
+        for (int dt = 0; dt < 4; ++dt) o[dt][0] = o[dt][1] = o[dt][2] = o[dt][3] = 0.f;
         const int kvt = T->kvt, lold = T->lold;
-        // two K/V tiles at a time (one online-softmax update per pair): a warp's 8-lane group
-        // scores QG positions of each tile
-        constexpr int QG = (KVPOS / 4 + CW - 1) / CW, QP = 2 * QG;
+        const int mi = lane >> 3, r8 = lane & 7;  // ldmatrix: this lane addresses row r8 of matrix mi
         for (int t = T->t_lo; t < T->t_hi;) {
             const int npa = min(KVPOS, lold - t * KVPOS);
             if (npa <= 0) {  // (only with no cached positions: nothing was copied)
@@ -712,110 +782,104 @@ struct XkConsumer {
                 continue;
             }
             const bool two = t + 1 < T->t_hi;  // (a later tile of the range is never empty)
-            const int npb = two ? min(KVPOS, lold - (t + 1) * KVPOS) : 0;
+            const int npb = two ? min(KVPOS, lold - (t + 1) * KVPOS) : 0, n = npa + npb;
             wait_seq(seq, 3);
             if (two) wait_seq(seq + 1, 3);
-            const __half *ka = reinterpret_cast<const __half *>(ring_at(seq)), *va = ka + npa * 64;
-            const __half *kb = two ? reinterpret_cast<const __half *>(ring_at(seq + 1)) : ka;
-            const __half *vb = two ? kb + npb * 64 : va;
-            float sc[QP];
-            uint4 vv[QP];
-            bool in[QP];
+            const int v0 = warp * 16;
+            if (v0 < n) {
+                const uint32_t ta = su32(ring_at(seq)), tb = two ? su32(ring_at(seq + 1)) : ta;
+                // K row of position v (row 0 of the first tile past the run)
+                auto row_of = [&](int v) -> uint32_t {
+                    const int vv = v < n ? v : 0;
+                    return vv < npa ? ta + vv * 128 : tb + (vv - npa) * 128;
+                };
+                // S = K q: A fragments rows v0 + r8 (+8 for matrices 1, 3), k chunks 2 kk (+1 for 2, 3)
+                const uint32_t rk = row_of(v0 + r8 + (mi & 1) * 8);
+                float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int q = 0; q < QP; ++q) {
-                const bool second = q >= QG;
-                const int pos = (warp + (second ? q - QG : q) * CW) * 4 + grp;
-                in[q] = pos < (second ? npb : npa);
-                const int pc = in[q] ? pos : 0;
-                const __half *kt = second ? kb : ka, *vt = second ? vb : va;
-                const uint4 kk = *reinterpret_cast<const uint4 *>(kt + pc * 64 + d8 * 8);
-                vv[q] = *reinterpret_cast<const uint4 *>(vt + pc * 64 + d8 * 8);
-                const __half2 *k2 = reinterpret_cast<const __half2 *>(&kk);
-                float s0 = 0.f, s1 = 0.f;
-#pragma unroll
-                for (int e = 0; e < 4; e += 2) {
-                    const float2 fa = __half22float2(k2[e]), fb = __half22float2(k2[e + 1]);
-                    s0 = fmaf(qv[2 * e], fa.x, s0);
-                    s1 = fmaf(qv[2 * e + 1], fa.y, s1);
-                    s0 = fmaf(qv[2 * e + 2], fb.x, s0);
-                    s1 = fmaf(qv[2 * e + 3], fb.y, s1);
+                for (int kk = 0; kk < 4; kk += 2) {
+                    uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+                    ldsm_x4(swz(rk, 2 * kk + (mi >> 1)), a0, a1, a2, a3);
+                    ldsm_x4(swz(rk, 2 * kk + 2 + (mi >> 1)), b0, b1, b2, b3);
+                    mma16816(s0, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
+                    mma16816(s1, b0, b1, b2, b3, qb[kk + 1][0], qb[kk + 1][1]);
                 }
-                sc[q] = s0 + s1;
-            }
+                // lanes (g, 0): scores of positions v0 + g and v0 + g + 8 (columns 0 + 1)
+                const bool va = c == 0 && v0 + g < n, vb = c == 0 && v0 + g + 8 < n;
+                const float sa = va ? (s0[0] + s0[1]) + (s1[0] + s1[1]) : -INFINITY;
+                const float sb = vb ? (s0[2] + s0[3]) + (s1[2] + s1[3]) : -INFINITY;
+                float mt = fmaxf(sa, sb);
+                mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 4));
+                mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 8));
+                mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
+                mt = fmaxf(m, __shfl_sync(0xffffffffu, mt, 0));
+                if (mt != m) {  // (uniform)
+                    const float corr = exp2f(m - mt);
+                    ls *= corr;
 #pragma unroll
-            for (int q = 0; q < QP; ++q) sc[q] += __shfl_xor_sync(0xffffffffu, sc[q], 1);
+                    for (int dt = 0; dt < 4; ++dt)
 #pragma unroll
-            for (int q = 0; q < QP; ++q) sc[q] += __shfl_xor_sync(0xffffffffu, sc[q], 2);
+                        for (int e = 0; e < 4; ++e) o[dt][e] *= corr;
+                    m = mt;
+                }
+                const float pa = va ? exp2f(sa - m) : 0.f, pb = vb ? exp2f(sb - m) : 0.f;
+                ls += pa + pb;
+                // P as B fragments: lane (g, c) takes positions 2c, 2c + 1 (b0) and 2c + 8, 2c + 9
+                // (b1) from lanes (2c, 0) and (2c + 1, 0); column 0 fp16 values, column 1 remainders
+                const float p0 = __shfl_sync(0xffffffffu, pa, 8 * c), p8 = __shfl_sync(0xffffffffu, pb, 8 * c);
+                const float p1 = __shfl_sync(0xffffffffu, pa, 8 * c + 4), p9 = __shfl_sync(0xffffffffu, pb, 8 * c + 4);
+                const __half2 h01 = __floats2half2_rn(p0, p1), h89 = __floats2half2_rn(p8, p9);
+                uint32_t pb0 = 0u, pb1 = 0u;
+                if (g == 0) {
+                    pb0 = *reinterpret_cast<const uint32_t *>(&h01);
+                    pb1 = *reinterpret_cast<const uint32_t *>(&h89);
+                } else if (g == 1) {
+                    const float2 f01 = __half22float2(h01), f89 = __half22float2(h89);
+                    pb0 = pack_h2(p0 - f01.x, p1 - f01.y);
+                    pb1 = pack_h2(p8 - f89.x, p9 - f89.y);
+                }
+                // O^T += V^T P: A fragments (ldmatrix.trans) positions v0 + r8 (+8 for matrices
+                // 2, 3), dim chunks 2 dt (+1 for matrices 1, 3)
+                const uint32_t rv = row_of(v0 + r8 + (mi >> 1) * 8) + KV_VOFF;
 #pragma unroll
-            for (int q = 0; q < QP; ++q) sc[q] += __shfl_xor_sync(0xffffffffu, sc[q], 4);
-            float mt = m;
-#pragma unroll
-            for (int q = 0; q < QP; ++q)
-                if (in[q]) mt = fmaxf(mt, sc[q]);
-            if (mt != m) {
-                const float corr = exp2f(m - mt);
-                ls *= corr;
-#pragma unroll
-                for (int e = 0; e < 8; ++e) acc[e] *= corr;
-                m = mt;
-            }
-#pragma unroll
-            for (int q = 0; q < QP; ++q) {
-                if (in[q]) {
-                    const float pj = exp2f(sc[q] - m);
-                    ls += pj;
-                    const __half2 *v2 = reinterpret_cast<const __half2 *>(&vv[q]);
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const float2 f = __half22float2(v2[e]);
-                        acc[2 * e] = fmaf(pj, f.x, acc[2 * e]);
-                        acc[2 * e + 1] = fmaf(pj, f.y, acc[2 * e + 1]);
-                    }
+                for (int dt = 0; dt < 4; ++dt) {
+                    uint32_t a0, a1, a2, a3;
+                    ldsm_x4_t(swz(rv, 2 * dt + (mi & 1)), a0, a1, a2, a3);
+                    mma16816(o[dt], a0, a1, a2, a3, pb0, pb1);
                 }
             }
             release(two ? 2 : 1);
             t += two ? 2 : 1;
         }
         if (T->active && T->t_hi == kvt && T->t_hi > T->t_lo && warp == CW - 1) {  // the new position
-            const float *kn = qkvh + 64 + d8 * 8;
-            const float *vn = kn + 64;
-            float s = 0.f;
+            const float *kn = qkvh + 64, *vn = qkvh + 128;
+            float s = fmaf(qkvh[2 * lane] * qscale, kn[2 * lane], qkvh[2 * lane + 1] * qscale * kn[2 * lane + 1]);
+            s = warp_sum(s);
+            const float mn = fmaxf(m, s), corr = exp2f(m - mn), pj = exp2f(s - mn);
+            ls *= corr;
+            if (lane == 0) ls += pj;
 #pragma unroll
-            for (int e = 0; e < 8; ++e) s = fmaf(qv[e], kn[e], s);
-            s += __shfl_xor_sync(0xffffffffu, s, 1);
-            s += __shfl_xor_sync(0xffffffffu, s, 2);
-            s += __shfl_xor_sync(0xffffffffu, s, 4);
-            if (grp == 0) {
-                const float mn = fmaxf(m, s);
-                const float corr = exp2f(m - mn);
-                const float pj = exp2f(s - mn);
-                ls = ls * corr + pj;
+            for (int dt = 0; dt < 4; ++dt) {
 #pragma unroll
-                for (int e = 0; e < 8; ++e) acc[e] = acc[e] * corr + pj * vn[e];
-                m = mn;
+                for (int e = 0; e < 4; ++e) o[dt][e] *= corr;
+                if (c == 0) {
+                    o[dt][0] = fmaf(pj, vn[16 * dt + g], o[dt][0]);
+                    o[dt][2] = fmaf(pj, vn[16 * dt + g + 8], o[dt][2]);
+                }
             }
+            m = mn;
         }
-        // merge the 4 position groups of each warp, then the 8 warps
-#pragma unroll
-        for (int off = 8; off <= 16; off <<= 1) {
-            const float m2 = __shfl_xor_sync(0xffffffffu, m, off);
-            const float l2 = __shfl_xor_sync(0xffffffffu, ls, off);
-            const float M = fmaxf(m, m2);
-            const float fa = m == -INFINITY ? 0.f : exp2f(m - M);
-            const float fb = m2 == -INFINITY ? 0.f : exp2f(m2 - M);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                const float a2 = __shfl_xor_sync(0xffffffffu, acc[e], off);
-                acc[e] = acc[e] * fa + a2 * fb;
-            }
-            ls = ls * fa + l2 * fb;
-            m = M;
-        }
-        if (grp == 0) {
+        {  // the warp's state: m, l, and O (columns 0 + 1 of lanes (g, 0))
+            const float lw = warp_sum(ls);
             float *sw = ascr + warp * REC;
-            if (d8 == 0) { sw[0] = m; sw[1] = ls; }
+            if (lane == 0) { sw[0] = m; sw[1] = lw; }
+            if (c == 0) {
 #pragma unroll
-            for (int e = 0; e < 8; ++e) sw[4 + d8 * 8 + e] = acc[e];
+                for (int dt = 0; dt < 4; ++dt) {
+                    sw[4 + 16 * dt + g] = o[dt][0] + o[dt][1];
+                    sw[4 + 16 * dt + g + 8] = o[dt][2] + o[dt][3];
+                }
+            }
         }
         csync();
         float *rec = ascr + CW * REC;
@@ -904,27 +968,26 @@ struct XkConsumer {
                 y0 = fmaf(s0, d0[0] + d1[0], fmaf(-1024.0f, s0, z0) * hsum);
                 y1 = fmaf(s1, d0[2] + d1[2], fmaf(-1024.0f, s1, z1) * hsum);
             };
-            // two chunks per warp at a time (the second one computed twice when absent), so
-            // that their loads and mma chains overlap
-            for (int i = warp; i < nc; i += 2 * CW) {
-                const int i2 = i + CW < nc ? i + CW : i;
-                float y0, y1, y2, y3;
+            // this warp's chunks warp and warp + CW (nc <= 2 CW), computed together (the second
+            // one twice when absent) so that their loads and mma chains overlap; the slot is
+            // released before the adds, so that the release does not order them
+            const int i = warp, i2 = i + CW < nc ? i + CW : i;
+            float y0 = 0.f, y1 = 0.f, y2 = 0.f, y3 = 0.f;
+            if (i < nc) {
                 chunk(i, y0, y1);
                 chunk(i2, y2, y3);
-                if (c == 0) {
-                    const int o = (r0 + i) * 16;
-                    add_part(acc + o + g, y0);
-                    add_part(acc + o + g + 8, y1);
-                    if (i2 != i) {
-                        const int o2 = (r0 + i2) * 16;
-                        add_part(acc + o2 + g, y2);
-                        add_part(acc + o2 + g + 8, y3);
-                    }
+            }
+            release(1);
+            if (c == 0 && i < nc) {
+                const int o = (r0 + i) * 16;
+                add_part(acc + o + g, y0);
+                add_part(acc + o + g + 8, y1);
+                if (i2 != i) {
+                    const int o2 = (r0 + i2) * 16;
+                    add_part(acc + o2 + g, y2);
+                    add_part(acc + o2 + g + 8, y3);
                 }
             }
-            __syncwarp();
-            if (lane == 0) mb_arrive(emptyp + slot);
-            ++seq;
         }
         trace();
     }
@@ -987,20 +1050,32 @@ struct XkConsumer {
         for (int s_lo = 0; s_lo < mine; s_lo += per_slot) {
             const int nh = 2 * (min(mine, s_lo + per_slot) - s_lo);
             wait_seq(seq, 4);
-            for (int h = (warp + CW - (2 * s_lo) % CW) % CW; h < nh; h += CW) {
-                const int s = s_lo + (h >> 1);
-                const uint8_t *tq = ring_at(seq) + (h >> 1) * sub, *tsb = tq + 16 * S;
-                float a0 = 0.f, a1 = 0.f;
-                const int j0 = (h & 1) * (G / 2);  // this half's first group
-                grp_j(tq, tsb, j0, half_sb, a0, a1);
-                if (G == 4) grp_j(tq, tsb, j0 + 1, half_sb, a0, a1);
-                if (c == 0) {
-                    const int o = (rank + CS * s) * 16;
-                    add_part(acc + o + g, a0);
-                    add_part(acc + o + g + 8, a1);
+            // this warp's halves of the slot (at most 2: per_slot <= CW), computed before the
+            // slot is released and added after, so that the release does not order the adds
+            float r[2][2];
+            int ro[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+                const int h = (warp + CW - (2 * s_lo) % CW) % CW + u * CW;
+                r[u][0] = r[u][1] = 0.f;
+                ro[u] = -1;
+                if (h < nh) {
+                    const uint8_t *tq = ring_at(seq) + (h >> 1) * sub, *tsb = tq + 16 * S;
+                    const int j0 = (h & 1) * (G / 2);  // this half's first group
+                    grp_j(tq, tsb, j0, half_sb, r[u][0], r[u][1]);
+                    if (G == 4) grp_j(tq, tsb, j0 + 1, half_sb, r[u][0], r[u][1]);
+                    ro[u] = (rank + CS * (s_lo + (h >> 1))) * 16;
                 }
             }
             release(1);  // (every consumer warp, once per slot)
+            if (c == 0) {
+#pragma unroll
+                for (int u = 0; u < 2; ++u)
+                    if (ro[u] >= 0) {
+                        add_part(acc + ro[u] + g, r[u][0]);
+                        add_part(acc + ro[u] + g + 8, r[u][1]);
+                    }
+            }
         }
         trace();
     }
@@ -1030,6 +1105,12 @@ __global__ void __launch_bounds__(NT, 1) xk_decode_kernel(const __grid_constant_
     extern __shared__ __align__(1024) uint8_t smem[];
     if (xp.dry) {  // launch-configuration probe
         cluster_sync_all();
+        return;
+    }
+    // the K/V tiles' 128-byte swizzle is laid out for 1,024-aligned ring slots (the same in
+    // every CTA, so all of them leave here together)
+    if (su32(smem) & 1023u) {
+        if (threadIdx.x == 0) atomicExch(xp.p.err, 98);
         return;
     }
     const MkParams &p = xp.p;
@@ -1115,7 +1196,7 @@ __global__ void __launch_bounds__(NT, 1) xk_decode_kernel(const __grid_constant_
             P.R = R;
             P.NR = NR;
             P.ok = true;
-            P.run(p, *T, reinterpret_cast<const MkLayer *>(smem + SL.lay), rank);
+            P.run(xp, *T, reinterpret_cast<const MkLayer *>(smem + SL.lay), rank);
         }
         __syncwarp();
     } else {
@@ -1217,7 +1298,9 @@ int xk_config(const ModelView &m, XkConfig *out) {
         for (const MkLin *x : {&L.qkv, &L.proj, &L.fc, &L.mlp})
             if (x->tile_bytes > SLOT || x->kc % 64) return -1;
         if (L.qkv.n_kc != 1 || L.proj.n_kc != 1 || L.fc.n_kc != 1) return -1;
-        if (!L.proj_h || (L.proj.n_rb + CS - 1) / CS * mk_projh_chunk_bytes(L.proj.sbb) > SLOT) return -1;
+        if (!L.proj_h || (L.proj.n_rb + CS - 1) / CS * mk_projh_chunk_bytes(L.proj.sbb) > SLOT ||
+            (L.proj.n_rb + CS - 1) / CS > 2 * CW)
+            return -1;
         if (L.qkv.out != 3 * m.d || L.proj.out != m.d || L.fc.out != m.ff || L.mlp.out != m.d) return -1;
         if (!L.mlp_k || !mlp_slice_ok(L.mlp, m.n_heads)) return -1;
     }
@@ -1288,9 +1371,31 @@ int xk_config(const ModelView &m, XkConfig *out) {
     return grid;
 }
 
+cudaError_t xk_make_kv_maps(const ModelView &m, __half *k_cache, __half *v_cache, int n_slots, int max_seq,
+                            XkBufs &b) {
+    EncodeTiledFn enc = encode_tiled();
+    if (!enc || n_slots < 1 || max_seq < 1) return cudaErrorNotSupported;
+    // kv_index order: ((layer * n_slots + slot) * heads + head) * max_seq + pos, 64 values each
+    const cuuint64_t rowb = kHeadDim * sizeof(__half);
+    const cuuint64_t dims[5] = {(cuuint64_t)kHeadDim, (cuuint64_t)max_seq, (cuuint64_t)m.n_heads, (cuuint64_t)n_slots,
+                                (cuuint64_t)m.n_layers};
+    const cuuint64_t strides[4] = {rowb, rowb * max_seq, rowb * max_seq * m.n_heads,
+                                   rowb * max_seq * m.n_heads * n_slots};
+    const cuuint32_t box[5] = {(cuuint32_t)kHeadDim, (cuuint32_t)KVPOS, 1, 1, 1};
+    const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    for (int i = 0; i < 2; ++i)
+        if (enc(i ? &b.vmap : &b.kmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, i ? v_cache : k_cache, dims, strides, box,
+                estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return cudaErrorInvalidValue;
+    return cudaSuccess;
+}
+
 cudaError_t xk_launch(const MkParams &p, const XkConfig &xc, const XkBufs &b, cudaStream_t st) {
     XkParams xp{};
     xp.p = p;
+    xp.kmap = b.kmap;
+    xp.vmap = b.vmap;
     xp.hacc = b.hacc;
     xp.xacc = b.xacc;
     xp.epoch = b.epoch;
@@ -1346,7 +1451,7 @@ __global__ void mlp_by_slice_kernel(const uint8_t *tiles, int tile_bytes, int kc
 bool mlp_slice_ok(const MkLin &W, int n_heads) {
     const int S = W.in / n_heads;
     return n_heads > 0 && W.in % n_heads == 0 && S % 128 == 0 && S <= 256 && W.kc % S == 0 &&
-           mk_mlpk_sub_bytes(S, W.sbb) <= SLOT;
+           mk_mlpk_sub_bytes(S, W.sbb) <= SLOT && SLOT / mk_mlpk_sub_bytes(S, W.sbb) <= CW;
 }
 
 size_t mlp_slice_bytes(const MkLin &W, int n_heads) {
