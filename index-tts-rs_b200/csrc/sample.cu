@@ -13,6 +13,7 @@ namespace itts {
 
 constexpr int kSampleThreads = 1024;
 constexpr int kMaxSampleLogits = 16384;
+static_assert(kMaxSampleLogits == kSmallMaxLogits, "one logit limit for both sampler kernels");
 
 __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleArgs a) {
     extern __shared__ __align__(16) unsigned char sm_raw[];

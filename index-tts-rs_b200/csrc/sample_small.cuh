@@ -73,6 +73,50 @@ static __device__ int draw_candidate(SlotState &st, const int *ids, const float 
     return token;
 }
 
+// The same by one warp (all 32 lanes call it; lane 0's result is returned to every lane):
+// the top-p divisions run on the lanes in parallel (they do not depend on the running sum),
+// the sequential sums stay in candidate order on lane 0 with their loads unrolled ahead.
+// norm is scratch for k floats.
+static __device__ int draw_candidate_warp(SlotState &st, const int *ids, const float *probs, float *norm, int k,
+                                          int lane) {
+    float prob_sum = 0.0f;
+    if (lane == 0) {
+#pragma unroll 8
+        for (int i = 0; i < k; ++i) prob_sum = __fadd_rn(prob_sum, probs[i]);
+    }
+    prob_sum = __shfl_sync(0xffffffffu, prob_sum, 0);
+    if (prob_sum <= 0.0f || !isfinite(prob_sum)) return ids[0];  // :250-252
+    for (int i = lane; i < k; i += 32) norm[i] = __fdiv_rn(probs[i], prob_sum);
+    __syncwarp();
+    int token = 0;
+    if (lane == 0) {
+        const float top_p = st.top_p;
+        float cum = 0.0f;
+        int active = k;
+        for (int i = 0; i < k; ++i) {  // :254-264
+            if (i > 0 && cum > top_p) { active = i; break; }
+            cum = __fadd_rn(cum, norm[i]);
+        }
+        float active_sum = 0.0f;
+#pragma unroll 8
+        for (int i = 0; i < active; ++i) active_sum = __fadd_rn(active_sum, probs[i]);
+        if (active_sum <= 0.0f || !isfinite(active_sum)) {  // :270-272
+            token = ids[0];
+        } else {
+            uint64_t rs = st.rng;
+            const float draw = __fmul_rn(rng_next_f32(rs), active_sum);  // :274
+            st.rng = rs;
+            token = ids[active - 1];  // :283
+            float acc = 0.0f;
+            for (int i = 0; i < active; ++i) {
+                acc = __fadd_rn(acc, probs[i]);
+                if (draw <= acc) { token = ids[i]; break; }
+            }
+        }
+    }
+    return __shfl_sync(0xffffffffu, token, 0);
+}
+
 // generate_codes_after's loop step after a sample (sampler.rs:371-389).
 static __device__ void loop_step(const SampleArgs &a, SlotState &st, int col, int tok, int n_codes) {
     if (a.token_out) a.token_out[col] = tok;
@@ -108,6 +152,7 @@ static __device__ void loop_step(const SampleArgs &a, SlotState &st, int col, in
 // instruction memory.
 // ---------------------------------------------------------------------------
 constexpr int kSmallK = 64;
+constexpr int kSmallMaxLogits = 16384;  // logits per column (one register set of NTH threads)
 
 static __device__ __forceinline__ uint32_t order_key(float v) {
     const uint32_t b = v == 0.0f ? 0u : __float_as_uint(v);
@@ -116,11 +161,12 @@ static __device__ __forceinline__ uint32_t order_key(float v) {
 
 // Shared memory of the routine besides the logits and keys ([n] floats, then [n] keys).
 struct SmallSampleSmem {
+    SlotState st;  // the column's slot state, copied in at the start and out at the end
     uint32_t hist[256];
     uint32_t bin, above, count, eq;
     uint64_t cand[kSmallK];
     int ids[kSmallK];
-    float probs[kSmallK];
+    float probs[kSmallK], norm[kSmallK];
     float bestv[32];
     int besti[32];
     int token;
@@ -135,34 +181,51 @@ static __device__ void sample_small_body(const SampleArgs &a, int col, SmallSamp
     uint32_t &s_bin = sm.bin, &s_above = sm.above, &s_count = sm.count, &s_eq = sm.eq;
     uint64_t *cand = sm.cand;
     int *s_ids = sm.ids;
-    float *s_probs = sm.probs, *s_bestv = sm.bestv;
+    float *s_probs = sm.probs, *s_norm = sm.norm, *s_bestv = sm.bestv;
     int *s_besti = sm.besti;
     int &s_token = sm.token;
-    SlotState &st = a.slots[a.batch_slot[col]];
-    if (!st.active) return;
+    SlotState &gst = a.slots[a.batch_slot[col]];
+    if (!gst.active) return;  // (every thread reads the same flag)
     const int n = a.n_logits, lane = tid & 31, warp = tid >> 5;
     uint32_t *keys = reinterpret_cast<uint32_t *>(lgs + n);
     float *row = a.logits + (size_t)col * a.ld_logits;
+    // this thread's logits i = tid + NTH j, all loads in flight at once; the slot state into
+    // shared memory meanwhile
+    constexpr int E = (kSmallMaxLogits + NTH - 1) / NTH;
+    float v[E];
+#pragma unroll
+    for (int j = 0; j < E; ++j) {
+        const int i = tid + NTH * j;
+        v[j] = i < n ? row[i] : 0.0f;
+    }
+    constexpr int SW = (int)(sizeof(SlotState) / 8);
+    static_assert(sizeof(SlotState) % 8 == 0, "slot state copied in 8-byte words");
+    if (tid < SW) reinterpret_cast<uint64_t *>(&sm.st)[tid] = reinterpret_cast<const uint64_t *>(&gst)[tid];
+    sync();
+    SlotState &st = sm.st;
     const int n_codes = st.n_codes;
     const bool mask_stop = n_codes < st.min_codes && kStopMel < n;
     const float pen = st.rep_penalty;
     const bool do_pen = fabsf(__fsub_rn(pen, 1.0f)) > 1.1920929e-7f;
-#pragma unroll 4
-    for (int i = tid; i < n; i += NTH) {  // STOP mask, repetition penalty (sampler.rs:138-157)
-        float v = (mask_stop && i == kStopMel) ? -INFINITY : row[i];
-        if (do_pen && i < kBitsetWords * 64 && ((st.seen[i >> 6] >> (i & 63)) & 1ULL))
-            v = v < 0.0f ? __fmul_rn(v, pen) : __fdiv_rn(v, pen);
-        lgs[i] = v;
-        if (a.write_back) row[i] = v;
+#pragma unroll
+    for (int j = 0; j < E; ++j) {  // STOP mask, repetition penalty (sampler.rs:138-157)
+        const int i = tid + NTH * j;
+        if (i < n) {
+            float x = (mask_stop && i == kStopMel) ? -INFINITY : v[j];
+            if (do_pen && i < kBitsetWords * 64 && ((st.seen[i >> 6] >> (i & 63)) & 1ULL))
+                x = x < 0.0f ? __fmul_rn(x, pen) : __fdiv_rn(x, pen);
+            v[j] = x;
+            if (a.write_back) row[i] = x;
+        }
     }
-    sync();
 
     if (st.greedy) {  // argmax_finite (sampler.rs:395-405)
         float bv = -INFINITY;
         int bi = 0x7FFFFFFF;
-        for (int i = tid; i < n; i += NTH) {
-            const float v = lgs[i];
-            if (isfinite(v) && (bi == 0x7FFFFFFF || v > bv)) { bv = v; bi = i; }
+#pragma unroll
+        for (int j = 0; j < E; ++j) {
+            const int i = tid + NTH * j;
+            if (i < n && isfinite(v[j]) && (bi == 0x7FFFFFFF || v[j] > bv)) { bv = v[j]; bi = i; }
         }
         for (int off = 16; off > 0; off >>= 1) {
             const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
@@ -184,11 +247,14 @@ static __device__ void sample_small_body(const SampleArgs &a, int col, SmallSamp
         sync();
     } else {
         const float inv_temp = __fdiv_rn(1.0f, st.temperature);  // sampler.rs:210
-        for (int i = tid; i < n; i += NTH) {
-            const float v = lgs[i];
-            const float sv = isfinite(v) ? __fmul_rn(v, inv_temp) : -INFINITY;
-            lgs[i] = sv;
-            keys[i] = order_key(sv);
+#pragma unroll
+        for (int j = 0; j < E; ++j) {
+            const int i = tid + NTH * j;
+            if (i < n) {
+                const float sv = isfinite(v[j]) ? __fmul_rn(v[j], inv_temp) : -INFINITY;
+                lgs[i] = sv;
+                keys[i] = order_key(sv);
+            }
         }
         const uint32_t raw_k = st.top_k;
         const int k = min(kSmallK, (raw_k == 0 || raw_k >= (uint32_t)n) ? n : (int)raw_k);  // :221-226
@@ -289,11 +355,14 @@ static __device__ void sample_small_body(const SampleArgs &a, int col, SmallSamp
                 }
             }
             __syncwarp();
-            if (lane == 0) s_token = draw_candidate(st, s_ids, s_probs, k);
+            const int tok = draw_candidate_warp(st, s_ids, s_probs, s_norm, k, lane);
+            if (lane == 0) s_token = tok;
         }
         sync();
     }
     if (tid == 0) loop_step(a, st, col, s_token, n_codes);
+    sync();
+    if (tid < SW) reinterpret_cast<uint64_t *>(&gst)[tid] = reinterpret_cast<const uint64_t *>(&sm.st)[tid];
 }
 
 }  // namespace itts
