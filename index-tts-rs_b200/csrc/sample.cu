@@ -216,7 +216,7 @@ __global__ void __launch_bounds__(kSampleThreads) sample_kernel(SampleArgs a) {
 constexpr int kSmallThreads = 1024;
 
 __global__ void __launch_bounds__(kSmallThreads) sample_small_kernel(SampleArgs a) {
-    extern __shared__ __align__(16) float lgs[];  // [n] logits, then [n] order keys
+    extern __shared__ __align__(16) float lgs[];  // [n] logits, [n] order keys, [n] keys of one bin
     __shared__ SmallSampleSmem sm;
     sample_small_body<kSmallThreads>(a, blockIdx.x, sm, lgs, threadIdx.x, [] { __syncthreads(); });
 }
@@ -233,7 +233,7 @@ static size_t sample_smem_bytes(int n) {
 
 void launch_sample(const SampleArgs &a, cudaStream_t st) {
     if (a.small_k)
-        sample_small_kernel<<<a.nb, kSmallThreads, (size_t)a.n_logits * 2 * sizeof(float), st>>>(a);
+        sample_small_kernel<<<a.nb, kSmallThreads, (size_t)a.n_logits * 3 * sizeof(float), st>>>(a);
     else
         sample_kernel<<<a.nb, kSampleThreads, sample_smem_bytes(a.n_logits), st>>>(a);
 }
@@ -245,7 +245,7 @@ void kernels_init_sample() {
     cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                          (int)sample_smem_bytes(kMaxSampleLogits));
     cudaFuncSetAttribute(sample_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)(kMaxSampleLogits * 2 * sizeof(float)));
+                         (int)(kMaxSampleLogits * 3 * sizeof(float)));
 }
 
 }  // namespace itts

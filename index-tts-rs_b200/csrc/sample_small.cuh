@@ -74,15 +74,22 @@ static __device__ int draw_candidate(SlotState &st, const int *ids, const float 
 }
 
 // The same by one warp (all 32 lanes call it; lane 0's result is returned to every lane):
-// the top-p divisions run on the lanes in parallel (they do not depend on the running sum),
-// the sequential sums stay in candidate order on lane 0 with their loads unrolled ahead.
-// norm is scratch for k floats.
+// the top-p divisions run on the lanes in parallel (they do not depend on the running sum);
+// the sequential sums stay in candidate order on lane 0, reading the candidates in blocks
+// of 8 so that the loads are not in the chain of adds.  probs, norm and ids hold kSmallK
+// entries (those past k are read but not used); norm is scratch.
 static __device__ int draw_candidate_warp(SlotState &st, const int *ids, const float *probs, float *norm, int k,
                                           int lane) {
     float prob_sum = 0.0f;
     if (lane == 0) {
-#pragma unroll 8
-        for (int i = 0; i < k; ++i) prob_sum = __fadd_rn(prob_sum, probs[i]);
+        for (int i0 = 0; i0 < k; i0 += 8) {
+            float q[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) q[u] = probs[i0 + u];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (i0 + u < k) prob_sum = __fadd_rn(prob_sum, q[u]);
+        }
     }
     prob_sum = __shfl_sync(0xffffffffu, prob_sum, 0);
     if (prob_sum <= 0.0f || !isfinite(prob_sum)) return ids[0];  // :250-252
@@ -93,25 +100,59 @@ static __device__ int draw_candidate_warp(SlotState &st, const int *ids, const f
         const float top_p = st.top_p;
         float cum = 0.0f;
         int active = k;
-        for (int i = 0; i < k; ++i) {  // :254-264
-            if (i > 0 && cum > top_p) { active = i; break; }
-            cum = __fadd_rn(cum, norm[i]);
+        bool cut = false;
+        for (int i0 = 0; i0 < k && !cut; i0 += 8) {  // :254-264
+            float q[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) q[u] = norm[i0 + u];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int i = i0 + u;
+                if (i < k && !cut) {
+                    if (i > 0 && cum > top_p) {
+                        active = i;
+                        cut = true;
+                    } else {
+                        cum = __fadd_rn(cum, q[u]);
+                    }
+                }
+            }
         }
         float active_sum = 0.0f;
-#pragma unroll 8
-        for (int i = 0; i < active; ++i) active_sum = __fadd_rn(active_sum, probs[i]);
+        for (int i0 = 0; i0 < active; i0 += 8) {
+            float q[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) q[u] = probs[i0 + u];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (i0 + u < active) active_sum = __fadd_rn(active_sum, q[u]);
+        }
         if (active_sum <= 0.0f || !isfinite(active_sum)) {  // :270-272
             token = ids[0];
         } else {
             uint64_t rs = st.rng;
             const float draw = __fmul_rn(rng_next_f32(rs), active_sum);  // :274
             st.rng = rs;
-            token = ids[active - 1];  // :283
+            int pick = active - 1;  // :283
             float acc = 0.0f;
-            for (int i = 0; i < active; ++i) {
-                acc = __fadd_rn(acc, probs[i]);
-                if (draw <= acc) { token = ids[i]; break; }
+            bool found = false;
+            for (int i0 = 0; i0 < active && !found; i0 += 8) {
+                float q[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) q[u] = probs[i0 + u];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const int i = i0 + u;
+                    if (i < active && !found) {
+                        acc = __fadd_rn(acc, q[u]);
+                        if (draw <= acc) {
+                            pick = i;
+                            found = true;
+                        }
+                    }
+                }
             }
+            token = ids[pick];
         }
     }
     return __shfl_sync(0xffffffffu, token, 0);
@@ -173,7 +214,8 @@ struct SmallSampleSmem {
 };
 
 // Samples batch column `col` with NTH threads (tid 0..NTH-1, a multiple of 32, at least
-// 256); sync() is a barrier over exactly those threads.  lgs holds 2 n_logits words.
+// 256); sync() is a barrier over exactly those threads.  lgs holds 3 n_logits words: the
+// scaled logits, their order keys, and the keys of the first radix pass's selected bin.
 template <int NTH, class Sync>
 static __device__ void sample_small_body(const SampleArgs &a, int col, SmallSampleSmem &sm, float *lgs, int tid,
                                          Sync sync) {
@@ -187,7 +229,7 @@ static __device__ void sample_small_body(const SampleArgs &a, int col, SmallSamp
     SlotState &gst = a.slots[a.batch_slot[col]];
     if (!gst.active) return;  // (every thread reads the same flag)
     const int n = a.n_logits, lane = tid & 31, warp = tid >> 5;
-    uint32_t *keys = reinterpret_cast<uint32_t *>(lgs + n);
+    uint32_t *keys = reinterpret_cast<uint32_t *>(lgs + n), *bin_keys = keys + n;
     float *row = a.logits + (size_t)col * a.ld_logits;
     // this thread's logits i = tid + NTH j, all loads in flight at once; the slot state into
     // shared memory meanwhile
@@ -247,33 +289,24 @@ static __device__ void sample_small_body(const SampleArgs &a, int col, SmallSamp
         sync();
     } else {
         const float inv_temp = __fdiv_rn(1.0f, st.temperature);  // sampler.rs:210
+        uint32_t kr[E];  // this thread's order keys (registers; 0 past n, below every key in use)
 #pragma unroll
         for (int j = 0; j < E; ++j) {
             const int i = tid + NTH * j;
+            kr[j] = 0u;
             if (i < n) {
                 const float sv = isfinite(v[j]) ? __fmul_rn(v[j], inv_temp) : -INFINITY;
                 lgs[i] = sv;
-                keys[i] = order_key(sv);
+                kr[j] = order_key(sv);
+                keys[i] = kr[j];
             }
         }
         const uint32_t raw_k = st.top_k;
         const int k = min(kSmallK, (raw_k == 0 || raw_k >= (uint32_t)n) ? n : (int)raw_k);  // :221-226
         uint32_t prefix = 0, pmask = 0, remaining = (uint32_t)k;
-        for (int shift = 24; shift >= 0; shift -= 8) {  // radix select of the k-th largest key
-            if (tid < 256) hist[tid] = 0;
-            sync();  // also: keys written / the previous pass's s_bin read
-            for (int i0 = 0; i0 < n; i0 += NTH) {  // (uniform trip count: warp-wide match)
-                const int i = i0 + tid;
-                uint32_t bin = 0x100u;  // no bin: out of range or outside the prefix
-                if (i < n) {
-                    const uint32_t key = keys[i];
-                    if ((key & pmask) == prefix) bin = (key >> shift) & 0xFFu;
-                }
-                // one shared-memory atomic per distinct bin of the warp (most keys share a few
-                // bins in the first passes)
-                const unsigned peers = __match_any_sync(0xffffffffu, bin);
-                if (bin != 0x100u && lane == __ffs(peers) - 1) atomicAdd(&hist[bin], (uint32_t)__popc(peers));
-            }
+        // the bin holding the k-th largest key among the keys matching (prefix, pmask) at this
+        // digit: s_bin, s_above (keys in higher bins) and s_eq (keys in the bin)
+        auto pick_bin = [&]() {
             sync();
             if (warp == 0) {  // lane L holds bins 255-8L .. 248-8L (top-down order)
                 uint32_t c[8], sum = 0;
@@ -299,6 +332,41 @@ static __device__ void sample_small_body(const SampleArgs &a, int col, SmallSamp
                 }
             }
             sync();
+        };
+        // one shared-memory atomic per distinct bin of the warp (most keys share a few bins)
+        auto count = [&](uint32_t key, bool in, int shift) {
+            const uint32_t bin = in && (key & pmask) == prefix ? (key >> shift) & 0xFFu : 0x100u;
+            const unsigned peers = __match_any_sync(0xffffffffu, bin);
+            if (bin != 0x100u && lane == __ffs(peers) - 1) atomicAdd(&hist[bin], (uint32_t)__popc(peers));
+        };
+        // radix select of the k-th largest key: the first digit over every key (registers),
+        // then the keys of its bin are gathered and the other three digits run over them only
+        if (tid < 256) hist[tid] = 0;
+        if (tid == 0) s_count = 0;
+        sync();
+#pragma unroll
+        for (int j = 0; j < E; ++j)
+            if (j * NTH < n) count(kr[j], tid + NTH * j < n, 24);  // (uniform trip count)
+        pick_bin();
+        prefix = s_bin << 24;
+        pmask = 0xFF000000u;
+        remaining -= s_above;
+        const int m = (int)s_eq;  // keys in the selected bin
+#pragma unroll
+        for (int j = 0; j < E; ++j) {  // gather them (any order: only their digits are counted)
+            if (j * NTH >= n) break;
+            const bool in = tid + NTH * j < n && (kr[j] & pmask) == prefix;
+            const unsigned bal = __ballot_sync(0xffffffffu, in);
+            uint32_t base = 0;
+            if (lane == 0 && bal) base = atomicAdd(&s_count, (uint32_t)__popc(bal));
+            base = __shfl_sync(0xffffffffu, base, 0);
+            if (in) bin_keys[base + __popc(bal & ((1u << lane) - 1u))] = kr[j];
+        }
+        for (int shift = 16; shift >= 0; shift -= 8) {
+            if (tid < 256) hist[tid] = 0;
+            sync();  // also: the gathered keys written / the previous pass's s_bin read
+            for (int t0 = 0; t0 < m; t0 += NTH) count(t0 + tid < m ? bin_keys[t0 + tid] : 0u, t0 + tid < m, shift);
+            pick_bin();
             prefix |= s_bin << shift;
             pmask |= 0xFFu << shift;
             remaining -= s_above;
