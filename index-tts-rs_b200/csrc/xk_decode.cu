@@ -746,8 +746,8 @@ struct XkConsumer {
     }
     // attention of the cluster's head over this rank's K/V tiles: one record (m, l, acc[64])
     // per rank into every CTA of the cluster, each of which merges them into the head's 64
-    // outputs.  Two tiles at a time, as one run of n <= 168 positions; warp w takes positions
-    // [16w, 16w + 16) of the run on the tensor cores: S = K q with mma.sync (K rows through
+    // outputs.  Up to four tiles at a time, as one run of n <= 336 positions; warp w takes the
+    // 16-position m-tiles w and w + CW of the run on the tensor cores: S = K q with mma.sync (K rows through
     // ldmatrix from the swizzled tile; q as the B operand, column 0 its fp16 value and column 1
     // the fp16 remainder, so the products carry about 22 bits of q), an online softmax per warp,
     // then O^T = V^T P (ldmatrix.trans; P split the same way into columns 0 and 1).  Rows past
@@ -775,40 +775,75 @@ struct XkConsumer {
         for (int dt = 0; dt < 4; ++dt) o[dt][0] = o[dt][1] = o[dt][2] = o[dt][3] = 0.f;
         const int kvt = T->kvt, lold = T->lold;
         const int mi = lane >> 3, r8 = lane & 7;  // ldmatrix: this lane addresses row r8 of matrix mi
+        // up to KVG tiles at a time as one run of n positions (v -> tile v / KVPOS, row v % KVPOS:
+        // only the last tile of the range can be short); warp w takes the 16-position m-tiles
+        // w and w + CW of the run (one online-softmax update for both)
+        constexpr int KVG = (2 * CW * 16) / KVPOS;  // 4
+        static_assert(KVG >= 1 && KVG <= NSLOT / 2, "K/V tiles per update");
         for (int t = T->t_lo; t < T->t_hi;) {
-            const int npa = min(KVPOS, lold - t * KVPOS);
-            if (npa <= 0) {  // (only with no cached positions: nothing was copied)
+            const int ng = min(KVG, T->t_hi - t);
+            const int n = min(ng * KVPOS, lold - t * KVPOS);
+            if (n <= 0) {  // (only with no cached positions: nothing was copied)
                 ++t;
                 continue;
             }
-            const bool two = t + 1 < T->t_hi;  // (a later tile of the range is never empty)
-            const int npb = two ? min(KVPOS, lold - (t + 1) * KVPOS) : 0, n = npa + npb;
-            wait_seq(seq, 3);
-            if (two) wait_seq(seq + 1, 3);
-            const int v0 = warp * 16;
-            if (v0 < n) {
-                const uint32_t ta = su32(ring_at(seq)), tb = two ? su32(ring_at(seq + 1)) : ta;
+            for (int gi = 0; gi < ng; ++gi) wait_seq(seq + gi, 3);
+            const int ma = warp * 16, mb = (warp + CW) * 16;  // first positions of the two m-tiles
+            if (ma < n) {
+                const uint32_t ring0 = su32(smem);
                 // K row of position v (row 0 of the first tile past the run)
                 auto row_of = [&](int v) -> uint32_t {
-                    const int vv = v < n ? v : 0;
-                    return vv < npa ? ta + vv * 128 : tb + (vv - npa) * 128;
+                    const int vv = v < n ? v : 0, tt = vv / KVPOS;
+                    return ring0 + ((seq + tt) & (NSLOT - 1)) * SLOT + (vv - tt * KVPOS) * 128;
                 };
-                // S = K q: A fragments rows v0 + r8 (+8 for matrices 1, 3), k chunks 2 kk (+1 for 2, 3)
-                const uint32_t rk = row_of(v0 + r8 + (mi & 1) * 8);
-                float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+                // S = K q for the m-tile at v0: A fragments rows v0 + r8 (+8 for matrices 1, 3), k
+                // chunks 2 kk (+1 for 2, 3); lanes (g, 0) get the scores of v0 + g and v0 + g + 8
+                auto scores = [&](int v0, float &sa, float &sb) {
+                    const uint32_t rk = row_of(v0 + r8 + (mi & 1) * 8);
+                    float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                for (int kk = 0; kk < 4; kk += 2) {
-                    uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
-                    ldsm_x4(swz(rk, 2 * kk + (mi >> 1)), a0, a1, a2, a3);
-                    ldsm_x4(swz(rk, 2 * kk + 2 + (mi >> 1)), b0, b1, b2, b3);
-                    mma16816(s0, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
-                    mma16816(s1, b0, b1, b2, b3, qb[kk + 1][0], qb[kk + 1][1]);
-                }
-                // lanes (g, 0): scores of positions v0 + g and v0 + g + 8 (columns 0 + 1)
-                const bool va = c == 0 && v0 + g < n, vb = c == 0 && v0 + g + 8 < n;
-                const float sa = va ? (s0[0] + s0[1]) + (s1[0] + s1[1]) : -INFINITY;
-                const float sb = vb ? (s0[2] + s0[3]) + (s1[2] + s1[3]) : -INFINITY;
-                float mt = fmaxf(sa, sb);
+                    for (int kk = 0; kk < 4; kk += 2) {
+                        uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+                        ldsm_x4(swz(rk, 2 * kk + (mi >> 1)), a0, a1, a2, a3);
+                        ldsm_x4(swz(rk, 2 * kk + 2 + (mi >> 1)), b0, b1, b2, b3);
+                        mma16816(s0, a0, a1, a2, a3, qb[kk][0], qb[kk][1]);
+                        mma16816(s1, b0, b1, b2, b3, qb[kk + 1][0], qb[kk + 1][1]);
+                    }
+                    sa = c == 0 && v0 + g < n ? (s0[0] + s0[1]) + (s1[0] + s1[1]) : -INFINITY;
+                    sb = c == 0 && v0 + g + 8 < n ? (s0[2] + s0[3]) + (s1[2] + s1[3]) : -INFINITY;
+                };
+                // O^T += V^T P for the m-tile at v0 with its weights pa (position v0 + g) and pb
+                // (v0 + g + 8) on lanes (g, 0): P as B fragments (lane (g, c) takes positions 2c,
+                // 2c + 1 and 2c + 8, 2c + 9 from lanes (2c, 0) and (2c + 1, 0); column 0 fp16
+                // values, column 1 remainders), V^T through ldmatrix.trans (positions v0 + r8, +8
+                // for matrices 2, 3; dim chunks 2 dt, +1 for matrices 1, 3)
+                auto accumulate = [&](int v0, float pa, float pb) {
+                    const float p0 = __shfl_sync(0xffffffffu, pa, 8 * c), p8 = __shfl_sync(0xffffffffu, pb, 8 * c);
+                    const float p1 = __shfl_sync(0xffffffffu, pa, 8 * c + 4);
+                    const float p9 = __shfl_sync(0xffffffffu, pb, 8 * c + 4);
+                    const __half2 h01 = __floats2half2_rn(p0, p1), h89 = __floats2half2_rn(p8, p9);
+                    uint32_t pb0 = 0u, pb1 = 0u;
+                    if (g == 0) {
+                        pb0 = *reinterpret_cast<const uint32_t *>(&h01);
+                        pb1 = *reinterpret_cast<const uint32_t *>(&h89);
+                    } else if (g == 1) {
+                        const float2 f01 = __half22float2(h01), f89 = __half22float2(h89);
+                        pb0 = pack_h2(p0 - f01.x, p1 - f01.y);
+                        pb1 = pack_h2(p8 - f89.x, p9 - f89.y);
+                    }
+                    const uint32_t rv = row_of(v0 + r8 + (mi >> 1) * 8) + KV_VOFF;
+#pragma unroll
+                    for (int dt = 0; dt < 4; ++dt) {
+                        uint32_t a0, a1, a2, a3;
+                        ldsm_x4_t(swz(rv, 2 * dt + (mi & 1)), a0, a1, a2, a3);
+                        mma16816(o[dt], a0, a1, a2, a3, pb0, pb1);
+                    }
+                };
+                const bool two = mb < n;  // (uniform)
+                float sa, sb, sc = -INFINITY, sd = -INFINITY;
+                scores(ma, sa, sb);
+                if (two) scores(mb, sc, sd);
+                float mt = fmaxf(fmaxf(sa, sb), fmaxf(sc, sd));
                 mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 4));
                 mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 8));
                 mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
@@ -822,34 +857,16 @@ struct XkConsumer {
                         for (int e = 0; e < 4; ++e) o[dt][e] *= corr;
                     m = mt;
                 }
-                const float pa = va ? exp2f(sa - m) : 0.f, pb = vb ? exp2f(sb - m) : 0.f;
-                ls += pa + pb;
-                // P as B fragments: lane (g, c) takes positions 2c, 2c + 1 (b0) and 2c + 8, 2c + 9
-                // (b1) from lanes (2c, 0) and (2c + 1, 0); column 0 fp16 values, column 1 remainders
-                const float p0 = __shfl_sync(0xffffffffu, pa, 8 * c), p8 = __shfl_sync(0xffffffffu, pb, 8 * c);
-                const float p1 = __shfl_sync(0xffffffffu, pa, 8 * c + 4), p9 = __shfl_sync(0xffffffffu, pb, 8 * c + 4);
-                const __half2 h01 = __floats2half2_rn(p0, p1), h89 = __floats2half2_rn(p8, p9);
-                uint32_t pb0 = 0u, pb1 = 0u;
-                if (g == 0) {
-                    pb0 = *reinterpret_cast<const uint32_t *>(&h01);
-                    pb1 = *reinterpret_cast<const uint32_t *>(&h89);
-                } else if (g == 1) {
-                    const float2 f01 = __half22float2(h01), f89 = __half22float2(h89);
-                    pb0 = pack_h2(p0 - f01.x, p1 - f01.y);
-                    pb1 = pack_h2(p8 - f89.x, p9 - f89.y);
-                }
-                // O^T += V^T P: A fragments (ldmatrix.trans) positions v0 + r8 (+8 for matrices
-                // 2, 3), dim chunks 2 dt (+1 for matrices 1, 3)
-                const uint32_t rv = row_of(v0 + r8 + (mi >> 1) * 8) + KV_VOFF;
-#pragma unroll
-                for (int dt = 0; dt < 4; ++dt) {
-                    uint32_t a0, a1, a2, a3;
-                    ldsm_x4_t(swz(rv, 2 * dt + (mi & 1)), a0, a1, a2, a3);
-                    mma16816(o[dt], a0, a1, a2, a3, pb0, pb1);
-                }
+                // (positions past the run weigh 0; a NaN score of a position in it stays NaN)
+                const bool c0 = c == 0;
+                const float pa = c0 && ma + g < n ? exp2f(sa - m) : 0.f, pb = c0 && ma + g + 8 < n ? exp2f(sb - m) : 0.f;
+                const float pc = c0 && mb + g < n ? exp2f(sc - m) : 0.f, pd = c0 && mb + g + 8 < n ? exp2f(sd - m) : 0.f;
+                ls += (pa + pb) + (pc + pd);
+                accumulate(ma, pa, pb);
+                if (two) accumulate(mb, pc, pd);
             }
-            release(two ? 2 : 1);
-            t += two ? 2 : 1;
+            release(ng);
+            t += ng;
         }
         if (T->active && T->t_hi == kvt && T->t_hi > T->t_lo && warp == CW - 1) {  // the new position
             const float *kn = qkvh + 64, *vn = qkvh + 128;
