@@ -117,7 +117,7 @@ class ClockSampler:
 
 
 METRIC = "mel tokens/s (cfg2 batch-1 decode)"
-XK_TRAFFIC = 685_748_992 + 8_116_736  # DRAM bytes of one batch-1 decode-step launch (ncu)
+XK_TRAFFIC = 686_756_096 + 5_795_328  # DRAM bytes of one batch-1 decode-step launch (ncu)
 DTYPE = "int8 weights (g64 affine, fp16 scales) x fp16 activations and KV, fp32 accumulate"
 
 
@@ -337,7 +337,7 @@ def run_ours(args, rank, world, local_rank):
                      # length, from an ncu capture of this kernel build (not measured here)
                      "traffic": XK_TRAFFIC if kname == "xk_decode_kernel" else None,
                      "traffic_source": "ncu --set full capture of one xk_decode_kernel launch at KV 1,384 "
-                                       "(685,748,992 B read + 8,116,736 B written); not measured in this run"},
+                                       "(686,756,096 B read + 5,795,328 B written); not measured in this run"},
         "clocks": clk,
     }
     if cfg5 is not None:
