@@ -139,8 +139,8 @@ int32_t itts_kv_max_seq(const itts_kv *kv);
 int32_t itts_kv_max_batch(const itts_kv *kv);
 /* Which decode-step kernel runs a step of `n_columns` batch columns on this cache:
  * 2 = the persistent grid-wide kernel (up to 4 columns), 3 = the multi-launch GEMM path,
- * 4 = one 6-CTA cluster per attention head (batch 1 by default; ITTS_XK=0 at
- * itts_kv_create turns it off).  No reference counterpart (the
+ * 4 = one 6-CTA cluster per attention head, launched once per column for up to 4 columns
+ * (the default; ITTS_XK=0 at itts_kv_create turns it off).  No reference counterpart (the
  * reference has one MLX code path); used by tests and the benchmark to name the kernel. */
 int32_t itts_kv_decode_kernel(const itts_kv *kv, int32_t n_columns);
 

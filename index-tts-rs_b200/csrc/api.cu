@@ -878,7 +878,7 @@ extern "C" int32_t itts_kv_max_seq(const itts_kv *kv) { return kv ? kv->max_seq 
 extern "C" int32_t itts_kv_max_batch(const itts_kv *kv) { return kv ? kv->max_batch : 0; }
 extern "C" int32_t itts_kv_decode_kernel(const itts_kv *kv, int32_t n_columns) {
     if (!kv || n_columns < 1 || n_columns > kv->max_batch) return 0;
-    if (n_columns == 1 && kv->db.xk.grid > 0) return 4;
+    if (n_columns <= XK_SEQ_MAX_NB && kv->db.xk.grid > 0) return 4;
     if (n_columns <= MK_MAX_NB && kv->db.mk_grid > 0 && kv->db.mk_nslot[n_columns] >= 2) return 2;
     return 3;
 }

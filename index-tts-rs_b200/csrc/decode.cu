@@ -277,14 +277,19 @@ static bool use_wide(const ModelView &m, const DecodeBufs &b, int nb) {
            skinny_ok(m.mel_head, nb);
 }
 
+// Steps of up to XK_SEQ_MAX_NB columns run the batch-1 cluster kernel once per column (each
+// launch streams the weights again, but a column costs less than in the grid-wide kernel).
+static bool use_xk(const DecodeBufs &b, int nb) { return b.xk.grid > 0 && nb <= XK_SEQ_MAX_NB; }
+
 int decode_forward_launches(const ModelView &m, const DecodeBufs &b, int nb) {
-    if ((nb == 1 && b.xk.grid > 0) || use_mk(b, nb)) return 1;
+    if (use_xk(b, nb)) return nb;
+    if (use_mk(b, nb)) return 1;
     if (use_wide(m, b, nb)) return 1 + 6 * m.n_layers + 3;
     return 1 + 7 * m.n_layers + 3;
 }
 
 bool decode_uses_f16_weights(const ModelView &m, const DecodeBufs &b, int nb) {
-    return !((nb == 1 && b.xk.grid > 0) || use_mk(b, nb) || use_wide(m, b, nb));
+    return !(use_xk(b, nb) || use_mk(b, nb) || use_wide(m, b, nb));
 }
 
 // Steps of 5..SK_MAX_NB columns: LayerNorms into fragment order, the skinny int8 GEMMs, the
@@ -314,7 +319,17 @@ static cudaError_t decode_forward_wide(const ModelView &m, const DecodeView &dv,
 
 cudaError_t decode_forward(const ModelView &m, const DecodeView &dv, DecodeBufs &b,
                            cudaStream_t st) {
-    if (dv.nb == 1 && b.xk.grid > 0) return xk_launch(mk_params(m, dv, b), b.xk, b.xkb, st);
+    if (use_xk(b, dv.nb)) {
+        for (int col = 0; col < dv.nb; ++col) {
+            MkParams p = mk_params(m, dv, b);
+            p.batch_slot = dv.batch_slot + col;
+            p.nb = 1;
+            p.logits = b.logits + (size_t)col * m.mel_vocab;
+            const cudaError_t e = xk_launch(p, b.xk, b.xkb, st);
+            if (e != cudaSuccess) return e;
+        }
+        return cudaSuccess;
+    }
     if (use_mk(b, dv.nb)) return mk_launch(mk_params(m, dv, b), st);
     if (use_wide(m, b, dv.nb)) return decode_forward_wide(m, dv, b, st);
     const int d = m.d;

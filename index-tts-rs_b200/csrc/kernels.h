@@ -118,6 +118,7 @@ cudaError_t decode_forward(const ModelView &m, const DecodeView &dv, DecodeBufs 
 // creation turns it off).
 // Fills `out` and returns the grid size, or -1 when the model or the device does not fit it.
 int xk_config(const ModelView &m, XkConfig *out);
+constexpr int XK_SEQ_MAX_NB = 4;  // steps of up to this many columns: one cluster-kernel launch per column
 // The K/V tensor maps of a cache (XkBufs::kmap / vmap).
 cudaError_t xk_make_kv_maps(const ModelView &m, __half *k_cache, __half *v_cache, int n_slots, int max_seq,
                             XkBufs &b);

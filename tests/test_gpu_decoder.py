@@ -75,7 +75,8 @@ def test_decode_kernel_selection(small, monkeypatch):
     gpt, _ = small
     kv4 = ig.KvCache(gpt, max_seq=256, max_batch=8)
     assert kv4.decode_kernel(1) == "xk_decode_kernel"
-    assert kv4.decode_kernel(2) == "mk_decode_kernel"
+    assert kv4.decode_kernel(2) == "xk_decode_kernel"  # (one launch per column up to 4 columns)
+    assert kv4.decode_kernel(4) == "xk_decode_kernel"
     assert kv4.decode_kernel(5) == "gemm path"
     for name in KERNELS:
         with monkeypatch.context() as mp:

@@ -93,11 +93,13 @@ def test_cfg2_kv_lengths_teacher_forced(full, cfg2_trajectory, monkeypatch, kern
     print(f"cfg2 KV 635-2135 on {kernel}: max |dlogit| {err:.2e}, argmax agreement {agree:.4f}")
 
 
-def test_cfg2_kv_lengths_two_columns(full, cfg2_trajectory):
-    """The same trajectory in both columns of 2-column decode steps (the persistent
-    grid-wide kernel with two columns): each column must match the checker."""
+def test_cfg2_kv_lengths_two_columns(full, cfg2_trajectory, monkeypatch):
+    """The same trajectory in both columns of 2-column decode steps on the persistent
+    grid-wide kernel (ITTS_XK=0: by default 2-column steps run the cluster kernel once per
+    column, which the batch-1 tests cover): each column must match the checker."""
     gpt, _ = full
     text, conds, codes, kept, am = cfg2_trajectory
+    monkeypatch.setenv("ITTS_XK", "0")
     kv = ig.KvCache(gpt, max_seq=PROMPT + N_STEPS + 8, max_batch=2)
     assert kv.decode_kernel(2) == "mk_decode_kernel"
     p0 = gpt.prefill(text, conds, 1, kv, slot=0)
