@@ -457,7 +457,10 @@ extern "C" int itts_gpt_from_tensors(const itts_tensor *tensors, int32_t n_tenso
     // (about 42 MB for the IndexTTS-2.5 decoder).  Every layer's c_proj must have layer 0's
     // shape; otherwise, or when the copy cannot be made, no layer gets one and batch-1 steps
     // run on the grid-wide kernel instead (xk_config declines a model without the copies).
-    {
+    // ITTS_XK=0 at load: neither these nor the sliced mlp copies below are made.
+    const char *xk_env = getenv("ITTS_XK");
+    const bool want_xk = !(xk_env && xk_env[0] == '0');
+    if (want_xk) {
         const MkLin &P0 = g->layers[0].proj;
         const size_t per = (size_t)(d / 64) * P0.n_rb * mk_projh_chunk_bytes(P0.sbb);
         bool fits = d % 64 == 0 && P0.n_kc == 1 && P0.kc == (int)d;
@@ -482,9 +485,9 @@ extern "C" int itts_gpt_from_tensors(const itts_tensor *tensors, int32_t n_tenso
         }
     }
     // copies of the mlp projections sliced by input (batch-1 cluster decode step: each cluster
-    // applies the rows of its own slice of the c_fc output), made once here (about 160 MB for
+    // applies the rows of its own slice of the c_fc output), made once here (about 167 MB for
     // the IndexTTS-2.5 decoder).  Same all-or-nothing rule as the c_proj copies.
-    {
+    if (want_xk) {
         const int H = (int)(d / 64);
         const MkLin &M0 = g->layers[0].mlp;
         const size_t per = mlp_slice_bytes(M0, H);
