@@ -29,15 +29,17 @@
 // round-robin over the grid (tile t on CTA t % grid).
 //
 // Per CTA: 11 consumer warps + 1 producer warp.  The producer lane streams the CTA's weight
-// tiles and K/V rows into an 8-slot cp.async.bulk ring (no multicast) ahead of the stages;
-// consumers dequantize in registers and run mma.sync m16n8k16 with the activation (the same
-// arithmetic as the other decode kernels), per-warp partial sums reduced once per tile.
+// tiles (cp.async.bulk) and K/V tiles (TMA tensor loads, 128-byte swizzle) into an 8-slot
+// ring (no multicast) ahead of the stages; consumers dequantize in registers and run
+// mma.sync m16n8k16 with the activation (the same arithmetic as the other decode kernels),
+// and run the attention on mma.sync too.
 //
-// Buffer reuse: the landing buffers (x/h, attention output, u, the head's q/k/v, rank 0's
-// records) are rewritten once per layer without double buffering.  A cluster peer can be
-// at most one exchange ahead of a CTA (finishing exchange e needs every peer's part of e,
-// sent only after that peer finished exchange e-1), and each buffer is rewritten only after
-// every CTA of the cluster has consumed its previous contents.
+// Buffer reuse: the landing buffers (x/h, u, the head's q/k/v, the head's attention records)
+// are rewritten once per layer without double buffering.  Each is rewritten by a peer only
+// after every CTA of the cluster has consumed its previous contents: a peer's next push into
+// it needs this CTA's own contribution to a later hand-off (its q/k/v rows, its attention
+// record, its c_fc rows or its accumulator partials), which this CTA makes only after it has
+// read the buffer.
 //
 // Every wait and poll is bounded; on a timeout the kernel records an error code in p.err
 // (read by the host as ITTS_E_TIMEOUT), skips the remaining waits and exits cleanly.
