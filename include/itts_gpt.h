@@ -309,14 +309,24 @@ int itts_codec_decode(itts_codec *codec, const int32_t *codes, int32_t n_codes, 
 int itts_bench_decode_forward(itts_gpt *gpt, itts_kv *kv, int32_t nb, int32_t kv_len,
                               int32_t iters, float *ms_per_step, int32_t *launches_per_step);
 
-/* The same for one step of nb <= 4 columns with per-CTA stage timestamps (device
- * globaltimer, ns) recorded by whichever single-launch decode-step kernel the cache runs for
- * nb (itts_kv_decode_kernel): out[cta * events_per_cta + i], 0 where a CTA recorded nothing
- * (the cluster kernels use fewer CTAs than the reported grid).  out_len must be at least
- * grid * 256.  No reference counterpart (a profiling aid). */
+/* The same for one step of nb <= 4 columns with per-CTA stage timestamps recorded by
+ * whichever single-launch decode-step kernel the cache runs for nb (itts_kv_decode_kernel):
+ * device globaltimer ns in the grid-wide kernel, SM clock cycles in the cluster kernel.
+ * out[cta * events_per_cta + i], 0 where a CTA recorded nothing (the cluster kernel uses fewer
+ * CTAs than the reported grid).  out_len must be at least grid * 512.  No reference
+ * counterpart (a profiling aid). */
 int itts_bench_trace(itts_gpt *gpt, itts_kv *kv, int32_t nb, int32_t kv_len,
                      unsigned long long *out, int32_t out_len, int32_t *grid,
                      int32_t *events_per_cta);
+
+/* ---- test hook (no reference counterpart) ------------------------------------------- */
+
+/* Makes the cache's batch-1 decode steps on the cluster kernel (xk_decode_kernel) start
+ * with a bounded wait on a device word that nothing sets: `polls` polls about 1 us apart,
+ * after which the step does nothing else and the call returns ITTS_E_TIMEOUT, with the
+ * slot's state as before the step.  polls == 0 turns the wait off.  ITTS_E_VALIDATION when
+ * polls is outside 0..2^20 or the cache runs another batch-1 kernel. */
+int itts_test_stall(itts_gpt *gpt, itts_kv *kv, int32_t polls);
 
 #ifdef __cplusplus
 }

@@ -792,6 +792,7 @@ extern "C" int itts_kv_create(itts_gpt *g, int32_t max_seq, int32_t max_batch, i
         if (e == cudaSuccess) e = cudaMemsetAsync(kv->db.epoch, 0, sizeof(uint32_t) * std::max(grid, 1024), g->stream);
         A((void **)&kv->db.err, sizeof(int) * 4);
         kv->db.trace = nullptr;
+        kv->db.stall = 0;
         kv->db.xk = XkConfig{};
         XkConfig xc;
         if (e == cudaSuccess && xk_config(m, &xc) > 0) {
@@ -1869,6 +1870,25 @@ extern "C" int itts_bench_trace(itts_gpt *g, itts_kv *kv, int32_t nb, int32_t kv
     *grid = kv->db.mk_grid;
     *events_per_cta = MK_TRACE_EVENTS;
     return rc;
+}
+
+// Test hook: batch-1 steps on the cluster kernel first poll a device word that nothing sets,
+// `polls` times about 1 us apart, then give up and report ITTS_E_TIMEOUT.  The step's cached
+// CUDA graphs are dropped so that generate captures the new value.
+extern "C" int itts_test_stall(itts_gpt *g, itts_kv *kv, int32_t polls) {
+    if (!g || !kv || kv->gpt != g) return validation("gpt", "null pointer or cache of another model");
+    if (polls < 0 || polls > (1 << 20)) return validation("polls", "out of range 0..2^20");
+    if (kv->db.xk.grid <= 0) return validation("polls", "this cache does not run the cluster kernel");
+    CUDA_TRY(cudaSetDevice(g->device));
+    CUDA_TRY(cudaStreamSynchronize(g->stream));
+    for (size_t i = 0; i < kv->graphs.size(); ++i) {
+        if (kv->graphs[i]) cudaGraphExecDestroy(kv->graphs[i]);
+        if (kv->graph_defs[i]) cudaGraphDestroy(kv->graph_defs[i]);
+        kv->graphs[i] = nullptr;
+        kv->graph_defs[i] = nullptr;
+    }
+    kv->db.stall = polls;
+    return ITTS_OK;
 }
 
 

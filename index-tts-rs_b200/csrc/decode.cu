@@ -263,6 +263,7 @@ static MkParams mk_params(const ModelView &m, const DecodeView &dv, DecodeBufs &
     p.epoch = b.epoch;
     p.err = b.err;
     p.trace = b.trace;
+    p.stall = b.stall;
     return p;
 }
 

@@ -60,6 +60,7 @@ struct DecodeBufs {
     XkBufs xkb;
     int *sk_counters;  // split-K counters of the skinny decode GEMMs (zero between launches)
     bool wide_int8;    // steps of 5..SK_MAX_NB columns run the skinny int8 GEMMs
+    int stall;         // test hook copied into MkParams::stall (itts_test_stall)
 };
 
 // Prefill scratch for one request of up to max_tokens positions.

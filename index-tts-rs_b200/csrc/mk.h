@@ -82,11 +82,15 @@ struct MkParams {
     int *err;
     unsigned long long *trace;  // optional [grid][MK_TRACE_EVENTS] stage stamps (globaltimer ns in
                                 // the grid-wide kernel, SM clock cycles in the cluster kernel)
+    int stall;  // test hook (0: off): the cluster kernel first polls err[3], which nothing sets,
+                // this many times and then reports a timeout (MK_ERR_STALL)
 };
 constexpr int MK_TRACE_EVENTS = 512;
 // Error word value of a decode step whose fixed-point c_proj sum would overflow (any other
 // nonzero value names a bounded wait that gave up).
 constexpr int MK_ERR_RANGE = 1000;
+// Error word value of the test hook's wait (MkParams::stall) that gave up.
+constexpr int MK_ERR_STALL = 97;
 
 __host__ __device__ inline int frag_pos_host(int k) {
     const int b = k >> 4, kk = k & 15, c = (kk & 7) >> 1, hi = kk >> 3, lo = kk & 1;

@@ -1154,6 +1154,21 @@ __global__ void __launch_bounds__(NT, 1) xk_decode_kernel(const __grid_constant_
     // CTA reads the same slot state, so all of them leave here, before any barrier, copy or
     // write (the launch counter and the accumulators stay as the last real step left them).
     if (!active) return;
+    // Test hook: a bounded wait on a word that nothing sets, made before any barrier, copy,
+    // push or write of the step, so that every CTA leaves here the way a stopped request's
+    // step does and the host reads the timeout from the error word.
+    if (p.stall > 0) {
+        if (tid == 0) {
+            const volatile int *never = p.err + 3;
+            int it = 0;
+            while (it < p.stall && *never == 0) {
+                __nanosleep(1000);
+                ++it;
+            }
+            if (it == p.stall) atomicExch(p.err, MK_ERR_STALL);
+        }
+        return;
+    }
     if (p.trace && tid == 0) {  // stamp 0: the CTA starts (SM clock cycles, as every stamp)
         unsigned long long t;
         asm volatile("mov.u64 %0, %%clock64;" : "=l"(t));

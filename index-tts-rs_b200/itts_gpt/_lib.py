@@ -96,6 +96,7 @@ SIGNATURES = [
      [_P, _P, _I32, _I32, _I32, C.POINTER(C.c_float), C.POINTER(_I32)]),
     ("itts_bench_trace", C.c_int,
      [_P, _P, _I32, _I32, _P, _I32, C.POINTER(_I32), C.POINTER(_I32)]),
+    ("itts_test_stall", C.c_int, [_P, _P, _I32]),
 ]
 
 _lib = None

@@ -492,3 +492,38 @@ def test_generate_stops_early_and_skips_idle_steps(small_weights, small_cfg):
         print(f"early stop: {n_early} replays in {t_early:.3f} ms; full run {per_step_full:.4f} ms per step")
     finally:
         gpt.close()
+
+
+def test_device_wait_timeout_leaves_the_handle_usable(small, small_cfg):
+    """A bounded device wait that runs out comes back as ITTS_E_TIMEOUT (the error convention
+    of crates/core/src/error.rs extended by a timeout kind).  The batch-1 kernel's test hook
+    (itts_test_stall) polls a word that nothing sets and gives up after 2,000 polls, before the
+    step does anything else.  The slot is then as before the step, so the same step on the same
+    handle gives the checker's logits; generate through the replayed graphs times out the same
+    way, and after the hook is turned off a fresh request generates the checker's codes."""
+    from itts_gpt import _lib as L
+    lib = L.load_lib()
+    gpt, om = small
+    text = make_text(20, small_cfg.text_vocab, seed=7)
+    conds = make_conds(small_cfg.d, 3, seed=8)
+    kv, okv = ig.KvCache(gpt, max_seq=256), om.kv(256)
+    assert kv.decode_kernel(1) == "xk_decode_kernel"
+    check_logits(gpt.prefill(text, conds, 1, kv), om.prefill(okv, text, conds, 1), "prefill")
+    n0 = kv.valid_len()
+    assert lib.itts_test_stall(gpt._h, kv._h, 2000) == 0
+    with pytest.raises(ig.TimeoutError_, match="timed out"):
+        gpt.step(kv, 5, 2)
+    assert kv.valid_len() == n0
+    assert lib.itts_test_stall(gpt._h, kv._h, -1) == L.ITTS_E_VALIDATION
+    assert lib.itts_test_stall(gpt._h, kv._h, 0) == 0
+    for i in range(3):
+        check_logits(gpt.step(kv, 5 + i, 2 + i), om.step(okv, 5 + i, 2 + i), f"step {i} after the timeout")
+
+    p = ig.SamplingParams(greedy=True, max_mel_tokens=16)
+    assert lib.itts_test_stall(gpt._h, kv._h, 2000) == 0
+    with pytest.raises(ig.TimeoutError_, match="timed out"):
+        ig.generate_codes(gpt, text, conds, 1, kv, p, ig.SamplerRng(0))
+    assert lib.itts_test_stall(gpt._h, kv._h, 0) == 0
+    codes = ig.generate_codes(gpt, text, conds, 1, kv, p, ig.SamplerRng(0))
+    ref, _ = om.generate(om.kv(256), text, conds, 1, orc.params_c(greedy=True, max_mel_tokens=16), 0)
+    assert codes == list(ref)
