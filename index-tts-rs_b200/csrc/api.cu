@@ -479,7 +479,6 @@ extern "C" int itts_gpt_from_tensors(const itts_tensor *tensors, int32_t n_tenso
         if (pe != cudaSuccess) {
             cudaGetLastError();
             cudaFree(g->projh_arena);
-    cudaFree(g->mlpk_arena);
             g->projh_arena = nullptr;
             for (int i = 0; i < n_layers; ++i) g->layers[i].proj_h = nullptr;
         }

@@ -356,6 +356,8 @@ bool skinny_ok(const MkLin &W, int nb) {
            W.n_rb <= 4096 && skinny_smem_bytes(W, nb) <= (size_t)SK_MAX_SMEM;
 }
 
+constexpr int LNF_CH = MK_MAX_D / 128;
+template <int NCH>
 __global__ void ln_frag_kernel(const float *x, const float *w, const float *b, int rows, int d, __half *y);
 
 void kernels_init_wide() {  // once per device, at model load
@@ -363,7 +365,10 @@ void kernels_init_wide() {  // once per device, at model load
     cudaFuncSetAttribute(skinny_q8_kernel<EPI_GELU>, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_MAX_SMEM);
     cudaFuncSetAttribute(skinny_q8_kernel<EPI_RESID>, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_MAX_SMEM);
     cudaFuncSetAttribute(skinny_q8_kernel<EPI_QKV>, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_MAX_SMEM);
-    cudaFuncSetAttribute(ln_frag_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    cudaFuncSetAttribute(ln_frag_kernel<2>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    cudaFuncSetAttribute(ln_frag_kernel<6>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    cudaFuncSetAttribute(ln_frag_kernel<10>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    cudaFuncSetAttribute(ln_frag_kernel<LNF_CH>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     cudaGetLastError();  // a refusal shows up as skinny_ok() launches failing, never as a stale error
 }
 
@@ -416,27 +421,32 @@ cudaError_t launch_skinny(int epi, const MkLin &W, const __half *x, int nb, void
 
 // ---------------------------------------------------------------------------
 // LayerNorm of nb rows into fp16 fragment order (the skinny GEMM's activation layout):
-// one warp per row, two-pass statistics over the row held in registers.
+// one warp per row and two rows per CTA (so a 64-row step spreads over 32 SMs), two-pass
+// statistics over the row held in registers; the row, its weights and its biases are all
+// loaded before the first reduction.  NCH (>= d / 128) sizes the register arrays.
 // ---------------------------------------------------------------------------
-constexpr int LNF_CH = MK_MAX_D / 128;
-
-__global__ void __launch_bounds__(256) ln_frag_kernel(const float *x, const float *w, const float *b, int rows,
-                                                      int d, __half *y) {
-    const int t = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+template <int NCH>
+__global__ void __launch_bounds__(64) ln_frag_kernel(const float *x, const float *w, const float *b, int rows,
+                                                     int d, __half *y) {
+    const int t = blockIdx.x * 2 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (t >= rows) return;
     const int nch = d / 128;
     const float4 *row = reinterpret_cast<const float4 *>(x + (size_t)t * d);
-    float4 v[LNF_CH];
+    float4 v[NCH], ww[NCH], bb[NCH];
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {  // every load issued before the first use (no early exit)
+        const bool in = c < nch;
+        v[c] = in ? row[c * 32 + lane] : make_float4(0.f, 0.f, 0.f, 0.f);
+        ww[c] = in ? __ldg(reinterpret_cast<const float4 *>(w) + c * 32 + lane) : v[c];
+        bb[c] = in ? __ldg(reinterpret_cast<const float4 *>(b) + c * 32 + lane) : v[c];
+    }
     float s = 0.f;
 #pragma unroll
-    for (int c = 0; c < LNF_CH; ++c)  // every load issued before the first use (no early exit)
-        v[c] = c < nch ? row[c * 32 + lane] : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int c = 0; c < LNF_CH; ++c) s += (v[c].x + v[c].y) + (v[c].z + v[c].w);
+    for (int c = 0; c < NCH; ++c) s += (v[c].x + v[c].y) + (v[c].z + v[c].w);
     const float mean = warp_sum(s) / (float)d;
     float q = 0.f;
 #pragma unroll
-    for (int c = 0; c < LNF_CH; ++c) {
+    for (int c = 0; c < NCH; ++c) {
         if (c < nch) {
             const float a0 = v[c].x - mean, a1 = v[c].y - mean, a2 = v[c].z - mean, a3 = v[c].w - mean;
             q += (a0 * a0 + a1 * a1) + (a2 * a2 + a3 * a3);
@@ -445,23 +455,24 @@ __global__ void __launch_bounds__(256) ln_frag_kernel(const float *x, const floa
     const float rstd = 1.0f / sqrtf(warp_sum(q) / (float)d + kNormEps);
     __half *yr = y + (size_t)t * d;
 #pragma unroll
-    for (int c = 0; c < LNF_CH; ++c) {
+    for (int c = 0; c < NCH; ++c) {
         if (c >= nch) break;
         const int k0 = (c * 32 + lane) * 4;
-        const float4 ww = __ldg(reinterpret_cast<const float4 *>(w + k0));
-        const float4 bb = __ldg(reinterpret_cast<const float4 *>(b + k0));
-        const float o[4] = {(v[c].x - mean) * rstd * ww.x + bb.x, (v[c].y - mean) * rstd * ww.y + bb.y,
-                            (v[c].z - mean) * rstd * ww.z + bb.z, (v[c].w - mean) * rstd * ww.w + bb.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const int k = k0 + e;
-            yr[(k & ~63) + frag_pos(k & 63)] = __float2half_rn(o[e]);
-        }
+        const float o0 = (v[c].x - mean) * rstd * ww[c].x + bb[c].x, o1 = (v[c].y - mean) * rstd * ww[c].y + bb[c].y;
+        const float o2 = (v[c].z - mean) * rstd * ww[c].z + bb[c].z, o3 = (v[c].w - mean) * rstd * ww[c].w + bb[c].w;
+        // inputs k, k + 1 (k even) sit next to each other in fragment order
+        __half *g = yr + (k0 & ~63);
+        *reinterpret_cast<__half2 *>(g + frag_pos(k0 & 63)) = __floats2half2_rn(o0, o1);
+        *reinterpret_cast<__half2 *>(g + frag_pos((k0 + 2) & 63)) = __floats2half2_rn(o2, o3);
     }
 }
 
 void launch_ln_frag(const float *x, const float *w, const float *b, int rows, int d, __half *y, cudaStream_t st) {
-    ln_frag_kernel<<<(rows + 7) / 8, 256, 0, st>>>(x, w, b, rows, d, y);
+    const int nch = d / 128, grid = (rows + 1) / 2;
+    if (nch <= 2) ln_frag_kernel<2><<<grid, 64, 0, st>>>(x, w, b, rows, d, y);
+    else if (nch <= 6) ln_frag_kernel<6><<<grid, 64, 0, st>>>(x, w, b, rows, d, y);
+    else if (nch <= 10) ln_frag_kernel<10><<<grid, 64, 0, st>>>(x, w, b, rows, d, y);
+    else ln_frag_kernel<LNF_CH><<<grid, 64, 0, st>>>(x, w, b, rows, d, y);
 }
 
 }  // namespace itts
