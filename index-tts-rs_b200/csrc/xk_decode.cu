@@ -66,6 +66,8 @@ static_assert(SLOT % 1024 == 0 && KVPOS * 128 <= KV_VOFF && KV_VOFF + KVPOS * 12
 constexpr int REC = 68;            // floats per attention record: m, l, 0, 0, acc[64]
 constexpr int QT = 12;             // QKV row blocks of one head (q, k, v x 64 rows / 16)
 constexpr uint32_t SPIN = 1u << 22;
+constexpr int TABW = 8;                          // layer-table words per thread loaded up front
+constexpr int EMBW = (MK_MAX_KC + CT - 1) / CT;  // embedding values per consumer thread (d <= MK_MAX_KC)
 constexpr int kXkRangeCode = MK_ERR_RANGE;  // error word: a partial outside the fixed-point range
 // counted fixed-point accumulator words (see the top of the file)
 // (2^-28 resolution: coarser units change the fp16 rounding of some activations downstream)
@@ -718,10 +720,7 @@ struct XkConsumer {
         const LnRegs ln1 = ln_prefetch(Ly.ln1_w, Ly.ln1_b);
         const float4 bpre = bias_pre<CS>(Ly.qkv, TM_QKV);
         if (l == 0) {
-            const float *e = p.mel_emb + (size_t)T->tok * d, *ps = p.mel_pos + (size_t)T->pos * d;
-            for (int k = tid; k < d; k += CT) land[k] = e[k] + ps[k];
-            csync();
-            trace();
+            trace();  // (the embedding went into land before the set-up barrier)
         } else {
             exchange_x(l - 1, 20);
         }
@@ -1143,6 +1142,17 @@ __global__ void __launch_bounds__(NT, 1) xk_decode_kernel(const __grid_constant_
     uint64_t *emptyp = fullp + NSLOT;
     uint64_t *stb = emptyp + NSLOT;
 
+    // Global loads issued ahead of the set-up, so that their latencies overlap: the layer
+    // table, this CTA's launch counter, the slot state and then the embedding rows it names.
+    const int words = (int)(p.n_layers * sizeof(MkLayer) / 4);
+    const uint32_t *tsrc = reinterpret_cast<const uint32_t *>(p.layers);
+    uint32_t tw[TABW];
+#pragma unroll
+    for (int j = 0; j < TABW; ++j) {
+        const int i = tid + j * NT;
+        tw[j] = i < words ? __ldg(tsrc + i) : 0u;
+    }
+    const uint32_t epoch = xp.epoch[R];
     // step shape: cluster c runs head c; rank k of it the k-th of CS ranges of the K/V tiles
     const int slot = p.batch_slot[0];
     const SlotState &st = p.slots[slot];
@@ -1150,6 +1160,16 @@ __global__ void __launch_bounds__(NT, 1) xk_decode_kernel(const __grid_constant_
     const int lold = active ? st.valid_len : 0;
     const int kvt = active ? max(1, (lold + KVPOS - 1) / KVPOS) : 0;
     const int head = R / CS;
+    const int tok = min(max(st.tok, 0), p.mel_vocab - 1), pos = min(max(st.pos, 0), p.mel_pos_len - 1);
+    float emb[EMBW];  // layer 0's input x = mel_emb[tok] + mel_pos[pos] (gpt.rs:706-754)
+    {
+        const float *e = p.mel_emb + (size_t)tok * p.d, *ps = p.mel_pos + (size_t)pos * p.d;
+#pragma unroll
+        for (int j = 0; j < EMBW; ++j) {
+            const int k = tid + j * CT;
+            emb[j] = tid < CT && k < p.d ? __ldg(e + k) + __ldg(ps + k) : 0.f;
+        }
+    }
     // A step of a request that has stopped (sampler.rs:378) or failed does nothing: every
     // CTA reads the same slot state, so all of them leave here, before any barrier, copy or
     // write (the launch counter and the accumulators stay as the last real step left them).
@@ -1175,10 +1195,21 @@ __global__ void __launch_bounds__(NT, 1) xk_decode_kernel(const __grid_constant_
         p.trace[(size_t)R * MK_TRACE_EVENTS] = t;
     }
     {
-        const int words = (int)(p.n_layers * sizeof(MkLayer) / 4);
-        const uint32_t *src = reinterpret_cast<const uint32_t *>(p.layers);
         uint32_t *dst = reinterpret_cast<uint32_t *>(smem + SL.lay);
-        for (int i = tid; i < words; i += NT) dst[i] = src[i];
+#pragma unroll
+        for (int j = 0; j < TABW; ++j) {
+            const int i = tid + j * NT;
+            if (i < words) dst[i] = tw[j];
+        }
+        for (int i = tid + TABW * NT; i < words; i += NT) dst[i] = tsrc[i];
+    }
+    if (tid < CT) {  // (no peer pushes into land before this CTA's own layer-0 rows are out)
+        float *land = reinterpret_cast<float *>(smem + SL.land);
+#pragma unroll
+        for (int j = 0; j < EMBW; ++j) {
+            const int k = tid + j * CT;
+            if (k < p.d) land[k] = emb[j];
+        }
     }
     if (tid == 0) {
         for (int s = 0; s < NSLOT; ++s) {
@@ -1200,11 +1231,10 @@ __global__ void __launch_bounds__(NT, 1) xk_decode_kernel(const __grid_constant_
         // smaller share
         T->t_lo = (rank * kvt + CS - 1) / CS;
         T->t_hi = ((rank + 1) * kvt + CS - 1) / CS;
-        T->tok = min(max(st.tok, 0), p.mel_vocab - 1);
-        T->pos = min(max(st.pos, 0), p.mel_pos_len - 1);
+        T->tok = tok;
+        T->pos = pos;
     }
     __syncthreads();
-    const uint32_t epoch = xp.epoch[R];
     {  // the next step's accumulator words (this step's were zeroed by the last)
         const uint32_t q = (epoch & 1u) ^ 1u;
         const size_t n = (size_t)p.n_layers * p.d;
