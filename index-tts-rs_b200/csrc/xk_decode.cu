@@ -456,7 +456,7 @@ struct XkConsumer {
         const float rstd = rsqrtf(fmaxf(t2 * inv_d - m1 * m1, 0.f) + kNormEps);
 #pragma unroll
         for (int j = 0; j < LNC; ++j) {
-            if (j * CT >= d / 4) break;  // (uniform: no thread of this round has inputs)
+            if (j * CT >= d / 4) break;  // (uniform: no thread has inputs in this pass)
             const int k4 = tid + j * CT;
             const bool in = k4 * 4 < d;
             float4 y;
