@@ -31,26 +31,29 @@
 namespace itts {
 namespace {
 
-constexpr int SK_THREADS = 256;
-constexpr int SK_WARPS = SK_THREADS / 32;
+// 16 warps per CTA when the K-part reduction buffer of 16 warps fits in shared memory, else 8
+// (one CTA per SM either way: the activation block takes most of the shared memory)
+constexpr int SK_THREADS = 512;
+constexpr int SK_WARPS_LO = 8;
 constexpr uint32_t SK_SPIN = 1u << 24;
 // Dynamic shared memory of the skinny kernel: at most this (the kernel's static shared
 // memory and the per-block reserve stay below the 227 KB opt-in limit of sm_100).
-constexpr int SK_MAX_SMEM = 224 * 1024;
+constexpr int SK_MAX_SMEM = 226 * 1024;
 constexpr int SK_RPITCH = 17;  // floats per column of the K-part reduction buffer (16 rows + pad)
 constexpr int SK_NTW = 2;      // n-tiles (8 columns each) per warp: its weight fragments serve both
 
-// Warp roles for nb columns: NT n-tiles in ng groups of ntw (a warp's weight fragments serve
-// its ntw n-tiles), ks = 8 / ng K parts (warp w: group w % ng, part w / ng); nc = ng*ntw*8.
+// Warp roles for nb columns and `warps` warps: NT n-tiles in ng groups of ntw (a warp's weight
+// fragments serve its ntw n-tiles), ks = warps / ng K parts (warp w: group w % ng, part w / ng);
+// nc = ng*ntw*8.
 struct SkShape {
     int ntw, ng, ks, nc;
 };
-__host__ __device__ inline SkShape sk_shape(int nb) {
+__host__ __device__ inline SkShape sk_shape(int nb, int warps) {
     const int NT = (nb + 7) / 8;
     SkShape s;
     s.ntw = NT < SK_NTW ? NT : SK_NTW;
     s.ng = (NT + s.ntw - 1) / s.ntw;
-    s.ks = SK_WARPS / s.ng;
+    s.ks = warps / s.ng;
     s.nc = s.ng * s.ntw * 8;
     return s;
 }
@@ -105,10 +108,11 @@ struct SkKvDest {
     unsigned char write[SK_MAX_NB];
 };
 
-// Outputs (o, n) for n = n0, n0 + 16, ... (< nb) of one row o: v[u] holds column n0 + 16u.
-// Every load of a thread is issued before its stores (the residual's x, nothing else).
+// Outputs (o, n) for n = n0, n0 + ec, ... (< nb) of one row o: v[u] holds column n0 + ec u
+// (ec = threads / 16: 16 or 32).  Every load of a thread is issued before its stores (the
+// residual's x, nothing else).
 template <int EPI>
-__device__ __forceinline__ void skinny_epilogue(const SkinnyParams &p, const SkKvDest &kd, int o, int n0,
+__device__ __forceinline__ void skinny_epilogue(const SkinnyParams &p, const SkKvDest &kd, int o, int n0, int ec,
                                                 const float *v) {
     const int OUT = p.W.out, nb = p.nb;
     float *y = p.gp.y;
@@ -116,18 +120,18 @@ __device__ __forceinline__ void skinny_epilogue(const SkinnyParams &p, const SkK
         float xv[SK_MAX_NB / 16];
 #pragma unroll
         for (int u = 0; u < SK_MAX_NB / 16; ++u) {
-            const int n = n0 + 16 * u;
+            const int n = n0 + ec * u;
             xv[u] = n < nb ? y[(size_t)n * OUT + o] : 0.f;
         }
 #pragma unroll
         for (int u = 0; u < SK_MAX_NB / 16; ++u) {
-            const int n = n0 + 16 * u;
+            const int n = n0 + ec * u;
             if (n < nb) y[(size_t)n * OUT + o] = xv[u] + v[u];
         }
     } else {
 #pragma unroll
         for (int u = 0; u < SK_MAX_NB / 16; ++u) {
-            const int n = n0 + 16 * u;
+            const int n = n0 + ec * u;
             if (n >= nb) break;
             if (EPI == EPI_GELU) {
                 const int kc = o / p.y_kc, w = o - kc * p.y_kc;
@@ -156,7 +160,8 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_q8_kernel(const __grid_c
     const int groups = gridDim.x / nkc, kc = blockIdx.x % nkc, gi = blockIdx.x / nkc;
     const int nmine = gi < W.n_rb ? (W.n_rb - gi + groups - 1) / groups : 0;  // row blocks gi + i groups
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
-    const SkShape sh = sk_shape(nb);
+    const SkShape sh = sk_shape(nb, (int)(blockDim.x >> 5));
+    const int nthr = (int)blockDim.x, ec = nthr >> 4;
     uint8_t *wbuf = smem;                                                    // [2][tile]
     __half *xs = reinterpret_cast<__half *>(smem + 2 * (size_t)tb);          // [nb][KC]
     float *sxs = reinterpret_cast<float *>(smem + 2 * (size_t)tb + (size_t)nb * KC * 2);  // [nb][G64] group sums
@@ -204,10 +209,10 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_q8_kernel(const __grid_c
     const int KS = sh.ks, NTW = sh.ntw, NC = sh.nc;
     const int ng = warp % sh.ng, kp = warp / sh.ng;  // n-tiles ng * NTW .. + NTW - 1, K part kp
     const bool half_sb = W.sbb == 4;
-    const int erow = tid & 15, en0 = tid >> 4;  // epilogue: row erow, columns en0 + 16 u
+    const int erow = tid & 15, en0 = tid >> 4;  // epilogue: row erow, columns en0 + ec u
     wait(bx, 0);
     // every column's group sums (the dequantization offset term), once for all row blocks
-    for (int q = tid; q < nb * G64; q += SK_THREADS) {
+    for (int q = tid; q < nb * G64; q += nthr) {
         const uint4 *src = reinterpret_cast<const uint4 *>(xs + (size_t)(q / G64) * KC + (q % G64) * 64);
         float a = 0.f;
 #pragma unroll
@@ -292,7 +297,7 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_q8_kernel(const __grid_c
         float v[SK_MAX_NB / 16];
 #pragma unroll
         for (int u = 0; u < SK_MAX_NB / 16; ++u) {
-            const int n = en0 + 16 * u;
+            const int n = en0 + ec * u;
             float a = 0.f;
             if (n < nb)
                 for (int k = 0; k < KS; ++k) a += red[((size_t)k * NC + n) * SK_RPITCH + erow];
@@ -302,14 +307,14 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_q8_kernel(const __grid_c
             if (erow_ok) {
 #pragma unroll
                 for (int u = 0; u < SK_MAX_NB / 16; ++u) v[u] += ebias;
-                skinny_epilogue<EPI>(p, kd, eo, en0, v);
+                skinny_epilogue<EPI>(p, kd, eo, en0, ec, v);
             }
         } else {  // several K chunks: partials, then the last of the row block's CTAs sums them
             if (erow_ok) {
                 float *wsk = p.ws + (size_t)kc * nb * W.out;
 #pragma unroll
                 for (int u = 0; u < SK_MAX_NB / 16; ++u) {
-                    const int n = en0 + 16 * u;
+                    const int n = en0 + ec * u;
                     if (n < nb) wsk[(size_t)n * W.out + eo] = v[u];
                 }
             }
@@ -330,13 +335,13 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_q8_kernel(const __grid_c
                         const float *wk = p.ws + (size_t)k * nb * W.out;
 #pragma unroll
                         for (int u = 0; u < SK_MAX_NB / 16; ++u) {
-                            const int n = en0 + 16 * u;
+                            const int n = en0 + ec * u;
                             if (n < nb) part[u] += __ldcg(wk + (size_t)n * W.out + eo);
                         }
                     }
 #pragma unroll
                     for (int u = 0; u < SK_MAX_NB / 16; ++u) t[u] += part[u];
-                    skinny_epilogue<EPI>(p, kd, eo, en0, t);
+                    skinny_epilogue<EPI>(p, kd, eo, en0, ec, t);
                 }
                 if (tid == 0) p.counters[rb] = 0;
             }
@@ -345,15 +350,25 @@ __global__ void __launch_bounds__(SK_THREADS, 1) skinny_q8_kernel(const __grid_c
     }
 }
 
-size_t skinny_smem_bytes(const MkLin &W, int nb) {
-    const SkShape sh = sk_shape(nb);
+size_t skinny_smem_bytes(const MkLin &W, int nb, int warps) {
+    const SkShape sh = sk_shape(nb, warps);
     return 2 * (size_t)W.tile_bytes + (size_t)nb * W.kc * 2 + (size_t)nb * (W.kc / 64) * 4 +
            (size_t)sh.ks * sh.nc * SK_RPITCH * 4;
 }
 
+// Warps per CTA for this GEMM and column count: 16 when every K part still gets at least 4 of
+// the tile's quantization groups and the larger reduction buffer fits, else 8.  (At 64 columns
+// 16 warps took the step from 3.42 to 3.33 ms; at 32 columns, 8 K parts of 2-3 groups each were
+// slower than 4 parts of 5.)
+static int skinny_warps(const MkLin &W, int nb) {
+    const int hi = SK_THREADS / 32;
+    const bool enough_groups = sk_shape(nb, hi).ks * 4 <= W.kc / 64;
+    return enough_groups && skinny_smem_bytes(W, nb, hi) <= (size_t)SK_MAX_SMEM ? hi : SK_WARPS_LO;
+}
+
 bool skinny_ok(const MkLin &W, int nb) {
     return nb >= 1 && nb <= SK_MAX_NB && W.kc % 64 == 0 && W.tile_bytes % 16 == 0 && (W.kc * 2) % 16 == 0 &&
-           W.n_rb <= 4096 && skinny_smem_bytes(W, nb) <= (size_t)SK_MAX_SMEM;
+           W.n_rb <= 4096 && skinny_smem_bytes(W, nb, SK_WARPS_LO) <= (size_t)SK_MAX_SMEM;
 }
 
 constexpr int LNF_CH = MK_MAX_D / 128;
@@ -374,7 +389,8 @@ void kernels_init_wide() {  // once per device, at model load
 
 template <int EPI>
 static cudaError_t skinny_launch_t(const SkinnyParams &p, cudaStream_t st) {
-    const size_t smem = skinny_smem_bytes(p.W, p.nb);
+    const int warps = skinny_warps(p.W, p.nb);
+    const size_t smem = skinny_smem_bytes(p.W, p.nb, warps);
     static int sms[64] = {0};  // SMs per device (one CTA per SM: the kernel takes most of the shared memory)
     int dev = 0;
     cudaGetDevice(&dev);
@@ -382,7 +398,7 @@ static cudaError_t skinny_launch_t(const SkinnyParams &p, cudaStream_t st) {
     const int n_sm = dev >= 0 && dev < 64 && sms[dev] > 0 ? sms[dev] : 148;
     const int groups = std::max(1, std::min(p.W.n_rb, n_sm / p.W.n_kc));
     dim3 grid(groups * p.W.n_kc);
-    skinny_q8_kernel<EPI><<<grid, SK_THREADS, smem, st>>>(p);
+    skinny_q8_kernel<EPI><<<grid, warps * 32, smem, st>>>(p);
     return cudaGetLastError();
 }
 

@@ -281,13 +281,19 @@ def test_teacher_forced_replay_full_size(full):
     np.testing.assert_allclose(got, maps2, atol=2e-3)
 
 
-def test_wide_steps_on_int8_tiles(full):
-    """Decode steps of 12 columns (the skinny int8 GEMMs, whose mlp projection sums its four
-    K chunks in a second pass) against the checker, column by column, for 4 steps."""
+@pytest.mark.parametrize("n", [12, 40])
+def test_wide_steps_on_int8_tiles(full, n):
+    """Decode steps of 12 and 40 columns on the skinny int8 GEMMs (8 warps per CTA at 12
+    columns, 16 at 40; the mlp projection sums its four K chunks in a second pass) against the
+    checker, column by column, for 4 steps.  The 40-column case uses short prompts to keep the
+    checker's prefills quick."""
     gpt, om = full
-    n = 12
-    prompts = [ig.CodePrompt(make_text(10 + 7 * r, CFG.text_vocab, seed=600 + r),
-                             make_conds(CFG.d, N_CONDS if r % 2 else 3, seed=700 + r), 1) for r in range(n)]
+    if n <= 12:
+        lens, n_conds = [10 + 7 * r for r in range(n)], [N_CONDS if r % 2 else 3 for r in range(n)]
+    else:
+        lens, n_conds = [8 + r % 24 for r in range(n)], [3] * n
+    prompts = [ig.CodePrompt(make_text(lens[r], CFG.text_vocab, seed=600 + r),
+                             make_conds(CFG.d, n_conds[r], seed=700 + r), 1) for r in range(n)]
     kv = ig.KvCache(gpt, max_seq=256, max_batch=n)
     assert kv.decode_kernel(n) == "gemm path"
     ig.prefill_batch(gpt, prompts, kv)
@@ -300,4 +306,4 @@ def test_wide_steps_on_int8_tiles(full):
         got = gpt.step_batch(kv, list(range(n)), codes[s].tolist(), [2 + s] * n)
         for r in range(n):
             errs.append(check_logits(got[r], om.step(okvs[r], int(codes[s, r]), 2 + s), f"column {r} step {s}"))
-    print(f"12-column steps on the int8 tiles: max |dlogit| {max(errs):.2e}")
+    print(f"{n}-column steps on the int8 tiles: max |dlogit| {max(errs):.2e}")
